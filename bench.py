@@ -1,0 +1,482 @@
+#!/usr/bin/env python
+"""Benchmark: Local-AR + sampling frames/s per GPU and per box, p50/p99
+per-frame latency.
+
+Workloads (synthetic, seeded; random-init weights ~N(0, 0.02) of the
+NeMo-default Local AR shape: in-projection 768->256, 1 layer, d=256, 4 heads,
+FFN 1024, 16 heads 256->2024, 16 tables 2024x768):
+
+* ``config4`` (default, the scaling metric): 1024 sessions x CFG pair sharded
+  evenly over the ranks (1024/N per GPU, no collective), 500 frames; 5% of the
+  sessions are forced to EOS (``finished``) at a frame drawn from U[50, 500]
+  and masked out afterwards; until then EOS is forbidden (``unfinished``);
+  ``forbid_eos`` holds for the first 2 decoder steps.  A bench *step* is the
+  whole 500-frame run of this rank's sessions; ``value`` = all ranks' session
+  frames / max-over-ranks time.
+* ``config3``: 64 sessions per GPU, EOS forced at U[200, 600], 600 frames.
+* ``config2`` latency (rank 0, N=1 only, also reported inside every N=1 line):
+  one session, CFG, seed 1234, 1000 frames with new hidden states, each frame
+  one CUDA-graph launch of the frame; p50/p99 over frames by CUDA events.
+
+A "frame" is one session's 16-position Local AR step (one decoder hidden in,
+16 codec tokens = 2 codec frames x 8 codebooks out).
+
+``--impl reference`` times the reference's path as its CPU oracle (the
+PyTorch restatement of the NeMo forward + the C restatement of the sampling
+plugin, bit-exact with the reference on its golden vectors) on the host cores,
+on bounded samples of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+from magpie_tts_rt_b200.model import EMBED, SHAPE_BASELINE, make_weights  # noqa: E402
+
+METRIC = "Local-AR+sampling frames/sec per GPU and box (1/2/4/8); p50 per-frame us"
+WORKLOADS = {
+    "config4": dict(total_streams=1024, frames=500, eos_frac=0.05, eos_lo=50, eos_hi=500, weak=False),
+    "config3": dict(per_gpu_streams=64, frames=600, eos_frac=1.0, eos_lo=200, eos_hi=600, weak=True),
+}
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=3)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="config4", choices=list(WORKLOADS))
+    ap.add_argument("--frames", type=int, default=None, help="override frames per step (profiling)")
+    ap.add_argument("--no-latency", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+# ---------------------------------------------------------------------------
+# distributed plumbing
+# ---------------------------------------------------------------------------
+
+def dist_init():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        backend = "nccl" if torch.cuda.is_available() else "gloo"
+        if torch.cuda.is_available():
+            torch.cuda.set_device(local)
+        dist.init_process_group(backend, timeout=datetime.timedelta(seconds=120))
+    elif torch.cuda.is_available():
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(value: float, world: int) -> float:
+    if world == 1:
+        return value
+    import torch.distributed as dist
+    t = torch.tensor([value], dtype=torch.float64, device="cuda" if torch.cuda.is_available() else "cpu")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def sum_over_ranks(value: float, world: int) -> float:
+    if world == 1:
+        return value
+    import torch.distributed as dist
+    t = torch.tensor([value], dtype=torch.float64, device="cuda" if torch.cuda.is_available() else "cpu")
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return float(t.item())
+
+
+# ---------------------------------------------------------------------------
+# workload
+# ---------------------------------------------------------------------------
+
+def rank_streams(cfg, world, rank):
+    if cfg["weak"]:
+        n = cfg["per_gpu_streams"]
+        return n, rank * n, n * world
+    total = cfg["total_streams"]
+    n = total // world
+    return n, rank * n, total
+
+
+def eos_schedule(cfg, total, frames, seed=2024):
+    """eos_frame[s] for every session of the job (same on all ranks)."""
+    rng = np.random.default_rng(seed)
+    eos = np.full(total, frames + 1, np.int64)  # never within the run
+    k = int(round(cfg["eos_frac"] * total))
+    chosen = rng.choice(total, k, replace=False) if k < total else np.arange(total)
+    eos[chosen] = rng.integers(cfg["eos_lo"], cfg["eos_hi"] + 1, k)
+    return eos
+
+
+def flag_tables(eos, frames):
+    f = np.arange(frames)[:, None]
+    e = eos[None, :]
+    active = f <= e
+    unfinished = f < e
+    finished = f == e
+    forbid = np.broadcast_to(f < 2, active.shape)
+    return active, unfinished, finished, forbid
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons during the timed region."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines = []
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        if self.thread:
+            self.thread.join(timeout=2)
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx.append(float(parts[2]))
+            except ValueError:
+                continue
+            for name, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(name)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def load_peaks():
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as fh:
+            p = json.load(fh)
+        return p, "measured"
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+# ---------------------------------------------------------------------------
+# our implementation
+# ---------------------------------------------------------------------------
+
+def run_ours(args, world, rank, local):
+    from magpie_tts_rt_b200 import _lib as L
+    from magpie_tts_rt_b200.local_ar import LocalArEngine, StreamBatch
+
+    cfg = WORKLOADS[args.workload]
+    frames = args.frames or cfg["frames"]
+    n, first, total = rank_streams(cfg, world, rank)
+    dev = torch.device("cuda", local)
+    w = make_weights(SHAPE_BASELINE, seed=0, dtype=torch.bfloat16, profile="baseline")
+    eng = LocalArEngine(w, max_streams=n, device=dev)
+    eos = eos_schedule(cfg, total, cfg["frames"])[first:first + n]
+    act, unf, fin, forb = flag_tables(eos, frames)
+    frames_per_step_local = int(act.sum())
+    T = lambda a, dt: torch.as_tensor(np.ascontiguousarray(a), dtype=dt).to(dev)
+    d_act, d_unf, d_fin, d_forb = (T(x, torch.bool) for x in (act, unf, fin, forb))
+    seeds = T(np.arange(first, first + n), torch.int64)
+
+    # inputs: new N(0,1) hidden states per frame per session (pinned host, seeded)
+    g = torch.Generator().manual_seed(1000 + rank)
+    host_hidden = torch.empty(frames, n, 2, EMBED, dtype=torch.bfloat16).pin_memory()
+    chunk = max(1, frames // 16)
+    for f0 in range(0, frames, chunk):
+        f1 = min(frames, f0 + chunk)
+        host_hidden[f0:f1].copy_(torch.randn(f1 - f0, n, 2, EMBED, generator=g))
+    dev_hidden = host_hidden.to(dev)
+    stage = torch.empty(n, 2, EMBED, dtype=torch.bfloat16, device=dev)
+
+    counters = torch.zeros(n, dtype=torch.int64, device=dev)
+    codec = torch.zeros(frames, n, 8, 2, dtype=torch.int64, device=dev)
+    invalid = torch.zeros(frames, n, dtype=torch.int32, device=dev)
+    end = torch.zeros(frames, n, dtype=torch.int32, device=dev)
+    nxt = torch.zeros(n, EMBED, dtype=torch.bfloat16, device=dev)
+    host_codec = torch.empty(frames, n, 8, 2, dtype=torch.int64).pin_memory()
+    host_end = torch.empty(frames, n, dtype=torch.int32).pin_memory()
+
+    def batches(hidden_of):
+        out = []
+        for f in range(frames):
+            b = StreamBatch(decoder_hidden=hidden_of(f), unfinished=d_unf[f], finished=d_fin[f],
+                            forbid_eos=d_forb[f], rng_seed=seeds, rng_counter=counters, codec_tokens=codec[f],
+                            invalid_rows=invalid[f], end_frame_index=end[f], next_embedding=nxt, active=d_act[f])
+            out.append(b.c_struct())
+        return out
+
+    resident = batches(lambda f: dev_hidden[f])
+    staged = batches(lambda f: stage)
+    shape, weights_c, sampling = eng._shape, eng._w, eng._sampling
+    ws, ws_bytes = ctypes.c_void_p(eng.workspace.data_ptr()), eng.workspace.numel()
+    launch = L.lib.mtt_b200_launch_local_ar_frame
+
+    def frame_call(cb, stream_handle):
+        st = launch(ctypes.byref(shape), ctypes.byref(weights_c), ctypes.byref(sampling), ctypes.byref(cb), ws,
+                    ws_bytes, stream_handle)
+        if st != 0:
+            raise RuntimeError(f"frame launch failed: {st}")
+
+    stream = torch.cuda.current_stream(dev)
+    sh = ctypes.c_void_p(stream.cuda_stream)
+
+    def step_resident():
+        counters.zero_()
+        for f in range(frames):
+            frame_call(resident[f], sh)
+
+    def step_e2e():
+        counters.zero_()
+        for f in range(frames):
+            stage.copy_(host_hidden[f], non_blocking=True)
+            frame_call(staged[f], sh)
+        host_codec.copy_(codec, non_blocking=True)
+        host_end.copy_(end, non_blocking=True)
+
+    def timed(fn, k):
+        barrier(world)
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(k):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        barrier(world)
+        return e0.elapsed_time(e1) / 1000.0
+
+    for _ in range(args.warmup):
+        step_resident()
+    torch.cuda.synchronize(dev)
+    clocks = ClockSampler(local)
+    clocks.start()
+    t_local = timed(step_resident, args.steps)
+    clk = clocks.stop()
+    t = max_over_ranks(t_local, world)
+    frames_total = sum_over_ranks(frames_per_step_local * args.steps, world)
+    value = frames_total / t
+
+    for _ in range(max(1, args.warmup // 2)):
+        step_e2e()
+    te_local = timed(step_e2e, args.steps)
+    te = max_over_ranks(te_local, world)
+    e2e_value = frames_total / te
+    h2d = host_hidden[0].numel() * 2 * frames
+    d2h = host_codec.numel() * 8 + host_end.numel() * 4
+
+    # sanity: every session's final frame is valid and the forced-EOS sessions ended at frame 0
+    bad = int((invalid.cpu().numpy()[act] != 0).sum())
+    end_np = end.cpu().numpy()
+    forced_ok = all(end_np[eos[s], s] == 0 for s in range(n) if eos[s] < frames)
+    launches_per_frame = eng.launch_count(n)
+    return dict(value=value, t=t, e2e=e2e_value, h2d=h2d, d2h=d2h, clocks=clk, n_local=n, total=total,
+                frames=frames, frames_per_step=frames_total / args.steps, invalid=bad, forced_ok=forced_ok,
+                launches=launches_per_frame * frames * args.steps, eng=eng, w=w)
+
+
+def latency_config2(eng_w, dev, frames=1000, warm=20):
+    """Config 2: B=1 CFG pair, seed 1234, new hidden each frame; one CUDA-graph
+    launch per frame; per-frame device time by CUDA events."""
+    from magpie_tts_rt_b200.local_ar import LocalArEngine, StreamBatch
+    eng = LocalArEngine(eng_w, max_streams=1, device=dev)
+    b = StreamBatch.allocate(1, device=dev)
+    b.rng_seed.fill_(1234)
+    b.unfinished.fill_(True)
+    g = torch.Generator().manual_seed(77)
+    hidden = torch.randn(frames + warm, 1, 2, EMBED, generator=g).to(torch.bfloat16).to(dev)
+    stream = torch.cuda.Stream(dev)
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            eng.frame(b)
+    torch.cuda.synchronize(dev)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        eng.frame(b)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(frames)]
+    with torch.cuda.stream(stream):
+        for f in range(frames + warm):
+            b.decoder_hidden.copy_(hidden[f])
+            b.forbid_eos.fill_(f < 2)
+            if f >= warm:
+                ev[f - warm][0].record(stream)
+            graph.replay()
+            if f >= warm:
+                ev[f - warm][1].record(stream)
+    torch.cuda.synchronize(dev)
+    us = np.array([a.elapsed_time(z) * 1000.0 for a, z in ev])
+    inv = int(b.invalid_rows.item())
+    del graph
+    return {"workload": "config2: 1 session x CFG pair, seed 1234, 1000 frames, CUDA graph per frame",
+            "p50_us": float(np.percentile(us, 50)), "p99_us": float(np.percentile(us, 99)),
+            "mean_us": float(us.mean()), "frames": frames, "invalid": inv}
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline (oracle restatement of the reference's path)
+# ---------------------------------------------------------------------------
+
+def cpu_oracle_sample(streams=64, min_seconds=10.0, max_frames=40, warm=1):
+    from oracle import lt_oracle
+    from oracle import sampler as S
+    torch.set_num_threads(os.cpu_count() or 1)
+    w = make_weights(SHAPE_BASELINE, seed=0, dtype=torch.bfloat16, profile="baseline", with_final=False)
+    g = torch.Generator().manual_seed(5)
+    seeds = np.arange(streams)
+    counter = np.zeros(streams, np.int64)
+    done = 0
+    t0 = None
+    for f in range(max_frames + warm):
+        if f == warm:
+            t0 = time.perf_counter()
+        hidden = torch.randn(streams, 2, EMBED, generator=g).to(torch.bfloat16)
+        r = lt_oracle.run_frame(w, hidden, True, False, f < 2, seeds, counter, S.SamplingParams(), eos=False)
+        counter = r.counter
+        if f >= warm:
+            done += 1
+            if time.perf_counter() - t0 >= min_seconds:
+                break
+    dt = time.perf_counter() - t0
+    return {"value": streams * done / dt, "unit": "frames/s", "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"{streams} sessions x CFG pair x {done} frames of the config-4 shape "
+                      f"(PyTorch-CPU NeMo-forward restatement + C sampling restatement), {dt:.1f} s"}
+
+
+def run_reference(args, world, rank):
+    """--impl reference: the reference path's CPU implementation on host cores."""
+    if rank != 0:
+        return None
+    cfg = WORKLOADS[args.workload]
+    steps = []
+    for i in range(args.warmup + args.steps):
+        s = cpu_oracle_sample(streams=64, min_seconds=0.0, max_frames=2, warm=0)
+        if i >= args.warmup:
+            steps.append(s["value"])
+    value = float(np.mean(steps))
+    s["value"] = value
+    s["sample"] = f"each step: 64 sessions x CFG pair x 2 frames of {args.workload} (bounded sample)"
+    return dict(value=value, cpu=s)
+
+
+def main():
+    args = parse()
+    world, rank, local = dist_init()
+    peaks, peaks_kind = load_peaks()
+    cfgw = WORKLOADS[args.workload]
+    config = {"workload": f"{args.workload}: " + (
+        "1024 sessions x CFG pair sharded over N GPUs, 500 frames, 5% forced EOS at U[50,500]"
+        if args.workload == "config4" else "64 sessions x CFG pair per GPU, forced EOS at U[200,600], 600 frames"),
+        "shape": "in-proj 768->256, 1 layer, d=256, 4 heads, FFN 1024, 16 heads 256->2024",
+        "sampling": "CFG 2.5, T 0.6, top-k 80, Philox seeds = session index",
+        "l2": "inputs larger than L2 (new hidden states every frame, >1 GB per step at N=1); weights stay "
+              "L2-resident across frames as in serving",
+        "parallelism": f"session-sharded dp{world}, no collective"}
+    if args.impl == "reference":
+        r = run_reference(args, world, rank)
+        if rank == 0:
+            line = {"metric": METRIC, "value": r["value"], "unit": "frames/s", "n_gpus": world,
+                    "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "impl": "reference",
+                    "scaling": "weak" if cfgw["weak"] else "strong", "vs_baseline": None, "dtype": "bf16",
+                    "data": "synthetic", "config": config, "cpu_baseline": r["cpu"],
+                    "e2e": {"value": r["value"], "unit": "frames/s", "h2d_bytes_per_step": 0,
+                            "d2h_bytes_per_step": 0}}
+            print(json.dumps(line), flush=True)
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+        return
+
+    res = run_ours(args, world, rank, local)
+    latency = None
+    if world == 1 and not args.no_latency:
+        latency = latency_config2(res["w"], torch.device("cuda", local))
+    cpu = None
+    if world == 1 and rank == 0 and not args.no_cpu_baseline:
+        cpu = cpu_oracle_sample()
+    if rank == 0:
+        shape = SHAPE_BASELINE
+        frames_per_step = res["frames_per_step"]
+        t_step = res["t"] / args.steps
+        # roofline over one frame step of this rank (algorithmic units per frame step)
+        active_per_frame = frames_per_step / world / res["frames"]
+        flops = active_per_frame * 2 * 2 * shape.macs_per_row()
+        bytes_ = shape.frame_weight_params() * 2 + active_per_frame * 31_000
+        t_frame = t_step / res["frames"]
+        tf = flops / t_frame / 1e12
+        gbs = bytes_ / t_frame / 1e9
+        tensor_peak = peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"])
+        roof = {"bound": "tensor", "kernel": "local_ar_frame (one frame step, all launches)",
+                "achieved": tf, "peak": tensor_peak, "unit": "TFLOP/s", "frac": tf / tensor_peak,
+                "peak_kind": f"{peaks_kind} sustained bf16", "traffic": None,
+                "hbm_achieved_gbs": gbs, "hbm_frac": gbs / peaks["hbm_gbs"],
+                "algorithmic_flops_per_frame_step": flops, "algorithmic_bytes_per_frame_step": bytes_}
+        line = {"metric": METRIC, "value": res["value"], "unit": "frames/s", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": res["t"] / args.steps * 1000.0,
+                "higher_is_better": True, "scaling": "weak" if cfgw["weak"] else "strong", "vs_baseline": None,
+                "dtype": "bf16", "data": "synthetic", "config": config,
+                "frames_per_step": frames_per_step, "per_gpu_frames_per_s": res["value"] / world,
+                "e2e": {"value": res["e2e"], "unit": "frames/s", "h2d_bytes_per_step": res["h2d"],
+                        "d2h_bytes_per_step": res["d2h"]},
+                "gpu_launches": res["launches"], "clocks": res["clocks"], "roofline": roof,
+                "latency_config2": latency, "cpu_baseline": cpu,
+                "checks": {"invalid_rows": res["invalid"], "forced_eos_ok": res["forced_ok"]}}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

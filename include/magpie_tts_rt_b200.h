@@ -1,0 +1,355 @@
+/*
+ * magpie_tts_rt_b200 -- B200 (sm_100a) implementation of MagpieTTS-RT's
+ * per-frame Local AR + sampling hot path, behind the reference's C ABI.
+ *
+ * Three groups of entry points:
+ *
+ * 1. The plugin-library ABI the runtime dlopen()s
+ *    (reference: include/magpie_tts_rt/magpie_tts_rt_plugin.h:70-152,
+ *    exported symbols cmake/magpie_tts_rt_plugins.map): mtt_plugin_get_api_v1
+ *    and mtt_plugin_get_main_device_position_class_table_v1, with
+ *    byte-identical structs and status codes.
+ *
+ * 2. The plugin kernel launchers (reference: plugins/local_ar_plugins.hpp:29-55,
+ *    src/runtime/synthesis_kernels.hpp launch_finalize_local_step), as
+ *    extern "C" functions with the same arguments, the same 0 / -1 return
+ *    convention (-1 for a null pointer or a failed launch), stream-ordered,
+ *    no host synchronisation, all buffers caller-owned device memory.  C++
+ *    callers also get inline forwarders under the reference's names in
+ *    namespace magpie_tts_rt::plugins (bottom of this header).
+ *
+ * 3. The batched frame entry (new; no single reference counterpart): one call
+ *    runs the whole 16-position Local AR frame, sampling, EOS and the
+ *    next-frame embedding sum for N independent sessions ("streams") held as
+ *    structure-of-arrays device state.  It replaces, for N sessions at once,
+ *    the reference's per-session Local AR graph launch plus
+ *    launch_finalize_local_step (src/runtime/synthesis_pipeline.cpp:511-569).
+ *
+ * Streams (`void* stream`) are cudaStream_t values; NULL is the legacy
+ * default stream.
+ */
+#ifndef MAGPIE_TTS_RT_B200_H_
+#define MAGPIE_TTS_RT_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+#ifndef __cplusplus
+#include <stdbool.h>
+#endif
+
+#if defined(__GNUC__) || defined(__clang__)
+#define MTT_B200_API __attribute__((visibility("default")))
+#else
+#define MTT_B200_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ------------------------------------------------------------------------ */
+/* 1. Plugin-library ABI v1 (byte-compatible with magpie_tts_rt_plugin.h)    */
+/* ------------------------------------------------------------------------ */
+
+#ifndef MAGPIE_TTS_RT_MAGPIE_TTS_RT_PLUGIN_H_
+#define MTT_PLUGIN_ABI_VERSION_1 UINT32_C(1)
+#define MTT_PLUGIN_CREATOR_COUNT_V1 UINT32_C(5)
+#define MTT_PLUGIN_CREATOR_NAME_CAPACITY UINT32_C(64)
+#define MTT_PLUGIN_CREATOR_VERSION_CAPACITY UINT32_C(16)
+#define MTT_PLUGIN_NAMESPACE_CAPACITY UINT32_C(64)
+
+typedef int32_t mtt_plugin_status_t;
+
+#define MTT_PLUGIN_STATUS_OK INT32_C(0)
+#define MTT_PLUGIN_STATUS_ALREADY_REGISTERED INT32_C(1)
+#define MTT_PLUGIN_STATUS_INVALID_ARGUMENT INT32_C(2)
+#define MTT_PLUGIN_STATUS_ABI_MISMATCH INT32_C(3)
+#define MTT_PLUGIN_STATUS_REGISTRY_UNAVAILABLE INT32_C(4)
+#define MTT_PLUGIN_STATUS_REGISTRATION_CONFLICT INT32_C(5)
+#define MTT_PLUGIN_STATUS_REGISTRATION_FAILED INT32_C(6)
+#define MTT_PLUGIN_STATUS_NOT_READY INT32_C(7)
+#define MTT_PLUGIN_STATUS_CLASS_TABLE_CONFLICT INT32_C(8)
+
+#define MTT_MAIN_DEVICE_POSITION_CLASS_COUNT_V1 UINT32_C(21)
+#define MTT_MAIN_DEVICE_POSITION_K_COUNT_V1 UINT32_C(249)
+#define MTT_MAIN_DEVICE_POSITION_FUNCTION_NAME_CAPACITY UINT32_C(256)
+
+typedef struct mtt_plugin_creator_v1 {
+  uint32_t struct_size;
+  uint32_t abi_version;
+  char name[MTT_PLUGIN_CREATOR_NAME_CAPACITY];
+  char version[MTT_PLUGIN_CREATOR_VERSION_CAPACITY];
+  char plugin_namespace[MTT_PLUGIN_NAMESPACE_CAPACITY];
+} mtt_plugin_creator_v1_t;
+
+typedef mtt_plugin_status_t (*mtt_plugin_register_v1_fn)(void);
+
+typedef struct mtt_plugin_api_v1 {
+  uint32_t struct_size;
+  uint32_t abi_version;
+  uint32_t creator_count;
+  uint32_t reserved_0;
+  mtt_plugin_creator_v1_t creators[MTT_PLUGIN_CREATOR_COUNT_V1];
+  mtt_plugin_register_v1_fn register_plugins;
+  uint64_t reserved[4];
+} mtt_plugin_api_v1_t;
+
+typedef struct mtt_main_device_position_class_v1 {
+  uint32_t struct_size;
+  uint32_t abi_version;
+  uint32_t operation;
+  uint32_t class_index;
+  uint32_t parameter_transport;
+  uint32_t block_x;
+  uint32_t block_y;
+  uint32_t block_z;
+  uint32_t shared_memory_bytes;
+  uint32_t reserved_0;
+  uint64_t parameter_offset;
+  uint64_t parameter_size;
+  char function_name[MTT_MAIN_DEVICE_POSITION_FUNCTION_NAME_CAPACITY];
+  uint64_t reserved[4];
+} mtt_main_device_position_class_v1_t;
+
+typedef struct mtt_main_device_position_k_v1 {
+  uint32_t struct_size;
+  uint32_t abi_version;
+  int32_t active_k;
+  int32_t qk_class_index;
+  uint32_t qk_grid_x;
+  uint32_t qk_grid_y;
+  uint32_t qk_grid_z;
+  int32_t pv_class_index;
+  uint32_t pv_grid_x;
+  uint32_t pv_grid_y;
+  uint32_t pv_grid_z;
+  uint32_t reserved_0;
+  uint64_t reserved[4];
+} mtt_main_device_position_k_v1_t;
+
+typedef struct mtt_main_device_position_class_table_v1 {
+  uint32_t struct_size;
+  uint32_t abi_version;
+  uint32_t class_count;
+  uint32_t k_count;
+  mtt_main_device_position_class_v1_t classes[MTT_MAIN_DEVICE_POSITION_CLASS_COUNT_V1];
+  mtt_main_device_position_k_v1_t k_records[MTT_MAIN_DEVICE_POSITION_K_COUNT_V1];
+  uint64_t reserved[4];
+} mtt_main_device_position_class_table_v1_t;
+#endif /* MAGPIE_TTS_RT_MAGPIE_TTS_RT_PLUGIN_H_ */
+
+/*
+ * Replaces mtt_plugin_get_api_v1 (plugins/local_ar_plugins.cu:4858-4900).
+ * The caller pre-fills struct_size and abi_version; NULL -> INVALID_ARGUMENT,
+ * mismatch -> ABI_MISMATCH.  Fills the five creator descriptors in the
+ * reference's order and names (MagpieLocalARSampling, MagpieLocalAREos,
+ * MagpieLayerNorm, MagpieGeluTanh, MagpieSoftmax; version "1", namespace
+ * "magpie_tts_rt").  register_plugins returns REGISTRY_UNAVAILABLE in builds
+ * without TensorRT (this build), else the reference's registration statuses.
+ */
+MTT_B200_API mtt_plugin_status_t mtt_plugin_get_api_v1(mtt_plugin_api_v1_t* api);
+
+/*
+ * Replaces mtt_plugin_get_main_device_position_class_table_v1
+ * (plugins/local_ar_plugins.cu:4083-4104,4908-4913).  The Main Decoder mode-8
+ * bank is outside this library's path, so the table never becomes ready:
+ * NULL -> INVALID_ARGUMENT, wrong struct_size/abi_version -> ABI_MISMATCH,
+ * otherwise NOT_READY.
+ */
+MTT_B200_API mtt_plugin_status_t mtt_plugin_get_main_device_position_class_table_v1(
+    mtt_main_device_position_class_table_v1_t* table);
+
+/* ------------------------------------------------------------------------ */
+/* 2. Plugin kernel launchers                                                */
+/* ------------------------------------------------------------------------ */
+
+/*
+ * Replaces launch_local_ar_sampling (plugins/local_ar_plugins.hpp:29-41).
+ * One Local AR position for one session: logits [2][2024] bf16 (conditional
+ * row, unconditional row); unfinished / finished / forbid_eos [1] bool;
+ * rng_seed [1] int64 in [0, 2^32); rng_counter [1] int64; embedding table
+ * [2024][768] bf16.  Writes sampled_token [1] int64, next_embedding [2][768]
+ * bf16 (the chosen row, duplicated for both CFG rows), updated_rng_counter [1]
+ * (counter + 1 when the counter is valid) and invalid_rows [1] int32.
+ * CFG 2.5, temperature 0.6, inclusive top-80, Philox-4x32-10 Gumbel.
+ */
+MTT_B200_API int mtt_b200_launch_local_ar_sampling(
+    const void* logits_bf16, const bool* unfinished, const bool* finished, const bool* forbid_eos,
+    const int64_t* rng_seed, const int64_t* rng_counter, const void* embedding_weight_bf16,
+    int64_t* sampled_token, void* next_embedding_bf16, int64_t* updated_rng_counter,
+    int32_t* invalid_rows, void* stream);
+
+/* Replaces local_ar_eos_workspace_size (plugins/local_ar_plugins.hpp:43):
+ * the same byte count, so callers size their buffers identically. */
+MTT_B200_API size_t mtt_b200_local_ar_eos_workspace_size(void);
+
+/*
+ * Replaces launch_local_ar_eos (plugins/local_ar_plugins.hpp:45-55).
+ * decoder_hidden [2][768] bf16, codec_tokens [1][8][2] int64, flags [1] bool,
+ * final projection weight [32384][768] bf16 and bias [32384] bf16, caller
+ * workspace of mtt_b200_local_ar_eos_workspace_size() bytes (256-byte
+ * aligned).  Writes end_frame_index [1] int32 in {-1, 0, 1}.
+ */
+MTT_B200_API int mtt_b200_launch_local_ar_eos(
+    const void* decoder_hidden_bf16, const int64_t* codec_tokens, const bool* unfinished,
+    const bool* finished, const bool* forbid_eos, const void* final_weight_bf16,
+    const void* final_bias_bf16, void* workspace, int32_t* end_frame_index, void* stream);
+
+/*
+ * Replaces launch_finalize_local_step (src/runtime/synthesis_kernels.cu:177-214):
+ * copies the step's [8][2] codec tokens into the [8][8] batch aggregate at
+ * frame_offset (0, 2, 4 or 6), copies the canonical invalid / EOS outputs
+ * into the step slots, commits updated_rng_counter into rng_counter and
+ * latches generation_finished when end_frame_index is 0 or 1.  Returns 0, or
+ * -1 for a null pointer, a bad frame_offset or a failed launch.
+ */
+MTT_B200_API int mtt_b200_launch_finalize_local_step(
+    const int64_t* step_codec_tokens, int64_t* aggregate_codec_tokens, uint32_t frame_offset,
+    const int32_t* canonical_invalid_rows, const int32_t* canonical_end_frame_index,
+    int32_t* step_invalid_rows, int32_t* step_end_frame_index, const int64_t* updated_rng_counter,
+    int64_t* rng_counter, bool* generation_finished, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* 3. Batched Local AR frame                                                 */
+/* ------------------------------------------------------------------------ */
+
+#define MTT_B200_STATUS_OK 0
+#define MTT_B200_STATUS_INVALID_ARGUMENT -1
+#define MTT_B200_STATUS_CUDA_ERROR -2
+#define MTT_B200_STATUS_UNSUPPORTED -3
+
+/* Model shape: head width is always 64; the in-projection 768 -> d_model
+ * exists iff d_model != 768 (magpietts.py:1347-1352). */
+typedef struct mtt_b200_local_ar_shape {
+  int32_t d_model;
+  int32_t n_layers;
+  int32_t n_heads;
+  int32_t d_ffn;
+} mtt_b200_local_ar_shape_t;
+
+/* Device pointers, bf16, PyTorch [out][in] layout.  in_proj_* are NULL when
+ * d_model == 768.  final_* may be NULL when EOS evaluation is never enabled
+ * (every stream unfinished, finished or forbid_eos on every frame). */
+typedef struct mtt_b200_local_ar_weights {
+  const void* in_proj_w; /* [d][768] */
+  const void* in_proj_b; /* [d] */
+  const void* pos;       /* [>=16][d] learnable position table */
+  const void* ln_self;   /* [L][d] */
+  const void* qkv;       /* [L][3d][d]: q rows, k rows, v rows */
+  const void* o;         /* [L][d][d] */
+  const void* ln_ff;     /* [L][d] */
+  const void* ffn1;      /* [L][F][d] */
+  const void* ffn2;      /* [L][d][F] */
+  const void* head_w;    /* [16][2024][d] */
+  const void* head_b;    /* [16][2024] */
+  const void* emb;       /* [16][2024][768] audio embedding tables */
+  const void* final_w;   /* [32384][768] Main Decoder final projection (EOS) */
+  const void* final_b;   /* [32384] */
+} mtt_b200_local_ar_weights_t;
+
+/* Sampling configuration; the reference's values are 80 / 0.6 / 2.5 with CFG
+ * and top-k.  argmax != 0 selects greedy decoding (no RNG, counter unchanged;
+ * magpietts_fused_sampling.py:136-197).  cfg == 0 runs one row per stream. */
+typedef struct mtt_b200_sampling_config {
+  int32_t top_k;
+  float temperature;
+  float cfg_scale;
+  int32_t argmax;
+  int32_t cfg;
+} mtt_b200_sampling_config_t;
+
+/*
+ * Structure-of-arrays session state for n_streams independent sessions
+ * (device pointers).  Stream s owns CFG rows 2s (conditional) and 2s+1
+ * (unconditional), its own seed (its session's seed: row 0 of a one-row
+ * application batch) and its own RNG counter.
+ */
+typedef struct mtt_b200_stream_batch {
+  int32_t n_streams;
+  int32_t reserved_0;
+  const void* decoder_hidden;  /* [n][rows][768] bf16, rows = 2 (cfg) or 1 */
+  const bool* unfinished;      /* [n] */
+  const bool* finished;        /* [n] */
+  const bool* forbid_eos;      /* [n] */
+  const bool* active;          /* [n] or NULL: inactive streams are skipped, outputs untouched */
+  const int64_t* rng_seed;     /* [n] */
+  int64_t* rng_counter;        /* [n] in/out: +16 per frame while valid (argmax: unchanged) */
+  int64_t* codec_tokens;       /* [n][8][2] out, position p = frame*8 + codebook */
+  int32_t* invalid_rows;       /* [n] out: 0 valid, else invalid (max over positions) */
+  int32_t* end_frame_index;    /* [n] out: -1, 0 or 1 */
+  void* next_embedding;        /* [n][768] bf16 out: sum_p table_p[tok_p] / 16 */
+  /* Optional (NULL in production): */
+  const int64_t* forced_tokens; /* [n][16]: next-position inputs replace the sampled
+                                   tokens (teacher forcing, for parity checks) */
+  void* logits_out;             /* [n][16][rows][2024] bf16 per-position logits */
+} mtt_b200_stream_batch_t;
+
+/* Device workspace bytes for launching up to max_streams streams. */
+MTT_B200_API size_t mtt_b200_local_ar_frame_workspace_size(const mtt_b200_local_ar_shape_t* shape,
+                                                          int32_t max_streams, int32_t cfg);
+
+/*
+ * One Local AR frame (16 positions) for a batch of streams, stream-ordered.
+ * workspace: >= mtt_b200_local_ar_frame_workspace_size(shape, n_streams, cfg)
+ * bytes, 256-byte aligned, caller-owned; contents need not be preserved
+ * between calls.  Returns MTT_B200_STATUS_*.  Data-plane failures (non-finite
+ * logits, no candidate, bad seed/counter, overlapping flags) are reported
+ * in-band through invalid_rows, as in the reference.
+ */
+MTT_B200_API int mtt_b200_launch_local_ar_frame(const mtt_b200_local_ar_shape_t* shape,
+                                               const mtt_b200_local_ar_weights_t* weights,
+                                               const mtt_b200_sampling_config_t* sampling,
+                                               const mtt_b200_stream_batch_t* batch, void* workspace,
+                                               size_t workspace_bytes, void* stream);
+
+/* Number of kernels mtt_b200_launch_local_ar_frame enqueues for this batch
+ * shape (for launch accounting). */
+MTT_B200_API int32_t mtt_b200_local_ar_frame_launch_count(const mtt_b200_local_ar_shape_t* shape,
+                                                          int32_t n_streams, int32_t eos_enabled);
+
+/* ------------------------------------------------------------------------ */
+/* Test hooks (no reference counterpart beyond launch_test_clamped_gumbel,   */
+/* plugins/local_ar_plugins.hpp:171-175)                                      */
+/* ------------------------------------------------------------------------ */
+
+/* gumbel[i] = -log(-log(clamp(uniform[i], 6e-8, 0.99999994))) on the device. */
+MTT_B200_API int mtt_b200_launch_test_clamped_gumbel(const float* uniform, float* gumbel, size_t count,
+                                                     void* stream);
+/* out[i] = the device's correctly rounded natural log of x[i]. */
+MTT_B200_API int mtt_b200_launch_test_log(const float* x, float* out, size_t count, void* stream);
+
+#ifdef __cplusplus
+} /* extern "C" */
+
+/* C++ forwarders under the reference's names (plugins/local_ar_plugins.hpp). */
+#if defined(__CUDACC__) || defined(CUDART_VERSION) || defined(__CUDA_RUNTIME_API_H__)
+#include <cstddef>
+#include <cstdint>
+namespace magpie_tts_rt::plugins {
+[[nodiscard]] inline int launch_local_ar_sampling(
+    const void* logits_bf16, const bool* unfinished, const bool* finished, const bool* forbid_eos,
+    const std::int64_t* rng_seed, const std::int64_t* rng_counter, const void* embedding_weight_bf16,
+    std::int64_t* sampled_token, void* next_embedding_bf16, std::int64_t* updated_rng_counter,
+    std::int32_t* invalid_rows, cudaStream_t stream) noexcept {
+  return mtt_b200_launch_local_ar_sampling(logits_bf16, unfinished, finished, forbid_eos, rng_seed,
+                                           rng_counter, embedding_weight_bf16, sampled_token,
+                                           next_embedding_bf16, updated_rng_counter, invalid_rows,
+                                           static_cast<void*>(stream));
+}
+[[nodiscard]] inline std::size_t local_ar_eos_workspace_size() noexcept {
+  return mtt_b200_local_ar_eos_workspace_size();
+}
+[[nodiscard]] inline int launch_local_ar_eos(const void* decoder_hidden_bf16, const std::int64_t* codec_tokens,
+                                             const bool* unfinished, const bool* finished,
+                                             const bool* forbid_eos, const void* final_weight_bf16,
+                                             const void* final_bias_bf16, void* workspace,
+                                             std::int32_t* end_frame_index, cudaStream_t stream) noexcept {
+  return mtt_b200_launch_local_ar_eos(decoder_hidden_bf16, codec_tokens, unfinished, finished, forbid_eos,
+                                      final_weight_bf16, final_bias_bf16, workspace, end_frame_index,
+                                      static_cast<void*>(stream));
+}
+}  // namespace magpie_tts_rt::plugins
+#endif
+#endif /* __cplusplus */
+
+#endif /* MAGPIE_TTS_RT_B200_H_ */

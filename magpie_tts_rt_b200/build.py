@@ -1,0 +1,83 @@
+"""Build the sm_100a shared library ``libmagpie_tts_rt_b200.so`` in-tree.
+
+nvcc compiles every ``csrc/*.cu`` / ``csrc/*.cpp`` for
+``-gencode arch=compute_100a,code=sm_100a`` (nvcc cross-compiles without a
+GPU) and links them with the CUDA runtime statically.  A linker version script
+exports only the ``mtt_*`` C symbols declared in ``include/*.h``, as the
+reference's plugin library exports only its C ABI
+(``cmake/magpie_tts_rt_plugins.map``).
+"""
+from __future__ import annotations
+
+import glob
+import os
+import subprocess
+import sys
+from concurrent.futures import ThreadPoolExecutor
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+REPO = os.path.dirname(HERE)
+CSRC = os.path.join(HERE, "csrc")
+BUILD = os.path.join(HERE, "_build")
+LIBRARY = os.path.join(HERE, "libmagpie_tts_rt_b200.so")
+NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
+ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
+COMMON = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC,-fvisibility=hidden",
+          "-I" + os.path.join(REPO, "include"), "--expt-relaxed-constexpr"]
+VERSION_SCRIPT = """{
+  global:
+    mtt_*;
+  local:
+    *;
+};
+"""
+
+
+def sources():
+    return sorted(glob.glob(os.path.join(CSRC, "*.cu")) + glob.glob(os.path.join(CSRC, "*.cpp")))
+
+
+def headers():
+    return sorted(glob.glob(os.path.join(CSRC, "*.cuh")) + glob.glob(os.path.join(REPO, "include", "*.h")))
+
+
+def _stale(target, deps):
+    if not os.path.exists(target):
+        return True
+    t = os.path.getmtime(target)
+    return any(os.path.getmtime(d) > t for d in deps)
+
+
+def _compile(src, extra):
+    obj = os.path.join(BUILD, os.path.basename(src) + ".o")
+    if _stale(obj, [src] + headers()):
+        cmd = [NVCC] + ARCH + COMMON + extra + ["-c", src, "-o", obj]
+        r = subprocess.run(cmd, capture_output=True, text=True)
+        if r.returncode != 0:
+            raise RuntimeError(f"nvcc failed for {src}:\n{r.stdout}\n{r.stderr}")
+    return obj
+
+
+def build(force: bool = False, verbose_ptxas: bool = False) -> str:
+    os.makedirs(BUILD, exist_ok=True)
+    if force:
+        for o in glob.glob(os.path.join(BUILD, "*.o")):
+            os.remove(o)
+    extra = ["-Xptxas", "-v"] if verbose_ptxas else []
+    srcs = sources()
+    with ThreadPoolExecutor(max_workers=min(8, len(srcs))) as pool:
+        objs = list(pool.map(lambda s: _compile(s, extra), srcs))
+    if force or _stale(LIBRARY, objs):
+        vs = os.path.join(BUILD, "exports.map")
+        with open(vs, "w") as fh:
+            fh.write(VERSION_SCRIPT)
+        cmd = [NVCC] + ARCH + ["-shared", "-cudart", "static", "-o", LIBRARY] + objs + [
+            "-Xlinker", "--version-script=" + vs, "-lcuda"]
+        r = subprocess.run(cmd, capture_output=True, text=True)
+        if r.returncode != 0:
+            raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")
+    return LIBRARY
+
+
+if __name__ == "__main__":
+    print(build(force="--force" in sys.argv, verbose_ptxas="-v" in sys.argv))

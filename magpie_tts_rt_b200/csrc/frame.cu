@@ -1,0 +1,630 @@
+// Batched Local AR frame: 16 positions of the causal Local Transformer, the
+// per-position heads, sampling, EOS and the next-frame embedding sum for N
+// independent sessions ("streams"), stream-ordered on one CUDA stream.
+//
+// Reference path being replaced (per session): the TensorRT Local AR plan
+// (tools/export/local_ar_wrapper.py:609-751 is its tensor statement; NeMo
+// forward: transformer_2501.py:405-442,761-851,1153-1232, ffn_modules.py:
+// 268-290), its MagpieLocalARSampling / MagpieLocalAREos plugins
+// (plugins/local_ar_plugins.cu:1149-1495), the Main Decoder's embedding sum
+// (tools/export/main_decoder_wrapper.py:796-810) and finalize_local_step
+// (src/runtime/synthesis_kernels.cu:53-86).
+//
+// bf16 storage, f32 accumulation, and a bf16 rounding at every point where the
+// PyTorch oracle rounds (each linear/conv output, the position add, every
+// residual add, LN output, GELU output, attention scores, probabilities and
+// context).
+//
+// Phase kernels (one launch each, per position):
+//   embed   : x = bf16(bf16(W_in src + b_in) + pos[p])   (src = decoder hidden
+//             at p = 0, else table_{p-1}[token_{p-1}]); identity in-projection
+//             shapes use a plain add
+//   per layer: LN1 -> qkv (K/V appended to the per-frame cache)
+//              -> attention over p + 1 keys -> o + residual
+//              -> LN2 -> FFN1 + GELU -> FFN2 + residual
+//   head    : logits = bf16(W_p x + b_p)
+//   sample  : one block per stream (sampling.cuh), token, counter, invalid,
+//             running bf16 embedding sum
+// then the EOS projection (eos.cuh) and the commit of tokens / counter /
+// invalid / end_frame / next embedding.
+//
+// Streams flagged inactive are compacted away on the device at the start of
+// the frame: every kernel is sized for n streams and its blocks beyond the
+// active count exit at once.
+#include <cstddef>
+
+#include "../../include/magpie_tts_rt_b200.h"
+#include "eos.cuh"
+#include "sampling.cuh"
+
+namespace mtt {
+namespace {
+
+using bf16 = __nv_bfloat16;
+
+constexpr int kLinThreads = 256;
+constexpr int kBM = 8;   // rows per linear tile (one warp per row in the prologue)
+constexpr int kBN = 32;  // output features per linear tile
+constexpr int kBeginThreads = 1024;
+
+struct Frame {
+  int d, L, H, F, rp, n, in_proj;
+  SamplingParams prm;
+  const bf16 *in_w, *in_b, *pos, *ln1, *qkv, *o, *ln2, *w1, *w2, *head_w, *head_b, *emb, *final_w, *final_b;
+  const bf16* hidden;
+  const bool *unfinished, *finished, *forbid, *active;
+  const int64_t* seed;
+  int64_t* counter_io;
+  int64_t* codec_tokens;
+  int32_t* invalid_rows;
+  int32_t* end_frame;
+  bf16* next_emb;
+  const int64_t* forced;
+  bf16* logits_out;
+  // workspace
+  int32_t *list, *count, *eos_list, *eos_count, *eos_slot;
+  bf16 *x, *q, *kc, *vc, *att, *h, *logits;
+  int32_t* tokens;
+  float* emb_acc;
+  int64_t* ctr;
+  int32_t* inv;
+  float *eos_partial, *eos_logit;
+};
+
+struct Layout {
+  size_t list, count, eos_list, eos_count, eos_slot, x, q, kc, vc, att, h, logits, tokens, emb_acc, ctr, inv,
+      eos_partial, eos_logit, total;
+};
+
+inline size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
+
+Layout make_layout(int d, int L, int F, int n, int rp) {
+  Layout lo{};
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    const size_t at = off;
+    off = align256(off + bytes);
+    return at;
+  };
+  const size_t R = static_cast<size_t>(n) * rp;
+  lo.list = take(4 * static_cast<size_t>(n));
+  lo.count = take(4);
+  lo.eos_list = take(4 * static_cast<size_t>(n));
+  lo.eos_count = take(4);
+  lo.eos_slot = take(4 * static_cast<size_t>(n));
+  lo.x = take(2 * R * d);
+  lo.q = take(2 * R * d);
+  lo.kc = take(2 * static_cast<size_t>(L) * R * kPositions * d);
+  lo.vc = take(2 * static_cast<size_t>(L) * R * kPositions * d);
+  lo.att = take(2 * R * d);
+  lo.h = take(2 * R * F);
+  lo.logits = take(2 * R * kVocab);
+  lo.tokens = take(4 * static_cast<size_t>(n) * kPositions);
+  lo.emb_acc = take(4 * static_cast<size_t>(n) * kEmbed);
+  lo.ctr = take(8 * static_cast<size_t>(n));
+  lo.inv = take(4 * static_cast<size_t>(n));
+  lo.eos_partial = take(4 * static_cast<size_t>(n) * kPositions * kEosChunks);
+  lo.eos_logit = take(4 * static_cast<size_t>(n) * kPositions);
+  lo.total = off;
+  return lo;
+}
+
+// ---------------------------------------------------------------------------
+// frame begin: compact the active streams, choose EOS-enabled ones, init state
+// ---------------------------------------------------------------------------
+
+__global__ void __launch_bounds__(kBeginThreads) frame_begin_kernel(Frame f) {
+  __shared__ int warp_act[kBeginThreads / 32], warp_en[kBeginThreads / 32];
+  __shared__ int base_act, base_en;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (threadIdx.x == 0) {
+    base_act = 0;
+    base_en = 0;
+  }
+  __syncthreads();
+  for (int start = 0; start < f.n; start += kBeginThreads) {
+    const int s = start + threadIdx.x;
+    const bool in = s < f.n;
+    const bool act = in && (f.active == nullptr || f.active[s]);
+    bool en = act && !f.unfinished[s] && !f.finished[s] && !f.forbid[s];
+    int32_t init_inv = 0;
+    if (en && f.final_w == nullptr) {
+      init_inv = 2;  // EOS evaluation required but no final projection supplied
+      en = false;
+    }
+    if (in) {
+      f.ctr[s] = f.counter_io[s];
+      f.inv[s] = init_inv;
+    }
+    const unsigned ba = __ballot_sync(0xffffffffu, act);
+    const unsigned be = __ballot_sync(0xffffffffu, en);
+    if (lane == 0) {
+      warp_act[warp] = __popc(ba);
+      warp_en[warp] = __popc(be);
+    }
+    __syncthreads();
+    int pa = base_act, pe = base_en;
+    for (int w = 0; w < warp; ++w) {
+      pa += warp_act[w];
+      pe += warp_en[w];
+    }
+    const unsigned below = (1u << lane) - 1u;
+    if (act) f.list[pa + __popc(ba & below)] = s;
+    if (in) f.eos_slot[s] = en ? pe + __popc(be & below) : -1;
+    if (en) f.eos_list[pe + __popc(be & below)] = s;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      for (int w = 0; w < kBeginThreads / 32; ++w) {
+        base_act += warp_act[w];
+        base_en += warp_en[w];
+      }
+    }
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) {
+    *f.count = base_act;
+    *f.eos_count = base_en;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// linear layers
+// ---------------------------------------------------------------------------
+
+enum Pro { kProHidden, kProGather, kProLn1, kProLn2, kProAtt, kProH, kProX };
+enum Epi { kEpiInProj, kEpiQkv, kEpiResid, kEpiGelu, kEpiHead };
+
+__device__ __forceinline__ void unpack8(const uint4& v, float (&f)[8]) {
+  const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&v);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const float2 t = __bfloat1622float2(h2[j]);
+    f[2 * j] = t.x;
+    f[2 * j + 1] = t.y;
+  }
+}
+
+__device__ __forceinline__ float gelu_tanh(float v) {
+  const float inner = 0.7978845608028654f * (v + 0.044715f * v * v * v);
+  return 0.5f * v * (1.0f + tanhf(inner));
+}
+
+// Token that feeds position p + 1: the sampled one, or the caller's forced
+// token (clamped into the vocabulary so a bad value cannot index outside the
+// table).
+__device__ __forceinline__ int64_t input_token(const Frame& f, int s, int p) {
+  if (f.forced) {
+    const int64_t t = f.forced[static_cast<int64_t>(s) * kPositions + p];
+    return t < 0 ? 0 : (t >= kVocab ? kVocab - 1 : t);
+  }
+  return f.tokens[static_cast<int64_t>(s) * kPositions + p];
+}
+
+// Fills xs[m][0..K) (bf16) for row r of the tile; one warp per row.
+template <int PRO>
+__device__ __forceinline__ void load_row(const Frame& f, int p, int l, int r, int K, bf16* xs_row) {
+  const int lane = threadIdx.x & 31;
+  const int i = r / f.rp, sub = r % f.rp;
+  const bf16* src = nullptr;
+  if constexpr (PRO == kProHidden) {
+    const int s = f.list[i];
+    src = f.hidden + (static_cast<int64_t>(s) * f.rp + sub) * kEmbed;
+  } else if constexpr (PRO == kProGather) {
+    const int s = f.list[i];
+    const int64_t tok = input_token(f, s, p - 1);
+    src = f.emb + (static_cast<int64_t>(p - 1) * kVocab + tok) * kEmbed;
+  } else if constexpr (PRO == kProAtt) {
+    src = f.att + static_cast<int64_t>(r) * f.d;
+  } else if constexpr (PRO == kProH) {
+    src = f.h + static_cast<int64_t>(r) * f.F;
+  } else if constexpr (PRO == kProX) {
+    src = f.x + static_cast<int64_t>(r) * f.d;
+  }
+  if constexpr (PRO == kProLn1 || PRO == kProLn2) {
+    const bf16* xr = f.x + static_cast<int64_t>(r) * f.d;
+    const bf16* w = (PRO == kProLn1 ? f.ln1 : f.ln2) + static_cast<int64_t>(l) * f.d;
+    float sum = 0.f;
+    for (int k = lane * 8; k < K; k += 256) {
+      float v[8];
+      unpack8(*reinterpret_cast<const uint4*>(xr + k), v);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) sum += v[j];
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    const float mean = sum / static_cast<float>(K);
+    float var = 0.f;
+    for (int k = lane * 8; k < K; k += 256) {
+      float v[8];
+      unpack8(*reinterpret_cast<const uint4*>(xr + k), v);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float dlt = v[j] - mean;
+        var += dlt * dlt;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) var += __shfl_xor_sync(0xffffffffu, var, o);
+    const float rstd = 1.0f / sqrtf(var / static_cast<float>(K) + 1.0e-5f);
+    for (int k = lane * 8; k < K; k += 256) {
+      float v[8], g[8];
+      unpack8(*reinterpret_cast<const uint4*>(xr + k), v);
+      unpack8(*reinterpret_cast<const uint4*>(w + k), g);
+      __align__(16) bf16 out[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) out[j] = f2bf(((v[j] - mean) * rstd) * g[j]);
+      *reinterpret_cast<uint4*>(xs_row + k) = *reinterpret_cast<const uint4*>(out);
+    }
+  } else {
+    for (int k = lane * 8; k < K; k += 256) {
+      *reinterpret_cast<uint4*>(xs_row + k) = *reinterpret_cast<const uint4*>(src + k);
+    }
+  }
+}
+
+template <int PRO, int EPI>
+__global__ void __launch_bounds__(kLinThreads) linear_kernel(Frame f, int p, int l, int N, int K, const bf16* W,
+                                                             const bf16* bias) {
+  extern __shared__ __align__(16) unsigned char lin_smem[];
+  bf16* xs = reinterpret_cast<bf16*>(lin_smem);
+  const int rows = *f.count * f.rp;
+  const int r0 = blockIdx.y * kBM;
+  if (r0 >= rows) return;
+  const int n0 = blockIdx.x * kBN;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  {
+    const int r = r0 + warp;
+    bf16* xr = xs + warp * K;
+    if (r < rows) {
+      load_row<PRO>(f, p, l, r, K, xr);
+    } else {
+      for (int k = lane * 8; k < K; k += 256) *reinterpret_cast<uint4*>(xr + k) = make_uint4(0, 0, 0, 0);
+    }
+  }
+  __syncthreads();
+  constexpr int kCols = kBN / (kLinThreads / 32);
+  for (int c = 0; c < kCols; ++c) {
+    const int n = n0 + warp * kCols + c;
+    if (n >= N) break;
+    float acc[kBM];
+#pragma unroll
+    for (int m = 0; m < kBM; ++m) acc[m] = 0.f;
+    const bf16* wr = W + static_cast<int64_t>(n) * K;
+    for (int k = lane * 8; k < K; k += 256) {
+      float wf[8];
+      unpack8(*reinterpret_cast<const uint4*>(wr + k), wf);
+#pragma unroll
+      for (int m = 0; m < kBM; ++m) {
+        float xf[8];
+        unpack8(*reinterpret_cast<const uint4*>(xs + m * K + k), xf);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[m] = fmaf(wf[j], xf[j], acc[m]);
+      }
+    }
+#pragma unroll
+    for (int m = 0; m < kBM; ++m) {
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) acc[m] += __shfl_xor_sync(0xffffffffu, acc[m], o);
+    }
+    float v = acc[0];
+#pragma unroll
+    for (int m = 1; m < kBM; ++m) v = (lane == m) ? acc[m] : v;
+    const int r = r0 + lane;
+    if (lane < kBM && r < rows) {
+      if constexpr (EPI == kEpiInProj) {
+        const float y = round_bf16(__fadd_rn(v, bf2f(bias[n])));
+        f.x[static_cast<int64_t>(r) * f.d + n] = f2bf(__fadd_rn(y, bf2f(f.pos[static_cast<int64_t>(p) * f.d + n])));
+      } else if constexpr (EPI == kEpiQkv) {
+        const bf16 y = f2bf(v);
+        if (n < f.d) {
+          f.q[static_cast<int64_t>(r) * f.d + n] = y;
+        } else {
+          const int which = n < 2 * f.d ? 0 : 1;
+          const int col = n - (which + 1) * f.d;
+          bf16* cache = which == 0 ? f.kc : f.vc;
+          const int64_t R = static_cast<int64_t>(f.n) * f.rp;
+          cache[((static_cast<int64_t>(l) * R + r) * kPositions + p) * f.d + col] = y;
+        }
+      } else if constexpr (EPI == kEpiResid) {
+        bf16* xp = f.x + static_cast<int64_t>(r) * f.d + n;
+        *xp = f2bf(__fadd_rn(bf2f(*xp), round_bf16(v)));
+      } else if constexpr (EPI == kEpiGelu) {
+        f.h[static_cast<int64_t>(r) * f.F + n] = f2bf(gelu_tanh(round_bf16(v)));
+      } else if constexpr (EPI == kEpiHead) {
+        const bf16 y = f2bf(__fadd_rn(v, bf2f(bias[n])));
+        f.logits[static_cast<int64_t>(r) * kVocab + n] = y;
+        if (f.logits_out) {
+          const int i = r / f.rp, sub = r % f.rp;
+          const int s = f.list[i];
+          f.logits_out[((static_cast<int64_t>(s) * kPositions + p) * f.rp + sub) * kVocab + n] = y;
+        }
+      }
+    }
+  }
+}
+
+// Identity in-projection (d == 768): x = bf16(src + pos[p]).
+__global__ void add_pos_kernel(Frame f, int p) {
+  const int rows = *f.count * f.rp;
+  const int64_t total = static_cast<int64_t>(rows) * f.d;
+  for (int64_t e = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; e < total;
+       e += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int r = static_cast<int>(e / f.d), k = static_cast<int>(e % f.d);
+    const int i = r / f.rp, sub = r % f.rp;
+    const int s = f.list[i];
+    float src;
+    if (p == 0) {
+      src = bf2f(f.hidden[(static_cast<int64_t>(s) * f.rp + sub) * kEmbed + k]);
+    } else {
+      const int64_t tok = input_token(f, s, p - 1);
+      src = bf2f(f.emb[(static_cast<int64_t>(p - 1) * kVocab + tok) * kEmbed + k]);
+    }
+    f.x[e] = f2bf(__fadd_rn(src, bf2f(f.pos[static_cast<int64_t>(p) * f.d + k])));
+  }
+}
+
+// ---------------------------------------------------------------------------
+// attention: one warp per (row, head), p + 1 keys
+// ---------------------------------------------------------------------------
+
+__global__ void __launch_bounds__(256) attention_kernel(Frame f, int p, int l) {
+  const int rows = *f.count * f.rp;
+  const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (gw >= rows * f.H) return;
+  const int r = gw / f.H, hd = gw % f.H;
+  const int64_t R = static_cast<int64_t>(f.n) * f.rp;
+  const float2 qv = __bfloat1622float2(
+      *reinterpret_cast<const __nv_bfloat162*>(f.q + static_cast<int64_t>(r) * f.d + hd * kHeadDim + 2 * lane));
+  const bf16* kbase = f.kc + ((static_cast<int64_t>(l) * R + r) * kPositions) * f.d + hd * kHeadDim + 2 * lane;
+  const bf16* vbase = f.vc + ((static_cast<int64_t>(l) * R + r) * kPositions) * f.d + hd * kHeadDim + 2 * lane;
+  float s[kPositions];
+  float mx = -CUDART_INF_F;
+#pragma unroll
+  for (int j = 0; j < kPositions; ++j) {
+    if (j <= p) {
+      const float2 kv = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(kbase + j * f.d));
+      float dot = qv.x * kv.x + qv.y * kv.y;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
+      s[j] = round_bf16(__fmul_rn(round_bf16(dot), 0.125f));
+      mx = fmaxf(mx, s[j]);
+    }
+  }
+  float sum = 0.f;
+#pragma unroll
+  for (int j = 0; j < kPositions; ++j) {
+    if (j <= p) {
+      s[j] = expf(s[j] - mx);
+      sum += s[j];
+    }
+  }
+  float o0 = 0.f, o1 = 0.f;
+#pragma unroll
+  for (int j = 0; j < kPositions; ++j) {
+    if (j <= p) {
+      const float prob = round_bf16(s[j] / sum);
+      const float2 vv = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(vbase + j * f.d));
+      o0 = fmaf(prob, vv.x, o0);
+      o1 = fmaf(prob, vv.y, o1);
+    }
+  }
+  *reinterpret_cast<__nv_bfloat162*>(f.att + static_cast<int64_t>(r) * f.d + hd * kHeadDim + 2 * lane) =
+      __floats2bfloat162_rn(o0, o1);
+}
+
+// ---------------------------------------------------------------------------
+// sampling + running embedding sum
+// ---------------------------------------------------------------------------
+
+__global__ void __launch_bounds__(kSampleThreads) sample_kernel(Frame f, int p) {
+  __shared__ SampleShared sh;
+  const int i = blockIdx.x;
+  if (i >= *f.count) return;
+  const int s = f.list[i];
+  SampleCall c;
+  c.logits = f.logits + static_cast<int64_t>(i) * f.rp * kVocab;
+  c.uncond_offset = kVocab;
+  c.kind = f.rp == 2 ? kLogitsBf16Cfg : kLogitsBf16;
+  c.unfinished = f.unfinished[s];
+  c.finished = f.finished[s];
+  c.forbid_eos = f.forbid[s];
+  c.seed = f.seed[s];
+  c.counter = f.ctr[s];
+  int invalid = 0;
+  const int token = sample_block(c, f.prm, sh, &invalid);
+  if (threadIdx.x == 0) {
+    f.tokens[s * kPositions + p] = token;
+    f.inv[s] |= invalid;
+    const bool counter_valid = c.counter >= 0 && c.counter <= kMaxCounter;
+    if (!f.prm.argmax && counter_valid) f.ctr[s] = c.counter + 1;
+  }
+  const bf16* row = f.emb + (static_cast<int64_t>(p) * kVocab + token) * kEmbed;
+  float* acc = f.emb_acc + static_cast<int64_t>(s) * kEmbed;
+  for (int k = threadIdx.x; k < kEmbed; k += blockDim.x) {
+    const float v = bf2f(row[k]);
+    acc[k] = p == 0 ? v : round_bf16(__fadd_rn(acc[k], v));
+  }
+}
+
+// ---------------------------------------------------------------------------
+// frame end: EOS decision and commit
+// ---------------------------------------------------------------------------
+
+__global__ void __launch_bounds__(256) frame_end_kernel(Frame f) {
+  const int i = blockIdx.x;
+  if (i >= *f.count) return;
+  const int s = f.list[i];
+  if (threadIdx.x == 0) {
+    const int32_t* tok = f.tokens + s * kPositions;
+    for (int p = 0; p < kPositions; ++p) {
+      f.codec_tokens[static_cast<int64_t>(s) * kPositions + (p % kCodebooks) * kFrames + p / kCodebooks] = tok[p];
+    }
+    const int slot = f.eos_slot[s];
+    const float* part = f.eos_partial + static_cast<int64_t>(slot < 0 ? 0 : slot) * kPositions * kEosChunks;
+    const float* el = f.eos_logit + static_cast<int64_t>(slot < 0 ? 0 : slot) * kPositions;
+    f.end_frame[s] = eos_decide(part, el, tok, slot >= 0, f.finished[s]);
+    f.counter_io[s] = f.ctr[s];
+    f.invalid_rows[s] = f.inv[s];
+  }
+  const float* acc = f.emb_acc + static_cast<int64_t>(s) * kEmbed;
+  for (int k = threadIdx.x; k < kEmbed; k += blockDim.x) {
+    f.next_emb[static_cast<int64_t>(s) * kEmbed + k] = f2bf(__fdiv_rn(acc[k], 16.0f));
+  }
+}
+
+template <int PRO, int EPI>
+void launch_linear(const Frame& f, cudaStream_t st, int p, int l, int N, int K, const bf16* W, const bf16* bias) {
+  const int rows_max = f.n * f.rp;
+  const dim3 grid((N + kBN - 1) / kBN, (rows_max + kBM - 1) / kBM);
+  const size_t smem = static_cast<size_t>(kBM) * K * sizeof(bf16);
+  linear_kernel<PRO, EPI><<<grid, kLinThreads, smem, st>>>(f, p, l, N, K, W, bias);
+}
+
+bool shape_ok(const mtt_b200_local_ar_shape_t* s) {
+  return s && s->d_model > 0 && s->n_heads > 0 && s->d_model == s->n_heads * kHeadDim && s->d_model % 256 == 0 &&
+         s->d_ffn % 256 == 0 && s->d_ffn > 0 && s->n_layers > 0 && s->n_layers <= 8 && s->d_ffn <= 3072 &&
+         s->d_model <= 3072;
+}
+
+}  // namespace
+}  // namespace mtt
+
+extern "C" MTT_B200_API size_t mtt_b200_local_ar_frame_workspace_size(const mtt_b200_local_ar_shape_t* shape,
+                                                                      int32_t max_streams, int32_t cfg) {
+  if (!mtt::shape_ok(shape) || max_streams <= 0) return 0;
+  return mtt::make_layout(shape->d_model, shape->n_layers, shape->d_ffn, max_streams, cfg ? 2 : 1).total;
+}
+
+extern "C" MTT_B200_API int32_t mtt_b200_local_ar_frame_launch_count(const mtt_b200_local_ar_shape_t* shape,
+                                                                     int32_t n_streams, int32_t eos_enabled) {
+  if (!mtt::shape_ok(shape) || n_streams <= 0) return 0;
+  (void)eos_enabled;
+  // begin + 16 x (embed + 5 per layer + head + sample) + eos projection + end
+  return 1 + mtt::kPositions * (1 + 5 * shape->n_layers + 2) + 2;
+}
+
+extern "C" MTT_B200_API int mtt_b200_launch_local_ar_frame(const mtt_b200_local_ar_shape_t* shape,
+                                                          const mtt_b200_local_ar_weights_t* w,
+                                                          const mtt_b200_sampling_config_t* sampling,
+                                                          const mtt_b200_stream_batch_t* b, void* workspace,
+                                                          size_t workspace_bytes, void* stream) {
+  using namespace mtt;
+  if (!shape_ok(shape) || !w || !sampling || !b || !workspace || b->n_streams <= 0) {
+    return MTT_B200_STATUS_INVALID_ARGUMENT;
+  }
+  const bool in_proj = shape->d_model != kEmbed;
+  if (!w->pos || !w->ln_self || !w->qkv || !w->o || !w->ln_ff || !w->ffn1 || !w->ffn2 || !w->head_w || !w->head_b ||
+      !w->emb || (in_proj && (!w->in_proj_w || !w->in_proj_b)) || (w->final_w == nullptr) != (w->final_b == nullptr)) {
+    return MTT_B200_STATUS_INVALID_ARGUMENT;
+  }
+  if (!b->decoder_hidden || !b->unfinished || !b->finished || !b->forbid_eos || !b->rng_seed || !b->rng_counter ||
+      !b->codec_tokens || !b->invalid_rows || !b->end_frame_index || !b->next_embedding) {
+    return MTT_B200_STATUS_INVALID_ARGUMENT;
+  }
+  if (sampling->top_k < 1 || sampling->top_k > kVocab || !(sampling->temperature > 0.f) ||
+      (reinterpret_cast<uintptr_t>(workspace) & 255u) != 0) {
+    return MTT_B200_STATUS_INVALID_ARGUMENT;
+  }
+  const int rp = sampling->cfg ? 2 : 1;
+  const Layout lo = make_layout(shape->d_model, shape->n_layers, shape->d_ffn, b->n_streams, rp);
+  if (workspace_bytes < lo.total) return MTT_B200_STATUS_INVALID_ARGUMENT;
+
+  Frame f{};
+  f.d = shape->d_model;
+  f.L = shape->n_layers;
+  f.H = shape->n_heads;
+  f.F = shape->d_ffn;
+  f.rp = rp;
+  f.n = b->n_streams;
+  f.in_proj = in_proj;
+  f.prm = SamplingParams{sampling->top_k, sampling->temperature, sampling->cfg_scale, sampling->argmax};
+  auto B = [](const void* p) { return static_cast<const bf16*>(p); };
+  f.in_w = B(w->in_proj_w);
+  f.in_b = B(w->in_proj_b);
+  f.pos = B(w->pos);
+  f.ln1 = B(w->ln_self);
+  f.qkv = B(w->qkv);
+  f.o = B(w->o);
+  f.ln2 = B(w->ln_ff);
+  f.w1 = B(w->ffn1);
+  f.w2 = B(w->ffn2);
+  f.head_w = B(w->head_w);
+  f.head_b = B(w->head_b);
+  f.emb = B(w->emb);
+  f.final_w = B(w->final_w);
+  f.final_b = B(w->final_b);
+  f.hidden = B(b->decoder_hidden);
+  f.unfinished = b->unfinished;
+  f.finished = b->finished;
+  f.forbid = b->forbid_eos;
+  f.active = b->active;
+  f.seed = b->rng_seed;
+  f.counter_io = b->rng_counter;
+  f.codec_tokens = b->codec_tokens;
+  f.invalid_rows = b->invalid_rows;
+  f.end_frame = b->end_frame_index;
+  f.next_emb = static_cast<bf16*>(b->next_embedding);
+  f.forced = b->forced_tokens;
+  f.logits_out = static_cast<bf16*>(b->logits_out);
+  char* ws = static_cast<char*>(workspace);
+  f.list = reinterpret_cast<int32_t*>(ws + lo.list);
+  f.count = reinterpret_cast<int32_t*>(ws + lo.count);
+  f.eos_list = reinterpret_cast<int32_t*>(ws + lo.eos_list);
+  f.eos_count = reinterpret_cast<int32_t*>(ws + lo.eos_count);
+  f.eos_slot = reinterpret_cast<int32_t*>(ws + lo.eos_slot);
+  f.x = reinterpret_cast<bf16*>(ws + lo.x);
+  f.q = reinterpret_cast<bf16*>(ws + lo.q);
+  f.kc = reinterpret_cast<bf16*>(ws + lo.kc);
+  f.vc = reinterpret_cast<bf16*>(ws + lo.vc);
+  f.att = reinterpret_cast<bf16*>(ws + lo.att);
+  f.h = reinterpret_cast<bf16*>(ws + lo.h);
+  f.logits = reinterpret_cast<bf16*>(ws + lo.logits);
+  f.tokens = reinterpret_cast<int32_t*>(ws + lo.tokens);
+  f.emb_acc = reinterpret_cast<float*>(ws + lo.emb_acc);
+  f.ctr = reinterpret_cast<int64_t*>(ws + lo.ctr);
+  f.inv = reinterpret_cast<int32_t*>(ws + lo.inv);
+  f.eos_partial = reinterpret_cast<float*>(ws + lo.eos_partial);
+  f.eos_logit = reinterpret_cast<float*>(ws + lo.eos_logit);
+
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int d = f.d, F = f.F;
+  frame_begin_kernel<<<1, kBeginThreads, 0, st>>>(f);
+  for (int p = 0; p < kPositions; ++p) {
+    if (in_proj) {
+      if (p == 0) {
+        launch_linear<kProHidden, kEpiInProj>(f, st, p, 0, d, kEmbed, f.in_w, f.in_b);
+      } else {
+        launch_linear<kProGather, kEpiInProj>(f, st, p, 0, d, kEmbed, f.in_w, f.in_b);
+      }
+    } else {
+      add_pos_kernel<<<148 * 4, 256, 0, st>>>(f, p);
+    }
+    for (int l = 0; l < f.L; ++l) {
+      const int64_t dd = static_cast<int64_t>(d) * d;
+      launch_linear<kProLn1, kEpiQkv>(f, st, p, l, 3 * d, d, f.qkv + l * 3 * dd, nullptr);
+      const int warps = f.n * f.rp * f.H;
+      attention_kernel<<<(warps + 7) / 8, 256, 0, st>>>(f, p, l);
+      launch_linear<kProAtt, kEpiResid>(f, st, p, l, d, d, f.o + l * dd, nullptr);
+      launch_linear<kProLn2, kEpiGelu>(f, st, p, l, F, d, f.w1 + static_cast<int64_t>(l) * F * d, nullptr);
+      launch_linear<kProH, kEpiResid>(f, st, p, l, d, F, f.w2 + static_cast<int64_t>(l) * F * d, nullptr);
+    }
+    launch_linear<kProX, kEpiHead>(f, st, p, 0, kVocab, d, f.head_w + static_cast<int64_t>(p) * kVocab * d,
+                                   f.head_b + static_cast<int64_t>(p) * kVocab);
+    sample_kernel<<<f.n, kSampleThreads, 0, st>>>(f, p);
+  }
+  EosArgs ea;
+  ea.hidden = f.hidden;
+  ea.hidden_stream_stride = static_cast<int64_t>(rp) * kEmbed;
+  ea.uncond_offset = rp == 2 ? kEmbed : 0;
+  ea.weight = f.final_w;
+  ea.bias = f.final_b;
+  ea.cfg_scale = rp == 2 ? f.prm.cfg_scale : 1.0f;
+  ea.eos_list = f.eos_list;
+  ea.eos_count = f.eos_count;
+  ea.partial_max = f.eos_partial;
+  ea.eos_logit = f.eos_logit;
+  eos_project_kernel<<<dim3(kEosChunks, kPositions), kEosThreads, 0, st>>>(ea);
+  frame_end_kernel<<<f.n, 256, 0, st>>>(f);
+  return cudaPeekAtLastError() == cudaSuccess ? MTT_B200_STATUS_OK : MTT_B200_STATUS_CUDA_ERROR;
+}

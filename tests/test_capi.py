@@ -1,0 +1,101 @@
+"""C-ABI library checks that need no GPU: the library loads, exports every
+symbol include/*.h declares (and nothing else), the plugin ABI structs are
+byte-compatible with the reference's, and the host-only entry points follow
+the reference's status conventions."""
+import ctypes
+import glob
+import os
+import re
+import subprocess
+
+import pytest
+
+REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+from magpie_tts_rt_b200 import _lib as L  # noqa: E402  (raises if the .so is missing)
+from magpie_tts_rt_b200 import local_ar  # noqa: E402
+
+
+def declared_symbols():
+    names = set()
+    for h in glob.glob(os.path.join(REPO, "include", "*.h")):
+        text = open(h).read()
+        for m in re.finditer(r"MTT_B200_API\s+[\w\s\*]+?\b(mtt_\w+)\s*\(", text):
+            names.add(m.group(1))
+    return names
+
+
+def exported_symbols():
+    out = subprocess.run(["nm", "-D", "--defined-only", L.LIBRARY], capture_output=True, text=True,
+                         check=True).stdout
+    return {line.split()[-1] for line in out.splitlines() if " T " in line}
+
+
+def test_exports_match_header():
+    declared = declared_symbols()
+    assert len(declared) >= 11
+    exported = exported_symbols()
+    assert declared == exported, (declared ^ exported)
+    for name in declared:
+        assert hasattr(L.lib, name)
+
+
+def test_struct_layout_matches_reference():
+    # sizeof / offsetof measured with gcc on the reference's
+    # include/magpie_tts_rt/magpie_tts_rt_plugin.h:70-146 (x86-64 / aarch64 LP64)
+    assert ctypes.sizeof(L.PluginCreatorV1) == 152
+    assert ctypes.sizeof(L.PluginApiV1) == 816
+    assert L.PluginApiV1.register_plugins.offset == 776
+    assert ctypes.sizeof(L.MainDevicePositionClassV1) == 344
+    assert ctypes.sizeof(L.MainDevicePositionKV1) == 80
+    assert ctypes.sizeof(L.MainDevicePositionClassTableV1) == 27192
+    assert L.MainDevicePositionClassTableV1.k_records.offset == 7240
+
+
+def test_plugin_api_negotiation():
+    """plugins/local_ar_plugins.cu:4858-4900 semantics."""
+    assert L.lib.mtt_plugin_get_api_v1(None) == 2  # INVALID_ARGUMENT
+    status, _ = local_ar.plugin_api(struct_size=ctypes.sizeof(L.PluginApiV1) - 8)
+    assert status == 3  # ABI_MISMATCH
+    status, _ = local_ar.plugin_api(abi_version=2)
+    assert status == 3
+    status, api = local_ar.plugin_api()
+    assert status == 0
+    assert api.struct_size == 816 and api.abi_version == 1 and api.creator_count == 5
+    names = [c.name.decode() for c in api.creators]
+    assert names == ["MagpieLocalARSampling", "MagpieLocalAREos", "MagpieLayerNorm",
+                     "MagpieGeluTanh", "MagpieSoftmax"]
+    for c in api.creators:
+        assert c.struct_size == 152 and c.abi_version == 1
+        assert c.version.decode() == "1" and c.plugin_namespace.decode() == "magpie_tts_rt"
+    # no TensorRT in this build: the registry is unavailable
+    assert api.register_plugins() == 4
+
+
+def test_class_table_never_ready():
+    assert L.lib.mtt_plugin_get_main_device_position_class_table_v1(None) == 2
+    status, _ = local_ar.main_device_position_class_table(struct_size=100)
+    assert status == 3
+    status, _ = local_ar.main_device_position_class_table()
+    assert status == 7  # NOT_READY
+
+
+def test_workspace_sizes():
+    # aligned(16*2017*4, 256) + 2*4, the reference's local_ar_eos_workspace_size
+    assert local_ar.local_ar_eos_workspace_size() == 129288
+    ok = L.Shape(256, 1, 4, 1024)
+    assert L.lib.mtt_b200_local_ar_frame_workspace_size(ctypes.byref(ok), 64, 1) > 0
+    assert L.lib.mtt_b200_local_ar_frame_workspace_size(ctypes.byref(L.Shape(768, 2, 12, 3072)), 1, 1) > 0
+    bad = L.Shape(256, 1, 3, 1024)  # head width must be 64
+    assert L.lib.mtt_b200_local_ar_frame_workspace_size(ctypes.byref(bad), 64, 1) == 0
+    assert L.lib.mtt_b200_local_ar_frame_workspace_size(ctypes.byref(ok), 0, 1) == 0
+    assert L.lib.mtt_b200_local_ar_frame_launch_count(ctypes.byref(ok), 64, 0) == 16 * 8 + 3
+
+
+def test_null_arguments_rejected_without_launch():
+    """Null pointers return -1 before any CUDA call (local_ar_plugins.cu:4141-4147)."""
+    assert L.lib.mtt_b200_launch_local_ar_sampling(*([None] * 12)) == -1
+    assert L.lib.mtt_b200_launch_local_ar_eos(*([None] * 10)) == -1
+    assert L.lib.mtt_b200_launch_finalize_local_step(None, None, 0, *([None] * 8)) == -1
+    assert L.lib.mtt_b200_launch_test_clamped_gumbel(None, None, 4, None) == -1
+    assert L.lib.mtt_b200_launch_local_ar_frame(None, None, None, None, None, 0, None) == -1

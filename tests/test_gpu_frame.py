@@ -1,0 +1,244 @@
+"""GPU parity of the batched Local AR frame against the oracle.
+
+For every case:
+* logits: the oracle is teacher-forced on the GPU's own tokens and its
+  per-position logits must agree with the GPU's within the bf16 tolerance
+  (|gpu - oracle| <= 1e-2 * |oracle| + 1e-2 * rms(oracle row));
+* tokens / RNG counter / invalid flag: the C oracle sampler applied to the
+  GPU's logits must reproduce the GPU's tokens bit for bit;
+* next-frame embedding: bit-exact sequential bf16 sum of the GPU tokens' rows;
+* end_frame_index: the oracle EOS decision on the GPU tokens.
+"""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from magpie_tts_rt_b200.model import (
+    EMBED, POSITIONS, SHAPE_BASELINE, SHAPE_SOFIA, VOCAB, LocalArShape, make_weights,
+)
+from oracle import lt_oracle
+from oracle import sampler as S
+
+pytestmark = pytest.mark.gpu
+
+RTOL = 1e-2
+
+
+def bits(t):
+    return t.contiguous().view(torch.int16).cpu().numpy().view(np.uint16)
+
+
+def from_bits(b):
+    return torch.from_numpy(np.ascontiguousarray(b).view(np.int16)).view(torch.bfloat16)
+
+
+_weights_cache = {}
+
+
+def weights(shape, seed, with_final=True):
+    key = (shape, seed, with_final)
+    if key not in _weights_cache:
+        _weights_cache[key] = make_weights(shape, seed=seed, dtype=torch.bfloat16, profile="parity",
+                                           with_final=with_final)
+    return _weights_cache[key]
+
+
+def run_gpu(engine, hidden, flags, seed, counter, forced=None, active=None, sentinel=False):
+    from magpie_tts_rt_b200.local_ar import StreamBatch
+    n = hidden.shape[0]
+    cfg = hidden.dim() == 3
+    rows = 2 if cfg else 1
+    b = StreamBatch.allocate(n, cfg=cfg)
+    b.decoder_hidden.copy_(hidden.reshape(n, rows, EMBED))
+    uf, fi, fb = (torch.as_tensor(np.asarray(f, dtype=bool)).cuda() for f in flags)
+    b.unfinished.copy_(uf); b.finished.copy_(fi); b.forbid_eos.copy_(fb)
+    b.rng_seed.copy_(torch.as_tensor(np.asarray(seed, dtype=np.int64)))
+    b.rng_counter.copy_(torch.as_tensor(np.asarray(counter, dtype=np.int64)))
+    b.logits_out = torch.zeros(n, POSITIONS, rows, VOCAB, dtype=torch.bfloat16, device="cuda")
+    if sentinel:
+        b.codec_tokens.fill_(-7); b.invalid_rows.fill_(-7); b.end_frame_index.fill_(-7)
+        b.next_embedding.fill_(7.0)
+    if forced is not None:
+        b.forced_tokens = torch.as_tensor(forced, dtype=torch.int64).cuda()
+    if active is not None:
+        b.active = torch.as_tensor(np.asarray(active, dtype=bool)).cuda()
+    engine.frame(b)
+    torch.cuda.synchronize()
+    codec = b.codec_tokens.cpu().numpy()
+    return dict(
+        codec=codec,
+        tokens=np.stack([codec[s].T.reshape(-1) for s in range(n)]),  # position-major
+        counter=b.rng_counter.cpu().numpy(), invalid=b.invalid_rows.cpu().numpy(),
+        end=b.end_frame_index.cpu().numpy(), next_emb=bits(b.next_embedding),
+        logits=bits(b.logits_out),
+    )
+
+
+def check_logits(gpu_bits, ref_bits, what):
+    g = S.bf16_bits_to_f32(gpu_bits).astype(np.float64)
+    r = S.bf16_bits_to_f32(ref_bits).astype(np.float64)
+    rms = np.sqrt(np.mean(r * r, axis=-1, keepdims=True))
+    err = np.abs(g - r)
+    bound = RTOL * np.abs(r) + RTOL * rms
+    worst = float(np.max(err / (np.abs(r) + rms)))
+    assert (err <= bound).all(), f"{what}: {int((err > bound).sum())} logits out of tolerance, worst {worst:.4g}"
+    return worst
+
+
+def check_frame(w, hidden, flags, seed, counter, gpu, params=S.SamplingParams(), streams=None):
+    cfg = hidden.dim() == 3
+    n = hidden.shape[0]
+    streams = range(n) if streams is None else streams
+    uf, fi, fb = (np.broadcast_to(np.asarray(f, dtype=bool), (n,)) for f in flags)
+    seed = np.broadcast_to(np.asarray(seed, dtype=np.int64), (n,))
+    counter = np.broadcast_to(np.asarray(counter, dtype=np.int64), (n,))
+    sel = list(streams)
+    r = lt_oracle.run_frame(w, hidden[sel], uf[sel], fi[sel], fb[sel], seed[sel], counter[sel], params,
+                            teacher_tokens=gpu["tokens"][sel], record_logits=True, eos=False)
+    rows = 2 if cfg else 1
+    worst = check_logits(gpu["logits"][sel], r.logits.reshape(len(sel), POSITIONS, rows, VOCAB), "logits")
+    emb_bits = bits(w.emb)
+    fw, fbias = (bits(w.final_w), bits(w.final_b)) if w.final_w.numel() else (None, None)
+    for j, s in enumerate(sel):
+        ctr = int(counter[s])
+        inv = 0
+        for p in range(POSITIONS):
+            lg = gpu["logits"][s, p]
+            lg_in = lg[None] if cfg else lg[:1]
+            tok, c2, iv = S.sample(lg_in, uf[s], fi[s], fb[s], seed[s], ctr, params)
+            assert tok[0] == gpu["tokens"][s, p], (s, p)
+            ctr = int(c2[0])
+            inv = max(inv, int(iv[0]))
+        assert gpu["counter"][s] == ctr, s
+        assert gpu["invalid"][s] == inv, s
+        np.testing.assert_array_equal(gpu["next_emb"][s], S.embedding_sum(emb_bits, gpu["tokens"][s]))
+        enabled = not (uf[s] or fi[s] or fb[s])
+        guided = None
+        if enabled and fw is not None:
+            hb = bits(hidden[s].reshape(rows, EMBED))
+            if not cfg:
+                hb = np.concatenate([hb, hb])
+            guided = S.eos_guided(hb, fw, fbias, params.cfg_scale if cfg else 1.0)
+        exp_end = S.eos_end_frame(guided, S.codec_layout(gpu["tokens"][s]), uf[s], fi[s], fb[s])
+        assert gpu["end"][s] == exp_end, (s, gpu["end"][s], exp_end)
+    return worst
+
+
+@pytest.fixture(scope="module")
+def engines():
+    from magpie_tts_rt_b200.local_ar import LocalArEngine
+    cache = {}
+
+    def get(shape, seed, max_streams, cfg=True, argmax=False, with_final=True):
+        key = (shape, seed, max_streams, cfg, argmax, with_final)
+        if key not in cache:
+            cache[key] = LocalArEngine(weights(shape, seed, with_final), max_streams=max_streams, cfg=cfg,
+                                       argmax=argmax)
+        return cache[key]
+    return get
+
+
+def _hidden(n, seed, cfg=True):
+    g = torch.Generator().manual_seed(seed)
+    return torch.randn(n, 2 if cfg else 1, EMBED, generator=g).to(torch.bfloat16).reshape(
+        (n, 2, EMBED) if cfg else (n, EMBED))
+
+
+FLAGS6 = ([0, 1, 0, 0, 0, 1], [0, 0, 0, 1, 0, 1], [0, 0, 1, 0, 0, 0])  # incl. an invalid overlap
+
+
+@pytest.mark.parametrize("shape,n", [(SHAPE_BASELINE, 6), (SHAPE_SOFIA, 3)])
+def test_frame_matches_oracle(engines, shape, n):
+    w = weights(shape, 21)
+    eng = engines(shape, 21, 8)
+    hidden = _hidden(n, 5)
+    flags = tuple(np.asarray(f[:n]) for f in FLAGS6)
+    seed = np.array([1234, 0, 7, (1 << 32) - 1, 99, 5][:n])
+    counter = np.array([0, 16, 3200, 48, S.MAX_COUNTER - 3, 0][:n])
+    gpu = run_gpu(eng, hidden, flags, seed, counter)
+    check_frame(w, hidden, flags, seed, counter, gpu)
+
+
+def test_frame_sequence_counters(engines):
+    """Three consecutive frames of 4 sessions: the counter advances by 16 per
+    frame and every frame matches the oracle (sequence_contract.py:95-160)."""
+    shape = SHAPE_BASELINE
+    w = weights(shape, 22)
+    eng = engines(shape, 22, 4)
+    seed = np.array([1234, 1, 2, 3])
+    counter = np.zeros(4, np.int64)
+    for f in range(3):
+        hidden = _hidden(4, 100 + f)
+        forbid = np.full(4, f < 2)
+        flags = (np.zeros(4, bool), np.zeros(4, bool), forbid)
+        gpu = run_gpu(eng, hidden, flags, seed, counter)
+        check_frame(w, hidden, flags, seed, counter, gpu)
+        np.testing.assert_array_equal(gpu["counter"], counter + 16)
+        if f < 2:
+            assert (gpu["end"] == -1).all()
+        counter = gpu["counter"]
+
+
+def test_inactive_streams_untouched(engines):
+    shape = SHAPE_BASELINE
+    w = weights(shape, 21)
+    eng = engines(shape, 21, 8)
+    n = 5
+    hidden = _hidden(n, 9)
+    flags = (np.zeros(n, bool), np.zeros(n, bool), np.ones(n, bool))
+    seed = np.arange(n) + 10
+    counter = np.arange(n) * 16
+    active = np.array([1, 0, 1, 0, 1], bool)
+    gpu = run_gpu(eng, hidden, flags, seed, counter, active=active, sentinel=True)
+    for s in np.nonzero(~active)[0]:
+        assert (gpu["codec"][s] == -7).all() and gpu["invalid"][s] == -7 and gpu["end"][s] == -7
+        assert gpu["counter"][s] == counter[s]
+    check_frame(w, hidden, flags, seed, counter, gpu, streams=np.nonzero(active)[0])
+
+
+def test_argmax_without_cfg(engines):
+    """Greedy decoding, one row per stream (config 1's mode, bf16 on the GPU):
+    no RNG, counter unchanged (magpietts_fused_sampling.py:136-197)."""
+    shape = SHAPE_BASELINE
+    w = weights(shape, 23)
+    eng = engines(shape, 23, 4, cfg=False, argmax=True)
+    n = 3
+    hidden = _hidden(n, 11, cfg=False)
+    flags = (np.array([0, 1, 0], bool), np.zeros(n, bool), np.array([0, 0, 1], bool))
+    seed = np.zeros(n, np.int64)
+    counter = np.array([0, 5, 17])
+    gpu = run_gpu(eng, hidden, flags, seed, counter)
+    check_frame(w, hidden, flags, seed, counter, gpu, params=S.SamplingParams(argmax=True))
+    np.testing.assert_array_equal(gpu["counter"], counter)
+
+
+@pytest.mark.parametrize("name", ["A_bf16_cfg", "R_bf16_cfg"])
+def test_frame_against_reference_golden(engines, golden, golden_dir, name):
+    """Teacher-forced on the reference's tokens, the GPU logits match the NeMo
+    oracle's recorded logits within tolerance."""
+    meta = golden["lt_frames"][name]
+    z = np.load(os.path.join(golden_dir, "lt_frames.npz"))
+    shape = LocalArShape(meta["d_model"], meta["n_layers"], meta["n_heads"], meta["d_ffn"])
+    eng = engines(shape, meta["weights_seed"], 1, with_final=False)
+    for f, fr in enumerate(meta["frames"]):
+        hidden = from_bits(z[f"{name}/f{f}/hidden"]).reshape(1, 2, EMBED)
+        ref_tokens = z[f"{name}/f{f}/tokens"]
+        flags = tuple(np.array([v], bool) for v in fr["flags"])
+        gpu = run_gpu(eng, hidden, flags, [meta["seed"]], [fr["counter_in"]], forced=ref_tokens[None])
+        check_logits(gpu["logits"][0], z[f"{name}/f{f}/logits"].reshape(POSITIONS, 2, VOCAB), name)
+
+
+def test_batch_of_64_streams(engines):
+    """Config 3's batch size: 64 sessions x CFG pair, seeds 0..63."""
+    shape = SHAPE_BASELINE
+    w = weights(shape, 24)
+    eng = engines(shape, 24, 64)
+    n = 64
+    hidden = _hidden(n, 12)
+    flags = (np.ones(n, bool), np.zeros(n, bool), np.zeros(n, bool))
+    seed = np.arange(n)
+    counter = np.full(n, 32)
+    gpu = run_gpu(eng, hidden, flags, seed, counter)
+    check_frame(w, hidden, flags, seed, counter, gpu, streams=range(0, 64, 7))
