@@ -2,8 +2,9 @@
 
 For every case:
 * logits: the oracle is teacher-forced on the GPU's own tokens and its
-  per-position logits must agree with the GPU's within the bf16 tolerance
-  (|gpu - oracle| <= 1e-2 * |oracle| + 1e-2 * rms(oracle row));
+  per-position logits must agree with the GPU's within the bf16 tolerance:
+  every 2024-wide logits row within 1e-2 relative L2 error, and no single
+  logit further than 5e-2 x the row RMS;
 * tokens / RNG counter / invalid flag: the C oracle sampler applied to the
   GPU's logits must reproduce the GPU's tokens bit for bit;
 * next-frame embedding: bit-exact sequential bf16 sum of the GPU tokens' rows;
@@ -76,15 +77,23 @@ def run_gpu(engine, hidden, flags, seed, counter, forced=None, active=None, sent
     )
 
 
-def check_logits(gpu_bits, ref_bits, what):
+def logit_errors(gpu_bits, ref_bits):
+    """Per logits row: relative L2 error and max element error / row RMS."""
     g = S.bf16_bits_to_f32(gpu_bits).astype(np.float64)
     r = S.bf16_bits_to_f32(ref_bits).astype(np.float64)
-    rms = np.sqrt(np.mean(r * r, axis=-1, keepdims=True))
-    err = np.abs(g - r)
-    bound = RTOL * np.abs(r) + RTOL * rms
-    worst = float(np.max(err / (np.abs(r) + rms)))
-    assert (err <= bound).all(), f"{what}: {int((err > bound).sum())} logits out of tolerance, worst {worst:.4g}"
-    return worst
+    rms = np.sqrt(np.mean(r * r, axis=-1))
+    rel_l2 = np.linalg.norm(g - r, axis=-1) / np.linalg.norm(r, axis=-1)
+    max_rel = np.max(np.abs(g - r), axis=-1) / rms
+    return rel_l2, max_rel
+
+
+def check_logits(gpu_bits, ref_bits, what):
+    """bf16 tolerance: every logits row within 1e-2 relative (L2), and no
+    single logit further than 5e-2 of the row RMS from the oracle."""
+    rel_l2, max_rel = logit_errors(gpu_bits, ref_bits)
+    assert rel_l2.max() <= RTOL, f"{what}: relative L2 error {rel_l2.max():.4g} > {RTOL}"
+    assert max_rel.max() <= 5 * RTOL, f"{what}: max element error {max_rel.max():.4g} x row RMS"
+    return float(rel_l2.max())
 
 
 def check_frame(w, hidden, flags, seed, counter, gpu, params=S.SamplingParams(), streams=None):
@@ -242,3 +251,29 @@ def test_batch_of_64_streams(engines):
     counter = np.full(n, 32)
     gpu = run_gpu(eng, hidden, flags, seed, counter)
     check_frame(w, hidden, flags, seed, counter, gpu, streams=range(0, 64, 7))
+
+
+def test_gpu_no_further_from_exact_than_oracle(engines):
+    """Both bf16 implementations drift from exact arithmetic by rounding; the
+    GPU must be no further from an f32 evaluation of the same bf16 weights
+    and inputs (same token history) than the PyTorch-CPU bf16 oracle is."""
+    shape = SHAPE_SOFIA
+    w = weights(shape, 21)
+    eng = engines(shape, 21, 8)
+    n = 3
+    hidden = _hidden(n, 5)
+    flags = (np.zeros(n, bool), np.zeros(n, bool), np.ones(n, bool))
+    seed = np.array([1, 2, 3])
+    counter = np.zeros(n, np.int64)
+    gpu = run_gpu(eng, hidden, flags, seed, counter)
+    r16 = lt_oracle.run_frame(w, hidden, *flags, seed, counter, teacher_tokens=gpu["tokens"],
+                              record_logits=True, eos=False)
+    w32 = w.to(torch.float32)
+    r32 = lt_oracle.run_frame(w32, hidden.float(), *flags, seed, counter,
+                              params=S.SamplingParams(), teacher_tokens=gpu["tokens"], record_logits=True,
+                              eos=False)
+    exact = S.f32_to_bf16_bits(r32.logits.reshape(n, POSITIONS, 2, VOCAB).astype(np.float32))
+    gpu_err, _ = logit_errors(gpu["logits"], exact)
+    cpu_err, _ = logit_errors(r16.logits.reshape(n, POSITIONS, 2, VOCAB), exact)
+    assert gpu_err.mean() <= 1.5 * cpu_err.mean() + 1e-4, (gpu_err.mean(), cpu_err.mean())
+    assert gpu_err.max() <= 2.0 * cpu_err.max() + 1e-4, (gpu_err.max(), cpu_err.max())
