@@ -245,17 +245,44 @@ typedef struct mtt_b200_local_ar_weights {
   const void* emb;       /* [16][2024][768] audio embedding tables */
   const void* final_w;   /* [32384][768] Main Decoder final projection (EOS) */
   const void* final_b;   /* [32384] */
+  /* Optional [16][2024][d] bf16: the in-projection folded into the embedding
+   * tables, emb_proj[p][v] = bf16(W_in table_p[v] + b_in), made once by
+   * mtt_b200_launch_fold_in_projection.  When present, positions 1..15 read
+   * their in-projected input row from it instead of multiplying the gathered
+   * 768-wide row by W_in (same rounding points: f32 accumulation, one bf16
+   * rounding, then the position add).  NULL: multiply at every position. */
+  const void* emb_proj;
 } mtt_b200_local_ar_weights_t;
+
+/* Bytes of the folded table for a shape (0 for identity in-projections). */
+MTT_B200_API size_t mtt_b200_fold_in_projection_bytes(const mtt_b200_local_ar_shape_t* shape);
+
+/* Computes emb_proj (see above) from weights->emb, in_proj_w, in_proj_b into
+ * `out` (mtt_b200_fold_in_projection_bytes bytes, 16-byte aligned).  A one-time
+ * weight transform, run when the weights are loaded.  Returns MTT_B200_STATUS_*. */
+MTT_B200_API int mtt_b200_launch_fold_in_projection(const mtt_b200_local_ar_shape_t* shape,
+                                                   const mtt_b200_local_ar_weights_t* weights, void* out,
+                                                   void* stream);
+
+/* Frame implementations: AUTO picks the fused cluster kernel when the shape
+ * (d_model 256, 4 heads, FFN 1024, 1 layer) and the device (16-CTA clusters
+ * with 220 KB of shared memory each) support it, else the phase kernels. */
+#define MTT_B200_FRAME_PATH_AUTO 0
+#define MTT_B200_FRAME_PATH_PHASE_KERNELS 1
+#define MTT_B200_FRAME_PATH_FUSED_CLUSTER 2
 
 /* Sampling configuration; the reference's values are 80 / 0.6 / 2.5 with CFG
  * and top-k.  argmax != 0 selects greedy decoding (no RNG, counter unchanged;
- * magpietts_fused_sampling.py:136-197).  cfg == 0 runs one row per stream. */
+ * magpietts_fused_sampling.py:136-197).  cfg == 0 runs one row per stream.
+ * path: MTT_B200_FRAME_PATH_*; requesting the fused path where it cannot run
+ * returns MTT_B200_STATUS_UNSUPPORTED. */
 typedef struct mtt_b200_sampling_config {
   int32_t top_k;
   float temperature;
   float cfg_scale;
   int32_t argmax;
   int32_t cfg;
+  int32_t path;
 } mtt_b200_sampling_config_t;
 
 /*
@@ -325,10 +352,17 @@ MTT_B200_API int mtt_b200_launch_local_ar_frame_static_workspace(const mtt_b200_
                                                                 const mtt_b200_stream_batch_t* batch,
                                                                 void* stream);
 
-/* Number of kernels mtt_b200_launch_local_ar_frame enqueues for this batch
- * shape (for launch accounting). */
+/* The path (MTT_B200_FRAME_PATH_PHASE_KERNELS or _FUSED_CLUSTER) that
+ * mtt_b200_launch_local_ar_frame takes for this shape and configuration on
+ * the current device, or MTT_B200_STATUS_UNSUPPORTED. */
+MTT_B200_API int32_t mtt_b200_local_ar_frame_path(const mtt_b200_local_ar_shape_t* shape,
+                                                  const mtt_b200_sampling_config_t* sampling);
+
+/* Number of kernels mtt_b200_launch_local_ar_frame enqueues for this shape,
+ * configuration and batch on the current device (for launch accounting). */
 MTT_B200_API int32_t mtt_b200_local_ar_frame_launch_count(const mtt_b200_local_ar_shape_t* shape,
-                                                          int32_t n_streams, int32_t eos_enabled);
+                                                          const mtt_b200_sampling_config_t* sampling,
+                                                          int32_t n_streams);
 
 /* ------------------------------------------------------------------------ */
 /* Test hooks (no reference counterpart beyond launch_test_clamped_gumbel,   */

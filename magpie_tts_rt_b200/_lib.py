@@ -88,12 +88,17 @@ class Shape(ctypes.Structure):
 class Weights(ctypes.Structure):
     _fields_ = [(n, P) for n in (
         "in_proj_w", "in_proj_b", "pos", "ln_self", "qkv", "o", "ln_ff", "ffn1", "ffn2",
-        "head_w", "head_b", "emb", "final_w", "final_b")]
+        "head_w", "head_b", "emb", "final_w", "final_b", "emb_proj")]
 
 
 class SamplingConfig(ctypes.Structure):
     _fields_ = [("top_k", I32), ("temperature", ctypes.c_float), ("cfg_scale", ctypes.c_float),
-                ("argmax", I32), ("cfg", I32)]
+                ("argmax", I32), ("cfg", I32), ("path", I32)]
+
+
+PATH_AUTO = 0
+PATH_PHASE_KERNELS = 1
+PATH_FUSED_CLUSTER = 2
 
 
 class StreamBatch(ctypes.Structure):
@@ -120,7 +125,12 @@ SIGNATURES = {
     "mtt_b200_launch_local_ar_frame": (
         I32, [ctypes.POINTER(Shape), ctypes.POINTER(Weights), ctypes.POINTER(SamplingConfig),
               ctypes.POINTER(StreamBatch), P, SZ, P]),
-    "mtt_b200_local_ar_frame_launch_count": (I32, [ctypes.POINTER(Shape), I32, I32]),
+    "mtt_b200_local_ar_frame_launch_count": (
+        I32, [ctypes.POINTER(Shape), ctypes.POINTER(SamplingConfig), I32]),
+    "mtt_b200_local_ar_frame_path": (I32, [ctypes.POINTER(Shape), ctypes.POINTER(SamplingConfig)]),
+    "mtt_b200_fold_in_projection_bytes": (SZ, [ctypes.POINTER(Shape)]),
+    "mtt_b200_launch_fold_in_projection": (
+        I32, [ctypes.POINTER(Shape), ctypes.POINTER(Weights), P, P]),
     "mtt_b200_launch_test_clamped_gumbel": (I32, [P, P, SZ, P]),
     "mtt_b200_launch_test_log": (I32, [P, P, SZ, P]),
 }

@@ -72,7 +72,7 @@ def build(force: bool = False, verbose_ptxas: bool = False) -> str:
         with open(vs, "w") as fh:
             fh.write(VERSION_SCRIPT)
         cmd = [NVCC] + ARCH + ["-shared", "-cudart", "static", "-o", LIBRARY] + objs + [
-            "-Xlinker", "--version-script=" + vs, "-lcuda"]
+            "-Xlinker", "--version-script=" + vs]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")

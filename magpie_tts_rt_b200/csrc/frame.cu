@@ -35,79 +35,16 @@
 
 #include "../../include/magpie_tts_rt_b200.h"
 #include "eos.cuh"
+#include "frame_common.cuh"
 #include "sampling.cuh"
 
 namespace mtt {
 namespace {
 
-using bf16 = __nv_bfloat16;
-
 constexpr int kLinThreads = 256;
 constexpr int kBM = 8;   // rows per linear tile (one warp per row in the prologue)
 constexpr int kBN = 32;  // output features per linear tile
 constexpr int kBeginThreads = 1024;
-
-struct Frame {
-  int d, L, H, F, rp, n, in_proj;
-  SamplingParams prm;
-  const bf16 *in_w, *in_b, *pos, *ln1, *qkv, *o, *ln2, *w1, *w2, *head_w, *head_b, *emb, *final_w, *final_b;
-  const bf16* hidden;
-  const bool *unfinished, *finished, *forbid, *active;
-  const int64_t* seed;
-  int64_t* counter_io;
-  int64_t* codec_tokens;
-  int32_t* invalid_rows;
-  int32_t* end_frame;
-  bf16* next_emb;
-  const int64_t* forced;
-  bf16* logits_out;
-  // workspace
-  int32_t *list, *count, *eos_list, *eos_count, *eos_slot;
-  bf16 *x, *q, *kc, *vc, *att, *h, *logits;
-  int32_t* tokens;
-  float* emb_acc;
-  int64_t* ctr;
-  int32_t* inv;
-  float *eos_partial, *eos_logit;
-};
-
-struct Layout {
-  size_t list, count, eos_list, eos_count, eos_slot, x, q, kc, vc, att, h, logits, tokens, emb_acc, ctr, inv,
-      eos_partial, eos_logit, total;
-};
-
-inline size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
-
-Layout make_layout(int d, int L, int F, int n, int rp) {
-  Layout lo{};
-  size_t off = 0;
-  auto take = [&](size_t bytes) {
-    const size_t at = off;
-    off = align256(off + bytes);
-    return at;
-  };
-  const size_t R = static_cast<size_t>(n) * rp;
-  lo.list = take(4 * static_cast<size_t>(n));
-  lo.count = take(4);
-  lo.eos_list = take(4 * static_cast<size_t>(n));
-  lo.eos_count = take(4);
-  lo.eos_slot = take(4 * static_cast<size_t>(n));
-  lo.x = take(2 * R * d);
-  lo.q = take(2 * R * d);
-  lo.kc = take(2 * static_cast<size_t>(L) * R * kPositions * d);
-  lo.vc = take(2 * static_cast<size_t>(L) * R * kPositions * d);
-  lo.att = take(2 * R * d);
-  lo.h = take(2 * R * F);
-  lo.logits = take(2 * R * kVocab);
-  lo.tokens = take(4 * static_cast<size_t>(n) * kPositions);
-  lo.emb_acc = take(4 * static_cast<size_t>(n) * kEmbed);
-  lo.ctr = take(8 * static_cast<size_t>(n));
-  lo.inv = take(4 * static_cast<size_t>(n));
-  lo.eos_partial = take(4 * static_cast<size_t>(n) * kPositions * kEosChunks);
-  lo.eos_logit = take(4 * static_cast<size_t>(n) * kPositions);
-  lo.total = off;
-  return lo;
-}
 
 // ---------------------------------------------------------------------------
 // frame begin: compact the active streams, choose EOS-enabled ones, init state
@@ -419,6 +356,7 @@ __global__ void __launch_bounds__(256) attention_kernel(Frame f, int p, int l) {
 
 __global__ void __launch_bounds__(kSampleThreads) sample_kernel(Frame f, int p) {
   __shared__ SampleShared sh;
+  __shared__ __align__(16) unsigned char scratch[kSampleScratchBytes];
   const int i = blockIdx.x;
   if (i >= *f.count) return;
   const int s = f.list[i];
@@ -432,7 +370,7 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(Frame f, int p) 
   c.seed = f.seed[s];
   c.counter = f.ctr[s];
   int invalid = 0;
-  const int token = sample_block(c, f.prm, sh, &invalid);
+  const int token = sample_block(c, f.prm, sh, scratch, &invalid);
   if (threadIdx.x == 0) {
     f.tokens[s * kPositions + p] = token;
     f.inv[s] |= invalid;
@@ -496,10 +434,45 @@ extern "C" MTT_B200_API size_t mtt_b200_local_ar_frame_workspace_size(const mtt_
   return mtt::make_layout(shape->d_model, shape->n_layers, shape->d_ffn, max_streams, cfg ? 2 : 1).total;
 }
 
+namespace {
+
+// Resolves the path for a shape / configuration on the current device.
+int32_t resolve_path(const mtt_b200_local_ar_shape_t* shape, const mtt_b200_sampling_config_t* sampling) {
+  mtt::Frame probe{};
+  probe.d = shape->d_model;
+  probe.L = shape->n_layers;
+  probe.H = shape->n_heads;
+  probe.F = shape->d_ffn;
+  probe.rp = sampling->cfg ? 2 : 1;
+  probe.in_proj = shape->d_model != mtt::kEmbed;
+  const bool fused = mtt::fused_frame_supported(probe);
+  switch (sampling->path) {
+    case MTT_B200_FRAME_PATH_AUTO:
+      return fused ? MTT_B200_FRAME_PATH_FUSED_CLUSTER : MTT_B200_FRAME_PATH_PHASE_KERNELS;
+    case MTT_B200_FRAME_PATH_PHASE_KERNELS:
+      return MTT_B200_FRAME_PATH_PHASE_KERNELS;
+    case MTT_B200_FRAME_PATH_FUSED_CLUSTER:
+      return fused ? MTT_B200_FRAME_PATH_FUSED_CLUSTER : MTT_B200_STATUS_UNSUPPORTED;
+    default:
+      return MTT_B200_STATUS_INVALID_ARGUMENT;
+  }
+}
+
+}  // namespace
+
+extern "C" MTT_B200_API int32_t mtt_b200_local_ar_frame_path(const mtt_b200_local_ar_shape_t* shape,
+                                                             const mtt_b200_sampling_config_t* sampling) {
+  if (!mtt::shape_ok(shape) || sampling == nullptr) return MTT_B200_STATUS_INVALID_ARGUMENT;
+  return resolve_path(shape, sampling);
+}
+
 extern "C" MTT_B200_API int32_t mtt_b200_local_ar_frame_launch_count(const mtt_b200_local_ar_shape_t* shape,
-                                                                     int32_t n_streams, int32_t eos_enabled) {
-  if (!mtt::shape_ok(shape) || n_streams <= 0) return 0;
-  (void)eos_enabled;
+                                                                     const mtt_b200_sampling_config_t* sampling,
+                                                                     int32_t n_streams) {
+  if (!mtt::shape_ok(shape) || sampling == nullptr || n_streams <= 0) return 0;
+  const int32_t path = resolve_path(shape, sampling);
+  if (path == MTT_B200_FRAME_PATH_FUSED_CLUSTER) return 3;  // fused frame, EOS projection, EOS finish
+  if (path != MTT_B200_FRAME_PATH_PHASE_KERNELS) return 0;
   // begin + 16 x (embed + 5 per layer + head + sample) + eos projection + end
   return 1 + mtt::kPositions * (1 + 5 * shape->n_layers + 2) + 2;
 }
@@ -554,6 +527,7 @@ extern "C" MTT_B200_API int mtt_b200_launch_local_ar_frame(const mtt_b200_local_
   f.emb = B(w->emb);
   f.final_w = B(w->final_w);
   f.final_b = B(w->final_b);
+  f.emb_proj = in_proj ? B(w->emb_proj) : nullptr;
   f.hidden = B(b->decoder_hidden);
   f.unfinished = b->unfinished;
   f.finished = b->finished;
@@ -588,6 +562,11 @@ extern "C" MTT_B200_API int mtt_b200_launch_local_ar_frame(const mtt_b200_local_
   f.eos_logit = reinterpret_cast<float*>(ws + lo.eos_logit);
 
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int32_t path = resolve_path(shape, sampling);
+  if (path < 0) return path;
+  if (path == MTT_B200_FRAME_PATH_FUSED_CLUSTER) {
+    return launch_fused_frame(f, st) == cudaSuccess ? MTT_B200_STATUS_OK : MTT_B200_STATUS_CUDA_ERROR;
+  }
   const int d = f.d, F = f.F;
   frame_begin_kernel<<<1, kBeginThreads, 0, st>>>(f);
   for (int p = 0; p < kPositions; ++p) {

@@ -1,0 +1,83 @@
+// Frame description shared by the two batched-frame implementations
+// (phase kernels in frame.cu, fused cluster kernel in frame_fused.cu).
+#pragma once
+
+#include <cstddef>
+
+#include "common.cuh"
+#include "eos.cuh"
+
+namespace mtt {
+
+using bf16 = __nv_bfloat16;
+
+struct Frame {
+  int d, L, H, F, rp, n, in_proj;
+  SamplingParams prm;
+  const bf16 *in_w, *in_b, *pos, *ln1, *qkv, *o, *ln2, *w1, *w2, *head_w, *head_b, *emb, *final_w, *final_b;
+  const bf16* emb_proj;  // optional folded in-projection tables [16][2024][d]
+  const bf16* hidden;
+  const bool *unfinished, *finished, *forbid, *active;
+  const int64_t* seed;
+  int64_t* counter_io;
+  int64_t* codec_tokens;
+  int32_t* invalid_rows;
+  int32_t* end_frame;
+  bf16* next_emb;
+  const int64_t* forced;
+  bf16* logits_out;
+  // workspace
+  int32_t *list, *count, *eos_list, *eos_count, *eos_slot;
+  bf16 *x, *q, *kc, *vc, *att, *h, *logits;
+  int32_t* tokens;
+  float* emb_acc;
+  int64_t* ctr;
+  int32_t* inv;
+  float *eos_partial, *eos_logit;
+};
+
+struct Layout {
+  size_t list, count, eos_list, eos_count, eos_slot, x, q, kc, vc, att, h, logits, tokens, emb_acc, ctr, inv,
+      eos_partial, eos_logit, total;
+};
+
+inline size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
+
+inline Layout make_layout(int d, int L, int F, int n, int rp) {
+  Layout lo{};
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    const size_t at = off;
+    off = align256(off + bytes);
+    return at;
+  };
+  const size_t R = static_cast<size_t>(n) * rp;
+  lo.list = take(4 * static_cast<size_t>(n));
+  lo.count = take(4);
+  lo.eos_list = take(4 * static_cast<size_t>(n));
+  lo.eos_count = take(4);
+  lo.eos_slot = take(4 * static_cast<size_t>(n));
+  lo.x = take(2 * R * d);
+  lo.q = take(2 * R * d);
+  lo.kc = take(2 * static_cast<size_t>(L) * R * kPositions * d);
+  lo.vc = take(2 * static_cast<size_t>(L) * R * kPositions * d);
+  lo.att = take(2 * R * d);
+  lo.h = take(2 * R * F);
+  lo.logits = take(2 * R * kVocab);
+  lo.tokens = take(4 * static_cast<size_t>(n) * kPositions);
+  lo.emb_acc = take(4 * static_cast<size_t>(n) * kEmbed);
+  lo.ctr = take(8 * static_cast<size_t>(n));
+  lo.inv = take(4 * static_cast<size_t>(n));
+  lo.eos_partial = take(4 * static_cast<size_t>(n) * kPositions * kEosChunks);
+  lo.eos_logit = take(4 * static_cast<size_t>(n) * kPositions);
+  lo.total = off;
+  return lo;
+}
+
+
+// Fused cluster kernel (frame_fused.cu).  Returns false when the shape or the
+// device cannot run it (the caller then uses the phase kernels).
+bool fused_frame_supported(const Frame& f);
+cudaError_t launch_fused_frame(const Frame& f, cudaStream_t stream);
+
+}  // namespace mtt

@@ -13,6 +13,7 @@ __global__ void __launch_bounds__(kSampleThreads) dropin_sampling_kernel(
     int64_t* sampled_token, __nv_bfloat16* next_embedding, int64_t* updated_rng_counter,
     int32_t* invalid_rows) {
   __shared__ SampleShared sh;
+  __shared__ __align__(16) unsigned char scratch[kSampleScratchBytes];
   SampleCall c;
   c.logits = logits;
   c.uncond_offset = kVocab;
@@ -24,7 +25,7 @@ __global__ void __launch_bounds__(kSampleThreads) dropin_sampling_kernel(
   c.counter = rng_counter[0];
   int invalid = 0;
   const SamplingParams reference_params{80, 0.6f, 2.5f, 0};  // local_ar_plugins.cu:41-43
-  const int token = sample_block(c, reference_params, sh, &invalid);
+  const int token = sample_block(c, reference_params, sh, scratch, &invalid);
   if (threadIdx.x == 0) {
     const bool counter_valid = c.counter >= 0 && c.counter <= kMaxCounter;
     sampled_token[0] = token;

@@ -6,11 +6,14 @@
 //      gate, finished -> EOS only, non-finite -> -inf + invalid);
 //   2. the inclusive top-k threshold (the k-th largest value, ties included)
 //      by an exact radix select over order-preserving keys: 2 passes of 8 bits
-//      for bf16-valued logits, 4 passes for f32 logits;
-//   3. Philox-Gumbel scores for eligible tokens only (a -inf value scores
-//      -inf for every finite Gumbel, so it is skipped without changing the
-//      result), left-most argmax over the block.
-// One block of kThreads threads; thread t owns tokens [8t, 8t+8).
+//      for bf16-valued logits, 4 passes for f32 logits, each pass one
+//      per-warp shared-memory histogram summed by warp 0;
+//   3. the finite eligible tokens (value >= threshold) compacted in token
+//      order, so each thread scores about one of them: Philox-Gumbel score,
+//      left-most argmax over the block.  A -inf value scores -inf for every
+//      finite Gumbel and can only be chosen when nothing is finite, which
+//      makes the row invalid with token 0; such tokens are not scored.
+// One block of kSampleThreads threads; thread t owns tokens [8t, 8t+8).
 #pragma once
 
 #include "common.cuh"
@@ -19,14 +22,21 @@ namespace mtt {
 
 constexpr int kSampleThreads = 256;
 constexpr int kItems = 8;  // tokens per thread
+constexpr int kSampleWarps = kSampleThreads / 32;
+// Scratch (shared memory, 16-byte aligned) for one call: per-warp histograms
+// [8][256] u32 followed by the eligible-token list [2048] u16.
+constexpr int kSampleScratchBytes = kSampleWarps * 256 * 4 + 2048 * 2;
 
 struct SampleShared {
-  uint32_t hist[256];
   uint32_t digit_and_remaining[2];
-  float warp_best[kSampleThreads / 32];
-  int32_t warp_best_id[kSampleThreads / 32];
-  int32_t flags;  // bit0 invalid (non-finite), bits 8.. finite count
+  uint32_t warp_nonfinite[kSampleWarps];
+  uint32_t warp_count[kSampleWarps];
+  uint32_t warp_finite[kSampleWarps];
+  float warp_best[kSampleWarps];
+  int32_t warp_best_id[kSampleWarps];
   int32_t finite_count;
+  int32_t nonfinite;
+  int32_t n_eligible;
   int32_t token;
   int32_t invalid;
 };
@@ -106,138 +116,91 @@ __device__ __forceinline__ float key_f32(uint32_t k) {
   return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
 }
 
+// One radix pass: histogram of digit (key >> shift) & 0xff over keys matching
+// (prefix, mask); warp 0 finds the digit holding the `remaining`-th largest.
+// Also sums the per-warp finite counts / non-finite flags on the first pass.
+template <bool kFirst>
+__device__ __forceinline__ void radix_pass(const uint32_t (&key)[kItems], int shift, uint32_t prefix, uint32_t mask,
+                                           uint32_t remaining, SampleShared& sh, uint32_t* hist) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int base = threadIdx.x * kItems;
+  uint32_t* wh = hist + warp * 256;
+#pragma unroll
+  for (int i = lane; i < 256; i += 32) wh[i] = 0;
+  __syncwarp();
+#pragma unroll
+  for (int i = 0; i < kItems; ++i) {
+    if (base + i < kVocab && (key[i] & mask) == prefix) atomicAdd(&wh[(key[i] >> shift) & 0xffu], 1u);
+  }
+  __syncthreads();
+  if (warp == 0) {
+    uint32_t c[8];
+    uint32_t sum = 0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int bin = 255 - lane * 8 - j;
+      uint32_t t = 0;
+#pragma unroll
+      for (int w = 0; w < kSampleWarps; ++w) t += hist[w * 256 + bin];
+      c[j] = t;
+      sum += t;
+    }
+    if (kFirst && lane == 0) {
+      uint32_t finite = 0, nf = 0;
+#pragma unroll
+      for (int w = 0; w < kSampleWarps; ++w) {
+        finite += sh.warp_finite[w];
+        nf |= sh.warp_nonfinite[w];
+      }
+      sh.finite_count = static_cast<int32_t>(finite);
+      sh.nonfinite = nf ? 1 : 0;
+    }
+    uint32_t incl = sum;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += y;
+    }
+    const uint32_t excl = incl - sum;
+    if (excl < remaining && remaining <= incl) {
+      uint32_t acc = excl;
+      int j = 0;
+      for (; j < 7; ++j) {
+        if (remaining <= acc + c[j]) break;
+        acc += c[j];
+      }
+      sh.digit_and_remaining[0] = 255u - lane * 8u - j;
+      sh.digit_and_remaining[1] = remaining - acc;
+    }
+  }
+  __syncthreads();
+}
+
 // Exact k-th largest key over the block (k >= 1, k <= number of valid tokens).
 // KEY_BITS is 16 (bf16-valued logits: key = top half of the f32 key) or 32.
 template <int KEY_BITS>
-__device__ __forceinline__ uint32_t block_kth_key(const uint32_t (&key)[kItems], int k, SampleShared& sh) {
-  const int lane = threadIdx.x & 31;
-  const int warp = threadIdx.x >> 5;
-  const int base = threadIdx.x * kItems;
+__device__ __forceinline__ uint32_t block_kth_key(const uint32_t (&key)[kItems], int k, SampleShared& sh,
+                                                  uint32_t* hist) {
   uint32_t prefix = 0, mask = 0;
   uint32_t remaining = static_cast<uint32_t>(k);
+  radix_pass<true>(key, KEY_BITS - 8, prefix, mask, remaining, sh, hist);
+  prefix = sh.digit_and_remaining[0] << (KEY_BITS - 8);
+  mask = 0xffu << (KEY_BITS - 8);
+  remaining = sh.digit_and_remaining[1];
 #pragma unroll
-  for (int shift = KEY_BITS - 8; shift >= 0; shift -= 8) {
-    for (int i = threadIdx.x; i < 256; i += blockDim.x) sh.hist[i] = 0;
-    __syncthreads();
-#pragma unroll
-    for (int i = 0; i < kItems; ++i) {
-      const bool part = (base + i < kVocab) && ((key[i] & mask) == prefix);
-      const uint32_t digit = part ? ((key[i] >> shift) & 0xffu) : 256u;
-      const unsigned peers = __match_any_sync(0xffffffffu, digit);
-      if (part && lane == __ffs(peers) - 1) atomicAdd(&sh.hist[digit], __popc(peers));
-    }
-    __syncthreads();
-    if (warp == 0) {
-      // lane l owns bins 255-8l .. 248-8l (descending)
-      uint32_t c[8];
-      uint32_t sum = 0;
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        c[j] = sh.hist[255 - lane * 8 - j];
-        sum += c[j];
-      }
-      uint32_t incl = sum;
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
-        if (lane >= o) incl += y;
-      }
-      const uint32_t excl = incl - sum;
-      if (excl < remaining && remaining <= incl) {
-        uint32_t acc = excl;
-        int j = 0;
-        for (; j < 7; ++j) {
-          if (remaining <= acc + c[j]) break;
-          acc += c[j];
-        }
-        sh.digit_and_remaining[0] = 255u - lane * 8u - j;
-        sh.digit_and_remaining[1] = remaining - acc;
-      }
-    }
-    __syncthreads();
+  for (int shift = KEY_BITS - 16; shift >= 0; shift -= 8) {
+    __syncthreads();  // every thread has read the previous pass's result
+    radix_pass<false>(key, shift, prefix, mask, remaining, sh, hist);
     prefix |= sh.digit_and_remaining[0] << shift;
     mask |= 0xffu << shift;
     remaining = sh.digit_and_remaining[1];
-    __syncthreads();
   }
   return prefix;
 }
 
-// Returns the sampled token (block-uniform) and sets *invalid_out (block-uniform).
-__device__ __forceinline__ int sample_block(const SampleCall& c, const SamplingParams& prm, SampleShared& sh,
-                                            int* invalid_out) {
-  const int lane = threadIdx.x & 31;
-  const int warp = threadIdx.x >> 5;
-  const int base = threadIdx.x * kItems;
-  if (threadIdx.x == 0) {
-    sh.invalid = 0;
-    sh.finite_count = 0;
-  }
-  __syncthreads();
-  float v[kItems];
-  const bool nonfinite = load_constrained(c, prm, v);
-  int finite = 0;
-#pragma unroll
-  for (int i = 0; i < kItems; ++i) finite += (base + i < kVocab && isfinite(v[i])) ? 1 : 0;
-  finite = __reduce_add_sync(0xffffffffu, finite);
-  const unsigned nf = __ballot_sync(0xffffffffu, nonfinite);
-  if (lane == 0) {
-    if (finite) atomicAdd(&sh.finite_count, finite);
-    if (nf) atomicOr(&sh.invalid, 1);
-  }
-  __syncthreads();
-  int invalid = sh.invalid | (sh.finite_count == 0 ? 1 : 0);
-
-  float best = -CUDART_INF_F;
-  int best_id = kVocab;
-  if (prm.argmax) {
-#pragma unroll
-    for (int i = 0; i < kItems; ++i) {
-      const int t = base + i;
-      if (t < kVocab && (v[i] > best || (v[i] == best && t < best_id))) {
-        best = v[i];
-        best_id = t;
-      }
-    }
-  } else {
-    if (c.unfinished && c.finished) invalid = 1;
-    if (c.finished && c.forbid_eos) invalid = 1;
-    const bool seed_valid = c.seed >= 0 && static_cast<uint64_t>(c.seed) < (1ull << 32);
-    const bool counter_valid = c.counter >= 0 && c.counter <= kMaxCounter;
-    if (!seed_valid || !counter_valid) invalid = 1;
-    float threshold;
-    if (c.kind == kLogitsF32) {
-      uint32_t key[kItems];
-#pragma unroll
-      for (int i = 0; i < kItems; ++i) key[i] = f32_key(v[i]);
-      threshold = key_f32(block_kth_key<32>(key, prm.top_k, sh));
-    } else {
-      uint32_t key[kItems];
-#pragma unroll
-      for (int i = 0; i < kItems; ++i) key[i] = f32_key(v[i]) >> 16;
-      const uint32_t k16 = block_kth_key<16>(key, prm.top_k, sh);
-      threshold = key_f32((k16 << 16) | ((k16 & 0x8000u) ? 0u : 0xffffu));
-    }
-    const uint32_t seed32 = seed_valid ? static_cast<uint32_t>(c.seed) : 0u;
-    const uint64_t off = counter_valid ? static_cast<uint64_t>(c.counter) * kPhiloxStride : 0ull;
-#pragma unroll
-    for (int i = 0; i < kItems; ++i) {
-      const int t = base + i;
-      if (t >= kVocab || v[i] < threshold) continue;
-      float score;
-      if (v[i] == -CUDART_INF_F) {
-        score = -CUDART_INF_F;
-      } else {
-        const float g = clamped_gumbel(philox_uniform(seed32, off + static_cast<uint64_t>(t)));
-        score = __fadd_rn(__fdiv_rn(v[i], prm.temperature), g);
-      }
-      if (score > best || (score == best && t < best_id)) {
-        best = score;
-        best_id = t;
-      }
-    }
-  }
-  // block arg-max, left-most on ties
+// Left-most arg-max of (best, id) over the block; returns the block-uniform pair in sh.
+__device__ __forceinline__ void block_argmax(float best, int best_id, SampleShared& sh) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
     const float ob = __shfl_down_sync(0xffffffffu, best, o);
@@ -252,27 +215,149 @@ __device__ __forceinline__ int sample_block(const SampleCall& c, const SamplingP
     sh.warp_best_id[warp] = best_id;
   }
   __syncthreads();
-  if (threadIdx.x == 0) {
-    float b = sh.warp_best[0];
-    int bi = sh.warp_best_id[0];
-    for (int w = 1; w < kSampleThreads / 32; ++w) {
-      if (sh.warp_best[w] > b || (sh.warp_best[w] == b && sh.warp_best_id[w] < bi)) {
-        b = sh.warp_best[w];
-        bi = sh.warp_best_id[w];
+  if (warp == 0) {
+    float b = lane < kSampleWarps ? sh.warp_best[lane] : -CUDART_INF_F;
+    int bi = lane < kSampleWarps ? sh.warp_best_id[lane] : kVocab;
+#pragma unroll
+    for (int o = 4; o > 0; o >>= 1) {
+      const float ob = __shfl_down_sync(0xffffffffu, b, o);
+      const int oi = __shfl_down_sync(0xffffffffu, bi, o);
+      if (ob > b || (ob == b && oi < bi)) {
+        b = ob;
+        bi = oi;
       }
     }
-    int inv = invalid;
-    if (bi >= kVocab || b == -CUDART_INF_F) {
-      inv = 1;
-      bi = 0;
+    if (lane == 0) {
+      sh.warp_best[0] = b;
+      sh.warp_best_id[0] = bi;
     }
-    sh.token = bi;
-    sh.invalid = inv;
   }
   __syncthreads();
-  *invalid_out = sh.invalid;
-  const int token = sh.token;
-  __syncthreads();
+}
+
+// Returns the sampled token (block-uniform) and sets *invalid_out (block-uniform).
+// scratch: kSampleScratchBytes of 16-byte aligned shared memory.
+__device__ __forceinline__ int sample_block(const SampleCall& c, const SamplingParams& prm, SampleShared& sh,
+                                            void* scratch, int* invalid_out) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int base = threadIdx.x * kItems;
+  uint32_t* hist = static_cast<uint32_t*>(scratch);
+  uint16_t* elig = reinterpret_cast<uint16_t*>(hist + kSampleWarps * 256);
+  float v[kItems];
+  const bool nonfinite = load_constrained(c, prm, v);
+  const unsigned nf = __ballot_sync(0xffffffffu, nonfinite);
+  uint32_t fin = 0;
+#pragma unroll
+  for (int i = 0; i < kItems; ++i) fin += (base + i < kVocab && v[i] != -CUDART_INF_F) ? 1u : 0u;
+  fin = __reduce_add_sync(0xffffffffu, fin);
+  if (lane == 0) {
+    sh.warp_nonfinite[warp] = nf;
+    sh.warp_finite[warp] = fin;
+  }
+
+  float best = -CUDART_INF_F;
+  int best_id = kVocab;
+  int invalid = 0;
+  if (prm.argmax) {
+#pragma unroll
+    for (int i = 0; i < kItems; ++i) {
+      const int t = base + i;
+      if (t < kVocab && (v[i] > best || (v[i] == best && t < best_id))) {
+        best = v[i];
+        best_id = t;
+      }
+    }
+    block_argmax(best, best_id, sh);  // its barriers publish warp_finite / warp_nonfinite
+    uint32_t total = 0, anynf = 0;
+#pragma unroll
+    for (int w = 0; w < kSampleWarps; ++w) {
+      total += sh.warp_finite[w];
+      anynf |= sh.warp_nonfinite[w];
+    }
+    invalid = (anynf || total == 0) ? 1 : 0;
+  } else {
+    uint32_t threshold_key;
+    float threshold;
+    if (c.kind == kLogitsF32) {
+      uint32_t key[kItems];
+#pragma unroll
+      for (int i = 0; i < kItems; ++i) key[i] = f32_key(v[i]);
+      threshold_key = block_kth_key<32>(key, prm.top_k, sh, hist);
+      threshold = key_f32(threshold_key);
+    } else {
+      uint32_t key[kItems];
+#pragma unroll
+      for (int i = 0; i < kItems; ++i) key[i] = f32_key(v[i]) >> 16;
+      threshold_key = block_kth_key<16>(key, prm.top_k, sh, hist);
+      threshold = key_f32((threshold_key << 16) | ((threshold_key & 0x8000u) ? 0u : 0xffffu));
+    }
+    invalid = (sh.nonfinite || sh.finite_count == 0) ? 1 : 0;
+    if (c.unfinished && c.finished) invalid = 1;
+    if (c.finished && c.forbid_eos) invalid = 1;
+    const bool seed_valid = c.seed >= 0 && static_cast<uint64_t>(c.seed) < (1ull << 32);
+    const bool counter_valid = c.counter >= 0 && c.counter <= kMaxCounter;
+    if (!seed_valid || !counter_valid) invalid = 1;
+
+    // compact the finite eligible tokens in token order
+    uint32_t emask = 0;
+#pragma unroll
+    for (int i = 0; i < kItems; ++i) {
+      if (base + i < kVocab && v[i] >= threshold && v[i] != -CUDART_INF_F) emask |= 1u << i;
+    }
+    const uint32_t cnt = __popc(emask);
+    uint32_t incl = cnt;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += y;
+    }
+    if (lane == 31) sh.warp_count[warp] = incl;
+    __syncthreads();
+    uint32_t off = incl - cnt;
+    uint32_t total = 0;
+#pragma unroll
+    for (int w = 0; w < kSampleWarps; ++w) {
+      const uint32_t wc = sh.warp_count[w];
+      off += w < warp ? wc : 0u;
+      total += wc;
+    }
+#pragma unroll
+    for (int i = 0; i < kItems; ++i) {
+      if (emask & (1u << i)) elig[off++] = static_cast<uint16_t>(base + i);
+    }
+    __syncthreads();
+    const uint32_t seed32 = seed_valid ? static_cast<uint32_t>(c.seed) : 0u;
+    const uint64_t off64 = counter_valid ? static_cast<uint64_t>(c.counter) * kPhiloxStride : 0ull;
+    for (uint32_t e = threadIdx.x; e < total; e += blockDim.x) {
+      const int t = elig[e];
+      // the constrained value of token t lives in the owning thread's registers;
+      // recompute it from the logits (cheap, exact) instead of exchanging it
+      float value;
+      if (c.kind == kLogitsF32) {
+        value = static_cast<const float*>(c.logits)[t];
+      } else {
+        const uint16_t* l = static_cast<const uint16_t*>(c.logits);
+        value = c.kind == kLogitsBf16Cfg ? guided_logit(bits2f(l[t]), bits2f(l[c.uncond_offset + t]), prm.cfg_scale)
+                                         : bits2f(l[t]);
+      }
+      if (c.finished) value = 0.0f;  // only EOS (value 0) is finite for a finished row
+      const float g = clamped_gumbel(philox_uniform(seed32, off64 + static_cast<uint64_t>(t)));
+      const float score = __fadd_rn(__fdiv_rn(value, prm.temperature), g);
+      if (score > best || (score == best && t < best_id)) {
+        best = score;
+        best_id = t;
+      }
+    }
+    block_argmax(best, best_id, sh);
+  }
+  const float b = sh.warp_best[0];
+  int token = sh.warp_best_id[0];
+  if (token >= kVocab || b == -CUDART_INF_F) {
+    invalid = 1;
+    token = 0;
+  }
+  *invalid_out = invalid;
+  __syncthreads();  // sh is reused by the next call
   return token;
 }
 

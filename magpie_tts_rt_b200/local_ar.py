@@ -153,7 +153,7 @@ class LocalArEngine:
 
     def __init__(self, weights: LocalArWeights, max_streams: int, device="cuda", cfg: bool = True,
                  top_k: int = TOP_K, temperature: float = TEMPERATURE, cfg_scale: float = CFG_SCALE,
-                 argmax: bool = False):
+                 argmax: bool = False, path: int = L.PATH_AUTO, fold_in_projection: bool = True):
         self.shape = weights.shape
         self.device = torch.device(device)
         self.cfg = cfg
@@ -171,16 +171,32 @@ class LocalArEngine:
             setattr(self._w, name[0], t.data_ptr() if t is not None else None)
         self._shape = L.Shape(self.shape.d_model, self.shape.n_layers, self.shape.n_heads,
                               self.shape.d_ffn)
-        self._sampling = L.SamplingConfig(top_k, temperature, cfg_scale, int(argmax), int(cfg))
+        # fold the in-projection into the embedding tables once (weight transform)
+        self.emb_proj = None
+        if fold_in_projection and self.shape.in_projection:
+            nbytes = L.lib.mtt_b200_fold_in_projection_bytes(ctypes.byref(self._shape))
+            self.emb_proj = torch.empty(nbytes // 2, dtype=torch.bfloat16, device=self.device)
+            status = L.lib.mtt_b200_launch_fold_in_projection(
+                ctypes.byref(self._shape), ctypes.byref(self._w),
+                ctypes.c_void_p(self.emb_proj.data_ptr()), _stream(None))
+            if status != L.STATUS_OK:
+                raise RuntimeError(f"mtt_b200_launch_fold_in_projection failed with status {status}")
+            self._w.emb_proj = self.emb_proj.data_ptr()
+        self._sampling = L.SamplingConfig(top_k, temperature, cfg_scale, int(argmax), int(cfg), int(path))
         size = L.lib.mtt_b200_local_ar_frame_workspace_size(ctypes.byref(self._shape), max_streams,
                                                            int(cfg))
         if size == 0:
             raise ValueError(f"unsupported shape {self.shape}")
         self.workspace = torch.empty(size, dtype=torch.uint8, device=self.device)
 
-    def launch_count(self, n_streams: int, eos_enabled: bool = False) -> int:
-        return int(L.lib.mtt_b200_local_ar_frame_launch_count(ctypes.byref(self._shape), n_streams,
-                                                              int(eos_enabled)))
+    @property
+    def path(self) -> int:
+        """Resolved frame path on the current device (1 phase kernels, 2 fused cluster)."""
+        return int(L.lib.mtt_b200_local_ar_frame_path(ctypes.byref(self._shape), ctypes.byref(self._sampling)))
+
+    def launch_count(self, n_streams: int) -> int:
+        return int(L.lib.mtt_b200_local_ar_frame_launch_count(ctypes.byref(self._shape),
+                                                              ctypes.byref(self._sampling), n_streams))
 
     def frame(self, batch: StreamBatch, stream=None) -> None:
         if batch.n > self.max_streams:

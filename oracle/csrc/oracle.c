@@ -104,17 +104,71 @@ float orc_philox_uniform(uint32_t seed, uint64_t offset) {
 /* The reference's three implementations of -log(-log u) each round their   */
 /* own f32 log (CUDA __logf, Triton tl.log, PyTorch CPU log); none is        */
 /* correctly rounded.  This build fixes the rounding: each log is evaluated */
-/* in double with the atanh series                                          */
-/*     log(m) = 2s(1 + s^2/3 + s^4/5 + ...),  s = (m-1)/(m+1),               */
-/* m in [sqrt(1/2), sqrt(2)), 12 terms (|s|^2 <= 0.0295, truncation < 2^-60),*/
-/* then rounded once to f32.  The CUDA kernels run the identical sequence of */
-/* IEEE double operations (no fused multiply-add), so the two agree bit for */
-/* bit by construction.  Valid for positive normal f32 inputs.               */
+/* in double by a table-driven reduction (Tang's method) and rounded once   */
+/* to f32.  x = 2^e * m with m in [sqrt(1/2), sqrt(2)); j = nearest(64(m-1)) */
+/* picks c_j = 1 + j/64 with a 29-bit inv_j ~ 1/c_j (so m * inv_j is exact) */
+/* and L_j = -log(inv_j); t = m * inv_j - 1 (|t| < 0.0113, exact);          */
+/* log(m) = L_j + log1p(t), log1p(t) = t + t^2 q(t) with 10 series terms.   */
+/* j = 0 has c = 1 exactly, so results near log 1 = 0 do not cancel.        */
+/* The CUDA kernels run the identical sequence of IEEE double operations    */
+/* (explicit fma / mul / add), so the two agree bit for bit by construction.*/
+/* Valid for positive normal f32 inputs.                                    */
 /* ------------------------------------------------------------------------ */
 
-static const double kLn2Hi = 0.69314718036912381649017333984375; /* 0x1.62e42feep-1 */
+static const double kLn2Hi = 0x1.62e42feep-1;
 static const double kLn2Lo = 1.9082149292705877e-10;
 static const double kSqrt2 = 1.4142135623730951;
+
+/* {inv_j, L_j} for j = -19 .. 27 */
+static const double kLogTable[47][2] = {
+    {0x1.6c16c17000000p+0, -0x1.68ac83f4c6a14p-2},  /* j = -19 */
+    {0x1.642c859000000p+0, -0x1.522ae0718a3d8p-2},  /* j = -18 */
+    {0x1.5c9882c000000p+0, -0x1.3c25278733184p-2},  /* j = -17 */
+    {0x1.5555555000000p+0, -0x1.269621034db92p-2},  /* j = -16 */
+    {0x1.4e5e0a7000000p+0, -0x1.1178e8197e47cp-2},  /* j = -15 */
+    {0x1.47ae148000000p+0, -0x1.f991c6eb3b379p-3},  /* j = -14 */
+    {0x1.4141414000000p+0, -0x1.d1037f1e55e7bp-3},  /* j = -13 */
+    {0x1.3b13b14000000p+0, -0x1.a93ed3e8ad9e3p-3},  /* j = -12 */
+    {0x1.3521cfb000000p+0, -0x1.823c16431a3c2p-3},  /* j = -11 */
+    {0x1.2f684be000000p+0, -0x1.5bf406dd43db2p-3},  /* j = -10 */
+    {0x1.29e412a000000p+0, -0x1.365fcb0d59016p-3},  /* j = -9 */
+    {0x1.2492492000000p+0, -0x1.1178e8027e47cp-3},  /* j = -8 */
+    {0x1.1f7047e000000p+0, -0x1.da727670446a2p-4},  /* j = -7 */
+    {0x1.1a7b961000000p+0, -0x1.9335e5bd94989p-4},  /* j = -6 */
+    {0x1.15b1e5f000000p+0, -0x1.4d31156607eacp-4},  /* j = -5 */
+    {0x1.1111111000000p+0, -0x1.08598b49e3a07p-4},  /* j = -4 */
+    {0x1.0c97150000000p+0, -0x1.894aa1c9fb343p-5},  /* j = -3 */
+    {0x1.0842108000000p+0, -0x1.0415d81e74444p-5},  /* j = -2 */
+    {0x1.0410410000000p+0, -0x1.0205648935847p-6},  /* j = -1 */
+    {0x1.0000000000000p+0, 0x0.0p+0},  /* j = 0 */
+    {0x1.f81f820000000p-1, 0x1.fc0a890fc03e4p-7},  /* j = 1 */
+    {0x1.f07c1f0000000p-1, 0x1.f829b1e783300p-6},  /* j = 2 */
+    {0x1.e9131ac000000p-1, 0x1.77458f532dcfcp-5},  /* j = 3 */
+    {0x1.e1e1e1e000000p-1, 0x1.f0a30c21162a6p-5},  /* j = 4 */
+    {0x1.dae6077000000p-1, 0x1.341d793bbd1d1p-4},  /* j = 5 */
+    {0x1.d41d41d000000p-1, 0x1.6f0d28d256b4cp-4},  /* j = 6 */
+    {0x1.cd85689000000p-1, 0x1.a926d3a6ad563p-4},  /* j = 7 */
+    {0x1.c71c71c000000p-1, 0x1.e2707722af2e6p-4},  /* j = 8 */
+    {0x1.c0e0704000000p-1, 0x1.0d77e7a908e59p-3},  /* j = 9 */
+    {0x1.bacf915000000p-1, 0x1.29552f6fff523p-3},  /* j = 10 */
+    {0x1.b4e81b5000000p-1, 0x1.44d2b6c5b7d1ep-3},  /* j = 11 */
+    {0x1.af286bd000000p-1, 0x1.5ff306ee793d4p-3},  /* j = 12 */
+    {0x1.a98ef60000000p-1, 0x1.7ab890410d909p-3},  /* j = 13 */
+    {0x1.a41a41a000000p-1, 0x1.9525a9e3456b4p-3},  /* j = 14 */
+    {0x1.9ec8e95000000p-1, 0x1.af3c94ed0bff3p-3},  /* j = 15 */
+    {0x1.999999a000000p-1, 0x1.c8ff7c59a9a22p-3},  /* j = 16 */
+    {0x1.948b0fd000000p-1, 0x1.e27076d5af2e6p-3},  /* j = 17 */
+    {0x1.8f9c190000000p-1, 0x1.fb9186b5e3e2bp-3},  /* j = 18 */
+    {0x1.8acb90f000000p-1, 0x1.0a324e38b90e3p-2},  /* j = 19 */
+    {0x1.8618618000000p-1, 0x1.1675cacaba60ep-2},  /* j = 20 */
+    {0x1.8181818000000p-1, 0x1.22941fc0f7966p-2},  /* j = 21 */
+    {0x1.7d05f41000000p-1, 0x1.2e8e2bc311d31p-2},  /* j = 22 */
+    {0x1.78a4c81000000p-1, 0x1.3a64c56b145eap-2},  /* j = 23 */
+    {0x1.745d174000000p-1, 0x1.4618bc31c5ec2p-2},  /* j = 24 */
+    {0x1.702e05c000000p-1, 0x1.51aad874df82dp-2},  /* j = 25 */
+    {0x1.6c16c17000000p-1, 0x1.5d1bdbea809cap-2},  /* j = 26 */
+    {0x1.6816817000000p-1, 0x1.686c81d3314afp-2},  /* j = 27 */
+};
 
 double orc_log_double(float x) {
   const uint32_t bits = f32_to_bits(x);
@@ -124,23 +178,22 @@ double orc_log_double(float x) {
     m = m * 0.5;
     exponent += 1;
   }
-  const double f = m - 1.0;
-  const double s = f / (2.0 + f);
-  const double z = s * s;
-  double p = 0.04; /* 1/25 */
-  p = p * z + 0.043478260869565216;
-  p = p * z + 0.047619047619047616;
-  p = p * z + 0.05263157894736842;
-  p = p * z + 0.058823529411764705;
-  p = p * z + 0.06666666666666667;
-  p = p * z + 0.07692307692307693;
-  p = p * z + 0.09090909090909091;
-  p = p * z + 0.1111111111111111;
-  p = p * z + 0.14285714285714285;
-  p = p * z + 0.2;
-  p = p * z + 0.3333333333333333;
-  const double two_s = s + s;
-  const double log_m = two_s + two_s * (z * p);
+  const int j = (int)lrint((m - 1.0) * 64.0);
+  const double inv = kLogTable[j + 19][0];
+  const double L = kLogTable[j + 19][1];
+  const double t = fma(m, inv, -1.0);
+  double q = 0x1.745d1745d1746p-4;
+  q = fma(q, t, -0x1.999999999999ap-4);
+  q = fma(q, t, 0x1.c71c71c71c71cp-4);
+  q = fma(q, t, -0x1.0000000000000p-3);
+  q = fma(q, t, 0x1.2492492492492p-3);
+  q = fma(q, t, -0x1.5555555555555p-3);
+  q = fma(q, t, 0x1.999999999999ap-3);
+  q = fma(q, t, -0x1.0000000000000p-2);
+  q = fma(q, t, 0x1.5555555555555p-2);
+  q = fma(q, t, -0x1.0000000000000p-1);
+  const double t2 = t * t;
+  const double log_m = L + fma(t2, q, t);
   const double e = (double)exponent;
   return e * kLn2Hi + (e * kLn2Lo + log_m);
 }

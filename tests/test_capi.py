@@ -89,7 +89,11 @@ def test_workspace_sizes():
     bad = L.Shape(256, 1, 3, 1024)  # head width must be 64
     assert L.lib.mtt_b200_local_ar_frame_workspace_size(ctypes.byref(bad), 64, 1) == 0
     assert L.lib.mtt_b200_local_ar_frame_workspace_size(ctypes.byref(ok), 0, 1) == 0
-    assert L.lib.mtt_b200_local_ar_frame_launch_count(ctypes.byref(ok), 64, 0) == 16 * 8 + 3
+    phase = L.SamplingConfig(80, 0.6, 2.5, 0, 1, L.PATH_PHASE_KERNELS)
+    assert L.lib.mtt_b200_local_ar_frame_launch_count(ctypes.byref(ok), ctypes.byref(phase), 64) == 16 * 8 + 3
+    assert L.lib.mtt_b200_local_ar_frame_path(ctypes.byref(ok), ctypes.byref(phase)) == L.PATH_PHASE_KERNELS
+    bad_path = L.SamplingConfig(80, 0.6, 2.5, 0, 1, 7)
+    assert L.lib.mtt_b200_local_ar_frame_path(ctypes.byref(ok), ctypes.byref(bad_path)) == -1
 
 
 def test_null_arguments_rejected_without_launch():

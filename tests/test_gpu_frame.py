@@ -25,6 +25,8 @@ from oracle import sampler as S
 pytestmark = pytest.mark.gpu
 
 RTOL = 1e-2
+PATH_AUTO, PHASE, FUSED = 0, 1, 2
+BOTH = [PHASE, FUSED]
 
 
 def bits(t):
@@ -140,11 +142,11 @@ def engines():
     from magpie_tts_rt_b200.local_ar import LocalArEngine
     cache = {}
 
-    def get(shape, seed, max_streams, cfg=True, argmax=False, with_final=True):
-        key = (shape, seed, max_streams, cfg, argmax, with_final)
+    def get(shape, seed, max_streams, cfg=True, argmax=False, with_final=True, path=PATH_AUTO):
+        key = (shape, seed, max_streams, cfg, argmax, with_final, path)
         if key not in cache:
             cache[key] = LocalArEngine(weights(shape, seed, with_final), max_streams=max_streams, cfg=cfg,
-                                       argmax=argmax)
+                                       argmax=argmax, path=path)
         return cache[key]
     return get
 
@@ -158,24 +160,32 @@ def _hidden(n, seed, cfg=True):
 FLAGS6 = ([0, 1, 0, 0, 0, 1], [0, 0, 0, 1, 0, 1], [0, 0, 1, 0, 0, 0])  # incl. an invalid overlap
 
 
-@pytest.mark.parametrize("shape,n", [(SHAPE_BASELINE, 6), (SHAPE_SOFIA, 3)])
-def test_frame_matches_oracle(engines, shape, n):
+@pytest.mark.parametrize("shape,n,path", [(SHAPE_BASELINE, 6, PHASE), (SHAPE_BASELINE, 6, FUSED),
+                                          (SHAPE_BASELINE, 11, FUSED), (SHAPE_SOFIA, 3, PHASE)])
+def test_frame_matches_oracle(engines, shape, n, path):
     w = weights(shape, 21)
-    eng = engines(shape, 21, 8)
+    eng = engines(shape, 21, 16, path=path)
+    assert eng.path == path
     hidden = _hidden(n, 5)
-    flags = tuple(np.asarray(f[:n]) for f in FLAGS6)
-    seed = np.array([1234, 0, 7, (1 << 32) - 1, 99, 5][:n])
-    counter = np.array([0, 16, 3200, 48, S.MAX_COUNTER - 3, 0][:n])
+    flags = tuple(np.resize(np.asarray(f), n) for f in FLAGS6)
+    seed = np.resize(np.array([1234, 0, 7, (1 << 32) - 1, 99, 5]), n)
+    counter = np.resize(np.array([0, 16, 3200, 48, S.MAX_COUNTER - 3, 0]), n)
     gpu = run_gpu(eng, hidden, flags, seed, counter)
     check_frame(w, hidden, flags, seed, counter, gpu)
 
 
-def test_frame_sequence_counters(engines):
+def test_auto_path_is_fused_for_the_benchmark_shape(engines):
+    assert engines(SHAPE_BASELINE, 21, 16).path == FUSED
+    assert engines(SHAPE_SOFIA, 21, 1, with_final=False).path == PHASE
+
+
+@pytest.mark.parametrize("path", BOTH)
+def test_frame_sequence_counters(engines, path):
     """Three consecutive frames of 4 sessions: the counter advances by 16 per
     frame and every frame matches the oracle (sequence_contract.py:95-160)."""
     shape = SHAPE_BASELINE
     w = weights(shape, 22)
-    eng = engines(shape, 22, 4)
+    eng = engines(shape, 22, 4, path=path)
     seed = np.array([1234, 1, 2, 3])
     counter = np.zeros(4, np.int64)
     for f in range(3):
@@ -190,10 +200,11 @@ def test_frame_sequence_counters(engines):
         counter = gpu["counter"]
 
 
-def test_inactive_streams_untouched(engines):
+@pytest.mark.parametrize("path", BOTH)
+def test_inactive_streams_untouched(engines, path):
     shape = SHAPE_BASELINE
     w = weights(shape, 21)
-    eng = engines(shape, 21, 8)
+    eng = engines(shape, 21, 8, path=path)
     n = 5
     hidden = _hidden(n, 9)
     flags = (np.zeros(n, bool), np.zeros(n, bool), np.ones(n, bool))
@@ -207,12 +218,13 @@ def test_inactive_streams_untouched(engines):
     check_frame(w, hidden, flags, seed, counter, gpu, streams=np.nonzero(active)[0])
 
 
-def test_argmax_without_cfg(engines):
+@pytest.mark.parametrize("path", BOTH)
+def test_argmax_without_cfg(engines, path):
     """Greedy decoding, one row per stream (config 1's mode, bf16 on the GPU):
     no RNG, counter unchanged (magpietts_fused_sampling.py:136-197)."""
     shape = SHAPE_BASELINE
     w = weights(shape, 23)
-    eng = engines(shape, 23, 4, cfg=False, argmax=True)
+    eng = engines(shape, 23, 4, cfg=False, argmax=True, path=path)
     n = 3
     hidden = _hidden(n, 11, cfg=False)
     flags = (np.array([0, 1, 0], bool), np.zeros(n, bool), np.array([0, 0, 1], bool))
@@ -230,7 +242,7 @@ def test_frame_against_reference_golden(engines, golden, golden_dir, name):
     meta = golden["lt_frames"][name]
     z = np.load(os.path.join(golden_dir, "lt_frames.npz"))
     shape = LocalArShape(meta["d_model"], meta["n_layers"], meta["n_heads"], meta["d_ffn"])
-    eng = engines(shape, meta["weights_seed"], 1, with_final=False)
+    eng = engines(shape, meta["weights_seed"], 1, with_final=False)  # AUTO: fused for A, phase for R
     for f, fr in enumerate(meta["frames"]):
         hidden = from_bits(z[f"{name}/f{f}/hidden"]).reshape(1, 2, EMBED)
         ref_tokens = z[f"{name}/f{f}/tokens"]
@@ -239,11 +251,12 @@ def test_frame_against_reference_golden(engines, golden, golden_dir, name):
         check_logits(gpu["logits"][0], z[f"{name}/f{f}/logits"].reshape(POSITIONS, 2, VOCAB), name)
 
 
-def test_batch_of_64_streams(engines):
+@pytest.mark.parametrize("path", BOTH)
+def test_batch_of_64_streams(engines, path):
     """Config 3's batch size: 64 sessions x CFG pair, seeds 0..63."""
     shape = SHAPE_BASELINE
     w = weights(shape, 24)
-    eng = engines(shape, 24, 64)
+    eng = engines(shape, 24, 64, path=path)
     n = 64
     hidden = _hidden(n, 12)
     flags = (np.ones(n, bool), np.zeros(n, bool), np.zeros(n, bool))
