@@ -1,18 +1,17 @@
 // Fused Local AR frame: one kernel launch runs all 16 positions of a frame
 // for every active session, one 16-CTA thread-block cluster per tile of
-// 8 sessions (16 CFG rows).  Clusters never wait on each other, so the only
-// synchronisation is the hardware cluster barrier.
+// 8 sessions (16 CFG rows).  Clusters never wait on each other.
 //
 // Per position and per tile (reference ops: tools/export/local_ar_wrapper.py:
 // 609-751; transformer_2501.py:405-442,761-851,1153-1232; sampling
 // plugins/local_ar_plugins.cu:1211-1370; embedding sum
 // main_decoder_wrapper.py:796-810), CTA c of the cluster:
 //
-//   Ph0 in-projection: features [16c, 16c+16) of bf16(bf16(W_in src + b) +
-//       pos[p]) for the 16 rows (src = decoder hidden at p = 0, else the
-//       sampled token's embedding row); all-gathered into every CTA's x.
-//       With the folded tables (fold.cu), positions 1..15 instead gather
-//       bf16(emb_proj[p-1][token] + pos[p]) for all features locally.
+//   Ph0 in-projection: at p = 0, features [16c, +16) of bf16(bf16(W_in h + b)
+//       + pos[0]) for the 16 decoder-hidden rows, all-gathered into every
+//       CTA's x.  At p >= 1 every CTA gathers x = bf16(emb_proj[p-1][token] +
+//       pos[p]) locally from the folded tables (fold.cu); without them the
+//       sampled token's embedding row is multiplied like the hidden rows.
 //   Ph1 LN1(x) (every CTA, all rows); qkv features of head h = c / 4,
 //       head-dims [16(c%4), +16): q kept, k/v appended to this CTA's K/V
 //       slice; partial q.k over those 16 dims sent to the 4 CTAs of head h.
@@ -20,24 +19,29 @@
 //       bf16 rounding, x 1/8, softmax, probability-weighted V slice;
 //       all-gathered into every CTA's attention buffer.
 //   Ph3 o-projection features [16c, +16) + residual, all-gathered into x.
-//   Ph4 LN2(x); FFN1 features [64c, +64) + GELU-tanh, all-gathered (FFN hidden).
-//   Ph5 FFN2 features [16c, +16) + residual, all-gathered into x.
-//   Ph6 head_p features [128c, +128) (+bias); each session's two logits rows
-//       are sent to the CTA that owns the session (CTA s owns session s).
+//   Ph4 LN2(x); FFN1 features [64c, +64) + GELU-tanh (kept locally); their
+//       FFN2 contribution h_c W2[:, 64c:+64]^T (f32) scattered to the owners
+//       of the output features.
+//   Ph5 the 16 partial sums of features [16c, +16), in CTA order, bf16, +
+//       residual, all-gathered into x.
+//   Ph6 head_p features [128c, +128) (+bias); each session's logits rows are
+//       sent to the CTA that owns the session (CTA s owns session s).
 //   Ph7 the owner samples (sampling.cuh) and broadcasts the token; it keeps
 //       the RNG counter and the invalid flag, and at the end of the frame
 //       forms the next-frame embedding sum from the 16 sampled rows.
 //
-// Each exchange ends with barrier.cluster (8 per position, 7 when the
-// in-projection is folded into the embedding tables: positions 1..15 then
-// gather their input rows locally).  Every CTA streams its slice of each
-// layer's weights from global memory (L2-resident across frames) through a
-// two-slot shared-memory ring: one TMA tensor copy (cp.async.bulk.tensor.2d,
-// 128-byte swizzle, no multicast) per 64-column panel, completing on an
-// mbarrier, issued one phase ahead of use; the swizzle makes the ldmatrix
-// reads bank-conflict free.  The 16-row tiles run on mma.sync m16n8k16 (bf16
-// in, f32 accumulate): at 16 rows the contraction is a weight-streaming GEMV,
-// below tcgen05's 64-row minimum.
+// Exchanges are pushes, not barriers: the data goes out with st.async to the
+// receivers' shared memory and completes on the receiver's round mbarrier;
+// every CTA also arrives (with the byte count it sent) on every CTA's round
+// mbarrier, so a completed round means every CTA finished the phase before
+// it.  No buffer written in a round is read by any CTA during that round, so
+// this ordering is enough.  Weight slices stream from global memory
+// (L2-resident across frames) through a two-slot ring of TMA tensor copies
+// (cp.async.bulk.tensor.2d, 128-byte swizzle, no multicast), one phase
+// ahead of use.  The 16-row tiles run on mma.sync m16n8k16 (bf16 in, f32
+// accumulate): at 16 rows each layer is a weight-streaming GEMV, below
+// tcgen05's 64-row minimum.  Every wait is bounded; a timeout sets invalid
+// bit 4 for the tile's sessions instead of hanging.
 //
 // Supported shape: d_model 256, 4 heads, FFN 1024, 1 layer, in-projection
 // (the benchmark shape); others use the phase kernels in frame.cu.
@@ -66,50 +70,58 @@ constexpr int kG = kCS / kHeads;    // 4 CTAs per head
 constexpr int kHD = kHeadDim / kG;  // 16 head dims per CTA
 constexpr int kLd256 = kD + 8;
 constexpr int kLd768 = kEmbed + 8;
-constexpr int kLd1024 = kF + 8;
+constexpr int kLdH = kFC + 8;
 constexpr int kHeadCols = 128;  // head features per CTA (the last CTA: 2024 - 15*128 = 104)
 constexpr int kPanel = 64;      // TMA box inner extent: 64 bf16 = one 128-byte swizzle row
 constexpr int kSlotElems = kHeadCols * kD;  // 64 KB: the largest chunk (head slice)
-constexpr uint32_t kWaitLimit = 1u << 22;   // bounded mbarrier wait (try_wait suspends per call)
+constexpr unsigned long long kWaitLimitNs = 20000000ull;  // bounded mbarrier wait: 20 ms
 
 static_assert(kHeadDim % kG == 0 && kHD == 16, "head split");
-static_assert(16 * kEmbed <= kSlotElems && 48 * kD <= kSlotElems && 64 * kD <= kSlotElems && 16 * kF <= kSlotElems,
+static_assert(16 * kEmbed <= kSlotElems && 48 * kD <= kSlotElems && 64 * kD <= kSlotElems && kD * kFC <= kSlotElems,
               "ring slot");
-static_assert(kSampleScratchBytes <= kM * kLd1024 * 2, "sampler scratch aliases the FFN buffer");
 
 // TMA descriptors of the weight matrices (2D, bf16, 128-byte swizzle).
 struct WeightMaps {
-  CUtensorMap in_proj;  // [256][768]   box 64 x 16
-  CUtensorMap qkv;      // [768][256]   box 64 x 16
-  CUtensorMap o;        // [256][256]   box 64 x 16
-  CUtensorMap ffn1;     // [1024][256]  box 64 x 64
-  CUtensorMap ffn2;     // [256][1024]  box 64 x 16
+  CUtensorMap in_proj;  // [256][768]    box 64 x 16
+  CUtensorMap qkv;      // [768][256]    box 64 x 16
+  CUtensorMap o;        // [256][256]    box 64 x 16
+  CUtensorMap ffn1;     // [1024][256]   box 64 x 64
+  CUtensorMap ffn2;     // [256][1024]   box 64 x 256 (a 64-column K slice)
   CUtensorMap head;     // [16*2024][256] box 64 x 128
 };
 
-struct __align__(1024) Smem;
+// Shared buffer reused by phases that never overlap: the in-projection
+// source rows (position 0 / unfolded), the FFN2 partial sums received from
+// the 16 CTAs, and the sampler's scratch.
+union BigBuffer {
+  bf16 src[kM * kLd768];
+  float recv[kCS][kM][kDC];
+  unsigned char sample_scratch[kSampleScratchBytes];
+};
+
 struct __align__(1024) Smem {
   bf16 ring[2][kSlotElems];  // 1024-byte aligned panels (128-byte swizzle atoms)
-  bf16 x[kM * kLd256];      // residual stream, all rows, all features
-  bf16 xa[kM * kLd256];     // LN output / attention output
-  bf16 big[kM * kLd1024];   // in-projection source rows (ld 776) / FFN hidden (ld 1032) / sampler scratch
+  bf16 x[kM * kLd256];       // residual stream, all rows, all features
+  bf16 xa[kM * kLd256];      // LN output / attention output
+  BigBuffer big;
+  bf16 hc[kM * kLdH];        // this CTA's FFN1 features (GELU output)
   bf16 kv[2][kM][kPositions][kHD];
   bf16 qs[kM][kHD];
-  float part[kG][kM][kPositions];
+  float part[kG][kM][kPositions];  // partial q.k received from the head group
   union {
-    bf16 lg[2 * kVocab];      // this CTA's session logits (owner), written by all CTAs
+    bf16 lg[2 * kVocab];       // this CTA's session logits (owner), written by all CTAs
     float red[8][kM * 8 * 2];  // cross-warp K-split partials
   } u;
-  bf16 stage[kM * kHeadCols];  // local slice before an all-gather
+  bf16 stage[kM * kHeadCols];  // outgoing slice (bf16) or partial scores (f32)
   SampleShared samp;
   int32_t tok[kM][kPositions];  // tokens of the tile's sessions (every CTA)
-  int32_t lead_token[kM];       // tokens feeding the next position (owner broadcast)
   int32_t sess[kM];             // stream ids of the tile's sessions
   int64_t ctr;                  // owner: working RNG counter
   int32_t inv;                  // owner: invalid flag
   int32_t n_sess;
   int32_t err;
-  unsigned long long mbar[2];
+  unsigned long long mbar[2];   // weight ring
+  unsigned long long xbar[2];   // exchange rounds, alternating by round parity
 };
 constexpr size_t kSmemBytes = sizeof(Smem) + 1024;
 
@@ -121,6 +133,12 @@ __device__ __forceinline__ uint32_t smem_addr(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
 
+__device__ __forceinline__ uint32_t cluster_addr(const void* local, int rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_addr(local)), "r"(rank));
+  return r;
+}
+
 __device__ __forceinline__ void mbar_init(unsigned long long* bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
 }
@@ -130,19 +148,53 @@ __device__ __forceinline__ void mbar_expect_tx(unsigned long long* bar, uint32_t
                : "memory");
 }
 
-// Returns false when the phase did not complete within the bounded wait.
+__device__ __forceinline__ unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Waits for the phase with the given parity; returns false when it did not
+// complete within kWaitLimitNs (the caller records the error and goes on, so
+// a broken exchange costs milliseconds, never a hang).
 __device__ __forceinline__ bool mbar_wait(unsigned long long* bar, uint32_t parity) {
   const uint32_t a = smem_addr(bar);
-  for (uint32_t i = 0; i < kWaitLimit; ++i) {
+  const unsigned long long t0 = global_ns();
+  while (true) {
     uint32_t done;
     asm volatile(
-        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n"
+        " selp.u32 %0, 1, 0, p;\n}\n"
         : "=r"(done)
         : "r"(a), "r"(parity)
         : "memory");
     if (done) return true;
+    if (global_ns() - t0 > kWaitLimitNs) return false;
   }
-  return false;
+}
+
+// Arrive on a (possibly remote) cluster barrier, announcing `bytes` of st.async data.
+__device__ __forceinline__ void remote_arrive_expect(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.release.cluster.shared::cluster.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ void st_async_v4(uint32_t addr, const uint4& v, uint32_t bar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.b32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(addr),
+               "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w), "r"(bar)
+               : "memory");
+}
+
+__device__ __forceinline__ void st_async_v2f(uint32_t addr, float a, float b, uint32_t bar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v2.f32 [%0], {%1, %2}, [%3];" ::"r"(addr),
+               "f"(a), "f"(b), "r"(bar)
+               : "memory");
+}
+
+__device__ __forceinline__ void st_async_b32(uint32_t addr, uint32_t v, uint32_t bar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.b32 [%0], %1, [%2];" ::"r"(addr), "r"(v),
+               "r"(bar)
+               : "memory");
 }
 
 __device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
@@ -175,15 +227,15 @@ __device__ __forceinline__ void mma16816(float (&c)[4], const uint32_t (&a)[4], 
 
 // ---------------------------------------------------------------------------
 // 16-row GEMM on the tile: C[16][8*NT] = A[16][16*KS] * B[8*NT][16*KS]^T.
-// Warps split N (WN warps) and, when N is narrow, K (KW chunks reduced in a
-// fixed order through shared memory).  Calls epi(row, col, value) once per
-// output element from the thread that holds it.
+// B is the weight slice in the ring: b_rows x (16*KS) stored as 64-column
+// panels of b_rows x 128 bytes, 128-byte swizzled (16-byte chunk j of row n at
+// chunk j ^ (n & 7)).  Warps split N (WN warps) and, when N is narrow, K (KW
+// chunks reduced in a fixed order through shared memory).  Calls
+// epi(row, col, v0, v1) once per pair of adjacent output columns (col even).
 // ---------------------------------------------------------------------------
 
 template <int NT, int KS, typename Epi>
 __device__ __forceinline__ void gemm16(const bf16* A, int lda, const bf16* B, int b_rows, float* red, Epi epi) {
-  // B: b_rows x (16*KS) weight slice stored as 64-column panels of b_rows x 128 B,
-  // 128-byte swizzled (16-byte chunk j of row n at chunk j ^ (n & 7)).
   constexpr int WN = NT < 8 ? NT : 8;
   constexpr int KW = 8 / WN;
   constexpr int NTW = NT / WN;
@@ -234,8 +286,8 @@ __device__ __forceinline__ void gemm16(const bf16* A, int lda, const bf16* B, in
 #pragma unroll
     for (int j = 0; j < NTW; ++j) {
       const int col0 = 8 * (wn * NTW + j) + 2 * (lane & 3);
-#pragma unroll
-      for (int e = 0; e < 4; ++e) epi((lane >> 2) + 8 * (e >> 1), col0 + (e & 1), acc[j][e]);
+      epi(lane >> 2, col0, acc[j][0], acc[j][1]);
+      epi((lane >> 2) + 8, col0, acc[j][2], acc[j][3]);
     }
   }
   __syncthreads();
@@ -290,31 +342,59 @@ __device__ __forceinline__ float gelu_tanh_f(float v) {
   return 0.5f * v * (1.0f + tanhf(inner));
 }
 
-// Copies a [16][cols] bf16 staging slice (row stride cols) into every CTA's
-// buffer at (dst_ld, dst_col).  cols * 2 and dst_col * 2 are multiples of 16.
-__device__ __forceinline__ void all_gather16(cg::cluster_group& cluster, const bf16* stage, int cols, bf16* dst,
-                                             int dst_ld, int dst_col) {
-  const int chunks_per_row = cols / 8;
-  const int chunks = kM * chunks_per_row;
+// ---------------------------------------------------------------------------
+// exchange rounds
+// ---------------------------------------------------------------------------
+
+// Exchange round r uses barrier xbar[r & 1]; its (r >> 1)-th phase.  Two
+// barriers keep a fast CTA's next-round arrivals off a barrier that is still
+// collecting this round (no CTA can start round r + 2 before every CTA has
+// finished round r).
+struct Round {
+  uint32_t r = 0;
+  __device__ __forceinline__ int bar() const { return static_cast<int>(r & 1u); }
+  __device__ __forceinline__ uint32_t parity() const { return (r >> 1) & 1u; }
+};
+
+// Pushes the [16][cols] bf16 staging slice to every CTA's buffer at
+// (dst_ld, dst_col) (cols * 2 and dst_col * 2 multiples of 16 bytes).
+__device__ __forceinline__ void push_all16(Smem& sm, const Round& rd, int cols, const bf16* dst, int dst_ld,
+                                           int dst_col) {
+  const int per_row = cols / 8;
+  const int chunks = kM * per_row;
   for (int i = threadIdx.x; i < chunks * kCS; i += blockDim.x) {
     const int rank = i / chunks, k = i % chunks;
-    const int r = k / chunks_per_row, cc = k % chunks_per_row;
-    const uint4 v = *reinterpret_cast<const uint4*>(stage + r * cols + cc * 8);
-    bf16* remote = cluster.map_shared_rank(dst, rank);
-    *reinterpret_cast<uint4*>(remote + r * dst_ld + dst_col + cc * 8) = v;
+    const int r = k / per_row, cc = k % per_row;
+    const uint4 v = *reinterpret_cast<const uint4*>(sm.stage + r * cols + cc * 8);
+    st_async_v4(cluster_addr(dst + r * dst_ld + dst_col + cc * 8, rank), v, cluster_addr(&sm.xbar[rd.bar()], rank));
   }
 }
 
-// Order of the weight chunks a CTA streams: chunk kinds 0 in-projection,
-// 1 qkv, 2 o, 3 FFN1, 4 FFN2, 5 head.  With the folded in-projection the
-// in-projection chunk exists only at position 0.
+// Every CTA arrives on every CTA's round barrier with the bytes it sent there,
+// then waits for its own round to complete.
+template <typename BytesTo>
+__device__ __forceinline__ void finish_round(Smem& sm, Round& rd, BytesTo bytes_to) {
+  if (threadIdx.x < kCS) {
+    const int d = static_cast<int>(threadIdx.x);
+    remote_arrive_expect(cluster_addr(&sm.xbar[rd.bar()], d), bytes_to(d));
+  }
+  if (sm.err == 0 && !mbar_wait(&sm.xbar[rd.bar()], rd.parity())) sm.err = 1;
+  ++rd.r;
+  __syncthreads();
+}
+
+// ---------------------------------------------------------------------------
+// weight stream
+// ---------------------------------------------------------------------------
+
+// Chunk kinds: 0 in-projection, 1 qkv, 2 o, 3 FFN1, 4 FFN2 (K slice), 5 head.
+// With the folded in-projection the in-projection chunk exists only at p = 0.
 __device__ __forceinline__ int chunk_index(bool folded, int p, int k) {
   return folded ? (k == 0 ? 0 : 1 + 5 * p + (k - 1)) : 6 * p + k;
 }
 
-// Rows of chunk kind k for CTA c (slot layout: 64-column panels of rows x 128 B).
 __device__ __forceinline__ int chunk_rows(int k) {
-  return k == 1 ? 3 * kHD : (k == 3 ? kFC : (k == 5 ? kHeadCols : kDC));
+  return k == 1 ? 3 * kHD : (k == 3 ? kFC : (k == 4 ? kD : (k == 5 ? kHeadCols : kDC)));
 }
 
 // Weight chunk (p, k) for CTA c: one TMA tensor copy per 64-column panel,
@@ -325,17 +405,17 @@ __device__ __forceinline__ void issue_chunk(const WeightMaps& maps, Smem& sm, bo
   const int lane = threadIdx.x & 31;
   const int rows = chunk_rows(k);
   const CUtensorMap* map;
-  int K, row0 = 0, requests;
+  int K, x0 = 0, row0 = 0;
   switch (k) {
     case 0: map = &maps.in_proj; K = kEmbed; row0 = kDC * c; break;
     case 1: map = &maps.qkv; K = kD; break;
     case 2: map = &maps.o; K = kD; row0 = kDC * c; break;
     case 3: map = &maps.ffn1; K = kD; row0 = kFC * c; break;
-    case 4: map = &maps.ffn2; K = kF; row0 = kDC * c; break;
+    case 4: map = &maps.ffn2; K = kFC; x0 = kFC * c; break;
     default: map = &maps.head; K = kD; row0 = p * kVocab + kHeadCols * c; break;
   }
   const int panels = K / kPanel;
-  requests = k == 1 ? 3 * panels : panels;
+  const int requests = k == 1 ? 3 * panels : panels;
   if (lane == 0) {
     fence_proxy_async();
     mbar_expect_tx(&sm.mbar[slot], static_cast<uint32_t>(rows * K * 2));
@@ -347,9 +427,25 @@ __device__ __forceinline__ void issue_chunk(const WeightMaps& maps, Smem& sm, bo
       const int y = part * kD + (c / kG) * kHeadDim + (c % kG) * kHD;
       tma_load_2d(dst + pp * (rows * kPanel) + part * (kHD * kPanel), map, pp * kPanel, y, &sm.mbar[slot]);
     } else {
-      tma_load_2d(dst + lane * (rows * kPanel), map, lane * kPanel, row0, &sm.mbar[slot]);
+      tma_load_2d(dst + lane * (rows * kPanel), map, x0 + lane * kPanel, row0, &sm.mbar[slot]);
     }
   }
+}
+
+// Waits for weight chunk (p, k) and issues the next chunk of the stream into
+// the other slot (freed by the previous weight GEMM).  Returns the slot.
+__device__ __forceinline__ const bf16* next_weights(const WeightMaps& maps, Smem& sm, bool folded, int p, int k,
+                                                    int c) {
+  const int idx = chunk_index(folded, p, k);
+  int np = p, nk = k + 1;
+  if (nk == 6) {
+    np = p + 1;
+    nk = folded ? 1 : 0;
+  }
+  if ((threadIdx.x >> 5) == 0 && np < kPositions) issue_chunk(maps, sm, folded, np, nk, c);
+  if (sm.err == 0 && !mbar_wait(&sm.mbar[idx & 1], (idx >> 1) & 1)) sm.err = 1;
+  __syncthreads();
+  return sm.ring[idx & 1];
 }
 
 __device__ __forceinline__ int64_t fused_input_token(const Frame& f, const Smem& sm, int s_local, int p) {
@@ -360,27 +456,16 @@ __device__ __forceinline__ int64_t fused_input_token(const Frame& f, const Smem&
   return sm.tok[s_local][p];
 }
 
-// Waits for weight chunk (p, k) and issues the next chunk of the stream into
-// the other slot (freed by the previous weight phase).  Returns the slot.
-__device__ __forceinline__ const bf16* next_weights(const WeightMaps& maps, Smem& sm, bool folded, int p, int k,
-                                                    int c) {
-  const int idx = chunk_index(folded, p, k);
-  int np = p, nk = k + 1;
-  if (nk == 6) {
-    np = p + 1;
-    nk = folded ? 1 : 0;
-  }
-  if ((threadIdx.x >> 5) == 0 && np < kPositions) issue_chunk(maps, sm, folded, np, nk, c);
-  if (!mbar_wait(&sm.mbar[idx & 1], (idx >> 1) & 1)) sm.err = 1;
-  __syncthreads();
-  return sm.ring[idx & 1];
+__device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<const uint32_t*>(&h);
 }
 
 __global__ void __cluster_dims__(kCS, 1, 1) __launch_bounds__(kThreads, 1)
     fused_frame_kernel(Frame f, const __grid_constant__ WeightMaps maps) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   // swizzled TMA destinations need 1024-byte alignment: align inside the
-  // allocation (sized kSmemBytes = sizeof(Smem) + 1024); uniform across CTAs
+  // allocation (kSmemBytes = sizeof(Smem) + 1024); uniform across CTAs
   const uint32_t pad = (1024u - (smem_addr(smem_raw) & 1023u)) & 1023u;
   Smem& sm = *reinterpret_cast<Smem*>(smem_raw + pad);
   cg::cluster_group cluster = cg::this_cluster();
@@ -411,12 +496,14 @@ __global__ void __cluster_dims__(kCS, 1, 1) __launch_bounds__(kThreads, 1)
   }
   __syncthreads();
   const int n_sess = sm.n_sess;
-  if (n_sess == 0) return;  // uniform across the cluster: no DSMEM traffic, no barrier
+  if (n_sess == 0) return;  // uniform across the cluster: no DSMEM traffic
   const int rows = n_sess * rp;
 
   if (threadIdx.x == 0) {
     mbar_init(&sm.mbar[0], 1);
     mbar_init(&sm.mbar[1], 1);
+    mbar_init(&sm.xbar[0], kCS);
+    mbar_init(&sm.xbar[1], kCS);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncthreads();
@@ -442,13 +529,14 @@ __global__ void __cluster_dims__(kCS, 1, 1) __launch_bounds__(kThreads, 1)
       f.eos_slot[sid] = -1;
     }
   }
-  cluster.sync();  // every CTA of the cluster is running before any DSMEM access
+  cluster.sync();  // every CTA is running and its barriers initialised before any DSMEM access
 
+  Round rd;
   const int head = c / kG, ds = c % kG;
+  const uint32_t slice_bytes = kM * kDC * 2;  // a [16][16] bf16 slice
   for (int p = 0; p < kPositions; ++p) {
     // ---------------- Ph0: in-projection + position embedding
     if (p > 0 && folded) {
-      // x = bf16(emb_proj[p-1][token] + pos[p]), every CTA, all features, locally
       for (int i = threadIdx.x; i < kM * (kD / 8); i += blockDim.x) {
         const int r = i / (kD / 8), ch = i % (kD / 8);
         __align__(16) bf16 out[8];
@@ -482,48 +570,55 @@ __global__ void __cluster_dims__(kCS, 1, 1) __launch_bounds__(kThreads, 1)
           }
           v = *reinterpret_cast<const uint4*>(src + ch * 8);
         }
-        *reinterpret_cast<uint4*>(sm.big + r * kLd768 + ch * 8) = v;
+        *reinterpret_cast<uint4*>(sm.big.src + r * kLd768 + ch * 8) = v;
       }
       const bf16* w = next_weights(maps, sm, folded, p, 0, c);
-      gemm16<2, 48>(sm.big, kLd768, w, kDC, &sm.u.red[0][0], [&](int r, int j, float v) {
+      gemm16<2, 48>(sm.big.src, kLd768, w, kDC, &sm.u.red[0][0], [&](int r, int j, float v0, float v1) {
         const int n = kDC * c + j;
-        const float y = round_bf16(__fadd_rn(v, bf2f(f.in_b[n])));
-        sm.stage[r * kDC + j] = f2bf(__fadd_rn(y, bf2f(f.pos[static_cast<int64_t>(p) * kD + n])));
+        const float y0 = round_bf16(__fadd_rn(v0, bf2f(f.in_b[n])));
+        const float y1 = round_bf16(__fadd_rn(v1, bf2f(f.in_b[n + 1])));
+        const bf16* pos = f.pos + static_cast<int64_t>(p) * kD + n;
+        *reinterpret_cast<uint32_t*>(sm.stage + r * kDC + j) =
+            pack_bf16x2(__fadd_rn(y0, bf2f(pos[0])), __fadd_rn(y1, bf2f(pos[1])));
       });
-      all_gather16(cluster, sm.stage, kDC, sm.x, kLd256, kDC * c);
-      cluster.sync();  // B1
+      push_all16(sm, rd, kDC, sm.x, kLd256, kDC * c);
+      finish_round(sm, rd, [&](int) { return slice_bytes; });
     }
 
-    // ---------------- Ph1: LN1, qkv slice, partial scores
+    // ---------------- Ph1: LN1, qkv slice, partial scores to the head group
     layer_norm16(sm.x, sm.xa, f.ln1);
     {
       const bf16* w = next_weights(maps, sm, folded, p, 1, c);
-      gemm16<6, 16>(sm.xa, kLd256, w, 3 * kHD, &sm.u.red[0][0], [&](int r, int j, float v) {
-        const bf16 y = f2bf(v);
-        const int part = j / kHD, i = j % kHD;
+      gemm16<6, 16>(sm.xa, kLd256, w, 3 * kHD, &sm.u.red[0][0], [&](int r, int j, float v0, float v1) {
+        const int part = j / kHD, i = j % kHD;  // j even: the pair stays inside one part
+        const uint32_t y = pack_bf16x2(v0, v1);
         if (part == 0) {
-          sm.qs[r][i] = y;
+          *reinterpret_cast<uint32_t*>(&sm.qs[r][i]) = y;
         } else {
-          sm.kv[part - 1][r][p][i] = y;
+          *reinterpret_cast<uint32_t*>(&sm.kv[part - 1][r][p][i]) = y;
         }
       });
     }
     {
+      float* scores = reinterpret_cast<float*>(sm.stage);  // [16][16] f32
       const int r = threadIdx.x >> 4, jk = threadIdx.x & 15;
       float s = 0.f;
       if (jk <= p) {
 #pragma unroll
         for (int i = 0; i < kHD; ++i) s = fmaf(bf2f(sm.qs[r][i]), bf2f(sm.kv[0][r][jk][i]), s);
       }
-#pragma unroll
-      for (int g = 0; g < kG; ++g) {
-        float* remote = cluster.map_shared_rank(&sm.part[0][0][0], head * kG + g);
-        remote[(ds * kM + r) * kPositions + jk] = s;
-      }
+      scores[r * kPositions + jk] = s;
+      __syncthreads();
+      // 1 KB to each of the 4 CTAs of head h: 64 chunks each
+      const int g = threadIdx.x >> 6, ch = threadIdx.x & 63;
+      const int dst = head * kG + g;
+      const uint4 v = *reinterpret_cast<const uint4*>(scores + ch * 4);
+      st_async_v4(cluster_addr(reinterpret_cast<const float*>(&sm.part[ds][0][0]) + ch * 4, dst), v,
+                  cluster_addr(&sm.xbar[rd.bar()], dst));
     }
-    cluster.sync();  // B2
+    finish_round(sm, rd, [&](int d) { return d / kG == head ? uint32_t(kM * kPositions * 4) : 0u; });
 
-    // ---------------- Ph2: attention (head, dims slice)
+    // ---------------- Ph2: attention (head, dims slice), all-gathered
     {
       const int r = threadIdx.x >> 4, jk = threadIdx.x & 15;
       float s = -CUDART_INF_F;
@@ -550,70 +645,85 @@ __global__ void __cluster_dims__(kCS, 1, 1) __launch_bounds__(kThreads, 1)
       sm.stage[r * kHD + jk] = f2bf(o_acc);
     }
     __syncthreads();
-    all_gather16(cluster, sm.stage, kHD, sm.xa, kLd256, head * kHeadDim + ds * kHD);
-    cluster.sync();  // B3
+    push_all16(sm, rd, kHD, sm.xa, kLd256, head * kHeadDim + ds * kHD);
+    finish_round(sm, rd, [&](int) { return slice_bytes; });
 
-    // ---------------- Ph3: o-projection + residual
+    // ---------------- Ph3: o-projection + residual, all-gathered
     {
       const bf16* w = next_weights(maps, sm, folded, p, 2, c);
-      gemm16<2, 16>(sm.xa, kLd256, w, kDC, &sm.u.red[0][0], [&](int r, int j, float v) {
+      gemm16<2, 16>(sm.xa, kLd256, w, kDC, &sm.u.red[0][0], [&](int r, int j, float v0, float v1) {
         const int n = kDC * c + j;
-        sm.stage[r * kDC + j] = f2bf(__fadd_rn(bf2f(sm.x[r * kLd256 + n]), round_bf16(v)));
+        const float x0 = bf2f(sm.x[r * kLd256 + n]), x1 = bf2f(sm.x[r * kLd256 + n + 1]);
+        *reinterpret_cast<uint32_t*>(sm.stage + r * kDC + j) =
+            pack_bf16x2(__fadd_rn(x0, round_bf16(v0)), __fadd_rn(x1, round_bf16(v1)));
       });
     }
-    all_gather16(cluster, sm.stage, kDC, sm.x, kLd256, kDC * c);
-    cluster.sync();  // B4
+    push_all16(sm, rd, kDC, sm.x, kLd256, kDC * c);
+    finish_round(sm, rd, [&](int) { return slice_bytes; });
 
-    // ---------------- Ph4: LN2, FFN1 + GELU
+    // ---------------- Ph4: LN2, FFN1 slice + GELU, FFN2 partials to the owners
     layer_norm16(sm.x, sm.xa, f.ln2);
     {
       const bf16* w = next_weights(maps, sm, folded, p, 3, c);
-      gemm16<8, 16>(sm.xa, kLd256, w, kFC, &sm.u.red[0][0], [&](int r, int j, float v) {
-        sm.stage[r * kFC + j] = f2bf(gelu_tanh_f(round_bf16(v)));
+      gemm16<8, 16>(sm.xa, kLd256, w, kFC, &sm.u.red[0][0], [&](int r, int j, float v0, float v1) {
+        *reinterpret_cast<uint32_t*>(sm.hc + r * kLdH + j) =
+            pack_bf16x2(gelu_tanh_f(round_bf16(v0)), gelu_tanh_f(round_bf16(v1)));
       });
     }
-    all_gather16(cluster, sm.stage, kFC, sm.big, kLd1024, kFC * c);
-    cluster.sync();  // B5
-
-    // ---------------- Ph5: FFN2 + residual
     {
       const bf16* w = next_weights(maps, sm, folded, p, 4, c);
-      gemm16<2, 64>(sm.big, kLd1024, w, kDC, &sm.u.red[0][0], [&](int r, int j, float v) {
-        const int n = kDC * c + j;
-        sm.stage[r * kDC + j] = f2bf(__fadd_rn(bf2f(sm.x[r * kLd256 + n]), round_bf16(v)));
+      gemm16<32, 4>(sm.hc, kLdH, w, kD, &sm.u.red[0][0], [&](int r, int j, float v0, float v1) {
+        const int dst = j / kDC;
+        st_async_v2f(cluster_addr(&sm.big.recv[c][r][j % kDC], dst), v0, v1, cluster_addr(&sm.xbar[rd.bar()], dst));
       });
     }
-    all_gather16(cluster, sm.stage, kDC, sm.x, kLd256, kDC * c);
-    cluster.sync();  // B6
+    finish_round(sm, rd, [&](int) { return uint32_t(kM * kDC * 4); });
+
+    // ---------------- Ph5: FFN2 output features (16 partials in CTA order) + residual
+    {
+      const int r = threadIdx.x >> 4, j = threadIdx.x & 15;
+      float acc = 0.f;
+#pragma unroll
+      for (int s = 0; s < kCS; ++s) acc += sm.big.recv[s][r][j];
+      const int n = kDC * c + j;
+      sm.stage[r * kDC + j] = f2bf(__fadd_rn(bf2f(sm.x[r * kLd256 + n]), round_bf16(acc)));
+    }
+    __syncthreads();
+    push_all16(sm, rd, kDC, sm.x, kLd256, kDC * c);
+    finish_round(sm, rd, [&](int) { return slice_bytes; });
 
     // ---------------- Ph6: head p; logits rows to the owners
     const int hcols = c < kCS - 1 ? kHeadCols : kVocab - (kCS - 1) * kHeadCols;
     {
       const bf16* w = next_weights(maps, sm, folded, p, 5, c);
-      gemm16<16, 16>(sm.x, kLd256, w, kHeadCols, &sm.u.red[0][0], [&](int r, int j, float v) {
-        if (j < hcols) {
+      gemm16<16, 16>(sm.x, kLd256, w, kHeadCols, &sm.u.red[0][0], [&](int r, int j, float v0, float v1) {
+        if (j < hcols) {  // hcols is even: pairs never straddle it
           const int n = kHeadCols * c + j;
-          const bf16 y = f2bf(__fadd_rn(v, bf2f(f.head_b[static_cast<int64_t>(p) * kVocab + n])));
-          sm.stage[r * kHeadCols + j] = y;
+          const bf16* hb = f.head_b + static_cast<int64_t>(p) * kVocab + n;
+          const bf16 y0 = f2bf(__fadd_rn(v0, bf2f(hb[0])));
+          const bf16 y1 = f2bf(__fadd_rn(v1, bf2f(hb[1])));
+          sm.stage[r * kHeadCols + j] = y0;
+          sm.stage[r * kHeadCols + j + 1] = y1;
           if (f.logits_out && r < rows) {
             const int sl = r / rp, sub = r % rp;
-            f.logits_out[((static_cast<int64_t>(sm.sess[sl]) * kPositions + p) * rp + sub) * kVocab + n] = y;
+            bf16* lo = f.logits_out + ((static_cast<int64_t>(sm.sess[sl]) * kPositions + p) * rp + sub) * kVocab + n;
+            lo[0] = y0;
+            lo[1] = y1;
           }
         }
       });
     }
     {
-      const int chunks_per_row = hcols / 8;
-      const int total = rows * chunks_per_row;
-      for (int i = threadIdx.x; i < total; i += blockDim.x) {
-        const int r = i / chunks_per_row, cc = i % chunks_per_row;
+      const int per_row = hcols / 8;
+      for (int i = threadIdx.x; i < rows * per_row; i += blockDim.x) {
+        const int r = i / per_row, cc = i % per_row;
         const int sl = r / rp, sub = r % rp;
         const uint4 v = *reinterpret_cast<const uint4*>(sm.stage + r * kHeadCols + cc * 8);
-        bf16* remote = cluster.map_shared_rank(&sm.u.lg[0], sl);
-        *reinterpret_cast<uint4*>(remote + sub * kVocab + kHeadCols * c + cc * 8) = v;
+        st_async_v4(cluster_addr(&sm.u.lg[sub * kVocab + kHeadCols * c + cc * 8], sl), v,
+                    cluster_addr(&sm.xbar[rd.bar()], sl));
       }
     }
-    cluster.sync();  // B7
+    finish_round(sm, rd, [&](int d) { return d < n_sess ? uint32_t(rp * hcols * 2) : 0u; });
 
     // ---------------- Ph7: owner samples, broadcasts the token
     if (owner) {
@@ -628,10 +738,10 @@ __global__ void __cluster_dims__(kCS, 1, 1) __launch_bounds__(kThreads, 1)
       call.seed = f.seed[sid];
       call.counter = sm.ctr;
       int invalid = 0;
-      const int token = sample_block(call, f.prm, sm.samp, sm.big, &invalid);
+      const int token = sample_block(call, f.prm, sm.samp, sm.big.sample_scratch, &invalid);
       if (threadIdx.x < kCS) {
-        int32_t* remote = cluster.map_shared_rank(&sm.tok[0][0], static_cast<int>(threadIdx.x));
-        remote[c * kPositions + p] = token;
+        const int d = static_cast<int>(threadIdx.x);
+        st_async_b32(cluster_addr(&sm.tok[c][p], d), static_cast<uint32_t>(token), cluster_addr(&sm.xbar[rd.bar()], d));
       }
       if (threadIdx.x == 0) {
         sm.inv |= invalid;
@@ -639,7 +749,7 @@ __global__ void __cluster_dims__(kCS, 1, 1) __launch_bounds__(kThreads, 1)
         if (!f.prm.argmax && counter_valid) sm.ctr = call.counter + 1;
       }
     }
-    cluster.sync();  // B8
+    finish_round(sm, rd, [&](int) { return owner ? 4u : 0u; });
   }
 
   // ---- commit (owner): tokens, counter, flags, next-frame embedding
@@ -667,6 +777,7 @@ __global__ void __cluster_dims__(kCS, 1, 1) __launch_bounds__(kThreads, 1)
       f.next_emb[static_cast<int64_t>(sid) * kEmbed + k] = f2bf(__fdiv_rn(acc, 16.0f));
     }
   }
+  cluster.sync();  // no CTA leaves while a peer may still address its shared memory
 }
 
 // EOS decision for the sessions the fused kernel registered; resets the count.
@@ -747,7 +858,7 @@ cudaError_t launch_fused_frame(const Frame& f, cudaStream_t stream) {
   WeightMaps maps;
   if (!make_map(&maps.in_proj, f.in_w, kEmbed, kD, kDC) || !make_map(&maps.qkv, f.qkv, kD, 3 * kD, kHD) ||
       !make_map(&maps.o, f.o, kD, kD, kDC) || !make_map(&maps.ffn1, f.w1, kD, kF, kFC) ||
-      !make_map(&maps.ffn2, f.w2, kF, kD, kDC) ||
+      !make_map(&maps.ffn2, f.w2, kF, kD, kD) ||
       !make_map(&maps.head, f.head_w, kD, static_cast<uint64_t>(kPositions) * kVocab, kHeadCols)) {
     return cudaErrorInvalidValue;
   }

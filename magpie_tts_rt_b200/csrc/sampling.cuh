@@ -32,6 +32,8 @@ struct SampleShared {
   uint32_t warp_nonfinite[kSampleWarps];
   uint32_t warp_count[kSampleWarps];
   uint32_t warp_finite[kSampleWarps];
+  uint32_t warp_max[kSampleWarps];
+  uint32_t window_ok;
   float warp_best[kSampleWarps];
   int32_t warp_best_id[kSampleWarps];
   int32_t finite_count;
@@ -176,11 +178,88 @@ __device__ __forceinline__ void radix_pass(const uint32_t (&key)[kItems], int sh
   __syncthreads();
 }
 
+// Fast path for 16-bit keys: the k-th largest usually lies within 255 key
+// steps (bf16 ulps) below the maximum key M.  One histogram of M - key over
+// that window; if it holds at least k keys, the k-th largest is exact.
+// Returns false (nothing decided) otherwise.  Also publishes the finite count.
+__device__ __forceinline__ bool window_kth_key16(const uint32_t (&key)[kItems], int k, SampleShared& sh,
+                                                 uint32_t* hist, uint32_t* out) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int base = threadIdx.x * kItems;
+  uint32_t m = 0;
+#pragma unroll
+  for (int i = 0; i < kItems; ++i) m = (base + i < kVocab && key[i] > m) ? key[i] : m;
+  m = __reduce_max_sync(0xffffffffu, m);
+  uint32_t* wh = hist + warp * 256;
+#pragma unroll
+  for (int i = lane; i < 256; i += 32) wh[i] = 0;
+  if (lane == 0) sh.warp_max[warp] = m;
+  __syncthreads();
+#pragma unroll
+  for (int w = 0; w < kSampleWarps; ++w) m = sh.warp_max[w] > m ? sh.warp_max[w] : m;
+#pragma unroll
+  for (int i = 0; i < kItems; ++i) {
+    const uint32_t dist = m - key[i];
+    if (base + i < kVocab && dist < 256u) atomicAdd(&wh[dist], 1u);
+  }
+  __syncthreads();
+  if (warp == 0) {
+    // lane l owns distances 8l .. 8l+7 (descending keys)
+    uint32_t c[8];
+    uint32_t sum = 0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      uint32_t t = 0;
+#pragma unroll
+      for (int w = 0; w < kSampleWarps; ++w) t += hist[w * 256 + lane * 8 + j];
+      c[j] = t;
+      sum += t;
+    }
+    if (lane == 0) {
+      uint32_t finite = 0, nf = 0;
+#pragma unroll
+      for (int w = 0; w < kSampleWarps; ++w) {
+        finite += sh.warp_finite[w];
+        nf |= sh.warp_nonfinite[w];
+      }
+      sh.finite_count = static_cast<int32_t>(finite);
+      sh.nonfinite = nf ? 1 : 0;
+    }
+    uint32_t incl = sum;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += y;
+    }
+    const uint32_t excl = incl - sum;
+    const uint32_t kk = static_cast<uint32_t>(k);
+    if (lane == 31) sh.window_ok = incl >= kk ? 1u : 0u;
+    if (excl < kk && kk <= incl) {
+      uint32_t acc = excl;
+      int j = 0;
+      for (; j < 7; ++j) {
+        if (kk <= acc + c[j]) break;
+        acc += c[j];
+      }
+      sh.digit_and_remaining[0] = m - static_cast<uint32_t>(lane * 8 + j);
+    }
+  }
+  __syncthreads();
+  *out = sh.digit_and_remaining[0];
+  const bool ok = sh.window_ok != 0;
+  __syncthreads();  // sh is rewritten by the fallback passes
+  return ok;
+}
+
 // Exact k-th largest key over the block (k >= 1, k <= number of valid tokens).
 // KEY_BITS is 16 (bf16-valued logits: key = top half of the f32 key) or 32.
 template <int KEY_BITS>
 __device__ __forceinline__ uint32_t block_kth_key(const uint32_t (&key)[kItems], int k, SampleShared& sh,
                                                   uint32_t* hist) {
+  if constexpr (KEY_BITS == 16) {
+    uint32_t t;
+    if (window_kth_key16(key, k, sh, hist, &t)) return t;
+  }
   uint32_t prefix = 0, mask = 0;
   uint32_t remaining = static_cast<uint32_t>(k);
   radix_pass<true>(key, KEY_BITS - 8, prefix, mask, remaining, sh, hist);
@@ -189,7 +268,6 @@ __device__ __forceinline__ uint32_t block_kth_key(const uint32_t (&key)[kItems],
   remaining = sh.digit_and_remaining[1];
 #pragma unroll
   for (int shift = KEY_BITS - 16; shift >= 0; shift -= 8) {
-    __syncthreads();  // every thread has read the previous pass's result
     radix_pass<false>(key, shift, prefix, mask, remaining, sh, hist);
     prefix |= sh.digit_and_remaining[0] << shift;
     mask |= 0xffu << shift;
