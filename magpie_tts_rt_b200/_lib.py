@@ -99,6 +99,7 @@ class SamplingConfig(ctypes.Structure):
 PATH_AUTO = 0
 PATH_PHASE_KERNELS = 1
 PATH_FUSED_CLUSTER = 2
+PATH_FUSED_TILE = 3
 
 
 class StreamBatch(ctypes.Structure):
@@ -127,7 +128,7 @@ SIGNATURES = {
               ctypes.POINTER(StreamBatch), P, SZ, P]),
     "mtt_b200_local_ar_frame_launch_count": (
         I32, [ctypes.POINTER(Shape), ctypes.POINTER(SamplingConfig), I32]),
-    "mtt_b200_local_ar_frame_path": (I32, [ctypes.POINTER(Shape), ctypes.POINTER(SamplingConfig)]),
+    "mtt_b200_local_ar_frame_path": (I32, [ctypes.POINTER(Shape), ctypes.POINTER(SamplingConfig), I32]),
     "mtt_b200_fold_in_projection_bytes": (SZ, [ctypes.POINTER(Shape)]),
     "mtt_b200_launch_fold_in_projection": (
         I32, [ctypes.POINTER(Shape), ctypes.POINTER(Weights), P, P]),

@@ -436,8 +436,12 @@ extern "C" MTT_B200_API size_t mtt_b200_local_ar_frame_workspace_size(const mtt_
 
 namespace {
 
-// Resolves the path for a shape / configuration on the current device.
-int32_t resolve_path(const mtt_b200_local_ar_shape_t* shape, const mtt_b200_sampling_config_t* sampling) {
+// Resolves the path for a shape / configuration / batch size on the current
+// device.  AUTO: the tile kernel (one CTA per 16-row tile) once the tiles
+// outnumber the fused kernel's concurrent clusters, the fused cluster kernel
+// below that (lower latency per tile), the phase kernels for other shapes.
+int32_t resolve_path(const mtt_b200_local_ar_shape_t* shape, const mtt_b200_sampling_config_t* sampling,
+                     int32_t n_streams) {
   mtt::Frame probe{};
   probe.d = shape->d_model;
   probe.L = shape->n_layers;
@@ -446,13 +450,21 @@ int32_t resolve_path(const mtt_b200_local_ar_shape_t* shape, const mtt_b200_samp
   probe.rp = sampling->cfg ? 2 : 1;
   probe.in_proj = shape->d_model != mtt::kEmbed;
   const bool fused = mtt::fused_frame_supported(probe);
+  const bool tile = mtt::tile_frame_supported(probe);
   switch (sampling->path) {
-    case MTT_B200_FRAME_PATH_AUTO:
-      return fused ? MTT_B200_FRAME_PATH_FUSED_CLUSTER : MTT_B200_FRAME_PATH_PHASE_KERNELS;
+    case MTT_B200_FRAME_PATH_AUTO: {
+      if (!fused && !tile) return MTT_B200_FRAME_PATH_PHASE_KERNELS;
+      const int spt = 16 / probe.rp;
+      const int tiles = (n_streams + spt - 1) / spt;
+      if (fused && (!tile || tiles <= mtt::fused_frame_clusters())) return MTT_B200_FRAME_PATH_FUSED_CLUSTER;
+      return MTT_B200_FRAME_PATH_FUSED_TILE;
+    }
     case MTT_B200_FRAME_PATH_PHASE_KERNELS:
       return MTT_B200_FRAME_PATH_PHASE_KERNELS;
     case MTT_B200_FRAME_PATH_FUSED_CLUSTER:
       return fused ? MTT_B200_FRAME_PATH_FUSED_CLUSTER : MTT_B200_STATUS_UNSUPPORTED;
+    case MTT_B200_FRAME_PATH_FUSED_TILE:
+      return tile ? MTT_B200_FRAME_PATH_FUSED_TILE : MTT_B200_STATUS_UNSUPPORTED;
     default:
       return MTT_B200_STATUS_INVALID_ARGUMENT;
   }
@@ -461,17 +473,20 @@ int32_t resolve_path(const mtt_b200_local_ar_shape_t* shape, const mtt_b200_samp
 }  // namespace
 
 extern "C" MTT_B200_API int32_t mtt_b200_local_ar_frame_path(const mtt_b200_local_ar_shape_t* shape,
-                                                             const mtt_b200_sampling_config_t* sampling) {
-  if (!mtt::shape_ok(shape) || sampling == nullptr) return MTT_B200_STATUS_INVALID_ARGUMENT;
-  return resolve_path(shape, sampling);
+                                                             const mtt_b200_sampling_config_t* sampling,
+                                                             int32_t n_streams) {
+  if (!mtt::shape_ok(shape) || sampling == nullptr || n_streams <= 0) return MTT_B200_STATUS_INVALID_ARGUMENT;
+  return resolve_path(shape, sampling, n_streams);
 }
 
 extern "C" MTT_B200_API int32_t mtt_b200_local_ar_frame_launch_count(const mtt_b200_local_ar_shape_t* shape,
                                                                      const mtt_b200_sampling_config_t* sampling,
                                                                      int32_t n_streams) {
   if (!mtt::shape_ok(shape) || sampling == nullptr || n_streams <= 0) return 0;
-  const int32_t path = resolve_path(shape, sampling);
-  if (path == MTT_B200_FRAME_PATH_FUSED_CLUSTER) return 3;  // fused frame, EOS projection, EOS finish
+  const int32_t path = resolve_path(shape, sampling, n_streams);
+  if (path == MTT_B200_FRAME_PATH_FUSED_CLUSTER || path == MTT_B200_FRAME_PATH_FUSED_TILE) {
+    return 3;  // fused frame, EOS projection, EOS finish
+  }
   if (path != MTT_B200_FRAME_PATH_PHASE_KERNELS) return 0;
   // begin + 16 x (embed + 5 per layer + head + sample) + eos projection + end
   return 1 + mtt::kPositions * (1 + 5 * shape->n_layers + 2) + 2;
@@ -562,10 +577,13 @@ extern "C" MTT_B200_API int mtt_b200_launch_local_ar_frame(const mtt_b200_local_
   f.eos_logit = reinterpret_cast<float*>(ws + lo.eos_logit);
 
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const int32_t path = resolve_path(shape, sampling);
+  const int32_t path = resolve_path(shape, sampling, b->n_streams);
   if (path < 0) return path;
   if (path == MTT_B200_FRAME_PATH_FUSED_CLUSTER) {
     return launch_fused_frame(f, st) == cudaSuccess ? MTT_B200_STATUS_OK : MTT_B200_STATUS_CUDA_ERROR;
+  }
+  if (path == MTT_B200_FRAME_PATH_FUSED_TILE) {
+    return launch_tile_frame(f, st) == cudaSuccess ? MTT_B200_STATUS_OK : MTT_B200_STATUS_CUDA_ERROR;
   }
   const int d = f.d, F = f.F;
   frame_begin_kernel<<<1, kBeginThreads, 0, st>>>(f);

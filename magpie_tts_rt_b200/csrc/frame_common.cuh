@@ -2,6 +2,8 @@
 // (phase kernels in frame.cu, fused cluster kernel in frame_fused.cu).
 #pragma once
 
+#include <cuda.h>
+
 #include <cstddef>
 
 #include "common.cuh"
@@ -78,6 +80,19 @@ inline Layout make_layout(int d, int L, int F, int n, int rp) {
 // Fused cluster kernel (frame_fused.cu).  Returns false when the shape or the
 // device cannot run it (the caller then uses the phase kernels).
 bool fused_frame_supported(const Frame& f);
+// Clusters of the fused kernel that fit on the device at once (0: unsupported).
+int fused_frame_clusters();
 cudaError_t launch_fused_frame(const Frame& f, cudaStream_t stream);
+
+// Tile kernel (frame_tile.cu): one CTA per 16-row tile, KV cache in TMEM.
+bool tile_frame_supported(const Frame& f);
+cudaError_t launch_tile_frame(const Frame& f, cudaStream_t stream);
+
+// EOS projection + decision for the sessions a fused or tile kernel registered.
+cudaError_t launch_frame_eos(const Frame& f, cudaStream_t stream);
+
+// 2D bf16 tensor map over a row-major [rows][cols] matrix, box 64 columns x
+// box_rows rows, 128-byte swizzle (false if the driver entry point is missing).
+bool make_weight_map(CUtensorMap* map, const void* base, uint64_t cols, uint64_t rows, uint32_t box_rows);
 
 }  // namespace mtt

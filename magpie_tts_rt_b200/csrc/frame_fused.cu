@@ -51,6 +51,7 @@
 #include <mutex>
 
 #include "frame_common.cuh"
+#include "ptx.cuh"
 #include "sampling.cuh"
 
 namespace cg = cooperative_groups;
@@ -124,106 +125,6 @@ struct __align__(1024) Smem {
   unsigned long long xbar[2];   // exchange rounds, alternating by round parity
 };
 constexpr size_t kSmemBytes = sizeof(Smem) + 1024;
-
-// ---------------------------------------------------------------------------
-// PTX helpers
-// ---------------------------------------------------------------------------
-
-__device__ __forceinline__ uint32_t smem_addr(const void* p) {
-  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-
-__device__ __forceinline__ uint32_t cluster_addr(const void* local, int rank) {
-  uint32_t r;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_addr(local)), "r"(rank));
-  return r;
-}
-
-__device__ __forceinline__ void mbar_init(unsigned long long* bar, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
-}
-
-__device__ __forceinline__ void mbar_expect_tx(unsigned long long* bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes)
-               : "memory");
-}
-
-__device__ __forceinline__ unsigned long long global_ns() {
-  unsigned long long t;
-  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
-  return t;
-}
-
-// Waits for the phase with the given parity; returns false when it did not
-// complete within kWaitLimitNs (the caller records the error and goes on, so
-// a broken exchange costs milliseconds, never a hang).
-__device__ __forceinline__ bool mbar_wait(unsigned long long* bar, uint32_t parity) {
-  const uint32_t a = smem_addr(bar);
-  const unsigned long long t0 = global_ns();
-  while (true) {
-    uint32_t done;
-    asm volatile(
-        "{\n .reg .pred p;\n mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n"
-        " selp.u32 %0, 1, 0, p;\n}\n"
-        : "=r"(done)
-        : "r"(a), "r"(parity)
-        : "memory");
-    if (done) return true;
-    if (global_ns() - t0 > kWaitLimitNs) return false;
-  }
-}
-
-// Arrive on a (possibly remote) cluster barrier, announcing `bytes` of st.async data.
-__device__ __forceinline__ void remote_arrive_expect(uint32_t bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.release.cluster.shared::cluster.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
-               : "memory");
-}
-
-__device__ __forceinline__ void st_async_v4(uint32_t addr, const uint4& v, uint32_t bar) {
-  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.b32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(addr),
-               "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w), "r"(bar)
-               : "memory");
-}
-
-__device__ __forceinline__ void st_async_v2f(uint32_t addr, float a, float b, uint32_t bar) {
-  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v2.f32 [%0], {%1, %2}, [%3];" ::"r"(addr),
-               "f"(a), "f"(b), "r"(bar)
-               : "memory");
-}
-
-__device__ __forceinline__ void st_async_b32(uint32_t addr, uint32_t v, uint32_t bar) {
-  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.b32 [%0], %1, [%2];" ::"r"(addr), "r"(v),
-               "r"(bar)
-               : "memory");
-}
-
-__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
-
-__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, unsigned long long* bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
-          "r"(smem_addr(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_addr(bar))
-      : "memory");
-}
-
-__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const void* p) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
-               : "r"(smem_addr(p)));
-}
-
-__device__ __forceinline__ void ldsm_x2(uint32_t (&r)[2], const void* p) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0,%1}, [%2];" : "=r"(r[0]), "=r"(r[1]) : "r"(smem_addr(p)));
-}
-
-__device__ __forceinline__ void mma16816(float (&c)[4], const uint32_t (&a)[4], const uint32_t (&b)[2]) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-      "{%0,%1,%2,%3};"
-      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
-}
 
 // ---------------------------------------------------------------------------
 // 16-row GEMM on the tile: C[16][8*NT] = A[16][16*KS] * B[8*NT][16*KS]^T.
@@ -456,10 +357,6 @@ __device__ __forceinline__ int64_t fused_input_token(const Frame& f, const Smem&
   return sm.tok[s_local][p];
 }
 
-__device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
-  const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
-  return *reinterpret_cast<const uint32_t*>(&h);
-}
 
 __global__ void __cluster_dims__(kCS, 1, 1) __launch_bounds__(kThreads, 1)
     fused_frame_kernel(Frame f, const __grid_constant__ WeightMaps maps) {
@@ -793,6 +690,8 @@ __global__ void __launch_bounds__(256) fused_eos_finish_kernel(Frame f) {
   if (threadIdx.x == 0) *f.eos_count = 0;
 }
 
+}  // namespace
+
 // ---------------------------------------------------------------------------
 // host: TMA descriptors
 // ---------------------------------------------------------------------------
@@ -816,7 +715,7 @@ EncodeTiledFn encode_tiled() {
   return fn;
 }
 
-bool make_map(CUtensorMap* map, const void* base, uint64_t cols, uint64_t rows, uint32_t box_rows) {
+bool make_weight_map(CUtensorMap* map, const void* base, uint64_t cols, uint64_t rows, uint32_t box_rows) {
   EncodeTiledFn fn = encode_tiled();
   if (fn == nullptr || base == nullptr) return false;
   const cuuint64_t dims[2] = {cols, rows};
@@ -828,15 +727,13 @@ bool make_map(CUtensorMap* map, const void* base, uint64_t cols, uint64_t rows, 
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-}  // namespace
 
-bool fused_frame_supported(const Frame& f) {
-  if (f.d != kD || f.H != kHeads || f.F != kF || f.L != 1 || !f.in_proj || (f.rp != 1 && f.rp != 2)) return false;
+int fused_frame_clusters() {
   static int cached = -1;  // per process: the cluster shape is a property of the device model
   static std::mutex mu;
   const std::lock_guard<std::mutex> lock(mu);
   if (cached < 0) {
-    int ok = 0;
+    int clusters = 0;
     if (encode_tiled() != nullptr &&
         cudaFuncSetAttribute(fused_frame_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(kSmemBytes)) == cudaSuccess &&
@@ -845,21 +742,25 @@ bool fused_frame_supported(const Frame& f) {
       cfg.gridDim = dim3(kCS);
       cfg.blockDim = dim3(kThreads);
       cfg.dynamicSmemBytes = kSmemBytes;
-      int clusters = 0;
-      if (cudaOccupancyMaxActiveClusters(&clusters, fused_frame_kernel, &cfg) == cudaSuccess && clusters > 0) ok = 1;
+      if (cudaOccupancyMaxActiveClusters(&clusters, fused_frame_kernel, &cfg) != cudaSuccess) clusters = 0;
     }
     cudaGetLastError();
-    cached = ok;
+    cached = clusters;
   }
-  return cached == 1;
+  return cached;
+}
+
+bool fused_frame_supported(const Frame& f) {
+  if (f.d != kD || f.H != kHeads || f.F != kF || f.L != 1 || !f.in_proj || (f.rp != 1 && f.rp != 2)) return false;
+  return fused_frame_clusters() > 0;
 }
 
 cudaError_t launch_fused_frame(const Frame& f, cudaStream_t stream) {
   WeightMaps maps;
-  if (!make_map(&maps.in_proj, f.in_w, kEmbed, kD, kDC) || !make_map(&maps.qkv, f.qkv, kD, 3 * kD, kHD) ||
-      !make_map(&maps.o, f.o, kD, kD, kDC) || !make_map(&maps.ffn1, f.w1, kD, kF, kFC) ||
-      !make_map(&maps.ffn2, f.w2, kF, kD, kD) ||
-      !make_map(&maps.head, f.head_w, kD, static_cast<uint64_t>(kPositions) * kVocab, kHeadCols)) {
+  if (!make_weight_map(&maps.in_proj, f.in_w, kEmbed, kD, kDC) || !make_weight_map(&maps.qkv, f.qkv, kD, 3 * kD, kHD) ||
+      !make_weight_map(&maps.o, f.o, kD, kD, kDC) || !make_weight_map(&maps.ffn1, f.w1, kD, kF, kFC) ||
+      !make_weight_map(&maps.ffn2, f.w2, kF, kD, kD) ||
+      !make_weight_map(&maps.head, f.head_w, kD, static_cast<uint64_t>(kPositions) * kVocab, kHeadCols)) {
     return cudaErrorInvalidValue;
   }
   const int spt = kM / f.rp;
@@ -867,6 +768,10 @@ cudaError_t launch_fused_frame(const Frame& f, cudaStream_t stream) {
   cudaError_t e = cudaMemsetAsync(f.eos_count, 0, sizeof(int32_t), stream);
   if (e != cudaSuccess) return e;
   fused_frame_kernel<<<tiles * kCS, kThreads, kSmemBytes, stream>>>(f, maps);
+  return launch_frame_eos(f, stream);
+}
+
+cudaError_t launch_frame_eos(const Frame& f, cudaStream_t stream) {
   EosArgs ea;
   ea.hidden = f.hidden;
   ea.hidden_stream_stride = static_cast<int64_t>(f.rp) * kEmbed;

@@ -191,8 +191,13 @@ class LocalArEngine:
 
     @property
     def path(self) -> int:
-        """Resolved frame path on the current device (1 phase kernels, 2 fused cluster)."""
-        return int(L.lib.mtt_b200_local_ar_frame_path(ctypes.byref(self._shape), ctypes.byref(self._sampling)))
+        """Frame path for a full batch of ``max_streams`` on the current device
+        (1 phase kernels, 2 fused cluster kernel, 3 tile kernel)."""
+        return self.path_for(self.max_streams)
+
+    def path_for(self, n_streams: int) -> int:
+        return int(L.lib.mtt_b200_local_ar_frame_path(ctypes.byref(self._shape), ctypes.byref(self._sampling),
+                                                      n_streams))
 
     def launch_count(self, n_streams: int) -> int:
         return int(L.lib.mtt_b200_local_ar_frame_launch_count(ctypes.byref(self._shape),

@@ -91,9 +91,10 @@ def test_workspace_sizes():
     assert L.lib.mtt_b200_local_ar_frame_workspace_size(ctypes.byref(ok), 0, 1) == 0
     phase = L.SamplingConfig(80, 0.6, 2.5, 0, 1, L.PATH_PHASE_KERNELS)
     assert L.lib.mtt_b200_local_ar_frame_launch_count(ctypes.byref(ok), ctypes.byref(phase), 64) == 16 * 8 + 3
-    assert L.lib.mtt_b200_local_ar_frame_path(ctypes.byref(ok), ctypes.byref(phase)) == L.PATH_PHASE_KERNELS
+    assert L.lib.mtt_b200_local_ar_frame_path(ctypes.byref(ok), ctypes.byref(phase), 64) == L.PATH_PHASE_KERNELS
+    assert L.lib.mtt_b200_local_ar_frame_path(ctypes.byref(ok), ctypes.byref(phase), 0) == -1
     bad_path = L.SamplingConfig(80, 0.6, 2.5, 0, 1, 7)
-    assert L.lib.mtt_b200_local_ar_frame_path(ctypes.byref(ok), ctypes.byref(bad_path)) == -1
+    assert L.lib.mtt_b200_local_ar_frame_path(ctypes.byref(ok), ctypes.byref(bad_path), 64) == -1
 
 
 def test_null_arguments_rejected_without_launch():

@@ -25,8 +25,8 @@ from oracle import sampler as S
 pytestmark = pytest.mark.gpu
 
 RTOL = 1e-2
-PATH_AUTO, PHASE, FUSED = 0, 1, 2
-BOTH = [PHASE, FUSED]
+PATH_AUTO, PHASE, FUSED, TILE = 0, 1, 2, 3
+BOTH = [PHASE, FUSED, TILE]
 
 
 def bits(t):
@@ -142,11 +142,11 @@ def engines():
     from magpie_tts_rt_b200.local_ar import LocalArEngine
     cache = {}
 
-    def get(shape, seed, max_streams, cfg=True, argmax=False, with_final=True, path=PATH_AUTO):
-        key = (shape, seed, max_streams, cfg, argmax, with_final, path)
+    def get(shape, seed, max_streams, cfg=True, argmax=False, with_final=True, path=PATH_AUTO, fold=True):
+        key = (shape, seed, max_streams, cfg, argmax, with_final, path, fold)
         if key not in cache:
             cache[key] = LocalArEngine(weights(shape, seed, with_final), max_streams=max_streams, cfg=cfg,
-                                       argmax=argmax, path=path)
+                                       argmax=argmax, path=path, fold_in_projection=fold)
         return cache[key]
     return get
 
@@ -160,11 +160,13 @@ def _hidden(n, seed, cfg=True):
 FLAGS6 = ([0, 1, 0, 0, 0, 1], [0, 0, 0, 1, 0, 1], [0, 0, 1, 0, 0, 0])  # incl. an invalid overlap
 
 
-@pytest.mark.parametrize("shape,n,path", [(SHAPE_BASELINE, 6, PHASE), (SHAPE_BASELINE, 6, FUSED),
-                                          (SHAPE_BASELINE, 11, FUSED), (SHAPE_SOFIA, 3, PHASE)])
-def test_frame_matches_oracle(engines, shape, n, path):
+@pytest.mark.parametrize("shape,n,path,fold", [
+    (SHAPE_BASELINE, 6, PHASE, True), (SHAPE_BASELINE, 6, FUSED, True), (SHAPE_BASELINE, 11, FUSED, True),
+    (SHAPE_BASELINE, 6, TILE, True), (SHAPE_BASELINE, 11, TILE, True), (SHAPE_BASELINE, 11, TILE, False),
+    (SHAPE_BASELINE, 11, FUSED, False), (SHAPE_SOFIA, 3, PHASE, True)])
+def test_frame_matches_oracle(engines, shape, n, path, fold):
     w = weights(shape, 21)
-    eng = engines(shape, 21, 16, path=path)
+    eng = engines(shape, 21, 16, path=path, fold=fold)
     assert eng.path == path
     hidden = _hidden(n, 5)
     flags = tuple(np.resize(np.asarray(f), n) for f in FLAGS6)
@@ -174,8 +176,13 @@ def test_frame_matches_oracle(engines, shape, n, path):
     check_frame(w, hidden, flags, seed, counter, gpu)
 
 
-def test_auto_path_is_fused_for_the_benchmark_shape(engines):
-    assert engines(SHAPE_BASELINE, 21, 16).path == FUSED
+def test_auto_path_for_the_benchmark_shape(engines):
+    """Few tiles: the cluster kernel (latency); more tiles than concurrent
+    clusters: the tile kernel (throughput); other shapes: phase kernels."""
+    eng = engines(SHAPE_BASELINE, 21, 16)
+    assert eng.path == FUSED
+    assert eng.path_for(1) == FUSED
+    assert eng.path_for(1024) == TILE
     assert engines(SHAPE_SOFIA, 21, 1, with_final=False).path == PHASE
 
 
@@ -235,14 +242,15 @@ def test_argmax_without_cfg(engines, path):
     np.testing.assert_array_equal(gpu["counter"], counter)
 
 
-@pytest.mark.parametrize("name", ["A_bf16_cfg", "R_bf16_cfg"])
-def test_frame_against_reference_golden(engines, golden, golden_dir, name):
+@pytest.mark.parametrize("name,path", [("A_bf16_cfg", PATH_AUTO), ("A_bf16_cfg", TILE), ("R_bf16_cfg", PATH_AUTO)])
+def test_frame_against_reference_golden(engines, golden, golden_dir, name, path):
     """Teacher-forced on the reference's tokens, the GPU logits match the NeMo
     oracle's recorded logits within tolerance."""
     meta = golden["lt_frames"][name]
     z = np.load(os.path.join(golden_dir, "lt_frames.npz"))
     shape = LocalArShape(meta["d_model"], meta["n_layers"], meta["n_heads"], meta["d_ffn"])
-    eng = engines(shape, meta["weights_seed"], 1, with_final=False)  # AUTO: fused for A, phase for R
+    # AUTO: fused cluster kernel for A, phase kernels for R
+    eng = engines(shape, meta["weights_seed"], 1, with_final=False, path=path)
     for f, fr in enumerate(meta["frames"]):
         hidden = from_bits(z[f"{name}/f{f}/hidden"]).reshape(1, 2, EMBED)
         ref_tokens = z[f"{name}/f{f}/tokens"]
