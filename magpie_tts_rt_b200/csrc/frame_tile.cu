@@ -1,38 +1,43 @@
 // Tile frame kernel: one CTA runs all 16 positions of a Local AR frame for a
-// tile of 16 rows (8 sessions x CFG pair, or 16 sessions without CFG), with
-// no communication between CTAs.  This is the throughput path: at a few
-// hundred sessions per GPU every SM holds its own tile, and the per-position
-// critical path is the weight stream through the SM, not a cluster exchange.
+// tile of up to 8 sessions (16 rows with CFG), with no communication between
+// CTAs.  This is the throughput path: at a few hundred sessions per GPU every
+// SM holds its own tile, and the per-position critical path is the weight
+// stream through the SM, not a cluster exchange.
 //
 // Per position (reference ops as in frame_fused.cu: local_ar_wrapper.py:609-751,
 // transformer_2501.py:405-442,761-851,1153-1232, sampling
 // local_ar_plugins.cu:1211-1370, embedding sum main_decoder_wrapper.py:796-810):
 //
-//   in-projection (p = 0, or every p without the folded tables) or the folded
-//   gather x = bf16(emb_proj[p-1][token] + pos[p]); LN1; qkv; k/v appended
-//   to the KV cache in tensor memory; causal attention over positions 0..p;
+//   input rows: the in-projection (p = 0, or every p without the folded
+//   tables), else x = bf16(emb_proj[p-1][token] + pos[p]) written by the
+//   sampling warp as soon as it has the token; LN1; qkv; k/v appended to the
+//   KV cache in tensor memory; causal attention over positions 0..p;
 //   o-projection + residual; LN2; FFN1 + GELU-tanh; FFN2 + residual; head p
-//   (+bias, CFG combine in the epilogue); one warp samples each session.
+//   (+bias, CFG combine, constraints, order keys and each session's maximum
+//   in the epilogue); one warp per session finds the exact top-k threshold,
+//   scores the eligible tokens with Philox-Gumbel and picks the token.
 //
 // Data layout:
 //   * Weights stream from global memory (L2-resident across frames) through a
-//     four-slot ring of 32 KB chunks (64 weight rows x 256 K columns, four
+//     five-slot ring of 32 KB chunks (64 weight rows x 256 K columns, four
 //     TMA boxes of 64 x 64 with 128-byte swizzle, no multicast), filled by a
 //     dedicated producer warp that runs ahead of the eight consumer warps;
 //     full/empty mbarriers per slot.  Every GEMM is C[16][N] = A[16][K] W^T on
 //     mma.sync m16n8k16 (bf16 in, f32 accumulate): at 16 rows this is a
 //     weight-streaming GEMV, below tcgen05's 64-row minimum.  A (the 16 rows)
 //     is held in registers for a whole GEMM; each warp reads its 8 weight rows
-//     of a chunk with ldmatrix exactly once.
+//     of a chunk with ldmatrix exactly once, in four independent accumulator
+//     chains, and finishes a chunk's epilogue while the next chunk's MMAs run.
 //   * The KV cache (16 rows x 16 positions x (256 k + 256 v) bf16 = 256 KB)
 //     lives in tensor memory: TMEM lane 32h + 2r + half holds, for row r and
 //     head h, dims [32 half, +32) of k_j at columns [16j, +16) and of v_j at
-//     columns [256 + 16j, +16) (bf16 pairs).  Warp h (h < 4) owns TMEM lanes
-//     [32h, +32) and computes head h's attention for all 16 rows.
-//   * Rows: row r is slot r % S, sub-row r / S (S = 16 / rows per session),
-//     so with CFG the conditional and unconditional rows of a session are rows
-//     s and s + 8, which one mma.sync thread holds together in the head
-//     epilogue (the CFG combine needs no exchange).
+//     columns [256 + 16j, +16) (bf16 pairs).  Warps h and h + 4 own TMEM lanes
+//     [32h, +32); warp h takes positions 0..7 of head h, warp h + 4 positions
+//     8..15, and they exchange scores and partial outputs in shared memory.
+//   * Rows: session slot s (s < 8) owns row s (conditional) and, with CFG,
+//     row s + 8 (unconditional); one mma.sync thread holds both rows of a
+//     session for the same columns, so the CFG combine needs no exchange.
+//     Without CFG rows 8..15 are idle.
 // Every wait is bounded; a timeout sets invalid bit 4 for the tile's sessions.
 #include <cuda.h>
 
@@ -45,25 +50,31 @@ namespace mtt {
 namespace {
 
 constexpr int kTRows = 16;
+constexpr int kTSess = 8;                    // session slots per tile
 constexpr int kTWarps = 8;                   // consumer warps
 constexpr int kTConsumers = kTWarps * 32;    // 256
-constexpr int kTThreads = kTConsumers + 32;  // + the TMA producer warp
+constexpr int kTThreads = kTConsumers + 128;  // + the producer warpgroup (one warp issues TMA)
+// Register split (setmaxnreg): launched at 168 per thread (65536 / 384, rounded
+// down to 8); the producer warpgroup drops to 40 and the consumers rise to 232:
+// 128 x 40 + 256 x 232 = 64512 = 384 x 168, so the increase never waits.
+constexpr int kProducerRegs = 40;
+constexpr int kConsumerRegs = 232;
+static_assert(128 * kProducerRegs + kTConsumers * kConsumerRegs <= kTThreads * 168, "register split");
 constexpr int kTD = 256;
 constexpr int kTF = 1024;
 constexpr int kTHeads = 4;
-constexpr int kCRows = 64;                      // weight rows per chunk
-constexpr int kCK = 256;                        // K columns per chunk
-constexpr int kCPanel = 64;                     // columns per TMA box (128 bytes)
-constexpr int kCElems = kCRows * kCK;           // 16384 bf16
-constexpr uint32_t kCBytes = kCElems * 2;       // 32 KB
-constexpr int kSlots = 4;
-constexpr int kLdX = kTD + 8;       // 264
-constexpr int kLdSrc = kEmbed + 8;  // 776
-constexpr int kLdQkv = 3 * kTD + 8; // 776
-constexpr int kLdHid = kTF + 8;     // 1032
-constexpr int kElig = 256;          // per-warp eligible-token list
+constexpr int kCRows = 64;                 // weight rows per chunk
+constexpr int kCK = 256;                   // K columns per chunk
+constexpr int kCPanel = 64;                // columns per TMA box (128 bytes)
+constexpr int kCElems = kCRows * kCK;      // 16384 bf16
+constexpr uint32_t kCBytes = kCElems * 2;  // 32 KB
+constexpr int kSlots = 5;
+constexpr int kLdX = kTD + 8;        // 264
+constexpr int kLdSrc = kEmbed + 8;   // 776
+constexpr int kLdQkv = 3 * kTD + 8;  // 776
+constexpr int kLdHid = kTF + 8;      // 1032
 constexpr int kTmemCols = 512;
-constexpr int kVocabChunks = kVocab / 8;  // 253 chunks of 8 logits per session row
+constexpr int kVocabChunks = kVocab / 8;  // 253 chunks of 8 keys per session
 
 static_assert(kVocab % 8 == 0, "vocab chunks");
 static_assert(kTHeads * kHeadDim == kTD, "heads");
@@ -77,25 +88,38 @@ struct TileMaps {
   CUtensorMap head;     // [16*2024][256]
 };
 
+// Attention exchange between the two warps of a head (inside TileU, after
+// q/k/v have been consumed).
+struct AttnExchange {
+  float s[2][kTHeads][32][8];  // scores of positions [8 part, +8)
+  float o[kTHeads][32][32];    // part-1 partial outputs
+};
+
 // Buffers of phases that never overlap within a position.
 union TileU {
-  bf16 src[kTRows * kLdSrc];  // in-projection input rows
-  bf16 qkv[kTRows * kLdQkv];  // q | k | v of the current position
-  bf16 hid[kTRows * kLdHid];  // FFN1 output
-  bf16 g[kTRows * kVocab];    // guided (or plain) logits, one row per session slot
+  bf16 src[kTRows * kLdSrc];      // in-projection input rows
+  bf16 qkv[kTRows * kLdQkv];      // q | k | v of the current position
+  AttnExchange att;               // after q/k/v are consumed
+  bf16 hid[kTRows * kLdHid];      // FFN1 output
+  uint16_t val[kTSess * kVocab];  // constrained (guided) logits, bf16 bits
 };
+static_assert(sizeof(AttnExchange) <= sizeof(bf16) * kTRows * kLdQkv, "attention exchange");
 
 struct __align__(1024) TileSmem {
   bf16 ring[kSlots][kCElems];  // 1024-byte aligned panels (128-byte swizzle atoms)
   bf16 x[kTRows * kLdX];       // residual stream
   bf16 xa[kTRows * kLdX];      // LN output / attention output
   TileU u;
-  uint32_t hist[kTWarps][256];
-  uint16_t elig[kTWarps][kElig];
-  int32_t tok[kTRows][kPositions];
-  int32_t sess[kTRows];
-  int64_t ctr[kTRows];
-  int32_t inv[kTRows];
+  uint32_t hist[kTSess][256];  // per session: the eligible-token list (u16)
+  __align__(16) bf16 hb[kVocab];  // bias of head p
+  int32_t tok[kTSess][kPositions];
+  int32_t sess[kTSess];
+  int64_t ctr[kTSess];
+  int64_t seed[kTSess];
+  uint32_t flags[kTSess];  // bit 0 unfinished, bit 1 finished, bit 2 forbid_eos
+  int32_t inv[kTSess];
+  uint32_t amax[kTSess];  // max of key << 16 | (0xffff - token): maximum key, left-most
+  uint32_t nonfinite[kTSess];
   int32_t last_issued[kSlots];
   int32_t n_sess;
   int32_t err;
@@ -199,108 +223,79 @@ __device__ __forceinline__ void load_a(uint32_t (&a)[16][4], const bf16* A, int 
   for (int ks = 0; ks < 16; ++ks) ldsm_x4(a[ks], p + 16 * ks);
 }
 
-// acc += A[16][256] x chunk rows [8w, 8w+8)^T for warp w.  The chunk is four
-// 64-column panels of 64 rows x 128 bytes; 16-byte unit j of row n sits at
-// unit j ^ (n & 7) (128-byte swizzle).
-__device__ __forceinline__ void mma_chunk(float (&acc)[4], const uint32_t (&a)[16][4], const bf16* chunk) {
+// c[j] += A[16][256] x chunk rows [8w, 8w+8)^T for warp w, k-steps j mod CH in
+// chain j.  The chunk is four 64-column panels of 64 rows x 128 bytes;
+// 16-byte unit j of row n sits at unit j ^ (n & 7) (128-byte swizzle).
+template <int CH>
+__device__ __forceinline__ void mma_chunk(float (&c)[CH][4], const uint32_t (&a)[16][4], const bf16* chunk) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int n = 8 * warp + (lane & 7);
   const int q = lane >> 3;
   const bf16* row = chunk + n * kCPanel;
   const int swz = n & 7;
-  float odd[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
   for (int ks2 = 0; ks2 < 8; ++ks2) {
     uint32_t b[4];
     ldsm_x4(b, row + (ks2 >> 1) * (kCRows * kCPanel) + (((4 * (ks2 & 1) + q) ^ swz) << 3));
-    mma16816(acc, a[2 * ks2], b[0], b[1]);
-    mma16816(odd, a[2 * ks2 + 1], b[2], b[3]);
+    mma16816(c[(2 * ks2) % CH], a[2 * ks2], b[0], b[1]);
+    mma16816(c[(2 * ks2 + 1) % CH], a[2 * ks2 + 1], b[2], b[3]);
   }
-#pragma unroll
-  for (int e = 0; e < 4; ++e) acc[e] += odd[e];
 }
 
-// C[16][64 nb_count] = A[16][256] W^T over nb_count chunks; epi(nb, acc) per chunk.
+// C[16][64 nb_count] = A[16][256] W^T over nb_count chunks; epi(nb, acc) per
+// chunk, one chunk behind the MMAs.
 template <typename Epi>
-__device__ __forceinline__ void gemm_n(TileSmem& sm, int& it, const bf16* A, int lda, int nb_count, Epi epi) {
-  uint32_t a[16][4];
-  load_a(a, A, lda);
+__device__ __forceinline__ void gemm_n(TileSmem& sm, int& it, const uint32_t (&a)[16][4], int nb_count, Epi epi) {
+  float prev[4][4];
   for (int nb = 0; nb < nb_count; ++nb, ++it) {
     const bf16* chunk = acquire(sm, it);
-    float acc[4] = {0.f, 0.f, 0.f, 0.f};
-    mma_chunk(acc, a, chunk);
+    float cur[4][4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) cur[j][0] = cur[j][1] = cur[j][2] = cur[j][3] = 0.f;
+    mma_chunk<4>(cur, a, chunk);
     release(sm, it);
-    epi(nb, acc);
+    if (nb > 0) {
+      float acc[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) acc[e] = (prev[0][e] + prev[1][e]) + (prev[2][e] + prev[3][e]);
+      epi(nb - 1, acc);
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) prev[j][e] = cur[j][e];
   }
+  float acc[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) acc[e] = (prev[0][e] + prev[1][e]) + (prev[2][e] + prev[3][e]);
+  epi(nb_count - 1, acc);
 }
 
 // C[16][256] = A[16][256 KB] W^T, chunks in K-block-major order; epi(nb, acc) at the end.
 template <int KB, typename Epi>
 __device__ __forceinline__ void gemm_k(TileSmem& sm, int& it, const bf16* A, int lda, Epi epi) {
-  float acc[4][4];
+  float c[4][2][4];
 #pragma unroll
-  for (int nb = 0; nb < 4; ++nb) acc[nb][0] = acc[nb][1] = acc[nb][2] = acc[nb][3] = 0.f;
+  for (int nb = 0; nb < 4; ++nb)
+#pragma unroll
+    for (int j = 0; j < 2; ++j) c[nb][j][0] = c[nb][j][1] = c[nb][j][2] = c[nb][j][3] = 0.f;
   for (int kb = 0; kb < KB; ++kb) {
     uint32_t a[16][4];
     load_a(a, A + kCK * kb, lda);
 #pragma unroll
     for (int nb = 0; nb < 4; ++nb, ++it) {
       const bf16* chunk = acquire(sm, it);
-      mma_chunk(acc[nb], a, chunk);
+      mma_chunk<2>(c[nb], a, chunk);
       release(sm, it);
     }
   }
 #pragma unroll
-  for (int nb = 0; nb < 4; ++nb) epi(nb, acc[nb]);
-}
-
-// LayerNorm (no bias, eps 1e-5) of the 16 rows of x into xa; warp w: rows 2w, 2w+1.
-__device__ __forceinline__ void layer_norm_rows(const bf16* x, bf16* xa, const bf16* w) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  float g[8];
-  {
-    const uint4 gv = *reinterpret_cast<const uint4*>(w + lane * 8);
-    const __nv_bfloat162* g2 = reinterpret_cast<const __nv_bfloat162*>(&gv);
+  for (int nb = 0; nb < 4; ++nb) {
+    float acc[4];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const float2 t = __bfloat1622float2(g2[j]);
-      g[2 * j] = t.x;
-      g[2 * j + 1] = t.y;
-    }
+    for (int e = 0; e < 4; ++e) acc[e] = c[nb][0][e] + c[nb][1][e];
+    epi(nb, acc);
   }
-#pragma unroll
-  for (int rr = 0; rr < 2; ++rr) {
-    const int r = 2 * warp + rr;
-    const uint4 xv = *reinterpret_cast<const uint4*>(x + r * kLdX + lane * 8);
-    const __nv_bfloat162* x2 = reinterpret_cast<const __nv_bfloat162*>(&xv);
-    float v[8];
-    float sum = 0.f;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const float2 t = __bfloat1622float2(x2[j]);
-      v[2 * j] = t.x;
-      v[2 * j + 1] = t.y;
-      sum += t.x + t.y;
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-    const float mean = sum / static_cast<float>(kTD);
-    float var = 0.f;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) var += (v[j] - mean) * (v[j] - mean);
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) var += __shfl_xor_sync(0xffffffffu, var, o);
-    const float rstd = 1.0f / sqrtf(var / static_cast<float>(kTD) + 1.0e-5f);
-    __align__(16) bf16 out[8];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) out[j] = f2bf(((v[j] - mean) * rstd) * g[j]);
-    *reinterpret_cast<uint4*>(xa + r * kLdX + lane * 8) = *reinterpret_cast<const uint4*>(out);
-  }
-}
-
-__device__ __forceinline__ float gelu_tanh(float v) {
-  const float inner = 0.7978845608028654f * (v + 0.044715f * v * v * v);
-  return 0.5f * v * (1.0f + tanhf(inner));
 }
 
 __device__ __forceinline__ void unpack8(const uint4& u, float (&f)[8]) {
@@ -313,110 +308,183 @@ __device__ __forceinline__ void unpack8(const uint4& u, float (&f)[8]) {
   }
 }
 
+__device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
+  uint4 u;
+  u.x = pack_bf16x2(f[0], f[1]);
+  u.y = pack_bf16x2(f[2], f[3]);
+  u.z = pack_bf16x2(f[4], f[5]);
+  u.w = pack_bf16x2(f[6], f[7]);
+  return u;
+}
+
+// LayerNorm (no bias, eps 1e-5) of the 16 rows of x into xa with this lane's
+// 8 weights g (columns 8 lane ..); warp w: rows 2w, 2w+1.
+__device__ __forceinline__ void layer_norm_rows(const bf16* x, bf16* xa, const float (&g)[8]) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int rr = 0; rr < 2; ++rr) {
+    const int r = 2 * warp + rr;
+    float v[8];
+    unpack8(*reinterpret_cast<const uint4*>(x + r * kLdX + lane * 8), v);
+    float sum = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) sum += v[j];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    const float mean = sum / static_cast<float>(kTD);
+    float var = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) var += (v[j] - mean) * (v[j] - mean);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) var += __shfl_xor_sync(0xffffffffu, var, o);
+    const float rstd = 1.0f / sqrtf(var / static_cast<float>(kTD) + 1.0e-5f);
+    float out[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) out[j] = ((v[j] - mean) * rstd) * g[j];
+    *reinterpret_cast<uint4*>(xa + r * kLdX + lane * 8) = pack8(out);
+  }
+}
+
+// GELU, tanh form: tanh(u) = 1 - 2 / (exp(2u) + 1), with the fast exponential
+// (error ~1e-6 relative before the result is rounded to bf16).
+__device__ __forceinline__ float gelu_tanh(float v) {
+  const float inner = 0.7978845608028654f * (v + 0.044715f * v * v * v);
+  const float t = 1.0f - __fdividef(2.0f, __expf(2.0f * inner) + 1.0f);
+  return 0.5f * v * (1.0f + t);
+}
+
 // ---------------------------------------------------------------------------
-// attention over the TMEM KV cache (warp h < 4: head h, thread t: row t / 2,
-// dims [32 (t % 2), +32) of the head)
+// attention over the TMEM KV cache: warp w, head h = w % 4, part = w / 4
+// (positions j = part, part + 2, ..); thread t: row t / 2, dims [32 (t % 2), +32)
 // ---------------------------------------------------------------------------
 
-__device__ __forceinline__ void attention_warp(TileSmem& sm, int p) {
-  const int lane = threadIdx.x & 31, h = threadIdx.x >> 5;
+// TMEM column block of position j: even positions in blocks 0..7, odd in 8..15,
+// so each part's positions are contiguous (four per 64-column load).
+__device__ __forceinline__ int tmem_block(int j) { return 8 * (j & 1) + (j >> 1); }
+
+__device__ __forceinline__ void attention(TileSmem& sm, int p) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int h = warp & 3, part = warp >> 2;
   const int r = lane >> 1, half = lane & 1;
   const uint32_t tl = sm.tmem + (static_cast<uint32_t>(32 * h) << 16);
   const bf16* qrow = sm.u.qkv + r * kLdQkv + kHeadDim * h + 32 * half;
-  {
+  {  // append k (part 0) or v (part 1) of position p
     uint32_t kv[16];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      const uint4 t = *reinterpret_cast<const uint4*>(qrow + kTD + 8 * j);
+      const uint4 t = *reinterpret_cast<const uint4*>(qrow + (1 + part) * kTD + 8 * j);
       kv[4 * j] = t.x;
       kv[4 * j + 1] = t.y;
       kv[4 * j + 2] = t.z;
       kv[4 * j + 3] = t.w;
     }
-    tmem_st16(tl + 16 * p, kv);
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const uint4 t = *reinterpret_cast<const uint4*>(qrow + 2 * kTD + 8 * j);
-      kv[4 * j] = t.x;
-      kv[4 * j + 1] = t.y;
-      kv[4 * j + 2] = t.z;
-      kv[4 * j + 3] = t.w;
-    }
-    tmem_st16(tl + 256 + 16 * p, kv);
+    tmem_st16(tl + 256 * part + 16 * tmem_block(p), kv);
     tmem_wait_st();
   }
   float q[32];
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
-    float f[8];
-    unpack8(*reinterpret_cast<const uint4*>(qrow + 8 * j), f);
+    float f8[8];
+    unpack8(*reinterpret_cast<const uint4*>(qrow + 8 * j), f8);
 #pragma unroll
-    for (int e = 0; e < 8; ++e) q[8 * j + e] = f[e];
+    for (int e = 0; e < 8; ++e) q[8 * j + e] = f8[e];
   }
-  float s[kPositions];
+  tmem_fence_before_sync();
+  cbar();  // k_p and v_p in TMEM; q/k/v staging free for the exchange
+  tmem_fence_after_sync();
+
+  // scores of this part's positions j = 2m + part (m = 0..7), four per TMEM load
+  float s[8];
 #pragma unroll
-  for (int j = 0; j < kPositions; ++j) {
-    s[j] = -CUDART_INF_F;
-    if (j <= p) {
-      uint32_t k[16];
-      tmem_ld16(k, tl + 16 * j);
-      float dot = 0.f;
+  for (int m = 0; m < 8; ++m) s[m] = -CUDART_INF_F;
 #pragma unroll
-      for (int e = 0; e < 16; ++e) {
-        const float2 t = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&k[e]));
-        dot = fmaf(q[2 * e], t.x, dot);
-        dot = fmaf(q[2 * e + 1], t.y, dot);
+  for (int g4 = 0; g4 < 2; ++g4) {
+    if (8 * g4 + part <= p) {
+      uint32_t k[64];
+      tmem_ld64(k, tl + 16 * (8 * part + 4 * g4));
+#pragma unroll
+      for (int jj = 0; jj < 4; ++jj) {
+        float dot = 0.f;
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          const float2 t = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&k[16 * jj + e]));
+          dot = fmaf(q[2 * e], t.x, dot);
+          dot = fmaf(q[2 * e + 1], t.y, dot);
+        }
+        dot += __shfl_xor_sync(0xffffffffu, dot, 1);
+        if (2 * (4 * g4 + jj) + part <= p) s[4 * g4 + jj] = round_bf16(__fmul_rn(round_bf16(dot), 0.125f));
       }
-      dot += __shfl_xor_sync(0xffffffffu, dot, 1);
-      s[j] = round_bf16(__fmul_rn(round_bf16(dot), 0.125f));
     }
   }
-  float mx = s[0];
+  float* my_s = sm.u.att.s[part][h][lane];
 #pragma unroll
-  for (int j = 1; j < kPositions; ++j) mx = fmaxf(mx, s[j]);
-  float e[kPositions];
+  for (int m = 0; m < 8; ++m) my_s[m] = s[m];
+  cbar();
+  // the full softmax over positions 0..p (both parts compute it)
+  float all[kPositions];
+#pragma unroll
+  for (int m = 0; m < 8; ++m) {
+    all[2 * m] = sm.u.att.s[0][h][lane][m];
+    all[2 * m + 1] = sm.u.att.s[1][h][lane][m];
+  }
+  float mx = all[0];
+#pragma unroll
+  for (int j = 1; j < kPositions; ++j) mx = fmaxf(mx, all[j]);
   float sum = 0.f;
 #pragma unroll
   for (int j = 0; j < kPositions; ++j) {
-    e[j] = j <= p ? expf(s[j] - mx) : 0.f;
-    sum += e[j];
+    all[j] = j <= p ? expf(all[j] - mx) : 0.f;
+    sum += all[j];
   }
   float o[32];
 #pragma unroll
   for (int d = 0; d < 32; ++d) o[d] = 0.f;
 #pragma unroll
-  for (int j = 0; j < kPositions; ++j) {
-    if (j <= p) {
-      const float prob = round_bf16(e[j] / sum);
-      uint32_t v[16];
-      tmem_ld16(v, tl + 256 + 16 * j);
+  for (int g4 = 0; g4 < 2; ++g4) {
+    if (8 * g4 + part <= p) {
+      uint32_t v[64];
+      tmem_ld64(v, tl + 256 + 16 * (8 * part + 4 * g4));
 #pragma unroll
-      for (int d = 0; d < 16; ++d) {
-        const float2 t = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&v[d]));
-        o[2 * d] = fmaf(prob, t.x, o[2 * d]);
-        o[2 * d + 1] = fmaf(prob, t.y, o[2 * d + 1]);
+      for (int jj = 0; jj < 4; ++jj) {
+        const int j = 2 * (4 * g4 + jj) + part;
+        if (j <= p) {
+          const float prob = round_bf16(all[j] / sum);
+#pragma unroll
+          for (int d = 0; d < 16; ++d) {
+            const float2 t = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&v[16 * jj + d]));
+            o[2 * d] = fmaf(prob, t.x, o[2 * d]);
+            o[2 * d + 1] = fmaf(prob, t.y, o[2 * d + 1]);
+          }
+        }
       }
     }
   }
-  bf16* out = sm.xa + r * kLdX + kHeadDim * h + 32 * half;
+  if (part == 1) {
+    float* dst = sm.u.att.o[h][lane];
 #pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    uint4 u;
-    u.x = pack_bf16x2(o[8 * j], o[8 * j + 1]);
-    u.y = pack_bf16x2(o[8 * j + 2], o[8 * j + 3]);
-    u.z = pack_bf16x2(o[8 * j + 4], o[8 * j + 5]);
-    u.w = pack_bf16x2(o[8 * j + 6], o[8 * j + 7]);
-    *reinterpret_cast<uint4*>(out + 8 * j) = u;
+    for (int d = 0; d < 32; ++d) dst[d] = o[d];
+  }
+  cbar();
+  if (part == 0) {
+    const float* src = sm.u.att.o[h][lane];
+#pragma unroll
+    for (int d = 0; d < 32; ++d) o[d] += src[d];
+    bf16* out = sm.xa + r * kLdX + kHeadDim * h + 32 * half;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float f8[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) f8[e] = o[8 * j + e];
+      *reinterpret_cast<uint4*>(out + 8 * j) = pack8(f8);
+    }
   }
 }
 
 // ---------------------------------------------------------------------------
-// warp sampler: one (session, position) call on a row of 2024 bf16 logits
-// (CFG already combined) in shared memory.  Same contract as sample_block in
-// sampling.cuh; lane l holds tokens [8c, 8c+8) for c = l + 32i.
+// sampling (same contract as sample_block in sampling.cuh)
 // ---------------------------------------------------------------------------
 
-constexpr uint32_t kKeyNegInf = 0x007fu;  // 16-bit order key of bf16 -inf
+constexpr uint32_t kKeyNegInf = 0x007fu;  // order key of bf16 -inf
 
 // Order key of a bf16 bit pattern with -0 folded onto +0 (key order == float order).
 __device__ __forceinline__ uint32_t sample_key(uint32_t b) {
@@ -424,233 +492,256 @@ __device__ __forceinline__ uint32_t sample_key(uint32_t b) {
   return (b & 0x8000u) ? (~b & 0xffffu) : (b | 0x8000u);
 }
 
-struct WarpSample {
-  const bf16* g;
-  bool unfinished, finished, forbid_eos;
-  int64_t seed, counter;
-};
-
-__device__ __forceinline__ uint32_t warp_count_ge(const uint32_t (&kp)[8][4], uint32_t t) {
-  const int lane = threadIdx.x & 31;
-  uint32_t c = 0;
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    if (lane + 32 * i < kVocabChunks) {
-#pragma unroll
-      for (int e = 0; e < 4; ++e) c += ((kp[i][e] & 0xffffu) >= t) + ((kp[i][e] >> 16) >= t);
-    }
+// Constrained value of token t (bf16 bits): non-finite -> -inf (and flagged),
+// forbidden specials / gated EOS -> -inf, finished -> EOS 0, others -inf.
+__device__ __forceinline__ uint32_t constrain(uint32_t b, int t, bool unfinished, bool finished, bool forbid,
+                                              bool& nonfinite) {
+  if ((b & 0x7f80u) == 0x7f80u) {
+    nonfinite = true;
+    b = 0xff80u;
   }
-  return __reduce_add_sync(0xffffffffu, c);
+  if (t >= kCodebook && (t != kEosId || unfinished || forbid)) b = 0xff80u;
+  if (finished) b = (t == kEosId) ? 0u : 0xff80u;
+  return b;
 }
 
-__device__ int warp_sample(const WarpSample& a, const SamplingParams& prm, uint32_t* hist, uint16_t* elig,
-                           int* invalid_out) {
+constexpr int kListCap = 512;  // candidate list per session (u16 tokens), in the xa buffer
+constexpr int kListStride = (kTRows * kLdX) / kTSess;  // 528 u16 per session slot
+static_assert(kListStride >= kListCap, "candidate list");
+
+struct Best {
+  float score;
+  int id;
+};
+
+__device__ __forceinline__ void keep_best(Best& b, float sc, int t) {
+  if (sc > b.score || (sc == b.score && t < b.id)) {
+    b.score = sc;
+    b.id = t;
+  }
+}
+
+__device__ __forceinline__ Best warp_best(Best b) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float os = __shfl_xor_sync(0xffffffffu, b.score, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, b.id, o);
+    keep_best(b, os, oi);
+  }
+  return b;
+}
+
+// Philox-Gumbel scores of the tokens list[0, total), four independent chains per lane.
+__device__ __forceinline__ void score_list(const uint16_t* list, uint32_t total, const uint16_t* vals, uint32_t seed32,
+                                           uint64_t off64, float temperature, Best& b) {
   const int lane = threadIdx.x & 31;
-  uint32_t kp[8][4];
-  bool nonfinite = false;
-  uint32_t mx = 0, finite = 0;
+  for (uint32_t base = 0; base < total; base += 128) {
+    int t[4];
+    float u[4];
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const int c = lane + 32 * i;
-    if (c < kVocabChunks) {
-      const uint4 v = *reinterpret_cast<const uint4*>(a.g + 8 * c);
-      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+    for (int j = 0; j < 4; ++j) {
+      const uint32_t e = base + lane + 32 * j;
+      t[j] = e < total ? list[e] : -1;
+      u[j] = philox_uniform(seed32, off64 + static_cast<uint64_t>(t[j] < 0 ? 0 : t[j]));
+    }
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        uint32_t key2[2];
-#pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-          const int t = 8 * c + 2 * e + hh;
-          uint32_t b = hh ? (w[e] >> 16) : (w[e] & 0xffffu);
-          if ((b & 0x7f80u) == 0x7f80u) {
-            nonfinite = true;
-            b = 0xff80u;
-          }
-          if (t >= kCodebook && (t != kEosId || a.unfinished || a.forbid_eos)) b = 0xff80u;
-          if (a.finished) b = (t == kEosId) ? 0u : 0xff80u;
-          key2[hh] = sample_key(b);
-          mx = key2[hh] > mx ? key2[hh] : mx;
-          finite += key2[hh] != kKeyNegInf ? 1u : 0u;
-        }
-        kp[i][e] = key2[0] | (key2[1] << 16);
-      }
-    } else {
-#pragma unroll
-      for (int e = 0; e < 4; ++e) kp[i][e] = 0;
+    for (int j = 0; j < 4; ++j) {
+      if (t[j] >= 0) keep_best(b, __fadd_rn(__fdiv_rn(bits2f(vals[t[j]]), temperature), clamped_gumbel(u[j])), t[j]);
     }
   }
-  mx = __reduce_max_sync(0xffffffffu, mx);
-  finite = __reduce_add_sync(0xffffffffu, finite);
-  nonfinite = __any_sync(0xffffffffu, nonfinite);
+}
 
-  int token;
-  int invalid;
+__device__ __forceinline__ __nv_bfloat162 bf2_of(uint32_t w) { return *reinterpret_cast<const __nv_bfloat162*>(&w); }
+
+// bf16 value of an order key (the smallest key is -inf).
+__device__ __forceinline__ __nv_bfloat16 key_value(uint32_t key) {
+  return __ushort_as_bfloat16(static_cast<unsigned short>(key_bf16(key < kKeyNegInf ? kKeyNegInf : key)));
+}
+
+// Number of values >= v in a session's row (warp total): bf16x2 compares
+// (-0 == +0, as in the float comparison the contract uses) summed in bf16x2.
+__device__ __forceinline__ uint32_t count_ge(const uint16_t* vals, __nv_bfloat16 v) {
+  const int lane = threadIdx.x & 31;
+  const __nv_bfloat162 t2 = __bfloat162bfloat162(v);
+  __nv_bfloat162 acc = __float2bfloat162_rn(0.f);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int ch = lane + 32 * i;
+    if (ch < kVocabChunks) {
+      const uint4 q = *reinterpret_cast<const uint4*>(vals + 8 * ch);
+      acc = __hadd2(acc, __hge2(bf2_of(q.x), t2));
+      acc = __hadd2(acc, __hge2(bf2_of(q.y), t2));
+      acc = __hadd2(acc, __hge2(bf2_of(q.z), t2));
+      acc = __hadd2(acc, __hge2(bf2_of(q.w), t2));
+    }
+  }
+  const float2 f = __bfloat1622float2(acc);
+  return __reduce_add_sync(0xffffffffu, static_cast<uint32_t>(f.x + f.y));
+}
+
+// The calling warp samples session `slot` at the current position from the
+// constrained bf16 values and the per-session maximum the head epilogue left.
+// Top-k threshold (the k-th largest value, ties included), without atomics:
+// one bf16x2 counting pass finds the smallest window of 32/64/128/256 key
+// steps below the maximum that holds k values; the window's tokens form a
+// candidate list whose distances below the maximum sit in registers, and a
+// binary search over them gives the exact k-th largest.  Only eligible
+// candidates are scored.  Rows whose window cannot be used (flat or very
+// spread rows) take an exact binary search over the whole row instead.
+__device__ int sample_slot(TileSmem& sm, const Frame& f, int slot, uint16_t* list, int* invalid_out) {
+  const int lane = threadIdx.x & 31;
+  const uint32_t fl = sm.flags[slot];
+  const bool unfinished = fl & 1u, finished = fl & 2u, forbid = fl & 4u;
+  const int64_t seed = sm.seed[slot];
+  const int64_t counter = sm.ctr[slot];
+  const SamplingParams& prm = f.prm;
+  const bool nonfinite = sm.nonfinite[slot] != 0;
+  const uint32_t top = sm.amax[slot];
+  const uint32_t M = top >> 16;
   if (prm.argmax) {
-    // left-most token holding the largest value
-    int first = kVocab;
+    *invalid_out = (nonfinite || M == kKeyNegInf) ? 1 : 0;
+    return M == kKeyNegInf ? 0 : static_cast<int>(0xffffu - (top & 0xffffu));
+  }
+  int invalid = (nonfinite || (unfinished && finished) || (finished && forbid)) ? 1 : 0;
+  const bool seed_valid = seed >= 0 && static_cast<uint64_t>(seed) < (1ull << 32);
+  const bool counter_valid = counter >= 0 && counter <= kMaxCounter;
+  if (!seed_valid || !counter_valid) invalid = 1;
+  if (finished) {  // only EOS (value 0) is finite: it is the only eligible token
+    *invalid_out = invalid;
+    return kEosId;
+  }
+  if (M == kKeyNegInf) {  // nothing finite
+    *invalid_out = 1;
+    return 0;
+  }
+  const uint32_t seed32 = seed_valid ? static_cast<uint32_t>(seed) : 0u;
+  const uint64_t off64 = counter_valid ? static_cast<uint64_t>(counter) * kPhiloxStride : 0ull;
+  const uint16_t* vals = sm.u.val + slot * kVocab;
+  const uint32_t kk = static_cast<uint32_t>(prm.top_k);
+
+  // ---- pass 1: values within 32 / 64 / 128 / 256 key steps below the maximum
+  __nv_bfloat162 lim[4];
 #pragma unroll
-    for (int i = 7; i >= 0; --i) {
-      const int c = lane + 32 * i;
-      if (c < kVocabChunks) {
+  for (int j = 0; j < 4; ++j) lim[j] = __bfloat162bfloat162(key_value(M + 1 < (32u << j) ? 0u : M + 1 - (32u << j)));
+  __nv_bfloat162 acc[4];
 #pragma unroll
-        for (int e = 3; e >= 0; --e) {
-          if ((kp[i][e] >> 16) == mx) first = 8 * c + 2 * e + 1;
-          if ((kp[i][e] & 0xffffu) == mx) first = 8 * c + 2 * e;
+  for (int j = 0; j < 4; ++j) acc[j] = __float2bfloat162_rn(0.f);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int ch = lane + 32 * i;
+    if (ch < kVocabChunks) {
+      const uint4 q = *reinterpret_cast<const uint4*>(vals + 8 * ch);
+      const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[j] = __hadd2(acc[j], __hge2(bf2_of(w[e]), lim[j]));
+    }
+  }
+  uint32_t mine4[4], tot[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const float2 f2 = __bfloat1622float2(acc[j]);
+    mine4[j] = static_cast<uint32_t>(f2.x + f2.y);
+    tot[j] = __reduce_add_sync(0xffffffffu, mine4[j]);
+  }
+  int win = 4;
+#pragma unroll
+  for (int j = 3; j >= 0; --j) win = tot[j] >= kk ? j : win;
+
+  Best best{-CUDART_INF_F, kVocab};
+  if (win < 4 && tot[win] <= static_cast<uint32_t>(kListCap)) {
+    const __nv_bfloat162 limw = win == 0 ? lim[0] : (win == 1 ? lim[1] : (win == 2 ? lim[2] : lim[3]));
+    const uint32_t mine = win == 0 ? mine4[0] : (win == 1 ? mine4[1] : (win == 2 ? mine4[2] : mine4[3]));
+    const uint32_t n_cand = tot[win];
+    uint32_t pos = mine;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t y = __shfl_up_sync(0xffffffffu, pos, o);
+      if (lane >= o) pos += y;
+    }
+    pos -= mine;
+    // ---- pass 2: the window's tokens
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int ch = lane + 32 * i;
+      if (ch < kVocabChunks) {
+        const uint4 q = *reinterpret_cast<const uint4*>(vals + 8 * ch);
+        const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const uint32_t m = __hge2_mask(bf2_of(w[e]), limw);
+          if (m & 0xffffu) list[pos++] = static_cast<uint16_t>(8 * ch + 2 * e);
+          if (m >> 16) list[pos++] = static_cast<uint16_t>(8 * ch + 2 * e + 1);
         }
       }
     }
-    first = __reduce_min_sync(0xffffffffu, first);
-    invalid = (nonfinite || finite == 0) ? 1 : 0;
-    token = (mx == kKeyNegInf || first >= kVocab) ? 0 : first;
-    if (mx == kKeyNegInf) invalid = 1;
-    *invalid_out = invalid;
-    return token;
-  }
-
-  // ---- k-th largest key: histogram of mx - key over the 256 keys below mx
-  const uint32_t kk = static_cast<uint32_t>(prm.top_k);
+    __syncwarp();
+    // ---- candidates' distances below the maximum, 16 per lane in registers
+    uint32_t dist[kListCap / 32];
+    uint16_t tokn[kListCap / 32];
 #pragma unroll
-  for (int i = 0; i < 8; ++i) hist[lane * 8 + i] = 0;
-  __syncwarp();
+    for (int m = 0; m < kListCap / 32; ++m) {
+      const uint32_t e = lane + 32 * m;
+      const int t = e < n_cand ? list[e] : 0;
+      tokn[m] = static_cast<uint16_t>(t);
+      dist[m] = e < n_cand ? M - sample_key(vals[t]) : 0xffffu;
+    }
+    // smallest d with count(dist <= d) >= k
+    int lo = -1, hi = static_cast<int>((32u << win) - 1);
+    while (hi - lo > 1) {
+      const int mid = (lo + hi) >> 1;
+      uint32_t cnt = 0;
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    if (lane + 32 * i < kVocabChunks) {
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const uint32_t d0 = mx - (kp[i][e] & 0xffffu), d1 = mx - (kp[i][e] >> 16);
-        if (d0 < 256u) atomicAdd(&hist[d0], 1u);
-        if (d1 < 256u) atomicAdd(&hist[d1], 1u);
+      for (int m = 0; m < kListCap / 32; ++m) cnt += dist[m] <= static_cast<uint32_t>(mid);
+      if (__reduce_add_sync(0xffffffffu, cnt) >= kk) {
+        hi = mid;
+      } else {
+        lo = mid;
       }
     }
-  }
-  __syncwarp();
-  uint32_t cnt[8];
-  uint32_t sum = 0;
+    const uint32_t dstar = static_cast<uint32_t>(hi);
+    // ---- eligible candidates (distance <= d*, finite), compacted into the histogram area
+    uint16_t* elig = reinterpret_cast<uint16_t*>(sm.hist[slot]);
+    uint32_t n_elig = 0;
 #pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    cnt[j] = hist[lane * 8 + j];
-    sum += cnt[j];
-  }
-  uint32_t incl = sum;
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
-    if (lane >= o) incl += y;
-  }
-  const uint32_t excl = incl - sum;
-  const uint32_t window_total = __shfl_sync(0xffffffffu, incl, 31);
-  uint32_t thr;
-  if (window_total >= kk) {
-    uint32_t cand = 0;
-    const bool here = excl < kk && kk <= incl;
-    if (here) {
-      uint32_t acc = excl;
-      int j = 0;
-      for (; j < 7; ++j) {
-        if (kk <= acc + cnt[j]) break;
-        acc += cnt[j];
-      }
-      cand = mx - static_cast<uint32_t>(lane * 8 + j);
+    for (int m = 0; m < kListCap / 32; ++m) {
+      const bool ok = dist[m] <= dstar && M - dist[m] != kKeyNegInf;
+      const unsigned b = __ballot_sync(0xffffffffu, ok);
+      if (ok) elig[n_elig + __popc(b & ((1u << lane) - 1u))] = tokn[m];
+      n_elig += __popc(b);
     }
-    const unsigned who = __ballot_sync(0xffffffffu, here);
-    thr = __shfl_sync(0xffffffffu, cand, __ffs(who) - 1);
+    __syncwarp();
+    score_list(elig, n_elig, vals, seed32, off64, prm.temperature, best);
   } else {
-    // exact binary search: count(key >= lo) >= k > count(key >= hi)
-    uint32_t lo = kKeyNegInf, hi = mx + 1;
+    // exact binary search over keys: count(value >= lo) >= k > count(value >= hi)
+    uint32_t lo = kKeyNegInf, hi = M + 1;
     while (hi - lo > 1) {
       const uint32_t mid = (lo + hi) >> 1;
-      if (warp_count_ge(kp, mid) >= kk) {
+      if (count_ge(vals, key_value(mid)) >= kk) {
         lo = mid;
       } else {
         hi = mid;
       }
     }
-    thr = lo;
-  }
-  __syncwarp();  // hist is reused by the next call
-
-  invalid = (nonfinite || finite == 0) ? 1 : 0;
-  if (a.unfinished && a.finished) invalid = 1;
-  if (a.finished && a.forbid_eos) invalid = 1;
-  const bool seed_valid = a.seed >= 0 && static_cast<uint64_t>(a.seed) < (1ull << 32);
-  const bool counter_valid = a.counter >= 0 && a.counter <= kMaxCounter;
-  if (!seed_valid || !counter_valid) invalid = 1;
-  const uint32_t seed32 = seed_valid ? static_cast<uint32_t>(a.seed) : 0u;
-  const uint64_t off64 = counter_valid ? static_cast<uint64_t>(a.counter) * kPhiloxStride : 0ull;
-
-  // ---- finite eligible tokens (key >= thr) in token order, scored by Philox-Gumbel
-  uint32_t mine = 0;
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    if (lane + 32 * i < kVocabChunks) {
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const uint32_t k0 = kp[i][e] & 0xffffu, k1 = kp[i][e] >> 16;
-        mine += (k0 >= thr && k0 != kKeyNegInf) + (k1 >= thr && k1 != kKeyNegInf);
-      }
-    }
-  }
-  uint32_t pos = mine;
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const uint32_t y = __shfl_up_sync(0xffffffffu, pos, o);
-    if (lane >= o) pos += y;
-  }
-  const uint32_t total = __shfl_sync(0xffffffffu, pos, 31);
-  pos -= mine;
-
-  float best = -CUDART_INF_F;
-  int best_id = kVocab;
-  auto score = [&](int t) {
-    const float value = a.finished ? 0.0f : bf2f(a.g[t]);
-    const float gm = clamped_gumbel(philox_uniform(seed32, off64 + static_cast<uint64_t>(t)));
-    const float sc = __fadd_rn(__fdiv_rn(value, prm.temperature), gm);
-    if (sc > best || (sc == best && t < best_id)) {
-      best = sc;
-      best_id = t;
-    }
-  };
-  if (total <= static_cast<uint32_t>(kElig)) {
-#pragma unroll
+#pragma unroll 1
     for (int i = 0; i < 8; ++i) {
-      const int c = lane + 32 * i;
-      if (c < kVocabChunks) {
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const uint32_t k0 = kp[i][e] & 0xffffu, k1 = kp[i][e] >> 16;
-          if (k0 >= thr && k0 != kKeyNegInf) elig[pos++] = static_cast<uint16_t>(8 * c + 2 * e);
-          if (k1 >= thr && k1 != kKeyNegInf) elig[pos++] = static_cast<uint16_t>(8 * c + 2 * e + 1);
-        }
-      }
-    }
-    __syncwarp();
-    for (uint32_t e = lane; e < total; e += 32) score(elig[e]);
-    __syncwarp();
-  } else {  // many ties: every lane scores its own eligible tokens
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const int c = lane + 32 * i;
-      if (c < kVocabChunks) {
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const uint32_t k0 = kp[i][e] & 0xffffu, k1 = kp[i][e] >> 16;
-          if (k0 >= thr && k0 != kKeyNegInf) score(8 * c + 2 * e);
-          if (k1 >= thr && k1 != kKeyNegInf) score(8 * c + 2 * e + 1);
+      const int ch = lane + 32 * i;
+      if (ch < kVocabChunks) {
+        for (int e = 0; e < 8; ++e) {
+          const int t = 8 * ch + e;
+          const uint32_t key = sample_key(vals[t]);
+          if (key >= lo && key != kKeyNegInf) {
+            const float g = clamped_gumbel(philox_uniform(seed32, off64 + static_cast<uint64_t>(t)));
+            keep_best(best, __fadd_rn(__fdiv_rn(bits2f(vals[t]), prm.temperature), g), t);
+          }
         }
       }
     }
   }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    const float ob = __shfl_xor_sync(0xffffffffu, best, o);
-    const int oi = __shfl_xor_sync(0xffffffffu, best_id, o);
-    if (ob > best || (ob == best && oi < best_id)) {
-      best = ob;
-      best_id = oi;
-    }
-  }
-  token = best_id;
-  if (token >= kVocab || best == -CUDART_INF_F) {
+  best = warp_best(best);
+  int token = best.id;
+  if (token >= kVocab || best.score == -CUDART_INF_F) {
     invalid = 1;
     token = 0;
   }
@@ -676,32 +767,31 @@ __global__ void __launch_bounds__(kTThreads, 1) tile_frame_kernel(Frame f, const
   TileSmem& sm = *reinterpret_cast<TileSmem*>(smem_raw + pad);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int rp = f.rp;
-  const int spt = kTRows / rp;  // sessions (slots) per tile
   const bool folded = f.emb_proj != nullptr;
 
-  // ---- sessions [spt * tile, +spt) of the active list
+  // ---- sessions [8 tile, +8) of the active list
   if (warp == 0) {
     int seen = 0;
-    const int first = spt * static_cast<int>(blockIdx.x);
+    const int first = kTSess * static_cast<int>(blockIdx.x);
     for (int base = 0; base < f.n; base += 32) {
       const int s = base + lane;
       const bool act = s < f.n && (f.active == nullptr || f.active[s]);
       const unsigned m = __ballot_sync(0xffffffffu, act);
       const int rank = seen + __popc(m & ((1u << lane) - 1u));
-      if (act && rank >= first && rank < first + spt) sm.sess[rank - first] = s;
+      if (act && rank >= first && rank < first + kTSess) sm.sess[rank - first] = s;
       seen += __popc(m);
     }
     if (lane == 0) {
       const int left = seen - first;
-      sm.n_sess = left <= 0 ? 0 : (left < spt ? left : spt);
+      sm.n_sess = left <= 0 ? 0 : (left < kTSess ? left : kTSess);
       sm.err = 0;
     }
   }
   __syncthreads();
   const int n_sess = sm.n_sess;
   if (n_sess == 0) return;
-  // row r belongs to session slot r % spt (sub-row r / spt); it is live iff that slot is
-  auto live = [&](int r) { return r % spt < n_sess; };
+  // row r belongs to session slot r % 8 (sub-row r / 8); live iff that slot is and r / 8 < rp
+  auto live = [&](int r) { return (r & 7) < n_sess && (r >> 3) < rp; };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kSlots; ++s) {
@@ -720,6 +810,8 @@ __global__ void __launch_bounds__(kTThreads, 1) tile_frame_kernel(Frame f, const
     const int s = threadIdx.x;
     const int sid = sm.sess[s];
     sm.ctr[s] = f.counter_io[sid];
+    sm.seed[s] = f.seed[sid];
+    sm.flags[s] = (f.unfinished[sid] ? 1u : 0u) | (f.finished[sid] ? 2u : 0u) | (f.forbid[sid] ? 4u : 0u);
     int32_t inv = 0;
     bool en = !f.unfinished[sid] && !f.finished[sid] && !f.forbid[sid];
     if (en && f.final_w == nullptr) {
@@ -739,18 +831,36 @@ __global__ void __launch_bounds__(kTThreads, 1) tile_frame_kernel(Frame f, const
   __syncthreads();
   tmem_fence_after_sync();
 
-  if (warp == kTWarps) {
-    if (lane == 0) producer(sm, maps, folded);
-  } else {
+  if (warp >= kTWarps) {  // producer warpgroup
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kProducerRegs));
+    if (warp == kTWarps && lane == 0) producer(sm, maps, folded);
+    return;  // its copies complete on the full barriers, which the consumers wait for
+  }
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kConsumerRegs));
+  {
+    // per-thread constants: LN weights of columns [8 lane, +8); flags of the
+    // session whose rows this thread holds in mma.sync fragments (slot lane / 4)
+    float g1[8], g2[8];
+    unpack8(*reinterpret_cast<const uint4*>(f.ln1 + lane * 8), g1);
+    unpack8(*reinterpret_cast<const uint4*>(f.ln2 + lane * 8), g2);
+    const int my_slot = lane >> 2;
+    const bool my_live = my_slot < n_sess;
+    bool my_unf = false, my_fin = false, my_forbid = false;
+    if (my_live) {
+      const int sid = sm.sess[my_slot];
+      my_unf = f.unfinished[sid];
+      my_fin = f.finished[sid];
+      my_forbid = f.forbid[sid];
+    }
     int it = 0;
     for (int p = 0; p < kPositions; ++p) {
-      // ---------------- input rows
+      // ---------------- input rows (folded p >= 1: written by the sampling warps)
       if (has_in_projection(folded, p)) {
         for (int i = threadIdx.x; i < kTRows * (kEmbed / 8); i += kTConsumers) {
           const int r = i / (kEmbed / 8), ch = i % (kEmbed / 8);
           uint4 v = make_uint4(0, 0, 0, 0);
           if (live(r)) {
-            const int slot = r % spt, sub = r / spt;
+            const int slot = r & 7, sub = r >> 3;
             const bf16* src;
             if (p == 0) {
               src = f.hidden + (static_cast<int64_t>(sm.sess[slot]) * rp + sub) * kEmbed;
@@ -775,66 +885,70 @@ __global__ void __launch_bounds__(kTThreads, 1) tile_frame_kernel(Frame f, const
             *reinterpret_cast<uint32_t*>(sm.x + r * kLdX + n) = pack_bf16x2(__fadd_rn(y0, q0), __fadd_rn(y1, q1));
           }
         });
-      } else {
-        for (int i = threadIdx.x; i < kTRows * (kTD / 8); i += kTConsumers) {
-          const int r = i / (kTD / 8), ch = i % (kTD / 8);
-          uint4 out = make_uint4(0, 0, 0, 0);
-          if (live(r)) {
-            const int slot = r % spt;
-            float e8[8], p8[8];
-            unpack8(*reinterpret_cast<const uint4*>(
-                        f.emb_proj + (static_cast<int64_t>(p - 1) * kVocab + tile_input_token(f, sm, slot, p - 1)) * kTD +
-                        ch * 8),
-                    e8);
-            unpack8(*reinterpret_cast<const uint4*>(f.pos + static_cast<int64_t>(p) * kTD + ch * 8), p8);
-            out.x = pack_bf16x2(__fadd_rn(e8[0], p8[0]), __fadd_rn(e8[1], p8[1]));
-            out.y = pack_bf16x2(__fadd_rn(e8[2], p8[2]), __fadd_rn(e8[3], p8[3]));
-            out.z = pack_bf16x2(__fadd_rn(e8[4], p8[4]), __fadd_rn(e8[5], p8[5]));
-            out.w = pack_bf16x2(__fadd_rn(e8[6], p8[6]), __fadd_rn(e8[7], p8[7]));
-          }
-          *reinterpret_cast<uint4*>(sm.x + r * kLdX + ch * 8) = out;
+      }
+      // head p bias; per-position sampling state (the histograms are zeroed per use)
+      {
+        const bf16* hb = f.head_b + static_cast<int64_t>(p) * kVocab;
+        if (threadIdx.x < kVocabChunks) {
+          *reinterpret_cast<uint4*>(sm.hb + 8 * threadIdx.x) = *reinterpret_cast<const uint4*>(hb + 8 * threadIdx.x);
+        }
+        if (threadIdx.x < kTSess) {
+          sm.amax[threadIdx.x] = 0;
+          sm.nonfinite[threadIdx.x] = 0;
         }
       }
       cbar();
 
       // ---------------- LN1, qkv
-      layer_norm_rows(sm.x, sm.xa, f.ln1);
+      layer_norm_rows(sm.x, sm.xa, g1);
       cbar();
-      gemm_n(sm, it, sm.xa, kLdX, 12, [&](int nb, const float (&acc)[4]) {
-        const int n = kCRows * nb + 8 * warp + 2 * (lane & 3);
-        const int r = lane >> 2;
-        *reinterpret_cast<uint32_t*>(sm.u.qkv + r * kLdQkv + n) = pack_bf16x2(acc[0], acc[1]);
-        *reinterpret_cast<uint32_t*>(sm.u.qkv + (r + 8) * kLdQkv + n) = pack_bf16x2(acc[2], acc[3]);
-      });
+      {
+        uint32_t a[16][4];
+        load_a(a, sm.xa, kLdX);
+        gemm_n(sm, it, a, 12, [&](int nb, const float (&acc)[4]) {
+          const int n = kCRows * nb + 8 * warp + 2 * (lane & 3);
+          const int r = lane >> 2;
+          *reinterpret_cast<uint32_t*>(sm.u.qkv + r * kLdQkv + n) = pack_bf16x2(acc[0], acc[1]);
+          *reinterpret_cast<uint32_t*>(sm.u.qkv + (r + 8) * kLdQkv + n) = pack_bf16x2(acc[2], acc[3]);
+        });
+      }
       cbar();
 
-      // ---------------- KV append + attention (warps 0-3, one head each)
-      if (warp < kTHeads) attention_warp(sm, p);
+      // ---------------- KV append + attention
+      attention(sm, p);
       cbar();
 
       // ---------------- o-projection + residual
-      gemm_n(sm, it, sm.xa, kLdX, 4, [&](int nb, const float (&acc)[4]) {
-        const int n = kCRows * nb + 8 * warp + 2 * (lane & 3);
+      {
+        uint32_t a[16][4];
+        load_a(a, sm.xa, kLdX);
+        gemm_n(sm, it, a, 4, [&](int nb, const float (&acc)[4]) {
+          const int n = kCRows * nb + 8 * warp + 2 * (lane & 3);
 #pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-          bf16* xr = sm.x + ((lane >> 2) + 8 * hh) * kLdX + n;
-          *reinterpret_cast<uint32_t*>(xr) = pack_bf16x2(__fadd_rn(bf2f(xr[0]), round_bf16(acc[2 * hh])),
-                                                         __fadd_rn(bf2f(xr[1]), round_bf16(acc[2 * hh + 1])));
-        }
-      });
+          for (int hh = 0; hh < 2; ++hh) {
+            bf16* xr = sm.x + ((lane >> 2) + 8 * hh) * kLdX + n;
+            *reinterpret_cast<uint32_t*>(xr) = pack_bf16x2(__fadd_rn(bf2f(xr[0]), round_bf16(acc[2 * hh])),
+                                                           __fadd_rn(bf2f(xr[1]), round_bf16(acc[2 * hh + 1])));
+          }
+        });
+      }
       cbar();
 
       // ---------------- LN2, FFN1 + GELU
-      layer_norm_rows(sm.x, sm.xa, f.ln2);
+      layer_norm_rows(sm.x, sm.xa, g2);
       cbar();
-      gemm_n(sm, it, sm.xa, kLdX, 16, [&](int nb, const float (&acc)[4]) {
-        const int n = kCRows * nb + 8 * warp + 2 * (lane & 3);
+      {
+        uint32_t a[16][4];
+        load_a(a, sm.xa, kLdX);
+        gemm_n(sm, it, a, 16, [&](int nb, const float (&acc)[4]) {
+          const int n = kCRows * nb + 8 * warp + 2 * (lane & 3);
 #pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-          *reinterpret_cast<uint32_t*>(sm.u.hid + ((lane >> 2) + 8 * hh) * kLdHid + n) =
-              pack_bf16x2(gelu_tanh(round_bf16(acc[2 * hh])), gelu_tanh(round_bf16(acc[2 * hh + 1])));
-        }
-      });
+          for (int hh = 0; hh < 2; ++hh) {
+            *reinterpret_cast<uint32_t*>(sm.u.hid + ((lane >> 2) + 8 * hh) * kLdHid + n) =
+                pack_bf16x2(gelu_tanh(round_bf16(acc[2 * hh])), gelu_tanh(round_bf16(acc[2 * hh + 1])));
+          }
+        });
+      }
       cbar();
 
       // ---------------- FFN2 + residual
@@ -849,59 +963,82 @@ __global__ void __launch_bounds__(kTThreads, 1) tile_frame_kernel(Frame f, const
       });
       cbar();
 
-      // ---------------- head p (+bias), CFG combine, raw logits to the test hook
+      // ---------------- head p: bias, CFG combine, constraints, order keys and
+      // the first radix digit (top-k) or the running left-most maximum (argmax)
       {
-        const bf16* hb = f.head_b + static_cast<int64_t>(p) * kVocab;
-        gemm_n(sm, it, sm.x, kLdX, 32, [&](int nb, const float (&acc)[4]) {
+        uint32_t a[16][4];
+        load_a(a, sm.x, kLdX);
+        bool nf = false;
+        uint32_t amax = 0;
+        uint16_t* vals = sm.u.val + my_slot * kVocab;
+        gemm_n(sm, it, a, 32, [&](int nb, const float (&acc)[4]) {
           const int n = kCRows * nb + 8 * warp + 2 * (lane & 3);
-          if (n < kVocab) {  // n is even and kVocab is even: the pair stays inside
-            const float b0 = bf2f(hb[n]), b1 = bf2f(hb[n + 1]);
-            const int r = lane >> 2;
+          if (n < kVocab && my_live) {  // n is even and kVocab is even: the pair stays inside
+            const float b0 = bf2f(sm.hb[n]), b1 = bf2f(sm.hb[n + 1]);
             const bf16 c0 = f2bf(__fadd_rn(acc[0], b0)), c1 = f2bf(__fadd_rn(acc[1], b1));
             const bf16 u0 = f2bf(__fadd_rn(acc[2], b0)), u1 = f2bf(__fadd_rn(acc[3], b1));
-            if (rp == 2) {
-              *reinterpret_cast<uint32_t*>(sm.u.g + r * kVocab + n) =
-                  pack_bf16x2(guided_logit(bf2f(c0), bf2f(u0), f.prm.cfg_scale),
-                              guided_logit(bf2f(c1), bf2f(u1), f.prm.cfg_scale));
-            } else {
-              *reinterpret_cast<uint32_t*>(sm.u.g + r * kVocab + n) = pack_bf16x2(bf2f(c0), bf2f(c1));
-              *reinterpret_cast<uint32_t*>(sm.u.g + (r + 8) * kVocab + n) = pack_bf16x2(bf2f(u0), bf2f(u1));
-            }
             if (f.logits_out) {
-#pragma unroll
-              for (int hh = 0; hh < 2; ++hh) {
-                const int row = r + 8 * hh;
-                if (live(row)) {
-                  const int slot = row % spt, sub = row / spt;
-                  bf16* lo = f.logits_out +
-                             ((static_cast<int64_t>(sm.sess[slot]) * kPositions + p) * rp + sub) * kVocab + n;
-                  lo[0] = hh ? u0 : c0;
-                  lo[1] = hh ? u1 : c1;
-                }
+              bf16* lo = f.logits_out + (static_cast<int64_t>(sm.sess[my_slot]) * kPositions + p) * rp * kVocab + n;
+              lo[0] = c0;
+              lo[1] = c1;
+              if (rp == 2) {
+                lo[kVocab] = u0;
+                lo[kVocab + 1] = u1;
               }
             }
+            float v0 = bf2f(c0), v1 = bf2f(c1);
+            if (rp == 2) {
+              v0 = guided_logit(v0, bf2f(u0), f.prm.cfg_scale);
+              v1 = guided_logit(v1, bf2f(u1), f.prm.cfg_scale);
+            }
+            const uint32_t b0c = constrain(__bfloat16_as_ushort(f2bf(v0)), n, my_unf, my_fin, my_forbid, nf);
+            const uint32_t b1c = constrain(__bfloat16_as_ushort(f2bf(v1)), n + 1, my_unf, my_fin, my_forbid, nf);
+            *reinterpret_cast<uint32_t*>(vals + n) = b0c | (b1c << 16);
+            const uint32_t k0 = sample_key(b0c), k1 = sample_key(b1c);
+            const uint32_t e0 = (k0 << 16) | (0xffffu - static_cast<uint32_t>(n));
+            const uint32_t e1 = (k1 << 16) | (0xffffu - static_cast<uint32_t>(n + 1));
+            amax = e0 > amax ? e0 : amax;
+            amax = e1 > amax ? e1 : amax;
           }
         });
+        amax = max(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+        amax = max(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+        if (my_live && (lane & 3) == 0) atomicMax(&sm.amax[my_slot], amax);
+        if (nf) atomicOr(&sm.nonfinite[my_slot], 1u);
       }
       cbar();
 
-      // ---------------- sampling: warp w takes slots w (and w + 8 without CFG)
-      for (int slot = warp; slot < n_sess; slot += kTWarps) {
-        const int sid = sm.sess[slot];
-        WarpSample ws;
-        ws.g = sm.u.g + slot * kVocab;
-        ws.unfinished = f.unfinished[sid];
-        ws.finished = f.finished[sid];
-        ws.forbid_eos = f.forbid[sid];
-        ws.seed = f.seed[sid];
-        ws.counter = sm.ctr[slot];
+      // ---------------- sampling: warp w takes session slot w, then writes the
+      // session's next input rows (folded tables)
+      if (warp < n_sess) {
+        const int slot = warp;
         int invalid = 0;
-        const int token = warp_sample(ws, f.prm, sm.hist[warp], sm.elig[warp], &invalid);
+        const int token =
+            sample_slot(sm, f, slot, reinterpret_cast<uint16_t*>(sm.xa) + slot * kListStride, &invalid);
+        const int64_t counter = sm.ctr[slot];
+        __syncwarp();
         if (lane == 0) {
           sm.tok[slot][p] = token;
           sm.inv[slot] |= invalid;
-          const bool counter_valid = ws.counter >= 0 && ws.counter <= kMaxCounter;
-          if (!f.prm.argmax && counter_valid) sm.ctr[slot] = ws.counter + 1;
+          const bool counter_valid = counter >= 0 && counter <= kMaxCounter;
+          if (!f.prm.argmax && counter_valid) sm.ctr[slot] = counter + 1;
+        }
+        if (folded && p + 1 < kPositions) {
+          int64_t tin = token;
+          if (f.forced) {
+            const int64_t t = f.forced[static_cast<int64_t>(sm.sess[slot]) * kPositions + p];
+            tin = t < 0 ? 0 : (t >= kVocab ? kVocab - 1 : t);
+          }
+          float e8[8], p8[8];
+          unpack8(*reinterpret_cast<const uint4*>(f.emb_proj + (static_cast<int64_t>(p) * kVocab + tin) * kTD + lane * 8),
+                  e8);
+          unpack8(*reinterpret_cast<const uint4*>(f.pos + static_cast<int64_t>(p + 1) * kTD + lane * 8), p8);
+          float y[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) y[e] = __fadd_rn(e8[e], p8[e]);
+          const uint4 row = pack8(y);
+          *reinterpret_cast<uint4*>(sm.x + slot * kLdX + lane * 8) = row;
+          if (rp == 2) *reinterpret_cast<uint4*>(sm.x + (slot + 8) * kLdX + lane * 8) = row;
         }
       }
       cbar();
@@ -909,7 +1046,7 @@ __global__ void __launch_bounds__(kTThreads, 1) tile_frame_kernel(Frame f, const
   }
 
   // ---- drain: no TMA copy may still be writing when the CTA leaves
-  __syncthreads();
+  cbar();
   if (threadIdx.x == 0 && sm.err) {
     for (int s = 0; s < kSlots; ++s) {
       const int last = sm.last_issued[s];
@@ -918,7 +1055,7 @@ __global__ void __launch_bounds__(kTThreads, 1) tile_frame_kernel(Frame f, const
   }
 
   // ---- commit: tokens, counters, flags, next-frame embedding
-  for (int i = threadIdx.x; i < n_sess * kPositions; i += blockDim.x) {
+  for (int i = threadIdx.x; i < n_sess * kPositions; i += kTConsumers) {
     const int slot = i / kPositions, pp = i % kPositions;
     const int sid = sm.sess[slot];
     const int32_t t = sm.tok[slot][pp];
@@ -933,7 +1070,7 @@ __global__ void __launch_bounds__(kTThreads, 1) tile_frame_kernel(Frame f, const
     if (f.eos_slot[sid] < 0) f.end_frame[sid] = f.finished[sid] ? 0 : -1;
   }
   // sum_p table_p[token_p], each add rounded to bf16, in position order; / 16
-  for (int i = threadIdx.x; i < n_sess * (kEmbed / 8); i += blockDim.x) {
+  for (int i = threadIdx.x; i < n_sess * (kEmbed / 8); i += kTConsumers) {
     const int slot = i / (kEmbed / 8), k8 = 8 * (i % (kEmbed / 8));
     float acc[8];
 #pragma unroll
@@ -945,16 +1082,14 @@ __global__ void __launch_bounds__(kTThreads, 1) tile_frame_kernel(Frame f, const
 #pragma unroll
       for (int e = 0; e < 8; ++e) acc[e] = pp == 0 ? v[e] : round_bf16(__fadd_rn(acc[e], v[e]));
     }
-    uint4 out;
-    out.x = pack_bf16x2(__fdiv_rn(acc[0], 16.0f), __fdiv_rn(acc[1], 16.0f));
-    out.y = pack_bf16x2(__fdiv_rn(acc[2], 16.0f), __fdiv_rn(acc[3], 16.0f));
-    out.z = pack_bf16x2(__fdiv_rn(acc[4], 16.0f), __fdiv_rn(acc[5], 16.0f));
-    out.w = pack_bf16x2(__fdiv_rn(acc[6], 16.0f), __fdiv_rn(acc[7], 16.0f));
-    *reinterpret_cast<uint4*>(f.next_emb + static_cast<int64_t>(sm.sess[slot]) * kEmbed + k8) = out;
+    float out[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) out[e] = __fdiv_rn(acc[e], 16.0f);
+    *reinterpret_cast<uint4*>(f.next_emb + static_cast<int64_t>(sm.sess[slot]) * kEmbed + k8) = pack8(out);
   }
 
   tmem_fence_before_sync();
-  __syncthreads();
+  cbar();
   if (warp == 0) {
     tmem_fence_after_sync();
     tmem_dealloc(sm.tmem, kTmemCols);
@@ -993,8 +1128,7 @@ cudaError_t launch_tile_frame(const Frame& f, cudaStream_t stream) {
       !make_weight_map(&maps.head, f.head_w, kTD, static_cast<uint64_t>(kPositions) * kVocab, kCRows)) {
     return cudaErrorInvalidValue;
   }
-  const int spt = kTRows / f.rp;
-  const int tiles = (f.n + spt - 1) / spt;
+  const int tiles = (f.n + kTSess - 1) / kTSess;
   cudaError_t e = cudaMemsetAsync(f.eos_count, 0, sizeof(int32_t), stream);
   if (e != cudaSuccess) return e;
   tile_frame_kernel<<<tiles, kTThreads, kTSmemBytes, stream>>>(f, maps);

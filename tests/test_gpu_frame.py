@@ -298,3 +298,36 @@ def test_gpu_no_further_from_exact_than_oracle(engines):
     cpu_err, _ = logit_errors(r16.logits.reshape(n, POSITIONS, 2, VOCAB), exact)
     assert gpu_err.mean() <= 1.5 * cpu_err.mean() + 1e-4, (gpu_err.mean(), cpu_err.mean())
     assert gpu_err.max() <= 2.0 * cpu_err.max() + 1e-4, (gpu_err.max(), cpu_err.max())
+
+
+@pytest.mark.parametrize("path", [FUSED, TILE])
+@pytest.mark.parametrize("kind", ["flat", "sharp", "ties"])
+def test_sampler_row_shapes(path, kind):
+    """Logit rows that drive each top-k select path: flat rows (every token
+    tied: the whole-row search), a few dominant tokens (the narrowest window)
+    and a tie block straddling the k-th place; tokens must match the oracle
+    sampler on the GPU's logits."""
+    from magpie_tts_rt_b200.local_ar import LocalArEngine
+    shape = SHAPE_BASELINE
+    w = make_weights(shape, seed=26, dtype=torch.bfloat16, profile="parity", with_final=True)
+    g = torch.Generator().manual_seed(9)
+    if kind == "flat":
+        w.head_w.zero_()
+        w.head_b.fill_(0.5)
+    elif kind == "sharp":
+        w.head_w.mul_(0.25)
+        for p in range(POSITIONS):
+            w.head_b[p, torch.randperm(2016, generator=g)[:40]] = 6.0
+    else:
+        w.head_w.zero_()
+        w.head_b.copy_(torch.randn(w.head_b.shape, generator=g).to(torch.bfloat16))
+        for p in range(POSITIONS):
+            w.head_b[p, torch.randperm(2016, generator=g)[:120]] = 3.0  # 120 ties around k = 80
+    eng = LocalArEngine(w, max_streams=8, path=path)
+    n = 5
+    hidden = _hidden(n, 31)
+    flags = (np.array([1, 1, 0, 1, 0], bool), np.array([0, 0, 0, 0, 1], bool), np.zeros(n, bool))
+    seed = np.arange(n) + 40
+    counter = np.arange(n) * 3
+    gpu = run_gpu(eng, hidden, flags, seed, counter)
+    check_frame(w, hidden, flags, seed, counter, gpu)
