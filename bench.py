@@ -459,9 +459,18 @@ def main():
         tf = flops / t_frame / 1e12
         gbs = bytes_ / t_frame / 1e9
         tensor_peak = peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"])
-        roof = {"bound": "tensor", "kernel": "local_ar_frame (one frame step, all launches)",
+        # dominant kernel: the frame kernel (98.4% of device time in the launch list); one frame
+        # call = that kernel + the EOS projection/decision kernels, timed together by CUDA events
+        tile = res["path"] == "tile kernel"
+        roof = {"bound": "tensor",
+                "kernel": ("tile_frame_kernel" if tile else res["path"]) +
+                          " (per frame call, with the EOS projection/decision kernels: 0.6% of device time)",
                 "achieved": tf, "peak": tensor_peak, "unit": "TFLOP/s", "frac": tf / tensor_peak,
-                "peak_kind": f"{peaks_kind} sustained bf16", "traffic": None,
+                "peak_kind": f"{peaks_kind} sustained bf16",
+                # dram__bytes_read.sum + dram__bytes_write.sum of one tile_frame_kernel launch at
+                # 1024 sessions (profiles/tile_frame_kernel_config4.md)
+                "traffic": 27.64e6 if tile and res["n_local"] == 1024 else None,
+                "avg_frame_call_us": t_frame * 1e6,
                 "hbm_achieved_gbs": gbs, "hbm_frac": gbs / peaks["hbm_gbs"],
                 "algorithmic_flops_per_frame_step": flops, "algorithmic_bytes_per_frame_step": bytes_}
         line = {"metric": METRIC, "value": res["value"], "unit": "frames/s", "n_gpus": world,
