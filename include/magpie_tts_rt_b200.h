@@ -265,17 +265,21 @@ MTT_B200_API int mtt_b200_launch_fold_in_projection(const mtt_b200_local_ar_shap
                                                    void* stream);
 
 /* Frame implementations.  For the shape d_model 256, 4 heads, FFN 1024,
- * 1 layer two fused single-launch kernels exist, both on 16-row tiles (8
- * sessions with CFG, 16 without): FUSED_CLUSTER spreads a tile over a 16-CTA
- * thread-block cluster (lowest latency per tile, at most a few clusters on
- * the device at once); FUSED_TILE runs a tile in one CTA with its KV cache in
- * tensor memory (every SM busy at large batches).  AUTO picks FUSED_TILE
- * when the batch has more tiles than the device runs clusters at once,
- * FUSED_CLUSTER otherwise, and the phase kernels for other shapes. */
+ * 1 layer three fused single-launch kernels exist: FUSED_CLUSTER spreads a
+ * 16-row tile (8 sessions with CFG, 16 without) over a 16-CTA thread-block
+ * cluster (lowest latency per tile, at most a few clusters on the device at
+ * once); FUSED_TILE runs 8 sessions in one CTA with their KV cache in tensor
+ * memory; FUSED_PAIR runs 16 sessions on a 2-CTA cluster, each CTA streaming
+ * half of every weight matrix (the most sessions per second at large
+ * batches with fewer weight bytes per SM).  AUTO picks FUSED_CLUSTER while
+ * the batch's 16-row tiles need at most two waves of the clusters the device
+ * runs at once, FUSED_TILE above that, and the phase kernels for other
+ * shapes. */
 #define MTT_B200_FRAME_PATH_AUTO 0
 #define MTT_B200_FRAME_PATH_PHASE_KERNELS 1
 #define MTT_B200_FRAME_PATH_FUSED_CLUSTER 2
 #define MTT_B200_FRAME_PATH_FUSED_TILE 3
+#define MTT_B200_FRAME_PATH_FUSED_PAIR 4
 
 /* Sampling configuration; the reference's values are 80 / 0.6 / 2.5 with CFG
  * and top-k.  argmax != 0 selects greedy decoding (no RNG, counter unchanged;
@@ -358,8 +362,8 @@ MTT_B200_API int mtt_b200_launch_local_ar_frame_static_workspace(const mtt_b200_
                                                                 const mtt_b200_stream_batch_t* batch,
                                                                 void* stream);
 
-/* The path (MTT_B200_FRAME_PATH_PHASE_KERNELS, _FUSED_CLUSTER or
- * _FUSED_TILE) that mtt_b200_launch_local_ar_frame takes for this shape,
+/* The path (MTT_B200_FRAME_PATH_PHASE_KERNELS, _FUSED_CLUSTER, _FUSED_TILE or
+ * _FUSED_PAIR) that mtt_b200_launch_local_ar_frame takes for this shape,
  * configuration and batch size on the current device, or
  * MTT_B200_STATUS_UNSUPPORTED. */
 MTT_B200_API int32_t mtt_b200_local_ar_frame_path(const mtt_b200_local_ar_shape_t* shape,

@@ -100,6 +100,7 @@ PATH_AUTO = 0
 PATH_PHASE_KERNELS = 1
 PATH_FUSED_CLUSTER = 2
 PATH_FUSED_TILE = 3
+PATH_FUSED_PAIR = 4
 
 
 class StreamBatch(ctypes.Structure):

@@ -437,9 +437,12 @@ extern "C" MTT_B200_API size_t mtt_b200_local_ar_frame_workspace_size(const mtt_
 namespace {
 
 // Resolves the path for a shape / configuration / batch size on the current
-// device.  AUTO: the tile kernel (one CTA per 16-row tile) once the tiles
-// outnumber the fused kernel's concurrent clusters, the fused cluster kernel
-// below that (lower latency per tile), the phase kernels for other shapes.
+// device.  AUTO: the fused cluster kernel while the batch's 16-row tiles need
+// at most two waves of the clusters the device runs at once (on B200 a wave
+// of the cluster kernel takes ~0.3 ms per frame, one wave of the tile kernel
+// ~0.8 ms), the tile kernel above that, the phase kernels for other shapes.
+// The pair kernel does the same work per SM as the tile kernel and is
+// selected explicitly.
 int32_t resolve_path(const mtt_b200_local_ar_shape_t* shape, const mtt_b200_sampling_config_t* sampling,
                      int32_t n_streams) {
   mtt::Frame probe{};
@@ -451,13 +454,16 @@ int32_t resolve_path(const mtt_b200_local_ar_shape_t* shape, const mtt_b200_samp
   probe.in_proj = shape->d_model != mtt::kEmbed;
   const bool fused = mtt::fused_frame_supported(probe);
   const bool tile = mtt::tile_frame_supported(probe);
+  const bool pair = mtt::pair_frame_supported(probe);
   switch (sampling->path) {
     case MTT_B200_FRAME_PATH_AUTO: {
-      if (!fused && !tile) return MTT_B200_FRAME_PATH_PHASE_KERNELS;
+      if (!fused && !tile && !pair) return MTT_B200_FRAME_PATH_PHASE_KERNELS;
       const int spt = 16 / probe.rp;
       const int tiles = (n_streams + spt - 1) / spt;
-      if (fused && (!tile || tiles <= mtt::fused_frame_clusters())) return MTT_B200_FRAME_PATH_FUSED_CLUSTER;
-      return MTT_B200_FRAME_PATH_FUSED_TILE;
+      if (fused && tiles <= 2 * mtt::fused_frame_clusters()) return MTT_B200_FRAME_PATH_FUSED_CLUSTER;
+      if (tile) return MTT_B200_FRAME_PATH_FUSED_TILE;
+      if (pair) return MTT_B200_FRAME_PATH_FUSED_PAIR;
+      return MTT_B200_FRAME_PATH_FUSED_CLUSTER;
     }
     case MTT_B200_FRAME_PATH_PHASE_KERNELS:
       return MTT_B200_FRAME_PATH_PHASE_KERNELS;
@@ -465,6 +471,8 @@ int32_t resolve_path(const mtt_b200_local_ar_shape_t* shape, const mtt_b200_samp
       return fused ? MTT_B200_FRAME_PATH_FUSED_CLUSTER : MTT_B200_STATUS_UNSUPPORTED;
     case MTT_B200_FRAME_PATH_FUSED_TILE:
       return tile ? MTT_B200_FRAME_PATH_FUSED_TILE : MTT_B200_STATUS_UNSUPPORTED;
+    case MTT_B200_FRAME_PATH_FUSED_PAIR:
+      return pair ? MTT_B200_FRAME_PATH_FUSED_PAIR : MTT_B200_STATUS_UNSUPPORTED;
     default:
       return MTT_B200_STATUS_INVALID_ARGUMENT;
   }
@@ -484,7 +492,8 @@ extern "C" MTT_B200_API int32_t mtt_b200_local_ar_frame_launch_count(const mtt_b
                                                                      int32_t n_streams) {
   if (!mtt::shape_ok(shape) || sampling == nullptr || n_streams <= 0) return 0;
   const int32_t path = resolve_path(shape, sampling, n_streams);
-  if (path == MTT_B200_FRAME_PATH_FUSED_CLUSTER || path == MTT_B200_FRAME_PATH_FUSED_TILE) {
+  if (path == MTT_B200_FRAME_PATH_FUSED_CLUSTER || path == MTT_B200_FRAME_PATH_FUSED_TILE ||
+      path == MTT_B200_FRAME_PATH_FUSED_PAIR) {
     return 3;  // fused frame, EOS projection, EOS finish
   }
   if (path != MTT_B200_FRAME_PATH_PHASE_KERNELS) return 0;
@@ -584,6 +593,9 @@ extern "C" MTT_B200_API int mtt_b200_launch_local_ar_frame(const mtt_b200_local_
   }
   if (path == MTT_B200_FRAME_PATH_FUSED_TILE) {
     return launch_tile_frame(f, st) == cudaSuccess ? MTT_B200_STATUS_OK : MTT_B200_STATUS_CUDA_ERROR;
+  }
+  if (path == MTT_B200_FRAME_PATH_FUSED_PAIR) {
+    return launch_pair_frame(f, st) == cudaSuccess ? MTT_B200_STATUS_OK : MTT_B200_STATUS_CUDA_ERROR;
   }
   const int d = f.d, F = f.F;
   frame_begin_kernel<<<1, kBeginThreads, 0, st>>>(f);

@@ -88,6 +88,12 @@ cudaError_t launch_fused_frame(const Frame& f, cudaStream_t stream);
 bool tile_frame_supported(const Frame& f);
 cudaError_t launch_tile_frame(const Frame& f, cudaStream_t stream);
 
+// Pair kernel (frame_pair.cu): a 2-CTA cluster per 16 sessions, each CTA
+// streaming half of every weight matrix.
+bool pair_frame_supported(const Frame& f);
+int pair_frame_clusters();
+cudaError_t launch_pair_frame(const Frame& f, cudaStream_t stream);
+
 // EOS projection + decision for the sessions a fused or tile kernel registered.
 cudaError_t launch_frame_eos(const Frame& f, cudaStream_t stream);
 

@@ -45,6 +45,7 @@
 
 #include "frame_common.cuh"
 #include "ptx.cuh"
+#include "tile_common.cuh"
 
 namespace mtt {
 namespace {
@@ -74,7 +75,6 @@ constexpr int kLdSrc = kEmbed + 8;   // 776
 constexpr int kLdQkv = 3 * kTD + 8;  // 776
 constexpr int kLdHid = kTF + 8;      // 1032
 constexpr int kTmemCols = 512;
-constexpr int kVocabChunks = kVocab / 8;  // 253 chunks of 8 keys per session
 
 static_assert(kVocab % 8 == 0, "vocab chunks");
 static_assert(kTHeads * kHeadDim == kTD, "heads");
@@ -298,25 +298,6 @@ __device__ __forceinline__ void gemm_k(TileSmem& sm, int& it, const bf16* A, int
   }
 }
 
-__device__ __forceinline__ void unpack8(const uint4& u, float (&f)[8]) {
-  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const float2 t = __bfloat1622float2(h[j]);
-    f[2 * j] = t.x;
-    f[2 * j + 1] = t.y;
-  }
-}
-
-__device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
-  uint4 u;
-  u.x = pack_bf16x2(f[0], f[1]);
-  u.y = pack_bf16x2(f[2], f[3]);
-  u.z = pack_bf16x2(f[4], f[5]);
-  u.w = pack_bf16x2(f[6], f[7]);
-  return u;
-}
-
 // LayerNorm (no bias, eps 1e-5) of the 16 rows of x into xa with this lane's
 // 8 weights g (columns 8 lane ..); warp w: rows 2w, 2w+1.
 __device__ __forceinline__ void layer_norm_rows(const bf16* x, bf16* xa, const float (&g)[8]) {
@@ -345,22 +326,10 @@ __device__ __forceinline__ void layer_norm_rows(const bf16* x, bf16* xa, const f
   }
 }
 
-// GELU, tanh form: tanh(u) = 1 - 2 / (exp(2u) + 1), with the fast exponential
-// (error ~1e-6 relative before the result is rounded to bf16).
-__device__ __forceinline__ float gelu_tanh(float v) {
-  const float inner = 0.7978845608028654f * (v + 0.044715f * v * v * v);
-  const float t = 1.0f - __fdividef(2.0f, __expf(2.0f * inner) + 1.0f);
-  return 0.5f * v * (1.0f + t);
-}
-
 // ---------------------------------------------------------------------------
 // attention over the TMEM KV cache: warp w, head h = w % 4, part = w / 4
 // (positions j = part, part + 2, ..); thread t: row t / 2, dims [32 (t % 2), +32)
 // ---------------------------------------------------------------------------
-
-// TMEM column block of position j: even positions in blocks 0..7, odd in 8..15,
-// so each part's positions are contiguous (four per 64-column load).
-__device__ __forceinline__ int tmem_block(int j) { return 8 * (j & 1) + (j >> 1); }
 
 __device__ __forceinline__ void attention(TileSmem& sm, int p) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -480,273 +449,19 @@ __device__ __forceinline__ void attention(TileSmem& sm, int p) {
   }
 }
 
-// ---------------------------------------------------------------------------
-// sampling (same contract as sample_block in sampling.cuh)
-// ---------------------------------------------------------------------------
-
-constexpr uint32_t kKeyNegInf = 0x007fu;  // order key of bf16 -inf
-
-// Order key of a bf16 bit pattern with -0 folded onto +0 (key order == float order).
-__device__ __forceinline__ uint32_t sample_key(uint32_t b) {
-  b = (b == 0x8000u) ? 0u : b;
-  return (b & 0x8000u) ? (~b & 0xffffu) : (b | 0x8000u);
-}
-
-// Constrained value of token t (bf16 bits): non-finite -> -inf (and flagged),
-// forbidden specials / gated EOS -> -inf, finished -> EOS 0, others -inf.
-__device__ __forceinline__ uint32_t constrain(uint32_t b, int t, bool unfinished, bool finished, bool forbid,
-                                              bool& nonfinite) {
-  if ((b & 0x7f80u) == 0x7f80u) {
-    nonfinite = true;
-    b = 0xff80u;
-  }
-  if (t >= kCodebook && (t != kEosId || unfinished || forbid)) b = 0xff80u;
-  if (finished) b = (t == kEosId) ? 0u : 0xff80u;
-  return b;
-}
-
-constexpr int kListCap = 512;  // candidate list per session (u16 tokens), in the xa buffer
-constexpr int kListStride = (kTRows * kLdX) / kTSess;  // 528 u16 per session slot
+constexpr int kListStride = (kTRows * kLdX) / kTSess;  // 528 u16 per session slot in xa
 static_assert(kListStride >= kListCap, "candidate list");
 
-struct Best {
-  float score;
-  int id;
-};
-
-__device__ __forceinline__ void keep_best(Best& b, float sc, int t) {
-  if (sc > b.score || (sc == b.score && t < b.id)) {
-    b.score = sc;
-    b.id = t;
-  }
-}
-
-__device__ __forceinline__ Best warp_best(Best b) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    const float os = __shfl_xor_sync(0xffffffffu, b.score, o);
-    const int oi = __shfl_xor_sync(0xffffffffu, b.id, o);
-    keep_best(b, os, oi);
-  }
-  return b;
-}
-
-// Philox-Gumbel scores of the tokens list[0, total), four independent chains per lane.
-__device__ __forceinline__ void score_list(const uint16_t* list, uint32_t total, const uint16_t* vals, uint32_t seed32,
-                                           uint64_t off64, float temperature, Best& b) {
-  const int lane = threadIdx.x & 31;
-  for (uint32_t base = 0; base < total; base += 128) {
-    int t[4];
-    float u[4];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const uint32_t e = base + lane + 32 * j;
-      t[j] = e < total ? list[e] : -1;
-      u[j] = philox_uniform(seed32, off64 + static_cast<uint64_t>(t[j] < 0 ? 0 : t[j]));
-    }
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      if (t[j] >= 0) keep_best(b, __fadd_rn(__fdiv_rn(bits2f(vals[t[j]]), temperature), clamped_gumbel(u[j])), t[j]);
-    }
-  }
-}
-
-__device__ __forceinline__ __nv_bfloat162 bf2_of(uint32_t w) { return *reinterpret_cast<const __nv_bfloat162*>(&w); }
-
-// bf16 value of an order key (the smallest key is -inf).
-__device__ __forceinline__ __nv_bfloat16 key_value(uint32_t key) {
-  return __ushort_as_bfloat16(static_cast<unsigned short>(key_bf16(key < kKeyNegInf ? kKeyNegInf : key)));
-}
-
-// Number of values >= v in a session's row (warp total): bf16x2 compares
-// (-0 == +0, as in the float comparison the contract uses) summed in bf16x2.
-__device__ __forceinline__ uint32_t count_ge(const uint16_t* vals, __nv_bfloat16 v) {
-  const int lane = threadIdx.x & 31;
-  const __nv_bfloat162 t2 = __bfloat162bfloat162(v);
-  __nv_bfloat162 acc = __float2bfloat162_rn(0.f);
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const int ch = lane + 32 * i;
-    if (ch < kVocabChunks) {
-      const uint4 q = *reinterpret_cast<const uint4*>(vals + 8 * ch);
-      acc = __hadd2(acc, __hge2(bf2_of(q.x), t2));
-      acc = __hadd2(acc, __hge2(bf2_of(q.y), t2));
-      acc = __hadd2(acc, __hge2(bf2_of(q.z), t2));
-      acc = __hadd2(acc, __hge2(bf2_of(q.w), t2));
-    }
-  }
-  const float2 f = __bfloat1622float2(acc);
-  return __reduce_add_sync(0xffffffffu, static_cast<uint32_t>(f.x + f.y));
-}
-
-// The calling warp samples session `slot` at the current position from the
-// constrained bf16 values and the per-session maximum the head epilogue left.
-// Top-k threshold (the k-th largest value, ties included), without atomics:
-// one bf16x2 counting pass finds the smallest window of 32/64/128/256 key
-// steps below the maximum that holds k values; the window's tokens form a
-// candidate list whose distances below the maximum sit in registers, and a
-// binary search over them gives the exact k-th largest.  Only eligible
-// candidates are scored.  Rows whose window cannot be used (flat or very
-// spread rows) take an exact binary search over the whole row instead.
-__device__ int sample_slot(TileSmem& sm, const Frame& f, int slot, uint16_t* list, int* invalid_out) {
-  const int lane = threadIdx.x & 31;
-  const uint32_t fl = sm.flags[slot];
-  const bool unfinished = fl & 1u, finished = fl & 2u, forbid = fl & 4u;
-  const int64_t seed = sm.seed[slot];
-  const int64_t counter = sm.ctr[slot];
-  const SamplingParams& prm = f.prm;
-  const bool nonfinite = sm.nonfinite[slot] != 0;
-  const uint32_t top = sm.amax[slot];
-  const uint32_t M = top >> 16;
-  if (prm.argmax) {
-    *invalid_out = (nonfinite || M == kKeyNegInf) ? 1 : 0;
-    return M == kKeyNegInf ? 0 : static_cast<int>(0xffffu - (top & 0xffffu));
-  }
-  int invalid = (nonfinite || (unfinished && finished) || (finished && forbid)) ? 1 : 0;
-  const bool seed_valid = seed >= 0 && static_cast<uint64_t>(seed) < (1ull << 32);
-  const bool counter_valid = counter >= 0 && counter <= kMaxCounter;
-  if (!seed_valid || !counter_valid) invalid = 1;
-  if (finished) {  // only EOS (value 0) is finite: it is the only eligible token
-    *invalid_out = invalid;
-    return kEosId;
-  }
-  if (M == kKeyNegInf) {  // nothing finite
-    *invalid_out = 1;
-    return 0;
-  }
-  const uint32_t seed32 = seed_valid ? static_cast<uint32_t>(seed) : 0u;
-  const uint64_t off64 = counter_valid ? static_cast<uint64_t>(counter) * kPhiloxStride : 0ull;
-  const uint16_t* vals = sm.u.val + slot * kVocab;
-  const uint32_t kk = static_cast<uint32_t>(prm.top_k);
-
-  // ---- pass 1: values within 32 / 64 / 128 / 256 key steps below the maximum
-  __nv_bfloat162 lim[4];
-#pragma unroll
-  for (int j = 0; j < 4; ++j) lim[j] = __bfloat162bfloat162(key_value(M + 1 < (32u << j) ? 0u : M + 1 - (32u << j)));
-  __nv_bfloat162 acc[4];
-#pragma unroll
-  for (int j = 0; j < 4; ++j) acc[j] = __float2bfloat162_rn(0.f);
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const int ch = lane + 32 * i;
-    if (ch < kVocabChunks) {
-      const uint4 q = *reinterpret_cast<const uint4*>(vals + 8 * ch);
-      const uint32_t w[4] = {q.x, q.y, q.z, q.w};
-#pragma unroll
-      for (int e = 0; e < 4; ++e)
-#pragma unroll
-        for (int j = 0; j < 4; ++j) acc[j] = __hadd2(acc[j], __hge2(bf2_of(w[e]), lim[j]));
-    }
-  }
-  uint32_t mine4[4], tot[4];
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const float2 f2 = __bfloat1622float2(acc[j]);
-    mine4[j] = static_cast<uint32_t>(f2.x + f2.y);
-    tot[j] = __reduce_add_sync(0xffffffffu, mine4[j]);
-  }
-  int win = 4;
-#pragma unroll
-  for (int j = 3; j >= 0; --j) win = tot[j] >= kk ? j : win;
-
-  Best best{-CUDART_INF_F, kVocab};
-  if (win < 4 && tot[win] <= static_cast<uint32_t>(kListCap)) {
-    const __nv_bfloat162 limw = win == 0 ? lim[0] : (win == 1 ? lim[1] : (win == 2 ? lim[2] : lim[3]));
-    const uint32_t mine = win == 0 ? mine4[0] : (win == 1 ? mine4[1] : (win == 2 ? mine4[2] : mine4[3]));
-    const uint32_t n_cand = tot[win];
-    uint32_t pos = mine;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const uint32_t y = __shfl_up_sync(0xffffffffu, pos, o);
-      if (lane >= o) pos += y;
-    }
-    pos -= mine;
-    // ---- pass 2: the window's tokens
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const int ch = lane + 32 * i;
-      if (ch < kVocabChunks) {
-        const uint4 q = *reinterpret_cast<const uint4*>(vals + 8 * ch);
-        const uint32_t w[4] = {q.x, q.y, q.z, q.w};
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const uint32_t m = __hge2_mask(bf2_of(w[e]), limw);
-          if (m & 0xffffu) list[pos++] = static_cast<uint16_t>(8 * ch + 2 * e);
-          if (m >> 16) list[pos++] = static_cast<uint16_t>(8 * ch + 2 * e + 1);
-        }
-      }
-    }
-    __syncwarp();
-    // ---- candidates' distances below the maximum, 16 per lane in registers
-    uint32_t dist[kListCap / 32];
-    uint16_t tokn[kListCap / 32];
-#pragma unroll
-    for (int m = 0; m < kListCap / 32; ++m) {
-      const uint32_t e = lane + 32 * m;
-      const int t = e < n_cand ? list[e] : 0;
-      tokn[m] = static_cast<uint16_t>(t);
-      dist[m] = e < n_cand ? M - sample_key(vals[t]) : 0xffffu;
-    }
-    // smallest d with count(dist <= d) >= k
-    int lo = -1, hi = static_cast<int>((32u << win) - 1);
-    while (hi - lo > 1) {
-      const int mid = (lo + hi) >> 1;
-      uint32_t cnt = 0;
-#pragma unroll
-      for (int m = 0; m < kListCap / 32; ++m) cnt += dist[m] <= static_cast<uint32_t>(mid);
-      if (__reduce_add_sync(0xffffffffu, cnt) >= kk) {
-        hi = mid;
-      } else {
-        lo = mid;
-      }
-    }
-    const uint32_t dstar = static_cast<uint32_t>(hi);
-    // ---- eligible candidates (distance <= d*, finite), compacted into the histogram area
-    uint16_t* elig = reinterpret_cast<uint16_t*>(sm.hist[slot]);
-    uint32_t n_elig = 0;
-#pragma unroll
-    for (int m = 0; m < kListCap / 32; ++m) {
-      const bool ok = dist[m] <= dstar && M - dist[m] != kKeyNegInf;
-      const unsigned b = __ballot_sync(0xffffffffu, ok);
-      if (ok) elig[n_elig + __popc(b & ((1u << lane) - 1u))] = tokn[m];
-      n_elig += __popc(b);
-    }
-    __syncwarp();
-    score_list(elig, n_elig, vals, seed32, off64, prm.temperature, best);
-  } else {
-    // exact binary search over keys: count(value >= lo) >= k > count(value >= hi)
-    uint32_t lo = kKeyNegInf, hi = M + 1;
-    while (hi - lo > 1) {
-      const uint32_t mid = (lo + hi) >> 1;
-      if (count_ge(vals, key_value(mid)) >= kk) {
-        lo = mid;
-      } else {
-        hi = mid;
-      }
-    }
-#pragma unroll 1
-    for (int i = 0; i < 8; ++i) {
-      const int ch = lane + 32 * i;
-      if (ch < kVocabChunks) {
-        for (int e = 0; e < 8; ++e) {
-          const int t = 8 * ch + e;
-          const uint32_t key = sample_key(vals[t]);
-          if (key >= lo && key != kKeyNegInf) {
-            const float g = clamped_gumbel(philox_uniform(seed32, off64 + static_cast<uint64_t>(t)));
-            keep_best(best, __fadd_rn(__fdiv_rn(bits2f(vals[t]), prm.temperature), g), t);
-          }
-        }
-      }
-    }
-  }
-  best = warp_best(best);
-  int token = best.id;
-  if (token >= kVocab || best.score == -CUDART_INF_F) {
-    invalid = 1;
-    token = 0;
-  }
-  *invalid_out = invalid;
-  return token;
+__device__ __forceinline__ int sample_slot(TileSmem& sm, const Frame& f, int slot, int* invalid_out) {
+  RowSample rs;
+  rs.vals = sm.u.val + slot * kVocab;
+  rs.top = sm.amax[slot];
+  rs.flags = sm.flags[slot];
+  rs.nonfinite = sm.nonfinite[slot] != 0;
+  rs.seed = sm.seed[slot];
+  rs.counter = sm.ctr[slot];
+  return sample_row(rs, f.prm, reinterpret_cast<uint16_t*>(sm.xa) + slot * kListStride,
+                    reinterpret_cast<uint16_t*>(sm.hist[slot]), invalid_out);
 }
 
 // ---------------------------------------------------------------------------
@@ -1013,8 +728,7 @@ __global__ void __launch_bounds__(kTThreads, 1) tile_frame_kernel(Frame f, const
       if (warp < n_sess) {
         const int slot = warp;
         int invalid = 0;
-        const int token =
-            sample_slot(sm, f, slot, reinterpret_cast<uint16_t*>(sm.xa) + slot * kListStride, &invalid);
+        const int token = sample_slot(sm, f, slot, &invalid);
         const int64_t counter = sm.ctr[slot];
         __syncwarp();
         if (lane == 0) {

@@ -192,7 +192,7 @@ class LocalArEngine:
     @property
     def path(self) -> int:
         """Frame path for a full batch of ``max_streams`` on the current device
-        (1 phase kernels, 2 fused cluster kernel, 3 tile kernel)."""
+        (1 phase kernels, 2 fused cluster kernel, 3 tile kernel, 4 pair kernel)."""
         return self.path_for(self.max_streams)
 
     def path_for(self, n_streams: int) -> int:

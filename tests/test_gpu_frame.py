@@ -25,8 +25,8 @@ from oracle import sampler as S
 pytestmark = pytest.mark.gpu
 
 RTOL = 1e-2
-PATH_AUTO, PHASE, FUSED, TILE = 0, 1, 2, 3
-BOTH = [PHASE, FUSED, TILE]
+PATH_AUTO, PHASE, FUSED, TILE, PAIR = 0, 1, 2, 3, 4
+BOTH = [PHASE, FUSED, TILE, PAIR]
 
 
 def bits(t):
@@ -163,10 +163,11 @@ FLAGS6 = ([0, 1, 0, 0, 0, 1], [0, 0, 0, 1, 0, 1], [0, 0, 1, 0, 0, 0])  # incl. a
 @pytest.mark.parametrize("shape,n,path,fold", [
     (SHAPE_BASELINE, 6, PHASE, True), (SHAPE_BASELINE, 6, FUSED, True), (SHAPE_BASELINE, 11, FUSED, True),
     (SHAPE_BASELINE, 6, TILE, True), (SHAPE_BASELINE, 11, TILE, True), (SHAPE_BASELINE, 11, TILE, False),
-    (SHAPE_BASELINE, 11, FUSED, False), (SHAPE_SOFIA, 3, PHASE, True)])
+    (SHAPE_BASELINE, 11, FUSED, False), (SHAPE_BASELINE, 6, PAIR, True), (SHAPE_BASELINE, 11, PAIR, True),
+    (SHAPE_BASELINE, 20, PAIR, True), (SHAPE_BASELINE, 11, PAIR, False), (SHAPE_SOFIA, 3, PHASE, True)])
 def test_frame_matches_oracle(engines, shape, n, path, fold):
     w = weights(shape, 21)
-    eng = engines(shape, 21, 16, path=path, fold=fold)
+    eng = engines(shape, 21, 24, path=path, fold=fold)
     assert eng.path == path
     hidden = _hidden(n, 5)
     flags = tuple(np.resize(np.asarray(f), n) for f in FLAGS6)
@@ -177,11 +178,12 @@ def test_frame_matches_oracle(engines, shape, n, path, fold):
 
 
 def test_auto_path_for_the_benchmark_shape(engines):
-    """Few tiles: the cluster kernel (latency); more tiles than concurrent
+    """Few tiles: the cluster kernel (latency); more than two waves of
     clusters: the tile kernel (throughput); other shapes: phase kernels."""
     eng = engines(SHAPE_BASELINE, 21, 16)
     assert eng.path == FUSED
     assert eng.path_for(1) == FUSED
+    assert eng.path_for(112) == FUSED
     assert eng.path_for(1024) == TILE
     assert engines(SHAPE_SOFIA, 21, 1, with_final=False).path == PHASE
 
@@ -242,7 +244,8 @@ def test_argmax_without_cfg(engines, path):
     np.testing.assert_array_equal(gpu["counter"], counter)
 
 
-@pytest.mark.parametrize("name,path", [("A_bf16_cfg", PATH_AUTO), ("A_bf16_cfg", TILE), ("R_bf16_cfg", PATH_AUTO)])
+@pytest.mark.parametrize("name,path", [("A_bf16_cfg", PATH_AUTO), ("A_bf16_cfg", TILE), ("A_bf16_cfg", PAIR),
+                                       ("R_bf16_cfg", PATH_AUTO)])
 def test_frame_against_reference_golden(engines, golden, golden_dir, name, path):
     """Teacher-forced on the reference's tokens, the GPU logits match the NeMo
     oracle's recorded logits within tolerance."""
@@ -300,7 +303,7 @@ def test_gpu_no_further_from_exact_than_oracle(engines):
     assert gpu_err.max() <= 2.0 * cpu_err.max() + 1e-4, (gpu_err.max(), cpu_err.max())
 
 
-@pytest.mark.parametrize("path", [FUSED, TILE])
+@pytest.mark.parametrize("path", [FUSED, TILE, PAIR])
 @pytest.mark.parametrize("kind", ["flat", "sharp", "ties"])
 def test_sampler_row_shapes(path, kind):
     """Logit rows that drive each top-k select path: flat rows (every token
