@@ -18,8 +18,8 @@
 //   own output features = CTA 0's partial + CTA 1's partial, + residual;
 //                                                             exchange R4
 //   head p vocabulary [1012c, +1012) for all 16 sessions (bias, CFG, the
-//     constraints, the row maximum): sessions 8c..8c+7 stay, the other eight
-//     sessions' values and maxima go to the peer;             exchange R5
+//     constraints): sessions 8c..8c+7 stay, the other eight sessions' values
+//     and non-finite flags go to the peer;                    exchange R5
 //   one warp per session samples sessions 8c..8c+7 and sends the peer the
 //     token and the session's next input rows.                exchange R6
 //
@@ -107,12 +107,9 @@ struct __align__(1024) PairSmem {
   int64_t ctr[kPOwn];
   int64_t seed[kPOwn];
   int32_t inv[kPOwn];
-  uint32_t top[kPOwn];          // row maxima of this CTA's half (own sessions)
-  uint32_t nonfinite[kPOwn];
-  uint32_t stage_top[kPOwn];    // row maxima of this CTA's half (the peer's sessions), before sending
-  uint32_t stage_nonfinite[kPOwn];
-  uint32_t peer_top[kPOwn];     // sent by the peer
-  uint32_t peer_nonfinite[kPOwn];
+  uint32_t nonfinite[kPOwn];        // this CTA's half, own sessions
+  uint32_t stage_nonfinite[kPOwn];  // this CTA's half, the peer's sessions, before sending
+  uint32_t peer_nonfinite[kPOwn];   // the peer's half, own sessions (sent by the peer)
   int32_t last_issued[kPSlots];
   int32_t n_sess;
   int32_t err;
@@ -626,9 +623,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
           *reinterpret_cast<uint2*>(sm.hb + 4 * threadIdx.x) = *reinterpret_cast<const uint2*>(hb + 4 * threadIdx.x);
         }
         if (threadIdx.x < kPOwn) {
-          sm.top[threadIdx.x] = 0;
           sm.nonfinite[threadIdx.x] = 0;
-          sm.stage_top[threadIdx.x] = 0;
           sm.stage_nonfinite[threadIdx.x] = 0;
         }
       }
@@ -757,84 +752,54 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
         uint32_t a[2][16][4];
         load_a2(a, sm.x, kLdX);
         bool nf_a = false, nf_b = false;
-        uint32_t mx_a = 0, mx_b = 0;
         const uint32_t rb = peer_bar(sm, rd, peer);
         const uint32_t fa = sm.flags[sa], fb = sm.flags[sb];
         const bool live_a = sa < n_sess, live_b = sb < n_sess;
-        const int sid_a = live_a ? sm.sess[sa] : 0, sid_b = live_b ? sm.sess[sb] : 0;
+        const bool cfg = rp == 2;
+        const float cfg_scale = f.prm.cfg_scale, uncond_scale = __fsub_rn(1.0f, f.prm.cfg_scale);
+        bf16* lo_a = (f.logits_out && live_a)
+                         ? f.logits_out + (static_cast<int64_t>(sm.sess[sa]) * kPositions + p) * rp * kVocab : nullptr;
+        bf16* lo_b = (f.logits_out && live_b)
+                         ? f.logits_out + (static_cast<int64_t>(sm.sess[sb]) * kPositions + p) * rp * kVocab : nullptr;
+        uint16_t* dst_row = sm.u.val + (lane >> 2) * kVocab;  // the slot's row in its sampling CTA
         gemm_n2(sm, it, a, 16, [&](int nb, const float (&acc)[2][4]) {
           const int j = kCRows * nb + 8 * warp + 2 * (lane & 3);
           if (j < kHalf) {
             const int n = kHalf * c + j;
-            const float b0 = bf2f(sm.hb[j]), b1 = bf2f(sm.hb[j + 1]);
+            const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(sm.hb + j));
 #pragma unroll
             for (int hh = 0; hh < 2; ++hh) {  // hh 0: slot sa (acc[.][0..1]), hh 1: slot sb (acc[.][2..3])
-              const bool lv = hh ? live_b : live_a;
-              if (!lv) continue;
-              const uint32_t fl = hh ? fb : fa;
-              const bf16 c0 = f2bf(__fadd_rn(acc[0][2 * hh], b0)), c1 = f2bf(__fadd_rn(acc[0][2 * hh + 1], b1));
-              const bf16 u0 = f2bf(__fadd_rn(acc[1][2 * hh], b0)), u1 = f2bf(__fadd_rn(acc[1][2 * hh + 1], b1));
-              if (f.logits_out) {
-                bf16* lo = f.logits_out + (static_cast<int64_t>(hh ? sid_b : sid_a) * kPositions + p) * rp * kVocab + n;
-                lo[0] = c0;
-                lo[1] = c1;
-                if (rp == 2) {
-                  lo[kVocab] = u0;
-                  lo[kVocab + 1] = u1;
-                }
+              if (!(hh ? live_b : live_a)) continue;
+              const uint32_t c2 = pack2_rn(__fadd_rn(acc[0][2 * hh], b.x), __fadd_rn(acc[0][2 * hh + 1], b.y));
+              const uint32_t u2 = pack2_rn(__fadd_rn(acc[1][2 * hh], b.x), __fadd_rn(acc[1][2 * hh + 1], b.y));
+              bf16* lo = hh ? lo_b : lo_a;
+              if (lo) {
+                *reinterpret_cast<uint32_t*>(lo + n) = c2;
+                if (cfg) *reinterpret_cast<uint32_t*>(lo + kVocab + n) = u2;
               }
-              float v0 = bf2f(c0), v1 = bf2f(c1);
-              if (rp == 2) {
-                v0 = guided_logit(v0, bf2f(u0), f.prm.cfg_scale);
-                v1 = guided_logit(v1, bf2f(u1), f.prm.cfg_scale);
-              }
-              bool& nf = hh ? nf_b : nf_a;
-              const uint32_t e0 = constrain(__bfloat16_as_ushort(f2bf(v0)), n, fl & 1u, fl & 2u, fl & 4u, nf);
-              const uint32_t e1 = constrain(__bfloat16_as_ushort(f2bf(v1)), n + 1, fl & 1u, fl & 2u, fl & 4u, nf);
-              const uint32_t k0 = (sample_key(e0) << 16) | (0xffffu - static_cast<uint32_t>(n));
-              const uint32_t k1 = (sample_key(e1) << 16) | (0xffffu - static_cast<uint32_t>(n + 1));
-              uint32_t& mx = hh ? mx_b : mx_a;
-              mx = k0 > mx ? k0 : mx;
-              mx = k1 > mx ? k1 : mx;
-              uint16_t* dst = sm.u.val + (lane >> 2) * kVocab + n;  // local index of the slot in its sampler CTA
-              const uint32_t pairv = e0 | (e1 << 16);
+              const uint32_t g = cfg ? guided_value2(c2, u2, cfg_scale, uncond_scale) : c2;
+              const uint32_t v = constrain2(g, n, hh ? fb : fa, hh ? nf_b : nf_a);
               if ((hh == 0) == own_is_a) {
-                *reinterpret_cast<uint32_t*>(dst) = pairv;
+                *reinterpret_cast<uint32_t*>(dst_row + n) = v;
               } else {
-                push_b32(dst, peer, pairv, rb);
+                push_b32(dst_row + n, peer, v, rb);
               }
             }
           }
         });
-        mx_a = max(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, 1));
-        mx_a = max(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, 2));
-        mx_b = max(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, 1));
-        mx_b = max(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, 2));
+        // the non-finite flags: slot a's to this CTA (own_is_a) or the peer, slot b's the other way round
         const int ls = lane >> 2;
-        // slot a's maximum is this CTA's (own_is_a) or the peer's; slot b the other way round
-        uint32_t* top_a = own_is_a ? &sm.top[ls] : &sm.stage_top[ls];
-        uint32_t* top_b = own_is_a ? &sm.stage_top[ls] : &sm.top[ls];
-        uint32_t* nf_dst_a = own_is_a ? &sm.nonfinite[ls] : &sm.stage_nonfinite[ls];
-        uint32_t* nf_dst_b = own_is_a ? &sm.stage_nonfinite[ls] : &sm.nonfinite[ls];
-        if ((lane & 3) == 0) {
-          if (live_a) atomicMax(top_a, mx_a);
-          if (live_b) atomicMax(top_b, mx_b);
-        }
-        if (nf_a) atomicOr(nf_dst_a, 1u);
-        if (nf_b) atomicOr(nf_dst_b, 1u);
+        if (nf_a) atomicOr(own_is_a ? &sm.nonfinite[ls] : &sm.stage_nonfinite[ls], 1u);
+        if (nf_b) atomicOr(own_is_a ? &sm.stage_nonfinite[ls] : &sm.nonfinite[ls], 1u);
         cbar();
-        if (threadIdx.x < kPOwn) {  // the peer's sessions' maxima of this half
-          push_b32(&sm.peer_top[threadIdx.x], peer, sm.stage_top[threadIdx.x], rb);
-          push_b32(&sm.peer_nonfinite[threadIdx.x], peer, sm.stage_nonfinite[threadIdx.x], rb);
-        }
+        if (threadIdx.x < kPOwn) push_b32(&sm.peer_nonfinite[threadIdx.x], peer, sm.stage_nonfinite[threadIdx.x], rb);
       }
-      finish_round(sm, rd, peer, n_peer * kHalf * 2 + kPOwn * 8);  // R5
+      finish_round(sm, rd, peer, n_peer * kHalf * 2 + kPOwn * 4);  // R5
       // ---------------- sampling of sessions 8c..8c+7; tokens and next input rows to both CTAs
       if (warp < n_own) {
         const int ls = warp, slot = own0 + warp;
         RowSample rs;
         rs.vals = sm.u.val + ls * kVocab;
-        rs.top = max(sm.top[ls], sm.peer_top[ls]);
         rs.flags = sm.flags[slot];
         rs.nonfinite = (sm.nonfinite[ls] | sm.peer_nonfinite[ls]) != 0;
         rs.seed = sm.seed[ls];

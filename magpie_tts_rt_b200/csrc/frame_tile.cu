@@ -118,7 +118,6 @@ struct __align__(1024) TileSmem {
   int64_t seed[kTSess];
   uint32_t flags[kTSess];  // bit 0 unfinished, bit 1 finished, bit 2 forbid_eos
   int32_t inv[kTSess];
-  uint32_t amax[kTSess];  // max of key << 16 | (0xffff - token): maximum key, left-most
   uint32_t nonfinite[kTSess];
   int32_t last_issued[kSlots];
   int32_t n_sess;
@@ -455,7 +454,6 @@ static_assert(kListStride >= kListCap, "candidate list");
 __device__ __forceinline__ int sample_slot(TileSmem& sm, const Frame& f, int slot, int* invalid_out) {
   RowSample rs;
   rs.vals = sm.u.val + slot * kVocab;
-  rs.top = sm.amax[slot];
   rs.flags = sm.flags[slot];
   rs.nonfinite = sm.nonfinite[slot] != 0;
   rs.seed = sm.seed[slot];
@@ -553,20 +551,13 @@ __global__ void __launch_bounds__(kTThreads, 1) tile_frame_kernel(Frame f, const
   }
   asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kConsumerRegs));
   {
-    // per-thread constants: LN weights of columns [8 lane, +8); flags of the
-    // session whose rows this thread holds in mma.sync fragments (slot lane / 4)
+    // per-thread constants: LN weights of columns [8 lane, +8); the session
+    // whose rows this thread holds in mma.sync fragments (slot lane / 4)
     float g1[8], g2[8];
     unpack8(*reinterpret_cast<const uint4*>(f.ln1 + lane * 8), g1);
     unpack8(*reinterpret_cast<const uint4*>(f.ln2 + lane * 8), g2);
     const int my_slot = lane >> 2;
     const bool my_live = my_slot < n_sess;
-    bool my_unf = false, my_fin = false, my_forbid = false;
-    if (my_live) {
-      const int sid = sm.sess[my_slot];
-      my_unf = f.unfinished[sid];
-      my_fin = f.finished[sid];
-      my_forbid = f.forbid[sid];
-    }
     int it = 0;
     for (int p = 0; p < kPositions; ++p) {
       // ---------------- input rows (folded p >= 1: written by the sampling warps)
@@ -607,10 +598,7 @@ __global__ void __launch_bounds__(kTThreads, 1) tile_frame_kernel(Frame f, const
         if (threadIdx.x < kVocabChunks) {
           *reinterpret_cast<uint4*>(sm.hb + 8 * threadIdx.x) = *reinterpret_cast<const uint4*>(hb + 8 * threadIdx.x);
         }
-        if (threadIdx.x < kTSess) {
-          sm.amax[threadIdx.x] = 0;
-          sm.nonfinite[threadIdx.x] = 0;
-        }
+        if (threadIdx.x < kTSess) sm.nonfinite[threadIdx.x] = 0;
       }
       cbar();
 
@@ -678,47 +666,32 @@ __global__ void __launch_bounds__(kTThreads, 1) tile_frame_kernel(Frame f, const
       });
       cbar();
 
-      // ---------------- head p: bias, CFG combine, constraints, order keys and
-      // the first radix digit (top-k) or the running left-most maximum (argmax)
+      // ---------------- head p: bias, CFG combine and constraints in the epilogue
       {
         uint32_t a[16][4];
         load_a(a, sm.x, kLdX);
         bool nf = false;
-        uint32_t amax = 0;
         uint16_t* vals = sm.u.val + my_slot * kVocab;
+        const bool cfg = rp == 2;
+        const float cfg_scale = f.prm.cfg_scale, uncond_scale = __fsub_rn(1.0f, f.prm.cfg_scale);
+        const uint32_t my_flags = my_live ? sm.flags[my_slot] : 0u;
+        bf16* lo_row = (f.logits_out && my_live)
+                           ? f.logits_out + (static_cast<int64_t>(sm.sess[my_slot]) * kPositions + p) * rp * kVocab
+                           : nullptr;
         gemm_n(sm, it, a, 32, [&](int nb, const float (&acc)[4]) {
           const int n = kCRows * nb + 8 * warp + 2 * (lane & 3);
           if (n < kVocab && my_live) {  // n is even and kVocab is even: the pair stays inside
-            const float b0 = bf2f(sm.hb[n]), b1 = bf2f(sm.hb[n + 1]);
-            const bf16 c0 = f2bf(__fadd_rn(acc[0], b0)), c1 = f2bf(__fadd_rn(acc[1], b1));
-            const bf16 u0 = f2bf(__fadd_rn(acc[2], b0)), u1 = f2bf(__fadd_rn(acc[3], b1));
-            if (f.logits_out) {
-              bf16* lo = f.logits_out + (static_cast<int64_t>(sm.sess[my_slot]) * kPositions + p) * rp * kVocab + n;
-              lo[0] = c0;
-              lo[1] = c1;
-              if (rp == 2) {
-                lo[kVocab] = u0;
-                lo[kVocab + 1] = u1;
-              }
+            const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(sm.hb + n));
+            const uint32_t c2 = pack2_rn(__fadd_rn(acc[0], b.x), __fadd_rn(acc[1], b.y));
+            const uint32_t u2 = pack2_rn(__fadd_rn(acc[2], b.x), __fadd_rn(acc[3], b.y));
+            if (lo_row) {
+              *reinterpret_cast<uint32_t*>(lo_row + n) = c2;
+              if (cfg) *reinterpret_cast<uint32_t*>(lo_row + kVocab + n) = u2;
             }
-            float v0 = bf2f(c0), v1 = bf2f(c1);
-            if (rp == 2) {
-              v0 = guided_logit(v0, bf2f(u0), f.prm.cfg_scale);
-              v1 = guided_logit(v1, bf2f(u1), f.prm.cfg_scale);
-            }
-            const uint32_t b0c = constrain(__bfloat16_as_ushort(f2bf(v0)), n, my_unf, my_fin, my_forbid, nf);
-            const uint32_t b1c = constrain(__bfloat16_as_ushort(f2bf(v1)), n + 1, my_unf, my_fin, my_forbid, nf);
-            *reinterpret_cast<uint32_t*>(vals + n) = b0c | (b1c << 16);
-            const uint32_t k0 = sample_key(b0c), k1 = sample_key(b1c);
-            const uint32_t e0 = (k0 << 16) | (0xffffu - static_cast<uint32_t>(n));
-            const uint32_t e1 = (k1 << 16) | (0xffffu - static_cast<uint32_t>(n + 1));
-            amax = e0 > amax ? e0 : amax;
-            amax = e1 > amax ? e1 : amax;
+            const uint32_t g = cfg ? guided_value2(c2, u2, cfg_scale, uncond_scale) : c2;
+            *reinterpret_cast<uint32_t*>(vals + n) = constrain2(g, n, my_flags, nf);
           }
         });
-        amax = max(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
-        amax = max(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
-        if (my_live && (lane & 3) == 0) atomicMax(&sm.amax[my_slot], amax);
         if (nf) atomicOr(&sm.nonfinite[my_slot], 1u);
       }
       cbar();

@@ -13,6 +13,8 @@ namespace {
 
 constexpr int kVocabChunks = kVocab / 8;  // 253 chunks of 8 values per row
 
+__device__ __forceinline__ __nv_bfloat162 bf2_of(uint32_t w) { return *reinterpret_cast<const __nv_bfloat162*>(&w); }
+
 __device__ __forceinline__ void unpack8(const uint4& u, float (&f)[8]) {
   const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
 #pragma unroll
@@ -109,7 +111,6 @@ __device__ __forceinline__ void score_list(const uint16_t* list, uint32_t total,
   }
 }
 
-__device__ __forceinline__ __nv_bfloat162 bf2_of(uint32_t w) { return *reinterpret_cast<const __nv_bfloat162*>(&w); }
 
 // bf16 value of an order key (the smallest key is -inf).
 __device__ __forceinline__ __nv_bfloat16 key_value(uint32_t key) {
@@ -148,13 +149,77 @@ __device__ __forceinline__ uint32_t count_ge(const uint16_t* vals, __nv_bfloat16
 // candidates are scored.  Rows whose window cannot be used (flat or very
 // spread rows) take an exact binary search over the whole row instead.
 // One session row at one position, as left by a head epilogue.
+// bf16x2 guided logits of two adjacent tokens from the conditional and
+// unconditional bf16x2 logits: bf16(bf16(c * s) + u * (1 - s)) per half, with
+// the f32 add then the bf16 rounding (the plugin's two roundings).
+__device__ __forceinline__ uint32_t guided_value2(uint32_t c2, uint32_t u2, float cfg_scale, float uncond_scale) {
+  const float2 cf = __bfloat1622float2(bf2_of(c2));
+  const float2 uf = __bfloat1622float2(bf2_of(u2));
+  const float2 sc = __bfloat1622float2(__floats2bfloat162_rn(__fmul_rn(cf.x, cfg_scale), __fmul_rn(cf.y, cfg_scale)));
+  const __nv_bfloat162 g = __floats2bfloat162_rn(__fadd_rn(sc.x, __fmul_rn(uf.x, uncond_scale)),
+                                                 __fadd_rn(sc.y, __fmul_rn(uf.y, uncond_scale)));
+  return *reinterpret_cast<const uint32_t*>(&g);
+}
+
+// Constrained values of tokens n, n + 1 (bf16x2); the slow path only for
+// non-finite values, the special tokens and finished rows.
+__device__ __forceinline__ uint32_t constrain2(uint32_t g, int n, uint32_t fl, bool& nonfinite) {
+  const bool bad = ((g & 0x7f80u) == 0x7f80u) || ((g & 0x7f800000u) == 0x7f800000u);
+  if (bad || n + 1 >= kCodebook || (fl & 2u)) {
+    const bool u = fl & 1u, fin = fl & 2u, fb = fl & 4u;
+    g = constrain(g & 0xffffu, n, u, fin, fb, nonfinite) | (constrain(g >> 16, n + 1, u, fin, fb, nonfinite) << 16);
+  }
+  return g;
+}
+
+__device__ __forceinline__ uint32_t pack2_rn(float a, float b) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+
 struct RowSample {
   const uint16_t* vals;  // 2024 constrained values (bf16 bits)
-  uint32_t top;          // max of key << 16 | (0xffff - token) over the row
   uint32_t flags;        // bit 0 unfinished, bit 1 finished, bit 2 forbid_eos
   bool nonfinite;        // some guided logit of the row was NaN or infinite
   int64_t seed, counter;
 };
+
+// Order key of the row's maximum (bf16x2 max over the row, warp total).
+__device__ __forceinline__ uint32_t row_max_key(const uint16_t* vals) {
+  const int lane = threadIdx.x & 31;
+  __nv_bfloat162 m2 = __bfloat162bfloat162(__ushort_as_bfloat16(static_cast<unsigned short>(0xff80u)));
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int ch = lane + 32 * i;
+    if (ch < kVocabChunks) {
+      const uint4 q = *reinterpret_cast<const uint4*>(vals + 8 * ch);
+      m2 = __hmax2(m2, __hmax2(__hmax2(bf2_of(q.x), bf2_of(q.y)), __hmax2(bf2_of(q.z), bf2_of(q.w))));
+    }
+  }
+  const uint32_t w = *reinterpret_cast<const uint32_t*>(&m2);
+  const uint32_t k0 = sample_key(w & 0xffffu), k1 = sample_key(w >> 16);
+  return __reduce_max_sync(0xffffffffu, k0 > k1 ? k0 : k1);
+}
+
+// Left-most token whose key is M (warp total).
+__device__ __forceinline__ int row_first_key(const uint16_t* vals, uint32_t M) {
+  const int lane = threadIdx.x & 31;
+  int first = kVocab;
+#pragma unroll
+  for (int i = 7; i >= 0; --i) {
+    const int ch = lane + 32 * i;
+    if (ch < kVocabChunks) {
+      const uint4 q = *reinterpret_cast<const uint4*>(vals + 8 * ch);
+      const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+      for (int e = 3; e >= 0; --e) {
+        if (sample_key(w[e] >> 16) == M) first = 8 * ch + 2 * e + 1;
+        if (sample_key(w[e] & 0xffffu) == M) first = 8 * ch + 2 * e;
+      }
+    }
+  }
+  return static_cast<int>(__reduce_min_sync(0xffffffffu, static_cast<uint32_t>(first)));
+}
 
 __device__ int sample_row(const RowSample& rs, const SamplingParams& prm, uint16_t* list, uint16_t* elig,
                           int* invalid_out) {
@@ -163,11 +228,10 @@ __device__ int sample_row(const RowSample& rs, const SamplingParams& prm, uint16
   const int64_t seed = rs.seed;
   const int64_t counter = rs.counter;
   const bool nonfinite = rs.nonfinite;
-  const uint32_t top = rs.top;
-  const uint32_t M = top >> 16;
+  const uint32_t M = row_max_key(rs.vals);
   if (prm.argmax) {
     *invalid_out = (nonfinite || M == kKeyNegInf) ? 1 : 0;
-    return M == kKeyNegInf ? 0 : static_cast<int>(0xffffu - (top & 0xffffu));
+    return M == kKeyNegInf ? 0 : row_first_key(rs.vals, M);
   }
   int invalid = (nonfinite || (unfinished && finished) || (finished && forbid)) ? 1 : 0;
   const bool seed_valid = seed >= 0 && static_cast<uint64_t>(seed) < (1ull << 32);
