@@ -209,6 +209,23 @@ MTT_B200_API int mtt_b200_launch_finalize_local_step(
     int32_t* step_invalid_rows, int32_t* step_end_frame_index, const int64_t* updated_rng_counter,
     int64_t* rng_counter, bool* generation_finished, void* stream);
 
+/*
+ * Replace the kernels behind the MagpieLayerNorm, MagpieGeluTanh and
+ * MagpieSoftmax (mode 0) plugins: launch_layer_norm / launch_gelu_tanh /
+ * launch_softmax (plugins/local_ar_plugins.hpp:57-76,
+ * plugins/local_ar_plugins.cu:4218-4356).  bf16 in and out, stream-ordered,
+ * return 0, or -1 for a null pointer, a size out of range or a failed launch.
+ *   layer_norm: rows of width 768, 1 <= row_count <= 1024, no bias, eps 1e-5;
+ *   gelu_tanh:  1 <= element_count <= 3072 * 512;
+ *   softmax:    batch_count >= 1 rows of 1 <= element_count <= 512.
+ */
+MTT_B200_API int mtt_b200_launch_layer_norm(const void* input_bf16, const void* weight_bf16, void* output_bf16,
+                                            int32_t row_count, void* stream);
+MTT_B200_API int mtt_b200_launch_gelu_tanh(const void* input_bf16, void* output_bf16, size_t element_count,
+                                           void* stream);
+MTT_B200_API int mtt_b200_launch_softmax(const void* input_bf16, void* output_bf16, int32_t batch_count,
+                                         int32_t element_count, void* stream);
+
 /* ------------------------------------------------------------------------ */
 /* 3. Batched Local AR frame                                                 */
 /* ------------------------------------------------------------------------ */
@@ -415,6 +432,18 @@ namespace magpie_tts_rt::plugins {
   return mtt_b200_launch_local_ar_eos(decoder_hidden_bf16, codec_tokens, unfinished, finished, forbid_eos,
                                       final_weight_bf16, final_bias_bf16, workspace, end_frame_index,
                                       static_cast<void*>(stream));
+}
+[[nodiscard]] inline int launch_layer_norm(const void* input_bf16, const void* weight_bf16, void* output_bf16,
+                                           std::int32_t row_count, cudaStream_t stream) noexcept {
+  return mtt_b200_launch_layer_norm(input_bf16, weight_bf16, output_bf16, row_count, static_cast<void*>(stream));
+}
+[[nodiscard]] inline int launch_gelu_tanh(const void* input_bf16, void* output_bf16, std::size_t element_count,
+                                          cudaStream_t stream) noexcept {
+  return mtt_b200_launch_gelu_tanh(input_bf16, output_bf16, element_count, static_cast<void*>(stream));
+}
+[[nodiscard]] inline int launch_softmax(const void* input_bf16, void* output_bf16, std::int32_t batch_count,
+                                        std::int32_t element_count, cudaStream_t stream) noexcept {
+  return mtt_b200_launch_softmax(input_bf16, output_bf16, batch_count, element_count, static_cast<void*>(stream));
 }
 }  // namespace magpie_tts_rt::plugins
 #endif

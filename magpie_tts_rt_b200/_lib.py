@@ -123,6 +123,9 @@ SIGNATURES = {
     "mtt_b200_launch_local_ar_eos": (I32, [P] * 9 + [P]),
     "mtt_b200_launch_finalize_local_step": (
         I32, [P, P, ctypes.c_uint32, P, P, P, P, P, P, P, P]),
+    "mtt_b200_launch_layer_norm": (I32, [P, P, P, I32, P]),
+    "mtt_b200_launch_gelu_tanh": (I32, [P, P, SZ, P]),
+    "mtt_b200_launch_softmax": (I32, [P, P, I32, I32, P]),
     "mtt_b200_local_ar_frame_workspace_size": (SZ, [ctypes.POINTER(Shape), I32, I32]),
     "mtt_b200_launch_local_ar_frame": (
         I32, [ctypes.POINTER(Shape), ctypes.POINTER(Weights), ctypes.POINTER(SamplingConfig),

@@ -73,7 +73,7 @@ constexpr int kLdQ = 384 + 8;   // 392: this CTA's q | k | v
 constexpr int kLdH = 512 + 8;   // 520: this CTA's half of the FFN hidden
 constexpr int kHalf = kVocab / 2;  // 1012
 constexpr int kTmemCols = 512;
-constexpr int kListBytes = 2 * kListCap * 2;  // candidate + eligible lists per sampled session
+constexpr int kListBytes = (2 * kListCap + 8) * 2;  // candidate (+ scratch entry) + eligible lists
 static_assert(kPOwn * kListBytes <= kPR * kLdX * 2, "sampler lists in xa");
 
 struct PairMaps {
@@ -806,7 +806,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
         rs.counter = sm.ctr[ls];
         uint16_t* lists = reinterpret_cast<uint16_t*>(reinterpret_cast<unsigned char*>(sm.xa) + ls * kListBytes);
         int invalid = 0;
-        const int token = sample_row(rs, f.prm, lists, lists + kListCap, &invalid);
+        const int token = sample_row(rs, f.prm, lists, lists + kListCap + 8, &invalid);
         __syncwarp();
         const uint32_t rb = peer_bar(sm, rd, peer);
         if (lane == 0) {

@@ -449,7 +449,7 @@ __device__ __forceinline__ void attention(TileSmem& sm, int p) {
 }
 
 constexpr int kListStride = (kTRows * kLdX) / kTSess;  // 528 u16 per session slot in xa
-static_assert(kListStride >= kListCap, "candidate list");
+static_assert(kListStride >= kListCap + 1, "candidate list");
 
 __device__ __forceinline__ int sample_slot(TileSmem& sm, const Frame& f, int slot, int* invalid_out) {
   RowSample rs;

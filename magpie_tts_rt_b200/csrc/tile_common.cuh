@@ -91,22 +91,58 @@ __device__ __forceinline__ Best warp_best(Best b) {
   return b;
 }
 
-// Philox-Gumbel scores of the tokens list[0, total), four independent chains per lane.
+// Philox-Gumbel scores of the tokens list[0, total), exact: with up to 128
+// tokens every token is first scored with the library logf (within 1e-5 of
+// the contract's correctly rounded Gumbel; scores stay within 1e-4), then
+// only the tokens whose fast score is within kVerifyMargin of the best fast
+// score are rescored with the correctly rounded log.  The exact winner's fast
+// score is at least (best fast score - 2e-4), so it is always rescored: the
+// result is the exact left-most argmax.  Longer lists are scored exactly.
+constexpr float kVerifyMargin = 1.0e-3f;
+
+__device__ __forceinline__ float fast_gumbel(float u) {
+  u = fmaxf(0.00000006f, fminf(0.99999994f, u));
+  return -logf(-logf(u));
+}
+
+// Score with the contract's Gumbel (one copy of the double-precision log code).
+__device__ __noinline__ float exact_score(float value, float temperature, uint32_t seed32, uint64_t offset) {
+  return __fadd_rn(__fdiv_rn(value, temperature), clamped_gumbel(philox_uniform(seed32, offset)));
+}
+
 __device__ __forceinline__ void score_list(const uint16_t* list, uint32_t total, const uint16_t* vals, uint32_t seed32,
                                            uint64_t off64, float temperature, Best& b) {
   const int lane = threadIdx.x & 31;
-  for (uint32_t base = 0; base < total; base += 128) {
-    int t[4];
-    float u[4];
+  if (total <= 128) {
+    float fs[4];
+    float best_fast = -CUDART_INF_F;
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      const uint32_t e = base + lane + 32 * j;
-      t[j] = e < total ? list[e] : -1;
-      u[j] = philox_uniform(seed32, off64 + static_cast<uint64_t>(t[j] < 0 ? 0 : t[j]));
+      fs[j] = -CUDART_INF_F;
+      const uint32_t e = lane + 32 * j;
+      if (e < total) {
+        const int t = list[e];
+        const float u = philox_uniform(seed32, off64 + static_cast<uint64_t>(t));
+        fs[j] = __fadd_rn(__fdiv_rn(bits2f(vals[t]), temperature), fast_gumbel(u));
+        best_fast = fmaxf(best_fast, fs[j]);
+      }
     }
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      if (t[j] >= 0) keep_best(b, __fadd_rn(__fdiv_rn(bits2f(vals[t[j]]), temperature), clamped_gumbel(u[j])), t[j]);
+    for (int o = 16; o > 0; o >>= 1) best_fast = fmaxf(best_fast, __shfl_xor_sync(0xffffffffu, best_fast, o));
+    const float cut = best_fast - kVerifyMargin;
+    uint32_t verify = 0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) verify |= (fs[j] >= cut ? 1u : 0u) << j;
+    while (verify) {
+      const int j = __ffs(verify) - 1;
+      verify &= verify - 1;
+      const int t = list[lane + 32 * j];
+      keep_best(b, exact_score(bits2f(vals[t]), temperature, seed32, off64 + static_cast<uint64_t>(t)), t);
+    }
+  } else {
+    for (uint32_t e = lane; e < total; e += 32) {
+      const int t = list[e];
+      keep_best(b, exact_score(bits2f(vals[t]), temperature, seed32, off64 + static_cast<uint64_t>(t)), t);
     }
   }
 }
@@ -302,8 +338,10 @@ __device__ int sample_row(const RowSample& rs, const SamplingParams& prm, uint16
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           const uint32_t m = __hge2_mask(bf2_of(w[e]), limw);
-          if (m & 0xffffu) list[pos++] = static_cast<uint16_t>(8 * ch + 2 * e);
-          if (m >> 16) list[pos++] = static_cast<uint16_t>(8 * ch + 2 * e + 1);
+          if (m & 1u) list[pos] = static_cast<uint16_t>(8 * ch + 2 * e);
+          pos += m & 1u;
+          if (m >> 31) list[pos] = static_cast<uint16_t>(8 * ch + 2 * e + 1);
+          pos += m >> 31;
         }
       }
     }

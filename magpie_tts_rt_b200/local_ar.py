@@ -1,7 +1,8 @@
 """Host-side mirror of the reference's Local AR plugin/launcher interface.
 
 * ``launch_local_ar_sampling`` / ``local_ar_eos_workspace_size`` /
-  ``launch_local_ar_eos`` / ``launch_finalize_local_step``: same names,
+  ``launch_local_ar_eos`` / ``launch_finalize_local_step`` /
+  ``launch_layer_norm`` / ``launch_gelu_tanh`` / ``launch_softmax``: same names,
   arguments and 0 / -1 return convention as the reference's C++ launchers
   (``plugins/local_ar_plugins.hpp:29-55``,
   ``src/runtime/synthesis_kernels.cu:177-214``), taking CUDA tensors and
@@ -92,6 +93,18 @@ def launch_finalize_local_step(step_codec_tokens, aggregate_codec_tokens, frame_
         _ptr(canonical_invalid_rows), _ptr(canonical_end_frame_index), _ptr(step_invalid_rows),
         _ptr(step_end_frame_index), _ptr(updated_rng_counter), _ptr(rng_counter),
         _ptr(generation_finished), _stream(stream))
+
+
+def launch_layer_norm(input, weight, output, row_count: int, stream=None) -> int:
+    return L.lib.mtt_b200_launch_layer_norm(_ptr(input), _ptr(weight), _ptr(output), row_count, _stream(stream))
+
+
+def launch_gelu_tanh(input, output, element_count: int, stream=None) -> int:
+    return L.lib.mtt_b200_launch_gelu_tanh(_ptr(input), _ptr(output), element_count, _stream(stream))
+
+
+def launch_softmax(input, output, batch_count: int, element_count: int, stream=None) -> int:
+    return L.lib.mtt_b200_launch_softmax(_ptr(input), _ptr(output), batch_count, element_count, _stream(stream))
 
 
 # ---------------------------------------------------------------------------
