@@ -406,10 +406,9 @@ __device__ __forceinline__ int sample_block(const SampleCall& c, const SamplingP
     __syncthreads();
     const uint32_t seed32 = seed_valid ? static_cast<uint32_t>(c.seed) : 0u;
     const uint64_t off64 = counter_valid ? static_cast<uint64_t>(c.counter) * kPhiloxStride : 0ull;
-    for (uint32_t e = threadIdx.x; e < total; e += blockDim.x) {
-      const int t = elig[e];
-      // the constrained value of token t lives in the owning thread's registers;
-      // recompute it from the logits (cheap, exact) instead of exchanging it
+    // the constrained value of token t lives in the owning thread's registers;
+    // recompute it from the logits (cheap, exact) instead of exchanging it
+    auto value_of = [&](int t) {
       float value;
       if (c.kind == kLogitsF32) {
         value = static_cast<const float*>(c.logits)[t];
@@ -418,15 +417,39 @@ __device__ __forceinline__ int sample_block(const SampleCall& c, const SamplingP
         value = c.kind == kLogitsBf16Cfg ? guided_logit(bits2f(l[t]), bits2f(l[c.uncond_offset + t]), prm.cfg_scale)
                                          : bits2f(l[t]);
       }
-      if (c.finished) value = 0.0f;  // only EOS (value 0) is finite for a finished row
-      const float g = clamped_gumbel(philox_uniform(seed32, off64 + static_cast<uint64_t>(t)));
-      const float score = __fadd_rn(__fdiv_rn(value, prm.temperature), g);
-      if (score > best || (score == best && t < best_id)) {
-        best = score;
-        best_id = t;
+      return c.finished ? 0.0f : value;  // only EOS (value 0) is finite for a finished row
+    };
+    bool exact = true;
+    if (total <= blockDim.x) {
+      // fast scores (library logf) first; the exact Gumbel only when more than
+      // one token lies within kVerifyMargin of the best fast score
+      const int t1 = threadIdx.x < total ? elig[threadIdx.x] : -1;
+      const float v1 = t1 >= 0 ? value_of(t1) : 0.0f;
+      const float f1 = t1 >= 0 ? __fadd_rn(__fdiv_rn(v1, prm.temperature),
+                                           fast_gumbel(philox_uniform(seed32, off64 + static_cast<uint64_t>(t1))))
+                               : -CUDART_INF_F;
+      block_argmax(f1, t1 >= 0 ? t1 : kVocab, sh);
+      const bool near = t1 >= 0 && f1 >= sh.warp_best[0] - kVerifyMargin;
+      if (__syncthreads_count(near) == 1) {
+        exact = false;  // sh holds the winner
+      } else if (near) {
+        const float g = clamped_gumbel(philox_uniform(seed32, off64 + static_cast<uint64_t>(t1)));
+        best = __fadd_rn(__fdiv_rn(v1, prm.temperature), g);
+        best_id = t1;
       }
+      if (exact) block_argmax(best, best_id, sh);
+    } else {
+      for (uint32_t e = threadIdx.x; e < total; e += blockDim.x) {
+        const int t = elig[e];
+        const float g = clamped_gumbel(philox_uniform(seed32, off64 + static_cast<uint64_t>(t)));
+        const float score = __fadd_rn(__fdiv_rn(value_of(t), prm.temperature), g);
+        if (score > best || (score == best && t < best_id)) {
+          best = score;
+          best_id = t;
+        }
+      }
+      block_argmax(best, best_id, sh);
     }
-    block_argmax(best, best_id, sh);
   }
   const float b = sh.warp_best[0];
   int token = sh.warp_best_id[0];

@@ -97,14 +97,8 @@ __device__ __forceinline__ Best warp_best(Best b) {
 // only the tokens whose fast score is within kVerifyMargin of the best fast
 // score are rescored with the correctly rounded log.  The exact winner's fast
 // score is at least (best fast score - 2e-4), so it is always rescored: the
-// result is the exact left-most argmax.  Longer lists are scored exactly.
-constexpr float kVerifyMargin = 1.0e-3f;
-
-__device__ __forceinline__ float fast_gumbel(float u) {
-  u = fmaxf(0.00000006f, fminf(0.99999994f, u));
-  return -logf(-logf(u));
-}
-
+// result is the exact left-most argmax; when it is the only token within the
+// margin it is the winner without rescoring.  Longer lists are scored exactly.
 // Score with the contract's Gumbel (one copy of the double-precision log code).
 __device__ __noinline__ float exact_score(float value, float temperature, uint32_t seed32, uint64_t offset) {
   return __fadd_rn(__fdiv_rn(value, temperature), clamped_gumbel(philox_uniform(seed32, offset)));
@@ -133,6 +127,15 @@ __device__ __forceinline__ void score_list(const uint16_t* list, uint32_t total,
     uint32_t verify = 0;
 #pragma unroll
     for (int j = 0; j < 4; ++j) verify |= (fs[j] >= cut ? 1u : 0u) << j;
+    if (__reduce_add_sync(0xffffffffu, __popc(verify)) == 1) {
+      // a single token within the margin: it is the exact winner (no other
+      // token's exact score can reach it), and only the token is needed
+      if (verify) {
+        const int j = __ffs(verify) - 1;
+        keep_best(b, fs[j], list[lane + 32 * j]);
+      }
+      return;
+    }
     while (verify) {
       const int j = __ffs(verify) - 1;
       verify &= verify - 1;
