@@ -47,6 +47,8 @@ import torch  # noqa: E402
 from magpie_tts_rt_b200.model import EMBED, SHAPE_BASELINE, make_weights  # noqa: E402
 
 METRIC = "Local-AR+sampling frames/sec per GPU and box (1/2/4/8); p50 per-frame us"
+PATH_NAMES = {1: "phase kernels", 2: "fused cluster kernel", 3: "tile kernel", 4: "pair kernel",
+              5: "split kernel x1", 6: "split kernel x2", 7: "split kernel x4"}
 WORKLOADS = {
     "config4": dict(total_streams=1024, frames=500, eos_frac=0.05, eos_lo=50, eos_hi=500, weak=False),
     "config3": dict(per_gpu_streams=64, frames=600, eos_frac=1.0, eos_lo=200, eos_hi=600, weak=True),
@@ -323,7 +325,7 @@ def run_ours(args, world, rank, local):
     forced_ok = all(end_np[eos[s], s] == 0 for s in range(n) if eos[s] < frames)
     launches_per_frame = eng.launch_count(n)
     return dict(value=value, t=t, e2e=e2e_value, h2d=h2d, d2h=d2h, clocks=clk, n_local=n, total=total,
-                path={1: "phase kernels", 2: "fused cluster kernel", 3: "tile kernel", 4: "pair kernel"}.get(eng.path, str(eng.path)),
+                path=PATH_NAMES.get(eng.path, str(eng.path)),
                 frames=frames, frames_per_step=frames_total / args.steps, invalid=bad, forced_ok=forced_ok,
                 launches=launches_per_frame * frames * args.steps, eng=eng, w=w)
 
@@ -361,7 +363,7 @@ def latency_config2(eng_w, dev, frames=1000, warm=20):
     inv = int(b.invalid_rows.item())
     del graph
     return {"workload": "config2: 1 session x CFG pair, seed 1234, 1000 frames, CUDA graph per frame",
-            "frame_path": {1: "phase kernels", 2: "fused cluster kernel", 3: "tile kernel", 4: "pair kernel"}.get(eng.path, str(eng.path)),
+            "frame_path": PATH_NAMES.get(eng.path, str(eng.path)),
             "p50_us": float(np.percentile(us, 50)), "p99_us": float(np.percentile(us, 99)),
             "mean_us": float(us.mean()), "frames": frames, "invalid": inv}
 
@@ -463,8 +465,10 @@ def main():
         # call = that kernel + the EOS projection/decision kernels, timed together by CUDA events
         tile = res["path"] == "tile kernel"
         roof = {"bound": "tensor",
-                "kernel": {"tile kernel": "tile_frame_kernel", "pair kernel": "pair_frame_kernel"}.get(
-                    res["path"], res["path"]) +
+                "kernel": {"tile kernel": "tile_frame_kernel", "pair kernel": "pair_frame_kernel",
+                           "fused cluster kernel": "fused_frame_kernel", "split kernel x1": "split_frame_kernel<1>",
+                           "split kernel x2": "split_frame_kernel<2>",
+                           "split kernel x4": "split_frame_kernel<4>"}.get(res["path"], res["path"]) +
                           " (per frame call, with the EOS projection/decision kernels: 0.6% of device time)",
                 "achieved": tf, "peak": tensor_peak, "unit": "TFLOP/s", "frac": tf / tensor_peak,
                 "peak_kind": f"{peaks_kind} sustained bf16",

@@ -282,21 +282,26 @@ MTT_B200_API int mtt_b200_launch_fold_in_projection(const mtt_b200_local_ar_shap
                                                    void* stream);
 
 /* Frame implementations.  For the shape d_model 256, 4 heads, FFN 1024,
- * 1 layer three fused single-launch kernels exist: FUSED_CLUSTER spreads a
+ * 1 layer these fused single-launch kernels exist: FUSED_CLUSTER spreads a
  * 16-row tile (8 sessions with CFG, 16 without) over a 16-CTA thread-block
  * cluster (lowest latency per tile, at most a few clusters on the device at
  * once); FUSED_TILE runs 8 sessions in one CTA with their KV cache in tensor
  * memory; FUSED_PAIR runs 16 sessions on a 2-CTA cluster, each CTA streaming
- * half of every weight matrix (the most sessions per second at large
- * batches with fewer weight bytes per SM).  AUTO picks FUSED_CLUSTER while
- * the batch's 16-row tiles need at most two waves of the clusters the device
- * runs at once, FUSED_TILE above that, and the phase kernels for other
- * shapes. */
+ * half of every weight matrix; SPLIT_1 / SPLIT_2 / SPLIT_4 run 8 sessions on
+ * a cluster of 1, 2 or 4 CTAs, each streaming that fraction of every weight
+ * matrix, with the GEMMs on tcgen05 tensor cores (accumulators and the KV
+ * cache in tensor memory).  AUTO picks FUSED_CLUSTER while the batch's tiles
+ * fit in one wave of its clusters, then SPLIT_4 and SPLIT_2 while theirs do
+ * (fewer sessions per GPU: more CTAs per session, shorter frames), then
+ * FUSED_TILE, and the phase kernels for other shapes. */
 #define MTT_B200_FRAME_PATH_AUTO 0
 #define MTT_B200_FRAME_PATH_PHASE_KERNELS 1
 #define MTT_B200_FRAME_PATH_FUSED_CLUSTER 2
 #define MTT_B200_FRAME_PATH_FUSED_TILE 3
 #define MTT_B200_FRAME_PATH_FUSED_PAIR 4
+#define MTT_B200_FRAME_PATH_SPLIT_1 5
+#define MTT_B200_FRAME_PATH_SPLIT_2 6
+#define MTT_B200_FRAME_PATH_SPLIT_4 7
 
 /* Sampling configuration; the reference's values are 80 / 0.6 / 2.5 with CFG
  * and top-k.  argmax != 0 selects greedy decoding (no RNG, counter unchanged;
@@ -379,12 +384,18 @@ MTT_B200_API int mtt_b200_launch_local_ar_frame_static_workspace(const mtt_b200_
                                                                 const mtt_b200_stream_batch_t* batch,
                                                                 void* stream);
 
-/* The path (MTT_B200_FRAME_PATH_PHASE_KERNELS, _FUSED_CLUSTER, _FUSED_TILE or
- * _FUSED_PAIR) that mtt_b200_launch_local_ar_frame takes for this shape,
+/* The path (MTT_B200_FRAME_PATH_PHASE_KERNELS, _FUSED_CLUSTER, _FUSED_TILE,
+ * _FUSED_PAIR, _SPLIT_1, _SPLIT_2 or _SPLIT_4) that mtt_b200_launch_local_ar_frame takes for this shape,
  * configuration and batch size on the current device, or
  * MTT_B200_STATUS_UNSUPPORTED. */
 MTT_B200_API int32_t mtt_b200_local_ar_frame_path(const mtt_b200_local_ar_shape_t* shape,
                                                   const mtt_b200_sampling_config_t* sampling, int32_t n_streams);
+
+/* Thread-block clusters of a fused frame path (MTT_B200_FRAME_PATH_FUSED_CLUSTER,
+ * _FUSED_TILE (1-CTA clusters), _FUSED_PAIR, _SPLIT_1, _SPLIT_2, _SPLIT_4) that
+ * the current device runs at once, each holding one tile of the batch; 0 when
+ * the path cannot run here.  AUTO compares the batch's tiles with these. */
+MTT_B200_API int32_t mtt_b200_local_ar_frame_path_clusters(int32_t path);
 
 /* Number of kernels mtt_b200_launch_local_ar_frame enqueues for this shape,
  * configuration and batch on the current device (for launch accounting). */

@@ -101,6 +101,9 @@ PATH_PHASE_KERNELS = 1
 PATH_FUSED_CLUSTER = 2
 PATH_FUSED_TILE = 3
 PATH_FUSED_PAIR = 4
+PATH_SPLIT_1 = 5
+PATH_SPLIT_2 = 6
+PATH_SPLIT_4 = 7
 
 
 class StreamBatch(ctypes.Structure):
@@ -133,6 +136,7 @@ SIGNATURES = {
     "mtt_b200_local_ar_frame_launch_count": (
         I32, [ctypes.POINTER(Shape), ctypes.POINTER(SamplingConfig), I32]),
     "mtt_b200_local_ar_frame_path": (I32, [ctypes.POINTER(Shape), ctypes.POINTER(SamplingConfig), I32]),
+    "mtt_b200_local_ar_frame_path_clusters": (I32, [I32]),
     "mtt_b200_fold_in_projection_bytes": (SZ, [ctypes.POINTER(Shape)]),
     "mtt_b200_launch_fold_in_projection": (
         I32, [ctypes.POINTER(Shape), ctypes.POINTER(Weights), P, P]),

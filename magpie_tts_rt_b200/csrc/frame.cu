@@ -437,12 +437,23 @@ extern "C" MTT_B200_API size_t mtt_b200_local_ar_frame_workspace_size(const mtt_
 namespace {
 
 // Resolves the path for a shape / configuration / batch size on the current
-// device.  AUTO: the fused cluster kernel while the batch's 16-row tiles need
-// at most two waves of the clusters the device runs at once (on B200 a wave
-// of the cluster kernel takes ~0.3 ms per frame, one wave of the tile kernel
-// ~0.8 ms), the tile kernel above that, the phase kernels for other shapes.
-// The pair kernel does the same work per SM as the tile kernel and is
-// selected explicitly.
+// device.  AUTO, benchmark shape, by the batch's 16-row tiles (8 sessions
+// each): the fused 16-CTA cluster kernel while the tiles fit in one wave of
+// its clusters (on B200 ~0.3 ms per frame); then the split kernel with the
+// widest cluster (4, else 2 CTAs per tile) whose tiles still fit in one wave
+// (~0.5 / ~0.6 ms per frame); above that the tile kernel (~0.75 ms per frame
+// for up to one CTA per SM).  So the frame time falls with the batch, and
+// sessions sharded over more GPUs run shorter frames.  Other shapes: the
+// phase kernels.
+int split_of_path(int32_t path) {
+  return path == MTT_B200_FRAME_PATH_SPLIT_4 ? 4 : (path == MTT_B200_FRAME_PATH_SPLIT_2 ? 2 : 1);
+}
+
+bool is_split_path(int32_t path) {
+  return path == MTT_B200_FRAME_PATH_SPLIT_1 || path == MTT_B200_FRAME_PATH_SPLIT_2 ||
+         path == MTT_B200_FRAME_PATH_SPLIT_4;
+}
+
 int32_t resolve_path(const mtt_b200_local_ar_shape_t* shape, const mtt_b200_sampling_config_t* sampling,
                      int32_t n_streams) {
   mtt::Frame probe{};
@@ -458,9 +469,17 @@ int32_t resolve_path(const mtt_b200_local_ar_shape_t* shape, const mtt_b200_samp
   switch (sampling->path) {
     case MTT_B200_FRAME_PATH_AUTO: {
       if (!fused && !tile && !pair) return MTT_B200_FRAME_PATH_PHASE_KERNELS;
-      const int spt = 16 / probe.rp;
-      const int tiles = (n_streams + spt - 1) / spt;
-      if (fused && tiles <= 2 * mtt::fused_frame_clusters()) return MTT_B200_FRAME_PATH_FUSED_CLUSTER;
+      const int spt = 16 / probe.rp;  // sessions per tile of the fused cluster kernel
+      if (fused && (n_streams + spt - 1) / spt <= mtt::fused_frame_clusters()) {
+        return MTT_B200_FRAME_PATH_FUSED_CLUSTER;
+      }
+      const int tiles = (n_streams + 7) / 8;  // split kernel tiles
+      if (tiles <= mtt::split_frame_clusters(4) && mtt::split_frame_supported(probe, 4)) {
+        return MTT_B200_FRAME_PATH_SPLIT_4;
+      }
+      if (tiles <= mtt::split_frame_clusters(2) && mtt::split_frame_supported(probe, 2)) {
+        return MTT_B200_FRAME_PATH_SPLIT_2;
+      }
       if (tile) return MTT_B200_FRAME_PATH_FUSED_TILE;
       if (pair) return MTT_B200_FRAME_PATH_FUSED_PAIR;
       return MTT_B200_FRAME_PATH_FUSED_CLUSTER;
@@ -473,6 +492,11 @@ int32_t resolve_path(const mtt_b200_local_ar_shape_t* shape, const mtt_b200_samp
       return tile ? MTT_B200_FRAME_PATH_FUSED_TILE : MTT_B200_STATUS_UNSUPPORTED;
     case MTT_B200_FRAME_PATH_FUSED_PAIR:
       return pair ? MTT_B200_FRAME_PATH_FUSED_PAIR : MTT_B200_STATUS_UNSUPPORTED;
+    case MTT_B200_FRAME_PATH_SPLIT_1:
+    case MTT_B200_FRAME_PATH_SPLIT_2:
+    case MTT_B200_FRAME_PATH_SPLIT_4:
+      return mtt::split_frame_supported(probe, split_of_path(sampling->path)) ? sampling->path
+                                                                                 : MTT_B200_STATUS_UNSUPPORTED;
     default:
       return MTT_B200_STATUS_INVALID_ARGUMENT;
   }
@@ -487,13 +511,25 @@ extern "C" MTT_B200_API int32_t mtt_b200_local_ar_frame_path(const mtt_b200_loca
   return resolve_path(shape, sampling, n_streams);
 }
 
+extern "C" MTT_B200_API int32_t mtt_b200_local_ar_frame_path_clusters(int32_t path) {
+  switch (path) {
+    case MTT_B200_FRAME_PATH_FUSED_CLUSTER: return mtt::fused_frame_clusters();
+    case MTT_B200_FRAME_PATH_FUSED_PAIR: return mtt::pair_frame_clusters();
+    case MTT_B200_FRAME_PATH_FUSED_TILE: return mtt::tile_frame_clusters();
+    case MTT_B200_FRAME_PATH_SPLIT_1:
+    case MTT_B200_FRAME_PATH_SPLIT_2:
+    case MTT_B200_FRAME_PATH_SPLIT_4: return mtt::split_frame_clusters(split_of_path(path));
+    default: return 0;
+  }
+}
+
 extern "C" MTT_B200_API int32_t mtt_b200_local_ar_frame_launch_count(const mtt_b200_local_ar_shape_t* shape,
                                                                      const mtt_b200_sampling_config_t* sampling,
                                                                      int32_t n_streams) {
   if (!mtt::shape_ok(shape) || sampling == nullptr || n_streams <= 0) return 0;
   const int32_t path = resolve_path(shape, sampling, n_streams);
   if (path == MTT_B200_FRAME_PATH_FUSED_CLUSTER || path == MTT_B200_FRAME_PATH_FUSED_TILE ||
-      path == MTT_B200_FRAME_PATH_FUSED_PAIR) {
+      path == MTT_B200_FRAME_PATH_FUSED_PAIR || is_split_path(path)) {
     return 3;  // fused frame, EOS projection, EOS finish
   }
   if (path != MTT_B200_FRAME_PATH_PHASE_KERNELS) return 0;
@@ -596,6 +632,10 @@ extern "C" MTT_B200_API int mtt_b200_launch_local_ar_frame(const mtt_b200_local_
   }
   if (path == MTT_B200_FRAME_PATH_FUSED_PAIR) {
     return launch_pair_frame(f, st) == cudaSuccess ? MTT_B200_STATUS_OK : MTT_B200_STATUS_CUDA_ERROR;
+  }
+  if (is_split_path(path)) {
+    return launch_split_frame(f, split_of_path(path), st) == cudaSuccess ? MTT_B200_STATUS_OK
+                                                                          : MTT_B200_STATUS_CUDA_ERROR;
   }
   const int d = f.d, F = f.F;
   frame_begin_kernel<<<1, kBeginThreads, 0, st>>>(f);

@@ -86,6 +86,7 @@ cudaError_t launch_fused_frame(const Frame& f, cudaStream_t stream);
 
 // Tile kernel (frame_tile.cu): one CTA per 16-row tile, KV cache in TMEM.
 bool tile_frame_supported(const Frame& f);
+int tile_frame_clusters();
 cudaError_t launch_tile_frame(const Frame& f, cudaStream_t stream);
 
 // Pair kernel (frame_pair.cu): a 2-CTA cluster per 16 sessions, each CTA
@@ -93,6 +94,14 @@ cudaError_t launch_tile_frame(const Frame& f, cudaStream_t stream);
 bool pair_frame_supported(const Frame& f);
 int pair_frame_clusters();
 cudaError_t launch_pair_frame(const Frame& f, cudaStream_t stream);
+
+// Split kernel (frame_split.cu): a cluster of `split` CTAs (1, 2 or 4) per
+// 16-row tile, each streaming 1/split of every weight matrix, GEMMs on
+// tcgen05 with TMEM accumulators.
+bool split_frame_supported(const Frame& f, int split);
+// Clusters of `split` CTAs that fit on the device at once (0: unsupported).
+int split_frame_clusters(int split);
+cudaError_t launch_split_frame(const Frame& f, int split, cudaStream_t stream);
 
 // EOS projection + decision for the sessions a fused or tile kernel registered.
 cudaError_t launch_frame_eos(const Frame& f, cudaStream_t stream);

@@ -1,0 +1,1196 @@
+// Split frame kernel: a C-CTA thread-block cluster (C = 1, 2 or 4) runs all
+// 16 positions of a Local AR frame for a tile of up to 8 sessions (16 rows
+// with CFG), each CTA streaming 1/C of every weight matrix, with the GEMMs on
+// the fifth-generation tensor cores (tcgen05.mma, accumulators in tensor
+// memory).  C is picked per batch so that the tiles x C CTAs fill the device:
+// fewer sessions per GPU means more CTAs per session and a shorter frame,
+// which is what lets session sharding over more GPUs scale.
+//
+// Reference ops per position (as in frame_tile.cu: local_ar_wrapper.py:609-751,
+// transformer_2501.py:405-442,761-851,1153-1232, sampling
+// local_ar_plugins.cu:1211-1370, embedding sum main_decoder_wrapper.py:796-810),
+// CTA c of the cluster, nh = 4 / C heads per CTA:
+//
+//   input rows: p = 0 (or every p without the folded tables) the full
+//     in-projection in every CTA, x = bf16(bf16(W_in h + b) + pos[p]);
+//     p >= 1: x = bf16(emb_proj[p-1][token] + pos[p]) gathered by every CTA
+//   LN1 (every CTA, all rows); q|k|v of heads [c nh, +nh); k/v appended to
+//     this CTA's TMEM KV cache; attention for those heads;      exchange R1
+//       (the heads' outputs to every CTA)
+//   o-projection features [256c/C, +256/C) + residual;          exchange R2
+//   LN2; FFN1 features [1024c/C, +1024/C) + GELU-tanh; FFN2 partial sums over
+//     those features for all 256 outputs, scattered to the owners of the
+//     output features (f32);                                     exchange R3
+//   own features = the C partial sums in CTA order, + residual;  exchange R4
+//   head p vocabulary [2048c/C, +2048/C) for all sessions (bias, CFG combine
+//     with the plugin's two roundings, constraints); the other CTAs' sessions'
+//     values and non-finite flags go to their owners;           exchange R5
+//   one warp per owned session (sessions [8c/C, +8/C)) samples and sends the
+//     token to every CTA                                         exchange R6
+//   (with C = 1 there are no exchanges).
+//
+// GEMMs (swap-AB): D[128 weight rows][16 tile rows] = W[128][K] x X[16][K]^T
+// on tcgen05.mma kind::f16 M=128 N=16 K=16, A = a weight chunk in shared
+// memory, B = the activation rows in shared memory, both K-major with the
+// 128-byte swizzle; one thread issues, tcgen05.commit signals the weight
+// slot free and the accumulator full.  A weight chunk is 128 rows x 128 K
+// columns (32 KB) as four 64 x 64 TMA boxes (no multicast); its two 64-row
+// halves may come from different places of the same matrix (a head's q and
+// k rows, say), and a half that the CTA does not need repeats the first.
+// Weights stream through a four-slot ring filled by a producer warp that
+// runs ahead across GEMMs and positions.  Two accumulator buffers of 16 TMEM
+// columns alternate by M-block, so the epilogue of one block overlaps the
+// MMAs of the next.
+//
+// Tensor memory (512 columns x 128 lanes): the KV cache of positions 0..14
+// of the CTA's heads, lane 32 lh + 2 r + half = local head lh, row r, head
+// dims [32 half, +32); K of position j at columns 16 b(j), V at 256 + 16 b(j),
+// b(j) = 8 (j mod 2) + j / 2.  Block b(15) is never written (position 15's
+// k/v are read from shared memory), so columns [240, 256) and [496, 512) are
+// the two accumulator buffers.
+//
+// Exchanges push data with st.async into the receivers' shared memory and
+// complete on the receiver's round mbarrier, on which every CTA of the
+// cluster also arrives with the byte count it pushed; two barriers alternate
+// by round parity.  Each round's pushes land in buffers the receiver does not
+// read or write during the phase that precedes that round.  Every wait is
+// bounded; a timeout sets invalid bit 4 for the CTA's sessions.
+#include <cooperative_groups.h>
+#include <cuda.h>
+
+#include <mutex>
+
+#include "frame_common.cuh"
+#include "ptx.cuh"
+#include "tile_common.cuh"
+
+namespace cg = cooperative_groups;
+
+namespace mtt {
+namespace {
+
+constexpr int kSR = 16;                    // rows per tile
+constexpr int kSS = 8;                     // session slots per tile
+constexpr int kSW = 8;                     // consumer warps
+constexpr int kSC = kSW * 32;              // consumer threads
+constexpr int kSThreads = kSC + 128;       // + the control warpgroup (TMA producer warp, MMA warp)
+constexpr int kSProducerRegs = 40;
+constexpr int kSConsumerRegs = 232;
+static_assert(128 * kSProducerRegs + kSC * kSConsumerRegs <= kSThreads * 168, "register split");
+constexpr int kD = 256;
+constexpr int kF = 1024;
+constexpr int kHeads = 4;
+constexpr int kSlots = 4;
+constexpr int kChunkRows = 128;
+constexpr int kChunkK = 128;
+constexpr int kPanelElems = kChunkRows * 64;      // one 128-row x 64-column swizzled panel (16 KB)
+constexpr int kChunkElems = 2 * kPanelElems;      // 32 KB
+constexpr uint32_t kChunkBytes = kChunkElems * 2;
+constexpr int kBoxRows = 64;
+constexpr int kOpPanel = kSR * 64;                // one 16-row x 64-column operand panel (2 KB)
+constexpr int kLdX = kD + 8;
+constexpr uint32_t kIdesc = umma_idesc_bf16(128, kSR);
+// TMEM columns of the two accumulator buffers (block b(15) of K and of V).
+__device__ __forceinline__ uint32_t dcol(int db) { return db ? 496u : 240u; }
+constexpr int kListBytes = 2 * (kListCap + 16) + 2 * kListCap;  // candidate list + eligible list (u16)
+
+enum Gemm { G_IN = 0, G_QKV, G_O, G_F1, G_F2, G_HEAD };
+
+template <int C>
+struct Cfg {
+  static constexpr int nh = kHeads / C;      // heads per CTA
+  static constexpr int nq = (3 * nh + 1) / 2;  // qkv M-blocks (pairs of 64-row head groups)
+  static constexpr int of = kD / C;          // o-projection / residual features per CTA
+  static constexpr int no = of >= 128 ? of / 128 : 1;
+  static constexpr int f1 = kF / C;          // FFN1 features per CTA = FFN2 K per CTA
+  static constexpr int nf1 = f1 / 128;
+  static constexpr int vs = 2048 / C;        // vocabulary slice per CTA (blocks of 128)
+  static constexpr int nhb = vs / 128;
+  static constexpr int own = kSS / C;        // sessions sampled per CTA
+  static constexpr int ldq = 3 * nh * 64 + 8;
+  static constexpr int qkv_elems = kSR * ldq;
+  static constexpr int hid_elems = kSR * f1;  // FFN hidden as 16-row panels
+  static_assert(nf1 >= 1 && nhb >= 1 && own >= 1, "split");
+};
+
+struct SplitMaps {
+  CUtensorMap in_proj, qkv, o, ffn1, ffn2, head;
+};
+
+// Attention exchange between the two warps of a head (scratch in the union).
+struct SplitAttn {
+  float s[2][kHeads][32][8];
+  float o[kHeads][32][32];
+};
+
+template <int C>
+struct __align__(1024) SplitSmem {
+  using K = Cfg<C>;
+  bf16 ring[kSlots][kChunkElems];  // weight chunks (1024-byte aligned panels)
+  bf16 xa[4 * kOpPanel];           // LN output (B operand)
+  bf16 ab[4 * kOpPanel];           // attention output / residual stream copy (B operand)
+  union U {
+    bf16 src[12 * kOpPanel];                    // in-projection input rows (B operand, K = 768)
+    SplitAttn att;                              // attention exchange
+    bf16 hid[K::hid_elems];                     // FFN hidden slice (B operand)
+    struct {
+      uint16_t own[K::own][kVocab];             // constrained values of the owned sessions
+      uint16_t out[C > 1 ? kSS : 1][C > 1 ? K::vs : 8];  // this CTA's slice of the other sessions, before sending
+    } v;
+  } u;
+  bf16 x[kSR * kLdX];  // residual stream (row-major)
+  union Q {
+    bf16 qkv[K::qkv_elems];                                  // q | k | v of the CTA's heads
+    unsigned char lists[K::own][kListBytes];                 // sampler scratch
+  } q;
+  float red[C > 1 ? C : 1][kSR][C > 1 ? K::of : 1];  // FFN2 partial sums of the owned features, by sender
+  __align__(16) bf16 hb[K::vs];                       // head p bias, this CTA's vocabulary slice
+  int32_t tok[kSS][kPositions];
+  int32_t sess[kSS];
+  uint32_t flags[kSS];  // bit 0 unfinished, bit 1 finished, bit 2 forbid_eos
+  uint32_t nf[kSS];     // non-finite guided logit in this CTA's vocabulary slice, per session
+  uint32_t peer_nf[C][K::own];
+  int64_t ctr[K::own];
+  int64_t seed[K::own];
+  int32_t inv[K::own];
+  int32_t last_issued[kSlots];
+  int32_t n_sess;
+  int32_t err;
+  int32_t producer_done;
+  int32_t mma_done;
+  uint32_t tmem;
+  unsigned long long full[kSlots];
+  unsigned long long empty[kSlots];
+  unsigned long long dfull[2];
+  unsigned long long dempty[2];
+  unsigned long long opready;
+  unsigned long long mmafin;
+  unsigned long long xbar[2];
+};
+
+template <int C>
+constexpr size_t split_smem_bytes() {
+  return sizeof(SplitSmem<C>) + 1024;
+}
+static_assert(split_smem_bytes<1>() <= 232448 && split_smem_bytes<2>() <= 232448 && split_smem_bytes<4>() <= 232448,
+              "split kernel shared memory");
+
+template <int C>
+__device__ __forceinline__ int err_flag(const SplitSmem<C>& sm) {
+  return *reinterpret_cast<const volatile int*>(&sm.err);
+}
+__device__ __forceinline__ void cbar() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+
+// Byte offset of element (row r, column k) of a 16-row operand stored as
+// 64-column panels with the 128-byte swizzle.
+__device__ __forceinline__ int op_off(int r, int k) {
+  return (k >> 6) * (kOpPanel * 2) + r * 128 + ((((k & 63) >> 3) ^ (r & 7)) << 4) + ((k & 7) << 1);
+}
+__device__ __forceinline__ void op_store(bf16* base, int r, int k, bf16 v) {
+  *reinterpret_cast<bf16*>(reinterpret_cast<unsigned char*>(base) + op_off(r, k)) = v;
+}
+// 16-byte unit (8 columns from k, k % 8 == 0).
+__device__ __forceinline__ uint4* op_unit(bf16* base, int r, int k) {
+  return reinterpret_cast<uint4*>(reinterpret_cast<unsigned char*>(base) + op_off(r, k));
+}
+
+// ---------------------------------------------------------------------------
+// the per-position GEMM schedule (producer and MMA warp walk it in the same order)
+// ---------------------------------------------------------------------------
+
+__device__ __forceinline__ bool has_in_projection(bool folded, int p) { return p == 0 || !folded; }
+
+template <int C>
+__device__ __forceinline__ int gemm_blocks(int g) {
+  using K = Cfg<C>;
+  switch (g) {
+    case G_IN: return 2;
+    case G_QKV: return K::nq;
+    case G_O: return K::no;
+    case G_F1: return K::nf1;
+    case G_F2: return 2;
+    default: return K::nhb;
+  }
+}
+
+template <int C>
+__device__ __forceinline__ int gemm_kchunks(int g) {
+  return g == G_IN ? kEmbed / kChunkK : (g == G_F2 ? Cfg<C>::f1 / kChunkK : kD / kChunkK);
+}
+
+// Weight rows of the head group gi (q groups, then k, then v; nh per type).
+template <int C>
+__device__ __forceinline__ int qkv_group_row(int c, int gi) {
+  using K = Cfg<C>;
+  return kD * (gi / K::nh) + kHeadDim * (c * K::nh + gi % K::nh);
+}
+
+// Tensor map and origins of chunk (M-block b, K-chunk k) of GEMM g: K column
+// x0, rows ra (A rows 0..63) and rb (A rows 64..127).
+template <int C>
+__device__ __forceinline__ const CUtensorMap* chunk_box(const SplitMaps& m, int c, int p, int g, int b, int k, int* x0,
+                                                        int* ra, int* rb) {
+  using K = Cfg<C>;
+  *x0 = kChunkK * k;
+  switch (g) {
+    case G_IN:
+      *ra = 128 * b;
+      *rb = 128 * b + 64;
+      return &m.in_proj;
+    case G_QKV: {
+      const int ga = 2 * b, gb = 2 * b + 1 < 3 * K::nh ? 2 * b + 1 : 2 * b;
+      *ra = qkv_group_row<C>(c, ga);
+      *rb = qkv_group_row<C>(c, gb);
+      return &m.qkv;
+    }
+    case G_O: {
+      const int base = K::of * c + 128 * b;
+      *ra = base;
+      *rb = K::of >= 128 ? base + 64 : base;
+      return &m.o;
+    }
+    case G_F1: {
+      const int base = K::f1 * c + 128 * b;
+      *ra = base;
+      *rb = base + 64;
+      return &m.ffn1;
+    }
+    case G_F2:
+      *x0 = K::f1 * c + kChunkK * k;
+      *ra = 128 * b;
+      *rb = 128 * b + 64;
+      return &m.ffn2;
+    default: {
+      const int base = p * kVocab + K::vs * c + 128 * b;  // the last block may overhang (ignored / zero fill)
+      *ra = base;
+      *rb = base + 64;
+      return &m.head;
+    }
+  }
+}
+
+template <int C>
+__device__ void producer(SplitSmem<C>& sm, const SplitMaps& maps, int c, bool folded) {
+  int it = 0;
+  for (int p = 0; p < kPositions; ++p) {
+    for (int g = has_in_projection(folded, p) ? G_IN : G_QKV; g <= G_HEAD; ++g) {
+      const int nb = gemm_blocks<C>(g), nk = gemm_kchunks<C>(g);
+      for (int b = 0; b < nb; ++b) {
+        for (int k = 0; k < nk; ++k, ++it) {
+          const int slot = it % kSlots;
+          if (it >= kSlots && err_flag(sm) == 0 && !mbar_wait(&sm.empty[slot], ((it / kSlots) - 1) & 1)) sm.err = 1;
+          if (err_flag(sm)) return;
+          int x0, ra, rb;
+          const CUtensorMap* map = chunk_box<C>(maps, c, p, g, b, k, &x0, &ra, &rb);
+          mbar_expect_tx(&sm.full[slot], kChunkBytes);
+          bf16* dst = sm.ring[slot];
+          tma_load_2d(dst, map, x0, ra, &sm.full[slot]);
+          tma_load_2d(dst + kBoxRows * 64, map, x0, rb, &sm.full[slot]);
+          tma_load_2d(dst + kPanelElems, map, x0 + 64, ra, &sm.full[slot]);
+          tma_load_2d(dst + kPanelElems + kBoxRows * 64, map, x0 + 64, rb, &sm.full[slot]);
+          sm.last_issued[slot] = it;
+        }
+      }
+    }
+  }
+}
+
+template <int C>
+__device__ __forceinline__ const bf16* gemm_operand(SplitSmem<C>& sm, int g) {
+  switch (g) {
+    case G_IN: return sm.u.src;
+    case G_QKV: return sm.xa;
+    case G_O: return sm.ab;
+    case G_F1: return sm.xa;
+    case G_F2: return sm.u.hid;
+    default: return sm.ab;
+  }
+}
+
+// The MMA warp's single thread: for every GEMM, wait until the consumers have
+// written its B operand, then per M-block wait for a free accumulator buffer,
+// per chunk wait for the weights, issue 8 MMAs (K = 128) and free the slot.
+template <int C>
+__device__ void mma_issuer(SplitSmem<C>& sm, bool folded) {
+  int it = 0, mb = 0, gn = 0;
+  for (int p = 0; p < kPositions && err_flag(sm) == 0; ++p) {
+    for (int g = has_in_projection(folded, p) ? G_IN : G_QKV; g <= G_HEAD && err_flag(sm) == 0; ++g, ++gn) {
+      if (!mbar_wait(&sm.opready, gn & 1)) {
+        sm.err = 1;
+        break;
+      }
+      tmem_fence_after_sync();
+      const bf16* bop = gemm_operand(sm, g);
+      const int nb = gemm_blocks<C>(g), nk = gemm_kchunks<C>(g);
+      for (int b = 0; b < nb && err_flag(sm) == 0; ++b, ++mb) {
+        const int db = mb & 1;
+        if (mb >= 2 && !mbar_wait(&sm.dempty[db], ((mb >> 1) - 1) & 1)) {
+          sm.err = 1;
+          break;
+        }
+        tmem_fence_after_sync();
+        const uint32_t d = sm.tmem + dcol(db);
+        for (int k = 0; k < nk; ++k, ++it) {
+          const int slot = it % kSlots;
+          if (!mbar_wait(&sm.full[slot], (it / kSlots) & 1)) {
+            sm.err = 1;
+            break;
+          }
+          tmem_fence_after_sync();
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk) {
+            const uint64_t a = umma_desc_sw128(sm.ring[slot] + (kk >> 2) * kPanelElems) + 2 * (kk & 3);
+            const uint64_t bd = umma_desc_sw128(bop + (2 * k + (kk >> 2)) * kOpPanel) + 2 * (kk & 3);
+            umma_bf16(d, a, bd, kIdesc, (k | kk) != 0);
+          }
+          umma_commit(&sm.empty[slot]);
+        }
+        umma_commit(&sm.dfull[db]);
+      }
+    }
+  }
+  // every MMA this thread issued has completed before the CTA frees TMEM
+  umma_commit(&sm.mmafin);
+  mbar_wait(&sm.mmafin, 0);
+  atomicExch(&sm.mma_done, 1);
+}
+
+// Epilogue helpers: warp w reads TMEM lanes [32 (w % 4), +32) (A rows m),
+// columns of sessions [4 (w / 4), +4): v[i] = row 4 (w / 4) + i (conditional),
+// v[4 + i] = row 8 + 4 (w / 4) + i (unconditional).
+template <int C>
+__device__ __forceinline__ void load_block(SplitSmem<C>& sm, int mb, float (&v)[8]) {
+  const int warp = threadIdx.x >> 5;
+  const int db = mb & 1;
+  if (err_flag(sm) == 0 && !mbar_wait(&sm.dfull[db], (mb >> 1) & 1)) sm.err = 1;
+  tmem_fence_after_sync();
+  const uint32_t ta = sm.tmem + (static_cast<uint32_t>(32 * (warp & 3)) << 16) + dcol(db) + 4 * (warp >> 2);
+  uint32_t r[8];
+  tmem_ld4x2(r, ta, ta + 8);
+  tmem_fence_before_sync();
+  __syncwarp();
+  if ((threadIdx.x & 31) == 0) mbar_arrive(&sm.dempty[db]);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ int epi_row(int i) {
+  const int sh = (threadIdx.x >> 5) >> 2;
+  return i < 4 ? 4 * sh + i : 8 + 4 * sh + (i - 4);
+}
+
+// B operand written: order the generic writes before the MMA warp's reads.
+template <int C>
+__device__ __forceinline__ void operand_ready(SplitSmem<C>& sm) {
+  fence_proxy_async();
+  cbar();
+  if (threadIdx.x == 0) mbar_arrive(&sm.opready);
+}
+
+// LayerNorm (no bias, eps 1e-5) of the 16 rows of x into the B operand xa;
+// lane holds weights g of columns [8 lane, +8); warp w: rows 2w, 2w+1.
+__device__ __forceinline__ void layer_norm_op(const bf16* x, bf16* xa, const float (&g)[8]) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int rr = 0; rr < 2; ++rr) {
+    const int r = 2 * warp + rr;
+    float v[8];
+    unpack8(*reinterpret_cast<const uint4*>(x + r * kLdX + lane * 8), v);
+    float sum = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) sum += v[j];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    const float mean = sum / static_cast<float>(kD);
+    float var = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) var += (v[j] - mean) * (v[j] - mean);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) var += __shfl_xor_sync(0xffffffffu, var, o);
+    const float rstd = 1.0f / sqrtf(var / static_cast<float>(kD) + 1.0e-5f);
+    float out[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) out[j] = ((v[j] - mean) * rstd) * g[j];
+    *op_unit(xa, r, lane * 8) = pack8(out);
+  }
+}
+
+// x (row-major) -> the B operand ab (the head's input).
+__device__ __forceinline__ void x_to_operand(const bf16* x, bf16* ab) {
+  for (int i = threadIdx.x; i < kSR * (kD / 8); i += kSC) {
+    const int r = i / (kD / 8), k8 = 8 * (i % (kD / 8));
+    *op_unit(ab, r, k8) = *reinterpret_cast<const uint4*>(x + r * kLdX + k8);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// exchange rounds
+// ---------------------------------------------------------------------------
+
+// Arrive on every CTA's barrier of round rd (announcing the bytes pushed to
+// each peer), then wait for this CTA's round to complete.
+template <int C, typename Bytes>
+__device__ __forceinline__ void finish_round(SplitSmem<C>& sm, uint32_t& rd, int c, Bytes bytes_to) {
+  cbar();
+  const int bar = static_cast<int>(rd & 1u);
+  if (threadIdx.x == 0) {
+#pragma unroll
+    for (int j = 0; j < C; ++j) {
+      if (j != c) remote_arrive_expect(cluster_addr(&sm.xbar[bar], j), bytes_to(j));
+    }
+    mbar_arrive(&sm.xbar[bar]);
+  }
+  if (err_flag(sm) == 0 && !mbar_wait(&sm.xbar[bar], (rd >> 1) & 1u)) sm.err = 1;
+  ++rd;
+}
+
+// ---------------------------------------------------------------------------
+// attention over the TMEM KV cache for the CTA's heads: warp w, local head
+// lh = w % 4 (< nh), part = w / 4 (positions of parity part); thread t: row
+// t / 2, head dims [32 (t % 2), +32).  Output to the operand ab at the global
+// head's columns, and pushed to every peer.
+// ---------------------------------------------------------------------------
+
+template <int C>
+__device__ __forceinline__ void attention(SplitSmem<C>& sm, int p, int c, uint32_t rd) {
+  using K = Cfg<C>;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int lh = warp & 3, part = warp >> 2;
+  const bool active = lh < K::nh;
+  const int r = lane >> 1, half = lane & 1;
+  const uint32_t tl = sm.tmem + (static_cast<uint32_t>(32 * lh) << 16);
+  const bf16* qrow = sm.q.qkv + r * K::ldq + kHeadDim * lh + 32 * half;
+  const bf16* krow = qrow + K::nh * kHeadDim;
+  const bf16* vrow = krow + K::nh * kHeadDim;
+  float q[32];
+  if (active) {
+    if (p < kPositions - 1) {  // append k (part 0) or v (part 1) of position p
+      const bf16* src = part == 0 ? krow : vrow;
+      uint32_t kv[16];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const uint4 t = *reinterpret_cast<const uint4*>(src + 8 * j);
+        kv[4 * j] = t.x;
+        kv[4 * j + 1] = t.y;
+        kv[4 * j + 2] = t.z;
+        kv[4 * j + 3] = t.w;
+      }
+      tmem_st16(tl + 256 * part + 16 * tmem_block(p), kv);
+      tmem_wait_st();
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float f8[8];
+      unpack8(*reinterpret_cast<const uint4*>(qrow + 8 * j), f8);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) q[8 * j + e] = f8[e];
+    }
+  }
+  tmem_fence_before_sync();
+  cbar();
+  tmem_fence_after_sync();
+
+  float s[8];
+#pragma unroll
+  for (int m = 0; m < 8; ++m) s[m] = -CUDART_INF_F;
+  if (active) {
+#pragma unroll
+    for (int g4 = 0; g4 < 2; ++g4) {
+      if (8 * g4 + part <= p) {
+        uint32_t k[64];
+        tmem_ld64(k, tl + 16 * (8 * part + 4 * g4));
+        if (p == kPositions - 1 && part == 1 && g4 == 1) {  // position 15: k from shared memory
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const uint4 t = *reinterpret_cast<const uint4*>(krow + 8 * j);
+            k[48 + 4 * j] = t.x;
+            k[48 + 4 * j + 1] = t.y;
+            k[48 + 4 * j + 2] = t.z;
+            k[48 + 4 * j + 3] = t.w;
+          }
+        }
+#pragma unroll
+        for (int jj = 0; jj < 4; ++jj) {
+          float dot = 0.f;
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            const float2 t = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&k[16 * jj + e]));
+            dot = fmaf(q[2 * e], t.x, dot);
+            dot = fmaf(q[2 * e + 1], t.y, dot);
+          }
+          dot += __shfl_xor_sync(0xffffffffu, dot, 1);
+          if (2 * (4 * g4 + jj) + part <= p) s[4 * g4 + jj] = round_bf16(__fmul_rn(round_bf16(dot), 0.125f));
+        }
+      }
+    }
+    float* my_s = sm.u.att.s[part][lh][lane];
+#pragma unroll
+    for (int m = 0; m < 8; ++m) my_s[m] = s[m];
+  }
+  cbar();
+  float o[32];
+#pragma unroll
+  for (int d = 0; d < 32; ++d) o[d] = 0.f;
+  if (active) {
+    float all[kPositions];
+#pragma unroll
+    for (int m = 0; m < 8; ++m) {
+      all[2 * m] = sm.u.att.s[0][lh][lane][m];
+      all[2 * m + 1] = sm.u.att.s[1][lh][lane][m];
+    }
+    float mx = all[0];
+#pragma unroll
+    for (int j = 1; j < kPositions; ++j) mx = fmaxf(mx, all[j]);
+    float sum = 0.f;
+#pragma unroll
+    for (int j = 0; j < kPositions; ++j) {
+      all[j] = j <= p ? expf(all[j] - mx) : 0.f;
+      sum += all[j];
+    }
+#pragma unroll
+    for (int g4 = 0; g4 < 2; ++g4) {
+      if (8 * g4 + part <= p) {
+        uint32_t v[64];
+        tmem_ld64(v, tl + 256 + 16 * (8 * part + 4 * g4));
+        if (p == kPositions - 1 && part == 1 && g4 == 1) {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const uint4 t = *reinterpret_cast<const uint4*>(vrow + 8 * j);
+            v[48 + 4 * j] = t.x;
+            v[48 + 4 * j + 1] = t.y;
+            v[48 + 4 * j + 2] = t.z;
+            v[48 + 4 * j + 3] = t.w;
+          }
+        }
+#pragma unroll
+        for (int jj = 0; jj < 4; ++jj) {
+          const int j = 2 * (4 * g4 + jj) + part;
+          if (j <= p) {
+            const float prob = round_bf16(all[j] / sum);
+#pragma unroll
+            for (int d = 0; d < 16; ++d) {
+              const float2 t = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&v[16 * jj + d]));
+              o[2 * d] = fmaf(prob, t.x, o[2 * d]);
+              o[2 * d + 1] = fmaf(prob, t.y, o[2 * d + 1]);
+            }
+          }
+        }
+      }
+    }
+    if (part == 1) {
+      float* dst = sm.u.att.o[lh][lane];
+#pragma unroll
+      for (int d = 0; d < 32; ++d) dst[d] = o[d];
+    }
+  }
+  cbar();
+  if (active && part == 0) {
+    const float* src = sm.u.att.o[lh][lane];
+#pragma unroll
+    for (int d = 0; d < 32; ++d) o[d] += src[d];
+    const int col = kHeadDim * (c * K::nh + lh) + 32 * half;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float f8[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) f8[e] = o[8 * j + e];
+      const uint4 u = pack8(f8);
+      uint4* dst = op_unit(sm.ab, r, col + 8 * j);
+      *dst = u;
+      if constexpr (C > 1) {
+#pragma unroll
+        for (int jc = 0; jc < C; ++jc) {
+          if (jc != c) st_async_v4(cluster_addr(dst, jc), u, cluster_addr(&sm.xbar[rd & 1u], jc));
+        }
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// the kernel
+// ---------------------------------------------------------------------------
+
+template <int C>
+__device__ __forceinline__ int64_t input_token(const Frame& f, const SplitSmem<C>& sm, int slot, int p) {
+  if (f.forced) {
+    const int64_t t = f.forced[static_cast<int64_t>(sm.sess[slot]) * kPositions + p];
+    return t < 0 ? 0 : (t >= kVocab ? kVocab - 1 : t);
+  }
+  return sm.tok[slot][p];
+}
+
+template <int C>
+__global__ void __launch_bounds__(kSThreads, 1) split_frame_kernel(Frame f, const __grid_constant__ SplitMaps maps) {
+  using K = Cfg<C>;
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  const uint32_t pad = (1024u - (smem_addr(smem_raw) & 1023u)) & 1023u;
+  SplitSmem<C>& sm = *reinterpret_cast<SplitSmem<C>*>(smem_raw + pad);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int rp = f.rp;
+  const bool folded = f.emb_proj != nullptr;
+  int c = 0;
+  if constexpr (C > 1) c = static_cast<int>(cg::this_cluster().block_rank());
+  const int tile = static_cast<int>(blockIdx.x) / C;
+
+  // ---- sessions [8 tile, +8) of the active list (every CTA of the cluster)
+  if (warp == 0) {
+    int seen = 0;
+    const int first = kSS * tile;
+    for (int base = 0; base < f.n; base += 32) {
+      const int s = base + lane;
+      const bool act = s < f.n && (f.active == nullptr || f.active[s]);
+      const unsigned m = __ballot_sync(0xffffffffu, act);
+      const int rank = seen + __popc(m & ((1u << lane) - 1u));
+      if (act && rank >= first && rank < first + kSS) sm.sess[rank - first] = s;
+      seen += __popc(m);
+    }
+    if (lane == 0) {
+      const int left = seen - first;
+      sm.n_sess = left <= 0 ? 0 : (left < kSS ? left : kSS);
+      sm.err = 0;
+      sm.producer_done = 0;
+      sm.mma_done = 0;
+    }
+  }
+  __syncthreads();
+  const int n_sess = sm.n_sess;
+  if (n_sess == 0) return;  // the same in every CTA of the cluster: none touches another
+  auto live = [&](int r) { return (r & 7) < n_sess && (r >> 3) < rp; };
+  const int own0 = K::own * c;
+  const int n_own = n_sess - own0 <= 0 ? 0 : (n_sess - own0 < K::own ? n_sess - own0 : K::own);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kSlots; ++s) {
+      mbar_init(&sm.full[s], 1);
+      mbar_init(&sm.empty[s], 1);
+      sm.last_issued[s] = -1;
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&sm.dfull[b], 1);
+      mbar_init(&sm.dempty[b], kSW);
+      mbar_init(&sm.xbar[b], C);
+    }
+    mbar_init(&sm.opready, 1);
+    mbar_init(&sm.mmafin, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncwarp();
+  if (warp == 0) {
+    tmem_alloc(&sm.tmem, 512);
+    tmem_relinquish();
+  }
+  if (threadIdx.x < n_sess) {
+    const int sid = sm.sess[threadIdx.x];
+    sm.flags[threadIdx.x] = (f.unfinished[sid] ? 1u : 0u) | (f.finished[sid] ? 2u : 0u) | (f.forbid[sid] ? 4u : 0u);
+  }
+  if (threadIdx.x < n_own) {  // per-session state and EOS registration of the owned sessions
+    const int ls = threadIdx.x;
+    const int sid = sm.sess[own0 + ls];
+    sm.ctr[ls] = f.counter_io[sid];
+    sm.seed[ls] = f.seed[sid];
+    int32_t inv = 0;
+    bool en = !f.unfinished[sid] && !f.finished[sid] && !f.forbid[sid];
+    if (en && f.final_w == nullptr) {
+      inv = 2;
+      en = false;
+    }
+    sm.inv[ls] = inv;
+    if (en) {
+      const int slot = atomicAdd(f.eos_count, 1);
+      f.eos_list[slot] = sid;
+      f.eos_slot[sid] = slot;
+    } else {
+      f.eos_slot[sid] = -1;
+    }
+  }
+  tmem_fence_before_sync();
+  __syncthreads();
+  tmem_fence_after_sync();
+  if constexpr (C > 1) cg::this_cluster().sync();  // every CTA's barriers exist before any push
+
+  if (warp >= kSW) {  // control warpgroup
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kSProducerRegs));
+    if (warp == kSW && lane == 0) {
+      producer<C>(sm, maps, c, folded);
+      // no copy may still be writing when the CTA leaves
+      for (int s = 0; s < kSlots; ++s) {
+        const int last = sm.last_issued[s];
+        if (last >= 0) mbar_wait(&sm.full[s], (last / kSlots) & 1);
+      }
+      atomicExch(&sm.producer_done, 1);
+    } else if (warp == kSW + 1 && lane == 0) {
+      mma_issuer<C>(sm, folded);
+    }
+    return;
+  }
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kSConsumerRegs));
+  {
+    float g1[8], g2[8];
+    unpack8(*reinterpret_cast<const uint4*>(f.ln1 + lane * 8), g1);
+    unpack8(*reinterpret_cast<const uint4*>(f.ln2 + lane * 8), g2);
+    const int q4 = warp & 3, sh = warp >> 2;
+    const int m_lane = 32 * q4 + lane;  // A row of an M-block held by this thread
+    const bool cfg = rp == 2;
+    const float cfg_scale = f.prm.cfg_scale, uncond_scale = __fsub_rn(1.0f, f.prm.cfg_scale);
+    int mb = 0;       // M-blocks consumed
+    uint32_t rd = 0;  // exchange rounds
+    for (int p = 0; p < kPositions; ++p) {
+      // ---------------- input rows
+      if (has_in_projection(folded, p)) {
+        for (int i = threadIdx.x; i < kSR * (kEmbed / 8); i += kSC) {
+          const int r = i / (kEmbed / 8), k8 = 8 * (i % (kEmbed / 8));
+          uint4 v = make_uint4(0, 0, 0, 0);
+          if (live(r)) {
+            const int slot = r & 7, sub = r >> 3;
+            const bf16* src;
+            if (p == 0) {
+              src = f.hidden + (static_cast<int64_t>(sm.sess[slot]) * rp + sub) * kEmbed;
+            } else {
+              src = f.emb + (static_cast<int64_t>(p - 1) * kVocab + input_token(f, sm, slot, p - 1)) * kEmbed;
+            }
+            v = *reinterpret_cast<const uint4*>(src + k8);
+          }
+          *op_unit(sm.u.src, r, k8) = v;
+        }
+        operand_ready(sm);
+        const bf16* pos = f.pos + static_cast<int64_t>(p) * kD;
+        for (int b = 0; b < 2; ++b, ++mb) {
+          float v[8];
+          load_block(sm, mb, v);
+          const int n = 128 * b + m_lane;
+          const float bias = bf2f(f.in_b[n]), pe = bf2f(pos[n]);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const float y = round_bf16(__fadd_rn(v[i], bias));
+            sm.x[epi_row(i) * kLdX + n] = f2bf(__fadd_rn(y, pe));
+          }
+        }
+      }
+      // head p bias slice; per-position flags
+      {
+        const bf16* hbp = f.head_b + static_cast<int64_t>(p) * kVocab;
+        for (int i = threadIdx.x; i < K::vs / 8; i += kSC) {
+          const int v0 = K::vs * c + 8 * i;
+          uint4 u = make_uint4(0, 0, 0, 0);
+          if (v0 < kVocab) u = *reinterpret_cast<const uint4*>(hbp + v0);  // kVocab % 8 == 0
+          *reinterpret_cast<uint4*>(sm.hb + 8 * i) = u;
+        }
+        if (threadIdx.x < kSS) sm.nf[threadIdx.x] = 0;
+      }
+      cbar();
+
+      // ---------------- LN1, qkv of the CTA's heads
+      layer_norm_op(sm.x, sm.xa, g1);
+      operand_ready(sm);
+      for (int b = 0; b < K::nq; ++b, ++mb) {
+        float v[8];
+        load_block(sm, mb, v);
+        const int gi = 2 * b + (m_lane >> 6);
+        if (gi < 3 * K::nh) {
+          const int col = kHeadDim * gi + (m_lane & 63);  // (type, local head) major, as the staging layout
+#pragma unroll
+          for (int i = 0; i < 8; ++i) sm.q.qkv[epi_row(i) * K::ldq + col] = f2bf(v[i]);
+        }
+      }
+      cbar();
+
+      // ---------------- attention (R1: the heads' outputs to every CTA)
+      attention<C>(sm, p, c, rd);
+      if constexpr (C > 1) {
+        finish_round(sm, rd, c, [](int) { return static_cast<uint32_t>(kSR * kHeadDim * K::nh * 2); });
+        fence_proxy_async();
+      }
+      operand_ready(sm);
+
+      // ---------------- o-projection + residual (R2: the CTA's features to every CTA)
+      for (int b = 0; b < K::no; ++b, ++mb) {
+        float v[8];
+        load_block(sm, mb, v);
+        const int nl = 128 * b + m_lane;
+        if (nl < K::of) {
+          const int n = K::of * c + nl;
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            bf16* xr = sm.x + epi_row(i) * kLdX + n;
+            *xr = f2bf(__fadd_rn(bf2f(*xr), round_bf16(v[i])));
+          }
+        }
+      }
+      cbar();
+      if constexpr (C > 1) {
+        // rows of the owned feature slice, 16-byte units
+        constexpr int upr = K::of / 8;
+        for (int i = threadIdx.x; i < kSR * upr; i += kSC) {
+          const int r = i / upr, k8 = K::of * c + 8 * (i % upr);
+          const uint4* src = reinterpret_cast<const uint4*>(sm.x + r * kLdX + k8);
+          const uint4 u = *src;
+#pragma unroll
+          for (int j = 0; j < C; ++j) {
+            if (j != c) st_async_v4(cluster_addr(src, j), u, cluster_addr(&sm.xbar[rd & 1u], j));
+          }
+        }
+        finish_round(sm, rd, c, [](int) { return static_cast<uint32_t>(kSR * K::of * 2); });
+      }
+
+      // ---------------- LN2, FFN1 + GELU
+      layer_norm_op(sm.x, sm.xa, g2);
+      operand_ready(sm);
+      for (int b = 0; b < K::nf1; ++b, ++mb) {
+        float v[8];
+        load_block(sm, mb, v);
+        const int fl = 128 * b + m_lane;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) op_store(sm.u.hid, epi_row(i), fl, f2bf(gelu_tanh(round_bf16(v[i]))));
+      }
+      operand_ready(sm);
+
+      // ---------------- FFN2 (+ R3 reduce-scatter, R4 all-gather) + residual
+      for (int b = 0; b < 2; ++b, ++mb) {
+        float v[8];
+        load_block(sm, mb, v);
+        const int n = 128 * b + m_lane;
+        if constexpr (C == 1) {
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            bf16* xr = sm.x + epi_row(i) * kLdX + n;
+            *xr = f2bf(__fadd_rn(bf2f(*xr), round_bf16(v[i])));
+          }
+        } else {
+          const int owner = n / K::of, nl = n % K::of;
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            float* dst = &sm.red[c][epi_row(i)][nl];
+            if (owner == c) {
+              *dst = v[i];
+            } else {
+              st_async_b32(cluster_addr(dst, owner), __float_as_uint(v[i]), cluster_addr(&sm.xbar[rd & 1u], owner));
+            }
+          }
+        }
+      }
+      if constexpr (C > 1) {
+        finish_round(sm, rd, c, [](int) { return static_cast<uint32_t>(kSR * K::of * 4); });
+        constexpr int upr = K::of / 8;
+        for (int i = threadIdx.x; i < kSR * upr; i += kSC) {
+          const int r = i / upr, k8 = 8 * (i % upr);
+          float s8[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) s8[e] = 0.f;
+#pragma unroll
+          for (int j = 0; j < C; ++j) {
+#pragma unroll
+            for (int e = 0; e < 8; ++e) s8[e] += sm.red[j][r][k8 + e];
+          }
+          uint4* xr = reinterpret_cast<uint4*>(sm.x + r * kLdX + K::of * c + k8);
+          float xv[8];
+          unpack8(*xr, xv);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) xv[e] = __fadd_rn(xv[e], round_bf16(s8[e]));
+          const uint4 u = pack8(xv);
+          *xr = u;
+#pragma unroll
+          for (int j = 0; j < C; ++j) {
+            if (j != c) st_async_v4(cluster_addr(xr, j), u, cluster_addr(&sm.xbar[rd & 1u], j));
+          }
+        }
+        finish_round(sm, rd, c, [](int) { return static_cast<uint32_t>(kSR * K::of * 2); });
+      } else {
+        cbar();
+      }
+      x_to_operand(sm.x, sm.ab);
+      operand_ready(sm);
+
+      // ---------------- head p: bias, CFG combine, constraints (R5: values to the owners)
+      {
+        bf16* lo_base = f.logits_out;
+        for (int b = 0; b < K::nhb; ++b, ++mb) {
+          float v[8];
+          load_block(sm, mb, v);
+          const int vl = 128 * b + m_lane;
+          const int t = K::vs * c + vl;
+          const bool in_vocab = t < kVocab;
+          const float bias = bf2f(sm.hb[vl]);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int slot = 4 * sh + i;
+            bool nfs = false;
+            if (in_vocab && slot < n_sess) {
+              const __nv_bfloat16 cb = f2bf(__fadd_rn(v[i], bias));
+              const __nv_bfloat16 ub = f2bf(__fadd_rn(v[4 + i], bias));
+              if (lo_base) {
+                bf16* lr = lo_base + (static_cast<int64_t>(sm.sess[slot]) * kPositions + p) * rp * kVocab;
+                lr[t] = cb;
+                if (cfg) lr[kVocab + t] = ub;
+              }
+              uint32_t g = __bfloat16_as_ushort(cb);
+              if (cfg) {
+                const float sc = round_bf16(__fmul_rn(bf2f(cb), cfg_scale));
+                g = __bfloat16_as_ushort(f2bf(__fadd_rn(sc, __fmul_rn(bf2f(ub), uncond_scale))));
+              }
+              const uint32_t fl = sm.flags[slot];
+              const uint16_t val =
+                  static_cast<uint16_t>(constrain(g, t, fl & 1u, (fl & 2u) != 0, (fl & 4u) != 0, nfs));
+              const int owner = slot / K::own;
+              if (owner == c) {
+                sm.u.v.own[slot - own0][t] = val;
+              } else {
+                sm.u.v.out[slot][vl] = val;
+              }
+            }
+            if (__any_sync(0xffffffffu, nfs) && lane == 0) atomicOr(&sm.nf[slot], 1u);
+          }
+        }
+        cbar();
+        if constexpr (C > 1) {
+          // the other CTAs' sessions: this CTA's vocabulary slice of each, and its non-finite flags
+          constexpr int full_units = K::vs / 8;
+          const int len = (K::vs * (c + 1) <= kVocab ? K::vs : kVocab - K::vs * c);  // multiple of 8
+          const int units = len / 8;
+          const int n_other = kSS - K::own;
+          for (int i = threadIdx.x; i < n_other * full_units; i += kSC) {
+            const int oi = i / full_units, u = i % full_units;
+            if (u < units) {
+              const int slot = oi < own0 ? oi : oi + K::own;  // skip the owned slots
+              const int owner = slot / K::own;
+              const uint4 val = *reinterpret_cast<const uint4*>(&sm.u.v.out[slot][8 * u]);
+              st_async_v4(cluster_addr(&sm.u.v.own[slot - K::own * owner][K::vs * c + 8 * u], owner), val,
+                          cluster_addr(&sm.xbar[rd & 1u], owner));
+            }
+          }
+          if (threadIdx.x < kSS) {
+            const int slot = threadIdx.x;
+            const int owner = slot / K::own;
+            if (owner != c) {
+              st_async_b32(cluster_addr(&sm.peer_nf[c][slot - K::own * owner], owner), sm.nf[slot],
+                           cluster_addr(&sm.xbar[rd & 1u], owner));
+            }
+          }
+          finish_round(sm, rd, c, [&](int) { return static_cast<uint32_t>(K::own * (len * 2 + 4)); });
+        }
+      }
+
+      // ---------------- sampling: warp w samples owned session w (R6: the token to every CTA)
+      if (warp < n_own) {
+        const int ls = warp, slot = own0 + ls;
+        uint32_t nfs = sm.nf[slot];
+        if constexpr (C > 1) {
+#pragma unroll
+          for (int j = 0; j < C; ++j) {
+            if (j != c) nfs |= sm.peer_nf[j][ls];
+          }
+        }
+        RowSample rs;
+        rs.vals = sm.u.v.own[ls];
+        rs.flags = sm.flags[slot];
+        rs.nonfinite = nfs != 0;
+        rs.seed = sm.seed[ls];
+        rs.counter = sm.ctr[ls];
+        uint16_t* list = reinterpret_cast<uint16_t*>(sm.q.lists[ls]);
+        int invalid = 0;
+        const int token = sample_row(rs, f.prm, list, list + kListCap + 16, &invalid);
+        __syncwarp();
+        if (lane == 0) {
+          const int64_t counter = sm.ctr[ls];
+          sm.tok[slot][p] = token;
+          sm.inv[ls] |= invalid;
+          const bool counter_valid = counter >= 0 && counter <= kMaxCounter;
+          if (!f.prm.argmax && counter_valid) sm.ctr[ls] = counter + 1;
+          if constexpr (C > 1) {
+            if (p + 1 < kPositions) {
+#pragma unroll
+              for (int j = 0; j < C; ++j) {
+                if (j != c) {
+                  st_async_b32(cluster_addr(&sm.tok[slot][p], j), static_cast<uint32_t>(token),
+                               cluster_addr(&sm.xbar[rd & 1u], j));
+                }
+              }
+            }
+          }
+        }
+      }
+      if constexpr (C > 1) {
+        if (p + 1 < kPositions) {
+          // dead owned slots still announce their 4 bytes: push a zero token for them
+          if (threadIdx.x >= n_own && threadIdx.x < K::own) {
+            const int slot = own0 + threadIdx.x;
+            sm.tok[slot][p] = 0;
+#pragma unroll
+            for (int j = 0; j < C; ++j) {
+              if (j != c) st_async_b32(cluster_addr(&sm.tok[slot][p], j), 0u, cluster_addr(&sm.xbar[rd & 1u], j));
+            }
+          }
+          finish_round(sm, rd, c, [](int) { return static_cast<uint32_t>(K::own * 4); });
+        } else {
+          cbar();
+        }
+      } else {
+        cbar();
+      }
+
+      // ---------------- next input rows (folded tables), every CTA, all sessions
+      if (folded && p + 1 < kPositions && warp < n_sess) {
+        const int slot = warp;
+        const int64_t tin = input_token(f, sm, slot, p);
+        float e8[8], p8[8];
+        unpack8(*reinterpret_cast<const uint4*>(f.emb_proj + (static_cast<int64_t>(p) * kVocab + tin) * kD + lane * 8),
+                e8);
+        unpack8(*reinterpret_cast<const uint4*>(f.pos + static_cast<int64_t>(p + 1) * kD + lane * 8), p8);
+        float y[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) y[e] = __fadd_rn(e8[e], p8[e]);
+        const uint4 row = pack8(y);
+        *reinterpret_cast<uint4*>(sm.x + slot * kLdX + lane * 8) = row;
+        if (rp == 2) *reinterpret_cast<uint4*>(sm.x + (slot + 8) * kLdX + lane * 8) = row;
+      }
+      cbar();
+    }
+
+    // ---- commit (owned sessions): tokens, counters, flags, next-frame embedding
+    for (int i = threadIdx.x; i < n_own * kPositions; i += kSC) {
+      const int ls = i / kPositions, pp = i % kPositions;
+      const int slot = own0 + ls;
+      const int sid = sm.sess[slot];
+      const int32_t t = sm.tok[slot][pp];
+      f.codec_tokens[static_cast<int64_t>(sid) * kPositions + (pp % kCodebooks) * kFrames + pp / kCodebooks] = t;
+      f.tokens[static_cast<int64_t>(sid) * kPositions + pp] = t;
+    }
+    if (threadIdx.x < n_own) {
+      const int ls = threadIdx.x;
+      const int sid = sm.sess[own0 + ls];
+      f.counter_io[sid] = sm.ctr[ls];
+      f.invalid_rows[sid] = sm.inv[ls] | (err_flag(sm) ? 4 : 0);
+      if (f.eos_slot[sid] < 0) f.end_frame[sid] = f.finished[sid] ? 0 : -1;
+    }
+    for (int i = threadIdx.x; i < n_own * (kEmbed / 8); i += kSC) {
+      const int ls = i / (kEmbed / 8), k8 = 8 * (i % (kEmbed / 8));
+      const int slot = own0 + ls;
+      float acc[8];
+#pragma unroll
+      for (int pp = 0; pp < kPositions; ++pp) {
+        float v[8];
+        unpack8(*reinterpret_cast<const uint4*>(f.emb + (static_cast<int64_t>(pp) * kVocab + sm.tok[slot][pp]) * kEmbed +
+                                                k8),
+                v);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc[e] = pp == 0 ? v[e] : round_bf16(__fadd_rn(acc[e], v[e]));
+      }
+      float out[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) out[e] = __fdiv_rn(acc[e], 16.0f);
+      *reinterpret_cast<uint4*>(f.next_emb + static_cast<int64_t>(sm.sess[slot]) * kEmbed + k8) = pack8(out);
+    }
+
+    // ---- teardown: the control warps' copies and MMAs have finished (bounded)
+    if (threadIdx.x == 0) {
+      const unsigned long long t0 = global_ns();
+      while ((*reinterpret_cast<volatile int*>(&sm.producer_done) == 0 ||
+              *reinterpret_cast<volatile int*>(&sm.mma_done) == 0) &&
+             global_ns() - t0 < 20000000ull) {
+        __nanosleep(1000);
+      }
+    }
+    tmem_fence_before_sync();
+    cbar();
+    if (warp == 0) {
+      tmem_fence_after_sync();
+      tmem_dealloc(sm.tmem, 512);
+    }
+  }
+  if constexpr (C > 1) cg::this_cluster().sync();  // no CTA leaves while a peer may still push into it
+}
+
+template <int C>
+int split_clusters() {
+  static int cached = -1;  // per process
+  static std::mutex mu;
+  const std::lock_guard<std::mutex> lock(mu);
+  if (cached < 0) {
+    int clusters = 0;
+    if (cudaFuncSetAttribute(split_frame_kernel<C>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(split_smem_bytes<C>())) == cudaSuccess) {
+      if constexpr (C == 1) {
+        int blocks = 0;
+        int dev = 0, sms = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, split_frame_kernel<C>, kSThreads,
+                                                          split_smem_bytes<C>()) == cudaSuccess &&
+            cudaGetDevice(&dev) == cudaSuccess &&
+            cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && blocks >= 1) {
+          clusters = blocks * sms;
+        }
+      } else {
+        cudaLaunchConfig_t cfg = {};
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = C;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.gridDim = dim3(C);
+        cfg.blockDim = dim3(kSThreads);
+        cfg.dynamicSmemBytes = split_smem_bytes<C>();
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        if (cudaOccupancyMaxActiveClusters(&clusters, split_frame_kernel<C>, &cfg) != cudaSuccess) clusters = 0;
+      }
+    }
+    cudaGetLastError();
+    cached = clusters;
+  }
+  return cached;
+}
+
+template <int C>
+cudaError_t launch_split(const Frame& f, const SplitMaps& maps, cudaStream_t stream) {
+  const int tiles = (f.n + kSS - 1) / kSS;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = C;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.gridDim = dim3(tiles * C);
+  cfg.blockDim = dim3(kSThreads);
+  cfg.dynamicSmemBytes = split_smem_bytes<C>();
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, split_frame_kernel<C>, f, maps);
+}
+
+}  // namespace
+
+int split_frame_clusters(int split) {
+  switch (split) {
+    case 1: return split_clusters<1>();
+    case 2: return split_clusters<2>();
+    case 4: return split_clusters<4>();
+    default: return 0;
+  }
+}
+
+bool split_frame_supported(const Frame& f, int split) {
+  if (f.d != kD || f.H != kHeads || f.F != kF || f.L != 1 || !f.in_proj || (f.rp != 1 && f.rp != 2)) return false;
+  return split_frame_clusters(split) > 0;
+}
+
+cudaError_t launch_split_frame(const Frame& f, int split, cudaStream_t stream) {
+  SplitMaps maps;
+  if (!make_weight_map(&maps.in_proj, f.in_w, kEmbed, kD, kBoxRows) ||
+      !make_weight_map(&maps.qkv, f.qkv, kD, 3 * kD, kBoxRows) || !make_weight_map(&maps.o, f.o, kD, kD, kBoxRows) ||
+      !make_weight_map(&maps.ffn1, f.w1, kD, kF, kBoxRows) || !make_weight_map(&maps.ffn2, f.w2, kF, kD, kBoxRows) ||
+      !make_weight_map(&maps.head, f.head_w, kD, static_cast<uint64_t>(kPositions) * kVocab, kBoxRows)) {
+    return cudaErrorInvalidValue;
+  }
+  cudaError_t e = cudaMemsetAsync(f.eos_count, 0, sizeof(int32_t), stream);
+  if (e != cudaSuccess) return e;
+  switch (split) {
+    case 1: e = launch_split<1>(f, maps, stream); break;
+    case 2: e = launch_split<2>(f, maps, stream); break;
+    case 4: e = launch_split<4>(f, maps, stream); break;
+    default: return cudaErrorInvalidValue;
+  }
+  if (e != cudaSuccess) return e;
+  return launch_frame_eos(f, stream);
+}
+
+}  // namespace mtt

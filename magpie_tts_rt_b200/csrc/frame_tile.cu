@@ -807,6 +807,23 @@ bool tile_frame_supported(const Frame& f) {
   return cached == 1;
 }
 
+int tile_frame_clusters() {
+  Frame probe{};
+  probe.d = kTD;
+  probe.H = kTHeads;
+  probe.F = kTF;
+  probe.L = 1;
+  probe.in_proj = 1;
+  probe.rp = 2;
+  if (!tile_frame_supported(probe)) return 0;
+  int dev = 0, sms = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  return sms;  // one CTA per SM
+}
+
 cudaError_t launch_tile_frame(const Frame& f, cudaStream_t stream) {
   TileMaps maps;
   if (!make_weight_map(&maps.in_proj, f.in_w, kEmbed, kTD, kCRows) ||

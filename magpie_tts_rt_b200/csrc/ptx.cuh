@@ -1,7 +1,8 @@
 // Inline-PTX helpers shared by the fused frame kernels (sm_100a): shared and
 // cluster addressing, mbarriers with bounded waits, TMA tensor loads (no
-// multicast), st.async, ldmatrix / mma.sync, and the tcgen05 tensor-memory
-// (TMEM) allocation, load and store forms.
+// multicast), st.async, ldmatrix / mma.sync, the tcgen05 tensor-memory (TMEM)
+// allocation, load and store forms, and tcgen05.mma with shared-memory
+// descriptors.
 #pragma once
 
 #include <cuda.h>
@@ -175,6 +176,62 @@ __device__ __forceinline__ void tmem_ld64(uint32_t (&v)[64], uint32_t taddr) {
                : "r"(taddr)
                : "memory");
   asm volatile("tcgen05.wait::ld.sync.aligned;" : "+r"(v[0]),"+r"(v[1]),"+r"(v[2]),"+r"(v[3]),"+r"(v[4]),"+r"(v[5]),"+r"(v[6]),"+r"(v[7]),"+r"(v[8]),"+r"(v[9]),"+r"(v[10]),"+r"(v[11]),"+r"(v[12]),"+r"(v[13]),"+r"(v[14]),"+r"(v[15]),"+r"(v[16]),"+r"(v[17]),"+r"(v[18]),"+r"(v[19]),"+r"(v[20]),"+r"(v[21]),"+r"(v[22]),"+r"(v[23]),"+r"(v[24]),"+r"(v[25]),"+r"(v[26]),"+r"(v[27]),"+r"(v[28]),"+r"(v[29]),"+r"(v[30]),"+r"(v[31]),"+r"(v[32]),"+r"(v[33]),"+r"(v[34]),"+r"(v[35]),"+r"(v[36]),"+r"(v[37]),"+r"(v[38]),"+r"(v[39]),"+r"(v[40]),"+r"(v[41]),"+r"(v[42]),"+r"(v[43]),"+r"(v[44]),"+r"(v[45]),"+r"(v[46]),"+r"(v[47]),"+r"(v[48]),"+r"(v[49]),"+r"(v[50]),"+r"(v[51]),"+r"(v[52]),"+r"(v[53]),"+r"(v[54]),"+r"(v[55]),"+r"(v[56]),"+r"(v[57]),"+r"(v[58]),"+r"(v[59]),"+r"(v[60]),"+r"(v[61]),"+r"(v[62]),"+r"(v[63]) : : "memory");
+}
+
+
+// ---- tcgen05 MMA (cta_group::1, kind::f16: bf16 A and B, f32 accumulate in TMEM)
+
+// Shared-memory matrix descriptor of a K-major operand stored with the
+// 128-byte swizzle: rows of 128 bytes (64 bf16 of K), 8-row groups 1024
+// bytes apart (SBO), the group base 1024-byte aligned; the start address
+// advances by 32 bytes per 16-element K step inside the swizzle row.
+__device__ __forceinline__ uint64_t umma_desc_sw128(const void* p) {
+  const uint32_t a = smem_addr(p);
+  uint64_t d = static_cast<uint64_t>((a & 0x3FFFFu) >> 4);
+  d |= static_cast<uint64_t>(1) << 16;          // leading byte offset (unused with this swizzle)
+  d |= static_cast<uint64_t>(1024 >> 4) << 32;  // stride byte offset: 8 rows x 128 bytes
+  d |= static_cast<uint64_t>(1) << 46;          // descriptor version (sm_100)
+  d |= static_cast<uint64_t>(2) << 61;          // 128-byte swizzle
+  return d;
+}
+
+// Instruction descriptor: D f32, A and B bf16, both K-major, M x N.
+__host__ __device__ constexpr uint32_t umma_idesc_bf16(int m, int n) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(n >> 3) << 17) |
+         (static_cast<uint32_t>(m >> 4) << 24);
+}
+
+// D[tmem] (+)= A[smem desc] x B[smem desc]^T, issued by one thread.
+__device__ __forceinline__ void umma_bf16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                          bool accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate ? 1u : 0u)
+      : "memory");
+}
+
+// Arrive (once) on a CTA-local mbarrier when every MMA this thread issued so
+// far has completed.
+__device__ __forceinline__ void umma_commit(unsigned long long* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
+               : "memory");
+}
+
+// Two 4-column loads (lanes of this warp's quadrant) and one wait.
+__device__ __forceinline__ void tmem_ld4x2(uint32_t (&v)[8], uint32_t ta, uint32_t tb) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3])
+               : "r"(ta)
+               : "memory");
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7])
+               : "r"(tb)
+               : "memory");
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(v[0]), "+r"(v[1]), "+r"(v[2]), "+r"(v[3]), "+r"(v[4]), "+r"(v[5]), "+r"(v[6]), "+r"(v[7])
+               :
+               : "memory");
 }
 
 }  // namespace mtt

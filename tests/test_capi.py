@@ -93,8 +93,13 @@ def test_workspace_sizes():
     assert L.lib.mtt_b200_local_ar_frame_launch_count(ctypes.byref(ok), ctypes.byref(phase), 64) == 16 * 8 + 3
     assert L.lib.mtt_b200_local_ar_frame_path(ctypes.byref(ok), ctypes.byref(phase), 64) == L.PATH_PHASE_KERNELS
     assert L.lib.mtt_b200_local_ar_frame_path(ctypes.byref(ok), ctypes.byref(phase), 0) == -1
-    bad_path = L.SamplingConfig(80, 0.6, 2.5, 0, 1, 7)
+    bad_path = L.SamplingConfig(80, 0.6, 2.5, 0, 1, 99)
     assert L.lib.mtt_b200_local_ar_frame_path(ctypes.byref(ok), ctypes.byref(bad_path), 64) == -1
+    # a fused path the device cannot run (here: no device at all) is UNSUPPORTED, not a fallback
+    for path in (L.PATH_FUSED_TILE, L.PATH_SPLIT_1, L.PATH_SPLIT_2, L.PATH_SPLIT_4):
+        cfg = L.SamplingConfig(80, 0.6, 2.5, 0, 1, path)
+        if L.lib.mtt_b200_local_ar_frame_path_clusters(path) == 0:
+            assert L.lib.mtt_b200_local_ar_frame_path(ctypes.byref(ok), ctypes.byref(cfg), 64) == -3
 
 
 def test_null_arguments_rejected_without_launch():

@@ -25,8 +25,9 @@ from oracle import sampler as S
 pytestmark = pytest.mark.gpu
 
 RTOL = 1e-2
-PATH_AUTO, PHASE, FUSED, TILE, PAIR = 0, 1, 2, 3, 4
-BOTH = [PHASE, FUSED, TILE, PAIR]
+PATH_AUTO, PHASE, FUSED, TILE, PAIR, SPLIT1, SPLIT2, SPLIT4 = 0, 1, 2, 3, 4, 5, 6, 7
+SPLITS = [SPLIT1, SPLIT2, SPLIT4]
+BOTH = [PHASE, FUSED, TILE, PAIR] + SPLITS
 
 
 def bits(t):
@@ -164,7 +165,8 @@ FLAGS6 = ([0, 1, 0, 0, 0, 1], [0, 0, 0, 1, 0, 1], [0, 0, 1, 0, 0, 0])  # incl. a
     (SHAPE_BASELINE, 6, PHASE, True), (SHAPE_BASELINE, 6, FUSED, True), (SHAPE_BASELINE, 11, FUSED, True),
     (SHAPE_BASELINE, 6, TILE, True), (SHAPE_BASELINE, 11, TILE, True), (SHAPE_BASELINE, 11, TILE, False),
     (SHAPE_BASELINE, 11, FUSED, False), (SHAPE_BASELINE, 6, PAIR, True), (SHAPE_BASELINE, 11, PAIR, True),
-    (SHAPE_BASELINE, 20, PAIR, True), (SHAPE_BASELINE, 11, PAIR, False), (SHAPE_SOFIA, 3, PHASE, True)])
+    (SHAPE_BASELINE, 20, PAIR, True), (SHAPE_BASELINE, 11, PAIR, False), (SHAPE_SOFIA, 3, PHASE, True)] +
+    [(SHAPE_BASELINE, n, sp, fold) for sp in SPLITS for n, fold in ((6, True), (11, True), (20, True), (11, False))])
 def test_frame_matches_oracle(engines, shape, n, path, fold):
     w = weights(shape, 21)
     eng = engines(shape, 21, 24, path=path, fold=fold)
@@ -178,12 +180,23 @@ def test_frame_matches_oracle(engines, shape, n, path, fold):
 
 
 def test_auto_path_for_the_benchmark_shape(engines):
-    """Few tiles: the cluster kernel (latency); more than two waves of
-    clusters: the tile kernel (throughput); other shapes: phase kernels."""
+    """One wave of 16-CTA clusters: the cluster kernel (latency); then the
+    split kernel with the widest cluster whose tiles fit in one wave (4, then
+    2 CTAs per 8 sessions); the tile kernel for the largest batches; other
+    shapes: phase kernels."""
+    from magpie_tts_rt_b200 import _lib as L
     eng = engines(SHAPE_BASELINE, 21, 16)
     assert eng.path == FUSED
     assert eng.path_for(1) == FUSED
-    assert eng.path_for(112) == FUSED
+    assert eng.path_for(56) == FUSED
+    c4 = L.lib.mtt_b200_local_ar_frame_path_clusters(SPLIT4)
+    c2 = L.lib.mtt_b200_local_ar_frame_path_clusters(SPLIT2)
+    assert L.lib.mtt_b200_local_ar_frame_path_clusters(FUSED) == 7
+    assert 16 <= c4 < c2 <= 148
+    assert eng.path_for(8 * c4) == SPLIT4
+    assert eng.path_for(8 * c4 + 1) == SPLIT2
+    assert eng.path_for(8 * c2) == SPLIT2
+    assert eng.path_for(8 * c2 + 1) == TILE
     assert eng.path_for(1024) == TILE
     assert engines(SHAPE_SOFIA, 21, 1, with_final=False).path == PHASE
 
@@ -245,7 +258,7 @@ def test_argmax_without_cfg(engines, path):
 
 
 @pytest.mark.parametrize("name,path", [("A_bf16_cfg", PATH_AUTO), ("A_bf16_cfg", TILE), ("A_bf16_cfg", PAIR),
-                                       ("R_bf16_cfg", PATH_AUTO)])
+                                       ("R_bf16_cfg", PATH_AUTO)] + [("A_bf16_cfg", sp) for sp in SPLITS])
 def test_frame_against_reference_golden(engines, golden, golden_dir, name, path):
     """Teacher-forced on the reference's tokens, the GPU logits match the NeMo
     oracle's recorded logits within tolerance."""
@@ -303,7 +316,7 @@ def test_gpu_no_further_from_exact_than_oracle(engines):
     assert gpu_err.max() <= 2.0 * cpu_err.max() + 1e-4, (gpu_err.max(), cpu_err.max())
 
 
-@pytest.mark.parametrize("path", [FUSED, TILE, PAIR])
+@pytest.mark.parametrize("path", [FUSED, TILE, PAIR] + SPLITS)
 @pytest.mark.parametrize("kind", ["flat", "sharp", "ties"])
 def test_sampler_row_shapes(path, kind):
     """Logit rows that drive each top-k select path: flat rows (every token
