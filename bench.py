@@ -48,7 +48,7 @@ from magpie_tts_rt_b200.model import EMBED, SHAPE_BASELINE, make_weights  # noqa
 
 METRIC = "Local-AR+sampling frames/sec per GPU and box (1/2/4/8); p50 per-frame us"
 PATH_NAMES = {1: "phase kernels", 2: "fused cluster kernel", 3: "tile kernel", 4: "pair kernel",
-              5: "split kernel x1", 6: "split kernel x2", 7: "split kernel x4"}
+              5: "split kernel x1", 6: "split kernel x2", 7: "split kernel x4", 8: "split kernel x8"}
 WORKLOADS = {
     "config4": dict(total_streams=1024, frames=500, eos_frac=0.05, eos_lo=50, eos_hi=500, weak=False),
     "config3": dict(per_gpu_streams=64, frames=600, eos_frac=1.0, eos_lo=200, eos_hi=600, weak=True),
@@ -468,7 +468,8 @@ def main():
                 "kernel": {"tile kernel": "tile_frame_kernel", "pair kernel": "pair_frame_kernel",
                            "fused cluster kernel": "fused_frame_kernel", "split kernel x1": "split_frame_kernel<1>",
                            "split kernel x2": "split_frame_kernel<2>",
-                           "split kernel x4": "split_frame_kernel<4>"}.get(res["path"], res["path"]) +
+                           "split kernel x4": "split_frame_kernel<4>",
+                           "split kernel x8": "split_frame_kernel<8>"}.get(res["path"], res["path"]) +
                           " (per frame call, with the EOS projection/decision kernels: 0.6% of device time)",
                 "achieved": tf, "peak": tensor_peak, "unit": "TFLOP/s", "frac": tf / tensor_peak,
                 "peak_kind": f"{peaks_kind} sustained bf16",

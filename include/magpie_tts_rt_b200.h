@@ -287,13 +287,14 @@ MTT_B200_API int mtt_b200_launch_fold_in_projection(const mtt_b200_local_ar_shap
  * cluster (lowest latency per tile, at most a few clusters on the device at
  * once); FUSED_TILE runs 8 sessions in one CTA with their KV cache in tensor
  * memory; FUSED_PAIR runs 16 sessions on a 2-CTA cluster, each CTA streaming
- * half of every weight matrix; SPLIT_1 / SPLIT_2 / SPLIT_4 run 8 sessions on
- * a cluster of 1, 2 or 4 CTAs, each streaming that fraction of every weight
+ * half of every weight matrix; SPLIT_1 / _2 / _4 / _8 run 8 sessions on a
+ * cluster of 1, 2, 4 or 8 CTAs, each streaming that fraction of every weight
  * matrix, with the GEMMs on tcgen05 tensor cores (accumulators and the KV
  * cache in tensor memory).  AUTO picks FUSED_CLUSTER while the batch's tiles
- * fit in one wave of its clusters, then SPLIT_4 and SPLIT_2 while theirs do
+ * fit in one wave of its clusters, then SPLIT_4 and _2 while theirs do
  * (fewer sessions per GPU: more CTAs per session, shorter frames), then
- * FUSED_TILE, and the phase kernels for other shapes. */
+ * FUSED_TILE, and the phase kernels for other shapes (SPLIT_8 only on request:
+ * it is no faster than SPLIT_4 per tile). */
 #define MTT_B200_FRAME_PATH_AUTO 0
 #define MTT_B200_FRAME_PATH_PHASE_KERNELS 1
 #define MTT_B200_FRAME_PATH_FUSED_CLUSTER 2
@@ -302,6 +303,7 @@ MTT_B200_API int mtt_b200_launch_fold_in_projection(const mtt_b200_local_ar_shap
 #define MTT_B200_FRAME_PATH_SPLIT_1 5
 #define MTT_B200_FRAME_PATH_SPLIT_2 6
 #define MTT_B200_FRAME_PATH_SPLIT_4 7
+#define MTT_B200_FRAME_PATH_SPLIT_8 8
 
 /* Sampling configuration; the reference's values are 80 / 0.6 / 2.5 with CFG
  * and top-k.  argmax != 0 selects greedy decoding (no RNG, counter unchanged;
@@ -385,14 +387,14 @@ MTT_B200_API int mtt_b200_launch_local_ar_frame_static_workspace(const mtt_b200_
                                                                 void* stream);
 
 /* The path (MTT_B200_FRAME_PATH_PHASE_KERNELS, _FUSED_CLUSTER, _FUSED_TILE,
- * _FUSED_PAIR, _SPLIT_1, _SPLIT_2 or _SPLIT_4) that mtt_b200_launch_local_ar_frame takes for this shape,
+ * _FUSED_PAIR or _SPLIT_1 / _2 / _4 / _8) that mtt_b200_launch_local_ar_frame takes for this shape,
  * configuration and batch size on the current device, or
  * MTT_B200_STATUS_UNSUPPORTED. */
 MTT_B200_API int32_t mtt_b200_local_ar_frame_path(const mtt_b200_local_ar_shape_t* shape,
                                                   const mtt_b200_sampling_config_t* sampling, int32_t n_streams);
 
 /* Thread-block clusters of a fused frame path (MTT_B200_FRAME_PATH_FUSED_CLUSTER,
- * _FUSED_TILE (1-CTA clusters), _FUSED_PAIR, _SPLIT_1, _SPLIT_2, _SPLIT_4) that
+ * _FUSED_TILE (1-CTA clusters), _FUSED_PAIR, _SPLIT_1 / _2 / _4 / _8) that
  * the current device runs at once, each holding one tile of the batch; 0 when
  * the path cannot run here.  AUTO compares the batch's tiles with these. */
 MTT_B200_API int32_t mtt_b200_local_ar_frame_path_clusters(int32_t path);

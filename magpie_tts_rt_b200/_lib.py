@@ -104,6 +104,7 @@ PATH_FUSED_PAIR = 4
 PATH_SPLIT_1 = 5
 PATH_SPLIT_2 = 6
 PATH_SPLIT_4 = 7
+PATH_SPLIT_8 = 8
 
 
 class StreamBatch(ctypes.Structure):

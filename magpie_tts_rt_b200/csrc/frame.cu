@@ -444,14 +444,19 @@ namespace {
 // (~0.5 / ~0.6 ms per frame); above that the tile kernel (~0.75 ms per frame
 // for up to one CTA per SM).  So the frame time falls with the batch, and
 // sessions sharded over more GPUs run shorter frames.  Other shapes: the
-// phase kernels.
+// phase kernels.  SPLIT_8 is not chosen: measured on B200 it is no faster
+// than SPLIT_4 per tile (the per-position time is exchange, attention and
+// sampling latency, not weight streaming) and fewer 8-CTA clusters fit.
 int split_of_path(int32_t path) {
-  return path == MTT_B200_FRAME_PATH_SPLIT_4 ? 4 : (path == MTT_B200_FRAME_PATH_SPLIT_2 ? 2 : 1);
+  return path == MTT_B200_FRAME_PATH_SPLIT_8 ? 8
+         : path == MTT_B200_FRAME_PATH_SPLIT_4 ? 4
+         : path == MTT_B200_FRAME_PATH_SPLIT_2 ? 2
+                                               : 1;
 }
 
 bool is_split_path(int32_t path) {
   return path == MTT_B200_FRAME_PATH_SPLIT_1 || path == MTT_B200_FRAME_PATH_SPLIT_2 ||
-         path == MTT_B200_FRAME_PATH_SPLIT_4;
+         path == MTT_B200_FRAME_PATH_SPLIT_4 || path == MTT_B200_FRAME_PATH_SPLIT_8;
 }
 
 int32_t resolve_path(const mtt_b200_local_ar_shape_t* shape, const mtt_b200_sampling_config_t* sampling,
@@ -495,6 +500,7 @@ int32_t resolve_path(const mtt_b200_local_ar_shape_t* shape, const mtt_b200_samp
     case MTT_B200_FRAME_PATH_SPLIT_1:
     case MTT_B200_FRAME_PATH_SPLIT_2:
     case MTT_B200_FRAME_PATH_SPLIT_4:
+    case MTT_B200_FRAME_PATH_SPLIT_8:
       return mtt::split_frame_supported(probe, split_of_path(sampling->path)) ? sampling->path
                                                                                  : MTT_B200_STATUS_UNSUPPORTED;
     default:
@@ -518,7 +524,8 @@ extern "C" MTT_B200_API int32_t mtt_b200_local_ar_frame_path_clusters(int32_t pa
     case MTT_B200_FRAME_PATH_FUSED_TILE: return mtt::tile_frame_clusters();
     case MTT_B200_FRAME_PATH_SPLIT_1:
     case MTT_B200_FRAME_PATH_SPLIT_2:
-    case MTT_B200_FRAME_PATH_SPLIT_4: return mtt::split_frame_clusters(split_of_path(path));
+    case MTT_B200_FRAME_PATH_SPLIT_4:
+    case MTT_B200_FRAME_PATH_SPLIT_8: return mtt::split_frame_clusters(split_of_path(path));
     default: return 0;
   }
 }

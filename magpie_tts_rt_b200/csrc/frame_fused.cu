@@ -31,11 +31,12 @@
 //       forms the next-frame embedding sum from the 16 sampled rows.
 //
 // Exchanges are pushes, not barriers: the data goes out with st.async to the
-// receivers' shared memory and completes on the receiver's round mbarrier;
-// every CTA also arrives (with the byte count it sent) on every CTA's round
-// mbarrier, so a completed round means every CTA finished the phase before
-// it.  No buffer written in a round is read by any CTA during that round, so
-// this ordering is enough.  Weight slices stream from global memory
+// receivers' shared memory and completes on the receiver's round mbarrier,
+// which the receiver arms with the bytes it expects; every CTA pushes to
+// every CTA in every round (a 4-byte token where it has no data for one), so
+// a completed round means every CTA finished the phase before it.  No buffer
+// written in a round is read by any CTA during that round, so this ordering
+// is enough.  Weight slices stream from global memory
 // (L2-resident across frames) through a two-slot ring of TMA tensor copies
 // (cp.async.bulk.tensor.2d, 128-byte swizzle, no multicast), one phase
 // ahead of use.  The 16-row tiles run on mma.sync m16n8k16 (bf16 in, f32
@@ -123,6 +124,7 @@ struct __align__(1024) Smem {
   int32_t err;
   unsigned long long mbar[2];   // weight ring
   unsigned long long xbar[2];   // exchange rounds, alternating by round parity
+  uint32_t sink[kCS];           // round tokens (never read)
 };
 constexpr size_t kSmemBytes = sizeof(Smem) + 1024;
 
@@ -271,18 +273,28 @@ __device__ __forceinline__ void push_all16(Smem& sm, const Round& rd, int cols, 
   }
 }
 
-// Every CTA arrives on every CTA's round barrier with the bytes it sent there,
-// then waits for its own round to complete.
-template <typename BytesTo>
-__device__ __forceinline__ void finish_round(Smem& sm, Round& rd, BytesTo bytes_to) {
-  if (threadIdx.x < kCS) {
-    const int d = static_cast<int>(threadIdx.x);
-    remote_arrive_expect(cluster_addr(&sm.xbar[rd.bar()], d), bytes_to(d));
-  }
+// Waits for this CTA's round: it arms its own round barrier with the bytes
+// the cluster pushes to it in this round, and the round completes when they
+// have all landed.  Every CTA pushes to every CTA in every round (rounds
+// whose data goes to a subset add a 4-byte token to each of the others), so
+// a completed round still means every CTA finished the phase before it.
+__device__ __forceinline__ void finish_round(Smem& sm, Round& rd, uint32_t bytes_in) {
+  __syncthreads();
+  if (threadIdx.x == 0) mbar_expect_tx(&sm.xbar[rd.bar()], bytes_in);
   if (sm.err == 0 && !mbar_wait(&sm.xbar[rd.bar()], rd.parity())) sm.err = 1;
   ++rd.r;
   __syncthreads();
 }
+
+// 4-byte token from this CTA (rank c) to every CTA, for rounds whose data
+// reaches only some of them.
+__device__ __forceinline__ void push_tokens(Smem& sm, const Round& rd, int c) {
+  if (threadIdx.x < kCS) {
+    const int d = static_cast<int>(threadIdx.x);
+    st_async_b32(cluster_addr(&sm.sink[c], d), 0u, cluster_addr(&sm.xbar[rd.bar()], d));
+  }
+}
+constexpr uint32_t kTokenBytes = kCS * 4;
 
 // ---------------------------------------------------------------------------
 // weight stream
@@ -399,8 +411,8 @@ __global__ void __cluster_dims__(kCS, 1, 1) __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     mbar_init(&sm.mbar[0], 1);
     mbar_init(&sm.mbar[1], 1);
-    mbar_init(&sm.xbar[0], kCS);
-    mbar_init(&sm.xbar[1], kCS);
+    mbar_init(&sm.xbar[0], 1);
+    mbar_init(&sm.xbar[1], 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncthreads();
@@ -479,7 +491,7 @@ __global__ void __cluster_dims__(kCS, 1, 1) __launch_bounds__(kThreads, 1)
             pack_bf16x2(__fadd_rn(y0, bf2f(pos[0])), __fadd_rn(y1, bf2f(pos[1])));
       });
       push_all16(sm, rd, kDC, sm.x, kLd256, kDC * c);
-      finish_round(sm, rd, [&](int) { return slice_bytes; });
+      finish_round(sm, rd, kCS * slice_bytes);
     }
 
     // ---------------- Ph1: LN1, qkv slice, partial scores to the head group
@@ -513,7 +525,8 @@ __global__ void __cluster_dims__(kCS, 1, 1) __launch_bounds__(kThreads, 1)
       st_async_v4(cluster_addr(reinterpret_cast<const float*>(&sm.part[ds][0][0]) + ch * 4, dst), v,
                   cluster_addr(&sm.xbar[rd.bar()], dst));
     }
-    finish_round(sm, rd, [&](int d) { return d / kG == head ? uint32_t(kM * kPositions * 4) : 0u; });
+    push_tokens(sm, rd, c);
+    finish_round(sm, rd, kG * uint32_t(kM * kPositions * 4) + kTokenBytes);
 
     // ---------------- Ph2: attention (head, dims slice), all-gathered
     {
@@ -543,7 +556,7 @@ __global__ void __cluster_dims__(kCS, 1, 1) __launch_bounds__(kThreads, 1)
     }
     __syncthreads();
     push_all16(sm, rd, kHD, sm.xa, kLd256, head * kHeadDim + ds * kHD);
-    finish_round(sm, rd, [&](int) { return slice_bytes; });
+    finish_round(sm, rd, kCS * slice_bytes);
 
     // ---------------- Ph3: o-projection + residual, all-gathered
     {
@@ -556,7 +569,7 @@ __global__ void __cluster_dims__(kCS, 1, 1) __launch_bounds__(kThreads, 1)
       });
     }
     push_all16(sm, rd, kDC, sm.x, kLd256, kDC * c);
-    finish_round(sm, rd, [&](int) { return slice_bytes; });
+    finish_round(sm, rd, kCS * slice_bytes);
 
     // ---------------- Ph4: LN2, FFN1 slice + GELU, FFN2 partials to the owners
     layer_norm16(sm.x, sm.xa, f.ln2);
@@ -574,7 +587,7 @@ __global__ void __cluster_dims__(kCS, 1, 1) __launch_bounds__(kThreads, 1)
         st_async_v2f(cluster_addr(&sm.big.recv[c][r][j % kDC], dst), v0, v1, cluster_addr(&sm.xbar[rd.bar()], dst));
       });
     }
-    finish_round(sm, rd, [&](int) { return uint32_t(kM * kDC * 4); });
+    finish_round(sm, rd, kCS * uint32_t(kM * kDC * 4));
 
     // ---------------- Ph5: FFN2 output features (16 partials in CTA order) + residual
     {
@@ -587,7 +600,7 @@ __global__ void __cluster_dims__(kCS, 1, 1) __launch_bounds__(kThreads, 1)
     }
     __syncthreads();
     push_all16(sm, rd, kDC, sm.x, kLd256, kDC * c);
-    finish_round(sm, rd, [&](int) { return slice_bytes; });
+    finish_round(sm, rd, kCS * slice_bytes);
 
     // ---------------- Ph6: head p; logits rows to the owners
     const int hcols = c < kCS - 1 ? kHeadCols : kVocab - (kCS - 1) * kHeadCols;
@@ -620,7 +633,8 @@ __global__ void __cluster_dims__(kCS, 1, 1) __launch_bounds__(kThreads, 1)
                     cluster_addr(&sm.xbar[rd.bar()], sl));
       }
     }
-    finish_round(sm, rd, [&](int d) { return d < n_sess ? uint32_t(rp * hcols * 2) : 0u; });
+    push_tokens(sm, rd, c);
+    finish_round(sm, rd, (c < n_sess ? uint32_t(rp * kVocab * 2) : 0u) + kTokenBytes);
 
     // ---------------- Ph7: owner samples, broadcasts the token
     if (owner) {
@@ -646,7 +660,8 @@ __global__ void __cluster_dims__(kCS, 1, 1) __launch_bounds__(kThreads, 1)
         if (!f.prm.argmax && counter_valid) sm.ctr = call.counter + 1;
       }
     }
-    finish_round(sm, rd, [&](int) { return owner ? 4u : 0u; });
+    if (!owner) push_tokens(sm, rd, c);  // the owners' tokens are their 4 bytes
+    finish_round(sm, rd, kTokenBytes);
   }
 
   // ---- commit (owner): tokens, counter, flags, next-frame embedding

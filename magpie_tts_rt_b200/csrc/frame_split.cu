@@ -1,4 +1,4 @@
-// Split frame kernel: a C-CTA thread-block cluster (C = 1, 2 or 4) runs all
+// Split frame kernel: a C-CTA thread-block cluster (C = 1, 2, 4 or 8) runs all
 // 16 positions of a Local AR frame for a tile of up to 8 sessions (16 rows
 // with CFG), each CTA streaming 1/C of every weight matrix, with the GEMMs on
 // the fifth-generation tensor cores (tcgen05.mma, accumulators in tensor
@@ -9,7 +9,8 @@
 // Reference ops per position (as in frame_tile.cu: local_ar_wrapper.py:609-751,
 // transformer_2501.py:405-442,761-851,1153-1232, sampling
 // local_ar_plugins.cu:1211-1370, embedding sum main_decoder_wrapper.py:796-810),
-// CTA c of the cluster, nh = 4 / C heads per CTA:
+// CTA c of the cluster, nh = 4 / C heads per CTA (C = 8: CTAs 2h and 2h + 1
+// both compute head h, each sending 8 of its 16 rows):
 //
 //   input rows: p = 0 (or every p without the folded tables) the full
 //     in-projection in every CTA, x = bf16(bf16(W_in h + b) + pos[p]);
@@ -50,10 +51,11 @@
 // the two accumulator buffers.
 //
 // Exchanges push data with st.async into the receivers' shared memory and
-// complete on the receiver's round mbarrier, on which every CTA of the
-// cluster also arrives with the byte count it pushed; two barriers alternate
-// by round parity.  Each round's pushes land in buffers the receiver does not
-// read or write during the phase that precedes that round.  Every wait is
+// complete on the receiver's round mbarrier, which the receiver arms with
+// the bytes it expects (every CTA pushes to every other in every round); two
+// barriers alternate by round parity.  Each round's pushes land in buffers
+// the receiver does not read or write during the phase that precedes that
+// round.  Every wait is
 // bounded; a timeout sets invalid bit 4 for the CTA's sessions.
 #include <cooperative_groups.h>
 #include <cuda.h>
@@ -98,7 +100,8 @@ enum Gemm { G_IN = 0, G_QKV, G_O, G_F1, G_F2, G_HEAD };
 
 template <int C>
 struct Cfg {
-  static constexpr int nh = kHeads / C;      // heads per CTA
+  static constexpr int nh = C <= kHeads ? kHeads / C : 1;  // heads per CTA (C = 8: a CTA pair shares one)
+  static constexpr int att_rows = C <= kHeads ? kSR : kSR / 2;  // attention rows each CTA sends
   static constexpr int nq = (3 * nh + 1) / 2;  // qkv M-blocks (pairs of 64-row head groups)
   static constexpr int of = kD / C;          // o-projection / residual features per CTA
   static constexpr int no = of >= 128 ? of / 128 : 1;
@@ -172,7 +175,8 @@ template <int C>
 constexpr size_t split_smem_bytes() {
   return sizeof(SplitSmem<C>) + 1024;
 }
-static_assert(split_smem_bytes<1>() <= 232448 && split_smem_bytes<2>() <= 232448 && split_smem_bytes<4>() <= 232448,
+static_assert(split_smem_bytes<1>() <= 232448 && split_smem_bytes<2>() <= 232448 && split_smem_bytes<4>() <= 232448 &&
+                  split_smem_bytes<8>() <= 232448,
               "split kernel shared memory");
 
 template <int C>
@@ -218,11 +222,18 @@ __device__ __forceinline__ int gemm_kchunks(int g) {
   return g == G_IN ? kEmbed / kChunkK : (g == G_F2 ? Cfg<C>::f1 / kChunkK : kD / kChunkK);
 }
 
+// First (global) head of CTA c: nh heads each, or with 8 CTAs head c / 2
+// for the pair 2h, 2h + 1 (both compute it; each sends half of its rows).
+template <int C>
+__device__ __forceinline__ int head_base(int c) {
+  return C <= kHeads ? c * Cfg<C>::nh : c / 2;
+}
+
 // Weight rows of the head group gi (q groups, then k, then v; nh per type).
 template <int C>
 __device__ __forceinline__ int qkv_group_row(int c, int gi) {
   using K = Cfg<C>;
-  return kD * (gi / K::nh) + kHeadDim * (c * K::nh + gi % K::nh);
+  return kD * (gi / K::nh) + kHeadDim * (head_base<C>(c) + gi % K::nh);
 }
 
 // Tensor map and origins of chunk (M-block b, K-chunk k) of GEMM g: K column
@@ -427,21 +438,38 @@ __device__ __forceinline__ void x_to_operand(const bf16* x, bf16* ab) {
 // exchange rounds
 // ---------------------------------------------------------------------------
 
-// Arrive on every CTA's barrier of round rd (announcing the bytes pushed to
-// each peer), then wait for this CTA's round to complete.
-template <int C, typename Bytes>
-__device__ __forceinline__ void finish_round(SplitSmem<C>& sm, uint32_t& rd, int c, Bytes bytes_to) {
+// Wait for round rd: this CTA announces on its own round barrier the bytes
+// its peers push to it in this round (every peer pushes to every other CTA
+// in every round), and the round completes when they have all landed.  No
+// CTA arrives on another's barrier: a peer's data arriving already shows
+// that the peer finished the phase before it, because every push follows
+// the pusher's last use of the buffers the round before it filled.
+template <int C>
+__device__ __forceinline__ void finish_round(SplitSmem<C>& sm, uint32_t& rd, uint32_t bytes_in) {
   cbar();
   const int bar = static_cast<int>(rd & 1u);
-  if (threadIdx.x == 0) {
-#pragma unroll
-    for (int j = 0; j < C; ++j) {
-      if (j != c) remote_arrive_expect(cluster_addr(&sm.xbar[bar], j), bytes_to(j));
-    }
-    mbar_arrive(&sm.xbar[bar]);
-  }
+  if (threadIdx.x == 0) mbar_expect_tx(&sm.xbar[bar], bytes_in);
   if (err_flag(sm) == 0 && !mbar_wait(&sm.xbar[bar], (rd >> 1) & 1u)) sm.err = 1;
   ++rd;
+}
+
+// Vocabulary values CTA j of the cluster holds of each session (its slice of
+// the head output, clipped to the vocabulary).
+template <int C>
+__host__ __device__ constexpr int slice_len(int j) {
+  return Cfg<C>::vs * (j + 1) <= kVocab ? Cfg<C>::vs : kVocab - Cfg<C>::vs * j;
+}
+
+// Bytes CTA c receives in the head-values round: from every peer j, its
+// slice of each of c's sessions plus one non-finite flag per session.
+template <int C>
+__device__ __forceinline__ uint32_t values_bytes_in(int c) {
+  uint32_t b = 0;
+#pragma unroll
+  for (int j = 0; j < C; ++j) {
+    if (j != c) b += static_cast<uint32_t>(Cfg<C>::own * (slice_len<C>(j) * 2 + 4));
+  }
+  return b;
 }
 
 // ---------------------------------------------------------------------------
@@ -588,7 +616,8 @@ __device__ __forceinline__ void attention(SplitSmem<C>& sm, int p, int c, uint32
     const float* src = sm.u.att.o[lh][lane];
 #pragma unroll
     for (int d = 0; d < 32; ++d) o[d] += src[d];
-    const int col = kHeadDim * (c * K::nh + lh) + 32 * half;
+    const int col = kHeadDim * (head_base<C>(c) + lh) + 32 * half;
+    const bool send = C <= kHeads || (r >> 3) == (c & 1);
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       float f8[8];
@@ -598,9 +627,11 @@ __device__ __forceinline__ void attention(SplitSmem<C>& sm, int p, int c, uint32
       uint4* dst = op_unit(sm.ab, r, col + 8 * j);
       *dst = u;
       if constexpr (C > 1) {
+        if (send) {
 #pragma unroll
-        for (int jc = 0; jc < C; ++jc) {
-          if (jc != c) st_async_v4(cluster_addr(dst, jc), u, cluster_addr(&sm.xbar[rd & 1u], jc));
+          for (int jc = 0; jc < C; ++jc) {
+            if (jc != c) st_async_v4(cluster_addr(dst, jc), u, cluster_addr(&sm.xbar[rd & 1u], jc));
+          }
         }
       }
     }
@@ -669,7 +700,7 @@ __global__ void __launch_bounds__(kSThreads, 1) split_frame_kernel(Frame f, cons
     for (int b = 0; b < 2; ++b) {
       mbar_init(&sm.dfull[b], 1);
       mbar_init(&sm.dempty[b], kSW);
-      mbar_init(&sm.xbar[b], C);
+      mbar_init(&sm.xbar[b], 1);
     }
     mbar_init(&sm.opready, 1);
     mbar_init(&sm.mmafin, 1);
@@ -798,7 +829,7 @@ __global__ void __launch_bounds__(kSThreads, 1) split_frame_kernel(Frame f, cons
       // ---------------- attention (R1: the heads' outputs to every CTA)
       attention<C>(sm, p, c, rd);
       if constexpr (C > 1) {
-        finish_round(sm, rd, c, [](int) { return static_cast<uint32_t>(kSR * kHeadDim * K::nh * 2); });
+        finish_round(sm, rd, static_cast<uint32_t>((C - 1) * K::att_rows * kHeadDim * K::nh * 2));
         fence_proxy_async();
       }
       operand_ready(sm);
@@ -830,7 +861,7 @@ __global__ void __launch_bounds__(kSThreads, 1) split_frame_kernel(Frame f, cons
             if (j != c) st_async_v4(cluster_addr(src, j), u, cluster_addr(&sm.xbar[rd & 1u], j));
           }
         }
-        finish_round(sm, rd, c, [](int) { return static_cast<uint32_t>(kSR * K::of * 2); });
+        finish_round(sm, rd, static_cast<uint32_t>((C - 1) * kSR * K::of * 2));
       }
 
       // ---------------- LN2, FFN1 + GELU
@@ -870,7 +901,7 @@ __global__ void __launch_bounds__(kSThreads, 1) split_frame_kernel(Frame f, cons
         }
       }
       if constexpr (C > 1) {
-        finish_round(sm, rd, c, [](int) { return static_cast<uint32_t>(kSR * K::of * 4); });
+        finish_round(sm, rd, static_cast<uint32_t>((C - 1) * kSR * K::of * 4));
         constexpr int upr = K::of / 8;
         for (int i = threadIdx.x; i < kSR * upr; i += kSC) {
           const int r = i / upr, k8 = 8 * (i % upr);
@@ -894,7 +925,7 @@ __global__ void __launch_bounds__(kSThreads, 1) split_frame_kernel(Frame f, cons
             if (j != c) st_async_v4(cluster_addr(xr, j), u, cluster_addr(&sm.xbar[rd & 1u], j));
           }
         }
-        finish_round(sm, rd, c, [](int) { return static_cast<uint32_t>(kSR * K::of * 2); });
+        finish_round(sm, rd, static_cast<uint32_t>((C - 1) * kSR * K::of * 2));
       } else {
         cbar();
       }
@@ -945,7 +976,7 @@ __global__ void __launch_bounds__(kSThreads, 1) split_frame_kernel(Frame f, cons
         if constexpr (C > 1) {
           // the other CTAs' sessions: this CTA's vocabulary slice of each, and its non-finite flags
           constexpr int full_units = K::vs / 8;
-          const int len = (K::vs * (c + 1) <= kVocab ? K::vs : kVocab - K::vs * c);  // multiple of 8
+          const int len = slice_len<C>(c);  // a multiple of 8
           const int units = len / 8;
           const int n_other = kSS - K::own;
           for (int i = threadIdx.x; i < n_other * full_units; i += kSC) {
@@ -966,7 +997,7 @@ __global__ void __launch_bounds__(kSThreads, 1) split_frame_kernel(Frame f, cons
                            cluster_addr(&sm.xbar[rd & 1u], owner));
             }
           }
-          finish_round(sm, rd, c, [&](int) { return static_cast<uint32_t>(K::own * (len * 2 + 4)); });
+          finish_round(sm, rd, values_bytes_in<C>(c));
         }
       }
 
@@ -1020,7 +1051,7 @@ __global__ void __launch_bounds__(kSThreads, 1) split_frame_kernel(Frame f, cons
               if (j != c) st_async_b32(cluster_addr(&sm.tok[slot][p], j), 0u, cluster_addr(&sm.xbar[rd & 1u], j));
             }
           }
-          finish_round(sm, rd, c, [](int) { return static_cast<uint32_t>(K::own * 4); });
+          finish_round(sm, rd, static_cast<uint32_t>((C - 1) * K::own * 4));
         } else {
           cbar();
         }
@@ -1164,6 +1195,7 @@ int split_frame_clusters(int split) {
     case 1: return split_clusters<1>();
     case 2: return split_clusters<2>();
     case 4: return split_clusters<4>();
+    case 8: return split_clusters<8>();
     default: return 0;
   }
 }
@@ -1187,6 +1219,7 @@ cudaError_t launch_split_frame(const Frame& f, int split, cudaStream_t stream) {
     case 1: e = launch_split<1>(f, maps, stream); break;
     case 2: e = launch_split<2>(f, maps, stream); break;
     case 4: e = launch_split<4>(f, maps, stream); break;
+    case 8: e = launch_split<8>(f, maps, stream); break;
     default: return cudaErrorInvalidValue;
   }
   if (e != cudaSuccess) return e;

@@ -25,8 +25,8 @@ from oracle import sampler as S
 pytestmark = pytest.mark.gpu
 
 RTOL = 1e-2
-PATH_AUTO, PHASE, FUSED, TILE, PAIR, SPLIT1, SPLIT2, SPLIT4 = 0, 1, 2, 3, 4, 5, 6, 7
-SPLITS = [SPLIT1, SPLIT2, SPLIT4]
+PATH_AUTO, PHASE, FUSED, TILE, PAIR, SPLIT1, SPLIT2, SPLIT4, SPLIT8 = 0, 1, 2, 3, 4, 5, 6, 7, 8
+SPLITS = [SPLIT1, SPLIT2, SPLIT4, SPLIT8]
 BOTH = [PHASE, FUSED, TILE, PAIR] + SPLITS
 
 
@@ -181,18 +181,20 @@ def test_frame_matches_oracle(engines, shape, n, path, fold):
 
 def test_auto_path_for_the_benchmark_shape(engines):
     """One wave of 16-CTA clusters: the cluster kernel (latency); then the
-    split kernel with the widest cluster whose tiles fit in one wave (4, then
-    2 CTAs per 8 sessions); the tile kernel for the largest batches; other
-    shapes: phase kernels."""
+    split kernel with the widest cluster whose tiles fit in one wave (4,
+    then 2 CTAs per 8 sessions); the tile kernel for the largest batches;
+    other shapes: phase kernels."""
     from magpie_tts_rt_b200 import _lib as L
     eng = engines(SHAPE_BASELINE, 21, 16)
     assert eng.path == FUSED
     assert eng.path_for(1) == FUSED
     assert eng.path_for(56) == FUSED
+    c8 = L.lib.mtt_b200_local_ar_frame_path_clusters(SPLIT8)
     c4 = L.lib.mtt_b200_local_ar_frame_path_clusters(SPLIT4)
     c2 = L.lib.mtt_b200_local_ar_frame_path_clusters(SPLIT2)
     assert L.lib.mtt_b200_local_ar_frame_path_clusters(FUSED) == 7
-    assert 16 <= c4 < c2 <= 148
+    assert 0 < c8 < c4 < c2 <= 148
+    assert eng.path_for(8 * 7 + 1) == SPLIT4  # SPLIT8 is never picked: no faster than SPLIT4
     assert eng.path_for(8 * c4) == SPLIT4
     assert eng.path_for(8 * c4 + 1) == SPLIT2
     assert eng.path_for(8 * c2) == SPLIT2
