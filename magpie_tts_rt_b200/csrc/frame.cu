@@ -439,14 +439,12 @@ namespace {
 // Resolves the path for a shape / configuration / batch size on the current
 // device.  AUTO, benchmark shape, by the batch's 16-row tiles (8 sessions
 // each): the fused 16-CTA cluster kernel while the tiles fit in one wave of
-// its clusters (on B200 ~0.3 ms per frame); then the split kernel with the
-// widest cluster (4, else 2 CTAs per tile) whose tiles still fit in one wave
-// (~0.5 / ~0.6 ms per frame); above that the tile kernel (~0.75 ms per frame
-// for up to one CTA per SM).  So the frame time falls with the batch, and
-// sessions sharded over more GPUs run shorter frames.  Other shapes: the
-// phase kernels.  SPLIT_8 is not chosen: measured on B200 it is no faster
-// than SPLIT_4 per tile (the per-position time is exchange, attention and
-// sampling latency, not weight streaming) and fewer 8-CTA clusters fit.
+// its clusters (on B200 0.24 ms per frame, 7 clusters); then the split
+// kernel with the widest cluster (8, 4, else 2 CTAs per tile) whose tiles
+// still fit in one wave (0.35 / 0.42 / 0.55 ms per frame; 15 / 33 / 74
+// clusters); above that the tile kernel (0.75 ms per frame, one CTA per SM).
+// So the frame time falls with the batch, and sessions sharded over more
+// GPUs run shorter frames.  Other shapes: the phase kernels.
 int split_of_path(int32_t path) {
   return path == MTT_B200_FRAME_PATH_SPLIT_8 ? 8
          : path == MTT_B200_FRAME_PATH_SPLIT_4 ? 4
@@ -479,6 +477,9 @@ int32_t resolve_path(const mtt_b200_local_ar_shape_t* shape, const mtt_b200_samp
         return MTT_B200_FRAME_PATH_FUSED_CLUSTER;
       }
       const int tiles = (n_streams + 7) / 8;  // split kernel tiles
+      if (tiles <= mtt::split_frame_clusters(8) && mtt::split_frame_supported(probe, 8)) {
+        return MTT_B200_FRAME_PATH_SPLIT_8;
+      }
       if (tiles <= mtt::split_frame_clusters(4) && mtt::split_frame_supported(probe, 4)) {
         return MTT_B200_FRAME_PATH_SPLIT_4;
       }

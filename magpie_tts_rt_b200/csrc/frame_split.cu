@@ -26,8 +26,10 @@
 //   head p vocabulary [2048c/C, +2048/C) for all sessions (bias, CFG combine
 //     with the plugin's two roundings, constraints); the other CTAs' sessions'
 //     values and non-finite flags go to their owners;           exchange R5
-//   one warp per owned session (sessions [8c/C, +8/C)) samples and sends the
-//     token to every CTA                                         exchange R6
+//   one warp, or with C >= 4 a group of C warps, per owned session
+//     (sessions [8c/C, +8/C)) samples it
+//     (tile_common.cuh: sample_row, sample_group) and send the token to
+//     every CTA                                                  exchange R6
 //   (with C = 1 there are no exchanges).
 //
 // GEMMs (swap-AB): D[128 weight rows][16 tile rows] = W[128][K] x X[16][K]^T
@@ -113,6 +115,10 @@ struct Cfg {
   static constexpr int ldq = 3 * nh * 64 + 8;
   static constexpr int qkv_elems = kSR * ldq;
   static constexpr int hid_elems = kSR * f1;  // FFN hidden as 16-row panels
+  // Warps per owned session in the sampler: a group of >= 4 warps shares one
+  // session (sample_group); with 2 or more sessions per 4 warps each warp
+  // samples its own (sample_row), which measured faster there.
+  static constexpr int sw = kSW / own >= 4 ? kSW / own : 1;
   static_assert(nf1 >= 1 && nhb >= 1 && own >= 1, "split");
 };
 
@@ -144,7 +150,8 @@ struct __align__(1024) SplitSmem {
   bf16 x[kSR * kLdX];  // residual stream (row-major)
   union Q {
     bf16 qkv[K::qkv_elems];                                  // q | k | v of the CTA's heads
-    unsigned char lists[K::own][kListBytes];                 // sampler scratch
+    unsigned char lists[K::own][kListBytes];                 // sampler scratch (one warp per session)
+    GroupScratch grp[K::own];                                // sampler scratch (warp groups)
   } q;
   float red[C > 1 ? C : 1][kSR][C > 1 ? K::of : 1];  // FFN2 partial sums of the owned features, by sender
   __align__(16) bf16 hb[K::vs];                       // head p bias, this CTA's vocabulary slice
@@ -152,7 +159,8 @@ struct __align__(1024) SplitSmem {
   int32_t sess[kSS];
   uint32_t flags[kSS];  // bit 0 unfinished, bit 1 finished, bit 2 forbid_eos
   uint32_t nf[kSS];     // non-finite guided logit in this CTA's vocabulary slice, per session
-  uint32_t peer_nf[C][K::own];
+  uint32_t vmax[kSS];   // largest order key of this CTA's vocabulary slice, per session
+  uint32_t peer_nf[C][K::own];  // from each peer: non-finite flag << 16 | its slice's largest key
   int64_t ctr[K::own];
   int64_t seed[K::own];
   int32_t inv[K::own];
@@ -807,7 +815,10 @@ __global__ void __launch_bounds__(kSThreads, 1) split_frame_kernel(Frame f, cons
           if (v0 < kVocab) u = *reinterpret_cast<const uint4*>(hbp + v0);  // kVocab % 8 == 0
           *reinterpret_cast<uint4*>(sm.hb + 8 * i) = u;
         }
-        if (threadIdx.x < kSS) sm.nf[threadIdx.x] = 0;
+        if (threadIdx.x < kSS) {
+          sm.nf[threadIdx.x] = 0;
+          sm.vmax[threadIdx.x] = 0;
+        }
       }
       cbar();
 
@@ -946,6 +957,7 @@ __global__ void __launch_bounds__(kSThreads, 1) split_frame_kernel(Frame f, cons
           for (int i = 0; i < 4; ++i) {
             const int slot = 4 * sh + i;
             bool nfs = false;
+            uint32_t key = 0;
             if (in_vocab && slot < n_sess) {
               const __nv_bfloat16 cb = f2bf(__fadd_rn(v[i], bias));
               const __nv_bfloat16 ub = f2bf(__fadd_rn(v[4 + i], bias));
@@ -962,6 +974,7 @@ __global__ void __launch_bounds__(kSThreads, 1) split_frame_kernel(Frame f, cons
               const uint32_t fl = sm.flags[slot];
               const uint16_t val =
                   static_cast<uint16_t>(constrain(g, t, fl & 1u, (fl & 2u) != 0, (fl & 4u) != 0, nfs));
+              key = sample_key(val);
               const int owner = slot / K::own;
               if (owner == c) {
                 sm.u.v.own[slot - own0][t] = val;
@@ -970,6 +983,10 @@ __global__ void __launch_bounds__(kSThreads, 1) split_frame_kernel(Frame f, cons
               }
             }
             if (__any_sync(0xffffffffu, nfs) && lane == 0) atomicOr(&sm.nf[slot], 1u);
+            if constexpr (K::sw > 1) {  // the group sampler takes the row maximum from here
+              const uint32_t km = __reduce_max_sync(0xffffffffu, key);
+              if (lane == 0 && km != 0) atomicMax(&sm.vmax[slot], km);
+            }
           }
         }
         cbar();
@@ -993,47 +1010,63 @@ __global__ void __launch_bounds__(kSThreads, 1) split_frame_kernel(Frame f, cons
             const int slot = threadIdx.x;
             const int owner = slot / K::own;
             if (owner != c) {
-              st_async_b32(cluster_addr(&sm.peer_nf[c][slot - K::own * owner], owner), sm.nf[slot],
-                           cluster_addr(&sm.xbar[rd & 1u], owner));
+              st_async_b32(cluster_addr(&sm.peer_nf[c][slot - K::own * owner], owner),
+                           (sm.nf[slot] << 16) | sm.vmax[slot], cluster_addr(&sm.xbar[rd & 1u], owner));
             }
           }
           finish_round(sm, rd, values_bytes_in<C>(c));
         }
       }
 
-      // ---------------- sampling: warp w samples owned session w (R6: the token to every CTA)
-      if (warp < n_own) {
-        const int ls = warp, slot = own0 + ls;
-        uint32_t nfs = sm.nf[slot];
-        if constexpr (C > 1) {
-#pragma unroll
-          for (int j = 0; j < C; ++j) {
-            if (j != c) nfs |= sm.peer_nf[j][ls];
-          }
-        }
-        RowSample rs;
-        rs.vals = sm.u.v.own[ls];
-        rs.flags = sm.flags[slot];
-        rs.nonfinite = nfs != 0;
-        rs.seed = sm.seed[ls];
-        rs.counter = sm.ctr[ls];
-        uint16_t* list = reinterpret_cast<uint16_t*>(sm.q.lists[ls]);
-        int invalid = 0;
-        const int token = sample_row(rs, f.prm, list, list + kListCap + 16, &invalid);
-        __syncwarp();
-        if (lane == 0) {
-          const int64_t counter = sm.ctr[ls];
-          sm.tok[slot][p] = token;
-          sm.inv[ls] |= invalid;
-          const bool counter_valid = counter >= 0 && counter <= kMaxCounter;
-          if (!f.prm.argmax && counter_valid) sm.ctr[ls] = counter + 1;
+      // ---------------- sampling (R6: the token to every CTA): one warp per owned
+      // session, or a group of 8 / own >= 4 warps per session
+      {
+        constexpr int W = K::sw;
+        const int ls = warp / W;
+        if (ls < n_own) {
+          const int slot = own0 + ls;
+          uint32_t nfs = sm.nf[slot], M = sm.vmax[slot];
           if constexpr (C > 1) {
-            if (p + 1 < kPositions) {
 #pragma unroll
-              for (int j = 0; j < C; ++j) {
-                if (j != c) {
-                  st_async_b32(cluster_addr(&sm.tok[slot][p], j), static_cast<uint32_t>(token),
-                               cluster_addr(&sm.xbar[rd & 1u], j));
+            for (int j = 0; j < C; ++j) {
+              if (j != c) {
+                const uint32_t pk = sm.peer_nf[j][ls];
+                nfs |= pk >> 16;
+                M = (pk & 0xffffu) > M ? (pk & 0xffffu) : M;
+              }
+            }
+          }
+          RowSample rs;
+          rs.vals = sm.u.v.own[ls];
+          rs.flags = sm.flags[slot];
+          rs.nonfinite = nfs != 0;
+          rs.seed = sm.seed[ls];
+          rs.counter = sm.ctr[ls];
+          int invalid = 0;
+          int token;
+          if constexpr (W == 1) {
+            uint16_t* list = reinterpret_cast<uint16_t*>(sm.q.lists[ls]);
+            token = sample_row(rs, f.prm, list, list + kListCap + 16, &invalid);
+          } else {
+            uint32_t* list32 = reinterpret_cast<uint32_t*>(sm.xa) + ls * kListCap;
+            token = sample_group<W>(rs, M < kKeyNegInf ? kKeyNegInf : M, f.prm, list32, sm.q.grp[ls], 2 + ls,
+                                    &invalid);
+          }
+          __syncwarp();
+          if (warp % W == 0 && lane == 0) {
+            const int64_t counter = sm.ctr[ls];
+            sm.tok[slot][p] = token;
+            sm.inv[ls] |= invalid;
+            const bool counter_valid = counter >= 0 && counter <= kMaxCounter;
+            if (!f.prm.argmax && counter_valid) sm.ctr[ls] = counter + 1;
+            if constexpr (C > 1) {
+              if (p + 1 < kPositions) {
+#pragma unroll
+                for (int j = 0; j < C; ++j) {
+                  if (j != c) {
+                    st_async_b32(cluster_addr(&sm.tok[slot][p], j), static_cast<uint32_t>(token),
+                                 cluster_addr(&sm.xbar[rd & 1u], j));
+                  }
                 }
               }
             }

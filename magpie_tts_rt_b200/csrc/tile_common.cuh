@@ -420,5 +420,301 @@ __device__ int sample_row(const RowSample& rs, const SamplingParams& prm, uint16
   return token;
 }
 
+
+// ---------------------------------------------------------------------------
+// Group sampler: W warps (32 W threads, named barrier `bar_id`) sample one
+// session row together.  Same contract and the same result as sample_row;
+// the row maximum M (order key) comes from the head epilogue.  The row is
+// split into W ranges of 8-value chunks; window counts, the candidate list,
+// the distance histogram that gives the exact k-th largest, and the scoring
+// of the eligible tokens are shared across the group.  Eligible tokens are
+// ranked with the fast Gumbel and those within kVerifyMargin of the best are
+// rescored with the contract's correctly rounded one (as score_list does).
+// ---------------------------------------------------------------------------
+
+struct GroupScratch {
+  uint32_t cnt[8][4];   // per-warp window counts
+  uint32_t cnt2[8][2];  // per-warp counts of the whole-row search (alternating)
+  uint32_t hist[256];   // candidates per distance below the maximum
+  float best_score[8];
+  int32_t best_id[8];
+};
+
+__device__ __forceinline__ void group_bar(int bar_id, int threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(bar_id), "r"(threads) : "memory");
+}
+
+template <int W>
+__device__ int sample_group(const RowSample& rs, uint32_t M, const SamplingParams& prm, uint32_t* list32,
+                            GroupScratch& gs, int bar_id, int* invalid_out) {
+  constexpr int kThreadsG = 32 * W;
+  constexpr int kCpw = (kVocabChunks + W - 1) / W;  // chunks per warp
+  constexpr int kIt = (kCpw + 31) / 32;             // chunks per lane
+  const int lane = threadIdx.x & 31;
+  const int g = (threadIdx.x >> 5) % W;
+  const int tid = 32 * g + lane;
+  const int ch0 = kCpw * g;
+  const int ch1 = ch0 + kCpw < kVocabChunks ? ch0 + kCpw : kVocabChunks;
+  const bool unfinished = rs.flags & 1u, finished = rs.flags & 2u, forbid = rs.flags & 4u;
+  const uint16_t* vals = rs.vals;
+  if (prm.argmax) {
+    *invalid_out = (rs.nonfinite || M == kKeyNegInf) ? 1 : 0;
+    if (M == kKeyNegInf) return 0;
+    int first = kVocab;
+#pragma unroll
+    for (int i = kIt - 1; i >= 0; --i) {
+      const int ch = ch0 + lane + 32 * i;
+      if (ch < ch1) {
+        const uint4 q = *reinterpret_cast<const uint4*>(vals + 8 * ch);
+        const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+        for (int e = 3; e >= 0; --e) {
+          if (sample_key(w[e] >> 16) == M) first = 8 * ch + 2 * e + 1;
+          if (sample_key(w[e] & 0xffffu) == M) first = 8 * ch + 2 * e;
+        }
+      }
+    }
+    first = static_cast<int>(__reduce_min_sync(0xffffffffu, static_cast<uint32_t>(first)));
+    if (lane == 0) gs.best_id[g] = first;
+    group_bar(bar_id, kThreadsG);
+    int t = kVocab;
+#pragma unroll
+    for (int j = 0; j < W; ++j) t = gs.best_id[j] < t ? gs.best_id[j] : t;
+    return t;
+  }
+  int invalid = (rs.nonfinite || (unfinished && finished) || (finished && forbid)) ? 1 : 0;
+  const int64_t seed = rs.seed, counter = rs.counter;
+  const bool seed_valid = seed >= 0 && static_cast<uint64_t>(seed) < (1ull << 32);
+  const bool counter_valid = counter >= 0 && counter <= kMaxCounter;
+  if (!seed_valid || !counter_valid) invalid = 1;
+  if (finished) {  // only EOS (value 0) is finite: it is the only eligible token
+    *invalid_out = invalid;
+    return kEosId;
+  }
+  if (M == kKeyNegInf) {
+    *invalid_out = 1;
+    return 0;
+  }
+  const uint32_t seed32 = seed_valid ? static_cast<uint32_t>(seed) : 0u;
+  const uint64_t off64 = counter_valid ? static_cast<uint64_t>(counter) * kPhiloxStride : 0ull;
+  const uint32_t kk = static_cast<uint32_t>(prm.top_k);
+
+  // ---- window counts: values within 32 / 64 / 128 / 256 key steps of the maximum
+  __nv_bfloat162 lim[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) lim[j] = __bfloat162bfloat162(key_value(M + 1 < (32u << j) ? 0u : M + 1 - (32u << j)));
+  __nv_bfloat162 acc[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) acc[j] = __float2bfloat162_rn(0.f);
+#pragma unroll
+  for (int i = 0; i < kIt; ++i) {
+    const int ch = ch0 + lane + 32 * i;
+    if (ch < ch1) {
+      const uint4 q = *reinterpret_cast<const uint4*>(vals + 8 * ch);
+      const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[j] = __hadd2(acc[j], __hge2(bf2_of(w[e]), lim[j]));
+    }
+  }
+  uint32_t mine4[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const float2 f2 = __bfloat1622float2(acc[j]);
+    mine4[j] = static_cast<uint32_t>(f2.x + f2.y);
+    const uint32_t wt = __reduce_add_sync(0xffffffffu, mine4[j]);
+    if (lane == 0) gs.cnt[g][j] = wt;
+  }
+  for (int i = tid; i < 256; i += kThreadsG) gs.hist[i] = 0;
+  group_bar(bar_id, kThreadsG);
+  uint32_t tot[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    tot[j] = 0;
+#pragma unroll
+    for (int q = 0; q < W; ++q) tot[j] += gs.cnt[q][j];
+  }
+  int win = 4;
+#pragma unroll
+  for (int j = 3; j >= 0; --j) win = tot[j] >= kk ? j : win;
+
+  Best best{-CUDART_INF_F, kVocab};
+  if (win < 4 && tot[win] <= static_cast<uint32_t>(kListCap)) {
+    const __nv_bfloat162 limw = win == 0 ? lim[0] : (win == 1 ? lim[1] : (win == 2 ? lim[2] : lim[3]));
+    const uint32_t mine = win == 0 ? mine4[0] : (win == 1 ? mine4[1] : (win == 2 ? mine4[2] : mine4[3]));
+    const uint32_t n_cand = tot[win];
+    uint32_t pos = mine;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t y = __shfl_up_sync(0xffffffffu, pos, o);
+      if (lane >= o) pos += y;
+    }
+    pos -= mine;
+#pragma unroll
+    for (int q = 0; q < W; ++q) pos += q < g ? gs.cnt[q][win] : 0u;
+    // ---- the window's tokens, with their keys
+#pragma unroll
+    for (int i = 0; i < kIt; ++i) {
+      const int ch = ch0 + lane + 32 * i;
+      if (ch < ch1) {
+        const uint4 q = *reinterpret_cast<const uint4*>(vals + 8 * ch);
+        const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const uint32_t m = __hge2_mask(bf2_of(w[e]), limw);
+          if (m & 1u) list32[pos++] = (sample_key(w[e] & 0xffffu) << 16) | static_cast<uint32_t>(8 * ch + 2 * e);
+          if (m >> 31) list32[pos++] = (sample_key(w[e] >> 16) << 16) | static_cast<uint32_t>(8 * ch + 2 * e + 1);
+        }
+      }
+    }
+    group_bar(bar_id, kThreadsG);
+    for (uint32_t e = tid; e < n_cand; e += kThreadsG) atomicAdd(&gs.hist[M - (list32[e] >> 16)], 1u);
+    group_bar(bar_id, kThreadsG);
+    // smallest d with (candidates at distance <= d) >= k: lane holds bins [8 lane, +8)
+    uint32_t h[8], part = 0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      h[j] = gs.hist[8 * lane + j];
+      part += h[j];
+    }
+    uint32_t incl = part;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += y;
+    }
+    const unsigned reach = __ballot_sync(0xffffffffu, incl >= kk);
+    const int L = __ffs(reach) - 1;  // tot[win] >= k, so some lane reaches k
+    uint32_t dstar = 0;
+    if (lane == L) {
+      uint32_t c = incl - part;  // candidates in the bins below this lane's
+      bool found = false;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        c += h[j];
+        if (!found && c >= kk) {
+          dstar = 8 * L + j;
+          found = true;
+        }
+      }
+    }
+    dstar = __shfl_sync(0xffffffffu, dstar, L);
+    // ---- eligible candidates (distance <= d*, finite): fast scores, the
+    // group's best fast score, then the exact score only for candidates
+    // within kVerifyMargin of it (a lone one is the winner as it stands)
+    constexpr int kPer = kListCap / kThreadsG;
+    float fs[kPer];
+    int tk[kPer];
+    float bf = -CUDART_INF_F;
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {
+      fs[i] = -CUDART_INF_F;
+      tk[i] = kVocab;
+      const uint32_t e = tid + kThreadsG * i;
+      if (e < n_cand) {
+        const uint32_t v = list32[e];
+        const uint32_t key = v >> 16;
+        if (M - key <= dstar && key != kKeyNegInf) {
+          const int t = static_cast<int>(v & 0xffffu);
+          tk[i] = t;
+          fs[i] = __fadd_rn(__fdiv_rn(bits2f(vals[t]), prm.temperature),
+                            fast_gumbel(philox_uniform(seed32, off64 + static_cast<uint64_t>(t))));
+          bf = fmaxf(bf, fs[i]);
+        }
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) bf = fmaxf(bf, __shfl_xor_sync(0xffffffffu, bf, o));
+    if (lane == 0) gs.best_score[g] = bf;
+    group_bar(bar_id, kThreadsG);
+    float gbf = -CUDART_INF_F;
+#pragma unroll
+    for (int q = 0; q < W; ++q) gbf = fmaxf(gbf, gs.best_score[q]);
+    const float cut = gbf - kVerifyMargin;
+    uint32_t near = 0;
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) near += (tk[i] < kVocab && fs[i] >= cut) ? 1u : 0u;
+    near = __reduce_add_sync(0xffffffffu, near);
+    if (lane == 0) gs.cnt2[g][0] = near;
+    group_bar(bar_id, kThreadsG);
+    uint32_t tot_near = 0;
+#pragma unroll
+    for (int q = 0; q < W; ++q) tot_near += gs.cnt2[q][0];
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {
+      if (tk[i] < kVocab && fs[i] >= cut) {
+        keep_best(best,
+                  tot_near == 1 ? fs[i]
+                                : exact_score(bits2f(vals[tk[i]]), prm.temperature, seed32,
+                                              off64 + static_cast<uint64_t>(tk[i])),
+                  tk[i]);
+      }
+    }
+  } else {
+    // exact search over keys: count(value >= lo) >= k > count(value >= hi)
+    uint32_t lo = kKeyNegInf, hi = M + 1;
+    int it = 0;
+    while (hi - lo > 1) {
+      const uint32_t mid = (lo + hi) >> 1;
+      const __nv_bfloat162 t2 = __bfloat162bfloat162(key_value(mid));
+      __nv_bfloat162 a2 = __float2bfloat162_rn(0.f);
+#pragma unroll
+      for (int i = 0; i < kIt; ++i) {
+        const int ch = ch0 + lane + 32 * i;
+        if (ch < ch1) {
+          const uint4 q = *reinterpret_cast<const uint4*>(vals + 8 * ch);
+          a2 = __hadd2(a2, __hge2(bf2_of(q.x), t2));
+          a2 = __hadd2(a2, __hge2(bf2_of(q.y), t2));
+          a2 = __hadd2(a2, __hge2(bf2_of(q.z), t2));
+          a2 = __hadd2(a2, __hge2(bf2_of(q.w), t2));
+        }
+      }
+      const float2 f2 = __bfloat1622float2(a2);
+      const uint32_t wt = __reduce_add_sync(0xffffffffu, static_cast<uint32_t>(f2.x + f2.y));
+      if (lane == 0) gs.cnt2[g][it & 1] = wt;
+      group_bar(bar_id, kThreadsG);
+      uint32_t c = 0;
+#pragma unroll
+      for (int q = 0; q < W; ++q) c += gs.cnt2[q][it & 1];
+      if (c >= kk) {
+        lo = mid;
+      } else {
+        hi = mid;
+      }
+      ++it;
+    }
+#pragma unroll 1
+    for (int i = 0; i < kIt; ++i) {
+      const int ch = ch0 + lane + 32 * i;
+      if (ch < ch1) {
+        for (int e = 0; e < 8; ++e) {
+          const int t = 8 * ch + e;
+          const uint32_t key = sample_key(vals[t]);
+          if (key >= lo && key != kKeyNegInf) {
+            keep_best(best, exact_score(bits2f(vals[t]), prm.temperature, seed32, off64 + static_cast<uint64_t>(t)), t);
+          }
+        }
+      }
+    }
+  }
+  best = warp_best(best);
+  if (lane == 0) {
+    gs.best_score[g] = best.score;
+    gs.best_id[g] = best.id;
+  }
+  group_bar(bar_id, kThreadsG);
+  Best all{-CUDART_INF_F, kVocab};
+#pragma unroll
+  for (int q = 0; q < W; ++q) keep_best(all, gs.best_score[q], gs.best_id[q]);
+  int token = all.id;
+  if (token >= kVocab || all.score == -CUDART_INF_F) {
+    invalid = 1;
+    token = 0;
+  }
+  *invalid_out = invalid;
+  return token;
+}
+
 }  // namespace
 }  // namespace mtt

@@ -181,7 +181,7 @@ def test_frame_matches_oracle(engines, shape, n, path, fold):
 
 def test_auto_path_for_the_benchmark_shape(engines):
     """One wave of 16-CTA clusters: the cluster kernel (latency); then the
-    split kernel with the widest cluster whose tiles fit in one wave (4,
+    split kernel with the widest cluster whose tiles fit in one wave (8, 4,
     then 2 CTAs per 8 sessions); the tile kernel for the largest batches;
     other shapes: phase kernels."""
     from magpie_tts_rt_b200 import _lib as L
@@ -193,8 +193,10 @@ def test_auto_path_for_the_benchmark_shape(engines):
     c4 = L.lib.mtt_b200_local_ar_frame_path_clusters(SPLIT4)
     c2 = L.lib.mtt_b200_local_ar_frame_path_clusters(SPLIT2)
     assert L.lib.mtt_b200_local_ar_frame_path_clusters(FUSED) == 7
-    assert 0 < c8 < c4 < c2 <= 148
-    assert eng.path_for(8 * 7 + 1) == SPLIT4  # SPLIT8 is never picked: no faster than SPLIT4
+    assert 7 < c8 < c4 < c2 <= 148
+    assert eng.path_for(8 * 7 + 1) == SPLIT8
+    assert eng.path_for(8 * c8) == SPLIT8
+    assert eng.path_for(8 * c8 + 1) == SPLIT4
     assert eng.path_for(8 * c4) == SPLIT4
     assert eng.path_for(8 * c4 + 1) == SPLIT2
     assert eng.path_for(8 * c2) == SPLIT2
