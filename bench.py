@@ -49,6 +49,8 @@ from magpie_tts_rt_b200.model import EMBED, SHAPE_BASELINE, make_weights  # noqa
 METRIC = "Local-AR+sampling frames/sec per GPU and box (1/2/4/8); p50 per-frame us"
 PATH_NAMES = {1: "phase kernels", 2: "fused cluster kernel", 3: "tile kernel", 4: "pair kernel",
               5: "split kernel x1", 6: "split kernel x2", 7: "split kernel x4", 8: "split kernel x8"}
+# DRAM bytes per launch of the frame kernel, measured by ncu (path, sessions per GPU)
+TRAFFIC = {("tile kernel", 1024): 27.64e6, ("split kernel x4", 256): 23.13e6}
 WORKLOADS = {
     "config4": dict(total_streams=1024, frames=500, eos_frac=0.05, eos_lo=50, eos_hi=500, weak=False),
     "config3": dict(per_gpu_streams=64, frames=600, eos_frac=1.0, eos_lo=200, eos_hi=600, weak=True),
@@ -63,6 +65,8 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="config4", choices=list(WORKLOADS))
     ap.add_argument("--frames", type=int, default=None, help="override frames per step (profiling)")
+    ap.add_argument("--sessions", type=int, default=None,
+                    help="override sessions per GPU (profiling a smaller per-GPU batch, e.g. 256 = config 4 at 4 GPUs)")
     ap.add_argument("--no-latency", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     return ap.parse_args()
@@ -82,7 +86,8 @@ def dist_init():
         backend = "nccl" if torch.cuda.is_available() else "gloo"
         if torch.cuda.is_available():
             torch.cuda.set_device(local)
-        dist.init_process_group(backend, timeout=datetime.timedelta(seconds=120))
+        kw = {"device_id": torch.device("cuda", local)} if backend == "nccl" else {}
+        dist.init_process_group(backend, timeout=datetime.timedelta(seconds=120), **kw)
     elif torch.cuda.is_available():
         torch.cuda.set_device(0)
     return world, rank, local
@@ -220,7 +225,9 @@ def run_ours(args, world, rank, local):
     from magpie_tts_rt_b200 import _lib as L
     from magpie_tts_rt_b200.local_ar import LocalArEngine, StreamBatch
 
-    cfg = WORKLOADS[args.workload]
+    cfg = dict(WORKLOADS[args.workload])
+    if args.sessions:
+        cfg.update(weak=True, per_gpu_streams=args.sessions)
     frames = args.frames or cfg["frames"]
     n, first, total = rank_streams(cfg, world, rank)
     dev = torch.device("cuda", local)
@@ -418,7 +425,9 @@ def main():
     args = parse()
     world, rank, local = dist_init()
     peaks, peaks_kind = load_peaks()
-    cfgw = WORKLOADS[args.workload]
+    cfgw = dict(WORKLOADS[args.workload])
+    if args.sessions:
+        cfgw.update(weak=True)
     config = {"workload": f"{args.workload}: " + (
         "1024 sessions x CFG pair sharded over N GPUs, 500 frames, 5% forced EOS at U[50,500]"
         if args.workload == "config4" else "64 sessions x CFG pair per GPU, forced EOS at U[200,600], 600 frames"),
@@ -427,6 +436,8 @@ def main():
         "l2": "inputs larger than L2 (new hidden states every frame, >1 GB per step at N=1); weights stay "
               "L2-resident across frames as in serving",
         "parallelism": f"session-sharded dp{world}, no collective"}
+    if args.sessions:
+        config["workload"] += f" (profiling override: {args.sessions} sessions per GPU)"
     if args.impl == "reference":
         r = run_reference(args, world, rank)
         if rank == 0:
@@ -463,7 +474,6 @@ def main():
         tensor_peak = peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"])
         # dominant kernel: the frame kernel (98.4% of device time in the launch list); one frame
         # call = that kernel + the EOS projection/decision kernels, timed together by CUDA events
-        tile = res["path"] == "tile kernel"
         roof = {"bound": "tensor",
                 "kernel": {"tile kernel": "tile_frame_kernel", "pair kernel": "pair_frame_kernel",
                            "fused cluster kernel": "fused_frame_kernel", "split kernel x1": "split_frame_kernel<1>",
@@ -473,9 +483,10 @@ def main():
                           " (per frame call, with the EOS projection/decision kernels: 0.6% of device time)",
                 "achieved": tf, "peak": tensor_peak, "unit": "TFLOP/s", "frac": tf / tensor_peak,
                 "peak_kind": f"{peaks_kind} sustained bf16",
-                # dram__bytes_read.sum + dram__bytes_write.sum of one tile_frame_kernel launch at
-                # 1024 sessions (profiles/tile_frame_kernel_config4.md)
-                "traffic": 27.64e6 if tile and res["n_local"] == 1024 else None,
+                # dram__bytes_read.sum + dram__bytes_write.sum of one frame-kernel launch from the
+                # ncu captures (profiles/tile_frame_kernel_config4.md at 1024 sessions,
+                # profiles/split_frame_kernel_x4_256sessions.md at 256 sessions)
+                "traffic": TRAFFIC.get((res["path"], res["n_local"])),
                 "avg_frame_call_us": t_frame * 1e6,
                 "hbm_achieved_gbs": gbs, "hbm_frac": gbs / peaks["hbm_gbs"],
                 "algorithmic_flops_per_frame_step": flops, "algorithmic_bytes_per_frame_step": bytes_}
