@@ -442,7 +442,9 @@ namespace {
 // its clusters (on B200 0.24 ms per frame, 7 clusters); then the split
 // kernel with the widest cluster (8, 4, else 2 CTAs per tile) whose tiles
 // still fit in one wave (0.35 / 0.42 / 0.55 ms per frame; 15 / 33 / 74
-// clusters); above that the tile kernel (0.75 ms per frame, one CTA per SM).
+// clusters); above that the pair kernel while its 16-session tiles fit in one
+// wave (0.73 ms per frame, 74 clusters of 2), then the tile kernel (0.75 ms
+// per frame, one CTA per SM).
 // So the frame time falls with the batch, and sessions sharded over more
 // GPUs run shorter frames.  Other shapes: the phase kernels.
 int split_of_path(int32_t path) {
@@ -486,6 +488,7 @@ int32_t resolve_path(const mtt_b200_local_ar_shape_t* shape, const mtt_b200_samp
       if (tiles <= mtt::split_frame_clusters(2) && mtt::split_frame_supported(probe, 2)) {
         return MTT_B200_FRAME_PATH_SPLIT_2;
       }
+      if (pair && (n_streams + 15) / 16 <= mtt::pair_frame_clusters()) return MTT_B200_FRAME_PATH_FUSED_PAIR;
       if (tile) return MTT_B200_FRAME_PATH_FUSED_TILE;
       if (pair) return MTT_B200_FRAME_PATH_FUSED_PAIR;
       return MTT_B200_FRAME_PATH_FUSED_CLUSTER;

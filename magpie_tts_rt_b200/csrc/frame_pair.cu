@@ -24,8 +24,8 @@
 //     token and the session's next input rows.                exchange R6
 //
 // Exchanges are pushes (st.async into the peer's shared memory, completing on
-// the peer's round mbarrier, which also counts both CTAs' arrivals); two
-// barriers alternate by round parity.  A CTA can be at most one round ahead
+// the peer's round mbarrier, which the receiver arms with the bytes it
+// expects); two barriers alternate by round parity.  A CTA can be at most one round ahead
 // of its peer, so each round's pushes land in buffers the receiver does not
 // touch during the phase before that round (x columns it does not own, the
 // peer-attention buffer xr, the FFN2 receive buffer red, the value columns of
@@ -117,6 +117,7 @@ struct __align__(1024) PairSmem {
   unsigned long long full[kPSlots];
   unsigned long long empty[kPSlots];
   unsigned long long xbar[2];
+  uint32_t sink;  // round token (never read)
 };
 constexpr size_t kPSmemBytes = sizeof(PairSmem) + 1024;
 static_assert(kPSmemBytes <= 232448, "pair kernel shared memory");
@@ -312,14 +313,14 @@ __device__ __forceinline__ uint32_t peer_bar(const PairSmem& sm, const Round& rd
   return cluster_addr(&sm.xbar[rd.bar()], peer);
 }
 
-// Arrive on both CTAs' barriers of this round (announcing the bytes pushed to
-// the peer), then wait for this CTA's round to complete.
-__device__ __forceinline__ void finish_round(PairSmem& sm, Round& rd, int peer, uint32_t bytes_to_peer) {
+// Wait for this CTA's round: it arms its own round barrier with the bytes
+// the peer pushes to it in this round, and the round completes when they
+// have landed.  The peer pushes something in every round (a 4-byte token in
+// the token round), so a completed round also shows the peer finished the
+// phase before it.
+__device__ __forceinline__ void finish_round(PairSmem& sm, Round& rd, uint32_t bytes_in) {
   cbar();
-  if (threadIdx.x == 0) {
-    remote_arrive_expect(peer_bar(sm, rd, peer), bytes_to_peer);
-    mbar_arrive(&sm.xbar[rd.bar()]);
-  }
+  if (threadIdx.x == 0) mbar_expect_tx(&sm.xbar[rd.bar()], bytes_in);
   if (err_flag(sm) == 0 && !mbar_wait(&sm.xbar[rd.bar()], rd.parity())) sm.err = 1;
   ++rd.r;
 }
@@ -504,8 +505,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
       mbar_init(&sm.empty[s], kPW);
       sm.last_issued[s] = -1;
     }
-    mbar_init(&sm.xbar[0], 2);
-    mbar_init(&sm.xbar[1], 2);
+    mbar_init(&sm.xbar[0], 1);
+    mbar_init(&sm.xbar[1], 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncwarp();
@@ -614,7 +615,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
               push_b32(xr_, peer, v, rb);
             }
         }
-        finish_round(sm, rd, peer, kPR * 128 * 2);  // R0
+        finish_round(sm, rd, kPR * 128 * 2);  // R0
       }
       // head p bias (this CTA's half), per-position sampling state
       {
@@ -647,7 +648,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
       cbar();
       // ---------------- attention of heads 2c, 2c+1; outputs to the peer
       attention_pair(sm, p, c, peer, peer_bar(sm, rd, peer));
-      finish_round(sm, rd, peer, kPR * 128 * 2);  // R1
+      finish_round(sm, rd, kPR * 128 * 2);  // R1
       // ---------------- o-projection features [128c, +128) + residual
       {
         uint32_t a[2][16][4];
@@ -667,7 +668,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
             }
         });
       }
-      finish_round(sm, rd, peer, kPR * 128 * 2);  // R2
+      finish_round(sm, rd, kPR * 128 * 2);  // R2
       // ---------------- LN2, FFN1 features [512c, +512) + GELU
       layer_norm_rows32(sm.x, sm.xa, g2);
       cbar();
@@ -723,7 +724,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
           }
         }
       }
-      finish_round(sm, rd, peer, kPR * 128 * 4);  // R3
+      finish_round(sm, rd, kPR * 128 * 4);  // R3
       // ---------------- own output features: CTA 0's partial + CTA 1's partial, + residual
       {
         const uint32_t rb = peer_bar(sm, rd, peer);
@@ -746,7 +747,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
             }
         }
       }
-      finish_round(sm, rd, peer, kPR * 128 * 2);  // R4
+      finish_round(sm, rd, kPR * 128 * 2);  // R4
       // ---------------- head p, this CTA's vocabulary half, all 16 sessions
       {
         uint32_t a[2][16][4];
@@ -794,7 +795,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
         cbar();
         if (threadIdx.x < kPOwn) push_b32(&sm.peer_nonfinite[threadIdx.x], peer, sm.stage_nonfinite[threadIdx.x], rb);
       }
-      finish_round(sm, rd, peer, n_peer * kHalf * 2 + kPOwn * 4);  // R5
+      finish_round(sm, rd, n_own * kHalf * 2 + kPOwn * 4);  // R5: the peer's half of this CTA's sessions
       // ---------------- sampling of sessions 8c..8c+7; tokens and next input rows to both CTAs
       if (warp < n_own) {
         const int ls = warp, slot = own0 + warp;
@@ -838,7 +839,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
         }
       }
       if (p + 1 < kPositions) {
-        finish_round(sm, rd, peer, n_own * (4 + (folded ? rp * kD * 2 : 0)));  // R6
+        if (threadIdx.x == 0) push_b32(&sm.sink, peer, 0u, peer_bar(sm, rd, peer));  // the round's token
+        finish_round(sm, rd, n_peer * (4 + (folded ? rp * kD * 2 : 0)) + 4);  // R6: the peer's tokens and rows
       } else {
         cbar();
       }

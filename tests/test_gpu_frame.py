@@ -182,8 +182,9 @@ def test_frame_matches_oracle(engines, shape, n, path, fold):
 def test_auto_path_for_the_benchmark_shape(engines):
     """One wave of 16-CTA clusters: the cluster kernel (latency); then the
     split kernel with the widest cluster whose tiles fit in one wave (8, 4,
-    then 2 CTAs per 8 sessions); the tile kernel for the largest batches;
-    other shapes: phase kernels."""
+    then 2 CTAs per 8 sessions); the pair kernel while its 16-session tiles
+    fit in one wave; the tile kernel for the largest batches; other shapes:
+    phase kernels."""
     from magpie_tts_rt_b200 import _lib as L
     eng = engines(SHAPE_BASELINE, 21, 16)
     assert eng.path == FUSED
@@ -200,8 +201,11 @@ def test_auto_path_for_the_benchmark_shape(engines):
     assert eng.path_for(8 * c4) == SPLIT4
     assert eng.path_for(8 * c4 + 1) == SPLIT2
     assert eng.path_for(8 * c2) == SPLIT2
-    assert eng.path_for(8 * c2 + 1) == TILE
-    assert eng.path_for(1024) == TILE
+    cp = L.lib.mtt_b200_local_ar_frame_path_clusters(PAIR)
+    assert 8 * c2 < 16 * cp
+    assert eng.path_for(8 * c2 + 1) == PAIR
+    assert eng.path_for(16 * cp) == PAIR
+    assert eng.path_for(16 * cp + 1) == TILE
     assert engines(SHAPE_SOFIA, 21, 1, with_final=False).path == PHASE
 
 
