@@ -50,7 +50,7 @@ METRIC = "Local-AR+sampling frames/sec per GPU and box (1/2/4/8); p50 per-frame 
 PATH_NAMES = {1: "phase kernels", 2: "fused cluster kernel", 3: "tile kernel", 4: "pair kernel",
               5: "split kernel x1", 6: "split kernel x2", 7: "split kernel x4", 8: "split kernel x8"}
 # DRAM bytes per launch of the frame kernel, measured by ncu (path, sessions per GPU)
-TRAFFIC = {("tile kernel", 1024): 27.64e6, ("split kernel x4", 256): 23.13e6}
+TRAFFIC = {("tile kernel", 1024): 27.64e6, ("pair kernel", 1024): 27.70e6, ("split kernel x4", 256): 23.13e6}
 WORKLOADS = {
     "config4": dict(total_streams=1024, frames=500, eos_frac=0.05, eos_lo=50, eos_hi=500, weak=False),
     "config3": dict(per_gpu_streams=64, frames=600, eos_frac=1.0, eos_lo=200, eos_hi=600, weak=True),
@@ -248,7 +248,8 @@ def run_ours(args, world, rank, local):
         f1 = min(frames, f0 + chunk)
         host_hidden[f0:f1].copy_(torch.randn(f1 - f0, n, 2, EMBED, generator=g))
     dev_hidden = host_hidden.to(dev)
-    stage = torch.empty(n, 2, EMBED, dtype=torch.bfloat16, device=dev)
+    # two staging buffers: frame f+1's host->device copy (copy stream) overlaps frame f
+    stages = [torch.empty(n, 2, EMBED, dtype=torch.bfloat16, device=dev) for _ in range(2)]
 
     counters = torch.zeros(n, dtype=torch.int64, device=dev)
     codec = torch.zeros(frames, n, 8, 2, dtype=torch.int64, device=dev)
@@ -268,7 +269,7 @@ def run_ours(args, world, rank, local):
         return out
 
     resident = batches(lambda f: dev_hidden[f])
-    staged = batches(lambda f: stage)
+    staged = batches(lambda f: stages[f % 2])
     shape, weights_c, sampling = eng._shape, eng._w, eng._sampling
     ws, ws_bytes = ctypes.c_void_p(eng.workspace.data_ptr()), eng.workspace.numel()
     launch = L.lib.mtt_b200_launch_local_ar_frame
@@ -287,11 +288,30 @@ def run_ours(args, world, rank, local):
         for f in range(frames):
             frame_call(resident[f], sh)
 
+    copy_stream = torch.cuda.Stream(dev)
+    copied = [torch.cuda.Event() for _ in range(2)]
+    used = [torch.cuda.Event() for _ in range(2)]
+
     def step_e2e():
+        # every step copies each frame's hidden states from pinned host memory and reads the
+        # codec tokens / end-frame indices back; the copy of frame f+1 overlaps frame f
         counters.zero_()
+        copy_stream.wait_stream(stream)  # the copies start inside the timed region
+
+        def stage_copy(f):
+            with torch.cuda.stream(copy_stream):
+                if f >= 2:
+                    copy_stream.wait_event(used[f % 2])  # frame f-2 has read this buffer
+                stages[f % 2].copy_(host_hidden[f], non_blocking=True)
+                copied[f % 2].record(copy_stream)
+
+        stage_copy(0)
         for f in range(frames):
-            stage.copy_(host_hidden[f], non_blocking=True)
+            if f + 1 < frames:
+                stage_copy(f + 1)
+            stream.wait_event(copied[f % 2])
             frame_call(staged[f], sh)
+            used[f % 2].record(stream)
         host_codec.copy_(codec, non_blocking=True)
         host_end.copy_(end, non_blocking=True)
 
@@ -484,8 +504,8 @@ def main():
                 "achieved": tf, "peak": tensor_peak, "unit": "TFLOP/s", "frac": tf / tensor_peak,
                 "peak_kind": f"{peaks_kind} sustained bf16",
                 # dram__bytes_read.sum + dram__bytes_write.sum of one frame-kernel launch from the
-                # ncu captures (profiles/tile_frame_kernel_config4.md at 1024 sessions,
-                # profiles/split_frame_kernel_x4_256sessions.md at 256 sessions)
+                # ncu captures (profiles/pair_frame_kernel_config4.md and tile_frame_kernel_config4.md
+                # at 1024 sessions, profiles/split_frame_kernel_x4_256sessions.md at 256 sessions)
                 "traffic": TRAFFIC.get((res["path"], res["n_local"])),
                 "avg_frame_call_us": t_frame * 1e6,
                 "hbm_achieved_gbs": gbs, "hbm_frac": gbs / peaks["hbm_gbs"],
