@@ -48,7 +48,8 @@ from magpie_tts_rt_b200.model import EMBED, SHAPE_BASELINE, make_weights  # noqa
 
 METRIC = "Local-AR+sampling frames/sec per GPU and box (1/2/4/8); p50 per-frame us"
 PATH_NAMES = {1: "phase kernels", 2: "fused cluster kernel", 3: "tile kernel", 4: "pair kernel",
-              5: "split kernel x1", 6: "split kernel x2", 7: "split kernel x4", 8: "split kernel x8"}
+              5: "split kernel x1", 6: "split kernel x2", 7: "split kernel x4", 8: "split kernel x8",
+              9: "split kernel x2, 32-row tiles"}
 # DRAM bytes per launch of the frame kernel, measured by ncu (path, sessions per GPU)
 TRAFFIC = {("tile kernel", 1024): 27.64e6, ("pair kernel", 1024): 27.70e6, ("split kernel x4", 256): 23.13e6}
 WORKLOADS = {
@@ -496,10 +497,11 @@ def main():
         # call = that kernel + the EOS projection/decision kernels, timed together by CUDA events
         roof = {"bound": "tensor",
                 "kernel": {"tile kernel": "tile_frame_kernel", "pair kernel": "pair_frame_kernel",
-                           "fused cluster kernel": "fused_frame_kernel", "split kernel x1": "split_frame_kernel<1>",
-                           "split kernel x2": "split_frame_kernel<2>",
-                           "split kernel x4": "split_frame_kernel<4>",
-                           "split kernel x8": "split_frame_kernel<8>"}.get(res["path"], res["path"]) +
+                           "fused cluster kernel": "fused_frame_kernel", "split kernel x1": "split_frame_kernel<1, 16>",
+                           "split kernel x2": "split_frame_kernel<2, 16>",
+                           "split kernel x4": "split_frame_kernel<4, 16>",
+                           "split kernel x8": "split_frame_kernel<8, 16>",
+                           "split kernel x2, 32-row tiles": "split_frame_kernel<2, 32>"}.get(res["path"], res["path"]) +
                           " (per frame call, with the EOS projection/decision kernels: 0.6% of device time)",
                 "achieved": tf, "peak": tensor_peak, "unit": "TFLOP/s", "frac": tf / tensor_peak,
                 "peak_kind": f"{peaks_kind} sustained bf16",

@@ -288,7 +288,8 @@ MTT_B200_API int mtt_b200_launch_fold_in_projection(const mtt_b200_local_ar_shap
  * once); FUSED_TILE runs 8 sessions in one CTA with their KV cache in tensor
  * memory; FUSED_PAIR runs 16 sessions on a 2-CTA cluster, each CTA streaming
  * half of every weight matrix; SPLIT_1 / _2 / _4 / _8 run 8 sessions on a
- * cluster of 1, 2, 4 or 8 CTAs, each streaming that fraction of every weight
+ * cluster of 1, 2, 4 or 8 CTAs (SPLIT_2X32: 16 sessions on 2 CTAs), each
+ * streaming that fraction of every weight
  * matrix, with the GEMMs on tcgen05 tensor cores (accumulators and the KV
  * cache in tensor memory).  AUTO picks FUSED_CLUSTER while the batch's tiles
  * fit in one wave of its clusters, then SPLIT_8, _4 and _2 while theirs do
@@ -304,6 +305,7 @@ MTT_B200_API int mtt_b200_launch_fold_in_projection(const mtt_b200_local_ar_shap
 #define MTT_B200_FRAME_PATH_SPLIT_2 6
 #define MTT_B200_FRAME_PATH_SPLIT_4 7
 #define MTT_B200_FRAME_PATH_SPLIT_8 8
+#define MTT_B200_FRAME_PATH_SPLIT_2X32 9
 
 /* Sampling configuration; the reference's values are 80 / 0.6 / 2.5 with CFG
  * and top-k.  argmax != 0 selects greedy decoding (no RNG, counter unchanged;

@@ -105,6 +105,7 @@ PATH_SPLIT_1 = 5
 PATH_SPLIT_2 = 6
 PATH_SPLIT_4 = 7
 PATH_SPLIT_8 = 8
+PATH_SPLIT_2X32 = 9
 
 
 class StreamBatch(ctypes.Structure):

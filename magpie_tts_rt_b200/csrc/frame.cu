@@ -450,13 +450,16 @@ namespace {
 int split_of_path(int32_t path) {
   return path == MTT_B200_FRAME_PATH_SPLIT_8 ? 8
          : path == MTT_B200_FRAME_PATH_SPLIT_4 ? 4
-         : path == MTT_B200_FRAME_PATH_SPLIT_2 ? 2
-                                               : 1;
+         : (path == MTT_B200_FRAME_PATH_SPLIT_2 || path == MTT_B200_FRAME_PATH_SPLIT_2X32) ? 2
+                                                                                          : 1;
 }
+
+int rows_of_path(int32_t path) { return path == MTT_B200_FRAME_PATH_SPLIT_2X32 ? 32 : 16; }
 
 bool is_split_path(int32_t path) {
   return path == MTT_B200_FRAME_PATH_SPLIT_1 || path == MTT_B200_FRAME_PATH_SPLIT_2 ||
-         path == MTT_B200_FRAME_PATH_SPLIT_4 || path == MTT_B200_FRAME_PATH_SPLIT_8;
+         path == MTT_B200_FRAME_PATH_SPLIT_4 || path == MTT_B200_FRAME_PATH_SPLIT_8 ||
+         path == MTT_B200_FRAME_PATH_SPLIT_2X32;
 }
 
 int32_t resolve_path(const mtt_b200_local_ar_shape_t* shape, const mtt_b200_sampling_config_t* sampling,
@@ -479,13 +482,13 @@ int32_t resolve_path(const mtt_b200_local_ar_shape_t* shape, const mtt_b200_samp
         return MTT_B200_FRAME_PATH_FUSED_CLUSTER;
       }
       const int tiles = (n_streams + 7) / 8;  // split kernel tiles
-      if (tiles <= mtt::split_frame_clusters(8) && mtt::split_frame_supported(probe, 8)) {
+      if (tiles <= mtt::split_frame_clusters(8, 16) && mtt::split_frame_supported(probe, 8, 16)) {
         return MTT_B200_FRAME_PATH_SPLIT_8;
       }
-      if (tiles <= mtt::split_frame_clusters(4) && mtt::split_frame_supported(probe, 4)) {
+      if (tiles <= mtt::split_frame_clusters(4, 16) && mtt::split_frame_supported(probe, 4, 16)) {
         return MTT_B200_FRAME_PATH_SPLIT_4;
       }
-      if (tiles <= mtt::split_frame_clusters(2) && mtt::split_frame_supported(probe, 2)) {
+      if (tiles <= mtt::split_frame_clusters(2, 16) && mtt::split_frame_supported(probe, 2, 16)) {
         return MTT_B200_FRAME_PATH_SPLIT_2;
       }
       if (pair && (n_streams + 15) / 16 <= mtt::pair_frame_clusters()) return MTT_B200_FRAME_PATH_FUSED_PAIR;
@@ -505,8 +508,10 @@ int32_t resolve_path(const mtt_b200_local_ar_shape_t* shape, const mtt_b200_samp
     case MTT_B200_FRAME_PATH_SPLIT_2:
     case MTT_B200_FRAME_PATH_SPLIT_4:
     case MTT_B200_FRAME_PATH_SPLIT_8:
-      return mtt::split_frame_supported(probe, split_of_path(sampling->path)) ? sampling->path
-                                                                                 : MTT_B200_STATUS_UNSUPPORTED;
+    case MTT_B200_FRAME_PATH_SPLIT_2X32:
+      return mtt::split_frame_supported(probe, split_of_path(sampling->path), rows_of_path(sampling->path))
+                 ? sampling->path
+                 : MTT_B200_STATUS_UNSUPPORTED;
     default:
       return MTT_B200_STATUS_INVALID_ARGUMENT;
   }
@@ -529,7 +534,8 @@ extern "C" MTT_B200_API int32_t mtt_b200_local_ar_frame_path_clusters(int32_t pa
     case MTT_B200_FRAME_PATH_SPLIT_1:
     case MTT_B200_FRAME_PATH_SPLIT_2:
     case MTT_B200_FRAME_PATH_SPLIT_4:
-    case MTT_B200_FRAME_PATH_SPLIT_8: return mtt::split_frame_clusters(split_of_path(path));
+    case MTT_B200_FRAME_PATH_SPLIT_8:
+    case MTT_B200_FRAME_PATH_SPLIT_2X32: return mtt::split_frame_clusters(split_of_path(path), rows_of_path(path));
     default: return 0;
   }
 }
@@ -645,8 +651,9 @@ extern "C" MTT_B200_API int mtt_b200_launch_local_ar_frame(const mtt_b200_local_
     return launch_pair_frame(f, st) == cudaSuccess ? MTT_B200_STATUS_OK : MTT_B200_STATUS_CUDA_ERROR;
   }
   if (is_split_path(path)) {
-    return launch_split_frame(f, split_of_path(path), st) == cudaSuccess ? MTT_B200_STATUS_OK
-                                                                          : MTT_B200_STATUS_CUDA_ERROR;
+    return launch_split_frame(f, split_of_path(path), rows_of_path(path), st) == cudaSuccess
+               ? MTT_B200_STATUS_OK
+               : MTT_B200_STATUS_CUDA_ERROR;
   }
   const int d = f.d, F = f.F;
   frame_begin_kernel<<<1, kBeginThreads, 0, st>>>(f);

@@ -95,13 +95,14 @@ bool pair_frame_supported(const Frame& f);
 int pair_frame_clusters();
 cudaError_t launch_pair_frame(const Frame& f, cudaStream_t stream);
 
-// Split kernel (frame_split.cu): a cluster of `split` CTAs (1, 2 or 4) per
-// 16-row tile, each streaming 1/split of every weight matrix, GEMMs on
-// tcgen05 with TMEM accumulators.
-bool split_frame_supported(const Frame& f, int split);
+// Split kernel (frame_split.cu): a cluster of `split` CTAs (1, 2, 4, 8) per
+// tile of `rows` rows (16: 8 sessions; 32: 16 sessions, split 2 only), each
+// CTA streaming 1/split of every weight matrix, GEMMs on tcgen05 with TMEM
+// accumulators.
+bool split_frame_supported(const Frame& f, int split, int rows);
 // Clusters of `split` CTAs that fit on the device at once (0: unsupported).
-int split_frame_clusters(int split);
-cudaError_t launch_split_frame(const Frame& f, int split, cudaStream_t stream);
+int split_frame_clusters(int split, int rows);
+cudaError_t launch_split_frame(const Frame& f, int split, int rows, cudaStream_t stream);
 
 // EOS projection + decision for the sessions a fused or tile kernel registered.
 cudaError_t launch_frame_eos(const Frame& f, cudaStream_t stream);

@@ -1,6 +1,7 @@
 // Split frame kernel: a C-CTA thread-block cluster (C = 1, 2, 4 or 8) runs all
 // 16 positions of a Local AR frame for a tile of up to 8 sessions (16 rows
-// with CFG), each CTA streaming 1/C of every weight matrix, with the GEMMs on
+// with CFG; or 16 sessions, 32 rows, on 2 CTAs), each CTA streaming 1/C of
+// every weight matrix, with the GEMMs on
 // the fifth-generation tensor cores (tcgen05.mma, accumulators in tensor
 // memory).  C is picked per batch so that the tiles x C CTAs fill the device:
 // fewer sessions per GPU means more CTAs per session and a shorter frame,
@@ -32,25 +33,28 @@
 //     every CTA                                                  exchange R6
 //   (with C = 1 there are no exchanges).
 //
-// GEMMs (swap-AB): D[128 weight rows][16 tile rows] = W[128][K] x X[16][K]^T
-// on tcgen05.mma kind::f16 M=128 N=16 K=16, A = a weight chunk in shared
+// GEMMs (swap-AB): D[128 weight rows][R tile rows] = W[128][K] x X[R][K]^T
+// on tcgen05.mma kind::f16 M=128 N=R K=16, A = a weight chunk in shared
 // memory, B = the activation rows in shared memory, both K-major with the
 // 128-byte swizzle; one thread issues, tcgen05.commit signals the weight
 // slot free and the accumulator full.  A weight chunk is 128 rows x 128 K
 // columns (32 KB) as four 64 x 64 TMA boxes (no multicast); its two 64-row
 // halves may come from different places of the same matrix (a head's q and
 // k rows, say), and a half that the CTA does not need repeats the first.
-// Weights stream through a four-slot ring filled by a producer warp that
-// runs ahead across GEMMs and positions.  Two accumulator buffers of 16 TMEM
-// columns alternate by M-block, so the epilogue of one block overlaps the
-// MMAs of the next.
+// Weights stream through a four-slot ring (three with 32-row tiles) filled
+// by a producer warp that runs ahead across GEMMs and positions.  With
+// 16-row tiles two accumulator buffers of 16 TMEM columns alternate by
+// M-block, so the epilogue of one block overlaps the MMAs of the next; a
+// 32-row tile has room for one 32-column buffer only.
 //
 // Tensor memory (512 columns x 128 lanes): the KV cache of positions 0..14
-// of the CTA's heads, lane 32 lh + 2 r + half = local head lh, row r, head
-// dims [32 half, +32); K of position j at columns 16 b(j), V at 256 + 16 b(j),
+// of the CTA's heads, lane 32 q + 2 r + half = quadrant q (local head q, or
+// with 32-row tiles head q / 2 and rows 16 (q mod 2)..), row r, head dims
+// [32 half, +32); K of position j at columns 16 b(j), V at V0 + 16 b(j),
 // b(j) = 8 (j mod 2) + j / 2.  Block b(15) is never written (position 15's
-// k/v are read from shared memory), so columns [240, 256) and [496, 512) are
-// the two accumulator buffers.
+// k/v are read from shared memory).  16-row tiles: V0 = 256, so columns
+// [240, 256) and [496, 512) are the two accumulator buffers; 32-row tiles:
+// V0 = 240 and [480, 512) is the one buffer.
 //
 // Exchanges push data with st.async into the receivers' shared memory and
 // complete on the receiver's round mbarrier, which the receiver arms with
@@ -73,8 +77,6 @@ namespace cg = cooperative_groups;
 namespace mtt {
 namespace {
 
-constexpr int kSR = 16;                    // rows per tile
-constexpr int kSS = 8;                     // session slots per tile
 constexpr int kSW = 8;                     // consumer warps
 constexpr int kSC = kSW * 32;              // consumer threads
 constexpr int kSThreads = kSC + 128;       // + the control warpgroup (TMA producer warp, MMA warp)
@@ -84,26 +86,25 @@ static_assert(128 * kSProducerRegs + kSC * kSConsumerRegs <= kSThreads * 168, "r
 constexpr int kD = 256;
 constexpr int kF = 1024;
 constexpr int kHeads = 4;
-constexpr int kSlots = 4;
+constexpr int kMaxSlots = 4;
 constexpr int kChunkRows = 128;
 constexpr int kChunkK = 128;
 constexpr int kPanelElems = kChunkRows * 64;      // one 128-row x 64-column swizzled panel (16 KB)
 constexpr int kChunkElems = 2 * kPanelElems;      // 32 KB
 constexpr uint32_t kChunkBytes = kChunkElems * 2;
 constexpr int kBoxRows = 64;
-constexpr int kOpPanel = kSR * 64;                // one 16-row x 64-column operand panel (2 KB)
 constexpr int kLdX = kD + 8;
-constexpr uint32_t kIdesc = umma_idesc_bf16(128, kSR);
-// TMEM columns of the two accumulator buffers (block b(15) of K and of V).
-__device__ __forceinline__ uint32_t dcol(int db) { return db ? 496u : 240u; }
 constexpr int kListBytes = 2 * (kListCap + 16) + 2 * kListCap;  // candidate list + eligible list (u16)
 
 enum Gemm { G_IN = 0, G_QKV, G_O, G_F1, G_F2, G_HEAD };
 
-template <int C>
+// Tile geometry per cluster size C and tile rows R (16: 8 sessions, 32: 16
+// sessions; R = 32 runs on 2-CTA clusters).
+template <int C, int R>
 struct Cfg {
+  static constexpr int S = R / 2;             // session slots per tile
   static constexpr int nh = C <= kHeads ? kHeads / C : 1;  // heads per CTA (C = 8: a CTA pair shares one)
-  static constexpr int att_rows = C <= kHeads ? kSR : kSR / 2;  // attention rows each CTA sends
+  static constexpr int att_rows = C <= kHeads ? R : R / 2;  // attention rows each CTA sends (C > 1)
   static constexpr int nq = (3 * nh + 1) / 2;  // qkv M-blocks (pairs of 64-row head groups)
   static constexpr int of = kD / C;          // o-projection / residual features per CTA
   static constexpr int no = of >= 128 ? of / 128 : 1;
@@ -111,99 +112,123 @@ struct Cfg {
   static constexpr int nf1 = f1 / 128;
   static constexpr int vs = 2048 / C;        // vocabulary slice per CTA (blocks of 128)
   static constexpr int nhb = vs / 128;
-  static constexpr int own = kSS / C;        // sessions sampled per CTA
+  static constexpr int own = S / C;          // sessions sampled per CTA
   static constexpr int ldq = 3 * nh * 64 + 8;
-  static constexpr int qkv_elems = kSR * ldq;
-  static constexpr int hid_elems = kSR * f1;  // FFN hidden as 16-row panels
+  static constexpr int qkv_elems = R * ldq;
+  static constexpr int hid_elems = R * f1;   // FFN hidden as R-row panels
+  static constexpr int op_panel = R * 64;    // one R-row x 64-column operand panel
+  // The in-projection input (K = 768) is staged in pieces of 256 columns
+  // with 32-row tiles (shared memory), whole with 16-row tiles.
+  static constexpr int in_pieces = R == 32 ? 3 : 1;
+  // Weight ring slots (32 KB each) and accumulator buffers (R TMEM columns
+  // each).  The KV cache takes 480 of the 512 TMEM columns; with 16-row
+  // tiles K and V keep 16-column gaps at 240 and 496 (two buffers), with
+  // 32-row tiles V starts at column 240 and the one buffer is [480, 512).
+  static constexpr int slots = R == 32 ? 3 : 4;
+  static constexpr int nbuf = R == 32 ? 1 : 2;
+  static constexpr uint32_t kv_v = R == 32 ? 240u : 256u;
+  static constexpr uint32_t idesc = umma_idesc_bf16(128, R);
   // Warps per owned session in the sampler: a group of >= 4 warps shares one
   // session (sample_group); with 2 or more sessions per 4 warps each warp
   // samples its own (sample_row), which measured faster there.
   static constexpr int sw = kSW / own >= 4 ? kSW / own : 1;
+  // FFN2 partial sums received: from every CTA (16-row tiles) or only from
+  // the peers, the CTA's own partials staying in registers (32-row tiles).
+  static constexpr int red_slots = C == 1 ? 1 : (R == 32 ? C - 1 : C);
+  static_assert(R == 16 || (R == 32 && C == 2), "32-row tiles run on 2-CTA clusters");
   static_assert(nf1 >= 1 && nhb >= 1 && own >= 1, "split");
+  __device__ static __forceinline__ uint32_t dcol(int db) { return R == 32 ? 480u : (db ? 496u : 240u); }
 };
 
 struct SplitMaps {
   CUtensorMap in_proj, qkv, o, ffn1, ffn2, head;
 };
 
-// Attention exchange between the two warps of a head (scratch in the union).
+// Attention exchange between the two warps of a TMEM lane quadrant (scratch
+// in the union).
 struct SplitAttn {
   float s[2][kHeads][32][8];
   float o[kHeads][32][32];
 };
 
-template <int C>
+template <int C, int R>
 struct __align__(1024) SplitSmem {
-  using K = Cfg<C>;
-  bf16 ring[kSlots][kChunkElems];  // weight chunks (1024-byte aligned panels)
-  bf16 xa[4 * kOpPanel];           // LN output (B operand)
-  bf16 ab[4 * kOpPanel];           // attention output / residual stream copy (B operand)
+  using K = Cfg<C, R>;
+  bf16 ring[K::slots][kChunkElems];  // weight chunks (1024-byte aligned panels)
+  bf16 xa[4 * K::op_panel];          // LN output (B operand); with 32-row tiles also the head
+                                     // values of the other CTA's sessions before sending
+  bf16 ab[4 * K::op_panel];          // attention output / residual stream copy (B operand)
   union U {
-    bf16 src[12 * kOpPanel];                    // in-projection input rows (B operand, K = 768)
+    bf16 src[(12 / K::in_pieces) * K::op_panel];  // in-projection input rows (B operand, K = 768 or a piece)
     SplitAttn att;                              // attention exchange
     bf16 hid[K::hid_elems];                     // FFN hidden slice (B operand)
     struct {
       uint16_t own[K::own][kVocab];             // constrained values of the owned sessions
-      uint16_t out[C > 1 ? kSS : 1][C > 1 ? K::vs : 8];  // this CTA's slice of the other sessions, before sending
+      uint16_t out[C > 1 && R == 16 ? K::S : 1][C > 1 && R == 16 ? K::vs : 8];  // other sessions, before sending
     } v;
   } u;
-  bf16 x[kSR * kLdX];  // residual stream (row-major)
+  bf16 x[R * kLdX];  // residual stream (row-major)
   union Q {
     bf16 qkv[K::qkv_elems];                                  // q | k | v of the CTA's heads
     unsigned char lists[K::own][kListBytes];                 // sampler scratch (one warp per session)
     GroupScratch grp[K::own];                                // sampler scratch (warp groups)
   } q;
-  float red[C > 1 ? C : 1][kSR][C > 1 ? K::of : 1];  // FFN2 partial sums of the owned features, by sender
-  __align__(16) bf16 hb[K::vs];                       // head p bias, this CTA's vocabulary slice
-  int32_t tok[kSS][kPositions];
-  int32_t sess[kSS];
-  uint32_t flags[kSS];  // bit 0 unfinished, bit 1 finished, bit 2 forbid_eos
-  uint32_t nf[kSS];     // non-finite guided logit in this CTA's vocabulary slice, per session
-  uint32_t vmax[kSS];   // largest order key of this CTA's vocabulary slice, per session
+  float red[K::red_slots][R][C > 1 ? K::of : 1];  // FFN2 partial sums of the owned features, by sender
+  __align__(16) bf16 hb[K::vs];                   // head p bias, this CTA's vocabulary slice
+  int32_t tok[K::S][kPositions];
+  int32_t sess[K::S];
+  uint32_t flags[K::S];  // bit 0 unfinished, bit 1 finished, bit 2 forbid_eos
+  uint32_t nf[K::S];     // non-finite guided logit in this CTA's vocabulary slice, per session
+  uint32_t vmax[K::S];   // largest order key of this CTA's vocabulary slice, per session
   uint32_t peer_nf[C][K::own];  // from each peer: non-finite flag << 16 | its slice's largest key
   int64_t ctr[K::own];
   int64_t seed[K::own];
   int32_t inv[K::own];
-  int32_t last_issued[kSlots];
+  int32_t last_issued[kMaxSlots];
   int32_t n_sess;
   int32_t err;
   int32_t producer_done;
   int32_t mma_done;
   uint32_t tmem;
-  unsigned long long full[kSlots];
-  unsigned long long empty[kSlots];
+  unsigned long long full[kMaxSlots];
+  unsigned long long empty[kMaxSlots];
   unsigned long long dfull[2];
   unsigned long long dempty[2];
   unsigned long long opready;
+  unsigned long long srcfree;  // the MMAs have read an in-projection input piece
   unsigned long long mmafin;
   unsigned long long xbar[2];
 };
 
-template <int C>
+template <int C, int R>
 constexpr size_t split_smem_bytes() {
-  return sizeof(SplitSmem<C>) + 1024;
+  return sizeof(SplitSmem<C, R>) + 1024;
 }
-static_assert(split_smem_bytes<1>() <= 232448 && split_smem_bytes<2>() <= 232448 && split_smem_bytes<4>() <= 232448 &&
-                  split_smem_bytes<8>() <= 232448,
+static_assert(split_smem_bytes<1, 16>() <= 232448 && split_smem_bytes<2, 16>() <= 232448 &&
+                  split_smem_bytes<4, 16>() <= 232448 && split_smem_bytes<8, 16>() <= 232448 &&
+                  split_smem_bytes<2, 32>() <= 232448,
               "split kernel shared memory");
 
-template <int C>
-__device__ __forceinline__ int err_flag(const SplitSmem<C>& sm) {
+template <int C, int R>
+__device__ __forceinline__ int err_flag(const SplitSmem<C, R>& sm) {
   return *reinterpret_cast<const volatile int*>(&sm.err);
 }
 __device__ __forceinline__ void cbar() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
 
-// Byte offset of element (row r, column k) of a 16-row operand stored as
+// Byte offset of element (row r, column k) of an R-row operand stored as
 // 64-column panels with the 128-byte swizzle.
+template <int R>
 __device__ __forceinline__ int op_off(int r, int k) {
-  return (k >> 6) * (kOpPanel * 2) + r * 128 + ((((k & 63) >> 3) ^ (r & 7)) << 4) + ((k & 7) << 1);
+  return (k >> 6) * (R * 128) + r * 128 + ((((k & 63) >> 3) ^ (r & 7)) << 4) + ((k & 7) << 1);
 }
+template <int R>
 __device__ __forceinline__ void op_store(bf16* base, int r, int k, bf16 v) {
-  *reinterpret_cast<bf16*>(reinterpret_cast<unsigned char*>(base) + op_off(r, k)) = v;
+  *reinterpret_cast<bf16*>(reinterpret_cast<unsigned char*>(base) + op_off<R>(r, k)) = v;
 }
 // 16-byte unit (8 columns from k, k % 8 == 0).
+template <int R>
 __device__ __forceinline__ uint4* op_unit(bf16* base, int r, int k) {
-  return reinterpret_cast<uint4*>(reinterpret_cast<unsigned char*>(base) + op_off(r, k));
+  return reinterpret_cast<uint4*>(reinterpret_cast<unsigned char*>(base) + op_off<R>(r, k));
 }
 
 // ---------------------------------------------------------------------------
@@ -212,9 +237,9 @@ __device__ __forceinline__ uint4* op_unit(bf16* base, int r, int k) {
 
 __device__ __forceinline__ bool has_in_projection(bool folded, int p) { return p == 0 || !folded; }
 
-template <int C>
+template <int C, int R>
 __device__ __forceinline__ int gemm_blocks(int g) {
-  using K = Cfg<C>;
+  using K = Cfg<C, R>;
   switch (g) {
     case G_IN: return 2;
     case G_QKV: return K::nq;
@@ -225,31 +250,31 @@ __device__ __forceinline__ int gemm_blocks(int g) {
   }
 }
 
-template <int C>
+template <int C, int R>
 __device__ __forceinline__ int gemm_kchunks(int g) {
-  return g == G_IN ? kEmbed / kChunkK : (g == G_F2 ? Cfg<C>::f1 / kChunkK : kD / kChunkK);
+  return g == G_IN ? kEmbed / kChunkK : (g == G_F2 ? Cfg<C, R>::f1 / kChunkK : kD / kChunkK);
 }
 
 // First (global) head of CTA c: nh heads each, or with 8 CTAs head c / 2
 // for the pair 2h, 2h + 1 (both compute it; each sends half of its rows).
-template <int C>
+template <int C, int R>
 __device__ __forceinline__ int head_base(int c) {
-  return C <= kHeads ? c * Cfg<C>::nh : c / 2;
+  return C <= kHeads ? c * Cfg<C, R>::nh : c / 2;
 }
 
 // Weight rows of the head group gi (q groups, then k, then v; nh per type).
-template <int C>
+template <int C, int R>
 __device__ __forceinline__ int qkv_group_row(int c, int gi) {
-  using K = Cfg<C>;
-  return kD * (gi / K::nh) + kHeadDim * (head_base<C>(c) + gi % K::nh);
+  using K = Cfg<C, R>;
+  return kD * (gi / K::nh) + kHeadDim * (head_base<C, R>(c) + gi % K::nh);
 }
 
 // Tensor map and origins of chunk (M-block b, K-chunk k) of GEMM g: K column
 // x0, rows ra (A rows 0..63) and rb (A rows 64..127).
-template <int C>
+template <int C, int R>
 __device__ __forceinline__ const CUtensorMap* chunk_box(const SplitMaps& m, int c, int p, int g, int b, int k, int* x0,
                                                         int* ra, int* rb) {
-  using K = Cfg<C>;
+  using K = Cfg<C, R>;
   *x0 = kChunkK * k;
   switch (g) {
     case G_IN:
@@ -258,8 +283,8 @@ __device__ __forceinline__ const CUtensorMap* chunk_box(const SplitMaps& m, int 
       return &m.in_proj;
     case G_QKV: {
       const int ga = 2 * b, gb = 2 * b + 1 < 3 * K::nh ? 2 * b + 1 : 2 * b;
-      *ra = qkv_group_row<C>(c, ga);
-      *rb = qkv_group_row<C>(c, gb);
+      *ra = qkv_group_row<C, R>(c, ga);
+      *rb = qkv_group_row<C, R>(c, gb);
       return &m.qkv;
     }
     case G_O: {
@@ -288,19 +313,20 @@ __device__ __forceinline__ const CUtensorMap* chunk_box(const SplitMaps& m, int 
   }
 }
 
-template <int C>
-__device__ void producer(SplitSmem<C>& sm, const SplitMaps& maps, int c, bool folded) {
+template <int C, int R>
+__device__ void producer(SplitSmem<C, R>& sm, const SplitMaps& maps, int c, bool folded) {
   int it = 0;
   for (int p = 0; p < kPositions; ++p) {
     for (int g = has_in_projection(folded, p) ? G_IN : G_QKV; g <= G_HEAD; ++g) {
-      const int nb = gemm_blocks<C>(g), nk = gemm_kchunks<C>(g);
+      const int nb = gemm_blocks<C, R>(g), nk = gemm_kchunks<C, R>(g);
       for (int b = 0; b < nb; ++b) {
         for (int k = 0; k < nk; ++k, ++it) {
-          const int slot = it % kSlots;
-          if (it >= kSlots && err_flag(sm) == 0 && !mbar_wait(&sm.empty[slot], ((it / kSlots) - 1) & 1)) sm.err = 1;
+          constexpr int kSl = Cfg<C, R>::slots;
+          const int slot = it % kSl;
+          if (it >= kSl && err_flag(sm) == 0 && !mbar_wait(&sm.empty[slot], ((it / kSl) - 1) & 1)) sm.err = 1;
           if (err_flag(sm)) return;
           int x0, ra, rb;
-          const CUtensorMap* map = chunk_box<C>(maps, c, p, g, b, k, &x0, &ra, &rb);
+          const CUtensorMap* map = chunk_box<C, R>(maps, c, p, g, b, k, &x0, &ra, &rb);
           mbar_expect_tx(&sm.full[slot], kChunkBytes);
           bf16* dst = sm.ring[slot];
           tma_load_2d(dst, map, x0, ra, &sm.full[slot]);
@@ -314,8 +340,8 @@ __device__ void producer(SplitSmem<C>& sm, const SplitMaps& maps, int c, bool fo
   }
 }
 
-template <int C>
-__device__ __forceinline__ const bf16* gemm_operand(SplitSmem<C>& sm, int g) {
+template <int C, int R>
+__device__ __forceinline__ const bf16* gemm_operand(SplitSmem<C, R>& sm, int g) {
   switch (g) {
     case G_IN: return sm.u.src;
     case G_QKV: return sm.xa;
@@ -329,29 +355,39 @@ __device__ __forceinline__ const bf16* gemm_operand(SplitSmem<C>& sm, int g) {
 // The MMA warp's single thread: for every GEMM, wait until the consumers have
 // written its B operand, then per M-block wait for a free accumulator buffer,
 // per chunk wait for the weights, issue 8 MMAs (K = 128) and free the slot.
-template <int C>
-__device__ void mma_issuer(SplitSmem<C>& sm, bool folded) {
+// With 32-row tiles the in-projection input comes in three 256-column pieces
+// per M-block: each piece has its own operand-ready phase, and a commit on
+// `srcfree` tells the consumers when its MMAs have read it.
+template <int C, int R>
+__device__ void mma_issuer(SplitSmem<C, R>& sm, bool folded) {
+  using K = Cfg<C, R>;
   int it = 0, mb = 0, gn = 0;
+  auto wait_operand = [&]() {
+    const bool ok = mbar_wait(&sm.opready, gn & 1);
+    ++gn;
+    if (!ok) sm.err = 1;
+    tmem_fence_after_sync();
+    return ok;
+  };
   for (int p = 0; p < kPositions && err_flag(sm) == 0; ++p) {
-    for (int g = has_in_projection(folded, p) ? G_IN : G_QKV; g <= G_HEAD && err_flag(sm) == 0; ++g, ++gn) {
-      if (!mbar_wait(&sm.opready, gn & 1)) {
-        sm.err = 1;
-        break;
-      }
-      tmem_fence_after_sync();
+    for (int g = has_in_projection(folded, p) ? G_IN : G_QKV; g <= G_HEAD && err_flag(sm) == 0; ++g) {
+      const bool pieces = g == G_IN && K::in_pieces > 1;
+      if (!pieces && !wait_operand()) break;
       const bf16* bop = gemm_operand(sm, g);
-      const int nb = gemm_blocks<C>(g), nk = gemm_kchunks<C>(g);
+      const int nb = gemm_blocks<C, R>(g), nk = gemm_kchunks<C, R>(g);
       for (int b = 0; b < nb && err_flag(sm) == 0; ++b, ++mb) {
-        const int db = mb & 1;
-        if (mb >= 2 && !mbar_wait(&sm.dempty[db], ((mb >> 1) - 1) & 1)) {
+        const int db = mb % K::nbuf, use = mb / K::nbuf;
+        if (use >= 1 && !mbar_wait(&sm.dempty[db], (use - 1) & 1)) {
           sm.err = 1;
           break;
         }
         tmem_fence_after_sync();
-        const uint32_t d = sm.tmem + dcol(db);
+        const uint32_t d = sm.tmem + K::dcol(db);
         for (int k = 0; k < nk; ++k, ++it) {
-          const int slot = it % kSlots;
-          if (!mbar_wait(&sm.full[slot], (it / kSlots) & 1)) {
+          if (pieces && (k & 1) == 0 && !wait_operand()) break;
+          const int kc = pieces ? (k & 1) : k;  // K-chunk within the operand buffer
+          const int slot = it % K::slots;
+          if (!mbar_wait(&sm.full[slot], (it / K::slots) & 1)) {
             sm.err = 1;
             break;
           }
@@ -359,10 +395,11 @@ __device__ void mma_issuer(SplitSmem<C>& sm, bool folded) {
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk) {
             const uint64_t a = umma_desc_sw128(sm.ring[slot] + (kk >> 2) * kPanelElems) + 2 * (kk & 3);
-            const uint64_t bd = umma_desc_sw128(bop + (2 * k + (kk >> 2)) * kOpPanel) + 2 * (kk & 3);
-            umma_bf16(d, a, bd, kIdesc, (k | kk) != 0);
+            const uint64_t bd = umma_desc_sw128(bop + (2 * kc + (kk >> 2)) * K::op_panel) + 2 * (kk & 3);
+            umma_bf16(d, a, bd, K::idesc, (k | kk) != 0);
           }
           umma_commit(&sm.empty[slot]);
+          if (pieces && (k & 1) == 1) umma_commit(&sm.srcfree);
         }
         umma_commit(&sm.dfull[db]);
       }
@@ -374,45 +411,75 @@ __device__ void mma_issuer(SplitSmem<C>& sm, bool folded) {
   atomicExch(&sm.mma_done, 1);
 }
 
+// Two loads of N TMEM columns (lanes of this warp's quadrant) and one wait.
+template <int N>
+__device__ __forceinline__ void tmem_ld_pair(uint32_t (&v)[2 * N], uint32_t ta, uint32_t tb) {
+  static_assert(N == 4 || N == 8, "width");
+  if constexpr (N == 4) {
+    tmem_ld4x2(v, ta, tb);
+  } else {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                 : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7])
+                 : "r"(ta)
+                 : "memory");
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                 : "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]),
+                   "=r"(v[15])
+                 : "r"(tb)
+                 : "memory");
+    asm volatile("tcgen05.wait::ld.sync.aligned;"
+                 : "+r"(v[0]), "+r"(v[1]), "+r"(v[2]), "+r"(v[3]), "+r"(v[4]), "+r"(v[5]), "+r"(v[6]), "+r"(v[7]),
+                   "+r"(v[8]), "+r"(v[9]), "+r"(v[10]), "+r"(v[11]), "+r"(v[12]), "+r"(v[13]), "+r"(v[14]),
+                   "+r"(v[15])
+                 :
+                 : "memory");
+  }
+}
+
 // Epilogue helpers: warp w reads TMEM lanes [32 (w % 4), +32) (A rows m),
-// columns of sessions [4 (w / 4), +4): v[i] = row 4 (w / 4) + i (conditional),
-// v[4 + i] = row 8 + 4 (w / 4) + i (unconditional).
-template <int C>
-__device__ __forceinline__ void load_block(SplitSmem<C>& sm, int mb, float (&v)[8]) {
+// the columns of session slots [S/2 (w / 4), +S/2): v[i] = row S/2 (w / 4) + i
+// (conditional), v[S/2 + i] = row S + S/2 (w / 4) + i (unconditional).
+template <int C, int R>
+__device__ __forceinline__ void load_block(SplitSmem<C, R>& sm, int mb, float (&v)[R / 2]) {
+  using K = Cfg<C, R>;
+  constexpr int H = R / 4;  // sessions per warp half
   const int warp = threadIdx.x >> 5;
-  const int db = mb & 1;
-  if (err_flag(sm) == 0 && !mbar_wait(&sm.dfull[db], (mb >> 1) & 1)) sm.err = 1;
+  const int db = mb % K::nbuf, use = mb / K::nbuf;
+  if (err_flag(sm) == 0 && !mbar_wait(&sm.dfull[db], use & 1)) sm.err = 1;
   tmem_fence_after_sync();
-  const uint32_t ta = sm.tmem + (static_cast<uint32_t>(32 * (warp & 3)) << 16) + dcol(db) + 4 * (warp >> 2);
-  uint32_t r[8];
-  tmem_ld4x2(r, ta, ta + 8);
+  const uint32_t ta = sm.tmem + (static_cast<uint32_t>(32 * (warp & 3)) << 16) + K::dcol(db) + H * (warp >> 2);
+  uint32_t r[R / 2];
+  tmem_ld_pair<H>(r, ta, ta + R / 2);
   tmem_fence_before_sync();
   __syncwarp();
   if ((threadIdx.x & 31) == 0) mbar_arrive(&sm.dempty[db]);
 #pragma unroll
-  for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
+  for (int i = 0; i < R / 2; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+template <int R>
 __device__ __forceinline__ int epi_row(int i) {
+  constexpr int H = R / 4;
   const int sh = (threadIdx.x >> 5) >> 2;
-  return i < 4 ? 4 * sh + i : 8 + 4 * sh + (i - 4);
+  return i < H ? H * sh + i : R / 2 + H * sh + (i - H);
 }
 
 // B operand written: order the generic writes before the MMA warp's reads.
-template <int C>
-__device__ __forceinline__ void operand_ready(SplitSmem<C>& sm) {
+template <int C, int R>
+__device__ __forceinline__ void operand_ready(SplitSmem<C, R>& sm) {
   fence_proxy_async();
   cbar();
   if (threadIdx.x == 0) mbar_arrive(&sm.opready);
 }
 
-// LayerNorm (no bias, eps 1e-5) of the 16 rows of x into the B operand xa;
-// lane holds weights g of columns [8 lane, +8); warp w: rows 2w, 2w+1.
+// LayerNorm (no bias, eps 1e-5) of the R rows of x into the B operand xa;
+// lane holds weights g of columns [8 lane, +8); warp w: rows R/8 w + [0, R/8).
+template <int R>
 __device__ __forceinline__ void layer_norm_op(const bf16* x, bf16* xa, const float (&g)[8]) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
 #pragma unroll
-  for (int rr = 0; rr < 2; ++rr) {
-    const int r = 2 * warp + rr;
+  for (int rr = 0; rr < R / 8; ++rr) {
+    const int r = (R / 8) * warp + rr;
     float v[8];
     unpack8(*reinterpret_cast<const uint4*>(x + r * kLdX + lane * 8), v);
     float sum = 0.f;
@@ -430,15 +497,16 @@ __device__ __forceinline__ void layer_norm_op(const bf16* x, bf16* xa, const flo
     float out[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) out[j] = ((v[j] - mean) * rstd) * g[j];
-    *op_unit(xa, r, lane * 8) = pack8(out);
+    *op_unit<R>(xa, r, lane * 8) = pack8(out);
   }
 }
 
 // x (row-major) -> the B operand ab (the head's input).
+template <int R>
 __device__ __forceinline__ void x_to_operand(const bf16* x, bf16* ab) {
-  for (int i = threadIdx.x; i < kSR * (kD / 8); i += kSC) {
+  for (int i = threadIdx.x; i < R * (kD / 8); i += kSC) {
     const int r = i / (kD / 8), k8 = 8 * (i % (kD / 8));
-    *op_unit(ab, r, k8) = *reinterpret_cast<const uint4*>(x + r * kLdX + k8);
+    *op_unit<R>(ab, r, k8) = *reinterpret_cast<const uint4*>(x + r * kLdX + k8);
   }
 }
 
@@ -452,8 +520,8 @@ __device__ __forceinline__ void x_to_operand(const bf16* x, bf16* ab) {
 // CTA arrives on another's barrier: a peer's data arriving already shows
 // that the peer finished the phase before it, because every push follows
 // the pusher's last use of the buffers the round before it filled.
-template <int C>
-__device__ __forceinline__ void finish_round(SplitSmem<C>& sm, uint32_t& rd, uint32_t bytes_in) {
+template <int C, int R>
+__device__ __forceinline__ void finish_round(SplitSmem<C, R>& sm, uint32_t& rd, uint32_t bytes_in) {
   cbar();
   const int bar = static_cast<int>(rd & 1u);
   if (threadIdx.x == 0) mbar_expect_tx(&sm.xbar[bar], bytes_in);
@@ -463,38 +531,41 @@ __device__ __forceinline__ void finish_round(SplitSmem<C>& sm, uint32_t& rd, uin
 
 // Vocabulary values CTA j of the cluster holds of each session (its slice of
 // the head output, clipped to the vocabulary).
-template <int C>
+template <int C, int R>
 __host__ __device__ constexpr int slice_len(int j) {
-  return Cfg<C>::vs * (j + 1) <= kVocab ? Cfg<C>::vs : kVocab - Cfg<C>::vs * j;
+  return Cfg<C, R>::vs * (j + 1) <= kVocab ? Cfg<C, R>::vs : kVocab - Cfg<C, R>::vs * j;
 }
 
 // Bytes CTA c receives in the head-values round: from every peer j, its
 // slice of each of c's sessions plus one non-finite flag per session.
-template <int C>
+template <int C, int R>
 __device__ __forceinline__ uint32_t values_bytes_in(int c) {
   uint32_t b = 0;
 #pragma unroll
   for (int j = 0; j < C; ++j) {
-    if (j != c) b += static_cast<uint32_t>(Cfg<C>::own * (slice_len<C>(j) * 2 + 4));
+    if (j != c) b += static_cast<uint32_t>(Cfg<C, R>::own * (slice_len<C, R>(j) * 2 + 4));
   }
   return b;
 }
 
 // ---------------------------------------------------------------------------
-// attention over the TMEM KV cache for the CTA's heads: warp w, local head
-// lh = w % 4 (< nh), part = w / 4 (positions of parity part); thread t: row
-// t / 2, head dims [32 (t % 2), +32).  Output to the operand ab at the global
-// head's columns, and pushed to every peer.
+// attention over the TMEM KV cache for the CTA's heads: warp w reads lane
+// quadrant q = w % 4, which holds local head q (16-row tiles) or head q / 2,
+// rows 16 (q % 2).. (32-row tiles); part = w / 4 takes the positions of
+// parity part; thread t: row t / 2 of the quadrant, head dims
+// [32 (t % 2), +32).  Output to the operand ab at the global head's columns,
+// and pushed to every peer.
 // ---------------------------------------------------------------------------
 
-template <int C>
-__device__ __forceinline__ void attention(SplitSmem<C>& sm, int p, int c, uint32_t rd) {
-  using K = Cfg<C>;
+template <int C, int R>
+__device__ __forceinline__ void attention(SplitSmem<C, R>& sm, int p, int c, uint32_t rd) {
+  using K = Cfg<C, R>;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int lh = warp & 3, part = warp >> 2;
+  const int q4 = warp & 3, part = warp >> 2;
+  const int lh = R == 32 ? q4 >> 1 : q4;  // local head of this quadrant
   const bool active = lh < K::nh;
-  const int r = lane >> 1, half = lane & 1;
-  const uint32_t tl = sm.tmem + (static_cast<uint32_t>(32 * lh) << 16);
+  const int r = (R == 32 ? 16 * (q4 & 1) : 0) + (lane >> 1), half = lane & 1;
+  const uint32_t tl = sm.tmem + (static_cast<uint32_t>(32 * q4) << 16);
   const bf16* qrow = sm.q.qkv + r * K::ldq + kHeadDim * lh + 32 * half;
   const bf16* krow = qrow + K::nh * kHeadDim;
   const bf16* vrow = krow + K::nh * kHeadDim;
@@ -511,7 +582,7 @@ __device__ __forceinline__ void attention(SplitSmem<C>& sm, int p, int c, uint32
         kv[4 * j + 2] = t.z;
         kv[4 * j + 3] = t.w;
       }
-      tmem_st16(tl + 256 * part + 16 * tmem_block(p), kv);
+      tmem_st16(tl + K::kv_v * part + 16 * tmem_block(p), kv);
       tmem_wait_st();
     }
 #pragma unroll
@@ -559,7 +630,7 @@ __device__ __forceinline__ void attention(SplitSmem<C>& sm, int p, int c, uint32
         }
       }
     }
-    float* my_s = sm.u.att.s[part][lh][lane];
+    float* my_s = sm.u.att.s[part][q4][lane];
 #pragma unroll
     for (int m = 0; m < 8; ++m) my_s[m] = s[m];
   }
@@ -571,8 +642,8 @@ __device__ __forceinline__ void attention(SplitSmem<C>& sm, int p, int c, uint32
     float all[kPositions];
 #pragma unroll
     for (int m = 0; m < 8; ++m) {
-      all[2 * m] = sm.u.att.s[0][lh][lane][m];
-      all[2 * m + 1] = sm.u.att.s[1][lh][lane][m];
+      all[2 * m] = sm.u.att.s[0][q4][lane][m];
+      all[2 * m + 1] = sm.u.att.s[1][q4][lane][m];
     }
     float mx = all[0];
 #pragma unroll
@@ -587,7 +658,7 @@ __device__ __forceinline__ void attention(SplitSmem<C>& sm, int p, int c, uint32
     for (int g4 = 0; g4 < 2; ++g4) {
       if (8 * g4 + part <= p) {
         uint32_t v[64];
-        tmem_ld64(v, tl + 256 + 16 * (8 * part + 4 * g4));
+        tmem_ld64(v, tl + K::kv_v + 16 * (8 * part + 4 * g4));
         if (p == kPositions - 1 && part == 1 && g4 == 1) {
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
@@ -614,17 +685,17 @@ __device__ __forceinline__ void attention(SplitSmem<C>& sm, int p, int c, uint32
       }
     }
     if (part == 1) {
-      float* dst = sm.u.att.o[lh][lane];
+      float* dst = sm.u.att.o[q4][lane];
 #pragma unroll
       for (int d = 0; d < 32; ++d) dst[d] = o[d];
     }
   }
   cbar();
   if (active && part == 0) {
-    const float* src = sm.u.att.o[lh][lane];
+    const float* src = sm.u.att.o[q4][lane];
 #pragma unroll
     for (int d = 0; d < 32; ++d) o[d] += src[d];
-    const int col = kHeadDim * (head_base<C>(c) + lh) + 32 * half;
+    const int col = kHeadDim * (head_base<C, R>(c) + lh) + 32 * half;
     const bool send = C <= kHeads || (r >> 3) == (c & 1);
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
@@ -632,7 +703,7 @@ __device__ __forceinline__ void attention(SplitSmem<C>& sm, int p, int c, uint32
 #pragma unroll
       for (int e = 0; e < 8; ++e) f8[e] = o[8 * j + e];
       const uint4 u = pack8(f8);
-      uint4* dst = op_unit(sm.ab, r, col + 8 * j);
+      uint4* dst = op_unit<R>(sm.ab, r, col + 8 * j);
       *dst = u;
       if constexpr (C > 1) {
         if (send) {
@@ -650,8 +721,8 @@ __device__ __forceinline__ void attention(SplitSmem<C>& sm, int p, int c, uint32
 // the kernel
 // ---------------------------------------------------------------------------
 
-template <int C>
-__device__ __forceinline__ int64_t input_token(const Frame& f, const SplitSmem<C>& sm, int slot, int p) {
+template <int C, int R>
+__device__ __forceinline__ int64_t input_token(const Frame& f, const SplitSmem<C, R>& sm, int slot, int p) {
   if (f.forced) {
     const int64_t t = f.forced[static_cast<int64_t>(sm.sess[slot]) * kPositions + p];
     return t < 0 ? 0 : (t >= kVocab ? kVocab - 1 : t);
@@ -659,12 +730,12 @@ __device__ __forceinline__ int64_t input_token(const Frame& f, const SplitSmem<C
   return sm.tok[slot][p];
 }
 
-template <int C>
+template <int C, int R>
 __global__ void __launch_bounds__(kSThreads, 1) split_frame_kernel(Frame f, const __grid_constant__ SplitMaps maps) {
-  using K = Cfg<C>;
+  using K = Cfg<C, R>;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   const uint32_t pad = (1024u - (smem_addr(smem_raw) & 1023u)) & 1023u;
-  SplitSmem<C>& sm = *reinterpret_cast<SplitSmem<C>*>(smem_raw + pad);
+  SplitSmem<C, R>& sm = *reinterpret_cast<SplitSmem<C, R>*>(smem_raw + pad);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int rp = f.rp;
   const bool folded = f.emb_proj != nullptr;
@@ -672,21 +743,21 @@ __global__ void __launch_bounds__(kSThreads, 1) split_frame_kernel(Frame f, cons
   if constexpr (C > 1) c = static_cast<int>(cg::this_cluster().block_rank());
   const int tile = static_cast<int>(blockIdx.x) / C;
 
-  // ---- sessions [8 tile, +8) of the active list (every CTA of the cluster)
+  // ---- sessions [S tile, +S) of the active list (every CTA of the cluster)
   if (warp == 0) {
     int seen = 0;
-    const int first = kSS * tile;
+    const int first = K::S * tile;
     for (int base = 0; base < f.n; base += 32) {
       const int s = base + lane;
       const bool act = s < f.n && (f.active == nullptr || f.active[s]);
       const unsigned m = __ballot_sync(0xffffffffu, act);
       const int rank = seen + __popc(m & ((1u << lane) - 1u));
-      if (act && rank >= first && rank < first + kSS) sm.sess[rank - first] = s;
+      if (act && rank >= first && rank < first + K::S) sm.sess[rank - first] = s;
       seen += __popc(m);
     }
     if (lane == 0) {
       const int left = seen - first;
-      sm.n_sess = left <= 0 ? 0 : (left < kSS ? left : kSS);
+      sm.n_sess = left <= 0 ? 0 : (left < K::S ? left : K::S);
       sm.err = 0;
       sm.producer_done = 0;
       sm.mma_done = 0;
@@ -695,12 +766,13 @@ __global__ void __launch_bounds__(kSThreads, 1) split_frame_kernel(Frame f, cons
   __syncthreads();
   const int n_sess = sm.n_sess;
   if (n_sess == 0) return;  // the same in every CTA of the cluster: none touches another
-  auto live = [&](int r) { return (r & 7) < n_sess && (r >> 3) < rp; };
+  // row r belongs to session slot r % S (sub-row r / S)
+  auto live = [&](int r) { return (r % K::S) < n_sess && (r / K::S) < rp; };
   const int own0 = K::own * c;
   const int n_own = n_sess - own0 <= 0 ? 0 : (n_sess - own0 < K::own ? n_sess - own0 : K::own);
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kSlots; ++s) {
+    for (int s = 0; s < K::slots; ++s) {
       mbar_init(&sm.full[s], 1);
       mbar_init(&sm.empty[s], 1);
       sm.last_issued[s] = -1;
@@ -711,6 +783,7 @@ __global__ void __launch_bounds__(kSThreads, 1) split_frame_kernel(Frame f, cons
       mbar_init(&sm.xbar[b], 1);
     }
     mbar_init(&sm.opready, 1);
+    mbar_init(&sm.srcfree, 1);
     mbar_init(&sm.mmafin, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -751,15 +824,15 @@ __global__ void __launch_bounds__(kSThreads, 1) split_frame_kernel(Frame f, cons
   if (warp >= kSW) {  // control warpgroup
     asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kSProducerRegs));
     if (warp == kSW && lane == 0) {
-      producer<C>(sm, maps, c, folded);
+      producer<C, R>(sm, maps, c, folded);
       // no copy may still be writing when the CTA leaves
-      for (int s = 0; s < kSlots; ++s) {
+      for (int s = 0; s < K::slots; ++s) {
         const int last = sm.last_issued[s];
-        if (last >= 0) mbar_wait(&sm.full[s], (last / kSlots) & 1);
+        if (last >= 0) mbar_wait(&sm.full[s], (last / K::slots) & 1);
       }
       atomicExch(&sm.producer_done, 1);
     } else if (warp == kSW + 1 && lane == 0) {
-      mma_issuer<C>(sm, folded);
+      mma_issuer<C, R>(sm, folded);
     }
     return;
   }
@@ -772,37 +845,54 @@ __global__ void __launch_bounds__(kSThreads, 1) split_frame_kernel(Frame f, cons
     const int m_lane = 32 * q4 + lane;  // A row of an M-block held by this thread
     const bool cfg = rp == 2;
     const float cfg_scale = f.prm.cfg_scale, uncond_scale = __fsub_rn(1.0f, f.prm.cfg_scale);
-    int mb = 0;       // M-blocks consumed
-    uint32_t rd = 0;  // exchange rounds
+    int mb = 0;          // M-blocks consumed
+    uint32_t rd = 0;     // exchange rounds
+    int src_pieces = 0;  // in-projection input pieces staged (32-row tiles)
     for (int p = 0; p < kPositions; ++p) {
       // ---------------- input rows
       if (has_in_projection(folded, p)) {
-        for (int i = threadIdx.x; i < kSR * (kEmbed / 8); i += kSC) {
-          const int r = i / (kEmbed / 8), k8 = 8 * (i % (kEmbed / 8));
-          uint4 v = make_uint4(0, 0, 0, 0);
-          if (live(r)) {
-            const int slot = r & 7, sub = r >> 3;
-            const bf16* src;
-            if (p == 0) {
-              src = f.hidden + (static_cast<int64_t>(sm.sess[slot]) * rp + sub) * kEmbed;
-            } else {
-              src = f.emb + (static_cast<int64_t>(p - 1) * kVocab + input_token(f, sm, slot, p - 1)) * kEmbed;
+        // the rows' 768 inputs (p = 0: decoder hidden; else the sampled token's
+        // embedding), whole or in pieces of 256 columns per M-block
+        auto stage_src = [&](int piece) {
+          constexpr int kw = kEmbed / K::in_pieces;
+          for (int i = threadIdx.x; i < R * (kw / 8); i += kSC) {
+            const int r = i / (kw / 8), k8 = 8 * (i % (kw / 8));
+            uint4 v = make_uint4(0, 0, 0, 0);
+            if (live(r)) {
+              const int slot = r % K::S, sub = r / K::S;
+              const bf16* src;
+              if (p == 0) {
+                src = f.hidden + (static_cast<int64_t>(sm.sess[slot]) * rp + sub) * kEmbed;
+              } else {
+                src = f.emb + (static_cast<int64_t>(p - 1) * kVocab + input_token(f, sm, slot, p - 1)) * kEmbed;
+              }
+              v = *reinterpret_cast<const uint4*>(src + kw * piece + k8);
             }
-            v = *reinterpret_cast<const uint4*>(src + k8);
+            *op_unit<R>(sm.u.src, r, k8) = v;
           }
-          *op_unit(sm.u.src, r, k8) = v;
+        };
+        if constexpr (K::in_pieces == 1) {
+          stage_src(0);
+          operand_ready(sm);
         }
-        operand_ready(sm);
         const bf16* pos = f.pos + static_cast<int64_t>(p) * kD;
         for (int b = 0; b < 2; ++b, ++mb) {
-          float v[8];
+          if constexpr (K::in_pieces > 1) {
+            for (int piece = 0; piece < K::in_pieces; ++piece, ++src_pieces) {
+              // the MMAs of the previous piece have read the buffer
+              if (src_pieces > 0 && err_flag(sm) == 0 && !mbar_wait(&sm.srcfree, (src_pieces - 1) & 1)) sm.err = 1;
+              stage_src(piece);
+              operand_ready(sm);
+            }
+          }
+          float v[R / 2];
           load_block(sm, mb, v);
           const int n = 128 * b + m_lane;
           const float bias = bf2f(f.in_b[n]), pe = bf2f(pos[n]);
 #pragma unroll
-          for (int i = 0; i < 8; ++i) {
+          for (int i = 0; i < R / 2; ++i) {
             const float y = round_bf16(__fadd_rn(v[i], bias));
-            sm.x[epi_row(i) * kLdX + n] = f2bf(__fadd_rn(y, pe));
+            sm.x[epi_row<R>(i) * kLdX + n] = f2bf(__fadd_rn(y, pe));
           }
         }
       }
@@ -815,7 +905,7 @@ __global__ void __launch_bounds__(kSThreads, 1) split_frame_kernel(Frame f, cons
           if (v0 < kVocab) u = *reinterpret_cast<const uint4*>(hbp + v0);  // kVocab % 8 == 0
           *reinterpret_cast<uint4*>(sm.hb + 8 * i) = u;
         }
-        if (threadIdx.x < kSS) {
+        if (threadIdx.x < K::S) {
           sm.nf[threadIdx.x] = 0;
           sm.vmax[threadIdx.x] = 0;
         }
@@ -823,22 +913,22 @@ __global__ void __launch_bounds__(kSThreads, 1) split_frame_kernel(Frame f, cons
       cbar();
 
       // ---------------- LN1, qkv of the CTA's heads
-      layer_norm_op(sm.x, sm.xa, g1);
+      layer_norm_op<R>(sm.x, sm.xa, g1);
       operand_ready(sm);
       for (int b = 0; b < K::nq; ++b, ++mb) {
-        float v[8];
+        float v[R / 2];
         load_block(sm, mb, v);
         const int gi = 2 * b + (m_lane >> 6);
         if (gi < 3 * K::nh) {
           const int col = kHeadDim * gi + (m_lane & 63);  // (type, local head) major, as the staging layout
 #pragma unroll
-          for (int i = 0; i < 8; ++i) sm.q.qkv[epi_row(i) * K::ldq + col] = f2bf(v[i]);
+          for (int i = 0; i < R / 2; ++i) sm.q.qkv[epi_row<R>(i) * K::ldq + col] = f2bf(v[i]);
         }
       }
       cbar();
 
       // ---------------- attention (R1: the heads' outputs to every CTA)
-      attention<C>(sm, p, c, rd);
+      attention<C, R>(sm, p, c, rd);
       if constexpr (C > 1) {
         finish_round(sm, rd, static_cast<uint32_t>((C - 1) * K::att_rows * kHeadDim * K::nh * 2));
         fence_proxy_async();
@@ -847,23 +937,23 @@ __global__ void __launch_bounds__(kSThreads, 1) split_frame_kernel(Frame f, cons
 
       // ---------------- o-projection + residual (R2: the CTA's features to every CTA)
       for (int b = 0; b < K::no; ++b, ++mb) {
-        float v[8];
+        float v[R / 2];
         load_block(sm, mb, v);
         const int nl = 128 * b + m_lane;
         if (nl < K::of) {
           const int n = K::of * c + nl;
 #pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            bf16* xr = sm.x + epi_row(i) * kLdX + n;
+          for (int i = 0; i < R / 2; ++i) {
+            bf16* xr = sm.x + epi_row<R>(i) * kLdX + n;
             *xr = f2bf(__fadd_rn(bf2f(*xr), round_bf16(v[i])));
           }
         }
       }
       cbar();
-      if constexpr (C > 1) {
-        // rows of the owned feature slice, 16-byte units
+      // rows of the CTA's feature slice of x to every peer, 16-byte units
+      auto push_x_slice = [&]() {
         constexpr int upr = K::of / 8;
-        for (int i = threadIdx.x; i < kSR * upr; i += kSC) {
+        for (int i = threadIdx.x; i < R * upr; i += kSC) {
           const int r = i / upr, k8 = K::of * c + 8 * (i % upr);
           const uint4* src = reinterpret_cast<const uint4*>(sm.x + r * kLdX + k8);
           const uint4 u = *src;
@@ -872,95 +962,122 @@ __global__ void __launch_bounds__(kSThreads, 1) split_frame_kernel(Frame f, cons
             if (j != c) st_async_v4(cluster_addr(src, j), u, cluster_addr(&sm.xbar[rd & 1u], j));
           }
         }
-        finish_round(sm, rd, static_cast<uint32_t>((C - 1) * kSR * K::of * 2));
+      };
+      if constexpr (C > 1) {
+        push_x_slice();
+        finish_round(sm, rd, static_cast<uint32_t>((C - 1) * R * K::of * 2));
       }
 
       // ---------------- LN2, FFN1 + GELU
-      layer_norm_op(sm.x, sm.xa, g2);
+      layer_norm_op<R>(sm.x, sm.xa, g2);
       operand_ready(sm);
       for (int b = 0; b < K::nf1; ++b, ++mb) {
-        float v[8];
+        float v[R / 2];
         load_block(sm, mb, v);
         const int fl = 128 * b + m_lane;
 #pragma unroll
-        for (int i = 0; i < 8; ++i) op_store(sm.u.hid, epi_row(i), fl, f2bf(gelu_tanh(round_bf16(v[i]))));
+        for (int i = 0; i < R / 2; ++i) op_store<R>(sm.u.hid, epi_row<R>(i), fl, f2bf(gelu_tanh(round_bf16(v[i]))));
       }
       operand_ready(sm);
 
       // ---------------- FFN2 (+ R3 reduce-scatter, R4 all-gather) + residual
+      float own_part[R / 2];  // 32-row tiles: this CTA's partials of its own features
+#pragma unroll
+      for (int i = 0; i < R / 2; ++i) own_part[i] = 0.f;
       for (int b = 0; b < 2; ++b, ++mb) {
-        float v[8];
+        float v[R / 2];
         load_block(sm, mb, v);
         const int n = 128 * b + m_lane;
         if constexpr (C == 1) {
 #pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            bf16* xr = sm.x + epi_row(i) * kLdX + n;
+          for (int i = 0; i < R / 2; ++i) {
+            bf16* xr = sm.x + epi_row<R>(i) * kLdX + n;
             *xr = f2bf(__fadd_rn(bf2f(*xr), round_bf16(v[i])));
           }
         } else {
           const int owner = n / K::of, nl = n % K::of;
+          // receive slot of this CTA at the owner: every CTA (16-row tiles), or
+          // the peers only (32-row tiles: the owner keeps its own in registers)
+          const int slot_at = K::red_slots == C ? c : (c < owner ? c : c - 1);
 #pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            float* dst = &sm.red[c][epi_row(i)][nl];
+          for (int i = 0; i < R / 2; ++i) {
             if (owner == c) {
-              *dst = v[i];
+              if constexpr (K::red_slots == C) {
+                sm.red[c][epi_row<R>(i)][nl] = v[i];
+              } else {
+                own_part[i] = v[i];
+              }
             } else {
-              st_async_b32(cluster_addr(dst, owner), __float_as_uint(v[i]), cluster_addr(&sm.xbar[rd & 1u], owner));
+              st_async_b32(cluster_addr(&sm.red[slot_at][epi_row<R>(i)][nl], owner), __float_as_uint(v[i]),
+                           cluster_addr(&sm.xbar[rd & 1u], owner));
             }
           }
         }
       }
       if constexpr (C > 1) {
-        finish_round(sm, rd, static_cast<uint32_t>((C - 1) * kSR * K::of * 4));
-        constexpr int upr = K::of / 8;
-        for (int i = threadIdx.x; i < kSR * upr; i += kSC) {
-          const int r = i / upr, k8 = 8 * (i % upr);
-          float s8[8];
+        finish_round(sm, rd, static_cast<uint32_t>((C - 1) * R * K::of * 4));
+        if constexpr (K::red_slots == C) {
+          constexpr int upr = K::of / 8;
+          for (int i = threadIdx.x; i < R * upr; i += kSC) {
+            const int r = i / upr, k8 = 8 * (i % upr);
+            float s8[8];
 #pragma unroll
-          for (int e = 0; e < 8; ++e) s8[e] = 0.f;
+            for (int e = 0; e < 8; ++e) s8[e] = 0.f;
 #pragma unroll
-          for (int j = 0; j < C; ++j) {
+            for (int j = 0; j < C; ++j) {
 #pragma unroll
-            for (int e = 0; e < 8; ++e) s8[e] += sm.red[j][r][k8 + e];
+              for (int e = 0; e < 8; ++e) s8[e] += sm.red[j][r][k8 + e];
+            }
+            uint4* xr = reinterpret_cast<uint4*>(sm.x + r * kLdX + K::of * c + k8);
+            float xv[8];
+            unpack8(*xr, xv);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) xv[e] = __fadd_rn(xv[e], round_bf16(s8[e]));
+            *xr = pack8(xv);
           }
-          uint4* xr = reinterpret_cast<uint4*>(sm.x + r * kLdX + K::of * c + k8);
-          float xv[8];
-          unpack8(*xr, xv);
+        } else {
+          // two CTAs: own + the peer's partial (f32 addition of two terms is
+          // the same in either order), + residual
+          static_assert(C == 2, "32-row tiles run on 2-CTA clusters");
+          const int n = K::of * c + m_lane;
 #pragma unroll
-          for (int e = 0; e < 8; ++e) xv[e] = __fadd_rn(xv[e], round_bf16(s8[e]));
-          const uint4 u = pack8(xv);
-          *xr = u;
-#pragma unroll
-          for (int j = 0; j < C; ++j) {
-            if (j != c) st_async_v4(cluster_addr(xr, j), u, cluster_addr(&sm.xbar[rd & 1u], j));
+          for (int i = 0; i < R / 2; ++i) {
+            bf16* xr = sm.x + epi_row<R>(i) * kLdX + n;
+            const float sum = __fadd_rn(own_part[i], sm.red[0][epi_row<R>(i)][m_lane]);
+            *xr = f2bf(__fadd_rn(bf2f(*xr), round_bf16(sum)));
           }
         }
-        finish_round(sm, rd, static_cast<uint32_t>((C - 1) * kSR * K::of * 2));
+        cbar();
+        push_x_slice();
+        finish_round(sm, rd, static_cast<uint32_t>((C - 1) * R * K::of * 2));
       } else {
         cbar();
       }
-      x_to_operand(sm.x, sm.ab);
+      x_to_operand<R>(sm.x, sm.ab);
       operand_ready(sm);
 
       // ---------------- head p: bias, CFG combine, constraints (R5: values to the owners)
       {
         bf16* lo_base = f.logits_out;
+        // with 32-row tiles the other CTA's sessions' values wait in xa (free
+        // between FFN1 and the next position's LN1), [non-owned slot][vs]
+        uint16_t* out32 = reinterpret_cast<uint16_t*>(sm.xa);
+        constexpr int H = R / 4;  // sessions per warp half
         for (int b = 0; b < K::nhb; ++b, ++mb) {
-          float v[8];
+          float v[R / 2];
           load_block(sm, mb, v);
           const int vl = 128 * b + m_lane;
           const int t = K::vs * c + vl;
           const bool in_vocab = t < kVocab;
           const float bias = bf2f(sm.hb[vl]);
 #pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const int slot = 4 * sh + i;
+          for (int i = 0; i < H; ++i) {
+            const int slot = H * sh + i;
             bool nfs = false;
             uint32_t key = 0;
             if (in_vocab && slot < n_sess) {
               const __nv_bfloat16 cb = f2bf(__fadd_rn(v[i], bias));
-              const __nv_bfloat16 ub = f2bf(__fadd_rn(v[4 + i], bias));
+              const __nv_bfloat16 ub = f2bf(__fadd_rn(v[H + i], bias));
               if (lo_base) {
                 bf16* lr = lo_base + (static_cast<int64_t>(sm.sess[slot]) * kPositions + p) * rp * kVocab;
                 lr[t] = cb;
@@ -978,8 +1095,10 @@ __global__ void __launch_bounds__(kSThreads, 1) split_frame_kernel(Frame f, cons
               const int owner = slot / K::own;
               if (owner == c) {
                 sm.u.v.own[slot - own0][t] = val;
-              } else {
+              } else if constexpr (R == 16) {
                 sm.u.v.out[slot][vl] = val;
+              } else {
+                out32[(slot < own0 ? slot : slot - K::own) * K::vs + vl] = val;
               }
             }
             if (__any_sync(0xffffffffu, nfs) && lane == 0) atomicOr(&sm.nf[slot], 1u);
@@ -993,20 +1112,25 @@ __global__ void __launch_bounds__(kSThreads, 1) split_frame_kernel(Frame f, cons
         if constexpr (C > 1) {
           // the other CTAs' sessions: this CTA's vocabulary slice of each, and its non-finite flags
           constexpr int full_units = K::vs / 8;
-          const int len = slice_len<C>(c);  // a multiple of 8
+          const int len = slice_len<C, R>(c);  // a multiple of 8
           const int units = len / 8;
-          const int n_other = kSS - K::own;
+          const int n_other = K::S - K::own;
           for (int i = threadIdx.x; i < n_other * full_units; i += kSC) {
             const int oi = i / full_units, u = i % full_units;
             if (u < units) {
               const int slot = oi < own0 ? oi : oi + K::own;  // skip the owned slots
               const int owner = slot / K::own;
-              const uint4 val = *reinterpret_cast<const uint4*>(&sm.u.v.out[slot][8 * u]);
+              uint4 val;
+              if constexpr (R == 16) {
+                val = *reinterpret_cast<const uint4*>(&sm.u.v.out[slot][8 * u]);
+              } else {
+                val = *reinterpret_cast<const uint4*>(&out32[oi * K::vs + 8 * u]);
+              }
               st_async_v4(cluster_addr(&sm.u.v.own[slot - K::own * owner][K::vs * c + 8 * u], owner), val,
                           cluster_addr(&sm.xbar[rd & 1u], owner));
             }
           }
-          if (threadIdx.x < kSS) {
+          if (threadIdx.x < K::S) {
             const int slot = threadIdx.x;
             const int owner = slot / K::own;
             if (owner != c) {
@@ -1014,7 +1138,7 @@ __global__ void __launch_bounds__(kSThreads, 1) split_frame_kernel(Frame f, cons
                            (sm.nf[slot] << 16) | sm.vmax[slot], cluster_addr(&sm.xbar[rd & 1u], owner));
             }
           }
-          finish_round(sm, rd, values_bytes_in<C>(c));
+          finish_round(sm, rd, values_bytes_in<C, R>(c));
         }
       }
 
@@ -1093,19 +1217,21 @@ __global__ void __launch_bounds__(kSThreads, 1) split_frame_kernel(Frame f, cons
       }
 
       // ---------------- next input rows (folded tables), every CTA, all sessions
-      if (folded && p + 1 < kPositions && warp < n_sess) {
-        const int slot = warp;
-        const int64_t tin = input_token(f, sm, slot, p);
-        float e8[8], p8[8];
-        unpack8(*reinterpret_cast<const uint4*>(f.emb_proj + (static_cast<int64_t>(p) * kVocab + tin) * kD + lane * 8),
-                e8);
-        unpack8(*reinterpret_cast<const uint4*>(f.pos + static_cast<int64_t>(p + 1) * kD + lane * 8), p8);
-        float y[8];
+      if (folded && p + 1 < kPositions) {
+        for (int slot = warp; slot < n_sess; slot += kSW) {
+          const int64_t tin = input_token(f, sm, slot, p);
+          float e8[8], p8[8];
+          unpack8(
+              *reinterpret_cast<const uint4*>(f.emb_proj + (static_cast<int64_t>(p) * kVocab + tin) * kD + lane * 8),
+              e8);
+          unpack8(*reinterpret_cast<const uint4*>(f.pos + static_cast<int64_t>(p + 1) * kD + lane * 8), p8);
+          float y[8];
 #pragma unroll
-        for (int e = 0; e < 8; ++e) y[e] = __fadd_rn(e8[e], p8[e]);
-        const uint4 row = pack8(y);
-        *reinterpret_cast<uint4*>(sm.x + slot * kLdX + lane * 8) = row;
-        if (rp == 2) *reinterpret_cast<uint4*>(sm.x + (slot + 8) * kLdX + lane * 8) = row;
+          for (int e = 0; e < 8; ++e) y[e] = __fadd_rn(e8[e], p8[e]);
+          const uint4 row = pack8(y);
+          *reinterpret_cast<uint4*>(sm.x + slot * kLdX + lane * 8) = row;
+          if (rp == 2) *reinterpret_cast<uint4*>(sm.x + (slot + K::S) * kLdX + lane * 8) = row;
+        }
       }
       cbar();
     }
@@ -1164,20 +1290,20 @@ __global__ void __launch_bounds__(kSThreads, 1) split_frame_kernel(Frame f, cons
   if constexpr (C > 1) cg::this_cluster().sync();  // no CTA leaves while a peer may still push into it
 }
 
-template <int C>
+template <int C, int R>
 int split_clusters() {
   static int cached = -1;  // per process
   static std::mutex mu;
   const std::lock_guard<std::mutex> lock(mu);
   if (cached < 0) {
     int clusters = 0;
-    if (cudaFuncSetAttribute(split_frame_kernel<C>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(split_smem_bytes<C>())) == cudaSuccess) {
+    if (cudaFuncSetAttribute(split_frame_kernel<C, R>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(split_smem_bytes<C, R>())) == cudaSuccess) {
       if constexpr (C == 1) {
         int blocks = 0;
         int dev = 0, sms = 0;
-        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, split_frame_kernel<C>, kSThreads,
-                                                          split_smem_bytes<C>()) == cudaSuccess &&
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, split_frame_kernel<C, R>, kSThreads,
+                                                          split_smem_bytes<C, R>()) == cudaSuccess &&
             cudaGetDevice(&dev) == cudaSuccess &&
             cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && blocks >= 1) {
           clusters = blocks * sms;
@@ -1191,10 +1317,10 @@ int split_clusters() {
         attr[0].val.clusterDim.z = 1;
         cfg.gridDim = dim3(C);
         cfg.blockDim = dim3(kSThreads);
-        cfg.dynamicSmemBytes = split_smem_bytes<C>();
+        cfg.dynamicSmemBytes = split_smem_bytes<C, R>();
         cfg.attrs = attr;
         cfg.numAttrs = 1;
-        if (cudaOccupancyMaxActiveClusters(&clusters, split_frame_kernel<C>, &cfg) != cudaSuccess) clusters = 0;
+        if (cudaOccupancyMaxActiveClusters(&clusters, split_frame_kernel<C, R>, &cfg) != cudaSuccess) clusters = 0;
       }
     }
     cudaGetLastError();
@@ -1203,9 +1329,9 @@ int split_clusters() {
   return cached;
 }
 
-template <int C>
+template <int C, int R>
 cudaError_t launch_split(const Frame& f, const SplitMaps& maps, cudaStream_t stream) {
-  const int tiles = (f.n + kSS - 1) / kSS;
+  const int tiles = (f.n + Cfg<C, R>::S - 1) / Cfg<C, R>::S;
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -1214,31 +1340,32 @@ cudaError_t launch_split(const Frame& f, const SplitMaps& maps, cudaStream_t str
   attr[0].val.clusterDim.z = 1;
   cfg.gridDim = dim3(tiles * C);
   cfg.blockDim = dim3(kSThreads);
-  cfg.dynamicSmemBytes = split_smem_bytes<C>();
+  cfg.dynamicSmemBytes = split_smem_bytes<C, R>();
   cfg.stream = stream;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, split_frame_kernel<C>, f, maps);
+  return cudaLaunchKernelEx(&cfg, split_frame_kernel<C, R>, f, maps);
 }
 
 }  // namespace
 
-int split_frame_clusters(int split) {
+int split_frame_clusters(int split, int rows) {
+  if (rows == 32) return split == 2 ? split_clusters<2, 32>() : 0;
   switch (split) {
-    case 1: return split_clusters<1>();
-    case 2: return split_clusters<2>();
-    case 4: return split_clusters<4>();
-    case 8: return split_clusters<8>();
+    case 1: return split_clusters<1, 16>();
+    case 2: return split_clusters<2, 16>();
+    case 4: return split_clusters<4, 16>();
+    case 8: return split_clusters<8, 16>();
     default: return 0;
   }
 }
 
-bool split_frame_supported(const Frame& f, int split) {
+bool split_frame_supported(const Frame& f, int split, int rows) {
   if (f.d != kD || f.H != kHeads || f.F != kF || f.L != 1 || !f.in_proj || (f.rp != 1 && f.rp != 2)) return false;
-  return split_frame_clusters(split) > 0;
+  return split_frame_clusters(split, rows) > 0;
 }
 
-cudaError_t launch_split_frame(const Frame& f, int split, cudaStream_t stream) {
+cudaError_t launch_split_frame(const Frame& f, int split, int rows, cudaStream_t stream) {
   SplitMaps maps;
   if (!make_weight_map(&maps.in_proj, f.in_w, kEmbed, kD, kBoxRows) ||
       !make_weight_map(&maps.qkv, f.qkv, kD, 3 * kD, kBoxRows) || !make_weight_map(&maps.o, f.o, kD, kD, kBoxRows) ||
@@ -1248,12 +1375,17 @@ cudaError_t launch_split_frame(const Frame& f, int split, cudaStream_t stream) {
   }
   cudaError_t e = cudaMemsetAsync(f.eos_count, 0, sizeof(int32_t), stream);
   if (e != cudaSuccess) return e;
-  switch (split) {
-    case 1: e = launch_split<1>(f, maps, stream); break;
-    case 2: e = launch_split<2>(f, maps, stream); break;
-    case 4: e = launch_split<4>(f, maps, stream); break;
-    case 8: e = launch_split<8>(f, maps, stream); break;
-    default: return cudaErrorInvalidValue;
+  if (rows == 32) {
+    if (split != 2) return cudaErrorInvalidValue;
+    e = launch_split<2, 32>(f, maps, stream);
+  } else {
+    switch (split) {
+      case 1: e = launch_split<1, 16>(f, maps, stream); break;
+      case 2: e = launch_split<2, 16>(f, maps, stream); break;
+      case 4: e = launch_split<4, 16>(f, maps, stream); break;
+      case 8: e = launch_split<8, 16>(f, maps, stream); break;
+      default: return cudaErrorInvalidValue;
+    }
   }
   if (e != cudaSuccess) return e;
   return launch_frame_eos(f, stream);

@@ -25,8 +25,8 @@ from oracle import sampler as S
 pytestmark = pytest.mark.gpu
 
 RTOL = 1e-2
-PATH_AUTO, PHASE, FUSED, TILE, PAIR, SPLIT1, SPLIT2, SPLIT4, SPLIT8 = 0, 1, 2, 3, 4, 5, 6, 7, 8
-SPLITS = [SPLIT1, SPLIT2, SPLIT4, SPLIT8]
+PATH_AUTO, PHASE, FUSED, TILE, PAIR, SPLIT1, SPLIT2, SPLIT4, SPLIT8, SPLIT2X32 = 0, 1, 2, 3, 4, 5, 6, 7, 8, 9
+SPLITS = [SPLIT1, SPLIT2, SPLIT4, SPLIT8, SPLIT2X32]
 BOTH = [PHASE, FUSED, TILE, PAIR] + SPLITS
 
 
@@ -166,7 +166,8 @@ FLAGS6 = ([0, 1, 0, 0, 0, 1], [0, 0, 0, 1, 0, 1], [0, 0, 1, 0, 0, 0])  # incl. a
     (SHAPE_BASELINE, 6, TILE, True), (SHAPE_BASELINE, 11, TILE, True), (SHAPE_BASELINE, 11, TILE, False),
     (SHAPE_BASELINE, 11, FUSED, False), (SHAPE_BASELINE, 6, PAIR, True), (SHAPE_BASELINE, 11, PAIR, True),
     (SHAPE_BASELINE, 20, PAIR, True), (SHAPE_BASELINE, 11, PAIR, False), (SHAPE_SOFIA, 3, PHASE, True)] +
-    [(SHAPE_BASELINE, n, sp, fold) for sp in SPLITS for n, fold in ((6, True), (11, True), (20, True), (11, False))])
+    [(SHAPE_BASELINE, n, sp, fold) for sp in SPLITS for n, fold in ((6, True), (11, True), (20, True), (11, False))] +
+    [(SHAPE_BASELINE, 24, SPLIT2X32, True), (SHAPE_BASELINE, 17, SPLIT2X32, False)])
 def test_frame_matches_oracle(engines, shape, n, path, fold):
     w = weights(shape, 21)
     eng = engines(shape, 21, 24, path=path, fold=fold)
