@@ -419,7 +419,10 @@ __device__ __forceinline__ void attention_pair(PairSmem& sm, int p, int c, int p
       for (int jj = 0; jj < 4; ++jj) {
         const int j = 2 * (4 * g4 + jj) + part;
         if (j <= p) {
-          const float prob = round_bf16(all[j] / sum);
+          // select between two compile-time indices (a runtime index would
+          // put `all` in local memory)
+          const float e = part ? all[2 * (4 * g4 + jj) + 1] : all[2 * (4 * g4 + jj)];
+          const float prob = round_bf16(e / sum);
 #pragma unroll
           for (int d = 0; d < 16; ++d) {
             const float2 t = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&v[16 * jj + d]));
@@ -709,17 +712,22 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
         const uint32_t rb = peer_bar(sm, rd, peer);
 #pragma unroll
         for (int j = 0; j < 2; ++j) {
-          const int nb_peer = 2 * peer + j, nb_own = 2 * c + j;
           const int col = kCRows * j + 8 * warp + 2 * (lane & 3);  // within the 128 features of a CTA
 #pragma unroll
           for (int m = 0; m < 2; ++m) {
+            // this CTA's blocks are nb = 2c + j, the peer's 2 peer + j: select between
+            // compile-time indices (a runtime index would put acc in local memory)
+            float mine[4], theirs[4];
 #pragma unroll
-            for (int e = 0; e < 4; ++e) own[j][m][e] = acc[nb_own][m][0][e];
+            for (int e = 0; e < 4; ++e) {
+              mine[e] = c ? acc[2 + j][m][0][e] : acc[j][m][0][e];
+              theirs[e] = c ? acc[j][m][0][e] : acc[2 + j][m][0][e];
+              own[j][m][e] = mine[e];
+            }
 #pragma unroll
             for (int hh = 0; hh < 2; ++hh) {
               const int r = 16 * m + (lane >> 2) + 8 * hh;
-              st_async_v2f(cluster_addr(&sm.red[r][col], peer), acc[nb_peer][m][0][2 * hh],
-                           acc[nb_peer][m][0][2 * hh + 1], rb);
+              st_async_v2f(cluster_addr(&sm.red[r][col], peer), theirs[2 * hh], theirs[2 * hh + 1], rb);
             }
           }
         }

@@ -618,13 +618,17 @@ __device__ __forceinline__ void attention(SplitSmem<C, R>& sm, int p, int c, uin
         }
 #pragma unroll
         for (int jj = 0; jj < 4; ++jj) {
-          float dot = 0.f;
+          float d0 = 0.f, d1 = 0.f;  // two chains
 #pragma unroll
-          for (int e = 0; e < 16; ++e) {
-            const float2 t = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&k[16 * jj + e]));
-            dot = fmaf(q[2 * e], t.x, dot);
-            dot = fmaf(q[2 * e + 1], t.y, dot);
+          for (int e = 0; e < 16; e += 2) {
+            const float2 t0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&k[16 * jj + e]));
+            const float2 t1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&k[16 * jj + e + 1]));
+            d0 = fmaf(q[2 * e], t0.x, d0);
+            d0 = fmaf(q[2 * e + 1], t0.y, d0);
+            d1 = fmaf(q[2 * e + 2], t1.x, d1);
+            d1 = fmaf(q[2 * e + 3], t1.y, d1);
           }
+          float dot = d0 + d1;
           dot += __shfl_xor_sync(0xffffffffu, dot, 1);
           if (2 * (4 * g4 + jj) + part <= p) s[4 * g4 + jj] = round_bf16(__fmul_rn(round_bf16(dot), 0.125f));
         }
@@ -673,7 +677,10 @@ __device__ __forceinline__ void attention(SplitSmem<C, R>& sm, int p, int c, uin
         for (int jj = 0; jj < 4; ++jj) {
           const int j = 2 * (4 * g4 + jj) + part;
           if (j <= p) {
-            const float prob = round_bf16(all[j] / sum);
+            // select between two compile-time indices (a runtime index would
+            // put `all` in local memory)
+            const float e = part ? all[2 * (4 * g4 + jj) + 1] : all[2 * (4 * g4 + jj)];
+            const float prob = round_bf16(e / sum);
 #pragma unroll
             for (int d = 0; d < 16; ++d) {
               const float2 t = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&v[16 * jj + d]));

@@ -416,7 +416,10 @@ __device__ __forceinline__ void attention(TileSmem& sm, int p) {
       for (int jj = 0; jj < 4; ++jj) {
         const int j = 2 * (4 * g4 + jj) + part;
         if (j <= p) {
-          const float prob = round_bf16(all[j] / sum);
+          // select between two compile-time indices (a runtime index would
+          // put `all` in local memory)
+          const float e = part ? all[2 * (4 * g4 + jj) + 1] : all[2 * (4 * g4 + jj)];
+          const float prob = round_bf16(e / sum);
 #pragma unroll
           for (int d = 0; d < 16; ++d) {
             const float2 t = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&v[16 * jj + d]));
