@@ -2,7 +2,7 @@
  * magpie_tts_rt_b200 -- B200 (sm_100a) implementation of MagpieTTS-RT's
  * per-frame Local AR + sampling hot path, behind the reference's C ABI.
  *
- * Three groups of entry points:
+ * Four groups of entry points:
  *
  * 1. The plugin-library ABI the runtime dlopen()s
  *    (reference: include/magpie_tts_rt/magpie_tts_rt_plugin.h:70-152,
@@ -24,6 +24,12 @@
  *    structure-of-arrays device state.  It replaces, for N sessions at once,
  *    the reference's per-session Local AR graph launch plus
  *    launch_finalize_local_step (src/runtime/synthesis_pipeline.cpp:511-569).
+ *
+ * 4. The alignment controller (reference: src/runtime/alignment_kernel.hpp
+ *    launch_alignment_controller), per utterance with the reference's
+ *    arguments, and batched over sessions together with the Local AR EOS
+ *    inputs (forbid_eos, unfinished, the finished latch) that the reference
+ *    prepares on the host before every Local AR step.
  *
  * Streams (`void* stream`) are cudaStream_t values; NULL is the legacy
  * default stream.
@@ -406,6 +412,85 @@ MTT_B200_API int32_t mtt_b200_local_ar_frame_path_clusters(int32_t path);
 MTT_B200_API int32_t mtt_b200_local_ar_frame_launch_count(const mtt_b200_local_ar_shape_t* shape,
                                                           const mtt_b200_sampling_config_t* sampling,
                                                           int32_t n_streams);
+
+/* ------------------------------------------------------------------------ */
+/* 4. Alignment controller and the Local AR's EOS inputs                     */
+/* ------------------------------------------------------------------------ */
+
+/* Layout-identical to AlignmentKernelContract (src/runtime/alignment_kernel.hpp:9-15). */
+typedef struct mtt_b200_alignment_contract {
+  uint32_t text_length;
+  uint32_t ignored_terminal_tokens;
+  uint32_t short_text_no_prior_max_tokens;
+  uint32_t lookahead;
+  uint32_t sink_threshold;
+} mtt_b200_alignment_contract_t;
+
+/*
+ * Replaces launch_alignment_controller (src/runtime/alignment_kernel.hpp:
+ * 20-29, alignment_kernel.cu:158-184): one utterance, all pointers device
+ * pointers.  alignment_scores [2][T] bf16 (only the conditional row 0 is
+ * read), counters [T] uint32 and last_attended [1] uint32 (state, updated),
+ * next_prior [2][1][T] bf16, attended_token_index [1] int64, unfinished_text
+ * [1] bool, invalid_state [1] int32.  Picks the attended token as the
+ * left-most maximum of row 0 over the search window, counts the visit, writes
+ * unfinished = attended < T - ignored_terminal_tokens and the next prior
+ * (0.1, with 1.0 at the history / attended / look-ahead tokens past the last
+ * sink, or on every token for short texts).  Data-plane errors are in-band:
+ * invalid_state = 1 for a rejected contract (nothing else written), a
+ * non-finite score anywhere in row 0 or a counter overflow (state advanced,
+ * prior not written).  Returns the launch's cudaError_t value (0 on
+ * success; cudaErrorInvalidValue for a NULL pointer), stream-ordered, no
+ * host synchronisation.
+ */
+MTT_B200_API int mtt_b200_launch_alignment_controller(
+    const void* alignment_scores_bf16, const mtt_b200_alignment_contract_t* contract, uint32_t* counters,
+    uint32_t* last_attended, void* next_prior_bf16, int64_t* attended_token_index, bool* unfinished_text,
+    int32_t* invalid_state, void* stream);
+
+/*
+ * The same controller for n_sessions utterances in one launch (new; the
+ * reference runs one launch per session), plus the Local AR inputs the
+ * reference's pipeline prepares around it on the host, so that one decoder
+ * step is [Main Decoder] -> this -> mtt_b200_launch_local_ar_frame with no
+ * host copy in between:
+ *   forbid_eos[s] = decoder_steps[s] < 2, then decoder_steps[s] += 1
+ *     (synthesis_pipeline.cpp:525-569, generated_decoder_steps_);
+ *   finished[s] |= end_frame_index[s] in {0, 1}, the previous frame's result
+ *     (the latch of launch_finalize_local_step, synthesis_kernels.cu:79-84;
+ *     initialise end_frame_index to -1);
+ *   unfinished[s] = the controller's unfinished_text.
+ * Point forbid_eos / unfinished / finished at the frame batch's arrays.
+ * Row layout: session s's score and prior rows at s * 2 * token_stride
+ * (conditional) and + token_stride (unconditional), its counters at
+ * s * token_stride; token_stride >= every text_length (a longer text is
+ * rejected in-band).  Inactive sessions (active[s] false) are untouched.
+ * decoder_steps / forbid_eos and end_frame_index / finished are optional
+ * pairs (both NULL or both set).  Returns MTT_B200_STATUS_*.
+ */
+typedef struct mtt_b200_alignment_batch {
+  int32_t n_sessions;
+  uint32_t token_stride;
+  uint32_t ignored_terminal_tokens;
+  uint32_t short_text_no_prior_max_tokens;
+  uint32_t lookahead;
+  uint32_t sink_threshold;
+  const uint32_t* text_length;    /* [n] */
+  const bool* active;             /* [n] or NULL */
+  const void* alignment_scores;   /* [n][2][token_stride] bf16 */
+  uint32_t* counters;             /* [n][token_stride] in/out */
+  uint32_t* last_attended;        /* [n] in/out */
+  void* next_prior;               /* [n][2][token_stride] bf16 out */
+  int64_t* attended_token_index;  /* [n] out */
+  bool* unfinished;               /* [n] out */
+  int32_t* invalid_state;         /* [n] out */
+  int64_t* decoder_steps;         /* [n] in/out, or NULL */
+  bool* forbid_eos;               /* [n] out, or NULL */
+  const int32_t* end_frame_index; /* [n] in, or NULL */
+  bool* finished;                 /* [n] in/out, or NULL */
+} mtt_b200_alignment_batch_t;
+
+MTT_B200_API int mtt_b200_launch_alignment_batch(const mtt_b200_alignment_batch_t* batch, void* stream);
 
 /* ------------------------------------------------------------------------ */
 /* Test hooks (no reference counterpart beyond launch_test_clamped_gumbel,   */

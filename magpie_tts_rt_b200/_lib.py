@@ -118,6 +118,24 @@ class StreamBatch(ctypes.Structure):
     ]
 
 
+class AlignmentContract(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_uint32) for n in (
+        "text_length", "ignored_terminal_tokens", "short_text_no_prior_max_tokens", "lookahead",
+        "sink_threshold")]
+
+
+class AlignmentBatch(ctypes.Structure):
+    _fields_ = [
+        ("n_sessions", I32), ("token_stride", ctypes.c_uint32),
+        ("ignored_terminal_tokens", ctypes.c_uint32), ("short_text_no_prior_max_tokens", ctypes.c_uint32),
+        ("lookahead", ctypes.c_uint32), ("sink_threshold", ctypes.c_uint32),
+        ("text_length", P), ("active", P), ("alignment_scores", P), ("counters", P),
+        ("last_attended", P), ("next_prior", P), ("attended_token_index", P), ("unfinished", P),
+        ("invalid_state", P), ("decoder_steps", P), ("forbid_eos", P), ("end_frame_index", P),
+        ("finished", P),
+    ]
+
+
 # name -> (restype, argtypes)
 SIGNATURES = {
     "mtt_plugin_get_api_v1": (I32, [ctypes.POINTER(PluginApiV1)]),
@@ -142,6 +160,9 @@ SIGNATURES = {
     "mtt_b200_fold_in_projection_bytes": (SZ, [ctypes.POINTER(Shape)]),
     "mtt_b200_launch_fold_in_projection": (
         I32, [ctypes.POINTER(Shape), ctypes.POINTER(Weights), P, P]),
+    "mtt_b200_launch_alignment_controller": (
+        I32, [P, ctypes.POINTER(AlignmentContract), P, P, P, P, P, P, P]),
+    "mtt_b200_launch_alignment_batch": (I32, [ctypes.POINTER(AlignmentBatch), P]),
     "mtt_b200_launch_test_clamped_gumbel": (I32, [P, P, SZ, P]),
     "mtt_b200_launch_test_log": (I32, [P, P, SZ, P]),
 }

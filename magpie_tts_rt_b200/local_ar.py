@@ -226,3 +226,112 @@ class LocalArEngine:
             _stream(stream))
         if status != L.STATUS_OK:
             raise RuntimeError(f"mtt_b200_launch_local_ar_frame failed with status {status}")
+
+
+# ---------------------------------------------------------------------------
+# alignment controller
+# ---------------------------------------------------------------------------
+
+@dataclass
+class AlignmentKernelContract:
+    """AlignmentKernelContract (src/runtime/alignment_kernel.hpp:9-15)."""
+
+    text_length: int
+    ignored_terminal_tokens: int = 3
+    short_text_no_prior_max_tokens: int = 5
+    lookahead: int = 6
+    sink_threshold: int = 4
+
+    def c_struct(self) -> L.AlignmentContract:
+        return L.AlignmentContract(self.text_length, self.ignored_terminal_tokens,
+                                   self.short_text_no_prior_max_tokens, self.lookahead, self.sink_threshold)
+
+
+def launch_alignment_controller(alignment_scores, contract: AlignmentKernelContract, counters, last_attended,
+                                next_prior, attended_token_index, unfinished_text, invalid_state,
+                                stream=None) -> int:
+    """launch_alignment_controller (src/runtime/alignment_kernel.hpp:20-29):
+    returns the cudaError_t value (0 success, 1 cudaErrorInvalidValue for a
+    missing buffer)."""
+    c = contract.c_struct() if contract is not None else None
+    return L.lib.mtt_b200_launch_alignment_controller(
+        _ptr(alignment_scores), ctypes.byref(c) if c is not None else None, _ptr(counters),
+        _ptr(last_attended), _ptr(next_prior), _ptr(attended_token_index), _ptr(unfinished_text),
+        _ptr(invalid_state), _stream(stream))
+
+
+@dataclass
+class AlignmentBatch:
+    """SoA alignment state for n sessions (one utterance each), rows padded to
+    ``token_stride`` tokens.  ``gate(frame)`` runs one controller step for
+    every active session and writes the frame batch's ``unfinished``,
+    ``forbid_eos`` and ``finished`` inputs on the device."""
+
+    text_length: torch.Tensor     # [n] uint32 (int32 storage)
+    alignment_scores: torch.Tensor  # [n, 2, S] bf16 (written by the Main Decoder step)
+    counters: torch.Tensor        # [n, S] uint32 (int32 storage)
+    last_attended: torch.Tensor   # [n] uint32 (int32 storage)
+    next_prior: torch.Tensor      # [n, 2, S] bf16
+    attended_token_index: torch.Tensor  # [n] int64
+    invalid_state: torch.Tensor   # [n] int32
+    decoder_steps: torch.Tensor   # [n] int64
+    ignored_terminal_tokens: int = 3
+    short_text_no_prior_max_tokens: int = 5
+    lookahead: int = 6
+    sink_threshold: int = 4
+
+    @property
+    def n(self) -> int:
+        return int(self.text_length.shape[0])
+
+    @property
+    def token_stride(self) -> int:
+        return int(self.alignment_scores.shape[2])
+
+    @staticmethod
+    def allocate(text_lengths, token_stride: int = 512, initial_attended: int = 1, device="cuda",
+                 **contract) -> "AlignmentBatch":
+        n = len(text_lengths)
+        z = lambda *s, dt: torch.zeros(*s, dtype=dt, device=device)
+        return AlignmentBatch(
+            text_length=torch.as_tensor(list(text_lengths), dtype=torch.int32, device=device),
+            alignment_scores=z(n, 2, token_stride, dt=torch.bfloat16),
+            counters=z(n, token_stride, dt=torch.int32),
+            last_attended=torch.full((n,), initial_attended, dtype=torch.int32, device=device),
+            next_prior=z(n, 2, token_stride, dt=torch.bfloat16),
+            attended_token_index=z(n, dt=torch.int64), invalid_state=z(n, dt=torch.int32),
+            decoder_steps=z(n, dt=torch.int64), **contract)
+
+    def c_struct(self, frame: Optional[StreamBatch] = None, unfinished=None, forbid_eos=None,
+                 finished=None, end_frame_index=None, active=None) -> L.AlignmentBatch:
+        if frame is not None:
+            unfinished = frame.unfinished if unfinished is None else unfinished
+            forbid_eos = frame.forbid_eos if forbid_eos is None else forbid_eos
+            finished = frame.finished if finished is None else finished
+            end_frame_index = frame.end_frame_index if end_frame_index is None else end_frame_index
+            active = frame.active if active is None else active
+        b = L.AlignmentBatch()
+        b.n_sessions = self.n
+        b.token_stride = self.token_stride
+        b.ignored_terminal_tokens = self.ignored_terminal_tokens
+        b.short_text_no_prior_max_tokens = self.short_text_no_prior_max_tokens
+        b.lookahead = self.lookahead
+        b.sink_threshold = self.sink_threshold
+        for name in ("text_length", "alignment_scores", "counters", "last_attended", "next_prior",
+                     "attended_token_index", "invalid_state"):
+            setattr(b, name, getattr(self, name).data_ptr())
+        b.unfinished = unfinished.data_ptr() if unfinished is not None else None
+        b.active = active.data_ptr() if active is not None else None
+        if forbid_eos is not None:
+            b.decoder_steps = self.decoder_steps.data_ptr()
+            b.forbid_eos = forbid_eos.data_ptr()
+        if finished is not None and end_frame_index is not None:
+            b.end_frame_index = end_frame_index.data_ptr()
+            b.finished = finished.data_ptr()
+        return b
+
+    def gate(self, frame: Optional[StreamBatch] = None, stream=None, **outputs) -> None:
+        cb = self.c_struct(frame, **outputs)
+        status = L.lib.mtt_b200_launch_alignment_batch(ctypes.byref(cb), _stream(stream))
+        if status != L.STATUS_OK:
+            raise RuntimeError(f"mtt_b200_launch_alignment_batch failed with status {status}")

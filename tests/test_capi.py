@@ -109,3 +109,23 @@ def test_null_arguments_rejected_without_launch():
     assert L.lib.mtt_b200_launch_finalize_local_step(None, None, 0, *([None] * 8)) == -1
     assert L.lib.mtt_b200_launch_test_clamped_gumbel(None, None, 4, None) == -1
     assert L.lib.mtt_b200_launch_local_ar_frame(None, None, None, None, None, 0, None) == -1
+
+
+def test_alignment_launchers_without_a_gpu():
+    """launch_alignment_controller's null-pointer status (cudaErrorInvalidValue,
+    alignment_kernel.cu:168-173) and the batch's argument checks, all decided
+    before any CUDA call; the contract struct is layout-identical to
+    AlignmentKernelContract (five uint32)."""
+    assert ctypes.sizeof(L.AlignmentContract) == 20
+    assert L.lib.mtt_b200_launch_alignment_controller(None, None, *([None] * 7)) == 1
+    c = L.AlignmentContract(12, 3, 5, 6, 4)
+    assert L.lib.mtt_b200_launch_alignment_controller(None, ctypes.byref(c), *([None] * 7)) == 1
+    assert L.lib.mtt_b200_launch_alignment_batch(None, None) == -1
+    b = L.AlignmentBatch()
+    b.n_sessions = 0
+    assert L.lib.mtt_b200_launch_alignment_batch(ctypes.byref(b), None) == 0
+    b.n_sessions = 4
+    b.token_stride = 16
+    assert L.lib.mtt_b200_launch_alignment_batch(ctypes.byref(b), None) == -1
+    b.n_sessions = -1
+    assert L.lib.mtt_b200_launch_alignment_batch(ctypes.byref(b), None) == -1
