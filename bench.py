@@ -18,6 +18,10 @@ FFN 1024, 16 heads 256->2024, 16 tables 2024x768):
   one session, CFG, seed 1234, 1000 frames with new hidden states, each frame
   one CUDA-graph launch of the frame; p50/p99 over frames by CUDA events.
 
+Also at N=1: the alignment gate (the controller step plus the Local AR's
+EOS inputs, once per decoder step) for the config-4 sessions of one GPU, with
+the reference's own host controller timed beside it.
+
 A "frame" is one session's 16-position Local AR step (one decoder hidden in,
 16 codec tokens = 2 codec frames x 8 codebooks out).
 
@@ -396,6 +400,86 @@ def latency_config2(eng_w, dev, frames=1000, warm=20):
             "mean_us": float(us.mean()), "frames": frames, "invalid": inv}
 
 
+def alignment_gate_measure(dev, peaks, n=1024, stride=512, steps=200, seed=11):
+    """The alignment gate (mtt_b200_launch_alignment_batch) for the config-4
+    sessions of one GPU: text lengths U[64, 512], a fresh score row per step
+    (copied in by a kernel of the same graph, as the Main Decoder writes it),
+    `steps` gate launches captured in one CUDA graph; per-launch device time
+    by CUDA events.  Algorithmic bytes per launch: per session the
+    conditional score row read (2T), the counters read (4T), the prior
+    written (4T) and ~40 bytes of scalars.  Beside it, the reference's own
+    host controller (oracle/_ref, compiled from the reference's
+    alignment_controller.cpp) on the same sessions on one host core."""
+    from magpie_tts_rt_b200.local_ar import AlignmentBatch
+    rng = np.random.default_rng(seed)
+    T = rng.integers(64, stride + 1, n)
+    ab = AlignmentBatch.allocate(T.tolist(), token_stride=stride, device=dev)
+    unf = torch.zeros(n, dtype=torch.bool, device=dev)
+    fe = torch.zeros(n, dtype=torch.bool, device=dev)
+    fin = torch.zeros(n, dtype=torch.bool, device=dev)
+    end = torch.full((n,), -1, dtype=torch.int32, device=dev)
+    frames = 8
+    g = torch.Generator().manual_seed(seed)
+    src = torch.randn(frames, n, 2, stride, generator=g).to(torch.bfloat16).to(dev)
+    stream = torch.cuda.Stream(dev)
+    outs = dict(unfinished=unf, forbid_eos=fe, finished=fin, end_frame_index=end)
+    with torch.cuda.stream(stream):
+        for f in range(3):
+            ab.alignment_scores.copy_(src[f % frames])
+            ab.gate(stream=stream, **outs)
+    torch.cuda.synchronize(dev)
+    graph = torch.cuda.CUDAGraph()
+    gate_only = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        for f in range(steps):
+            ab.alignment_scores.copy_(src[f % frames])
+            ab.gate(stream=stream, **outs)
+    with torch.cuda.graph(gate_only, stream=stream):
+        for f in range(steps):
+            ab.gate(stream=stream, **outs)
+    e = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+    with torch.cuda.stream(stream):
+        graph.replay()
+        gate_only.replay()
+        e[0].record(stream)
+        graph.replay()
+        e[1].record(stream)
+        e[2].record(stream)
+        gate_only.replay()
+        e[3].record(stream)
+    torch.cuda.synchronize(dev)
+    with_copy_us = e[0].elapsed_time(e[1]) * 1000.0 / steps
+    gate_us = e[2].elapsed_time(e[3]) * 1000.0 / steps
+    inv = int((ab.invalid_state != 0).sum().item())
+    del graph, gate_only
+    bytes_ = int(T.sum()) * (2 + 4 + 4) + n * 40
+    gbs = bytes_ / (gate_us * 1e-6) / 1e9
+    out = {"workload": f"{n} sessions (config 4 at 1 GPU), text lengths U[64,{stride}], token stride {stride}",
+           "kernel": "alignment_gate_kernel<true>", "us_per_launch": gate_us,
+           "us_per_step_with_score_copy": with_copy_us, "invalid_sessions": inv,
+           "roofline": {"bound": "hbm", "algorithmic_bytes": bytes_, "achieved": gbs, "unit": "GB/s",
+                        "peak": peaks["hbm_gbs"], "frac": gbs / peaks["hbm_gbs"]}}
+    try:
+        from oracle import alignment_ref as R
+        if os.path.exists(R.LIBRARY):
+            ctrl = [R.RefController(int(t)) for t in T]
+            rows = src[0, :, 0].float().cpu().numpy()
+            t0 = time.perf_counter()
+            reps = 0
+            while time.perf_counter() - t0 < 2.0:
+                for s, c in enumerate(ctrl):
+                    c.advance(rows[s, :T[s]])
+                reps += 1
+            dt = time.perf_counter() - t0
+            out["cpu_baseline"] = {"value": dt / reps * 1e6, "unit": "us per step of all sessions", "cores": 1,
+                                   "kind": "reference",
+                                   "sample": f"the reference's AlignmentControllerReference::advance on "
+                                             f"{n} sessions x {reps} steps"}
+    except Exception as ex:  # the baseline is optional; the GPU figure stands alone
+        out["cpu_baseline"] = {"unavailable": repr(ex)[:200]}
+    return out
+
+
 # ---------------------------------------------------------------------------
 # CPU baseline (oracle restatement of the reference's path)
 # ---------------------------------------------------------------------------
@@ -478,6 +562,9 @@ def main():
     latency = None
     if world == 1 and not args.no_latency:
         latency = latency_config2(res["w"], torch.device("cuda", local))
+    align = None
+    if world == 1 and not args.no_latency:
+        align = alignment_gate_measure(torch.device("cuda", local), peaks)
     cpu = None
     if world == 1 and rank == 0 and not args.no_cpu_baseline:
         cpu = cpu_oracle_sample()
@@ -521,7 +608,7 @@ def main():
                         "d2h_bytes_per_step": res["d2h"]},
                 "gpu_launches": res["launches"], "frame_path": res["path"], "clocks": res["clocks"],
                 "roofline": roof,
-                "latency_config2": latency, "cpu_baseline": cpu,
+                "latency_config2": latency, "alignment_gate": align, "cpu_baseline": cpu,
                 "checks": {"invalid_rows": res["invalid"], "forced_eos_ok": res["forced_ok"]}}
         print(json.dumps(line), flush=True)
     if world > 1:

@@ -64,24 +64,25 @@ __device__ __forceinline__ uint32_t chunk_u32(const uint4& c, int e) {
   return e == 0 ? c.x : e == 1 ? c.y : e == 2 ? c.z : c.w;
 }
 
-// kVec: rows start 16-byte aligned and the stride is a multiple of 8, so
-// whole 16-byte chunks below the stride may be loaded; else element loads.
+// Chunks of the elements below `lim`.  kVec: rows start 16-byte aligned and
+// lim (the stride, capped at 512) is a multiple of 8, so whole 16-byte chunks
+// are loaded; else element loads.
 template <bool kVec>
-__device__ __forceinline__ uint4 load_row_chunk(const uint16_t* row, uint32_t first, uint32_t t) {
-  if (first >= t) return make_uint4(0, 0, 0, 0);
+__device__ __forceinline__ uint4 load_row_chunk(const uint16_t* row, uint32_t first, uint32_t lim) {
+  if (first >= lim) return make_uint4(0, 0, 0, 0);
   if constexpr (kVec) return __ldg(reinterpret_cast<const uint4*>(row + first));
   uint32_t h[8];
 #pragma unroll
-  for (int e = 0; e < 8; ++e) h[e] = first + e < t ? row[first + e] : 0u;
+  for (int e = 0; e < 8; ++e) h[e] = first + e < lim ? row[first + e] : 0u;
   return make_uint4(h[0] | (h[1] << 16), h[2] | (h[3] << 16), h[4] | (h[5] << 16), h[6] | (h[7] << 16));
 }
 template <bool kVec>
-__device__ __forceinline__ uint4 load_count_chunk(const uint32_t* cnt, uint32_t first, uint32_t t) {
-  if (first >= t) return make_uint4(0, 0, 0, 0);
+__device__ __forceinline__ uint4 load_count_chunk(const uint32_t* cnt, uint32_t first, uint32_t lim) {
+  if (first >= lim) return make_uint4(0, 0, 0, 0);
   if constexpr (kVec) return *reinterpret_cast<const uint4*>(cnt + first);
   uint32_t h[4];
 #pragma unroll
-  for (int e = 0; e < 4; ++e) h[e] = first + e < t ? cnt[first + e] : 0u;
+  for (int e = 0; e < 4; ++e) h[e] = first + e < lim ? cnt[first + e] : 0u;
   return make_uint4(h[0], h[1], h[2], h[3]);
 }
 
@@ -100,39 +101,43 @@ template <bool kVec>
 __global__ void __launch_bounds__(kAlignWarps * 32) alignment_gate_kernel(const AlignArgs a) {
   const uint32_t lane = threadIdx.x & 31u;
   const int s = static_cast<int>(blockIdx.x) * kAlignWarps + static_cast<int>(threadIdx.x >> 5);
-  if (s >= a.n || (a.active != nullptr && !a.active[s])) return;
+  if (s >= a.n) return;
+
+  // Every load of the step is issued before any is used: the session's
+  // scalars and its score / counter chunks -- up to the stride on the 16-byte
+  // path (in bounds whatever the text length; entries past it are masked
+  // below), up to the text length on the element path.
+  const bool act = a.active == nullptr || a.active[s];
+  const uint32_t t = a.text_length != nullptr ? a.text_length[s] : a.single_t;
+  const uint32_t la = a.last_attended[s];
+  const int64_t steps = a.steps != nullptr ? a.steps[s] : 0;
+  const int32_t end_frame = a.end_frame != nullptr ? a.end_frame[s] : -1;
+  const size_t base = static_cast<size_t>(s) * 2u * a.stride;
+  const uint16_t* row = a.scores + base;
+  uint32_t* cnt = a.counters + static_cast<size_t>(s) * a.stride;
+  const uint32_t lim = kVec ? min(a.stride, kMaxText) : min(min(t, a.stride), kMaxText);
+  uint4 rc[kRowChunks], cc[kCountChunks];
+#pragma unroll
+  for (int j = 0; j < kRowChunks; ++j) rc[j] = load_row_chunk<kVec>(row, 8u * (lane + 32u * j), lim);
+#pragma unroll
+  for (int j = 0; j < kCountChunks; ++j) cc[j] = load_count_chunk<kVec>(cnt, 4u * (lane + 32u * j), lim);
+  if (!act) return;
 
   // Local AR EOS inputs, whatever the alignment outcome (the host computes
   // them unconditionally, synthesis_pipeline.cpp:525-569).
   if (lane == 0) {
     if (a.steps != nullptr) {
-      const int64_t st = a.steps[s];
-      a.forbid[s] = st < 2;
-      a.steps[s] = st + 1;
+      a.forbid[s] = steps < 2;
+      a.steps[s] = steps + 1;
     }
-    if (a.end_frame != nullptr) {
-      const int32_t e = a.end_frame[s];
-      if (e == 0 || e == 1) a.finished[s] = true;
-    }
+    if (a.end_frame != nullptr && (end_frame == 0 || end_frame == 1)) a.finished[s] = true;
   }
 
-  const uint32_t t = a.text_length != nullptr ? a.text_length[s] : a.single_t;
   // alignment_kernel.cu:33-37 (t > stride: rows would overlap, also rejected)
   if (t == 0 || t > kMaxText || t > a.stride || t <= a.ignored || a.lookahead == 0 || a.sink == 0) {
     if (lane == 0) a.invalid[s] = 1;
     return;
   }
-  const size_t base = static_cast<size_t>(s) * 2u * a.stride;
-  const uint16_t* row = a.scores + base;
-  uint32_t* cnt = a.counters + static_cast<size_t>(s) * a.stride;
-
-  // one wave of loads
-  const uint32_t la = a.last_attended[s];
-  uint4 rc[kRowChunks], cc[kCountChunks];
-#pragma unroll
-  for (int j = 0; j < kRowChunks; ++j) rc[j] = load_row_chunk<kVec>(row, 8u * (lane + 32u * j), t);
-#pragma unroll
-  for (int j = 0; j < kCountChunks; ++j) cc[j] = load_count_chunk<kVec>(cnt, 4u * (lane + 32u * j), t);
 
   // search window (alignment_kernel.cu:39-59)
   bool invalid = false;
