@@ -351,6 +351,14 @@ typedef struct mtt_b200_stream_batch {
   const int64_t* forced_tokens; /* [n][16]: next-position inputs replace the sampled
                                    tokens (teacher forcing, for parity checks) */
   void* logits_out;             /* [n][16][rows][2024] bf16 per-position logits */
+  /* Folding launch_finalize_local_step (src/runtime/synthesis_kernels.cu:53-86)
+   * into the frame call (zero-initialised: the [n][8][2] layout, no latch): */
+  int32_t codec_frames_stride;  /* codec_tokens is [n][8][stride]; 0 means 2.  8 writes the
+                                   steady emission aggregate [n][8][8] directly */
+  int32_t codec_frame_offset;   /* this frame's two frames go to columns offset, offset + 1
+                                   (0, 2, 4, 6 for the aggregate); even, offset + 2 <= stride */
+  bool* finished_latch;         /* [n] or NULL: set to true where end_frame_index is 0 or 1
+                                   (may alias `finished`; it is written after the frame read it) */
 } mtt_b200_stream_batch_t;
 
 /* Device workspace bytes for launching up to max_streams streams. */

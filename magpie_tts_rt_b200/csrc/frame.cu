@@ -396,12 +396,12 @@ __global__ void __launch_bounds__(256) frame_end_kernel(Frame f) {
   if (threadIdx.x == 0) {
     const int32_t* tok = f.tokens + s * kPositions;
     for (int p = 0; p < kPositions; ++p) {
-      f.codec_tokens[static_cast<int64_t>(s) * kPositions + (p % kCodebooks) * kFrames + p / kCodebooks] = tok[p];
+      f.codec_tokens[codec_index(f, s, p)] = tok[p];
     }
     const int slot = f.eos_slot[s];
     const float* part = f.eos_partial + static_cast<int64_t>(slot < 0 ? 0 : slot) * kPositions * kEosChunks;
     const float* el = f.eos_logit + static_cast<int64_t>(slot < 0 ? 0 : slot) * kPositions;
-    f.end_frame[s] = eos_decide(part, el, tok, slot >= 0, f.finished[s]);
+    commit_end(f, s, eos_decide(part, el, tok, slot >= 0, f.finished[s]));
     f.counter_io[s] = f.ctr[s];
     f.invalid_rows[s] = f.inv[s];
   }
@@ -572,6 +572,13 @@ extern "C" MTT_B200_API int mtt_b200_launch_local_ar_frame(const mtt_b200_local_
       !b->codec_tokens || !b->invalid_rows || !b->end_frame_index || !b->next_embedding) {
     return MTT_B200_STATUS_INVALID_ARGUMENT;
   }
+  // codec rows: [n][8][stride] with the frame's two frames at offset, offset
+  // even (finalize_local_step's frame offsets 0, 2, 4, 6 for stride 8)
+  if (b->codec_frames_stride < 0 || (b->codec_frames_stride != 0 && b->codec_frames_stride < kFrames) ||
+      b->codec_frame_offset < 0 || b->codec_frame_offset % kFrames != 0 ||
+      b->codec_frame_offset + kFrames > (b->codec_frames_stride == 0 ? kFrames : b->codec_frames_stride)) {
+    return MTT_B200_STATUS_INVALID_ARGUMENT;
+  }
   if (sampling->top_k < 1 || sampling->top_k > kVocab || !(sampling->temperature > 0.f) ||
       (reinterpret_cast<uintptr_t>(workspace) & 255u) != 0) {
     return MTT_B200_STATUS_INVALID_ARGUMENT;
@@ -613,6 +620,9 @@ extern "C" MTT_B200_API int mtt_b200_launch_local_ar_frame(const mtt_b200_local_
   f.seed = b->rng_seed;
   f.counter_io = b->rng_counter;
   f.codec_tokens = b->codec_tokens;
+  f.codec_stride = b->codec_frames_stride == 0 ? kFrames : b->codec_frames_stride;
+  f.codec_offset = b->codec_frame_offset;
+  f.finished_latch = b->finished_latch;
   f.invalid_rows = b->invalid_rows;
   f.end_frame = b->end_frame_index;
   f.next_emb = static_cast<bf16*>(b->next_embedding);

@@ -23,6 +23,8 @@ struct Frame {
   const int64_t* seed;
   int64_t* counter_io;
   int64_t* codec_tokens;
+  int codec_stride, codec_offset;  // frames per codebook row of codec_tokens, first frame written
+  bool* finished_latch;            // optional: set where the frame's EOS decision ends the utterance
   int32_t* invalid_rows;
   int32_t* end_frame;
   bf16* next_emb;
@@ -37,6 +39,21 @@ struct Frame {
   int32_t* inv;
   float *eos_partial, *eos_logit;
 };
+
+// Position p of session s in codec_tokens: codebook p % 8, frame p / 8 of
+// this frame call, frames codec_offset + {0, 1} of a row codec_stride frames
+// wide ([n][8][2] by default, or the [n][8][8] emission aggregate that
+// finalize_local_step assembles, synthesis_kernels.cu:53-86).
+__device__ __forceinline__ int64_t codec_index(const Frame& f, int s, int p) {
+  return (static_cast<int64_t>(s) * kCodebooks + p % kCodebooks) * f.codec_stride + f.codec_offset + p / kCodebooks;
+}
+
+// end_frame_index of session s, and the finished latch of
+// finalize_local_step (synthesis_kernels.cu:79-84) when the caller asked for it.
+__device__ __forceinline__ void commit_end(const Frame& f, int s, int32_t end) {
+  f.end_frame[s] = end;
+  if (f.finished_latch != nullptr && (end == 0 || end == 1)) f.finished_latch[s] = true;
+}
 
 struct Layout {
   size_t list, count, eos_list, eos_count, eos_slot, x, q, kc, vc, att, h, logits, tokens, emb_acc, ctr, inv,

@@ -670,13 +670,13 @@ __global__ void __cluster_dims__(kCS, 1, 1) __launch_bounds__(kThreads, 1)
     if (threadIdx.x < kPositions) {
       const int pp = threadIdx.x;
       const int32_t t = sm.tok[c][pp];
-      f.codec_tokens[static_cast<int64_t>(sid) * kPositions + (pp % kCodebooks) * kFrames + pp / kCodebooks] = t;
+      f.codec_tokens[codec_index(f, sid, pp)] = t;
       f.tokens[static_cast<int64_t>(sid) * kPositions + pp] = t;
     }
     if (threadIdx.x == 0) {
       f.counter_io[sid] = sm.ctr;
       f.invalid_rows[sid] = sm.inv | (sm.err ? 4 : 0);
-      if (f.eos_slot[sid] < 0) f.end_frame[sid] = f.finished[sid] ? 0 : -1;
+      if (f.eos_slot[sid] < 0) commit_end(f, sid, f.finished[sid] ? 0 : -1);
     }
     // sum_p table_p[token_p], each add rounded to bf16, in position order; / 16
     for (int k = threadIdx.x; k < kEmbed; k += blockDim.x) {
@@ -697,9 +697,10 @@ __global__ void __launch_bounds__(256) fused_eos_finish_kernel(Frame f) {
   const int count = *f.eos_count;
   for (int e = threadIdx.x; e < count; e += blockDim.x) {
     const int s = f.eos_list[e];
-    f.end_frame[s] = eos_decide(f.eos_partial + static_cast<int64_t>(e) * kPositions * kEosChunks,
-                                f.eos_logit + static_cast<int64_t>(e) * kPositions, f.tokens + s * kPositions,
-                                true, false);
+    const int32_t end = eos_decide(f.eos_partial + static_cast<int64_t>(e) * kPositions * kEosChunks,
+                                   f.eos_logit + static_cast<int64_t>(e) * kPositions, f.tokens + s * kPositions,
+                                   true, false);
+    commit_end(f, s, end);
   }
   __syncthreads();
   if (threadIdx.x == 0) *f.eos_count = 0;

@@ -864,7 +864,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
       const int ls = i / kPositions, pp = i % kPositions;
       const int sid = sm.sess[own0 + ls];
       const int32_t t = sm.tok[own0 + ls][pp];
-      f.codec_tokens[static_cast<int64_t>(sid) * kPositions + (pp % kCodebooks) * kFrames + pp / kCodebooks] = t;
+      f.codec_tokens[codec_index(f, sid, pp)] = t;
       f.tokens[static_cast<int64_t>(sid) * kPositions + pp] = t;
     }
     if (threadIdx.x < n_own) {
@@ -872,7 +872,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
       const int sid = sm.sess[own0 + ls];
       f.counter_io[sid] = sm.ctr[ls];
       f.invalid_rows[sid] = sm.inv[ls] | (sm.err ? 4 : 0);
-      if (f.eos_slot[sid] < 0) f.end_frame[sid] = f.finished[sid] ? 0 : -1;
+      if (f.eos_slot[sid] < 0) commit_end(f, sid, f.finished[sid] ? 0 : -1);
     }
     for (int i = threadIdx.x; i < n_own * (kEmbed / 8); i += kPC) {
       const int ls = i / (kEmbed / 8), k8 = 8 * (i % (kEmbed / 8));

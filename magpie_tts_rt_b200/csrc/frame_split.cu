@@ -1249,7 +1249,7 @@ __global__ void __launch_bounds__(kSThreads, 1) split_frame_kernel(Frame f, cons
       const int slot = own0 + ls;
       const int sid = sm.sess[slot];
       const int32_t t = sm.tok[slot][pp];
-      f.codec_tokens[static_cast<int64_t>(sid) * kPositions + (pp % kCodebooks) * kFrames + pp / kCodebooks] = t;
+      f.codec_tokens[codec_index(f, sid, pp)] = t;
       f.tokens[static_cast<int64_t>(sid) * kPositions + pp] = t;
     }
     if (threadIdx.x < n_own) {
@@ -1257,7 +1257,7 @@ __global__ void __launch_bounds__(kSThreads, 1) split_frame_kernel(Frame f, cons
       const int sid = sm.sess[own0 + ls];
       f.counter_io[sid] = sm.ctr[ls];
       f.invalid_rows[sid] = sm.inv[ls] | (err_flag(sm) ? 4 : 0);
-      if (f.eos_slot[sid] < 0) f.end_frame[sid] = f.finished[sid] ? 0 : -1;
+      if (f.eos_slot[sid] < 0) commit_end(f, sid, f.finished[sid] ? 0 : -1);
     }
     for (int i = threadIdx.x; i < n_own * (kEmbed / 8); i += kSC) {
       const int ls = i / (kEmbed / 8), k8 = 8 * (i % (kEmbed / 8));

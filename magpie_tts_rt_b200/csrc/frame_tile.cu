@@ -749,7 +749,7 @@ __global__ void __launch_bounds__(kTThreads, 1) tile_frame_kernel(Frame f, const
     const int slot = i / kPositions, pp = i % kPositions;
     const int sid = sm.sess[slot];
     const int32_t t = sm.tok[slot][pp];
-    f.codec_tokens[static_cast<int64_t>(sid) * kPositions + (pp % kCodebooks) * kFrames + pp / kCodebooks] = t;
+    f.codec_tokens[codec_index(f, sid, pp)] = t;
     f.tokens[static_cast<int64_t>(sid) * kPositions + pp] = t;
   }
   if (threadIdx.x < n_sess) {
@@ -757,7 +757,7 @@ __global__ void __launch_bounds__(kTThreads, 1) tile_frame_kernel(Frame f, const
     const int sid = sm.sess[slot];
     f.counter_io[sid] = sm.ctr[slot];
     f.invalid_rows[sid] = sm.inv[slot] | (sm.err ? 4 : 0);
-    if (f.eos_slot[sid] < 0) f.end_frame[sid] = f.finished[sid] ? 0 : -1;
+    if (f.eos_slot[sid] < 0) commit_end(f, sid, f.finished[sid] ? 0 : -1);
   }
   // sum_p table_p[token_p], each add rounded to bf16, in position order; / 16
   for (int i = threadIdx.x; i < n_sess * (kEmbed / 8); i += kTConsumers) {

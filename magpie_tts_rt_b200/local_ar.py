@@ -121,13 +121,17 @@ class StreamBatch:
     forbid_eos: torch.Tensor
     rng_seed: torch.Tensor  # [n] int64
     rng_counter: torch.Tensor  # [n] int64 (in/out)
-    codec_tokens: torch.Tensor  # [n, 8, 2] int64 (out)
+    codec_tokens: torch.Tensor  # [n, 8, 2] int64 (out), or the [n, 8, 8] aggregate
     invalid_rows: torch.Tensor  # [n] int32 (out)
     end_frame_index: torch.Tensor  # [n] int32 (out)
     next_embedding: torch.Tensor  # [n, 768] bf16 (out)
     active: Optional[torch.Tensor] = None  # [n] bool
     forced_tokens: Optional[torch.Tensor] = None  # [n, 16] int64
     logits_out: Optional[torch.Tensor] = None  # [n, 16, rows, 2024] bf16
+    # finalize_local_step folded into the frame: codec_tokens may be the
+    # [n, 8, 8] emission aggregate (stride 8, this frame at codec_frame_offset)
+    codec_frame_offset: int = 0
+    finished_latch: Optional[torch.Tensor] = None  # [n] bool, may be `finished`
 
     @property
     def n(self) -> int:
@@ -156,6 +160,9 @@ class StreamBatch:
         b.active = self.active.data_ptr() if self.active is not None else None
         b.forced_tokens = self.forced_tokens.data_ptr() if self.forced_tokens is not None else None
         b.logits_out = self.logits_out.data_ptr() if self.logits_out is not None else None
+        b.codec_frames_stride = int(self.codec_tokens.shape[2])
+        b.codec_frame_offset = self.codec_frame_offset
+        b.finished_latch = self.finished_latch.data_ptr() if self.finished_latch is not None else None
         return b
 
 

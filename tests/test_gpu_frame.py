@@ -250,6 +250,57 @@ def test_inactive_streams_untouched(engines, path):
 
 
 @pytest.mark.parametrize("path", BOTH)
+def test_frames_fill_the_emission_aggregate(path):
+    """launch_finalize_local_step folded into the frame call
+    (synthesis_kernels.cu:53-86): four frames write their [8][2] tokens
+    straight into the [n][8][8] emission aggregate at frame offsets 0, 2, 4, 6
+    (the same tokens, counters and EOS as the [n][8][2] layout), and
+    finished_latch is set exactly where end_frame_index is 0 or 1.  The EOS
+    bias is raised so that every session with EOS enabled ends at frame 0."""
+    from magpie_tts_rt_b200 import _lib as L
+    from magpie_tts_rt_b200.local_ar import LocalArEngine, StreamBatch
+    import ctypes
+    w = make_weights(SHAPE_BASELINE, seed=21, dtype=torch.bfloat16, profile="parity", with_final=True)
+    w.final_b.view(POSITIONS, VOCAB)[:, S.EOS_ID] = 50.0
+    n = 8
+    eng = LocalArEngine(w, max_streams=n, path=path)
+    uf = torch.tensor([1, 0, 0, 0, 1, 0, 0, 0], dtype=torch.bool)
+    fi = torch.tensor([0, 1, 0, 0, 0, 1, 0, 0], dtype=torch.bool)
+    fb = torch.tensor([0, 0, 1, 0, 0, 0, 1, 0], dtype=torch.bool)
+    agg, ref = StreamBatch.allocate(n), StreamBatch.allocate(n)
+    agg.codec_tokens = torch.full((n, 8, 8), -7, dtype=torch.int64, device="cuda")
+    agg.finished_latch = torch.zeros(n, dtype=torch.bool, device="cuda")
+    for b in (agg, ref):
+        b.unfinished.copy_(uf); b.finished.copy_(fi); b.forbid_eos.copy_(fb)
+        b.rng_seed.copy_(torch.arange(n) + 3)
+    latch = np.zeros(n, bool)
+    for k, off in enumerate((0, 2, 4, 6)):
+        hidden = _hidden(n, 40 + k).cuda()
+        agg.decoder_hidden.copy_(hidden); ref.decoder_hidden.copy_(hidden)
+        agg.codec_frame_offset = off
+        eng.frame(agg)
+        eng.frame(ref)
+        torch.cuda.synchronize()
+        assert torch.equal(agg.codec_tokens[:, :, off:off + 2], ref.codec_tokens)
+        assert (agg.codec_tokens[:, :, off + 2:] == -7).all()
+        for name in ("end_frame_index", "rng_counter", "invalid_rows", "next_embedding"):
+            assert torch.equal(getattr(agg, name), getattr(ref, name)), name
+        end = ref.end_frame_index.cpu().numpy()
+        enabled = ~(uf | fi | fb).numpy()
+        assert (end[enabled] == 0).all() and (end[fi.numpy()] == 0).all() and (end[(uf | fb).numpy() & ~fi.numpy()] == -1).all()
+        latch |= (end == 0) | (end == 1)
+        np.testing.assert_array_equal(agg.finished_latch.cpu().numpy(), latch)
+    # argument checks: stride below 2, odd offset, offset past the row
+    for stride, off in ((1, 0), (8, 3), (8, 8), (2, 2), (-2, 0)):
+        cb = agg.c_struct()
+        cb.codec_frames_stride, cb.codec_frame_offset = stride, off
+        rc = L.lib.mtt_b200_launch_local_ar_frame(
+            ctypes.byref(eng._shape), ctypes.byref(eng._w), ctypes.byref(eng._sampling), ctypes.byref(cb),
+            ctypes.c_void_p(eng.workspace.data_ptr()), eng.workspace.numel(), None)
+        assert rc == L.STATUS_INVALID_ARGUMENT, (stride, off)
+
+
+@pytest.mark.parametrize("path", BOTH)
 def test_argmax_without_cfg(engines, path):
     """Greedy decoding, one row per stream (config 1's mode, bf16 on the GPU):
     no RNG, counter unchanged (magpietts_fused_sampling.py:136-197)."""
