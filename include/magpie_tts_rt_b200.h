@@ -2,7 +2,7 @@
  * magpie_tts_rt_b200 -- B200 (sm_100a) implementation of MagpieTTS-RT's
  * per-frame Local AR + sampling hot path, behind the reference's C ABI.
  *
- * Four groups of entry points:
+ * Five groups of entry points:
  *
  * 1. The plugin-library ABI the runtime dlopen()s
  *    (reference: include/magpie_tts_rt/magpie_tts_rt_plugin.h:70-152,
@@ -30,6 +30,10 @@
  *    arguments, and batched over sessions together with the Local AR EOS
  *    inputs (forbid_eos, unfinished, the finished latch) that the reference
  *    prepares on the host before every Local AR step.
+ *
+ * 5. The Main Decoder one-step (reference:
+ *    tools/export/main_decoder_wrapper.py MainDecoderStepWrapper), batched
+ *    over sessions: the decoder position between two Local AR frames.
  *
  * Streams (`void* stream`) are cudaStream_t values; NULL is the legacy
  * default stream.
@@ -499,6 +503,73 @@ typedef struct mtt_b200_alignment_batch {
 } mtt_b200_alignment_batch_t;
 
 MTT_B200_API int mtt_b200_launch_alignment_batch(const mtt_b200_alignment_batch_t* batch, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* 5. Main Decoder one-step                                                  */
+/* ------------------------------------------------------------------------ */
+
+/* Device pointers, bf16, PyTorch [out][in] layout, layer-major
+ * (tools/export/main_decoder_wrapper.py:778-911; accepted shape 12 layers,
+ * width 768, 12 self-attention heads of 64, one 128-wide cross-attention
+ * head, FFN 3072 of kernel-one convolutions). */
+typedef struct mtt_b200_main_decoder_weights {
+  const void* pos;      /* [pos_rows][768] learnable position embeddings */
+  const void* ln_self;  /* [L][768] */
+  const void* qkv;      /* [L][2304][768]: q, k, v rows (12 heads x 64 each) */
+  const void* o;        /* [L][768][768] */
+  const void* ln_xq;    /* [L][768] cross-attention query norm */
+  const void* xq;       /* [L][128][768] */
+  const void* xo;       /* [L][768][128] */
+  const void* ln_ff;    /* [L][768] */
+  const void* ffn1;     /* [L][3072][768] */
+  const void* ffn2;     /* [L][768][3072] */
+  const void* norm_out; /* [768] */
+  int32_t n_layers;     /* >= 10 (alignment layers 4, 5, 8, 9; prior layers 2..10) */
+  int32_t pos_rows;     /* >= cache_capacity */
+} mtt_b200_main_decoder_weights_t;
+
+/* Structure-of-arrays state of n sessions (device pointers).  Rows 2s and
+ * 2s + 1 are session s's conditional and unconditional rows.  S =
+ * token_stride (a multiple of 8, <= 512, >= every text length). */
+typedef struct mtt_b200_main_decoder_batch {
+  int32_t n_sessions;
+  int32_t cache_capacity;      /* positions per session cache (the reference: 467) */
+  int32_t token_stride;        /* S */
+  int32_t reserved_0;
+  const void* embedded;        /* [n][768] bf16: the codec-token embedding sum
+                                  (the Local AR frame's next_embedding) */
+  const int64_t* position;     /* [n] absolute position this step writes, in [0, cache_capacity) */
+  const uint32_t* text_length; /* [n] text tokens T, 1 <= T <= S */
+  const bool* active;          /* [n] or NULL: inactive sessions are skipped, their outputs untouched */
+  void* self_k;                /* [n][L][2][12][cache_capacity][64] bf16, in/out */
+  void* self_v;                /* same */
+  bool* self_mask;             /* [n][2][cache_capacity] key mask, in/out (one for all layers) */
+  const void* cross_k;         /* [n][L][2][S][128] bf16 text keys (prefill output) */
+  const void* cross_v;         /* same */
+  const bool* cond_mask;       /* [n][2][S] condition mask */
+  const void* prior;           /* [n][2][S] bf16 attention prior (the alignment gate's next_prior) */
+  void* hidden;                /* [n][2][768] bf16 out: the Local AR frame's decoder_hidden */
+  void* alignment;             /* [n][2][S] bf16 out: the alignment gate's scores */
+  int32_t* status;             /* [n] out: 0, or 1 for a position or text length out of range */
+} mtt_b200_main_decoder_batch_t;
+
+/* Workspace bytes for up to max_sessions sessions (0 for bad arguments). */
+MTT_B200_API size_t mtt_b200_main_decoder_workspace_size(int32_t max_sessions, int32_t token_stride);
+
+/*
+ * One Main Decoder position for every session (replaces one
+ * MainDecoderStepWrapper engine launch per session,
+ * src/runtime/synthesis_pipeline.cpp:572-648): writes each session's new
+ * key / value at its position and sets its key mask there, and produces the
+ * decoder hidden state and the alignment scores.  Stream-ordered; the layer
+ * GEMMs are cuBLASLt calls (its handle is created by the first call on a
+ * device: make that call before any stream capture).  workspace: >=
+ * mtt_b200_main_decoder_workspace_size bytes, 256-byte aligned.  Returns
+ * MTT_B200_STATUS_*.
+ */
+MTT_B200_API int mtt_b200_launch_main_decoder_step(const mtt_b200_main_decoder_weights_t* weights,
+                                                   const mtt_b200_main_decoder_batch_t* batch, void* workspace,
+                                                   size_t workspace_bytes, void* stream);
 
 /* ------------------------------------------------------------------------ */
 /* Test hooks (no reference counterpart beyond launch_test_clamped_gumbel,   */

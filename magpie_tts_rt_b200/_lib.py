@@ -137,6 +137,20 @@ class AlignmentBatch(ctypes.Structure):
     ]
 
 
+class MainDecoderWeights(ctypes.Structure):
+    _fields_ = [(n, P) for n in ("pos", "ln_self", "qkv", "o", "ln_xq", "xq", "xo", "ln_ff", "ffn1", "ffn2",
+                                 "norm_out")] + [("n_layers", I32), ("pos_rows", I32)]
+
+
+class MainDecoderBatch(ctypes.Structure):
+    _fields_ = [
+        ("n_sessions", I32), ("cache_capacity", I32), ("token_stride", I32), ("reserved_0", I32),
+        ("embedded", P), ("position", P), ("text_length", P), ("active", P), ("self_k", P), ("self_v", P),
+        ("self_mask", P), ("cross_k", P), ("cross_v", P), ("cond_mask", P), ("prior", P), ("hidden", P),
+        ("alignment", P), ("status", P),
+    ]
+
+
 # name -> (restype, argtypes)
 SIGNATURES = {
     "mtt_plugin_get_api_v1": (I32, [ctypes.POINTER(PluginApiV1)]),
@@ -164,6 +178,9 @@ SIGNATURES = {
     "mtt_b200_launch_alignment_controller": (
         I32, [P, ctypes.POINTER(AlignmentContract), P, P, P, P, P, P, P]),
     "mtt_b200_launch_alignment_batch": (I32, [ctypes.POINTER(AlignmentBatch), P]),
+    "mtt_b200_main_decoder_workspace_size": (SZ, [I32, I32]),
+    "mtt_b200_launch_main_decoder_step": (
+        I32, [ctypes.POINTER(MainDecoderWeights), ctypes.POINTER(MainDecoderBatch), P, SZ, P]),
     "mtt_b200_launch_test_clamped_gumbel": (I32, [P, P, SZ, P]),
     "mtt_b200_launch_test_log": (I32, [P, P, SZ, P]),
 }

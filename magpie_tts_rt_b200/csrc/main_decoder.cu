@@ -1,0 +1,702 @@
+// Main Decoder one-step for N sessions (both CFG rows each) per launch
+// sequence: the decoder position that produces the Local AR's input hidden
+// state and the alignment controller's scores.
+//
+// Reference: tools/export/main_decoder_wrapper.py:778-911
+// (MainDecoderStepWrapper.forward: one TensorRT engine per session per step,
+// K/V state as explicit engine I/O, src/runtime/synthesis_pipeline.cpp:
+// 572-648).  Per layer:
+//   add_ln     x = bf16(x + o); LN(x) (fused; the layer-0 form adds the
+//              position embedding to the codec embedding sum)
+//   GEMM       q|k|v = LN(x) W_qkv^T                  (cuBLASLt, bf16 in/out, f32 accumulate)
+//   self_attn  k, v written at the session's position; attention of the 12
+//              heads over positions [0, position] of the session's cache
+//   GEMM       o = att W_o^T
+//   add_ln     x += o; LN_xq(x)
+//   GEMM       q_x = LN_xq(x) W_xq^T                  (one 128-wide head)
+//   cross_attn attention over the session's text keys with the condition
+//              mask, renormalised by the alignment prior on layers 2..10;
+//              layers 4, 5, 8, 9 keep their probabilities, layer 9 writes
+//              their mean (the alignment scores)
+//   GEMM       o = ctx W_xo^T
+//   add_ln     x += o; LN_ff(x)
+//   GEMM, gelu h = GELU(LN_ff(x) W_ffn1^T)
+//   GEMM       o = h W_ffn2^T
+//   add_ln     x += o; LN of the next layer (or the output norm)
+// The GEMMs are plain library GEMMs (M = 2 x sessions rows); the attention,
+// normalisation and activation kernels are this file's.  The self-attention
+// cache stream is the step's dominant traffic (keys and values of every
+// layer, head and CFG row up to the position), so that kernel is written for
+// HBM bandwidth: one CTA per (session, row, head), 16-byte loads, four key
+// batches of 16 in flight per warp.
+#include <cublasLt.h>
+
+#include <map>
+#include <mutex>
+#include <tuple>
+
+#include "../../include/magpie_tts_rt_b200.h"
+#include "common.cuh"
+
+namespace mtt {
+namespace {
+
+using bf16 = __nv_bfloat16;
+
+constexpr int kW = 768;          // model width
+constexpr int kMH = 12;          // self-attention heads
+constexpr int kMD = 64;          // self-attention head width
+constexpr int kXD = 128;         // cross-attention head width (one head)
+constexpr int kFF = 3072;        // FFN width
+constexpr int kQKV = 3 * kW;
+constexpr int kMaxText = 512;
+constexpr int kAlignSlots = 4;
+constexpr int kLnThreads = 128;  // 4 rows per CTA, one warp per row
+
+__device__ __forceinline__ float bfr(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
+
+__device__ __forceinline__ void unpack8f(const uint4& u, float (&f)[8]) {
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const float2 t = __bfloat1622float2(h[j]);
+    f[2 * j] = t.x;
+    f[2 * j + 1] = t.y;
+  }
+}
+
+__device__ __forceinline__ uint4 pack8f(const float (&f)[8]) {
+  uint4 u;
+  __nv_bfloat162 h[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) h[j] = __floats2bfloat162_rn(f[2 * j], f[2 * j + 1]);
+  u.x = *reinterpret_cast<uint32_t*>(&h[0]);
+  u.y = *reinterpret_cast<uint32_t*>(&h[1]);
+  u.z = *reinterpret_cast<uint32_t*>(&h[2]);
+  u.w = *reinterpret_cast<uint32_t*>(&h[3]);
+  return u;
+}
+
+struct Step {
+  int n, L, cap, S;
+  const bf16 *pos, *ln_self, *qkv_w, *o_w, *ln_xq, *xq_w, *xo_w, *ln_ff, *ffn1_w, *ffn2_w, *norm_out;
+  const bf16* embedded;
+  const int64_t* position;
+  const uint32_t* text_length;
+  const bool* active;
+  bf16 *self_k, *self_v;
+  bool* self_mask;
+  const bf16 *cross_k, *cross_v;
+  const bool* cond_mask;
+  const bf16* prior;
+  bf16* hidden;
+  bf16* alignment;
+  int32_t* status;
+  // workspace
+  bf16 *x, *ln, *qkv, *att, *o, *xq, *ctx, *h, *align;
+};
+
+__device__ __forceinline__ bool session_active(const Step& st, int s) {
+  return st.active == nullptr || st.active[s];
+}
+
+__device__ __forceinline__ bool session_live(const Step& st, int s) {
+  if (!session_active(st, s)) return false;
+  const int64_t p = st.position[s];
+  const uint32_t t = st.text_length[s];
+  return p >= 0 && p < st.cap && t >= 1 && t <= static_cast<uint32_t>(st.S);
+}
+
+// ---------------------------------------------------------------------------
+// x = bf16(x + o), then LN(x) with the weight (no bias, eps 1e-5): one warp
+// per row of 768 (24 values per lane, two passes for the variance).  kEmbed:
+// layer 0's input instead, x = bf16(embedded[s] + pos[position[s]]) for both
+// rows of session s (main_decoder_wrapper.py:826-829), and the session's
+// status.  `out` receives the normalised row; rows of sessions that are
+// inactive or out of range are left as they are.
+// ---------------------------------------------------------------------------
+template <bool kEmbed>
+__global__ void __launch_bounds__(kLnThreads) add_ln_kernel(Step st, const bf16* __restrict__ w, bf16* out) {
+  const int lane = threadIdx.x & 31;
+  const int row = blockIdx.x * (kLnThreads / 32) + (threadIdx.x >> 5);
+  if (row >= 2 * st.n) return;
+  const int s = row >> 1;
+  if (kEmbed && lane == 0 && (row & 1) == 0 && session_active(st, s)) st.status[s] = session_live(st, s) ? 0 : 1;
+  if (!session_live(st, s)) return;
+  float v[24];
+  bf16* xr = st.x + static_cast<size_t>(row) * kW;
+#pragma unroll
+  for (int c = 0; c < 3; ++c) {
+    const int col = 8 * (lane + 32 * c);
+    float a[8], b[8];
+    if (kEmbed) {
+      unpack8f(*reinterpret_cast<const uint4*>(st.embedded + static_cast<size_t>(s) * kW + col), a);
+      unpack8f(*reinterpret_cast<const uint4*>(st.pos + static_cast<size_t>(st.position[s]) * kW + col), b);
+    } else {
+      unpack8f(*reinterpret_cast<const uint4*>(xr + col), a);
+      unpack8f(*reinterpret_cast<const uint4*>(st.o + static_cast<size_t>(row) * kW + col), b);
+    }
+    float t[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      t[e] = bfr(a[e] + b[e]);
+      v[8 * c + e] = t[e];
+    }
+    *reinterpret_cast<uint4*>(xr + col) = pack8f(t);
+  }
+  float sum = 0.f;
+#pragma unroll
+  for (int i = 0; i < 24; ++i) sum += v[i];
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+  const float mean = sum * (1.0f / kW);
+  float sq = 0.f;
+#pragma unroll
+  for (int i = 0; i < 24; ++i) {
+    const float d = v[i] - mean;
+    sq += d * d;
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, off);
+  const float rstd = 1.0f / sqrtf(sq * (1.0f / kW) + 1e-5f);
+#pragma unroll
+  for (int c = 0; c < 3; ++c) {
+    const int col = 8 * (lane + 32 * c);
+    float g[8], y[8];
+    unpack8f(*reinterpret_cast<const uint4*>(w + col), g);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) y[e] = (v[8 * c + e] - mean) * rstd * g[e];
+    *reinterpret_cast<uint4*>(out + static_cast<size_t>(row) * kW + col) = pack8f(y);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Self-attention of one (session, row, head) over positions [0, p]
+// (main_decoder_wrapper.py:836-877 and :188-228): the step's key and value
+// are written at position p of the cache first (torch.where on the cache
+// position); scores bf16(bf16(q.k) * 1/8), masked by the key mask (position p
+// itself is always valid: the step's query mask is all ones), softmax in f32
+// rounded to bf16, then the probability-weighted sum of the values, rounded
+// to bf16.  Keys are read as 128-byte rows, eight lanes per row, four rows
+// per warp per batch step and four batch steps per load wave.
+// ---------------------------------------------------------------------------
+constexpr int kSAThreads = 128;
+
+__global__ void __launch_bounds__(kSAThreads) self_attn_kernel(Step st, int l) {
+  extern __shared__ float sc[];  // [cap] scores, then probabilities
+  __shared__ float qs[kMD];
+  __shared__ __align__(16) bf16 kn[kMD];
+  __shared__ __align__(16) bf16 vn[kMD];
+  __shared__ float part[kSAThreads / 32][kMD];
+  __shared__ float red[kSAThreads / 32];
+  const int h = blockIdx.x, r = blockIdx.y, s = blockIdx.z;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int row = 2 * s + r;
+  bf16* out = st.att + static_cast<size_t>(row) * kW + h * kMD;
+  if (!session_live(st, s)) {
+    if (session_active(st, s) && tid < kMD) out[tid] = __float2bfloat16_rn(0.f);
+    return;
+  }
+  const int p = static_cast<int>(st.position[s]);
+  const bf16* qkv = st.qkv + static_cast<size_t>(row) * kQKV;
+  const size_t cbase = ((((static_cast<size_t>(s) * st.L + l) * 2 + r) * kMH + h) * st.cap) * kMD;
+  bf16* K = st.self_k + cbase;
+  bf16* V = st.self_v + cbase;
+  bool* mrow = st.self_mask + (static_cast<size_t>(s) * 2 + r) * st.cap;
+  // updated_mask (main_decoder_wrapper.py:853): the step's position joins the
+  // keys; no CTA reads mrow[p] (position p counts as valid below)
+  if (l == 0 && h == 0 && tid == 0) mrow[p] = true;
+  if (tid < kMD) {
+    qs[tid] = __bfloat162float(qkv[h * kMD + tid]);
+    const bf16 k = qkv[kW + h * kMD + tid], v = qkv[2 * kW + h * kMD + tid];
+    kn[tid] = k;
+    vn[tid] = v;
+    K[static_cast<size_t>(p) * kMD + tid] = k;
+    V[static_cast<size_t>(p) * kMD + tid] = v;
+  }
+  __syncthreads();
+  const int sub = lane & 7, slot = lane >> 3;  // 16-byte chunk of a row, row within the warp's four
+  float q8[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) q8[e] = qs[8 * sub + e];
+  // scores
+  for (int base = warp * 16; base <= p; base += 64) {
+    uint4 kv[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int j = base + 4 * u + slot;
+      kv[u] = make_uint4(0, 0, 0, 0);
+      if (j < p) kv[u] = *reinterpret_cast<const uint4*>(K + static_cast<size_t>(j) * kMD + 8 * sub);
+      else if (j == p) kv[u] = *reinterpret_cast<const uint4*>(kn + 8 * sub);
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int j = base + 4 * u + slot;
+      float k8[8];
+      unpack8f(kv[u], k8);
+      float d = 0.f;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) d = fmaf(q8[e], k8[e], d);
+      d += __shfl_xor_sync(0xffffffffu, d, 1);
+      d += __shfl_xor_sync(0xffffffffu, d, 2);
+      d += __shfl_xor_sync(0xffffffffu, d, 4);
+      if (sub == 0 && j <= p) {
+        const bool valid = j == p || mrow[j];
+        sc[j] = valid ? bfr(bfr(d) * 0.125f) : -CUDART_INF_F;
+      }
+    }
+  }
+  __syncthreads();
+  // softmax over [0, p] (position p is valid, so the maximum is finite)
+  float m = -CUDART_INF_F;
+  for (int j = tid; j <= p; j += kSAThreads) m = fmaxf(m, sc[j]);
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+  if (lane == 0) red[warp] = m;
+  __syncthreads();
+  m = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+  __syncthreads();
+  float sum = 0.f;
+  for (int j = tid; j <= p; j += kSAThreads) {
+    const float e = expf(sc[j] - m);
+    sc[j] = e;
+    sum += e;
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+  if (lane == 0) red[warp] = sum;
+  __syncthreads();
+  sum = (red[0] + red[1]) + (red[2] + red[3]);
+  for (int j = tid; j <= p; j += kSAThreads) sc[j] = bfr(sc[j] / sum);
+  __syncthreads();
+  // probability-weighted values
+  float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  for (int base = warp * 16; base <= p; base += 64) {
+    uint4 vv[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int j = base + 4 * u + slot;
+      vv[u] = make_uint4(0, 0, 0, 0);
+      if (j < p) vv[u] = *reinterpret_cast<const uint4*>(V + static_cast<size_t>(j) * kMD + 8 * sub);
+      else if (j == p) vv[u] = *reinterpret_cast<const uint4*>(vn + 8 * sub);
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int j = base + 4 * u + slot;
+      if (j <= p) {
+        const float pj = sc[j];
+        float v8[8];
+        unpack8f(vv[u], v8);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc[e] = fmaf(pj, v8[e], acc[e]);
+      }
+    }
+  }
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    acc[e] += __shfl_xor_sync(0xffffffffu, acc[e], 8);
+    acc[e] += __shfl_xor_sync(0xffffffffu, acc[e], 16);
+  }
+  if (slot == 0) {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) part[warp][8 * sub + e] = acc[e];
+  }
+  __syncthreads();
+  if (tid < kMD) out[tid] = __float2bfloat16_rn((part[0][tid] + part[1][tid]) + (part[2][tid] + part[3][tid]));
+}
+
+// ---------------------------------------------------------------------------
+// Cross-attention of one (session, row) (main_decoder_wrapper.py:559-603,
+// :101-122, :293-309): scores bf16(bf16(q.k) * 128^-1/2) over the session's T
+// text keys, condition-masked, softmax rounded to bf16; on prior layers
+// p = bf16(n / bf16(sum n)) with n = bf16(p * bf16(prior + tiny)); the context
+// is the probability-weighted sum of the values.  Alignment layers keep p
+// (slots 0..2) and the last writes bf16(mean of the four) (:325-345).
+// Sixteen lanes per 256-byte key row, two rows per warp per step.
+// ---------------------------------------------------------------------------
+constexpr int kXAThreads = 256;
+
+__global__ void __launch_bounds__(kXAThreads) cross_attn_kernel(Step st, int l, int prior_layer, int align_slot) {
+  __shared__ float sc[kMaxText];
+  __shared__ float qs[kXD];
+  __shared__ float part[kXAThreads / 32][kXD];
+  __shared__ float red[kXAThreads / 32];
+  const int r = blockIdx.x, s = blockIdx.y;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int row = 2 * s + r;
+  bf16* out = st.ctx + static_cast<size_t>(row) * kXD;
+  if (!session_live(st, s)) {
+    if (session_active(st, s) && tid < kXD) out[tid] = __float2bfloat16_rn(0.f);
+    return;
+  }
+  const int T = static_cast<int>(st.text_length[s]);
+  const size_t kb = ((static_cast<size_t>(s) * st.L + l) * 2 + r) * st.S * kXD;
+  const bf16* K = st.cross_k + kb;
+  const bf16* V = st.cross_v + kb;
+  const size_t rb = (static_cast<size_t>(s) * 2 + r) * st.S;
+  const bool* cm = st.cond_mask + rb;
+  if (tid < kXD) qs[tid] = __bfloat162float(st.xq[static_cast<size_t>(row) * kXD + tid]);
+  __syncthreads();
+  const int sub = lane & 15, slot = lane >> 4;
+  float q8[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) q8[e] = qs[8 * sub + e];
+  const float scale = 0.08838834764831845f;  // 128 ** -0.5
+  for (int base = warp * 8; base < T; base += 64) {
+    uint4 kv[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int j = base + 2 * u + slot;
+      kv[u] = j < T ? *reinterpret_cast<const uint4*>(K + static_cast<size_t>(j) * kXD + 8 * sub)
+                    : make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int j = base + 2 * u + slot;
+      float k8[8];
+      unpack8f(kv[u], k8);
+      float d = 0.f;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) d = fmaf(q8[e], k8[e], d);
+#pragma unroll
+      for (int off = 1; off < 16; off <<= 1) d += __shfl_xor_sync(0xffffffffu, d, off);
+      if (sub == 0 && j < T) sc[j] = cm[j] ? bfr(bfr(d) * scale) : -CUDART_INF_F;
+    }
+  }
+  __syncthreads();
+  float m = -CUDART_INF_F;
+  for (int j = tid; j < T; j += kXAThreads) m = fmaxf(m, sc[j]);
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+  if (lane == 0) red[warp] = m;
+  __syncthreads();
+  m = red[0];
+#pragma unroll
+  for (int w = 1; w < kXAThreads / 32; ++w) m = fmaxf(m, red[w]);
+  __syncthreads();
+  float sum = 0.f;
+  for (int j = tid; j < T; j += kXAThreads) {
+    const float e = m == -CUDART_INF_F ? 0.f : expf(sc[j] - m);
+    sc[j] = e;
+    sum += e;
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+  if (lane == 0) red[warp] = sum;
+  __syncthreads();
+  sum = 0.f;
+#pragma unroll
+  for (int w = 0; w < kXAThreads / 32; ++w) sum += red[w];
+  __syncthreads();
+  float nsum = 0.f;
+  const bf16* pr = st.prior + rb;
+  for (int j = tid; j < T; j += kXAThreads) {
+    float pj = cm[j] ? bfr(sc[j] / sum) : 0.f;  // softmax, then masked_fill(~valid, 0)
+    if (prior_layer) {
+      const float pri = bfr(__bfloat162float(pr[j]) + 1.17549435e-38f);  // prior + finfo(bf16).tiny
+      pj = bfr(pj * pri);
+      nsum += pj;
+    }
+    sc[j] = pj;
+  }
+  if (prior_layer) {
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) nsum += __shfl_xor_sync(0xffffffffu, nsum, off);
+    if (lane == 0) red[warp] = nsum;
+    __syncthreads();
+    nsum = 0.f;
+#pragma unroll
+    for (int w = 0; w < kXAThreads / 32; ++w) nsum += red[w];
+    const float den = bfr(nsum);
+    for (int j = tid; j < T; j += kXAThreads) sc[j] = bfr(sc[j] / den);
+  }
+  __syncthreads();
+  if (align_slot >= 0) {
+    for (int j = tid; j < T; j += kXAThreads) {
+      if (align_slot < kAlignSlots - 1) {
+        st.align[(static_cast<size_t>(align_slot) * 2 * st.n + row) * st.S + j] = __float2bfloat16_rn(sc[j]);
+      } else {
+        // stack(...).mean(dim=1): the four layers' values summed in layer order, then / 4
+        const float a0 = __bfloat162float(st.align[(static_cast<size_t>(0) * 2 * st.n + row) * st.S + j]);
+        const float a1 = __bfloat162float(st.align[(static_cast<size_t>(1) * 2 * st.n + row) * st.S + j]);
+        const float a2 = __bfloat162float(st.align[(static_cast<size_t>(2) * 2 * st.n + row) * st.S + j]);
+        st.alignment[rb + j] = __float2bfloat16_rn((((a0 + a1) + a2) + sc[j]) * 0.25f);
+      }
+    }
+  }
+  // context
+  float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  for (int base = warp * 8; base < T; base += 64) {
+    uint4 vv[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int j = base + 2 * u + slot;
+      vv[u] = j < T ? *reinterpret_cast<const uint4*>(V + static_cast<size_t>(j) * kXD + 8 * sub)
+                    : make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int j = base + 2 * u + slot;
+      if (j < T) {
+        const float pj = sc[j];
+        float v8[8];
+        unpack8f(vv[u], v8);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc[e] = fmaf(pj, v8[e], acc[e]);
+      }
+    }
+  }
+#pragma unroll
+  for (int e = 0; e < 8; ++e) acc[e] += __shfl_xor_sync(0xffffffffu, acc[e], 16);
+  if (slot == 0) {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) part[warp][8 * sub + e] = acc[e];
+  }
+  __syncthreads();
+  if (tid < kXD) {
+    float o = 0.f;
+#pragma unroll
+    for (int w = 0; w < kXAThreads / 32; ++w) o += part[w][tid];
+    out[tid] = __float2bfloat16_rn(o);
+  }
+}
+
+// GELU-tanh in place, bf16 (text_encoder_wrapper.py:61-70: F.gelu(approximate="tanh")).
+__global__ void gelu_kernel(bf16* h, size_t count8) {
+  const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= count8) return;
+  float f[8];
+  unpack8f(reinterpret_cast<const uint4*>(h)[i], f);
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    const float v = f[e];
+    f[e] = 0.5f * v * (1.0f + tanhf(0.7978845608028654f * (v + 0.044715f * v * v * v)));
+  }
+  reinterpret_cast<uint4*>(h)[i] = pack8f(f);
+}
+
+// ---------------------------------------------------------------------------
+// host: cuBLASLt GEMMs  C[M][N] = A[M][K] W[N][K]^T  (bf16, f32 accumulate)
+// ---------------------------------------------------------------------------
+
+struct GemmPlan {
+  cublasLtMatmulDesc_t op = nullptr;
+  cublasLtMatrixLayout_t la = nullptr, lb = nullptr, lc = nullptr;
+  cublasLtMatmulAlgo_t algo{};
+  bool ok = false;
+};
+
+struct LtState {
+  cublasLtHandle_t handle = nullptr;
+  std::map<std::tuple<int, int, int, size_t>, GemmPlan> plans;
+  std::mutex mu;
+};
+
+LtState& lt_state(int device) {
+  static std::mutex mu;
+  static std::map<int, LtState*> states;
+  std::lock_guard<std::mutex> lock(mu);
+  LtState*& s = states[device];
+  if (s == nullptr) {
+    s = new LtState();
+    if (cublasLtCreate(&s->handle) != CUBLAS_STATUS_SUCCESS) s->handle = nullptr;
+  }
+  return *s;
+}
+
+const GemmPlan* gemm_plan(LtState& st, int M, int N, int K, size_t ws_bytes) {
+  std::lock_guard<std::mutex> lock(st.mu);
+  auto key = std::make_tuple(M, N, K, ws_bytes);
+  auto it = st.plans.find(key);
+  if (it != st.plans.end()) return it->second.ok ? &it->second : nullptr;
+  GemmPlan& p = st.plans[key];
+  if (st.handle == nullptr) return nullptr;
+  const cublasOperation_t ta = CUBLAS_OP_T, tb = CUBLAS_OP_N;
+  bool ok = cublasLtMatmulDescCreate(&p.op, CUBLAS_COMPUTE_32F, CUDA_R_32F) == CUBLAS_STATUS_SUCCESS &&
+            cublasLtMatmulDescSetAttribute(p.op, CUBLASLT_MATMUL_DESC_TRANSA, &ta, sizeof(ta)) ==
+                CUBLAS_STATUS_SUCCESS &&
+            cublasLtMatmulDescSetAttribute(p.op, CUBLASLT_MATMUL_DESC_TRANSB, &tb, sizeof(tb)) ==
+                CUBLAS_STATUS_SUCCESS &&
+            // column-major view: W is K x N (op T), the activations K x M, C N x M
+            cublasLtMatrixLayoutCreate(&p.la, CUDA_R_16BF, K, N, K) == CUBLAS_STATUS_SUCCESS &&
+            cublasLtMatrixLayoutCreate(&p.lb, CUDA_R_16BF, K, M, K) == CUBLAS_STATUS_SUCCESS &&
+            cublasLtMatrixLayoutCreate(&p.lc, CUDA_R_16BF, N, M, N) == CUBLAS_STATUS_SUCCESS;
+  if (ok) {
+    cublasLtMatmulPreference_t pref = nullptr;
+    ok = cublasLtMatmulPreferenceCreate(&pref) == CUBLAS_STATUS_SUCCESS;
+    if (ok) {
+      const uint64_t ws = ws_bytes;
+      cublasLtMatmulPreferenceSetAttribute(pref, CUBLASLT_MATMUL_PREF_MAX_WORKSPACE_BYTES, &ws, sizeof(ws));
+      cublasLtMatmulHeuristicResult_t res{};
+      int found = 0;
+      ok = cublasLtMatmulAlgoGetHeuristic(st.handle, p.op, p.la, p.lb, p.lc, p.lc, pref, 1, &res, &found) ==
+               CUBLAS_STATUS_SUCCESS &&
+           found > 0;
+      if (ok) p.algo = res.algo;
+      cublasLtMatmulPreferenceDestroy(pref);
+    }
+  }
+  p.ok = ok;
+  return ok ? &p : nullptr;
+}
+
+bool gemm(LtState& st, const bf16* A, const bf16* W, bf16* C, int M, int N, int K, void* ws, size_t ws_bytes,
+          cudaStream_t stream) {
+  const GemmPlan* p = gemm_plan(st, M, N, K, ws_bytes);
+  if (p == nullptr) return false;
+  const float alpha = 1.f, beta = 0.f;
+  return cublasLtMatmul(st.handle, p->op, &alpha, W, p->la, A, p->lb, &beta, C, p->lc, C, p->lc, &p->algo, ws,
+                        ws_bytes, stream) == CUBLAS_STATUS_SUCCESS;
+}
+
+constexpr size_t kGemmWorkspace = 32u << 20;
+
+struct MdLayout {
+  size_t x, ln, qkv, att, o, xq, ctx, h, align, gemm_ws, total;
+};
+
+MdLayout md_layout(int n, int S) {
+  MdLayout lo{};
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    const size_t at = off;
+    off += (bytes + 255) & ~static_cast<size_t>(255);
+    return at;
+  };
+  const size_t rows = 2 * static_cast<size_t>(n);
+  lo.x = take(rows * kW * 2);
+  lo.ln = take(rows * kW * 2);
+  lo.qkv = take(rows * kQKV * 2);
+  lo.att = take(rows * kW * 2);
+  lo.o = take(rows * kW * 2);
+  lo.xq = take(rows * kXD * 2);
+  lo.ctx = take(rows * kXD * 2);
+  lo.h = take(rows * kFF * 2);
+  lo.align = take((kAlignSlots - 1) * rows * S * 2);
+  lo.gemm_ws = take(kGemmWorkspace);
+  lo.total = off;
+  return lo;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace
+}  // namespace mtt
+
+extern "C" MTT_B200_API size_t mtt_b200_main_decoder_workspace_size(int32_t max_sessions, int32_t token_stride) {
+  if (max_sessions <= 0 || token_stride <= 0 || token_stride > mtt::kMaxText || token_stride % 8 != 0) return 0;
+  return mtt::md_layout(max_sessions, token_stride).total;
+}
+
+extern "C" MTT_B200_API int mtt_b200_launch_main_decoder_step(const mtt_b200_main_decoder_weights_t* w,
+                                                             const mtt_b200_main_decoder_batch_t* b, void* workspace,
+                                                             size_t workspace_bytes, void* stream) {
+  using namespace mtt;
+  if (w == nullptr || b == nullptr || workspace == nullptr || b->n_sessions <= 0 || w->n_layers < 10 ||
+      b->cache_capacity <= 0 || b->token_stride <= 0 || b->token_stride > kMaxText || b->token_stride % 8 != 0) {
+    return MTT_B200_STATUS_INVALID_ARGUMENT;
+  }
+  if (!w->pos || !w->ln_self || !w->qkv || !w->o || !w->ln_xq || !w->xq || !w->xo || !w->ln_ff || !w->ffn1 ||
+      !w->ffn2 || !w->norm_out || w->pos_rows < b->cache_capacity) {
+    return MTT_B200_STATUS_INVALID_ARGUMENT;
+  }
+  if (!b->embedded || !b->position || !b->text_length || !b->self_k || !b->self_v || !b->self_mask || !b->cross_k ||
+      !b->cross_v || !b->cond_mask || !b->prior || !b->hidden || !b->alignment || !b->status) {
+    return MTT_B200_STATUS_INVALID_ARGUMENT;
+  }
+  const void* vec[] = {b->embedded, b->self_k, b->self_v, b->cross_k, b->cross_v, b->hidden, w->pos, w->ln_self,
+                       w->ln_xq, w->ln_ff, w->norm_out};
+  for (const void* p : vec)
+    if (!aligned16(p)) return MTT_B200_STATUS_INVALID_ARGUMENT;
+  const MdLayout lo = md_layout(b->n_sessions, b->token_stride);
+  if (workspace_bytes < lo.total || (reinterpret_cast<uintptr_t>(workspace) & 255u) != 0)
+    return MTT_B200_STATUS_INVALID_ARGUMENT;
+  int device = 0;
+  if (cudaGetDevice(&device) != cudaSuccess) return MTT_B200_STATUS_CUDA_ERROR;
+  LtState& lt = lt_state(device);
+  if (lt.handle == nullptr) return MTT_B200_STATUS_CUDA_ERROR;
+  const cudaStream_t cs = static_cast<cudaStream_t>(stream);
+
+  Step st{};
+  st.n = b->n_sessions;
+  st.L = w->n_layers;
+  st.cap = b->cache_capacity;
+  st.S = b->token_stride;
+  auto B = [](const void* p) { return static_cast<const bf16*>(p); };
+  st.pos = B(w->pos);
+  st.ln_self = B(w->ln_self);
+  st.qkv_w = B(w->qkv);
+  st.o_w = B(w->o);
+  st.ln_xq = B(w->ln_xq);
+  st.xq_w = B(w->xq);
+  st.xo_w = B(w->xo);
+  st.ln_ff = B(w->ln_ff);
+  st.ffn1_w = B(w->ffn1);
+  st.ffn2_w = B(w->ffn2);
+  st.norm_out = B(w->norm_out);
+  st.embedded = B(b->embedded);
+  st.position = b->position;
+  st.text_length = b->text_length;
+  st.active = b->active;
+  st.self_k = static_cast<bf16*>(b->self_k);
+  st.self_v = static_cast<bf16*>(b->self_v);
+  st.self_mask = b->self_mask;
+  st.cross_k = B(b->cross_k);
+  st.cross_v = B(b->cross_v);
+  st.cond_mask = b->cond_mask;
+  st.prior = B(b->prior);
+  st.hidden = static_cast<bf16*>(b->hidden);
+  st.alignment = static_cast<bf16*>(b->alignment);
+  st.status = b->status;
+  char* ws = static_cast<char*>(workspace);
+  st.x = reinterpret_cast<bf16*>(ws + lo.x);
+  st.ln = reinterpret_cast<bf16*>(ws + lo.ln);
+  st.qkv = reinterpret_cast<bf16*>(ws + lo.qkv);
+  st.att = reinterpret_cast<bf16*>(ws + lo.att);
+  st.o = reinterpret_cast<bf16*>(ws + lo.o);
+  st.xq = reinterpret_cast<bf16*>(ws + lo.xq);
+  st.ctx = reinterpret_cast<bf16*>(ws + lo.ctx);
+  st.h = reinterpret_cast<bf16*>(ws + lo.h);
+  st.align = reinterpret_cast<bf16*>(ws + lo.align);
+  void* gws = ws + lo.gemm_ws;
+
+  const int M = 2 * st.n;
+  const unsigned ln_grid = static_cast<unsigned>((M + kLnThreads / 32 - 1) / (kLnThreads / 32));
+  const size_t sa_smem = static_cast<size_t>(st.cap) * sizeof(float);
+  if (sa_smem > 48 * 1024 &&
+      cudaFuncSetAttribute(self_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           static_cast<int>(sa_smem)) != cudaSuccess) {
+    return MTT_B200_STATUS_INVALID_ARGUMENT;
+  }
+  auto layer_w = [](const bf16* base, size_t per_layer, int l) { return base + per_layer * l; };
+  add_ln_kernel<true><<<ln_grid, kLnThreads, 0, cs>>>(st, st.ln_self, st.ln);
+  int slot = 0;
+  for (int l = 0; l < st.L; ++l) {
+    bool ok = gemm(lt, st.ln, layer_w(st.qkv_w, static_cast<size_t>(kQKV) * kW, l), st.qkv, M, kQKV, kW, gws,
+                   kGemmWorkspace, cs);
+    self_attn_kernel<<<dim3(kMH, 2, st.n), kSAThreads, sa_smem, cs>>>(st, l);
+    ok = ok && gemm(lt, st.att, layer_w(st.o_w, static_cast<size_t>(kW) * kW, l), st.o, M, kW, kW, gws,
+                    kGemmWorkspace, cs);
+    add_ln_kernel<false><<<ln_grid, kLnThreads, 0, cs>>>(st, layer_w(st.ln_xq, kW, l), st.ln);
+    ok = ok && gemm(lt, st.ln, layer_w(st.xq_w, static_cast<size_t>(kXD) * kW, l), st.xq, M, kXD, kW, gws,
+                    kGemmWorkspace, cs);
+    const bool prior_layer = l >= 2 && l <= 10;
+    const bool align_layer = l == 4 || l == 5 || l == 8 || l == 9;
+    cross_attn_kernel<<<dim3(2, st.n), kXAThreads, 0, cs>>>(st, l, prior_layer ? 1 : 0, align_layer ? slot : -1);
+    if (align_layer) ++slot;
+    ok = ok && gemm(lt, st.ctx, layer_w(st.xo_w, static_cast<size_t>(kW) * kXD, l), st.o, M, kW, kXD, gws,
+                    kGemmWorkspace, cs);
+    add_ln_kernel<false><<<ln_grid, kLnThreads, 0, cs>>>(st, layer_w(st.ln_ff, kW, l), st.ln);
+    ok = ok && gemm(lt, st.ln, layer_w(st.ffn1_w, static_cast<size_t>(kFF) * kW, l), st.h, M, kFF, kW, gws,
+                    kGemmWorkspace, cs);
+    const size_t count8 = static_cast<size_t>(M) * kFF / 8;
+    gelu_kernel<<<static_cast<unsigned>((count8 + 255) / 256), 256, 0, cs>>>(st.h, count8);
+    ok = ok && gemm(lt, st.h, layer_w(st.ffn2_w, static_cast<size_t>(kW) * kFF, l), st.o, M, kW, kFF, gws,
+                    kGemmWorkspace, cs);
+    const bool last = l + 1 == st.L;
+    add_ln_kernel<false><<<ln_grid, kLnThreads, 0, cs>>>(st, last ? st.norm_out : layer_w(st.ln_self, kW, l + 1),
+                                                         last ? st.hidden : st.ln);
+    if (!ok) return MTT_B200_STATUS_CUDA_ERROR;
+  }
+  return cudaPeekAtLastError() == cudaSuccess ? MTT_B200_STATUS_OK : MTT_B200_STATUS_CUDA_ERROR;
+}

@@ -129,3 +129,15 @@ def test_alignment_launchers_without_a_gpu():
     assert L.lib.mtt_b200_launch_alignment_batch(ctypes.byref(b), None) == -1
     b.n_sessions = -1
     assert L.lib.mtt_b200_launch_alignment_batch(ctypes.byref(b), None) == -1
+
+
+def test_main_decoder_entry_without_a_gpu():
+    """Argument checks decided before any CUDA call."""
+    assert L.lib.mtt_b200_main_decoder_workspace_size(0, 128) == 0
+    assert L.lib.mtt_b200_main_decoder_workspace_size(4, 513) == 0
+    assert L.lib.mtt_b200_main_decoder_workspace_size(4, 100) == 0
+    assert L.lib.mtt_b200_main_decoder_workspace_size(4, 128) > 32 << 20
+    assert L.lib.mtt_b200_launch_main_decoder_step(None, None, None, 0, None) == -1
+    w, b = L.MainDecoderWeights(), L.MainDecoderBatch()
+    b.n_sessions, b.cache_capacity, b.token_stride, w.n_layers = 2, 467, 100, 12  # stride not a multiple of 8
+    assert L.lib.mtt_b200_launch_main_decoder_step(ctypes.byref(w), ctypes.byref(b), None, 0, None) == -1
