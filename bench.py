@@ -20,7 +20,9 @@ FFN 1024, 16 heads 256->2024, 16 tables 2024x768):
 
 Also at N=1: the alignment gate (the controller step plus the Local AR's
 EOS inputs, once per decoder step) for the config-4 sessions of one GPU, with
-the reference's own host controller timed beside it.
+the reference's own host controller timed beside it; and the Main Decoder
+step for config 5's 256 sessions per GPU (``main_decoder_step``), with the
+CPU restatement timed beside it.
 
 A "frame" is one session's 16-position Local AR step (one decoder hidden in,
 16 codec tokens = 2 codec frames x 8 codebooks out).
@@ -73,6 +75,10 @@ def parse():
     ap.add_argument("--sessions", type=int, default=None,
                     help="override sessions per GPU (profiling a smaller per-GPU batch, e.g. 256 = config 4 at 4 GPUs)")
     ap.add_argument("--no-latency", action="store_true")
+    ap.add_argument("--main-decoder-only", action="store_true",
+                    help="run only the Main Decoder step measurement and print its object (profiling)")
+    ap.add_argument("--md-sessions", type=int, default=256, help="Main Decoder sessions per GPU (config 5: 256)")
+    ap.add_argument("--md-steps", type=int, default=20)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     return ap.parse_args()
 
@@ -480,6 +486,91 @@ def alignment_gate_measure(dev, peaks, n=1024, stride=512, steps=200, seed=11):
     return out
 
 
+def main_decoder_measure(dev, peaks, n=256, steps=20, text=128, cap=467, seed=13, with_cpu=True):
+    """The Main Decoder step (mtt_b200_launch_main_decoder_step) for config
+    5's sessions of one GPU: n sessions x CFG pair, the reference's cache of
+    467 positions, 128 text tokens, positions starting U[218, 466 - steps]
+    and advancing one per step; `steps` steps timed by CUDA events after 3
+    warm-up steps.  Algorithmic bytes per step: the layer weights once, and
+    per session the keys and values of every layer, head and row up to its
+    position, the text keys and values of every layer, and its ~20 KB of
+    activations; FLOPs: 2 x 2 rows x 87.3 M MAC of projections per session
+    plus the attention."""
+    from magpie_tts_rt_b200.main_decoder import (
+        CROSS_DIM, HEAD_DIM, HEADS, LAYERS, WIDTH, MainDecoderBatch, MainDecoderEngine,
+        make_main_decoder_weights, step_weight_bytes,
+    )
+    w = make_main_decoder_weights(seed, positions=cap)
+    eng = MainDecoderEngine(w, max_sessions=n, token_stride=text, device=dev)
+    b = MainDecoderBatch.allocate(n, cap=cap, token_stride=text, device=dev)
+    rng = np.random.default_rng(seed)
+    pos0 = torch.from_numpy(rng.integers(218, cap - steps - 4, n)).to(dev)
+    g = torch.Generator(device=dev).manual_seed(seed)
+    b.embedded.normal_(0, 0.05, generator=g)
+    b.cross_k.normal_(generator=g)
+    b.cross_v.normal_(generator=g)
+    b.self_k.normal_(generator=g)
+    b.self_v.normal_(generator=g)
+    b.text_length.fill_(text)
+    b.cond_mask.fill_(True)
+    b.cond_mask[:, 1, 1:] = False
+    b.prior.fill_(0.1)
+    b.prior[:, 0, :16] = 1.0
+    idx = torch.arange(cap, device=dev)
+    b.self_mask.copy_((idx[None, None, :] < pos0[:, None, None]).expand(n, 2, cap))
+    b.position.copy_(pos0)
+    stream = torch.cuda.Stream(dev)
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            eng.step(b, stream=stream)
+            b.position += 1
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start_pos = b.position.clone()
+        e0.record(stream)
+        for _ in range(steps):
+            eng.step(b, stream=stream)
+            b.position += 1
+        e1.record(stream)
+    torch.cuda.synchronize(dev)
+    us = e0.elapsed_time(e1) * 1000.0 / steps
+    bad = int((b.status != 0).sum().item())
+    active = (start_pos.double() + 1).cpu().numpy()  # keys read per row and head at the first timed step
+    kv = float(LAYERS * 2 * HEADS * HEAD_DIM * 2 * 2) * (active.sum() + n * (steps - 1) / 2)
+    cross = float(n * LAYERS * 2 * text * CROSS_DIM * 2 * 2)
+    act = n * 2 * 20_000.0
+    bytes_ = step_weight_bytes() + kv + cross + act
+    macs_proj = LAYERS * (3 * WIDTH * WIDTH + WIDTH * WIDTH + 2 * CROSS_DIM * WIDTH + 2 * 3072 * WIDTH)
+    flops = 2 * 2 * n * macs_proj + 2 * 2 * n * LAYERS * (HEADS * HEAD_DIM * 2 * active.mean() + CROSS_DIM * 2 * text)
+    gbs = bytes_ / (us * 1e-6) / 1e9
+    out = {"workload": f"config 5 per GPU: {n} sessions x CFG pair, cache {cap}, {text} text tokens, positions "
+                       f"U[218, {cap - steps - 4}) advancing one per step, {steps} steps",
+           "us_per_step": us, "decoder_steps_per_s": n * 1e6 / us, "status_nonzero": bad,
+           "kernels": "per layer: 6 cuBLASLt GEMMs + self_attn_kernel + cross_attn_kernel + 3 add_ln_kernel + "
+                      "gelu_kernel",
+           "gpu_launches_per_step": 1 + LAYERS * 12,
+           "roofline": {"bound": "hbm", "algorithmic_bytes_per_step": bytes_, "achieved": gbs, "unit": "GB/s",
+                        "peak": peaks["hbm_gbs"], "frac": gbs / peaks["hbm_gbs"],
+                        "algorithmic_flops_per_step": flops,
+                        "tflops": flops / (us * 1e-6) / 1e12}}
+    del b, eng
+    torch.cuda.empty_cache()
+    if with_cpu:
+        from oracle import main_decoder as OMD
+        torch.set_num_threads(os.cpu_count() or 1)
+        k = 0
+        t0 = time.perf_counter()
+        while time.perf_counter() - t0 < 8.0 or k < 2:
+            inp = OMD.make_step_inputs(100 + k, text, 300, cap)
+            OMD.step(w, inp)
+            k += 1
+        dt = (time.perf_counter() - t0) / k
+        out["cpu_baseline"] = {"value": n * dt * 1e6, "unit": "us per step of all sessions", "kind": "port",
+                               "cores": torch.get_num_threads(),
+                               "sample": f"{k} single-session steps of the PyTorch-CPU restatement (bit-exact with "
+                                         f"the reference wrapper), position 300, scaled to {n} sessions"}
+    return out
+
+
 # ---------------------------------------------------------------------------
 # CPU baseline (oracle restatement of the reference's path)
 # ---------------------------------------------------------------------------
@@ -530,6 +621,12 @@ def main():
     args = parse()
     world, rank, local = dist_init()
     peaks, peaks_kind = load_peaks()
+    if args.main_decoder_only:
+        out = main_decoder_measure(torch.device("cuda", local), peaks, n=args.md_sessions, steps=args.md_steps,
+                                   with_cpu=False)
+        if rank == 0:
+            print(json.dumps({"main_decoder_step": out}), flush=True)
+        return
     cfgw = dict(WORKLOADS[args.workload])
     if args.sessions:
         cfgw.update(weak=True)
@@ -565,6 +662,10 @@ def main():
     align = None
     if world == 1 and not args.no_latency:
         align = alignment_gate_measure(torch.device("cuda", local), peaks)
+    md = None
+    if world == 1 and not args.no_latency:
+        md = main_decoder_measure(torch.device("cuda", local), peaks, n=args.md_sessions, steps=args.md_steps,
+                                  with_cpu=rank == 0 and not args.no_cpu_baseline)
     cpu = None
     if world == 1 and rank == 0 and not args.no_cpu_baseline:
         cpu = cpu_oracle_sample()
@@ -608,7 +709,8 @@ def main():
                         "d2h_bytes_per_step": res["d2h"]},
                 "gpu_launches": res["launches"], "frame_path": res["path"], "clocks": res["clocks"],
                 "roofline": roof,
-                "latency_config2": latency, "alignment_gate": align, "cpu_baseline": cpu,
+                "latency_config2": latency, "alignment_gate": align, "main_decoder_step": md,
+                "cpu_baseline": cpu,
                 "checks": {"invalid_rows": res["invalid"], "forced_eos_ok": res["forced_ok"]}}
         print(json.dumps(line), flush=True)
     if world > 1:

@@ -27,8 +27,8 @@
 // normalisation and activation kernels are this file's.  The self-attention
 // cache stream is the step's dominant traffic (keys and values of every
 // layer, head and CFG row up to the position), so that kernel is written for
-// HBM bandwidth: one CTA per (session, row, head), 16-byte loads, four key
-// batches of 16 in flight per warp.
+// HBM bandwidth: one CTA per (session, row, head), keys and values streamed
+// together in one pass through a shared-memory ring filled by bulk copies.
 #include <cublasLt.h>
 
 #include <map>
@@ -175,20 +175,76 @@ __global__ void __launch_bounds__(kLnThreads) add_ln_kernel(Step st, const bf16*
 // (main_decoder_wrapper.py:836-877 and :188-228): the step's key and value
 // are written at position p of the cache first (torch.where on the cache
 // position); scores bf16(bf16(q.k) * 1/8), masked by the key mask (position p
-// itself is always valid: the step's query mask is all ones), softmax in f32
-// rounded to bf16, then the probability-weighted sum of the values, rounded
-// to bf16.  Keys are read as 128-byte rows, eight lanes per row, four rows
-// per warp per batch step and four batch steps per load wave.
+// itself is always valid: the step's query mask is all ones), softmax and the
+// probability-weighted sum of the values in one pass over the cache (running
+// maximum and sum per 8-lane group, rescaled once per four keys, merged at
+// the end), rounded to bf16 once.  The probabilities are not rounded to bf16
+// before the value sum, as the reference's two separate operations do: one
+// rounding fewer, no further from the exact result.
+//
+// The cache rows [0, p) stream through a three-stage shared-memory ring of
+// 64-key chunks (8 KB of keys + 8 KB of values per stage), filled by 1-D bulk
+// copies (cp.async.bulk, no multicast) that one thread issues and an mbarrier
+// per stage completes; the copies need no registers, so four CTAs per SM keep
+// up to 12 chunks in flight.  Eight lanes read one 128-byte row from shared
+// memory.  A wait that does not complete within its bound marks the session's
+// status 2; the kernel then stops issuing and waits (bounded) for the copies
+// it issued before it exits.
 // ---------------------------------------------------------------------------
 constexpr int kSAThreads = 128;
+constexpr int kSAGroups = kSAThreads / 8;  // 8-lane groups, one key row each per step
+constexpr int kSAChunk = 64;               // keys per stage
+constexpr int kSAStages = 3;
+constexpr uint32_t kSARowBytes = kMD * 2;  // 128 bytes per key or value row
+
+struct SAStage {
+  bf16 k[kSAChunk * kMD];
+  bf16 v[kSAChunk * kMD];
+};
+constexpr size_t kSASmem = kSAStages * sizeof(SAStage);  // 48 KB
+
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, unsigned long long* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+               ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(dst))), "l"(src), "r"(bytes),
+               "r"(static_cast<uint32_t>(__cvta_generic_to_shared(bar)))
+               : "memory");
+}
+
+__device__ __forceinline__ bool sa_wait(unsigned long long* bar, uint32_t parity) {
+  const uint32_t a = static_cast<uint32_t>(__cvta_generic_to_shared(bar));
+  unsigned long long t0;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t0));
+  while (true) {
+    uint32_t done;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(done)
+        : "r"(a), "r"(parity)
+        : "memory");
+    if (done) return true;
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+    if (t - t0 > 20000000ull) return false;  // 20 ms
+  }
+}
+
+// Running softmax state of an 8-lane group: maximum, sum of exponentials
+// and the lane's eight dimensions of the weighted value sum.
+struct SARun {
+  float m, l;
+  float acc[8];
+};
 
 __global__ void __launch_bounds__(kSAThreads) self_attn_kernel(Step st, int l) {
-  extern __shared__ float sc[];  // [cap] scores, then probabilities
+  extern __shared__ __align__(128) unsigned char sa_dyn[];
+  SAStage* stage = reinterpret_cast<SAStage*>(sa_dyn);
+  __shared__ unsigned long long full[kSAStages];
   __shared__ float qs[kMD];
   __shared__ __align__(16) bf16 kn[kMD];
   __shared__ __align__(16) bf16 vn[kMD];
-  __shared__ float part[kSAThreads / 32][kMD];
-  __shared__ float red[kSAThreads / 32];
+  __shared__ float gm[kSAGroups], gl[kSAGroups];
+  __shared__ float gacc[kSAGroups][kMD];
+  __shared__ int err, issued;
   const int h = blockIdx.x, r = blockIdx.y, s = blockIdx.z;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int row = 2 * s + r;
@@ -203,6 +259,28 @@ __global__ void __launch_bounds__(kSAThreads) self_attn_kernel(Step st, int l) {
   bf16* K = st.self_k + cbase;
   bf16* V = st.self_v + cbase;
   bool* mrow = st.self_mask + (static_cast<size_t>(s) * 2 + r) * st.cap;
+  const int nchunks = (p + kSAChunk - 1) / kSAChunk;  // cache rows [0, p)
+  auto issue = [&](int c) {  // thread 0
+    const uint32_t rows = static_cast<uint32_t>(min(kSAChunk, p - kSAChunk * c));
+    SAStage& sg = stage[c % kSAStages];
+    unsigned long long* bar = &full[c % kSAStages];
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;"
+                 ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(bar))), "r"(2 * rows * kSARowBytes)
+                 : "memory");
+    bulk_load(sg.k, K + static_cast<size_t>(kSAChunk) * c * kMD, rows * kSARowBytes, bar);
+    bulk_load(sg.v, V + static_cast<size_t>(kSAChunk) * c * kMD, rows * kSARowBytes, bar);
+    issued = c + 1;
+  };
+  if (tid == 0) {
+    err = 0;
+    issued = 0;
+#pragma unroll
+    for (int i = 0; i < kSAStages; ++i)
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(&full[i])))
+                   : "memory");
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    for (int c = 0; c < min(kSAStages, nchunks); ++c) issue(c);
+  }
   // updated_mask (main_decoder_wrapper.py:853): the step's position joins the
   // keys; no CTA reads mrow[p] (position p counts as valid below)
   if (l == 0 && h == 0 && tid == 0) mrow[p] = true;
@@ -216,93 +294,109 @@ __global__ void __launch_bounds__(kSAThreads) self_attn_kernel(Step st, int l) {
   }
   __syncthreads();
   const int sub = lane & 7, slot = lane >> 3;  // 16-byte chunk of a row, row within the warp's four
+  const int group = warp * 4 + slot;
   float q8[8];
 #pragma unroll
   for (int e = 0; e < 8; ++e) q8[e] = qs[8 * sub + e];
-  // scores
-  for (int base = warp * 16; base <= p; base += 64) {
-    uint4 kv[4];
+  SARun run{-CUDART_INF_F, 0.f, {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f}};
+  // fold up to four keys (scores sc[u], valid[u], value rows vr[u]) into the run
+  auto fold4 = [&](const float (&sc)[4], const bool (&ok)[4], const uint4 (&vr)[4]) {
+    float mn = run.m;
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+      if (ok[u]) mn = fmaxf(mn, sc[u]);
+    if (mn == -CUDART_INF_F) return;  // no valid key yet
+    const float c = __expf(run.m - mn);
+    run.l *= c;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) run.acc[e] *= c;
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
-      const int j = base + 4 * u + slot;
-      kv[u] = make_uint4(0, 0, 0, 0);
-      if (j < p) kv[u] = *reinterpret_cast<const uint4*>(K + static_cast<size_t>(j) * kMD + 8 * sub);
-      else if (j == p) kv[u] = *reinterpret_cast<const uint4*>(kn + 8 * sub);
+      if (ok[u]) {
+        const float ej = __expf(sc[u] - mn);
+        float v8[8];
+        unpack8f(vr[u], v8);
+        run.l += ej;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) run.acc[e] = fmaf(ej, v8[e], run.acc[e]);
+      }
     }
+    run.m = mn;
+  };
+  for (int c = 0; c < nchunks; ++c) {
+    const SAStage& sg = stage[c % kSAStages];
+    if (!sa_wait(&full[c % kSAStages], static_cast<uint32_t>((c / kSAStages) & 1))) err = 1;
+    const int rows = min(kSAChunk, p - kSAChunk * c);
+    float sc[4];
+    bool ok[4];
+    uint4 vr[4];
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
-      const int j = base + 4 * u + slot;
+      const int jj = warp * 16 + 4 * u + slot;
+      const bool in = jj < rows;
+      const uint4 kr = in ? *reinterpret_cast<const uint4*>(sg.k + jj * kMD + 8 * sub) : make_uint4(0, 0, 0, 0);
+      vr[u] = in ? *reinterpret_cast<const uint4*>(sg.v + jj * kMD + 8 * sub) : make_uint4(0, 0, 0, 0);
       float k8[8];
-      unpack8f(kv[u], k8);
+      unpack8f(kr, k8);
       float d = 0.f;
 #pragma unroll
       for (int e = 0; e < 8; ++e) d = fmaf(q8[e], k8[e], d);
       d += __shfl_xor_sync(0xffffffffu, d, 1);
       d += __shfl_xor_sync(0xffffffffu, d, 2);
       d += __shfl_xor_sync(0xffffffffu, d, 4);
-      if (sub == 0 && j <= p) {
-        const bool valid = j == p || mrow[j];
-        sc[j] = valid ? bfr(bfr(d) * 0.125f) : -CUDART_INF_F;
-      }
+      sc[u] = bfr(bfr(d) * 0.125f);
+      ok[u] = in && mrow[kSAChunk * c + jj];
+    }
+    fold4(sc, ok, vr);
+    __syncthreads();  // every thread is done with this stage
+    if (tid == 0 && err == 0 && c + kSAStages < nchunks) {
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      issue(c + kSAStages);
     }
   }
-  __syncthreads();
-  // softmax over [0, p] (position p is valid, so the maximum is finite)
-  float m = -CUDART_INF_F;
-  for (int j = tid; j <= p; j += kSAThreads) m = fmaxf(m, sc[j]);
+  // position p: the step's own key and value, from shared memory (group 0)
+  {
+    const uint4 kr = *reinterpret_cast<const uint4*>(kn + 8 * sub);
+    float k8[8];
+    unpack8f(kr, k8);
+    float d = 0.f;
 #pragma unroll
-  for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
-  if (lane == 0) red[warp] = m;
-  __syncthreads();
-  m = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
-  __syncthreads();
-  float sum = 0.f;
-  for (int j = tid; j <= p; j += kSAThreads) {
-    const float e = expf(sc[j] - m);
-    sc[j] = e;
-    sum += e;
+    for (int e = 0; e < 8; ++e) d = fmaf(q8[e], k8[e], d);
+    d += __shfl_xor_sync(0xffffffffu, d, 1);
+    d += __shfl_xor_sync(0xffffffffu, d, 2);
+    d += __shfl_xor_sync(0xffffffffu, d, 4);
+    const float sc[4] = {bfr(bfr(d) * 0.125f), 0.f, 0.f, 0.f};
+    const bool ok[4] = {group == 0, false, false, false};
+    const uint4 vr[4] = {*reinterpret_cast<const uint4*>(vn + 8 * sub), make_uint4(0, 0, 0, 0),
+                         make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)};
+    fold4(sc, ok, vr);
+  }
+  if (sub == 0) {
+    gm[group] = run.m;
+    gl[group] = run.l;
   }
 #pragma unroll
-  for (int off = 16; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
-  if (lane == 0) red[warp] = sum;
+  for (int e = 0; e < 8; ++e) gacc[group][8 * sub + e] = run.acc[e];
   __syncthreads();
-  sum = (red[0] + red[1]) + (red[2] + red[3]);
-  for (int j = tid; j <= p; j += kSAThreads) sc[j] = bfr(sc[j] / sum);
-  __syncthreads();
-  // probability-weighted values
-  float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-  for (int base = warp * 16; base <= p; base += 64) {
-    uint4 vv[4];
+  if (tid == 0 && err != 0) {
+    // a wait gave up: wait (bounded) for every copy this CTA issued, then flag the session
+    for (int c = max(0, issued - kSAStages); c < issued; ++c)
+      sa_wait(&full[c % kSAStages], static_cast<uint32_t>((c / kSAStages) & 1));
+    st.status[s] = 2;
+  }
+  if (tid < kMD) {
+    float mx = gm[0];
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const int j = base + 4 * u + slot;
-      vv[u] = make_uint4(0, 0, 0, 0);
-      if (j < p) vv[u] = *reinterpret_cast<const uint4*>(V + static_cast<size_t>(j) * kMD + 8 * sub);
-      else if (j == p) vv[u] = *reinterpret_cast<const uint4*>(vn + 8 * sub);
+    for (int g = 1; g < kSAGroups; ++g) mx = fmaxf(mx, gm[g]);  // finite: position p is valid
+    float L = 0.f, o = 0.f;
+#pragma unroll
+    for (int g = 0; g < kSAGroups; ++g) {
+      const float c = gm[g] == -CUDART_INF_F ? 0.f : __expf(gm[g] - mx);  // 0 for a group without keys
+      L = fmaf(gl[g], c, L);
+      o = fmaf(gacc[g][tid], c, o);
     }
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const int j = base + 4 * u + slot;
-      if (j <= p) {
-        const float pj = sc[j];
-        float v8[8];
-        unpack8f(vv[u], v8);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) acc[e] = fmaf(pj, v8[e], acc[e]);
-      }
-    }
+    out[tid] = __float2bfloat16_rn(o / L);
   }
-#pragma unroll
-  for (int e = 0; e < 8; ++e) {
-    acc[e] += __shfl_xor_sync(0xffffffffu, acc[e], 8);
-    acc[e] += __shfl_xor_sync(0xffffffffu, acc[e], 16);
-  }
-  if (slot == 0) {
-#pragma unroll
-    for (int e = 0; e < 8; ++e) part[warp][8 * sub + e] = acc[e];
-  }
-  __syncthreads();
-  if (tid < kMD) out[tid] = __float2bfloat16_rn((part[0][tid] + part[1][tid]) + (part[2][tid] + part[3][tid]));
 }
 
 // ---------------------------------------------------------------------------
@@ -662,11 +756,9 @@ extern "C" MTT_B200_API int mtt_b200_launch_main_decoder_step(const mtt_b200_mai
 
   const int M = 2 * st.n;
   const unsigned ln_grid = static_cast<unsigned>((M + kLnThreads / 32 - 1) / (kLnThreads / 32));
-  const size_t sa_smem = static_cast<size_t>(st.cap) * sizeof(float);
-  if (sa_smem > 48 * 1024 &&
-      cudaFuncSetAttribute(self_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           static_cast<int>(sa_smem)) != cudaSuccess) {
-    return MTT_B200_STATUS_INVALID_ARGUMENT;
+  if (cudaFuncSetAttribute(self_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           static_cast<int>(kSASmem)) != cudaSuccess) {
+    return MTT_B200_STATUS_CUDA_ERROR;
   }
   auto layer_w = [](const bf16* base, size_t per_layer, int l) { return base + per_layer * l; };
   add_ln_kernel<true><<<ln_grid, kLnThreads, 0, cs>>>(st, st.ln_self, st.ln);
@@ -674,7 +766,7 @@ extern "C" MTT_B200_API int mtt_b200_launch_main_decoder_step(const mtt_b200_mai
   for (int l = 0; l < st.L; ++l) {
     bool ok = gemm(lt, st.ln, layer_w(st.qkv_w, static_cast<size_t>(kQKV) * kW, l), st.qkv, M, kQKV, kW, gws,
                    kGemmWorkspace, cs);
-    self_attn_kernel<<<dim3(kMH, 2, st.n), kSAThreads, sa_smem, cs>>>(st, l);
+    self_attn_kernel<<<dim3(kMH, 2, st.n), kSAThreads, kSASmem, cs>>>(st, l);
     ok = ok && gemm(lt, st.att, layer_w(st.o_w, static_cast<size_t>(kW) * kW, l), st.o, M, kW, kW, gws,
                     kGemmWorkspace, cs);
     add_ln_kernel<false><<<ln_grid, kLnThreads, 0, cs>>>(st, layer_w(st.ln_xq, kW, l), st.ln);
