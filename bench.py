@@ -22,7 +22,9 @@ Also at N=1: the alignment gate (the controller step plus the Local AR's
 EOS inputs, once per decoder step) for the config-4 sessions of one GPU, with
 the reference's own host controller timed beside it; and the Main Decoder
 step for config 5's 256 sessions per GPU (``main_decoder_step``), with the
-CPU restatement timed beside it.
+CPU restatement timed beside it; and config 5's full per-frame loop
+(``config5_loop``: decoder step -> alignment gate -> Local AR frame for 256
+sessions x 1024 frames, all on the device).
 
 A "frame" is one session's 16-position Local AR step (one decoder hidden in,
 16 codec tokens = 2 codec frames x 8 codebooks out).
@@ -79,6 +81,9 @@ def parse():
                     help="run only the Main Decoder step measurement and print its object (profiling)")
     ap.add_argument("--md-sessions", type=int, default=256, help="Main Decoder sessions per GPU (config 5: 256)")
     ap.add_argument("--md-steps", type=int, default=20)
+    ap.add_argument("--no-loop", action="store_true", help="skip the config-5 loop measurement")
+    ap.add_argument("--loop-only", action="store_true", help="run only the config-5 loop and print its object")
+    ap.add_argument("--loop-steps", type=int, default=1024)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     return ap.parse_args()
 
@@ -571,6 +576,86 @@ def main_decoder_measure(dev, peaks, n=256, steps=20, text=128, cap=467, seed=13
     return out
 
 
+def loop_measure(dev, peaks, n=256, steps=1024, text=128, seed=17):
+    """Config 5: the full per-frame loop on the device for n sessions x CFG
+    pair per GPU, `steps` frames each.  One frame = Main Decoder step (cache
+    growing from position 0 to steps - 1, capacity = steps; 128 text states
+    ~N(0, 1)) -> alignment gate -> Local AR frame (16 positions, sampling,
+    EOS); the decoder's hidden state, the frame's embedding sum, the
+    alignment scores and the prior are shared buffers, so nothing crosses to
+    the host inside the timed loop.  Random-init weights (decoder ~N(0, 0.02),
+    Local AR as config 4).  Timed by CUDA events around the whole loop after a
+    3-frame warm-up (state reset afterwards)."""
+    from magpie_tts_rt_b200.local_ar import AlignmentBatch, LocalArEngine, StreamBatch
+    from magpie_tts_rt_b200.main_decoder import MainDecoderBatch, MainDecoderEngine, make_main_decoder_weights
+    cap = steps
+    wd = make_main_decoder_weights(seed, positions=cap)
+    dec = MainDecoderEngine(wd, max_sessions=n, token_stride=text, device=dev)
+    wl = make_weights(SHAPE_BASELINE, seed=0, dtype=torch.bfloat16, profile="baseline", with_final=True)
+    lar = LocalArEngine(wl, max_streams=n, device=dev)
+    db = MainDecoderBatch.allocate(n, cap=cap, token_stride=text, device=dev)
+    g = torch.Generator(device=dev).manual_seed(seed)
+    db.cross_k.normal_(generator=g)
+    db.cross_v.normal_(generator=g)
+    db.text_length.fill_(text)
+    db.cond_mask.fill_(True)
+    db.cond_mask[:, 1, 1:] = False
+    gate = AlignmentBatch.allocate([text] * n, token_stride=text, device=dev)
+    fb = StreamBatch.allocate(n, device=dev)
+    fb.rng_seed.copy_(torch.arange(n, device=dev))
+    fb.decoder_hidden = db.hidden
+    fb.next_embedding = db.embedded
+    gate.alignment_scores = db.alignment
+    gate.next_prior = db.prior
+
+    def reset():
+        db.position.zero_()
+        db.self_mask.zero_()
+        db.embedded.normal_(0, 0.05, generator=g)
+        db.prior.fill_(1.0)
+        gate.counters.zero_()
+        gate.last_attended.fill_(1)
+        gate.decoder_steps.zero_()
+        fb.finished.zero_()
+        fb.end_frame_index.fill_(-1)
+        fb.rng_counter.zero_()
+
+    stream = torch.cuda.Stream(dev)
+    with torch.cuda.stream(stream):
+        reset()
+        for _ in range(3):
+            dec.step(db, stream=stream)
+            gate.gate(fb, stream=stream)
+            lar.frame(fb, stream=stream)
+            db.position += 1
+        reset()
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for _ in range(steps):
+            dec.step(db, stream=stream)
+            gate.gate(fb, stream=stream)
+            lar.frame(fb, stream=stream)
+            db.position += 1
+        e1.record(stream)
+    torch.cuda.synchronize(dev)
+    ms = e0.elapsed_time(e1)
+    bad = int((db.status != 0).sum().item()) + int((gate.invalid_state != 0).sum().item()) + \
+        int((fb.invalid_rows != 0).sum().item())
+    finished = int(fb.finished.sum().item())
+    launches = steps * (145 + 1 + lar.launch_count(n) + 1)
+    out = {"workload": f"config 5 per GPU: {n} sessions x CFG pair, {steps} frames, decoder cache growing to "
+                       f"{steps}, {text} text states; frame = Main Decoder step -> alignment gate -> Local AR "
+                       f"frame, all on the device",
+           "frames_per_s": n * steps / (ms * 1e-3), "ms_per_frame_step": ms / steps, "total_s": ms * 1e-3,
+           "gpu_launches": launches, "local_ar_path": PATH_NAMES.get(lar.path_for(n), str(lar.path_for(n))),
+           "sessions_finished": finished, "invalid": bad}
+    del db, gate, fb, dec, lar
+    torch.cuda.empty_cache()
+    return out
+
+
 # ---------------------------------------------------------------------------
 # CPU baseline (oracle restatement of the reference's path)
 # ---------------------------------------------------------------------------
@@ -621,6 +706,11 @@ def main():
     args = parse()
     world, rank, local = dist_init()
     peaks, peaks_kind = load_peaks()
+    if args.loop_only:
+        out = loop_measure(torch.device("cuda", local), peaks, steps=args.loop_steps)
+        if rank == 0:
+            print(json.dumps({"config5_loop": out}), flush=True)
+        return
     if args.main_decoder_only:
         out = main_decoder_measure(torch.device("cuda", local), peaks, n=args.md_sessions, steps=args.md_steps,
                                    with_cpu=False)
@@ -666,6 +756,9 @@ def main():
     if world == 1 and not args.no_latency:
         md = main_decoder_measure(torch.device("cuda", local), peaks, n=args.md_sessions, steps=args.md_steps,
                                   with_cpu=rank == 0 and not args.no_cpu_baseline)
+    loop = None
+    if world == 1 and not args.no_latency and not args.no_loop:
+        loop = loop_measure(torch.device("cuda", local), peaks, steps=args.loop_steps)
     cpu = None
     if world == 1 and rank == 0 and not args.no_cpu_baseline:
         cpu = cpu_oracle_sample()
@@ -710,6 +803,7 @@ def main():
                 "gpu_launches": res["launches"], "frame_path": res["path"], "clocks": res["clocks"],
                 "roofline": roof,
                 "latency_config2": latency, "alignment_gate": align, "main_decoder_step": md,
+                "config5_loop": loop,
                 "cpu_baseline": cpu,
                 "checks": {"invalid_rows": res["invalid"], "forced_eos_ok": res["forced_ok"]}}
         print(json.dumps(line), flush=True)
