@@ -550,7 +550,9 @@ typedef struct mtt_b200_main_decoder_batch {
   const void* prior;           /* [n][2][S] bf16 attention prior (the alignment gate's next_prior) */
   void* hidden;                /* [n][2][768] bf16 out: the Local AR frame's decoder_hidden */
   void* alignment;             /* [n][2][S] bf16 out: the alignment gate's scores */
-  int32_t* status;             /* [n] out: 0, or 1 for a position or text length out of range */
+  int32_t* status;             /* [n] out: 0; 1 for a position or text length out of range
+                                  (nothing written for the session); 2 when a cache copy did
+                                  not complete within its bounded wait (outputs unreliable) */
 } mtt_b200_main_decoder_batch_t;
 
 /* Workspace bytes for up to max_sessions sessions (0 for bad arguments). */
