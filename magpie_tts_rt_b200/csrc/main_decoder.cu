@@ -125,6 +125,9 @@ __global__ void __launch_bounds__(kLnThreads) add_ln_kernel(Step st, const bf16*
   if (!session_live(st, s)) return;
   float v[24];
   bf16* xr = st.x + static_cast<size_t>(row) * kW;
+  uint4 wq[3];  // the LayerNorm weights, loaded with the inputs (no dependent load later)
+#pragma unroll
+  for (int c = 0; c < 3; ++c) wq[c] = *reinterpret_cast<const uint4*>(w + 8 * (lane + 32 * c));
 #pragma unroll
   for (int c = 0; c < 3; ++c) {
     const int col = 8 * (lane + 32 * c);
@@ -163,7 +166,7 @@ __global__ void __launch_bounds__(kLnThreads) add_ln_kernel(Step st, const bf16*
   for (int c = 0; c < 3; ++c) {
     const int col = 8 * (lane + 32 * c);
     float g[8], y[8];
-    unpack8f(*reinterpret_cast<const uint4*>(w + col), g);
+    unpack8f(wq[c], g);
 #pragma unroll
     for (int e = 0; e < 8; ++e) y[e] = (v[8 * c + e] - mean) * rstd * g[e];
     *reinterpret_cast<uint4*>(out + static_cast<size_t>(row) * kW + col) = pack8f(y);
