@@ -72,7 +72,8 @@ def parse():
     ap.add_argument("--steps", type=int, default=3)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="config4", choices=list(WORKLOADS))
+    ap.add_argument("--workload", default="config4", choices=list(WORKLOADS) + ["config5"],
+                    help="config5: the full per-frame loop, 256 sessions per GPU on every rank (weak scaling)")
     ap.add_argument("--frames", type=int, default=None, help="override frames per step (profiling)")
     ap.add_argument("--sessions", type=int, default=None,
                     help="override sessions per GPU (profiling a smaller per-GPU batch, e.g. 256 = config 4 at 4 GPUs)")
@@ -710,6 +711,24 @@ def main():
         out = loop_measure(torch.device("cuda", local), peaks, steps=args.loop_steps)
         if rank == 0:
             print(json.dumps({"config5_loop": out}), flush=True)
+        return
+    if args.workload == "config5":
+        # every rank runs its own 256 sessions (no data-path collective); the
+        # box value is all ranks' frames over the slowest rank's loop time
+        barrier(world)
+        out = loop_measure(torch.device("cuda", local), peaks, steps=args.loop_steps)
+        t = max_over_ranks(out["total_s"], world)
+        frames = sum_over_ranks(256.0 * args.loop_steps, world)
+        bad = sum_over_ranks(float(out["invalid"]), world)
+        if rank == 0:
+            print(json.dumps({"metric": "config 5 full per-frame loop frames/sec (box)", "value": frames / t,
+                              "unit": "frames/s", "n_gpus": world, "higher_is_better": True, "scaling": "weak",
+                              "per_gpu_frames_per_s": frames / t / world, "max_rank_s": t,
+                              "rank0": out, "invalid": bad, "vs_baseline": None, "dtype": "bf16",
+                              "data": "synthetic"}), flush=True)
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
         return
     if args.main_decoder_only:
         out = main_decoder_measure(torch.device("cuda", local), peaks, n=args.md_sessions, steps=args.md_steps,
