@@ -363,6 +363,11 @@ typedef struct mtt_b200_stream_batch {
                                    (0, 2, 4, 6 for the aggregate); even, offset + 2 <= stride */
   bool* finished_latch;         /* [n] or NULL: set to true where end_frame_index is 0 or 1
                                    (may alias `finished`; it is written after the frame read it) */
+  int32_t* codec_frames;        /* [n] or NULL: for sessions not finished on entry, the audio
+                                   frames of the aggregate so far -- offset + 2, or offset +
+                                   end_frame_index at the EOS frame (the EOS frame is not audio;
+                                   src/runtime/eos_contract.hpp:14-30): the F of the NanoCodec
+                                   [1][8][F] route after the emission batch's last frame */
 } mtt_b200_stream_batch_t;
 
 /* Device workspace bytes for launching up to max_streams streams. */

@@ -116,6 +116,7 @@ class StreamBatch(ctypes.Structure):
         ("invalid_rows", P), ("end_frame_index", P), ("next_embedding", P),
         ("forced_tokens", P), ("logits_out", P),
         ("codec_frames_stride", I32), ("codec_frame_offset", I32), ("finished_latch", P),
+        ("codec_frames", P),
     ]
 
 

@@ -623,6 +623,7 @@ extern "C" MTT_B200_API int mtt_b200_launch_local_ar_frame(const mtt_b200_local_
   f.codec_stride = b->codec_frames_stride == 0 ? kFrames : b->codec_frames_stride;
   f.codec_offset = b->codec_frame_offset;
   f.finished_latch = b->finished_latch;
+  f.codec_frames = b->codec_frames;
   f.invalid_rows = b->invalid_rows;
   f.end_frame = b->end_frame_index;
   f.next_emb = static_cast<bf16*>(b->next_embedding);

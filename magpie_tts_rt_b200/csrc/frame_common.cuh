@@ -25,6 +25,7 @@ struct Frame {
   int64_t* codec_tokens;
   int codec_stride, codec_offset;  // frames per codebook row of codec_tokens, first frame written
   bool* finished_latch;            // optional: set where the frame's EOS decision ends the utterance
+  int32_t* codec_frames;           // optional: audio frames in the emission aggregate (see commit_end)
   int32_t* invalid_rows;
   int32_t* end_frame;
   bf16* next_emb;
@@ -50,9 +51,14 @@ __device__ __forceinline__ int64_t codec_index(const Frame& f, int s, int p) {
 
 // end_frame_index of session s, and the finished latch of
 // finalize_local_step (synthesis_kernels.cu:79-84) when the caller asked for it.
+// With codec_frames, also the session's count of audio frames in the
+// aggregate (eos_contract.hpp:14-30, retained_codec_frames_before_eos: the
+// EOS frame itself is not audio): offset + 2 after a frame without EOS,
+// offset + end at the EOS frame, unchanged for a session already finished.
 __device__ __forceinline__ void commit_end(const Frame& f, int s, int32_t end) {
   f.end_frame[s] = end;
   if (f.finished_latch != nullptr && (end == 0 || end == 1)) f.finished_latch[s] = true;
+  if (f.codec_frames != nullptr && !f.finished[s]) f.codec_frames[s] = f.codec_offset + (end >= 0 ? end : kFrames);
 }
 
 struct Layout {

@@ -132,6 +132,7 @@ class StreamBatch:
     # [n, 8, 8] emission aggregate (stride 8, this frame at codec_frame_offset)
     codec_frame_offset: int = 0
     finished_latch: Optional[torch.Tensor] = None  # [n] bool, may be `finished`
+    codec_frames: Optional[torch.Tensor] = None  # [n] int32: audio frames in the aggregate so far
 
     @property
     def n(self) -> int:
@@ -163,6 +164,7 @@ class StreamBatch:
         b.codec_frames_stride = int(self.codec_tokens.shape[2])
         b.codec_frame_offset = self.codec_frame_offset
         b.finished_latch = self.finished_latch.data_ptr() if self.finished_latch is not None else None
+        b.codec_frames = self.codec_frames.data_ptr() if self.codec_frames is not None else None
         return b
 
 

@@ -255,7 +255,8 @@ def test_frames_fill_the_emission_aggregate(path):
     (synthesis_kernels.cu:53-86): four frames write their [8][2] tokens
     straight into the [n][8][8] emission aggregate at frame offsets 0, 2, 4, 6
     (the same tokens, counters and EOS as the [n][8][2] layout), and
-    finished_latch is set exactly where end_frame_index is 0 or 1.  The EOS
+    finished_latch is set exactly where end_frame_index is 0 or 1, and
+    codec_frames counts the aggregate's audio frames.  The EOS
     bias is raised so that every session with EOS enabled ends at frame 0."""
     from magpie_tts_rt_b200 import _lib as L
     from magpie_tts_rt_b200.local_ar import LocalArEngine, StreamBatch
@@ -270,6 +271,7 @@ def test_frames_fill_the_emission_aggregate(path):
     agg, ref = StreamBatch.allocate(n), StreamBatch.allocate(n)
     agg.codec_tokens = torch.full((n, 8, 8), -7, dtype=torch.int64, device="cuda")
     agg.finished_latch = torch.zeros(n, dtype=torch.bool, device="cuda")
+    agg.codec_frames = torch.full((n,), -1, dtype=torch.int32, device="cuda")
     for b in (agg, ref):
         b.unfinished.copy_(uf); b.finished.copy_(fi); b.forbid_eos.copy_(fb)
         b.rng_seed.copy_(torch.arange(n) + 3)
@@ -290,6 +292,10 @@ def test_frames_fill_the_emission_aggregate(path):
         assert (end[enabled] == 0).all() and (end[fi.numpy()] == 0).all() and (end[(uf | fb).numpy() & ~fi.numpy()] == -1).all()
         latch |= (end == 0) | (end == 1)
         np.testing.assert_array_equal(agg.finished_latch.cpu().numpy(), latch)
+        # audio frames of the aggregate (eos_contract.hpp:14-30): offset + 2, or offset + end at the
+        # EOS frame, for sessions not finished on entry (those keep their count: -1 here)
+        exp_frames = np.where(fi.numpy(), -1, np.where(end >= 0, off + end, off + 2))
+        np.testing.assert_array_equal(agg.codec_frames.cpu().numpy(), exp_frames)
     # argument checks: stride below 2, odd offset, offset past the row
     for stride, off in ((1, 0), (8, 3), (8, 8), (2, 2), (-2, 0)):
         cb = agg.c_struct()
