@@ -55,6 +55,13 @@ constexpr int kLnThreads = 128;  // 4 rows per CTA, one warp per row
 
 __device__ __forceinline__ float bfr(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
 
+// Every kernel of the step is launched with programmatic stream serialization
+// (launch_after below): its CTAs may be scheduled while the previous launch on
+// the stream (a library GEMM, say) is still finishing, and they wait here, before
+// the first global memory access, until that launch has completed and its
+// writes are visible.  Launched without the attribute this is a no-op.
+__device__ __forceinline__ void wait_prior_grid() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 __device__ __forceinline__ void unpack8f(const uint4& u, float (&f)[8]) {
   const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
 #pragma unroll
@@ -117,6 +124,7 @@ __device__ __forceinline__ bool session_live(const Step& st, int s) {
 // ---------------------------------------------------------------------------
 template <bool kEmbed>
 __global__ void __launch_bounds__(kLnThreads) add_ln_kernel(Step st, const bf16* __restrict__ w, bf16* out) {
+  wait_prior_grid();
   const int lane = threadIdx.x & 31;
   const int row = blockIdx.x * (kLnThreads / 32) + (threadIdx.x >> 5);
   if (row >= 2 * st.n) return;
@@ -249,6 +257,7 @@ __global__ void __launch_bounds__(kSAThreads) self_attn_kernel(Step st, int l) {
   __shared__ float gm[kSAGroups], gl[kSAGroups];
   __shared__ float gacc[kSAGroups][kMD];
   __shared__ int err, issued;
+  wait_prior_grid();
   const int h = blockIdx.x, r = blockIdx.y, s = blockIdx.z;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int row = 2 * s + r;
@@ -419,6 +428,7 @@ __global__ void __launch_bounds__(kXAThreads) cross_attn_kernel(Step st, int l, 
   __shared__ float qs[kXD];
   __shared__ float part[kXAThreads / 32][kXD];
   __shared__ float red[kXAThreads / 32];
+  wait_prior_grid();
   const int r = blockIdx.x, s = blockIdx.y;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int row = 2 * s + r;
@@ -561,6 +571,7 @@ __global__ void __launch_bounds__(kXAThreads) cross_attn_kernel(Step st, int l, 
 
 // GELU-tanh in place, bf16 (text_encoder_wrapper.py:61-70: F.gelu(approximate="tanh")).
 __global__ void gelu_kernel(bf16* h, size_t count8) {
+  wait_prior_grid();
   const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (i >= count8) return;
   float f[8];
@@ -678,6 +689,25 @@ MdLayout md_layout(int n, int S) {
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// Launches one of this file's kernels with programmatic stream serialization:
+// the launch may begin while the previous one on the stream drains, and the
+// kernel's wait_prior_grid() orders its memory accesses after it.
+template <typename... KArgs, typename... Args>
+bool launch_after(void (*kernel)(KArgs...), dim3 grid, unsigned block, size_t smem, cudaStream_t stream,
+                  Args... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(block, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...) == cudaSuccess;
+}
+
 }  // namespace
 }  // namespace mtt
 
@@ -765,33 +795,38 @@ extern "C" MTT_B200_API int mtt_b200_launch_main_decoder_step(const mtt_b200_mai
     return MTT_B200_STATUS_CUDA_ERROR;
   }
   auto layer_w = [](const bf16* base, size_t per_layer, int l) { return base + per_layer * l; };
-  add_ln_kernel<true><<<ln_grid, kLnThreads, 0, cs>>>(st, st.ln_self, st.ln);
+  if (!launch_after(add_ln_kernel<true>, dim3(ln_grid), kLnThreads, 0, cs, st, st.ln_self, st.ln)) {
+    return MTT_B200_STATUS_CUDA_ERROR;
+  }
   int slot = 0;
   for (int l = 0; l < st.L; ++l) {
     bool ok = gemm(lt, st.ln, layer_w(st.qkv_w, static_cast<size_t>(kQKV) * kW, l), st.qkv, M, kQKV, kW, gws,
                    kGemmWorkspace, cs);
-    self_attn_kernel<<<dim3(kMH, 2, st.n), kSAThreads, kSASmem, cs>>>(st, l);
+    ok = ok && launch_after(self_attn_kernel, dim3(kMH, 2, st.n), kSAThreads, kSASmem, cs, st, l);
     ok = ok && gemm(lt, st.att, layer_w(st.o_w, static_cast<size_t>(kW) * kW, l), st.o, M, kW, kW, gws,
                     kGemmWorkspace, cs);
-    add_ln_kernel<false><<<ln_grid, kLnThreads, 0, cs>>>(st, layer_w(st.ln_xq, kW, l), st.ln);
+    ok = ok && launch_after(add_ln_kernel<false>, dim3(ln_grid), kLnThreads, 0, cs, st, layer_w(st.ln_xq, kW, l),
+                            st.ln);
     ok = ok && gemm(lt, st.ln, layer_w(st.xq_w, static_cast<size_t>(kXD) * kW, l), st.xq, M, kXD, kW, gws,
                     kGemmWorkspace, cs);
     const bool prior_layer = l >= 2 && l <= 10;
     const bool align_layer = l == 4 || l == 5 || l == 8 || l == 9;
-    cross_attn_kernel<<<dim3(2, st.n), kXAThreads, 0, cs>>>(st, l, prior_layer ? 1 : 0, align_layer ? slot : -1);
+    ok = ok && launch_after(cross_attn_kernel, dim3(2, st.n), kXAThreads, 0, cs, st, l, prior_layer ? 1 : 0,
+                            align_layer ? slot : -1);
     if (align_layer) ++slot;
     ok = ok && gemm(lt, st.ctx, layer_w(st.xo_w, static_cast<size_t>(kW) * kXD, l), st.o, M, kW, kXD, gws,
                     kGemmWorkspace, cs);
-    add_ln_kernel<false><<<ln_grid, kLnThreads, 0, cs>>>(st, layer_w(st.ln_ff, kW, l), st.ln);
+    ok = ok && launch_after(add_ln_kernel<false>, dim3(ln_grid), kLnThreads, 0, cs, st, layer_w(st.ln_ff, kW, l),
+                            st.ln);
     ok = ok && gemm(lt, st.ln, layer_w(st.ffn1_w, static_cast<size_t>(kFF) * kW, l), st.h, M, kFF, kW, gws,
                     kGemmWorkspace, cs);
     const size_t count8 = static_cast<size_t>(M) * kFF / 8;
-    gelu_kernel<<<static_cast<unsigned>((count8 + 255) / 256), 256, 0, cs>>>(st.h, count8);
+    ok = ok && launch_after(gelu_kernel, dim3(static_cast<unsigned>((count8 + 255) / 256)), 256, 0, cs, st.h, count8);
     ok = ok && gemm(lt, st.h, layer_w(st.ffn2_w, static_cast<size_t>(kW) * kFF, l), st.o, M, kW, kFF, gws,
                     kGemmWorkspace, cs);
     const bool last = l + 1 == st.L;
-    add_ln_kernel<false><<<ln_grid, kLnThreads, 0, cs>>>(st, last ? st.norm_out : layer_w(st.ln_self, kW, l + 1),
-                                                         last ? st.hidden : st.ln);
+    ok = ok && launch_after(add_ln_kernel<false>, dim3(ln_grid), kLnThreads, 0, cs, st,
+                            last ? st.norm_out : layer_w(st.ln_self, kW, l + 1), last ? st.hidden : st.ln);
     if (!ok) return MTT_B200_STATUS_CUDA_ERROR;
   }
   return cudaPeekAtLastError() == cudaSuccess ? MTT_B200_STATUS_OK : MTT_B200_STATUS_CUDA_ERROR;
