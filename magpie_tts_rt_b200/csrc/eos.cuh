@@ -45,6 +45,7 @@ struct EosArgs {
 __global__ void __launch_bounds__(kEosThreads) eos_project_kernel(EosArgs a) {
   __shared__ __align__(16) float hs[2][kEmbed];
   __shared__ float warp_max[kEosThreads / 32];
+  wait_prior_grid();  // launched after the frame kernel with programmatic serialization
   const int chunk = blockIdx.x;
   const int p = blockIdx.y;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;

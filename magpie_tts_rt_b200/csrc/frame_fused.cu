@@ -694,6 +694,7 @@ __global__ void __cluster_dims__(kCS, 1, 1) __launch_bounds__(kThreads, 1)
 
 // EOS decision for the sessions the fused kernel registered; resets the count.
 __global__ void __launch_bounds__(256) fused_eos_finish_kernel(Frame f) {
+  wait_prior_grid();  // launched after eos_project_kernel with programmatic serialization
   const int count = *f.eos_count;
   for (int e = threadIdx.x; e < count; e += blockDim.x) {
     const int s = f.eos_list[e];
@@ -799,8 +800,12 @@ cudaError_t launch_frame_eos(const Frame& f, cudaStream_t stream) {
   ea.eos_count = f.eos_count;
   ea.partial_max = f.eos_partial;
   ea.eos_logit = f.eos_logit;
-  eos_project_kernel<<<dim3(kEosChunks, kPositions), kEosThreads, 0, stream>>>(ea);
-  fused_eos_finish_kernel<<<1, 256, 0, stream>>>(f);
+  // each launch may start while the one before it drains (wait_prior_grid)
+  cudaError_t e = launch_serialized(eos_project_kernel, dim3(kEosChunks, kPositions), dim3(kEosThreads), 0, stream,
+                                    ea);
+  if (e != cudaSuccess) return e;
+  e = launch_serialized(fused_eos_finish_kernel, dim3(1), dim3(256), 0, stream, f);
+  if (e != cudaSuccess) return e;
   return cudaPeekAtLastError();
 }
 

@@ -55,13 +55,6 @@ constexpr int kLnThreads = 128;  // 4 rows per CTA, one warp per row
 
 __device__ __forceinline__ float bfr(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
 
-// Every kernel of the step is launched with programmatic stream serialization
-// (launch_after below): its CTAs may be scheduled while the previous launch on
-// the stream (a library GEMM, say) is still finishing, and they wait here, before
-// the first global memory access, until that launch has completed and its
-// writes are visible.  Launched without the attribute this is a no-op.
-__device__ __forceinline__ void wait_prior_grid() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
-
 __device__ __forceinline__ void unpack8f(const uint4& u, float (&f)[8]) {
   const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
 #pragma unroll
@@ -689,23 +682,14 @@ MdLayout md_layout(int n, int S) {
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-// Launches one of this file's kernels with programmatic stream serialization:
-// the launch may begin while the previous one on the stream drains, and the
-// kernel's wait_prior_grid() orders its memory accesses after it.
+// Every kernel of the step is launched with programmatic stream serialization
+// (common.cuh): its CTAs may be scheduled while the previous launch on the
+// stream (a library GEMM, say) drains, and each kernel calls wait_prior_grid()
+// before its first global memory access.
 template <typename... KArgs, typename... Args>
 bool launch_after(void (*kernel)(KArgs...), dim3 grid, unsigned block, size_t smem, cudaStream_t stream,
                   Args... args) {
-  cudaLaunchConfig_t cfg{};
-  cfg.gridDim = grid;
-  cfg.blockDim = dim3(block, 1, 1);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...) == cudaSuccess;
+  return launch_serialized(kernel, grid, dim3(block, 1, 1), smem, stream, args...) == cudaSuccess;
 }
 
 }  // namespace
