@@ -578,7 +578,7 @@ def main_decoder_measure(dev, peaks, n=256, steps=20, text=128, cap=467, seed=13
     return out
 
 
-def loop_measure(dev, peaks, n=256, steps=1024, text=128, seed=17):
+def loop_measure(dev, peaks, n=256, steps=1024, text=128, seed=17, graph=True):
     """Config 5: the full per-frame loop on the device for n sessions x CFG
     pair per GPU, `steps` frames each.  One frame = Main Decoder step (cache
     growing from position 0 to steps - 1, capacity = steps; 128 text states
@@ -587,7 +587,11 @@ def loop_measure(dev, peaks, n=256, steps=1024, text=128, seed=17):
     alignment scores and the prior are shared buffers, so nothing crosses to
     the host inside the timed loop.  Random-init weights (decoder ~N(0, 0.02),
     Local AR as config 4).  Timed by CUDA events around the whole loop after a
-    3-frame warm-up (state reset afterwards)."""
+    3-frame warm-up (state reset afterwards).  With ``graph`` one frame step
+    (decoder step, gate, frame, position advance) is captured once as a CUDA
+    graph after the warm-up and replayed per frame, as a serving loop would run
+    it; the decoder and frame state advance on the device, so every replay is
+    the next frame."""
     from magpie_tts_rt_b200.local_ar import AlignmentBatch, LocalArEngine, StreamBatch
     from magpie_tts_rt_b200.main_decoder import MainDecoderBatch, MainDecoderEngine, make_main_decoder_weights
     cap = steps
@@ -622,24 +626,34 @@ def loop_measure(dev, peaks, n=256, steps=1024, text=128, seed=17):
         fb.end_frame_index.fill_(-1)
         fb.rng_counter.zero_()
 
+    def frame_step():
+        dec.step(db, stream=stream)
+        gate.gate(fb, stream=stream)
+        lar.frame(fb, stream=stream)
+        db.position += 1
+
     stream = torch.cuda.Stream(dev)
     with torch.cuda.stream(stream):
         reset()
         for _ in range(3):
-            dec.step(db, stream=stream)
-            gate.gate(fb, stream=stream)
-            lar.frame(fb, stream=stream)
-            db.position += 1
+            frame_step()
         reset()
     torch.cuda.synchronize(dev)
+    cuda_graph = None
+    if graph:
+        # the library's one-time set-up (cuBLASLt handle and plans) ran in the warm-up
+        cuda_graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(cuda_graph, stream=stream):
+            frame_step()
+        torch.cuda.synchronize(dev)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with torch.cuda.stream(stream):
         e0.record(stream)
         for _ in range(steps):
-            dec.step(db, stream=stream)
-            gate.gate(fb, stream=stream)
-            lar.frame(fb, stream=stream)
-            db.position += 1
+            if cuda_graph is not None:
+                cuda_graph.replay()
+            else:
+                frame_step()
         e1.record(stream)
     torch.cuda.synchronize(dev)
     ms = e0.elapsed_time(e1)
@@ -651,9 +665,10 @@ def loop_measure(dev, peaks, n=256, steps=1024, text=128, seed=17):
                        f"{steps}, {text} text states; frame = Main Decoder step -> alignment gate -> Local AR "
                        f"frame, all on the device",
            "frames_per_s": n * steps / (ms * 1e-3), "ms_per_frame_step": ms / steps, "total_s": ms * 1e-3,
-           "gpu_launches": launches, "local_ar_path": PATH_NAMES.get(lar.path_for(n), str(lar.path_for(n))),
+           "gpu_launches": launches, "cuda_graph_per_frame": graph,
+           "local_ar_path": PATH_NAMES.get(lar.path_for(n), str(lar.path_for(n))),
            "sessions_finished": finished, "invalid": bad}
-    del db, gate, fb, dec, lar
+    del cuda_graph, db, gate, fb, dec, lar
     torch.cuda.empty_cache()
     return out
 

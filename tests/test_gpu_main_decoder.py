@@ -214,3 +214,69 @@ def test_device_decoder_loop():
         db.position += 1
         torch.cuda.synchronize()
         assert int(fb.invalid_rows.sum()) == 0
+
+
+def _loop_state(seed_base: int):
+    """One decoder-loop pool (4 sessions) with its own engines and shared
+    buffers wired as in test_device_decoder_loop."""
+    from magpie_tts_rt_b200.local_ar import AlignmentBatch, LocalArEngine, StreamBatch
+    from magpie_tts_rt_b200.model import SHAPE_BASELINE, make_weights
+    n, cap, S = 4, 300, 64
+    wd = make_main_decoder_weights(3, positions=cap)
+    wl = make_weights(SHAPE_BASELINE, seed=21, dtype=torch.bfloat16, profile="parity", with_final=True)
+    dec = MainDecoderEngine(wd, max_sessions=n, token_stride=S)
+    lar = LocalArEngine(wl, max_streams=n)
+    db = MainDecoderBatch.allocate(n, cap=cap, token_stride=S)
+    T = [12, 40, 64, 33]
+    for s in range(n):
+        load_session(db, s, OMD.make_step_inputs(seed_base + s, T[s], 220 + s, cap))
+    gate = AlignmentBatch.allocate(T, token_stride=S)
+    fb = StreamBatch.allocate(n)
+    fb.rng_seed.copy_(torch.arange(n))
+    fb.end_frame_index.fill_(-1)
+    fb.decoder_hidden = db.hidden
+    fb.next_embedding = db.embedded
+    gate.alignment_scores = db.alignment
+    gate.next_prior = db.prior
+
+    def frame_step():
+        dec.step(db)
+        gate.gate(fb)
+        lar.frame(fb)
+        db.position += 1
+
+    return frame_step, db, gate, fb
+
+
+def test_decoder_loop_graph_replay_matches_eager():
+    """The per-frame loop captured once as a CUDA graph (decoder step, gate,
+    frame with its EOS kernels, position advance) and replayed, as the bench's
+    config-5 loop runs it, leaves exactly the state that the same launches
+    made one by one leave: cache, hidden state, scores, prior, counters,
+    tokens, end-frame indices."""
+    eager_step, e_db, e_gate, e_fb = _loop_state(200)
+    graph_step, g_db, g_gate, g_fb = _loop_state(200)
+    eager_step()  # also the library's one-time set-up (cuBLASLt handle and plans)
+    graph_step()
+    torch.cuda.synchronize()
+    stream = torch.cuda.Stream()
+    stream.wait_stream(torch.cuda.current_stream())
+    cuda_graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(cuda_graph, stream=stream):
+        graph_step()
+    for _ in range(4):
+        eager_step()
+        cuda_graph.replay()
+    torch.cuda.synchronize()
+    pairs = [(e_db.self_k, g_db.self_k), (e_db.self_v, g_db.self_v), (e_db.self_mask, g_db.self_mask),
+             (e_db.hidden, g_db.hidden), (e_db.embedded, g_db.embedded), (e_db.alignment, g_db.alignment),
+             (e_db.prior, g_db.prior), (e_db.position, g_db.position), (e_db.status, g_db.status),
+             (e_gate.counters, g_gate.counters), (e_gate.last_attended, g_gate.last_attended),
+             (e_gate.decoder_steps, g_gate.decoder_steps), (e_fb.codec_tokens, g_fb.codec_tokens),
+             (e_fb.rng_counter, g_fb.rng_counter), (e_fb.end_frame_index, g_fb.end_frame_index),
+             (e_fb.invalid_rows, g_fb.invalid_rows), (e_fb.finished, g_fb.finished)]
+    for i, (a, b) in enumerate(pairs):
+        assert torch.equal(a, b), f"state {i} differs between graph replay and eager launches"
+    assert int(e_db.position[0]) == 220 + 5
+    assert int(e_fb.invalid_rows.sum()) == 0 and int((e_db.status != 0).sum()) == 0
+    del cuda_graph
