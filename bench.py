@@ -493,7 +493,7 @@ def alignment_gate_measure(dev, peaks, n=1024, stride=512, steps=200, seed=11):
     return out
 
 
-def main_decoder_measure(dev, peaks, n=256, steps=20, text=128, cap=467, seed=13, with_cpu=True):
+def main_decoder_measure(dev, peaks, n=256, steps=20, text=128, cap=467, seed=13, with_cpu=True, graph=True):
     """The Main Decoder step (mtt_b200_launch_main_decoder_step) for config
     5's sessions of one GPU: n sessions x CFG pair, the reference's cache of
     467 positions, 128 text tokens, positions starting U[218, 466 - steps]
@@ -526,19 +526,35 @@ def main_decoder_measure(dev, peaks, n=256, steps=20, text=128, cap=467, seed=13
     idx = torch.arange(cap, device=dev)
     b.self_mask.copy_((idx[None, None, :] < pos0[:, None, None]).expand(n, 2, cap))
     b.position.copy_(pos0)
+    def one_step():
+        eng.step(b, stream=stream)
+        b.position += 1
+
     stream = torch.cuda.Stream(dev)
     with torch.cuda.stream(stream):
         for _ in range(3):
-            eng.step(b, stream=stream)
-            b.position += 1
+            one_step()
+    torch.cuda.synchronize(dev)
+    cuda_graph = None
+    if graph:
+        # one step captured once (the cuBLASLt handle and plans exist after the
+        # warm-up) and replayed; the positions advance on the device
+        cuda_graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(cuda_graph, stream=stream):
+            one_step()
+        torch.cuda.synchronize(dev)
+    with torch.cuda.stream(stream):
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         start_pos = b.position.clone()
         e0.record(stream)
         for _ in range(steps):
-            eng.step(b, stream=stream)
-            b.position += 1
+            if cuda_graph is not None:
+                cuda_graph.replay()
+            else:
+                one_step()
         e1.record(stream)
     torch.cuda.synchronize(dev)
+    del cuda_graph
     us = e0.elapsed_time(e1) * 1000.0 / steps
     bad = int((b.status != 0).sum().item())
     active = (start_pos.double() + 1).cpu().numpy()  # keys read per row and head at the first timed step
@@ -555,6 +571,7 @@ def main_decoder_measure(dev, peaks, n=256, steps=20, text=128, cap=467, seed=13
            "kernels": "per layer: 6 cuBLASLt GEMMs + self_attn_kernel + cross_attn_kernel + 3 add_ln_kernel + "
                       "gelu_kernel",
            "gpu_launches_per_step": 1 + LAYERS * 12,
+           "cuda_graph_per_step": graph,
            "roofline": {"bound": "hbm", "algorithmic_bytes_per_step": bytes_, "achieved": gbs, "unit": "GB/s",
                         "peak": peaks["hbm_gbs"], "frac": gbs / peaks["hbm_gbs"],
                         "algorithmic_flops_per_step": flops,
