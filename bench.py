@@ -838,10 +838,12 @@ def main():
                           " (per frame call, with the EOS projection/decision kernels: 0.6% of device time)",
                 "achieved": tf, "peak": tensor_peak, "unit": "TFLOP/s", "frac": tf / tensor_peak,
                 "peak_kind": f"{peaks_kind} sustained bf16",
-                # dram__bytes_read.sum + dram__bytes_write.sum of one frame-kernel launch from the
-                # ncu captures (profiles/pair_frame_kernel_config4.md and tile_frame_kernel_config4.md
-                # at 1024 sessions, profiles/split_frame_kernel_x4_256sessions.md at 256 sessions)
+                # dram__bytes_read.sum + dram__bytes_write.sum of one frame-kernel launch, taken
+                # from an ncu capture of the same kernel at the same sessions per GPU (L2 flushed
+                # by ncu before the pass); null for a (kernel, batch) with no capture
                 "traffic": TRAFFIC.get((res["path"], res["n_local"])),
+                "traffic_source": ("ncu capture of this kernel at this batch (not measured in this run)"
+                                   if (res["path"], res["n_local"]) in TRAFFIC else None),
                 "avg_frame_call_us": t_frame * 1e6,
                 "hbm_achieved_gbs": gbs, "hbm_frac": gbs / peaks["hbm_gbs"],
                 "algorithmic_flops_per_frame_step": flops, "algorithmic_bytes_per_frame_step": bytes_}

@@ -393,17 +393,20 @@ MTT_B200_API int mtt_b200_launch_local_ar_frame(const mtt_b200_local_ar_shape_t*
  * in the reference).  For callers that cannot call cudaMalloc where frames
  * run: a TensorRT plugin's enqueue(), code being captured into a CUDA graph,
  * a real-time synthesis thread that must not stall on an allocation.  The
- * scratch memory is a 2 MiB device array inside this library (held by every
- * GPU that loads it, until exit) instead of a caller workspace: enough for the
- * benchmark shape (d=256, 1 layer, FFN 1024) with up to 32 sessions x CFG, or
- * the d=768 2-layer shape with up to 8.  A batch whose
- * mtt_b200_local_ar_frame_workspace_size exceeds 2 MiB is rejected with
+ * scratch memory is a device array of MTT_B200_STATIC_FRAME_WORKSPACE_BYTES
+ * (2 MiB) inside this library (held by every GPU that loads it, until exit)
+ * instead of a caller workspace.  A batch fits when
+ * mtt_b200_local_ar_frame_workspace_size(shape, n_streams, cfg) is at most
+ * that size: with CFG up to 40 sessions of the benchmark shape (d=256,
+ * 1 layer, FFN 1024) or 9 of the d=768 2-layer shape (74 and 17 without
+ * CFG).  A larger batch is rejected with
  * MTT_B200_STATUS_STATIC_WORKSPACE_TOO_SMALL and nothing is launched.  The
  * first call on a device (that device current) resolves the array's device
  * address; make it before any stream capture.  All calls share the array:
  * calls whose kernels overlap on the GPU race.  Other arguments and results
  * are those of mtt_b200_launch_local_ar_frame.
  */
+#define MTT_B200_STATIC_FRAME_WORKSPACE_BYTES ((size_t)2 << 20)
 #define MTT_B200_STATUS_STATIC_WORKSPACE_TOO_SMALL -4
 MTT_B200_API int mtt_b200_launch_local_ar_frame_static_workspace(const mtt_b200_local_ar_shape_t* shape,
                                                                 const mtt_b200_local_ar_weights_t* weights,

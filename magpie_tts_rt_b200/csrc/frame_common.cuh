@@ -5,6 +5,8 @@
 #include <cuda.h>
 
 #include <cstddef>
+#include <map>
+#include <mutex>
 
 #include "common.cuh"
 #include "eos.cuh"
@@ -99,6 +101,34 @@ inline Layout make_layout(int d, int L, int F, int n, int rp) {
   return lo;
 }
 
+
+// One int per device ordinal, computed by `make` the first time it is asked
+// for with that device current.  A kernel's dynamic shared-memory opt-in
+// (cudaFuncSetAttribute) is a setting of the current device's context and
+// its occupancy a property of that device, so a process that runs frames on
+// several GPUs must make the setting on each of them.  Returns -1 when the
+// current device cannot be queried.
+class PerDeviceInt {
+ public:
+  template <typename Make>
+  int get(Make make) {
+    int device = -1;
+    if (cudaGetDevice(&device) != cudaSuccess) {
+      cudaGetLastError();
+      return -1;
+    }
+    const std::lock_guard<std::mutex> lock(mu_);
+    auto it = values_.find(device);
+    if (it != values_.end()) return it->second;
+    const int v = make();
+    values_.emplace(device, v);
+    return v;
+  }
+
+ private:
+  std::mutex mu_;
+  std::map<int, int> values_;
+};
 
 // Fused cluster kernel (frame_fused.cu).  Returns false when the shape or the
 // device cannot run it (the caller then uses the phase kernels).

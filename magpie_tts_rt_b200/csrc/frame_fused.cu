@@ -746,10 +746,8 @@ bool make_weight_map(CUtensorMap* map, const void* base, uint64_t cols, uint64_t
 
 
 int fused_frame_clusters() {
-  static int cached = -1;  // per process: the cluster shape is a property of the device model
-  static std::mutex mu;
-  const std::lock_guard<std::mutex> lock(mu);
-  if (cached < 0) {
+  static PerDeviceInt cache;  // the opt-in below is per device context
+  return cache.get([] {
     int clusters = 0;
     if (encode_tiled() != nullptr &&
         cudaFuncSetAttribute(fused_frame_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -762,9 +760,8 @@ int fused_frame_clusters() {
       if (cudaOccupancyMaxActiveClusters(&clusters, fused_frame_kernel, &cfg) != cudaSuccess) clusters = 0;
     }
     cudaGetLastError();
-    cached = clusters;
-  }
-  return cached;
+    return clusters;
+  });
 }
 
 bool fused_frame_supported(const Frame& f) {

@@ -905,10 +905,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
 }  // namespace
 
 int pair_frame_clusters() {
-  static int cached = -1;  // per process
-  static std::mutex mu;
-  const std::lock_guard<std::mutex> lock(mu);
-  if (cached < 0) {
+  static PerDeviceInt cache;  // the opt-in below is per device context
+  return cache.get([] {
     int clusters = 0;
     if (cudaFuncSetAttribute(pair_frame_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(kPSmemBytes)) == cudaSuccess) {
@@ -919,9 +917,8 @@ int pair_frame_clusters() {
       if (cudaOccupancyMaxActiveClusters(&clusters, pair_frame_kernel, &cfg) != cudaSuccess) clusters = 0;
     }
     cudaGetLastError();
-    cached = clusters;
-  }
-  return cached;
+    return clusters;
+  });
 }
 
 bool pair_frame_supported(const Frame& f) {

@@ -1299,10 +1299,8 @@ __global__ void __launch_bounds__(kSThreads, 1) split_frame_kernel(Frame f, cons
 
 template <int C, int R>
 int split_clusters() {
-  static int cached = -1;  // per process
-  static std::mutex mu;
-  const std::lock_guard<std::mutex> lock(mu);
-  if (cached < 0) {
+  static PerDeviceInt cache;  // the opt-in below is per device context
+  return cache.get([] {
     int clusters = 0;
     if (cudaFuncSetAttribute(split_frame_kernel<C, R>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(split_smem_bytes<C, R>())) == cudaSuccess) {
@@ -1331,9 +1329,8 @@ int split_clusters() {
       }
     }
     cudaGetLastError();
-    cached = clusters;
-  }
-  return cached;
+    return clusters;
+  });
 }
 
 template <int C, int R>

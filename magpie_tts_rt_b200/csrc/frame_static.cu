@@ -28,7 +28,7 @@
 
 namespace {
 
-constexpr size_t kStaticFrameWorkspaceBytes = size_t(2) << 20;
+constexpr size_t kStaticFrameWorkspaceBytes = MTT_B200_STATIC_FRAME_WORKSPACE_BYTES;
 constexpr int kMaxDevices = 64;
 
 __device__ __align__(256) unsigned char g_static_frame_workspace[kStaticFrameWorkspaceBytes];

@@ -790,10 +790,8 @@ __global__ void __launch_bounds__(kTThreads, 1) tile_frame_kernel(Frame f, const
 
 bool tile_frame_supported(const Frame& f) {
   if (f.d != kTD || f.H != kTHeads || f.F != kTF || f.L != 1 || !f.in_proj || (f.rp != 1 && f.rp != 2)) return false;
-  static int cached = -1;  // per process
-  static std::mutex mu;
-  const std::lock_guard<std::mutex> lock(mu);
-  if (cached < 0) {
+  static PerDeviceInt cache;  // the opt-in below is per device context
+  return cache.get([] {
     int ok = 0;
     if (cudaFuncSetAttribute(tile_frame_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(kTSmemBytes)) == cudaSuccess) {
@@ -805,9 +803,8 @@ bool tile_frame_supported(const Frame& f) {
       }
     }
     cudaGetLastError();
-    cached = ok;
-  }
-  return cached == 1;
+    return ok;
+  }) == 1;
 }
 
 int tile_frame_clusters() {

@@ -413,3 +413,31 @@ def test_sampler_row_shapes(path, kind):
     counter = np.arange(n) * 3
     gpu = run_gpu(eng, hidden, flags, seed, counter)
     check_frame(w, hidden, flags, seed, counter, gpu)
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs in this process")
+@pytest.mark.parametrize("path", [PATH_AUTO, FUSED, TILE, PAIR, SPLIT4, SPLIT8])
+def test_frames_on_two_devices_in_one_process(path):
+    """One process drives frames on cuda:0 and then cuda:1 (the reference
+    allows several runtimes per process, tests/c_api/multi_runtime_plugin_gpu_tests.cpp).
+    Each device makes its own kernel set-up (the shared-memory opt-in is a
+    per-device setting); each GPU uses only its own memory.  Both match the
+    oracle and agree with each other bit for bit."""
+    from magpie_tts_rt_b200.local_ar import LocalArEngine
+    shape = SHAPE_BASELINE
+    w = weights(shape, 21)
+    n = 6
+    hidden = _hidden(n, 5)
+    flags = tuple(np.resize(np.asarray(f), n) for f in FLAGS6)
+    seed = np.resize(np.array([1234, 0, 7, (1 << 32) - 1, 99, 5]), n)
+    counter = np.resize(np.array([0, 16, 3200, 48, S.MAX_COUNTER - 3, 0]), n)
+    out = []
+    for dev in (0, 1):
+        with torch.cuda.device(dev):
+            eng = LocalArEngine(w, max_streams=n, device=f"cuda:{dev}", path=path)
+            assert path == PATH_AUTO or eng.path == path
+            gpu = run_gpu(eng, hidden, flags, seed, counter)
+        check_frame(w, hidden, flags, seed, counter, gpu)
+        out.append(gpu)
+    for k in ("tokens", "counter", "invalid", "end", "next_emb", "logits"):
+        np.testing.assert_array_equal(out[0][k], out[1][k], err_msg=k)

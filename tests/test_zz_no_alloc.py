@@ -13,11 +13,12 @@ import numpy as np
 import pytest
 import torch
 
-from magpie_tts_rt_b200.model import EMBED, POSITIONS, SHAPE_BASELINE, VOCAB, make_weights
+from magpie_tts_rt_b200.model import EMBED, POSITIONS, SHAPE_BASELINE, SHAPE_SOFIA, VOCAB, make_weights
 
 pytestmark = pytest.mark.gpu
 
 STATIC_WORKSPACE_TOO_SMALL = -4
+STATIC_BYTES = 2 << 20
 
 
 def _entry():
@@ -47,11 +48,17 @@ def _outputs(b):
                                 b.next_embedding, b.logits_out)]
 
 
-def test_static_workspace_entry_matches_workspace_entry():
+def _call(fn, eng, batch, stream=None):
+    stream = torch.cuda.current_stream() if stream is None else stream
+    return fn(ctypes.byref(eng._shape), ctypes.byref(eng._w), ctypes.byref(eng._sampling),
+              ctypes.byref(batch.c_struct()), ctypes.c_void_p(stream.cuda_stream))
+
+
+@pytest.mark.parametrize("shape,n", [(SHAPE_BASELINE, 6), (SHAPE_SOFIA, 5)])
+def test_static_workspace_entry_matches_workspace_entry(shape, n):
     from magpie_tts_rt_b200.local_ar import LocalArEngine
     L, fn = _entry()
-    w = make_weights(SHAPE_BASELINE, seed=31, profile="parity")
-    n = 6
+    w = make_weights(shape, seed=31, profile="parity")
     eng = LocalArEngine(w, max_streams=n)
     stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
     ref = _batch(n, 1)
@@ -83,3 +90,63 @@ def test_static_workspace_entry_rejects_oversized_batch():
     torch.cuda.synchronize()
     assert status == STATIC_WORKSPACE_TOO_SMALL
     assert int((b.codec_tokens != -9).sum()) == 0
+
+
+def _largest_fitting(L, eng, cfg=1):
+    size = lambda n: L.lib.mtt_b200_local_ar_frame_workspace_size(ctypes.byref(eng._shape), n, cfg)
+    n = 1
+    while size(n + 1) <= STATIC_BYTES:
+        n += 1
+    return n
+
+
+def test_static_workspace_entry_boundary():
+    """The largest batch whose workspace size fits the 2 MiB array runs (and
+    matches the workspace entry); one session more is rejected untouched."""
+    from magpie_tts_rt_b200.local_ar import LocalArEngine
+    L, fn = _entry()
+    w = make_weights(SHAPE_BASELINE, seed=33, profile="parity")
+    probe = LocalArEngine(w, max_streams=1)
+    n = _largest_fitting(L, probe)
+    assert n >= 32
+    eng = LocalArEngine(w, max_streams=n + 1)
+    ref, got = _batch(n, 4), _batch(n, 4)
+    eng.frame(ref)
+    assert _call(fn, eng, got) == 0
+    torch.cuda.synchronize()
+    for a, b in zip(_outputs(ref), _outputs(got)):
+        assert torch.equal(a, b)
+    over = _batch(n + 1, 5)
+    over.codec_tokens.fill_(-9)
+    assert _call(fn, eng, over) == STATIC_WORKSPACE_TOO_SMALL
+    torch.cuda.synchronize()
+    assert int((over.codec_tokens != -9).sum()) == 0
+
+
+def test_static_workspace_entry_in_a_cuda_graph():
+    """The use the entry exists for: after a first call on the device (which
+    resolves the array's address), the call is recorded into a CUDA graph in
+    global capture mode (where an allocation would fail the capture) and
+    replayed; each replay gives bit for bit what the workspace entry gives for
+    the same frame."""
+    from magpie_tts_rt_b200.local_ar import LocalArEngine
+    L, fn = _entry()
+    w = make_weights(SHAPE_BASELINE, seed=34, profile="parity")
+    n = 6
+    eng = LocalArEngine(w, max_streams=n)
+    ref, got = _batch(n, 6), _batch(n, 6)
+    assert _call(fn, eng, got) == 0  # the first call on this device, outside any capture
+    eng.frame(ref)
+    torch.cuda.synchronize()
+    side = torch.cuda.Stream()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=side, capture_error_mode="global"):
+        status = _call(fn, eng, got, stream=side)
+    assert status == 0
+    for replay in range(2):
+        graph.replay()
+        eng.frame(ref)
+        torch.cuda.synchronize()
+        for a, b in zip(_outputs(ref), _outputs(got)):
+            assert torch.equal(a, b), replay
+    del graph
