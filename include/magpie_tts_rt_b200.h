@@ -572,8 +572,9 @@ MTT_B200_API size_t mtt_b200_main_decoder_workspace_size(int32_t max_sessions, i
  * src/runtime/synthesis_pipeline.cpp:572-648): writes each session's new
  * key / value at its position and sets its key mask there, and produces the
  * decoder hidden state and the alignment scores.  Stream-ordered; the layer
- * GEMMs are cuBLASLt calls (its handle is created by the first call on a
- * device: make that call before any stream capture).  workspace: >=
+ * GEMMs run on this library's tcgen05 kernel (the first call on a device
+ * sets its shared-memory opt-in there: make that call before any stream
+ * capture).  workspace: >=
  * mtt_b200_main_decoder_workspace_size bytes, 256-byte aligned.  Returns
  * MTT_B200_STATUS_*.
  */
@@ -591,6 +592,17 @@ MTT_B200_API int mtt_b200_launch_test_clamped_gumbel(const float* uniform, float
                                                      void* stream);
 /* out[i] = the device's correctly rounded natural log of x[i]. */
 MTT_B200_API int mtt_b200_launch_test_log(const float* x, float* out, size_t count, void* stream);
+
+/* The projection GEMM of the Main Decoder step on its own (for numerics tests
+ * and timing): Y[rows][n] = bf16(X[rows][k] W[n][k]^T) with f32 accumulation
+ * on the tcgen05 kernel; gelu != 0 applies GELU-tanh to the bf16-rounded
+ * product; splits > 1 splits K and writes the f32 partial sums to
+ * partial[splits][rows][n] instead of Y (Y untouched).  n a multiple of 128,
+ * k of 64 * splits; X, W, Y, partial 16-byte aligned device pointers.
+ * Returns MTT_B200_STATUS_*. */
+MTT_B200_API int mtt_b200_launch_test_gemm(const void* x_bf16, const void* w_bf16, void* y_bf16, int32_t rows,
+                                           int32_t n, int32_t k, int32_t gelu, int32_t splits, float* partial,
+                                           void* stream);
 
 #ifdef __cplusplus
 } /* extern "C" */

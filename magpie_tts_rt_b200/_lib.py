@@ -184,6 +184,7 @@ SIGNATURES = {
         I32, [ctypes.POINTER(MainDecoderWeights), ctypes.POINTER(MainDecoderBatch), P, SZ, P]),
     "mtt_b200_launch_test_clamped_gumbel": (I32, [P, P, SZ, P]),
     "mtt_b200_launch_test_log": (I32, [P, P, SZ, P]),
+    "mtt_b200_launch_test_gemm": (I32, [P, P, P, I32, I32, I32, I32, I32, P, P]),
 }
 
 

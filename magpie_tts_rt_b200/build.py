@@ -2,8 +2,8 @@
 
 nvcc compiles every ``csrc/*.cu`` / ``csrc/*.cpp`` for
 ``-gencode arch=compute_100a,code=sm_100a`` (nvcc cross-compiles without a
-GPU) and links them with the CUDA runtime statically and with cuBLASLt (the
-Main Decoder step's plain projection GEMMs).  A linker version script
+GPU) and links them with the CUDA runtime statically; no other library is
+linked (every GEMM is this library's own tcgen05 kernel).  A linker version script
 exports only the ``mtt_*`` C symbols declared in ``include/*.h``, as the
 reference's plugin library exports only its C ABI
 (``cmake/magpie_tts_rt_plugins.map``).
@@ -74,7 +74,7 @@ def build(force: bool = False, verbose_ptxas: bool = False) -> str:
             fh.write(VERSION_SCRIPT)
         cuda_lib = os.path.join(os.path.dirname(os.path.dirname(NVCC)), "lib64")
         cmd = [NVCC] + ARCH + ["-shared", "-cudart", "static", "-o", LIBRARY] + objs + [
-            "-L" + cuda_lib, "-lcublasLt", "-Xlinker", "-rpath," + cuda_lib,
+            "-L" + cuda_lib, "-Xlinker", "-rpath," + cuda_lib,
             "-Xlinker", "--version-script=" + vs]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:

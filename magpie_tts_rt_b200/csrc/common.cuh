@@ -17,6 +17,9 @@
 #include <math_constants.h>
 #include <stdint.h>
 
+#include <map>
+#include <mutex>
+
 namespace mtt {
 
 constexpr int kVocab = 2024;
@@ -206,5 +209,33 @@ inline cudaError_t launch_serialized(void (*kernel)(KArgs...), dim3 grid, dim3 b
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
 }
+
+// One int per device ordinal, computed by `make` the first time it is asked
+// for with that device current.  A kernel's dynamic shared-memory opt-in
+// (cudaFuncSetAttribute) is a setting of the current device's context and
+// its occupancy a property of that device, so a process that runs frames on
+// several GPUs must make the setting on each of them.  Returns -1 when the
+// current device cannot be queried.
+class PerDeviceInt {
+ public:
+  template <typename Make>
+  int get(Make make) {
+    int device = -1;
+    if (cudaGetDevice(&device) != cudaSuccess) {
+      cudaGetLastError();
+      return -1;
+    }
+    const std::lock_guard<std::mutex> lock(mu_);
+    auto it = values_.find(device);
+    if (it != values_.end()) return it->second;
+    const int v = make();
+    values_.emplace(device, v);
+    return v;
+  }
+
+ private:
+  std::mutex mu_;
+  std::map<int, int> values_;
+};
 
 }  // namespace mtt

@@ -399,11 +399,13 @@ __global__ void __launch_bounds__(256) frame_end_kernel(Frame f) {
       f.codec_tokens[codec_index(f, s, p)] = tok[p];
     }
     const int slot = f.eos_slot[s];
-    const float* part = f.eos_partial + static_cast<int64_t>(slot < 0 ? 0 : slot) * kPositions * kEosChunks;
+    const uint32_t* mk =
+        reinterpret_cast<const uint32_t*>(f.eos_partial) + static_cast<int64_t>(slot < 0 ? 0 : slot) * kPositions;
     const float* el = f.eos_logit + static_cast<int64_t>(slot < 0 ? 0 : slot) * kPositions;
-    commit_end(f, s, eos_decide(part, el, tok, slot >= 0, f.finished[s]));
+    commit_end(f, s, eos_decide_proj(mk, el, tok, slot >= 0, f.finished[s]));
     f.counter_io[s] = f.ctr[s];
-    f.invalid_rows[s] = f.inv[s];
+    // a projection whose bounded waits gave up marks its sessions invalid (bit 4)
+    f.invalid_rows[s] = f.inv[s] | (slot >= 0 && f.eos_count[1] != 0 ? 16 : 0);
   }
   const float* acc = f.emb_acc + static_cast<int64_t>(s) * kEmbed;
   for (int k = threadIdx.x; k < kEmbed; k += blockDim.x) {
@@ -691,18 +693,9 @@ extern "C" MTT_B200_API int mtt_b200_launch_local_ar_frame(const mtt_b200_local_
                                    f.head_b + static_cast<int64_t>(p) * kVocab);
     sample_kernel<<<f.n, kSampleThreads, 0, st>>>(f, p);
   }
-  EosArgs ea;
-  ea.hidden = f.hidden;
-  ea.hidden_stream_stride = static_cast<int64_t>(rp) * kEmbed;
-  ea.uncond_offset = rp == 2 ? kEmbed : 0;
-  ea.weight = f.final_w;
-  ea.bias = f.final_b;
-  ea.cfg_scale = rp == 2 ? f.prm.cfg_scale : 1.0f;
-  ea.eos_list = f.eos_list;
-  ea.eos_count = f.eos_count;
-  ea.partial_max = f.eos_partial;
-  ea.eos_logit = f.eos_logit;
-  eos_project_kernel<<<dim3(kEosChunks, kPositions), kEosThreads, 0, st>>>(ea);
+  if (f.final_w != nullptr && launch_eos_projection(frame_eos_args(f), st) != cudaSuccess) {
+    return MTT_B200_STATUS_CUDA_ERROR;
+  }
   frame_end_kernel<<<f.n, 256, 0, st>>>(f);
   return cudaPeekAtLastError() == cudaSuccess ? MTT_B200_STATUS_OK : MTT_B200_STATUS_CUDA_ERROR;
 }

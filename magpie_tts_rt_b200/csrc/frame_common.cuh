@@ -5,11 +5,10 @@
 #include <cuda.h>
 
 #include <cstddef>
-#include <map>
-#include <mutex>
 
 #include "common.cuh"
 #include "eos.cuh"
+#include "eos_proj.cuh"
 
 namespace mtt {
 
@@ -102,34 +101,6 @@ inline Layout make_layout(int d, int L, int F, int n, int rp) {
 }
 
 
-// One int per device ordinal, computed by `make` the first time it is asked
-// for with that device current.  A kernel's dynamic shared-memory opt-in
-// (cudaFuncSetAttribute) is a setting of the current device's context and
-// its occupancy a property of that device, so a process that runs frames on
-// several GPUs must make the setting on each of them.  Returns -1 when the
-// current device cannot be queried.
-class PerDeviceInt {
- public:
-  template <typename Make>
-  int get(Make make) {
-    int device = -1;
-    if (cudaGetDevice(&device) != cudaSuccess) {
-      cudaGetLastError();
-      return -1;
-    }
-    const std::lock_guard<std::mutex> lock(mu_);
-    auto it = values_.find(device);
-    if (it != values_.end()) return it->second;
-    const int v = make();
-    values_.emplace(device, v);
-    return v;
-  }
-
- private:
-  std::mutex mu_;
-  std::map<int, int> values_;
-};
-
 // Fused cluster kernel (frame_fused.cu).  Returns false when the shape or the
 // device cannot run it (the caller then uses the phase kernels).
 bool fused_frame_supported(const Frame& f);
@@ -157,8 +128,12 @@ bool split_frame_supported(const Frame& f, int split, int rows);
 int split_frame_clusters(int split, int rows);
 cudaError_t launch_split_frame(const Frame& f, int split, int rows, cudaStream_t stream);
 
-// EOS projection + decision for the sessions a fused or tile kernel registered.
+// EOS projection (tcgen05 GEMM, eos_proj.cuh) + decision for the sessions a
+// frame kernel registered in eos_list / eos_count.
 cudaError_t launch_frame_eos(const Frame& f, cudaStream_t stream);
+// The projection arguments of a frame: the registered sessions' rows, the
+// maxima in eos_partial (as keys), the EOS logits in eos_logit.
+EosProjArgs frame_eos_args(const Frame& f);
 
 // 2D bf16 tensor map over a row-major [rows][cols] matrix, box 64 columns x
 // box_rows rows, 128-byte swizzle (false if the driver entry point is missing).

@@ -51,6 +51,7 @@
 
 #include <mutex>
 
+#include "eos_proj.cuh"
 #include "frame_common.cuh"
 #include "ptx.cuh"
 #include "sampling.cuh"
@@ -692,16 +693,21 @@ __global__ void __cluster_dims__(kCS, 1, 1) __launch_bounds__(kThreads, 1)
   cluster.sync();  // no CTA leaves while a peer may still address its shared memory
 }
 
-// EOS decision for the sessions the fused kernel registered; resets the count.
+// EOS decision for the sessions the frame kernel registered (projection from
+// launch_eos_projection); resets the count.  A projection whose bounded waits
+// gave up marks the sessions invalid (bit 4).
 __global__ void __launch_bounds__(256) fused_eos_finish_kernel(Frame f) {
-  wait_prior_grid();  // launched after eos_project_kernel with programmatic serialization
+  wait_prior_grid();  // launched after the EOS projection with programmatic serialization
   const int count = *f.eos_count;
+  const bool failed = f.eos_count[1] != 0;
+  const uint32_t* max_key = reinterpret_cast<const uint32_t*>(f.eos_partial);
   for (int e = threadIdx.x; e < count; e += blockDim.x) {
     const int s = f.eos_list[e];
-    const int32_t end = eos_decide(f.eos_partial + static_cast<int64_t>(e) * kPositions * kEosChunks,
-                                   f.eos_logit + static_cast<int64_t>(e) * kPositions, f.tokens + s * kPositions,
-                                   true, false);
+    const int32_t end = eos_decide_proj(max_key + static_cast<int64_t>(e) * kPositions,
+                                        f.eos_logit + static_cast<int64_t>(e) * kPositions, f.tokens + s * kPositions,
+                                        true, false);
     commit_end(f, s, end);
+    if (failed) f.invalid_rows[s] |= 16;
   }
   __syncthreads();
   if (threadIdx.x == 0) *f.eos_count = 0;
@@ -786,24 +792,32 @@ cudaError_t launch_fused_frame(const Frame& f, cudaStream_t stream) {
 }
 
 cudaError_t launch_frame_eos(const Frame& f, cudaStream_t stream) {
-  EosArgs ea;
-  ea.hidden = f.hidden;
-  ea.hidden_stream_stride = static_cast<int64_t>(f.rp) * kEmbed;
-  ea.uncond_offset = f.rp == 2 ? kEmbed : 0;
-  ea.weight = f.final_w;
-  ea.bias = f.final_b;
-  ea.cfg_scale = f.rp == 2 ? f.prm.cfg_scale : 1.0f;
-  ea.eos_list = f.eos_list;
-  ea.eos_count = f.eos_count;
-  ea.partial_max = f.eos_partial;
-  ea.eos_logit = f.eos_logit;
-  // each launch may start while the one before it drains (wait_prior_grid)
-  cudaError_t e = launch_serialized(eos_project_kernel, dim3(kEosChunks, kPositions), dim3(kEosThreads), 0, stream,
-                                    ea);
-  if (e != cudaSuccess) return e;
+  cudaError_t e = cudaSuccess;
+  if (f.final_w != nullptr) {  // without the projection no session was registered
+    e = launch_eos_projection(frame_eos_args(f), stream);
+    if (e != cudaSuccess) return e;
+  }
   e = launch_serialized(fused_eos_finish_kernel, dim3(1), dim3(256), 0, stream, f);
   if (e != cudaSuccess) return e;
   return cudaPeekAtLastError();
+}
+
+EosProjArgs frame_eos_args(const Frame& f) {
+  EosProjArgs a;
+  a.hidden = f.hidden;
+  a.hidden_stream_stride = static_cast<int64_t>(f.rp) * kEmbed;
+  a.uncond_offset = f.rp == 2 ? kEmbed : 0;
+  a.list = f.eos_list;
+  a.count = f.eos_count;
+  a.n_max = f.n;
+  a.weight = f.final_w;
+  a.bias = f.final_b;
+  a.cfg_scale = f.rp == 2 ? f.prm.cfg_scale : 1.0f;
+  a.rows = f.logits;  // the phase kernels' logits scratch is free once the frame's positions are done
+  a.max_key = reinterpret_cast<uint32_t*>(f.eos_partial);
+  a.eos_logit = f.eos_logit;
+  a.status = f.eos_count + 1;
+  return a;
 }
 
 }  // namespace mtt

@@ -8,7 +8,7 @@
 // 572-648).  Per layer:
 //   add_ln     x = bf16(x + o); LN(x) (fused; the layer-0 form adds the
 //              position embedding to the codec embedding sum)
-//   GEMM       q|k|v = LN(x) W_qkv^T                  (cuBLASLt, bf16 in/out, f32 accumulate)
+//   GEMM       q|k|v = LN(x) W_qkv^T                  (tcgen05, bf16 in/out, f32 accumulate)
 //   self_attn  k, v written at the session's position; attention of the 12
 //              heads over positions [0, position] of the session's cache
 //   GEMM       o = att W_o^T
@@ -20,23 +20,23 @@
 //              their mean (the alignment scores)
 //   GEMM       o = ctx W_xo^T
 //   add_ln     x += o; LN_ff(x)
-//   GEMM, gelu h = GELU(LN_ff(x) W_ffn1^T)
-//   GEMM       o = h W_ffn2^T
-//   add_ln     x += o; LN of the next layer (or the output norm)
-// The GEMMs are plain library GEMMs (M = 2 x sessions rows); the attention,
-// normalisation and activation kernels are this file's.  The self-attention
+//   GEMM+gelu  h = GELU(bf16(LN_ff(x) W_ffn1^T))      (GELU in the GEMM's epilogue)
+//   GEMM       o = h W_ffn2^T                          (K split in 4: f32 partial sums)
+//   add_ln     x += bf16(sum of the partials); LN of the next layer (or the output norm)
+// The GEMMs run on gemm_tc.cuh's persistent tcgen05 kernel with the 2 x
+// sessions activation rows on the MMA's M side (128 per tile) and the output
+// features on its N side (256 per tile, the full-rate shape).  The self-attention
 // cache stream is the step's dominant traffic (keys and values of every
 // layer, head and CFG row up to the position), so that kernel is written for
 // HBM bandwidth: one CTA per (session, row, head), keys and values streamed
 // together in one pass through a shared-memory ring filled by bulk copies.
-#include <cublasLt.h>
-
 #include <map>
 #include <mutex>
 #include <tuple>
 
 #include "../../include/magpie_tts_rt_b200.h"
 #include "common.cuh"
+#include "gemm_tc.cuh"
 
 namespace mtt {
 namespace {
@@ -94,6 +94,7 @@ struct Step {
   int32_t* status;
   // workspace
   bf16 *x, *ln, *qkv, *att, *o, *xq, *ctx, *h, *align;
+  float* part;  // split-K partial sums [splits][2n][768] of the GEMM before an add_ln
 };
 
 __device__ __forceinline__ bool session_active(const Step& st, int s) {
@@ -116,7 +117,10 @@ __device__ __forceinline__ bool session_live(const Step& st, int s) {
 // inactive or out of range are left as they are.
 // ---------------------------------------------------------------------------
 template <bool kEmbed>
-__global__ void __launch_bounds__(kLnThreads) add_ln_kernel(Step st, const bf16* __restrict__ w, bf16* out) {
+__global__ void __launch_bounds__(kLnThreads) add_ln_kernel(Step st, const bf16* __restrict__ w, bf16* out,
+                                                            int partials) {
+  // one wave of small CTAs: let the next GEMM set up and fetch its weights meanwhile
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   wait_prior_grid();
   const int lane = threadIdx.x & 31;
   const int row = blockIdx.x * (kLnThreads / 32) + (threadIdx.x >> 5);
@@ -136,6 +140,20 @@ __global__ void __launch_bounds__(kLnThreads) add_ln_kernel(Step st, const bf16*
     if (kEmbed) {
       unpack8f(*reinterpret_cast<const uint4*>(st.embedded + static_cast<size_t>(s) * kW + col), a);
       unpack8f(*reinterpret_cast<const uint4*>(st.pos + static_cast<size_t>(st.position[s]) * kW + col), b);
+    } else if (partials > 0) {
+      // the split GEMM's output: its partial sums in split order, rounded once to bf16
+      unpack8f(*reinterpret_cast<const uint4*>(xr + col), a);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) b[e] = 0.f;
+      for (int ks = 0; ks < partials; ++ks) {
+        const float4* pp =
+            reinterpret_cast<const float4*>(st.part + (static_cast<size_t>(ks) * 2 * st.n + row) * kW + col);
+        const float4 p0 = pp[0], p1 = pp[1];
+        b[0] += p0.x; b[1] += p0.y; b[2] += p0.z; b[3] += p0.w;
+        b[4] += p1.x; b[5] += p1.y; b[6] += p1.z; b[7] += p1.w;
+      }
+#pragma unroll
+      for (int e = 0; e < 8; ++e) b[e] = bfr(b[e]);
     } else {
       unpack8f(*reinterpret_cast<const uint4*>(xr + col), a);
       unpack8f(*reinterpret_cast<const uint4*>(st.o + static_cast<size_t>(row) * kW + col), b);
@@ -562,99 +580,160 @@ __global__ void __launch_bounds__(kXAThreads) cross_attn_kernel(Step st, int l, 
   }
 }
 
-// GELU-tanh in place, bf16 (text_encoder_wrapper.py:61-70: F.gelu(approximate="tanh")).
-__global__ void gelu_kernel(bf16* h, size_t count8) {
-  wait_prior_grid();
-  const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (i >= count8) return;
-  float f[8];
-  unpack8f(reinterpret_cast<const uint4*>(h)[i], f);
+// ---------------------------------------------------------------------------
+// GEMM epilogues (gemm_tc.cuh): lane = output feature m, columns = rows n
+// ---------------------------------------------------------------------------
+
+// The projection GEMMs put the activation rows on the MMA's M side (128 per
+// tile) and the output features on its N side (256 per tile; 128 for the
+// 128-wide cross-attention query): a tcgen05.mma of M = 128, K = 16 costs the
+// same for every N up to 256, so N = 256 is the full-rate shape, and each
+// epilogue lane then holds 32 consecutive output features of its own row,
+// which leave as four 16-byte stores.
+
+// C[m][n] = bf16(D), or GELU-tanh of the bf16-rounded D (the reference rounds
+// the FFN1 output before its activation, text_encoder_wrapper.py:61-70).
+// Each lane holds 64 bytes of its own row per chunk; the warp stages its 32
+// rows in shared memory (row stride 80 bytes: conflict-free 16-byte access)
+// and writes them back four lanes per row, so each store instruction covers
+// eight whole 64-byte row segments instead of 32 scattered 16-byte pieces.
+constexpr int kStageRowB = 40;  // bf16 per staged row (64 bytes + 16 of padding)
+struct EpiRows {
+  bf16* c;
+  int ldc;
+  int rows;
+  int gelu;
+  __device__ __forceinline__ void chunk(int m, int n0, int /*ks*/, const uint32_t (&v)[32], int /*n_cols*/) const {
+    __shared__ __align__(16) bf16 stage[kGemmEpiWarps][32][kStageRowB];
+    const int lane = threadIdx.x & 31, w = gemm_epi_warp();
+    uint32_t packed[16];
 #pragma unroll
-  for (int e = 0; e < 8; ++e) {
-    const float v = f[e];
-    f[e] = 0.5f * v * (1.0f + tanhf(0.7978845608028654f * (v + 0.044715f * v * v * v)));
+    for (int j = 0; j < 16; ++j) {
+      float a = __uint_as_float(v[2 * j]), b = __uint_as_float(v[2 * j + 1]);
+      if (gelu) {
+        a = bfr(a);
+        b = bfr(b);
+        a = 0.5f * a * (1.0f + tanhf(0.7978845608028654f * (a + 0.044715f * a * a * a)));
+        b = 0.5f * b * (1.0f + tanhf(0.7978845608028654f * (b + 0.044715f * b * b * b)));
+      }
+      const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+      packed[j] = *reinterpret_cast<const uint32_t*>(&h);
+    }
+    uint4* mine = reinterpret_cast<uint4*>(stage[w][lane]);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) mine[q] = make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
+    __syncwarp();
+    const int m0 = m - lane;  // the warp's first row
+#pragma unroll
+    for (int it = 0; it < 4; ++it) {
+      const int r = 8 * it + (lane >> 2), q = lane & 3;
+      if (m0 + r < rows) {
+        reinterpret_cast<uint4*>(c + static_cast<size_t>(m0 + r) * ldc + n0)[q] =
+            reinterpret_cast<const uint4*>(stage[w][r])[q];
+      }
+    }
+    __syncwarp();
   }
-  reinterpret_cast<uint4*>(h)[i] = pack8f(f);
-}
-
-// ---------------------------------------------------------------------------
-// host: cuBLASLt GEMMs  C[M][N] = A[M][K] W[N][K]^T  (bf16, f32 accumulate)
-// ---------------------------------------------------------------------------
-
-struct GemmPlan {
-  cublasLtMatmulDesc_t op = nullptr;
-  cublasLtMatrixLayout_t la = nullptr, lb = nullptr, lc = nullptr;
-  cublasLtMatmulAlgo_t algo{};
-  bool ok = false;
 };
 
-struct LtState {
-  cublasLtHandle_t handle = nullptr;
-  std::map<std::tuple<int, int, int, size_t>, GemmPlan> plans;
-  std::mutex mu;
-};
-
-LtState& lt_state(int device) {
-  static std::mutex mu;
-  static std::map<int, LtState*> states;
-  std::lock_guard<std::mutex> lock(mu);
-  LtState*& s = states[device];
-  if (s == nullptr) {
-    s = new LtState();
-    if (cublasLtCreate(&s->handle) != CUBLAS_STATUS_SUCCESS) s->handle = nullptr;
-  }
-  return *s;
-}
-
-const GemmPlan* gemm_plan(LtState& st, int M, int N, int K, size_t ws_bytes) {
-  std::lock_guard<std::mutex> lock(st.mu);
-  auto key = std::make_tuple(M, N, K, ws_bytes);
-  auto it = st.plans.find(key);
-  if (it != st.plans.end()) return it->second.ok ? &it->second : nullptr;
-  GemmPlan& p = st.plans[key];
-  if (st.handle == nullptr) return nullptr;
-  const cublasOperation_t ta = CUBLAS_OP_T, tb = CUBLAS_OP_N;
-  bool ok = cublasLtMatmulDescCreate(&p.op, CUBLAS_COMPUTE_32F, CUDA_R_32F) == CUBLAS_STATUS_SUCCESS &&
-            cublasLtMatmulDescSetAttribute(p.op, CUBLASLT_MATMUL_DESC_TRANSA, &ta, sizeof(ta)) ==
-                CUBLAS_STATUS_SUCCESS &&
-            cublasLtMatmulDescSetAttribute(p.op, CUBLASLT_MATMUL_DESC_TRANSB, &tb, sizeof(tb)) ==
-                CUBLAS_STATUS_SUCCESS &&
-            // column-major view: W is K x N (op T), the activations K x M, C N x M
-            cublasLtMatrixLayoutCreate(&p.la, CUDA_R_16BF, K, N, K) == CUBLAS_STATUS_SUCCESS &&
-            cublasLtMatrixLayoutCreate(&p.lb, CUDA_R_16BF, K, M, K) == CUBLAS_STATUS_SUCCESS &&
-            cublasLtMatrixLayoutCreate(&p.lc, CUDA_R_16BF, N, M, N) == CUBLAS_STATUS_SUCCESS;
-  if (ok) {
-    cublasLtMatmulPreference_t pref = nullptr;
-    ok = cublasLtMatmulPreferenceCreate(&pref) == CUBLAS_STATUS_SUCCESS;
-    if (ok) {
-      const uint64_t ws = ws_bytes;
-      cublasLtMatmulPreferenceSetAttribute(pref, CUBLASLT_MATMUL_PREF_MAX_WORKSPACE_BYTES, &ws, sizeof(ws));
-      cublasLtMatmulHeuristicResult_t res{};
-      int found = 0;
-      ok = cublasLtMatmulAlgoGetHeuristic(st.handle, p.op, p.la, p.lb, p.lc, p.lc, pref, 1, &res, &found) ==
-               CUBLAS_STATUS_SUCCESS &&
-           found > 0;
-      if (ok) p.algo = res.algo;
-      cublasLtMatmulPreferenceDestroy(pref);
+// part[ks][m][n] = D of split ks (f32), summed by the next add_ln_kernel;
+// staged like EpiRows, 16 columns (64 bytes per row) at a time.
+constexpr int kStageRowF = 20;  // f32 per staged row (64 bytes + 16 of padding)
+struct EpiPartial {
+  float* part;
+  int ldc;
+  int rows;
+  size_t split_stride;
+  __device__ __forceinline__ void chunk(int m, int n0, int ks, const uint32_t (&v)[32], int /*n_cols*/) const {
+    __shared__ __align__(16) float stage[kGemmEpiWarps][32][kStageRowF];
+    const int lane = threadIdx.x & 31, w = gemm_epi_warp();
+    const int m0 = m - lane;
+    float* base = part + static_cast<size_t>(ks) * split_stride;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      float4* mine = reinterpret_cast<float4*>(stage[w][lane]);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        mine[q] = make_float4(__uint_as_float(v[16 * h + 4 * q]), __uint_as_float(v[16 * h + 4 * q + 1]),
+                              __uint_as_float(v[16 * h + 4 * q + 2]), __uint_as_float(v[16 * h + 4 * q + 3]));
+      }
+      __syncwarp();
+#pragma unroll
+      for (int it = 0; it < 4; ++it) {
+        const int r = 8 * it + (lane >> 2), q = lane & 3;
+        if (m0 + r < rows) {
+          reinterpret_cast<float4*>(base + static_cast<size_t>(m0 + r) * ldc + n0 + 16 * h)[q] =
+              reinterpret_cast<const float4*>(stage[w][r])[q];
+        }
+      }
+      __syncwarp();
     }
   }
-  p.ok = ok;
-  return ok ? &p : nullptr;
+};
+
+// Tensor maps are host-encoded; the same (pointer, shape, box) recurs every
+// step, so they are kept (a few hundred per process at most).
+bool cached_map(CUtensorMap* out, const void* base, uint64_t cols, uint64_t rows, uint32_t box_rows) {
+  static std::mutex mu;
+  static std::map<std::tuple<const void*, uint64_t, uint64_t, uint32_t>, CUtensorMap> maps;
+  const auto key = std::make_tuple(base, cols, rows, box_rows);
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    auto it = maps.find(key);
+    if (it != maps.end()) {
+      *out = it->second;
+      return true;
+    }
+  }
+  CUtensorMap m;
+  if (!make_weight_map(&m, base, cols, rows, box_rows)) return false;
+  std::lock_guard<std::mutex> lock(mu);
+  if (maps.size() > 4096) maps.clear();
+  maps.emplace(key, m);
+  *out = m;
+  return true;
 }
 
-bool gemm(LtState& st, const bf16* A, const bf16* W, bf16* C, int M, int N, int K, void* ws, size_t ws_bytes,
-          cudaStream_t stream) {
-  const GemmPlan* p = gemm_plan(st, M, N, K, ws_bytes);
-  if (p == nullptr) return false;
-  const float alpha = 1.f, beta = 0.f;
-  return cublasLtMatmul(st.handle, p->op, &alpha, W, p->la, A, p->lb, &beta, C, p->lc, C, p->lc, &p->algo, ws,
-                        ws_bytes, stream) == CUBLAS_STATUS_SUCCESS;
-}
+// FFN2 (K = 3072) splits its K range in 4 (12 chunks of 64 each, as long as
+// the other GEMMs' K = 768); add_ln_kernel sums the f32 partials.  Splitting
+// the K = 768 GEMMs as well measured slower (the partials' traffic costs more
+// than the shorter K range saves).
+constexpr int kFfn2Splits = 4;
+constexpr int kMaxSplits = kFfn2Splits;
 
-constexpr size_t kGemmWorkspace = 32u << 20;
+// C[rows][N] = X[rows][K] W[N][K]^T on the tensor cores (K a multiple of
+// 64 x splits, N of 128); with partial != nullptr the K range is split in
+// `splits` and the f32 partial sums go to partial[split][rows][N].
+bool tc_gemm(const bf16* X, const bf16* W, bf16* C, int rows, int N, int K, bool gelu, int splits, float* partial,
+             cudaStream_t stream) {
+  const int bn = N % 256 == 0 ? 256 : 128;
+  CUtensorMap amap, bmap;
+  if (!cached_map(&amap, X, static_cast<uint64_t>(K), static_cast<uint64_t>(rows), 128) ||
+      !cached_map(&bmap, W, static_cast<uint64_t>(K), static_cast<uint64_t>(N), static_cast<uint32_t>(bn))) {
+    return false;
+  }
+  GemmProblem pr;
+  pr.m_tiles = (rows + 127) / 128;
+  pr.n_rows = N;
+  pr.n_rows_dev = nullptr;
+  pr.n_rows_scale = 1;
+  pr.splits = partial != nullptr ? splits : 1;
+  pr.k_chunks = K / kGemmKChunk / pr.splits;
+  pr.status = nullptr;
+  pr.b_constant = 1;  // the weights: fetched while the previous kernel finishes
+  cudaError_t e;
+  if (partial != nullptr) {
+    EpiPartial epi{partial, N, rows, static_cast<size_t>(rows) * N};
+    e = bn == 128 ? launch_gemm_tc<128>(amap, bmap, pr, epi, stream) : launch_gemm_tc<256>(amap, bmap, pr, epi, stream);
+  } else {
+    EpiRows epi{C, N, rows, gelu ? 1 : 0};
+    e = bn == 128 ? launch_gemm_tc<128>(amap, bmap, pr, epi, stream) : launch_gemm_tc<256>(amap, bmap, pr, epi, stream);
+  }
+  return e == cudaSuccess;
+}
 
 struct MdLayout {
-  size_t x, ln, qkv, att, o, xq, ctx, h, align, gemm_ws, total;
+  size_t x, ln, qkv, att, o, xq, ctx, h, align, part, total;
 };
 
 MdLayout md_layout(int n, int S) {
@@ -675,7 +754,7 @@ MdLayout md_layout(int n, int S) {
   lo.ctx = take(rows * kXD * 2);
   lo.h = take(rows * kFF * 2);
   lo.align = take((kAlignSlots - 1) * rows * S * 2);
-  lo.gemm_ws = take(kGemmWorkspace);
+  lo.part = take(static_cast<size_t>(kMaxSplits) * rows * kW * 4);
   lo.total = off;
   return lo;
 }
@@ -723,10 +802,6 @@ extern "C" MTT_B200_API int mtt_b200_launch_main_decoder_step(const mtt_b200_mai
   const MdLayout lo = md_layout(b->n_sessions, b->token_stride);
   if (workspace_bytes < lo.total || (reinterpret_cast<uintptr_t>(workspace) & 255u) != 0)
     return MTT_B200_STATUS_INVALID_ARGUMENT;
-  int device = 0;
-  if (cudaGetDevice(&device) != cudaSuccess) return MTT_B200_STATUS_CUDA_ERROR;
-  LtState& lt = lt_state(device);
-  if (lt.handle == nullptr) return MTT_B200_STATUS_CUDA_ERROR;
   const cudaStream_t cs = static_cast<cudaStream_t>(stream);
 
   Step st{};
@@ -770,7 +845,7 @@ extern "C" MTT_B200_API int mtt_b200_launch_main_decoder_step(const mtt_b200_mai
   st.ctx = reinterpret_cast<bf16*>(ws + lo.ctx);
   st.h = reinterpret_cast<bf16*>(ws + lo.h);
   st.align = reinterpret_cast<bf16*>(ws + lo.align);
-  void* gws = ws + lo.gemm_ws;
+  st.part = reinterpret_cast<float*>(ws + lo.part);
 
   const int M = 2 * st.n;
   const unsigned ln_grid = static_cast<unsigned>((M + kLnThreads / 32 - 1) / (kLnThreads / 32));
@@ -779,39 +854,52 @@ extern "C" MTT_B200_API int mtt_b200_launch_main_decoder_step(const mtt_b200_mai
     return MTT_B200_STATUS_CUDA_ERROR;
   }
   auto layer_w = [](const bf16* base, size_t per_layer, int l) { return base + per_layer * l; };
-  if (!launch_after(add_ln_kernel<true>, dim3(ln_grid), kLnThreads, 0, cs, st, st.ln_self, st.ln)) {
+  if (!launch_after(add_ln_kernel<true>, dim3(ln_grid), kLnThreads, 0, cs, st, st.ln_self, st.ln, 0)) {
     return MTT_B200_STATUS_CUDA_ERROR;
   }
   int slot = 0;
   for (int l = 0; l < st.L; ++l) {
-    bool ok = gemm(lt, st.ln, layer_w(st.qkv_w, static_cast<size_t>(kQKV) * kW, l), st.qkv, M, kQKV, kW, gws,
-                   kGemmWorkspace, cs);
+    bool ok = tc_gemm(st.ln, layer_w(st.qkv_w, static_cast<size_t>(kQKV) * kW, l), st.qkv, M, kQKV, kW, false, 1,
+                      nullptr, cs);
     ok = ok && launch_after(self_attn_kernel, dim3(kMH, 2, st.n), kSAThreads, kSASmem, cs, st, l);
-    ok = ok && gemm(lt, st.att, layer_w(st.o_w, static_cast<size_t>(kW) * kW, l), st.o, M, kW, kW, gws,
-                    kGemmWorkspace, cs);
+    ok = ok && tc_gemm(st.att, layer_w(st.o_w, static_cast<size_t>(kW) * kW, l), st.o, M, kW, kW, false, 1, nullptr,
+                       cs);
     ok = ok && launch_after(add_ln_kernel<false>, dim3(ln_grid), kLnThreads, 0, cs, st, layer_w(st.ln_xq, kW, l),
-                            st.ln);
-    ok = ok && gemm(lt, st.ln, layer_w(st.xq_w, static_cast<size_t>(kXD) * kW, l), st.xq, M, kXD, kW, gws,
-                    kGemmWorkspace, cs);
+                            st.ln, 0);
+    ok = ok && tc_gemm(st.ln, layer_w(st.xq_w, static_cast<size_t>(kXD) * kW, l), st.xq, M, kXD, kW, false, 1,
+                       nullptr, cs);
     const bool prior_layer = l >= 2 && l <= 10;
     const bool align_layer = l == 4 || l == 5 || l == 8 || l == 9;
     ok = ok && launch_after(cross_attn_kernel, dim3(2, st.n), kXAThreads, 0, cs, st, l, prior_layer ? 1 : 0,
                             align_layer ? slot : -1);
     if (align_layer) ++slot;
-    ok = ok && gemm(lt, st.ctx, layer_w(st.xo_w, static_cast<size_t>(kW) * kXD, l), st.o, M, kW, kXD, gws,
-                    kGemmWorkspace, cs);
+    ok = ok && tc_gemm(st.ctx, layer_w(st.xo_w, static_cast<size_t>(kW) * kXD, l), st.o, M, kW, kXD, false, 1,
+                       nullptr, cs);
     ok = ok && launch_after(add_ln_kernel<false>, dim3(ln_grid), kLnThreads, 0, cs, st, layer_w(st.ln_ff, kW, l),
-                            st.ln);
-    ok = ok && gemm(lt, st.ln, layer_w(st.ffn1_w, static_cast<size_t>(kFF) * kW, l), st.h, M, kFF, kW, gws,
-                    kGemmWorkspace, cs);
-    const size_t count8 = static_cast<size_t>(M) * kFF / 8;
-    ok = ok && launch_after(gelu_kernel, dim3(static_cast<unsigned>((count8 + 255) / 256)), 256, 0, cs, st.h, count8);
-    ok = ok && gemm(lt, st.h, layer_w(st.ffn2_w, static_cast<size_t>(kW) * kFF, l), st.o, M, kW, kFF, gws,
-                    kGemmWorkspace, cs);
+                            st.ln, 0);
+    ok = ok && tc_gemm(st.ln, layer_w(st.ffn1_w, static_cast<size_t>(kFF) * kW, l), st.h, M, kFF, kW, true, 1,
+                       nullptr, cs);
+    ok = ok && tc_gemm(st.h, layer_w(st.ffn2_w, static_cast<size_t>(kW) * kFF, l), nullptr, M, kW, kFF, false,
+                       kFfn2Splits, st.part, cs);
     const bool last = l + 1 == st.L;
     ok = ok && launch_after(add_ln_kernel<false>, dim3(ln_grid), kLnThreads, 0, cs, st,
-                            last ? st.norm_out : layer_w(st.ln_self, kW, l + 1), last ? st.hidden : st.ln);
+                            last ? st.norm_out : layer_w(st.ln_self, kW, l + 1), last ? st.hidden : st.ln,
+                            kFfn2Splits);
     if (!ok) return MTT_B200_STATUS_CUDA_ERROR;
   }
   return cudaPeekAtLastError() == cudaSuccess ? MTT_B200_STATUS_OK : MTT_B200_STATUS_CUDA_ERROR;
+}
+
+extern "C" MTT_B200_API int mtt_b200_launch_test_gemm(const void* x_bf16, const void* w_bf16, void* y_bf16,
+                                                     int32_t rows, int32_t n, int32_t k, int32_t gelu, int32_t splits,
+                                                     float* partial, void* stream) {
+  using namespace mtt;
+  if (x_bf16 == nullptr || w_bf16 == nullptr || rows <= 0 || n <= 0 || n % 128 != 0 || k <= 0 || splits <= 0 ||
+      k % (kGemmKChunk * splits) != 0 || (splits > 1 ? partial == nullptr : y_bf16 == nullptr)) {
+    return MTT_B200_STATUS_INVALID_ARGUMENT;
+  }
+  const bool ok = tc_gemm(static_cast<const bf16*>(x_bf16), static_cast<const bf16*>(w_bf16),
+                          static_cast<bf16*>(y_bf16), rows, n, k, gelu != 0, splits, splits > 1 ? partial : nullptr,
+                          static_cast<cudaStream_t>(stream));
+  return ok && cudaPeekAtLastError() == cudaSuccess ? MTT_B200_STATUS_OK : MTT_B200_STATUS_CUDA_ERROR;
 }
