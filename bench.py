@@ -87,6 +87,10 @@ def parse():
     ap.add_argument("--loop-only", action="store_true", help="run only the config-5 loop and print its object")
     ap.add_argument("--loop-steps", type=int, default=1024)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--eos-only", action="store_true",
+                    help="run only the EOS-projection measurement and print its object (profiling)")
+    ap.add_argument("--eos-sessions", type=int, nargs="*", default=None,
+                    help="EOS-enabled sessions per measured batch (default 64 and 1024)")
     return ap.parse_args()
 
 
@@ -411,6 +415,76 @@ def latency_config2(eng_w, dev, frames=1000, warm=20):
             "frame_path": PATH_NAMES.get(eng.path, str(eng.path)),
             "p50_us": float(np.percentile(us, 50)), "p99_us": float(np.percentile(us, 99)),
             "mean_us": float(us.mean()), "frames": frames, "invalid": inv}
+
+
+def tensor_probe(dev):
+    """The two measurements behind the frame kernels' shape (library hooks
+    mtt_b200_test_umma_cycles / _dsmem_cycles): SM cycles of one tcgen05.mma
+    (M = 128, K = 16) for each N, issued back to back on every SM, and the
+    bytes per cycle an SM pushes into its 7 cluster peers' shared memory."""
+    from magpie_tts_rt_b200 import _lib as L
+    st = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    out = {"umma_cycles_per_instruction": {}, "umma_mac_per_cycle_per_sm": {}}
+    cyc = torch.zeros(1024, dtype=torch.int64, device=dev)
+    n_mma = 2048
+    for n in (16, 32, 64, 128, 256):
+        if L.lib.mtt_b200_test_umma_cycles(n, 1, n_mma, sms, ctypes.c_void_p(cyc.data_ptr()), st) != 0:
+            return None
+        torch.cuda.synchronize(dev)
+        c = cyc[:sms].cpu().numpy()
+        per = float(np.median(c[c > 0])) / n_mma if (c > 0).any() else None
+        out["umma_cycles_per_instruction"][n] = per
+        out["umma_mac_per_cycle_per_sm"][n] = 128 * n * 16 / per if per else None
+    rounds, clusters, bytes_ = 20, 16, 16384
+    if L.lib.mtt_b200_test_dsmem_cycles(bytes_, rounds, clusters, ctypes.c_void_p(cyc.data_ptr()), st) != 0:
+        return None
+    torch.cuda.synchronize(dev)
+    c = cyc[:8 * clusters].cpu().numpy()
+    per_round = float(np.median(c[c > 0])) / rounds if (c > 0).any() else None
+    out["dsmem_bulk_bytes_per_cycle_per_sm"] = 7 * bytes_ / per_round if per_round else None
+    out["dsmem_note"] = "7 peers x 16 KB per round, rounds separated by cluster barriers, 8-CTA clusters"
+    return out
+
+
+def eos_measure(w, dev, peaks, sizes=(64, 1024), calls=20):
+    """The frame's EOS projection (tcgen05 GEMM over the enabled sessions'
+    rows, guided-logit reduction in the epilogue): frame calls with every
+    session's EOS enabled minus the same calls with EOS disabled, CUDA events.
+    Algorithmic work: 2 rows x 32,384 x 768 MAC per enabled session, and the
+    49.7 MB final projection read once."""
+    from magpie_tts_rt_b200.local_ar import LocalArEngine, StreamBatch
+    out = {}
+    stream = torch.cuda.Stream(dev)
+    for n in sizes:
+        eng = LocalArEngine(w, max_streams=n, device=dev)
+        b = StreamBatch.allocate(n, device=dev)
+        g = torch.Generator().manual_seed(n)
+        b.decoder_hidden.copy_(torch.randn(n, 2, EMBED, generator=g).to(torch.bfloat16))
+        b.rng_seed.copy_(torch.arange(n))
+        times = {}
+        for enabled in (False, True):
+            b.unfinished.fill_(not enabled)
+            with torch.cuda.stream(stream):
+                for _ in range(3):
+                    eng.frame(b, stream=stream)
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+                for _ in range(calls):
+                    eng.frame(b, stream=stream)
+                e1.record(stream)
+            torch.cuda.synchronize(dev)
+            times[enabled] = e0.elapsed_time(e1) * 1000.0 / calls
+        d_us = times[True] - times[False]
+        macs = 2 * n * 32384 * 768
+        tflops = 2 * macs / (d_us * 1e-6) / 1e12 if d_us > 0 else None
+        gbs = (32384 * 768 * 2 + n * 2 * 768 * 2) / (d_us * 1e-6) / 1e9 if d_us > 0 else None
+        tensor_peak = peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"])
+        out[str(n)] = {"frame_call_us_eos_enabled": times[True], "frame_call_us_eos_disabled": times[False],
+                       "eos_projection_us": d_us, "tflops": tflops, "tensor_frac": tflops / tensor_peak if tflops else None,
+                       "hbm_gbs": gbs, "hbm_frac": gbs / peaks["hbm_gbs"] if gbs else None,
+                       "frame_path": PATH_NAMES.get(eng.path, str(eng.path))}
+    return out
 
 
 def alignment_gate_measure(dev, peaks, n=1024, stride=512, steps=200, seed=11):
@@ -763,6 +837,12 @@ def main():
             import torch.distributed as dist
             dist.destroy_process_group()
         return
+    if args.eos_only:
+        w = make_weights(SHAPE_BASELINE, seed=0, dtype=torch.bfloat16, profile="baseline")
+        out = eos_measure(w, torch.device("cuda", local), peaks, sizes=tuple(args.eos_sessions or (64, 1024)))
+        if rank == 0:
+            print(json.dumps({"eos_projection": out}), flush=True)
+        return
     if args.main_decoder_only:
         out = main_decoder_measure(torch.device("cuda", local), peaks, n=args.md_sessions, steps=args.md_steps,
                                    with_cpu=False)
@@ -811,6 +891,10 @@ def main():
     loop = None
     if world == 1 and not args.no_latency and not args.no_loop:
         loop = loop_measure(torch.device("cuda", local), peaks, steps=args.loop_steps)
+    probe = eos = None
+    if world == 1 and not args.no_latency:
+        probe = tensor_probe(torch.device("cuda", local))
+        eos = eos_measure(res["w"], torch.device("cuda", local), peaks)
     cpu = None
     if world == 1 and rank == 0 and not args.no_cpu_baseline:
         cpu = cpu_oracle_sample()
@@ -857,7 +941,7 @@ def main():
                 "gpu_launches": res["launches"], "frame_path": res["path"], "clocks": res["clocks"],
                 "roofline": roof,
                 "latency_config2": latency, "alignment_gate": align, "main_decoder_step": md,
-                "config5_loop": loop,
+                "config5_loop": loop, "eos_projection": eos, "tensor_probe": probe,
                 "cpu_baseline": cpu,
                 "checks": {"invalid_rows": res["invalid"], "forced_eos_ok": res["forced_ok"]}}
         print(json.dumps(line), flush=True)

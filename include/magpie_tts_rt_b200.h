@@ -368,6 +368,11 @@ typedef struct mtt_b200_stream_batch {
                                    end_frame_index at the EOS frame (the EOS frame is not audio;
                                    src/runtime/eos_contract.hpp:14-30): the F of the NanoCodec
                                    [1][8][F] route after the emission batch's last frame */
+  /* Optional: the EOS projection of these sessions' decoder_hidden, already
+   * computed by the Main Decoder step that produced it
+   * (mtt_b200_main_decoder_batch_t.eos_projection, [n][32] 32-bit words).
+   * The frame then skips its own projection and decides EOS from it. */
+  const void* eos_projection;
 } mtt_b200_stream_batch_t;
 
 /* Device workspace bytes for launching up to max_streams streams. */
@@ -534,6 +539,10 @@ typedef struct mtt_b200_main_decoder_weights {
   const void* norm_out; /* [768] */
   int32_t n_layers;     /* >= 10 (alignment layers 4, 5, 8, 9; prior layers 2..10) */
   int32_t pos_rows;     /* >= cache_capacity */
+  /* Optional (for eos_projection): the final projection [16 x 2024][768] and
+   * its bias [16 x 2024], bf16, as in mtt_b200_local_ar_weights_t. */
+  const void* final_w;
+  const void* final_b;
 } mtt_b200_main_decoder_weights_t;
 
 /* Structure-of-arrays state of n sessions (device pointers).  Rows 2s and
@@ -561,6 +570,17 @@ typedef struct mtt_b200_main_decoder_batch {
   int32_t* status;             /* [n] out: 0; 1 for a position or text length out of range
                                   (nothing written for the session); 2 when a cache copy did
                                   not complete within its bounded wait (outputs unreliable) */
+  /* Optional [n][32] 32-bit words out (NULL: not computed): the Local AR's EOS
+   * projection of the hidden state this step produces (the Main Decoder
+   * final projection's guided logits reduced per position,
+   * plugins/local_ar_plugins.cu:1372-1432), computed right after the last
+   * layer on the tensor cores for every session: words [0, 16) the largest
+   * guided code logit of positions 0..15 as order-preserving keys, words
+   * [16, 32) the guided EOS logits (f32).  Pass it to the frame as
+   * mtt_b200_stream_batch_t.eos_projection.  Needs weights final_w / final_b. */
+  void* eos_projection;
+  float eos_cfg_scale;         /* CFG scale of the guided logits (the reference: 2.5) */
+  int32_t reserved_1;
 } mtt_b200_main_decoder_batch_t;
 
 /* Workspace bytes for up to max_sessions sessions (0 for bad arguments). */
@@ -600,6 +620,19 @@ MTT_B200_API int mtt_b200_launch_test_log(const float* x, float* out, size_t cou
  * partial[splits][rows][n] instead of Y (Y untouched).  n a multiple of 128,
  * k of 64 * splits; X, W, Y, partial 16-byte aligned device pointers.
  * Returns MTT_B200_STATUS_*. */
+/* Measurement hooks (no reference counterpart).  cycles[c] of CTA c, 0 when
+ * a bounded wait gave up.
+ * umma_cycles: SM cycles for n_mma back-to-back tcgen05.mma kind::f16 of
+ *   M = 128, N = n (16..256, multiple of 16), K = 16 into `accumulators`
+ *   TMEM accumulators (accumulators * n <= 512), on `ctas` CTAs.
+ * dsmem_cycles: SM cycles for `rounds` rounds in which every CTA of an 8-CTA
+ *   cluster bulk-copies bytes_per_peer (16..16384, multiple of 16) of its
+ *   shared memory into each of its 7 peers', on `clusters` clusters. */
+MTT_B200_API int mtt_b200_test_umma_cycles(int32_t n, int32_t accumulators, int32_t n_mma, int32_t ctas,
+                                           uint64_t* cycles, void* stream);
+MTT_B200_API int mtt_b200_test_dsmem_cycles(int32_t bytes_per_peer, int32_t rounds, int32_t clusters,
+                                            uint64_t* cycles, void* stream);
+
 MTT_B200_API int mtt_b200_launch_test_gemm(const void* x_bf16, const void* w_bf16, void* y_bf16, int32_t rows,
                                            int32_t n, int32_t k, int32_t gelu, int32_t splits, float* partial,
                                            void* stream);

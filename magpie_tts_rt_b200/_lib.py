@@ -116,7 +116,7 @@ class StreamBatch(ctypes.Structure):
         ("invalid_rows", P), ("end_frame_index", P), ("next_embedding", P),
         ("forced_tokens", P), ("logits_out", P),
         ("codec_frames_stride", I32), ("codec_frame_offset", I32), ("finished_latch", P),
-        ("codec_frames", P),
+        ("codec_frames", P), ("eos_projection", P),
     ]
 
 
@@ -140,7 +140,8 @@ class AlignmentBatch(ctypes.Structure):
 
 class MainDecoderWeights(ctypes.Structure):
     _fields_ = [(n, P) for n in ("pos", "ln_self", "qkv", "o", "ln_xq", "xq", "xo", "ln_ff", "ffn1", "ffn2",
-                                 "norm_out")] + [("n_layers", I32), ("pos_rows", I32)]
+                                 "norm_out")] + [("n_layers", I32), ("pos_rows", I32), ("final_w", P),
+                                                 ("final_b", P)]
 
 
 class MainDecoderBatch(ctypes.Structure):
@@ -148,7 +149,8 @@ class MainDecoderBatch(ctypes.Structure):
         ("n_sessions", I32), ("cache_capacity", I32), ("token_stride", I32), ("reserved_0", I32),
         ("embedded", P), ("position", P), ("text_length", P), ("active", P), ("self_k", P), ("self_v", P),
         ("self_mask", P), ("cross_k", P), ("cross_v", P), ("cond_mask", P), ("prior", P), ("hidden", P),
-        ("alignment", P), ("status", P),
+        ("alignment", P), ("status", P), ("eos_projection", P), ("eos_cfg_scale", ctypes.c_float),
+        ("reserved_1", I32),
     ]
 
 
@@ -185,6 +187,8 @@ SIGNATURES = {
     "mtt_b200_launch_test_clamped_gumbel": (I32, [P, P, SZ, P]),
     "mtt_b200_launch_test_log": (I32, [P, P, SZ, P]),
     "mtt_b200_launch_test_gemm": (I32, [P, P, P, I32, I32, I32, I32, I32, P, P]),
+    "mtt_b200_test_umma_cycles": (I32, [I32, I32, I32, I32, P, P]),
+    "mtt_b200_test_dsmem_cycles": (I32, [I32, I32, I32, P, P]),
 }
 
 

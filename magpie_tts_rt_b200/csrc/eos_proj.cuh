@@ -69,8 +69,9 @@ struct EosProjArgs {
   const __nv_bfloat16* bias;     // [16 x 2024]
   float cfg_scale;               // 1 without CFG
   __nv_bfloat16* rows;           // scratch: [2 n_max][768], 16-byte aligned
-  uint32_t* max_key;             // out [slot][16]
-  float* eos_logit;              // out [slot][16]
+  uint32_t* max_key;             // out [slot][16], slot stride proj_stride
+  float* eos_logit;              // out [slot][16], slot stride proj_stride
+  int proj_stride;               // 32-bit words between consecutive slots (16: separate arrays)
   int32_t* status;               // out: set to 1 when a bounded wait of the GEMM gave up (zeroed here)
 };
 

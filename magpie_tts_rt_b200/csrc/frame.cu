@@ -399,13 +399,11 @@ __global__ void __launch_bounds__(256) frame_end_kernel(Frame f) {
       f.codec_tokens[codec_index(f, s, p)] = tok[p];
     }
     const int slot = f.eos_slot[s];
-    const uint32_t* mk =
-        reinterpret_cast<const uint32_t*>(f.eos_partial) + static_cast<int64_t>(slot < 0 ? 0 : slot) * kPositions;
-    const float* el = f.eos_logit + static_cast<int64_t>(slot < 0 ? 0 : slot) * kPositions;
-    commit_end(f, s, eos_decide_proj(mk, el, tok, slot >= 0, f.finished[s]));
+    const int e = slot < 0 ? 0 : slot;
+    commit_end(f, s, eos_decide_proj(eos_keys(f, s, e), eos_logits(f, s, e), tok, slot >= 0, f.finished[s]));
     f.counter_io[s] = f.ctr[s];
     // a projection whose bounded waits gave up marks its sessions invalid (bit 4)
-    f.invalid_rows[s] = f.inv[s] | (slot >= 0 && f.eos_count[1] != 0 ? 16 : 0);
+    f.invalid_rows[s] = f.inv[s] | (slot >= 0 && f.eos_pre == nullptr && f.eos_count[1] != 0 ? 16 : 0);
   }
   const float* acc = f.emb_acc + static_cast<int64_t>(s) * kEmbed;
   for (int k = threadIdx.x; k < kEmbed; k += blockDim.x) {
@@ -631,6 +629,7 @@ extern "C" MTT_B200_API int mtt_b200_launch_local_ar_frame(const mtt_b200_local_
   f.next_emb = static_cast<bf16*>(b->next_embedding);
   f.forced = b->forced_tokens;
   f.logits_out = static_cast<bf16*>(b->logits_out);
+  f.eos_pre = static_cast<const uint32_t*>(b->eos_projection);
   char* ws = static_cast<char*>(workspace);
   f.list = reinterpret_cast<int32_t*>(ws + lo.list);
   f.count = reinterpret_cast<int32_t*>(ws + lo.count);
@@ -693,7 +692,7 @@ extern "C" MTT_B200_API int mtt_b200_launch_local_ar_frame(const mtt_b200_local_
                                    f.head_b + static_cast<int64_t>(p) * kVocab);
     sample_kernel<<<f.n, kSampleThreads, 0, st>>>(f, p);
   }
-  if (f.final_w != nullptr && launch_eos_projection(frame_eos_args(f), st) != cudaSuccess) {
+  if (f.final_w != nullptr && f.eos_pre == nullptr && launch_eos_projection(frame_eos_args(f), st) != cudaSuccess) {
     return MTT_B200_STATUS_CUDA_ERROR;
   }
   frame_end_kernel<<<f.n, 256, 0, st>>>(f);

@@ -32,6 +32,7 @@ struct Frame {
   bf16* next_emb;
   const int64_t* forced;
   bf16* logits_out;
+  const uint32_t* eos_pre;  // optional [n][32]: the EOS projection from the Main Decoder step
   // workspace
   int32_t *list, *count, *eos_list, *eos_count, *eos_slot;
   bf16 *x, *q, *kc, *vc, *att, *h, *logits;
@@ -134,6 +135,18 @@ cudaError_t launch_frame_eos(const Frame& f, cudaStream_t stream);
 // The projection arguments of a frame: the registered sessions' rows, the
 // maxima in eos_partial (as keys), the EOS logits in eos_logit.
 EosProjArgs frame_eos_args(const Frame& f);
+
+// The EOS projection of session s (registered in slot e): the frame's own
+// (slot arrays) or the one the Main Decoder step computed (eos_pre).
+__device__ __forceinline__ const uint32_t* eos_keys(const Frame& f, int s, int e) {
+  return f.eos_pre != nullptr ? f.eos_pre + static_cast<int64_t>(s) * 2 * kPositions
+                              : reinterpret_cast<const uint32_t*>(f.eos_partial) + static_cast<int64_t>(e) * kPositions;
+}
+__device__ __forceinline__ const float* eos_logits(const Frame& f, int s, int e) {
+  return f.eos_pre != nullptr ? reinterpret_cast<const float*>(f.eos_pre + static_cast<int64_t>(s) * 2 * kPositions) +
+                                    kPositions
+                              : f.eos_logit + static_cast<int64_t>(e) * kPositions;
+}
 
 // 2D bf16 tensor map over a row-major [rows][cols] matrix, box 64 columns x
 // box_rows rows, 128-byte swizzle (false if the driver entry point is missing).

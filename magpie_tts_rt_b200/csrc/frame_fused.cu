@@ -699,13 +699,10 @@ __global__ void __cluster_dims__(kCS, 1, 1) __launch_bounds__(kThreads, 1)
 __global__ void __launch_bounds__(256) fused_eos_finish_kernel(Frame f) {
   wait_prior_grid();  // launched after the EOS projection with programmatic serialization
   const int count = *f.eos_count;
-  const bool failed = f.eos_count[1] != 0;
-  const uint32_t* max_key = reinterpret_cast<const uint32_t*>(f.eos_partial);
+  const bool failed = f.eos_pre == nullptr && f.eos_count[1] != 0;
   for (int e = threadIdx.x; e < count; e += blockDim.x) {
     const int s = f.eos_list[e];
-    const int32_t end = eos_decide_proj(max_key + static_cast<int64_t>(e) * kPositions,
-                                        f.eos_logit + static_cast<int64_t>(e) * kPositions, f.tokens + s * kPositions,
-                                        true, false);
+    const int32_t end = eos_decide_proj(eos_keys(f, s, e), eos_logits(f, s, e), f.tokens + s * kPositions, true, false);
     commit_end(f, s, end);
     if (failed) f.invalid_rows[s] |= 16;
   }
@@ -793,7 +790,9 @@ cudaError_t launch_fused_frame(const Frame& f, cudaStream_t stream) {
 
 cudaError_t launch_frame_eos(const Frame& f, cudaStream_t stream) {
   cudaError_t e = cudaSuccess;
-  if (f.final_w != nullptr) {  // without the projection no session was registered
+  // without the final projection no session was registered; with the Main
+  // Decoder's projection (eos_pre) there is nothing to compute here
+  if (f.final_w != nullptr && f.eos_pre == nullptr) {
     e = launch_eos_projection(frame_eos_args(f), stream);
     if (e != cudaSuccess) return e;
   }
@@ -816,6 +815,7 @@ EosProjArgs frame_eos_args(const Frame& f) {
   a.rows = f.logits;  // the phase kernels' logits scratch is free once the frame's positions are done
   a.max_key = reinterpret_cast<uint32_t*>(f.eos_partial);
   a.eos_logit = f.eos_logit;
+  a.proj_stride = kPositions;
   a.status = f.eos_count + 1;
   return a;
 }

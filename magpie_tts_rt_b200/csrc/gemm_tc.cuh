@@ -44,7 +44,9 @@ constexpr int kGemmThreads = 64 + 32 * kGemmEpiWarps;
 constexpr int kGemmKChunk = 64;  // K columns per stage: one 128-byte swizzle row of bf16
 
 struct GemmProblem {
-  int m_tiles;             // M / 128
+  int m_tiles;             // M / 128 (with m_rows_dev: the largest)
+  const int* m_rows_dev;   // optional device count: M = m_rows_scale * *m_rows_dev
+  int m_rows_scale;
   int n_rows;              // N when n_rows_dev is null, else the largest N (grid sizing)
   const int* n_rows_dev;   // optional device count: N = n_rows_scale * *n_rows_dev
   int n_rows_scale;
@@ -88,6 +90,17 @@ __device__ __forceinline__ void tmem_ld32(uint32_t (&v)[32], uint32_t taddr) {
 }
 
 __device__ __forceinline__ int gemm_epi_warp() { return (static_cast<int>(threadIdx.x) >> 5) - 2; }
+__device__ __forceinline__ void gemm_epi_sync() {
+  asm volatile("bar.sync 1, %0;" ::"n"(32 * kGemmEpiWarps) : "memory");
+}
+template <class Epi, class = void>
+struct EpiHasTileEnd {
+  static constexpr bool value = false;
+};
+template <class Epi>
+struct EpiHasTileEnd<Epi, decltype(void(Epi::kTileEnd))> {
+  static constexpr bool value = Epi::kTileEnd;
+};
 
 __device__ __forceinline__ int gemm_n_rows(const GemmProblem& pr) {
   return pr.n_rows_dev != nullptr ? pr.n_rows_scale * *pr.n_rows_dev : pr.n_rows;
@@ -97,7 +110,12 @@ __device__ __forceinline__ int gemm_n_rows(const GemmProblem& pr) {
 //   __device__ void chunk(int m, int n0, int ks, const uint32_t (&v)[32], int n_rows) const;
 // called by every lane of an epilogue warp together (warp-uniform n0): lane
 // holds D[m][n0 + j] (f32 bits) of its row m for j < 32; columns at or past
-// n_rows are padding.  gemm_epi_warp() (0..7) names the calling warp.
+// n_rows are padding.  gemm_epi_warp() (0..7) names the calling warp.  With
+// `static constexpr bool kTileEnd = true` it also has
+//   __device__ void tile_begin(int mt, int nt) const;  __device__ void tile_end(int mt, int nt, int n_rows) const;
+// called by all epilogue threads before the first and after the last chunk
+// of each tile, between barriers of the epilogue warps (for per-tile
+// reductions in shared memory).
 template <int BN, class Epi>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CUtensorMap bmap,
@@ -146,19 +164,19 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   // it waits for this grid's completion before reading what it wrote.
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
-  auto decode = [&](int i, int n_tiles_, int& mt, int& nt, int& ks) {
+  auto decode = [&](int i, int n_tiles_, int m_tiles_, int& mt, int& nt, int& ks) {
     nt = i % n_tiles_;
     const int rest = i / n_tiles_;
-    mt = rest % pr.m_tiles;
-    ks = rest / pr.m_tiles;
+    mt = rest % m_tiles_;
+    ks = rest / m_tiles_;
   };
   // Stages whose constant B box was issued before the wait (first tile only).
   int pre = 0;
-  if (warp == 0 && lane == 0 && pr.b_constant && pr.n_rows_dev == nullptr) {
+  if (warp == 0 && lane == 0 && pr.b_constant && pr.n_rows_dev == nullptr && pr.m_rows_dev == nullptr) {
     const int n_tiles0 = (pr.n_rows + BN - 1) / BN;
     if (static_cast<int>(blockIdx.x) < pr.m_tiles * n_tiles0 * pr.splits) {
       int mt, nt, ks;
-      decode(blockIdx.x, n_tiles0, mt, nt, ks);
+      decode(blockIdx.x, n_tiles0, pr.m_tiles, mt, nt, ks);
       pre = pr.k_chunks < S ? pr.k_chunks : S;
       for (int kc = 0; kc < pre; ++kc) {
         unsigned char* sa = ring + static_cast<size_t>(kc) * G::kStageBytes;
@@ -169,17 +187,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
   }
 
-  wait_prior_grid();  // inputs (and the device row count) of the previous launch
+  wait_prior_grid();  // inputs (and the device row counts) of the previous launch
   const int n_rows = gemm_n_rows(pr);
   const int n_tiles = (n_rows + BN - 1) / BN;
-  const int items = pr.m_tiles * n_tiles * pr.splits;  // a CTA past the work only frees its tensor memory
+  const int m_tiles = pr.m_rows_dev != nullptr ? (pr.m_rows_scale * *pr.m_rows_dev + 127) / 128 : pr.m_tiles;
+  const int items = m_tiles * n_tiles * pr.splits;  // a CTA past the work only frees its tensor memory
 
   if (warp == 0) {
     if (lane == 0) {
       int it = 0;
       for (int i = blockIdx.x; i < items && *errv == 0; i += gridDim.x) {
         int mt, nt, ks;
-        decode(i, n_tiles, mt, nt, ks);
+        decode(i, n_tiles, m_tiles, mt, nt, ks);
         for (int kc = 0; kc < pr.k_chunks; ++kc, ++it) {
           const int s = it % S;
           if (it >= S && !mbar_wait(&empty[s], ((it / S) - 1) & 1)) *errv = 1;
@@ -247,7 +266,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
       tmem_fence_after_sync();
       int mt, nt, ks;
-      decode(i, n_tiles, mt, nt, ks);
+      decode(i, n_tiles, m_tiles, mt, nt, ks);
+      if constexpr (EpiHasTileEnd<Epi>::value) {
+        epi.tile_begin(mt, nt);
+        gemm_epi_sync();
+      }
       const int m = mt * 128 + 32 * q + lane;
       const uint32_t ta = tmem + (static_cast<uint32_t>(32 * q) << 16) + static_cast<uint32_t>(buf * BN);
 #pragma unroll 1
@@ -261,6 +284,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       tmem_fence_before_sync();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[buf]);
+      if constexpr (EpiHasTileEnd<Epi>::value) {
+        gemm_epi_sync();
+        epi.tile_end(mt, nt, n_rows);
+        gemm_epi_sync();
+      }
     }
   }
   tmem_fence_before_sync();

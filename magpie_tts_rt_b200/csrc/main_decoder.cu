@@ -36,6 +36,7 @@
 
 #include "../../include/magpie_tts_rt_b200.h"
 #include "common.cuh"
+#include "eos_proj.cuh"
 #include "gemm_tc.cuh"
 
 namespace mtt {
@@ -584,6 +585,16 @@ __global__ void __launch_bounds__(kXAThreads) cross_attn_kernel(Step st, int l, 
 // GEMM epilogues (gemm_tc.cuh): lane = output feature m, columns = rows n
 // ---------------------------------------------------------------------------
 
+// The EOS projection's bounded waits gave up: its outputs are unreliable, as
+// a cache copy that timed out would make them (status 2).
+__global__ void eos_status_kernel(Step st, const int32_t* eos_status) {
+  wait_prior_grid();
+  if (*eos_status == 0) return;
+  for (int s = blockIdx.x * blockDim.x + threadIdx.x; s < st.n; s += gridDim.x * blockDim.x) {
+    if (session_live(st, s)) st.status[s] = 2;
+  }
+}
+
 // The projection GEMMs put the activation rows on the MMA's M side (128 per
 // tile) and the output features on its N side (256 per tile; 128 for the
 // 128-wide cross-attention query): a tcgen05.mma of M = 128, K = 16 costs the
@@ -714,6 +725,8 @@ bool tc_gemm(const bf16* X, const bf16* W, bf16* C, int rows, int N, int K, bool
   }
   GemmProblem pr;
   pr.m_tiles = (rows + 127) / 128;
+  pr.m_rows_dev = nullptr;
+  pr.m_rows_scale = 1;
   pr.n_rows = N;
   pr.n_rows_dev = nullptr;
   pr.n_rows_scale = 1;
@@ -733,7 +746,7 @@ bool tc_gemm(const bf16* X, const bf16* W, bf16* C, int rows, int N, int K, bool
 }
 
 struct MdLayout {
-  size_t x, ln, qkv, att, o, xq, ctx, h, align, part, total;
+  size_t x, ln, qkv, att, o, xq, ctx, h, align, part, eos_status, total;
 };
 
 MdLayout md_layout(int n, int S) {
@@ -755,6 +768,7 @@ MdLayout md_layout(int n, int S) {
   lo.h = take(rows * kFF * 2);
   lo.align = take((kAlignSlots - 1) * rows * S * 2);
   lo.part = take(static_cast<size_t>(kMaxSplits) * rows * kW * 4);
+  lo.eos_status = take(4);
   lo.total = off;
   return lo;
 }
@@ -793,6 +807,10 @@ extern "C" MTT_B200_API int mtt_b200_launch_main_decoder_step(const mtt_b200_mai
   }
   if (!b->embedded || !b->position || !b->text_length || !b->self_k || !b->self_v || !b->self_mask || !b->cross_k ||
       !b->cross_v || !b->cond_mask || !b->prior || !b->hidden || !b->alignment || !b->status) {
+    return MTT_B200_STATUS_INVALID_ARGUMENT;
+  }
+  if (b->eos_projection != nullptr && (w->final_w == nullptr || w->final_b == nullptr || !aligned16(w->final_w) ||
+                                      !aligned16(b->eos_projection))) {
     return MTT_B200_STATUS_INVALID_ARGUMENT;
   }
   const void* vec[] = {b->embedded, b->self_k, b->self_v, b->cross_k, b->cross_v, b->hidden, w->pos, w->ln_self,
@@ -886,6 +904,30 @@ extern "C" MTT_B200_API int mtt_b200_launch_main_decoder_step(const mtt_b200_mai
                             last ? st.norm_out : layer_w(st.ln_self, kW, l + 1), last ? st.hidden : st.ln,
                             kFfn2Splits);
     if (!ok) return MTT_B200_STATUS_CUDA_ERROR;
+  }
+  if (b->eos_projection != nullptr) {
+    // The Local AR's EOS projection of the hidden state just produced, for
+    // every session, on the tensor cores (eos_proj.cuh); the LN buffer is free.
+    EosProjArgs ea;
+    ea.hidden = st.hidden;
+    ea.hidden_stream_stride = 2 * static_cast<int64_t>(kW);
+    ea.uncond_offset = kW;
+    ea.list = nullptr;
+    ea.count = nullptr;
+    ea.n_max = st.n;
+    ea.weight = static_cast<const bf16*>(w->final_w);
+    ea.bias = static_cast<const bf16*>(w->final_b);
+    ea.cfg_scale = b->eos_cfg_scale;
+    ea.rows = st.ln;
+    ea.max_key = static_cast<uint32_t*>(b->eos_projection);
+    ea.eos_logit = static_cast<float*>(b->eos_projection) + kPositions;
+    ea.proj_stride = 2 * kPositions;
+    ea.status = reinterpret_cast<int32_t*>(ws + lo.eos_status);
+    if (launch_eos_projection(ea, cs) != cudaSuccess ||
+        !launch_after(eos_status_kernel, dim3((st.n + 255) / 256), 256, 0, cs, st,
+                      static_cast<const int32_t*>(ea.status))) {
+      return MTT_B200_STATUS_CUDA_ERROR;
+    }
   }
   return cudaPeekAtLastError() == cudaSuccess ? MTT_B200_STATUS_OK : MTT_B200_STATUS_CUDA_ERROR;
 }

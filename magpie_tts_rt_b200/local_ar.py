@@ -133,6 +133,9 @@ class StreamBatch:
     codec_frame_offset: int = 0
     finished_latch: Optional[torch.Tensor] = None  # [n] bool, may be `finished`
     codec_frames: Optional[torch.Tensor] = None  # [n] int32: audio frames in the aggregate so far
+    # [n, 32] int32 from the Main Decoder step that produced decoder_hidden
+    # (MainDecoderBatch.eos_projection): the frame skips its own EOS projection
+    eos_projection: Optional[torch.Tensor] = None
 
     @property
     def n(self) -> int:
@@ -165,6 +168,7 @@ class StreamBatch:
         b.codec_frame_offset = self.codec_frame_offset
         b.finished_latch = self.finished_latch.data_ptr() if self.finished_latch is not None else None
         b.codec_frames = self.codec_frames.data_ptr() if self.codec_frames is not None else None
+        b.eos_projection = self.eos_projection.data_ptr() if self.eos_projection is not None else None
         return b
 
 

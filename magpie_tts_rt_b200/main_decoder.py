@@ -115,6 +115,11 @@ class MainDecoderBatch:
     alignment: torch.Tensor    # [n, 2, S] bf16 out
     status: torch.Tensor       # [n] int32 out
     active: Optional[torch.Tensor] = None
+    # optional [n, 32] int32 out: the Local AR's EOS projection of `hidden`
+    # (needs the engine's final projection); hand it to the frame's
+    # StreamBatch.eos_projection
+    eos_projection: Optional[torch.Tensor] = None
+    eos_cfg_scale: float = 2.5
 
     @property
     def n(self) -> int:
@@ -151,6 +156,8 @@ class MainDecoderBatch:
                   "cond_mask", "prior", "hidden", "alignment", "status"):
             setattr(b, f, getattr(self, f).data_ptr())
         b.active = self.active.data_ptr() if self.active is not None else None
+        b.eos_projection = self.eos_projection.data_ptr() if self.eos_projection is not None else None
+        b.eos_cfg_scale = float(self.eos_cfg_scale)
         return b
 
 
@@ -159,13 +166,20 @@ class MainDecoderEngine:
     ``max_sessions`` sessions; ``step(batch)`` enqueues one decoder position
     for every session on the current (or given) CUDA stream."""
 
-    def __init__(self, weights: MainDecoderWeights, max_sessions: int, token_stride: int = 128, device="cuda"):
+    def __init__(self, weights: MainDecoderWeights, max_sessions: int, token_stride: int = 128, device="cuda",
+                 final_w: Optional[torch.Tensor] = None, final_b: Optional[torch.Tensor] = None):
+        """final_w / final_b ([16 x 2024, 768] / [16 x 2024] bf16): the final
+        projection, needed only for batches that ask for eos_projection."""
         from magpie_tts_rt_b200 import _lib as L
         self.device = torch.device(device)
         self.dev = weights.to(device=self.device, dtype=torch.bfloat16)
         self._w = L.MainDecoderWeights()
         for name, t in self.dev.tensors():
             setattr(self._w, name, t.data_ptr())
+        self.final_w = final_w.to(self.device, torch.bfloat16).contiguous() if final_w is not None else None
+        self.final_b = final_b.to(self.device, torch.bfloat16).contiguous() if final_b is not None else None
+        self._w.final_w = self.final_w.data_ptr() if self.final_w is not None else None
+        self._w.final_b = self.final_b.data_ptr() if self.final_b is not None else None
         self._w.n_layers = int(self.dev.qkv.shape[0])
         self._w.pos_rows = int(self.dev.pos.shape[0])
         self.max_sessions = max_sessions

@@ -280,3 +280,70 @@ def test_decoder_loop_graph_replay_matches_eager():
     assert int(e_db.position[0]) == 220 + 5
     assert int(e_fb.invalid_rows.sum()) == 0 and int((e_db.status != 0).sum()) == 0
     del cuda_graph
+
+
+def _key_value(keys):
+    """Order-preserving 32-bit keys (0: none) back to floats."""
+    k = keys.astype(np.uint32)
+    neg = (k & 0x80000000) == 0
+    bits = np.where(neg, ~k, k & 0x7FFFFFFF).astype(np.uint32)
+    vals = bits.view(np.float32).copy()
+    vals[k == 0] = -np.inf
+    return vals
+
+
+def test_eos_projection_in_the_decoder_step(golden_engine):
+    """The EOS projection folded into the decoder step (the reference runs it
+    as a per-session GEMV inside the Local AR step, local_ar_plugins.cu:
+    1372-1432, on the hidden state the decoder has just produced): for every
+    session the step leaves the largest guided code logit and the guided EOS
+    logit of each position.  They match the C oracle's guided logits of the
+    step's own hidden state within one bf16 rounding (the 768-long dot
+    products are summed in another order), and a frame handed this
+    projection decides EOS exactly as a frame that computes its own."""
+    from magpie_tts_rt_b200.local_ar import LocalArEngine, StreamBatch
+    from magpie_tts_rt_b200.model import POSITIONS, SHAPE_BASELINE, VOCAB, make_weights
+    from oracle import sampler as S
+    z, w, _ = golden_engine
+    cap = int(z["cap"])
+    lw = make_weights(SHAPE_BASELINE, seed=41, profile="parity", with_final=True)
+    fbias = lw.final_b.view(POSITIONS, VOCAB)
+    fbias[:8, S.EOS_ID] += 4.0
+    fbias[8:, S.EOS_ID] += 4.5
+    eng = MainDecoderEngine(w, max_sessions=8, token_stride=512, final_w=lw.final_w, final_b=lw.final_b)
+    n = 6
+    rng = np.random.default_rng(17)
+    b = MainDecoderBatch.allocate(n, cap=cap, token_stride=512)
+    for s in range(n):
+        load_session(b, s, OMD.make_step_inputs(300 + s, int(rng.integers(8, 200)), int(rng.integers(0, cap)), cap))
+    b.eos_projection = torch.zeros(n, 32, dtype=torch.int32, device="cuda")
+    eng.step(b)
+    torch.cuda.synchronize()
+    assert (b.status.cpu() == 0).all()
+    bits = lambda t: t.contiguous().view(torch.int16).cpu().numpy().view(np.uint16)
+    proj = b.eos_projection.cpu().numpy().view(np.uint32)
+    got_max, got_eos = _key_value(proj[:, :16]), proj[:, 16:].copy().view(np.float32)
+    fw, fb = bits(lw.final_w), bits(lw.final_b)
+    exact = 0
+    for s in range(n):
+        guided = S.eos_guided(bits(b.hidden[s]), fw, fb, 2.5)
+        exp_max, exp_eos = guided[:, :2016].max(axis=1), guided[:, 2016]
+        for got, exp in ((got_max[s], exp_max), (got_eos[s], exp_eos)):
+            assert np.all(np.abs(got - exp) <= 2.0 ** -7 * np.abs(exp) + 1e-6), (s, got, exp)
+            exact += int(np.sum(got == exp))
+    assert exact >= 0.9 * 2 * n * POSITIONS
+    # the frame with the decoder's projection decides as the frame with its own
+    leng = LocalArEngine(lw, max_streams=n)
+    out = []
+    for pre in (b.eos_projection, None):
+        fbatch = StreamBatch.allocate(n)
+        fbatch.decoder_hidden.copy_(b.hidden)
+        fbatch.rng_seed.copy_(torch.arange(n) + 5)
+        fbatch.eos_projection = pre
+        leng.frame(fbatch)
+        torch.cuda.synchronize()
+        out.append((fbatch.end_frame_index.cpu().clone(), fbatch.codec_tokens.cpu().clone(),
+                    fbatch.invalid_rows.cpu().clone()))
+    assert torch.equal(out[0][1], out[1][1]) and torch.equal(out[0][2], out[1][2])
+    assert torch.equal(out[0][0], out[1][0]), (out[0][0], out[1][0])
+    assert (out[0][2] == 0).all()
