@@ -25,6 +25,20 @@ NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 COMMON = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC,-fvisibility=hidden",
           "-I" + os.path.join(REPO, "include"), "--expt-relaxed-constexpr"]
+# TensorRT (optional): with NvInfer.h found, trt_plugins.cpp's IPluginV3
+# creators are compiled in and register_plugins registers them; without it
+# (this image) register_plugins reports REGISTRY_UNAVAILABLE.
+TENSORRT_DIRS = [d for d in (os.environ.get("TENSORRT_ROOT", ""), "/usr", "/usr/local/tensorrt") if d]
+
+
+def tensorrt():
+    for root in TENSORRT_DIRS:
+        for inc in (os.path.join(root, "include"), os.path.join(root, "include", "x86_64-linux-gnu")):
+            if os.path.exists(os.path.join(inc, "NvInfer.h")):
+                return inc, os.path.join(root, "lib")
+    return None
+
+
 VERSION_SCRIPT = """{
   global:
     mtt_*;
@@ -65,6 +79,9 @@ def build(force: bool = False, verbose_ptxas: bool = False) -> str:
         for o in glob.glob(os.path.join(BUILD, "*.o")):
             os.remove(o)
     extra = ["-Xptxas", "-v"] if verbose_ptxas else []
+    trt = tensorrt()
+    if trt is not None:
+        extra += ["-DMTT_B200_WITH_TENSORRT", "-I" + trt[0]]
     srcs = sources()
     with ThreadPoolExecutor(max_workers=min(8, len(srcs))) as pool:
         objs = list(pool.map(lambda s: _compile(s, extra), srcs))
@@ -75,7 +92,7 @@ def build(force: bool = False, verbose_ptxas: bool = False) -> str:
         cuda_lib = os.path.join(os.path.dirname(os.path.dirname(NVCC)), "lib64")
         cmd = [NVCC] + ARCH + ["-shared", "-cudart", "static", "-o", LIBRARY] + objs + [
             "-L" + cuda_lib, "-Xlinker", "-rpath," + cuda_lib,
-            "-Xlinker", "--version-script=" + vs]
+            "-Xlinker", "--version-script=" + vs] + (["-L" + trt[1], "-lnvinfer"] if trt is not None else [])
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")

@@ -6,10 +6,12 @@
 // contract and are therefore the same as the reference's
 // (include/magpie_tts_rt/magpie_tts_rt_plugin.h, docs/engine-contracts.md:247-250).
 //
-// This build has no TensorRT (NvInfer.h is absent), so the IPluginV3 creator
-// shells are not compiled and register_plugins reports that no plugin
-// registry is available.  The kernels behind the five creators are exported
-// directly as the mtt_b200_launch_* C functions.
+// register_plugins registers the five IPluginV3 creators of trt_plugins.cpp
+// (one generic plugin over the contracts of plugin_contract.cpp) into
+// TensorRT's process-wide registry when the library is built against
+// TensorRT (MTT_B200_WITH_TENSORRT); otherwise it reports that no plugin
+// registry is available, and the kernels behind the five creators are
+// reached directly through the mtt_b200_launch_* C functions.
 #include <cstring>
 
 #include "../../include/magpie_tts_rt_b200.h"
@@ -22,7 +24,18 @@ constexpr const char* kCreatorNames[MTT_PLUGIN_CREATOR_COUNT_V1] = {
     "MagpieLocalARSampling", "MagpieLocalAREos", "MagpieLayerNorm", "MagpieGeluTanh", "MagpieSoftmax",
 };
 
-mtt_plugin_status_t register_plugins_unavailable() { return MTT_PLUGIN_STATUS_REGISTRY_UNAVAILABLE; }
+#if defined(MTT_B200_WITH_TENSORRT)
+}  // namespace
+namespace mtt {
+namespace plugin {
+mtt_plugin_status_t register_tensorrt_plugins() noexcept;
+}  // namespace plugin
+}  // namespace mtt
+namespace {
+mtt_plugin_status_t register_plugins_entry() { return mtt::plugin::register_tensorrt_plugins(); }
+#else
+mtt_plugin_status_t register_plugins_entry() { return MTT_PLUGIN_STATUS_REGISTRY_UNAVAILABLE; }
+#endif
 
 void fill_creator(mtt_plugin_creator_v1_t& creator, const char* name) {
   creator.struct_size = sizeof(creator);
@@ -43,7 +56,7 @@ extern "C" MTT_B200_API mtt_plugin_status_t mtt_plugin_get_api_v1(mtt_plugin_api
   populated.struct_size = sizeof(populated);
   populated.abi_version = MTT_PLUGIN_ABI_VERSION_1;
   populated.creator_count = MTT_PLUGIN_CREATOR_COUNT_V1;
-  populated.register_plugins = &register_plugins_unavailable;
+  populated.register_plugins = &register_plugins_entry;
   for (unsigned i = 0; i < MTT_PLUGIN_CREATOR_COUNT_V1; ++i) fill_creator(populated.creators[i], kCreatorNames[i]);
   *api = populated;
   return MTT_PLUGIN_STATUS_OK;
