@@ -669,97 +669,65 @@ def main_decoder_measure(dev, peaks, n=256, steps=20, text=128, cap=467, seed=13
     return out
 
 
-def loop_measure(dev, peaks, n=256, steps=1024, text=128, seed=17, graph=True):
+def loop_measure(dev, peaks, n=256, steps=1024, text=128, seed=17):
     """Config 5: the full per-frame loop on the device for n sessions x CFG
-    pair per GPU, `steps` frames each.  One frame = Main Decoder step (cache
-    growing from position 0 to steps - 1, capacity = steps; 128 text states
-    ~N(0, 1)) -> alignment gate -> Local AR frame (16 positions, sampling,
-    EOS); the decoder's hidden state, the frame's embedding sum, the
+    pair per GPU, `steps` frames each, driven by the C++ session engine
+    (mtt_b200_session_engine_*): one frame = Main Decoder step (cache growing
+    from position 0 to steps - 1, capacity = steps; 128 text states ~N(0, 1))
+    -> alignment gate -> Local AR frame (16 positions, sampling, EOS) ->
+    position + 1, one CUDA graph per frame replayed by the engine on its own
+    stream; the decoder's hidden state, the frame's embedding sum, the
     alignment scores and the prior are shared buffers, so nothing crosses to
     the host inside the timed loop.  Random-init weights (decoder ~N(0, 0.02),
     Local AR as config 4).  Timed by CUDA events around the whole loop after a
-    3-frame warm-up (state reset afterwards).  With ``graph`` one frame step
-    (decoder step, gate, frame, position advance) is captured once as a CUDA
-    graph after the warm-up and replayed per frame, as a serving loop would run
-    it; the decoder and frame state advance on the device, so every replay is
-    the next frame."""
-    from magpie_tts_rt_b200.local_ar import AlignmentBatch, LocalArEngine, StreamBatch
-    from magpie_tts_rt_b200.main_decoder import MainDecoderBatch, MainDecoderEngine, make_main_decoder_weights
+    3-frame warm-up (every session re-opened afterwards)."""
+    from magpie_tts_rt_b200.local_ar import LocalArEngine
+    from magpie_tts_rt_b200.main_decoder import (CROSS_DIM, LAYERS, MainDecoderEngine, make_main_decoder_weights)
+    from magpie_tts_rt_b200.session_engine import SessionEngine
     cap = steps
     wd = make_main_decoder_weights(seed, positions=cap)
     dec = MainDecoderEngine(wd, max_sessions=n, token_stride=text, device=dev)
     wl = make_weights(SHAPE_BASELINE, seed=0, dtype=torch.bfloat16, profile="baseline", with_final=True)
     lar = LocalArEngine(wl, max_streams=n, device=dev)
-    db = MainDecoderBatch.allocate(n, cap=cap, token_stride=text, device=dev)
+    eng = SessionEngine(lar, n, text, decoder=dec, cache_capacity=cap)
     g = torch.Generator(device=dev).manual_seed(seed)
-    db.cross_k.normal_(generator=g)
-    db.cross_v.normal_(generator=g)
-    db.text_length.fill_(text)
-    db.cond_mask.fill_(True)
-    db.cond_mask[:, 1, 1:] = False
-    gate = AlignmentBatch.allocate([text] * n, token_stride=text, device=dev)
-    fb = StreamBatch.allocate(n, device=dev)
-    fb.rng_seed.copy_(torch.arange(n, device=dev))
-    fb.decoder_hidden = db.hidden
-    fb.next_embedding = db.embedded
-    gate.alignment_scores = db.alignment
-    gate.next_prior = db.prior
-
-    def reset():
-        db.position.zero_()
-        db.self_mask.zero_()
-        db.embedded.normal_(0, 0.05, generator=g)
-        db.prior.fill_(1.0)
-        gate.counters.zero_()
-        gate.last_attended.fill_(1)
-        gate.decoder_steps.zero_()
-        fb.finished.zero_()
-        fb.end_frame_index.fill_(-1)
-        fb.rng_counter.zero_()
-
-    def frame_step():
-        dec.step(db, stream=stream)
-        gate.gate(fb, stream=stream)
-        lar.frame(fb, stream=stream)
-        db.position += 1
-
-    stream = torch.cuda.Stream(dev)
-    with torch.cuda.stream(stream):
-        reset()
-        for _ in range(3):
-            frame_step()
-        reset()
+    cross_k = torch.randn(LAYERS, 2, text, CROSS_DIM, generator=g, device=dev).to(torch.bfloat16)
+    cross_v = torch.randn(LAYERS, 2, text, CROSS_DIM, generator=g, device=dev).to(torch.bfloat16)
+    cond = torch.ones(2, text, dtype=torch.bool, device=dev)
+    cond[1, 1:] = False
+    first = (torch.randn(n, EMBED, generator=g, device=dev) * 0.05).to(torch.bfloat16)
     torch.cuda.synchronize(dev)
-    cuda_graph = None
-    if graph:
-        # the library's one-time set-up (cuBLASLt handle and plans) ran in the warm-up
-        cuda_graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(cuda_graph, stream=stream):
-            frame_step()
-        torch.cuda.synchronize(dev)
+
+    def open_all():
+        for s in range(n):
+            eng.open(s, s, text, cross_k, cross_v, cond, first[s])
+
+    open_all()
+    for _ in range(3):  # eager step, then the captured graph
+        eng.step()
+    open_all()
+    stream = torch.cuda.ExternalStream(eng.stream_handle, device=dev)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with torch.cuda.stream(stream):
-        e0.record(stream)
-        for _ in range(steps):
-            if cuda_graph is not None:
-                cuda_graph.replay()
-            else:
-                frame_step()
-        e1.record(stream)
+    e0.record(stream)
+    for _ in range(steps):
+        eng.step()
+    e1.record(stream)
     torch.cuda.synchronize(dev)
     ms = e0.elapsed_time(e1)
-    bad = int((db.status != 0).sum().item()) + int((gate.invalid_state != 0).sum().item()) + \
-        int((fb.invalid_rows != 0).sum().item())
-    finished = int(fb.finished.sum().item())
+    codes, end, inv = eng.collect(n)
+    bad = int((inv != 0).sum())
+    finished = int(torch.from_numpy(end).ge(0).sum())
     launches = steps * (145 + 1 + lar.launch_count(n) + 1)
     out = {"workload": f"config 5 per GPU: {n} sessions x CFG pair, {steps} frames, decoder cache growing to "
                        f"{steps}, {text} text states; frame = Main Decoder step -> alignment gate -> Local AR "
                        f"frame, all on the device",
+           "driver": "C++ session engine (mtt_b200_session_engine_*), one CUDA graph per frame step",
            "frames_per_s": n * steps / (ms * 1e-3), "ms_per_frame_step": ms / steps, "total_s": ms * 1e-3,
-           "gpu_launches": launches, "cuda_graph_per_frame": graph,
+           "gpu_launches": launches, "cuda_graph_per_frame": True,
            "local_ar_path": PATH_NAMES.get(lar.path_for(n), str(lar.path_for(n))),
-           "sessions_finished": finished, "invalid": bad}
-    del cuda_graph, db, gate, fb, dec, lar
+           "sessions_ended_last_frame": finished, "invalid": bad}
+    eng.close_engine()
+    del eng, dec, lar
     torch.cuda.empty_cache()
     return out
 

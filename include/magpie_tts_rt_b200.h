@@ -603,6 +603,99 @@ MTT_B200_API int mtt_b200_launch_main_decoder_step(const mtt_b200_main_decoder_w
                                                    size_t workspace_bytes, void* stream);
 
 /* ------------------------------------------------------------------------ */
+/* 6. Per-GPU session engine (the host side of the per-step loop)            */
+/* ------------------------------------------------------------------------ */
+
+/*
+ * Replaces, for up to max_sessions sessions on one GPU, the reference's
+ * per-session step sequence of SynthesisPipeline::run_local
+ * (src/runtime/synthesis_pipeline.cpp:511-569: a D2D copy of `unfinished`, an
+ * H2D copy of forbid_eos, the Local AR graph launch, finalize_local_step) and
+ * the per-session CUDA graphs of SessionResources
+ * (src/runtime/session_resources.cpp:661-684).  The engine owns every
+ * session's structure-of-arrays state on the device (RNG seed and counter,
+ * alignment counters and prior, EOS flags, codec tokens, decoder cache when
+ * with_decoder) and its own CUDA stream; one step is one replay of a CUDA
+ * graph captured on the engine's second step (the first runs the same
+ * launches one by one):
+ *   [Main Decoder step -> ]alignment gate -> Local AR frame[ -> position + 1]
+ * for every open session, with no host copy inside.  Sessions are opened and
+ * closed between steps by slot; a closed slot is skipped by every kernel.
+ * Weights are caller-owned device memory that must outlive the engine.
+ * Every function returns MTT_B200_STATUS_*; the engine is not thread-safe
+ * (one host thread drives one engine, as one request thread drives one
+ * reference session).
+ */
+typedef struct mtt_b200_session_engine mtt_b200_session_engine_t;
+
+typedef struct mtt_b200_session_engine_config {
+  int32_t max_sessions;
+  int32_t token_stride;      /* text tokens per row: a multiple of 8, <= 512 */
+  int32_t with_decoder;      /* 1: each step starts with the Main Decoder step */
+  int32_t cache_capacity;    /* decoder positions per session (with_decoder) */
+  /* the alignment contract (src/runtime/alignment_kernel.hpp:9-15) */
+  uint32_t ignored_terminal_tokens;
+  uint32_t short_text_no_prior_max_tokens;
+  uint32_t lookahead;
+  uint32_t sink_threshold;
+  mtt_b200_local_ar_shape_t shape;
+  mtt_b200_local_ar_weights_t local_ar;    /* device pointers (final_w / final_b for EOS) */
+  mtt_b200_sampling_config_t sampling;
+  mtt_b200_main_decoder_weights_t decoder; /* with_decoder */
+  /* Optional caller-owned device buffers (NULL: the engine allocates them):
+   * decoder_hidden [n][rows][768] bf16 (rows 2 with CFG), alignment_scores
+   * [n][2][S] bf16, next_embedding [n][768] bf16; 16-byte aligned. */
+  void* decoder_hidden;
+  void* alignment_scores;
+  void* next_embedding;
+} mtt_b200_session_engine_config_t;
+
+/* Device buffers of the engine, for the caller to fill or read on the
+ * engine's stream (sessions in slot order; rows 2s / 2s + 1). */
+typedef struct mtt_b200_session_engine_buffers {
+  void* stream;                 /* cudaStream_t of the engine */
+  void* decoder_hidden;         /* [n][2][768] bf16: the frame's input (written by the decoder
+                                   step with with_decoder, else by the caller before each step) */
+  void* alignment_scores;       /* [n][2][S] bf16: the gate's input (likewise) */
+  void* next_embedding;         /* [n][768] bf16: the frame's embedding sum (the decoder's next input) */
+  int64_t* codec_tokens;        /* [n][8][2] int64: the last step's tokens */
+  int32_t* end_frame_index;     /* [n] */
+  int32_t* invalid_rows;        /* [n] */
+  int64_t* rng_counter;         /* [n] */
+  bool* finished;               /* [n] */
+  int64_t* position;            /* [n] decoder positions (with_decoder) */
+  int32_t* decoder_status;      /* [n] (with_decoder) */
+} mtt_b200_session_engine_buffers_t;
+
+MTT_B200_API int mtt_b200_session_engine_create(const mtt_b200_session_engine_config_t* config,
+                                                mtt_b200_session_engine_t** engine);
+MTT_B200_API void mtt_b200_session_engine_destroy(mtt_b200_session_engine_t* engine);
+MTT_B200_API int mtt_b200_session_engine_buffers(const mtt_b200_session_engine_t* engine,
+                                                 mtt_b200_session_engine_buffers_t* buffers);
+
+/* Opens session `slot` (its state reset on the engine's stream): seed in
+ * [0, 2^32) (row 0 of a one-row request, docs/c-abi.md random_seed), text
+ * length 1..token_stride.  With the decoder: cross_k / cross_v [L][2][T][128]
+ * bf16 and cond_mask [2][T] bool (device pointers, the prefill's outputs; T =
+ * text_length) are copied into the slot, initial_embedding [768] bf16 (or
+ * NULL for zeros) is its first decoder input, its cache starts empty at
+ * position 0. */
+MTT_B200_API int mtt_b200_session_engine_open(mtt_b200_session_engine_t* engine, int32_t slot, int64_t seed,
+                                              uint32_t text_length, const void* cross_k, const void* cross_v,
+                                              const bool* cond_mask, const void* initial_embedding);
+MTT_B200_API int mtt_b200_session_engine_close(mtt_b200_session_engine_t* engine, int32_t slot);
+
+/* One step for every open session, enqueued on the engine's stream. */
+MTT_B200_API int mtt_b200_session_engine_step(mtt_b200_session_engine_t* engine);
+
+/* Copies the last step's codec tokens [n][8][2], end-frame indices [n] and
+ * invalid flags [n] of slots [0, n) to host memory (any pointer may be NULL)
+ * and waits for the engine's stream. */
+MTT_B200_API int mtt_b200_session_engine_collect(mtt_b200_session_engine_t* engine, int32_t n,
+                                                 int64_t* codec_tokens, int32_t* end_frame_index,
+                                                 int32_t* invalid_rows);
+
+/* ------------------------------------------------------------------------ */
 /* Test hooks (no reference counterpart beyond launch_test_clamped_gumbel,   */
 /* plugins/local_ar_plugins.hpp:171-175)                                      */
 /* ------------------------------------------------------------------------ */

@@ -154,6 +154,22 @@ class MainDecoderBatch(ctypes.Structure):
     ]
 
 
+class SessionEngineConfig(ctypes.Structure):
+    _fields_ = [
+        ("max_sessions", I32), ("token_stride", I32), ("with_decoder", I32), ("cache_capacity", I32),
+        ("ignored_terminal_tokens", ctypes.c_uint32), ("short_text_no_prior_max_tokens", ctypes.c_uint32),
+        ("lookahead", ctypes.c_uint32), ("sink_threshold", ctypes.c_uint32),
+        ("shape", Shape), ("local_ar", Weights), ("sampling", SamplingConfig), ("decoder", MainDecoderWeights),
+        ("decoder_hidden", P), ("alignment_scores", P), ("next_embedding", P),
+    ]
+
+
+class SessionEngineBuffers(ctypes.Structure):
+    _fields_ = [(n, P) for n in ("stream", "decoder_hidden", "alignment_scores", "next_embedding", "codec_tokens",
+                                 "end_frame_index", "invalid_rows", "rng_counter", "finished", "position",
+                                 "decoder_status")]
+
+
 # name -> (restype, argtypes)
 SIGNATURES = {
     "mtt_plugin_get_api_v1": (I32, [ctypes.POINTER(PluginApiV1)]),
@@ -189,6 +205,13 @@ SIGNATURES = {
     "mtt_b200_launch_test_gemm": (I32, [P, P, P, I32, I32, I32, I32, I32, P, P]),
     "mtt_b200_test_umma_cycles": (I32, [I32, I32, I32, I32, P, P]),
     "mtt_b200_test_dsmem_cycles": (I32, [I32, I32, I32, P, P]),
+    "mtt_b200_session_engine_create": (I32, [ctypes.POINTER(SessionEngineConfig), ctypes.POINTER(P)]),
+    "mtt_b200_session_engine_destroy": (None, [P]),
+    "mtt_b200_session_engine_buffers": (I32, [P, ctypes.POINTER(SessionEngineBuffers)]),
+    "mtt_b200_session_engine_open": (I32, [P, I32, ctypes.c_int64, ctypes.c_uint32, P, P, P, P]),
+    "mtt_b200_session_engine_close": (I32, [P, I32]),
+    "mtt_b200_session_engine_step": (I32, [P]),
+    "mtt_b200_session_engine_collect": (I32, [P, I32, P, P, P]),
 }
 
 

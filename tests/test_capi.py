@@ -142,3 +142,52 @@ def test_main_decoder_entry_without_a_gpu():
     w, b = L.MainDecoderWeights(), L.MainDecoderBatch()
     b.n_sessions, b.cache_capacity, b.token_stride, w.n_layers = 2, 467, 100, 12  # stride not a multiple of 8
     assert L.lib.mtt_b200_launch_main_decoder_step(ctypes.byref(w), ctypes.byref(b), None, 0, None) == -1
+
+
+def test_session_engine_argument_checks_without_a_gpu():
+    """Configuration checks decided before any CUDA call; without a device
+    the engine cannot be created (CUDA error), never a crash."""
+    h = ctypes.c_void_p()
+    cfg = L.SessionEngineConfig()
+    assert L.lib.mtt_b200_session_engine_create(ctypes.byref(cfg), ctypes.byref(h)) == -1  # no sessions
+    cfg.max_sessions, cfg.token_stride, cfg.lookahead, cfg.sink_threshold = 4, 100, 6, 4
+    assert L.lib.mtt_b200_session_engine_create(ctypes.byref(cfg), ctypes.byref(h)) == -1  # stride not x8
+    cfg.token_stride, cfg.with_decoder = 64, 1
+    assert L.lib.mtt_b200_session_engine_create(ctypes.byref(cfg), ctypes.byref(h)) == -1  # decoder w/o capacity
+    assert L.lib.mtt_b200_session_engine_create(ctypes.byref(cfg), None) == -1
+    assert L.lib.mtt_b200_session_engine_step(None) == -1
+    assert L.lib.mtt_b200_session_engine_open(None, 0, 1, 1, None, None, None, None) == -1
+    assert L.lib.mtt_b200_session_engine_collect(None, 0, None, None, None) == -1
+    L.lib.mtt_b200_session_engine_destroy(None)
+
+
+def test_struct_layouts_match_the_header(tmp_path):
+    """sizeof and offsetof of this library's C structs, measured with gcc on
+    include/magpie_tts_rt_b200.h, equal the ctypes mirrors'."""
+    import shutil
+    import subprocess
+    if shutil.which("gcc") is None:
+        pytest.skip("needs gcc")
+    mirrors = {"mtt_b200_stream_batch_t": L.StreamBatch, "mtt_b200_local_ar_weights_t": L.Weights,
+               "mtt_b200_sampling_config_t": L.SamplingConfig, "mtt_b200_alignment_batch_t": L.AlignmentBatch,
+               "mtt_b200_main_decoder_weights_t": L.MainDecoderWeights,
+               "mtt_b200_main_decoder_batch_t": L.MainDecoderBatch,
+               "mtt_b200_session_engine_config_t": L.SessionEngineConfig,
+               "mtt_b200_session_engine_buffers_t": L.SessionEngineBuffers}
+    lines = ['#include <stdio.h>', '#include <stddef.h>', '#include "magpie_tts_rt_b200.h"', 'int main(void) {']
+    for cname, py in mirrors.items():
+        lines.append(f'  printf("{cname} %zu\\n", sizeof({cname}));')
+        for fname, _ in py._fields_:
+            lines.append(f'  printf("{cname}.{fname} %zu\\n", offsetof({cname}, {fname}));')
+    lines += ['  return 0;', '}']
+    src = tmp_path / "layout.c"
+    src.write_text("\n".join(lines))
+    exe = tmp_path / "layout"
+    inc = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "include")
+    subprocess.run(["gcc", "-I", inc, str(src), "-o", str(exe)], check=True)
+    got = dict(line.rsplit(" ", 1) for line in subprocess.run([str(exe)], capture_output=True, text=True,
+                                                               check=True).stdout.splitlines())
+    for cname, py in mirrors.items():
+        assert int(got[cname]) == ctypes.sizeof(py), cname
+        for fname, _ in py._fields_:
+            assert int(got[f"{cname}.{fname}"]) == getattr(py, fname).offset, (cname, fname)
