@@ -52,7 +52,7 @@ sys.path.insert(0, REPO)
 import numpy as np  # noqa: E402
 import torch  # noqa: E402
 
-from magpie_tts_rt_b200.model import EMBED, SHAPE_BASELINE, make_weights  # noqa: E402
+from magpie_tts_rt_b200.model import EMBED, SHAPE_BASELINE, SHAPE_SOFIA, make_weights  # noqa: E402
 
 METRIC = "Local-AR+sampling frames/sec per GPU and box (1/2/4/8); p50 per-frame us"
 PATH_NAMES = {1: "phase kernels", 2: "fused cluster kernel", 3: "tile kernel", 4: "pair kernel",
@@ -87,6 +87,9 @@ def parse():
     ap.add_argument("--loop-only", action="store_true", help="run only the config-5 loop and print its object")
     ap.add_argument("--loop-steps", type=int, default=1024)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--r-shape-only", action="store_true",
+                    help="run only the d=768 / 2-layer Local AR frame measurement and print its object")
+    ap.add_argument("--r-sessions", type=int, nargs="*", default=None)
     ap.add_argument("--eos-only", action="store_true",
                     help="run only the EOS-projection measurement and print its object (profiling)")
     ap.add_argument("--eos-sessions", type=int, nargs="*", default=None,
@@ -487,6 +490,63 @@ def eos_measure(w, dev, peaks, sizes=(64, 1024), calls=20):
     return out
 
 
+def r_shape_measure(dev, peaks, sizes=(64, 1024), calls=10, seed=5):
+    """The reference bundle's accepted Local AR shape (d=768, 2 layers, 12
+    heads, FFN 3072, identity in-projection) through the frame entry point:
+    its AUTO path is the phase kernels, whose layer GEMMs and 16 heads run on
+    the tcgen05 GEMM (gemm_tc.cuh).  One frame call per step, CUDA events on
+    the launching stream, eager and replayed from a CUDA graph.  Algorithmic
+    work: 2 rows x macs_per_row() MAC per session per frame."""
+    from magpie_tts_rt_b200.local_ar import LocalArEngine, StreamBatch
+    w = make_weights(SHAPE_SOFIA, seed=seed, dtype=torch.bfloat16, profile="baseline")
+    tensor_peak = peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"])
+    out = {"shape": "d=768, 2 layers, 12 heads, FFN 3072, 16 heads 768->2024, CFG pair, EOS enabled"}
+    stream = torch.cuda.Stream(dev)
+    for n in sizes:
+        eng = LocalArEngine(w, max_streams=n, device=dev)
+        b = StreamBatch.allocate(n, device=dev)
+        g = torch.Generator().manual_seed(n)
+        b.decoder_hidden.copy_(torch.randn(n, 2, EMBED, generator=g).to(torch.bfloat16))
+        b.rng_seed.copy_(torch.arange(n))
+        b.unfinished.fill_(True)
+        res = {"frame_path": PATH_NAMES.get(eng.path, str(eng.path))}
+        with torch.cuda.stream(stream):
+            for _ in range(3):
+                eng.frame(b, stream=stream)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for _ in range(calls):
+                eng.frame(b, stream=stream)
+            e1.record(stream)
+        torch.cuda.synchronize(dev)
+        t_eager = e0.elapsed_time(e1) * 1000.0 / calls
+        t_graph = None
+        try:
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=stream):
+                eng.frame(b, stream=stream)
+            with torch.cuda.stream(stream):
+                graph.replay()
+                e0.record(stream)
+                for _ in range(calls):
+                    graph.replay()
+                e1.record(stream)
+            torch.cuda.synchronize(dev)
+            t_graph = e0.elapsed_time(e1) * 1000.0 / calls
+            del graph
+        except RuntimeError as exc:  # capture refused: report the eager number alone
+            res["graph_error"] = str(exc).splitlines()[0]
+        inv = int(b.invalid_rows.count_nonzero().item())
+        t = min(x for x in (t_eager, t_graph) if x is not None)
+        flops = n * 2 * 2 * SHAPE_SOFIA.macs_per_row()
+        tf = flops / (t * 1e-6) / 1e12
+        res.update({"frame_call_us_eager": t_eager, "frame_call_us_graph": t_graph,
+                    "frames_per_s": n / (t * 1e-6), "tflops": tf, "tensor_frac": tf / tensor_peak,
+                    "algorithmic_flops_per_call": flops, "invalid_rows": inv})
+        out[str(n)] = res
+    return out
+
+
 def alignment_gate_measure(dev, peaks, n=1024, stride=512, steps=200, seed=11):
     """The alignment gate (mtt_b200_launch_alignment_batch) for the config-4
     sessions of one GPU: text lengths U[64, 512], a fresh score row per step
@@ -811,6 +871,11 @@ def main():
         if rank == 0:
             print(json.dumps({"eos_projection": out}), flush=True)
         return
+    if args.r_shape_only:
+        out = r_shape_measure(torch.device("cuda", local), peaks, sizes=tuple(args.r_sessions or (64, 1024)))
+        if rank == 0:
+            print(json.dumps({"r_shape_frame": out}), flush=True)
+        return
     if args.main_decoder_only:
         out = main_decoder_measure(torch.device("cuda", local), peaks, n=args.md_sessions, steps=args.md_steps,
                                    with_cpu=False)
@@ -859,10 +924,11 @@ def main():
     loop = None
     if world == 1 and not args.no_latency and not args.no_loop:
         loop = loop_measure(torch.device("cuda", local), peaks, steps=args.loop_steps)
-    probe = eos = None
+    probe = eos = rshape = None
     if world == 1 and not args.no_latency:
         probe = tensor_probe(torch.device("cuda", local))
         eos = eos_measure(res["w"], torch.device("cuda", local), peaks)
+        rshape = r_shape_measure(torch.device("cuda", local), peaks)
     cpu = None
     if world == 1 and rank == 0 and not args.no_cpu_baseline:
         cpu = cpu_oracle_sample()
@@ -909,7 +975,7 @@ def main():
                 "gpu_launches": res["launches"], "frame_path": res["path"], "clocks": res["clocks"],
                 "roofline": roof,
                 "latency_config2": latency, "alignment_gate": align, "main_decoder_step": md,
-                "config5_loop": loop, "eos_projection": eos, "tensor_probe": probe,
+                "config5_loop": loop, "eos_projection": eos, "tensor_probe": probe, "r_shape_frame": rshape,
                 "cpu_baseline": cpu,
                 "checks": {"invalid_rows": res["invalid"], "forced_eos_ok": res["forced_ok"]}}
         print(json.dumps(line), flush=True)

@@ -36,6 +36,7 @@
 #include "../../include/magpie_tts_rt_b200.h"
 #include "eos.cuh"
 #include "frame_common.cuh"
+#include "gemm_tc.cuh"
 #include "sampling.cuh"
 
 namespace mtt {
@@ -278,6 +279,153 @@ __global__ void __launch_bounds__(kLinThreads) linear_kernel(Frame f, int p, int
       }
     }
   }
+}
+
+// ---------------------------------------------------------------------------
+// tensor-core linear layers (shapes with K a multiple of 64): the
+// activations are materialised as bf16 rows (LayerNorm rows first go to
+// `att`, which is free at both LayerNorms), then gemm_tc.cuh runs them with
+// the active rows on the MMA's M side (count on the device) and the layer's
+// output features on its N side (256 per tile); the epilogue does what
+// linear_kernel's does, 32 consecutive features of one row per lane.
+// ---------------------------------------------------------------------------
+
+template <int PRO>
+__global__ void __launch_bounds__(256) ln_rows_kernel(Frame f, int p, int l) {
+  const int rows = *f.count * f.rp;
+  const int r = blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (r >= rows) return;
+  load_row<PRO>(f, p, l, r, f.d, f.att + static_cast<int64_t>(r) * f.d);
+}
+
+template <int EPI>
+struct EpiPhase {
+  Frame f;
+  int p, l, N;
+  const bf16* bias;
+
+  __device__ __forceinline__ void chunk(int r, int n0, int /*ks*/, const uint32_t (&v)[32], int /*n_cols*/) const {
+    if (r >= *f.count * f.rp) return;  // rows past the active ones are padding
+    float y[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) y[j] = __uint_as_float(v[j]);
+    if constexpr (EPI == kEpiHead) {
+      const int i = r / f.rp, sub = r % f.rp;
+      bf16* out = f.logits_out != nullptr
+                      ? f.logits_out + ((static_cast<int64_t>(f.list[i]) * kPositions + p) * f.rp + sub) * kVocab
+                      : nullptr;
+      bf16* lg = f.logits + static_cast<int64_t>(r) * kVocab;
+      if (n0 + 32 <= N) {  // rows of 2024 bf16 keep every 32-column chunk 16-byte aligned
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const uint4 b = reinterpret_cast<const uint4*>(bias + n0)[q];
+          float t[8];
+          unpack8(b, t);
+          uint32_t w[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const __nv_bfloat162 h = __floats2bfloat162_rn(__fadd_rn(y[8 * q + 2 * e], t[2 * e]),
+                                                           __fadd_rn(y[8 * q + 2 * e + 1], t[2 * e + 1]));
+            w[e] = *reinterpret_cast<const uint32_t*>(&h);
+          }
+          const uint4 o = make_uint4(w[0], w[1], w[2], w[3]);
+          reinterpret_cast<uint4*>(lg + n0)[q] = o;
+          if (out != nullptr) reinterpret_cast<uint4*>(out + n0)[q] = o;
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const int n = n0 + j;
+          if (n < N) {
+            const bf16 o = f2bf(__fadd_rn(y[j], bf2f(bias[n])));
+            lg[n] = o;
+            if (out != nullptr) out[n] = o;
+          }
+        }
+      }
+      return;
+    } else {
+      if (n0 >= N) return;
+      bf16* dst;
+      if constexpr (EPI == kEpiQkv) {
+        if (n0 < f.d) {
+          dst = f.q + static_cast<int64_t>(r) * f.d + n0;
+        } else {
+          const int which = n0 < 2 * f.d ? 0 : 1;
+          const int col = n0 - (which + 1) * f.d;
+          const int64_t R = static_cast<int64_t>(f.n) * f.rp;
+          dst = (which == 0 ? f.kc : f.vc) + ((static_cast<int64_t>(l) * R + r) * kPositions + p) * f.d + col;
+        }
+      } else if constexpr (EPI == kEpiResid) {
+        dst = f.x + static_cast<int64_t>(r) * f.d + n0;
+        float x[32];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          float t[8];
+          unpack8(reinterpret_cast<const uint4*>(dst)[q], t);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) x[8 * q + e] = t[e];
+        }
+#pragma unroll
+        for (int j = 0; j < 32; ++j) y[j] = __fadd_rn(x[j], round_bf16(y[j]));
+      } else {  // kEpiGelu
+        dst = f.h + static_cast<int64_t>(r) * f.F + n0;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) y[j] = gelu_tanh(round_bf16(y[j]));
+      }
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        uint32_t w[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const __nv_bfloat162 h = __floats2bfloat162_rn(y[8 * q + 2 * e], y[8 * q + 2 * e + 1]);
+          w[e] = *reinterpret_cast<const uint32_t*>(&h);
+        }
+        reinterpret_cast<uint4*>(dst)[q] = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+    }
+  }
+};
+
+// A operand of a tensor-core linear layer: the rows it reads.
+template <int PRO>
+const bf16* tc_rows(const Frame& f) {
+  if constexpr (PRO == kProAtt || PRO == kProLn1 || PRO == kProLn2) return f.att;
+  if constexpr (PRO == kProH) return f.h;
+  return f.x;  // kProX
+}
+
+// K in whole 64-column chunks; q, k and v start on 32-column chunk bounds;
+// the row buffers on the 16-byte boundary a tensor map needs.
+bool tc_linear_supported(const Frame& f) {
+  const auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  return f.d % 64 == 0 && f.F % 64 == 0 && a16(f.att) && a16(f.h) && a16(f.x);
+}
+
+template <int PRO, int EPI>
+cudaError_t launch_linear_tc(const Frame& f, cudaStream_t st, int p, int l, int N, int K, const bf16* W,
+                             const bf16* bias) {
+  const int rows_max = f.n * f.rp;
+  if constexpr (PRO == kProLn1 || PRO == kProLn2) {
+    ln_rows_kernel<PRO><<<(rows_max + 7) / 8, 256, 0, st>>>(f, p, l);
+  }
+  CUtensorMap amap, bmap;
+  if (!cached_map(&amap, tc_rows<PRO>(f), static_cast<uint64_t>(K), static_cast<uint64_t>(rows_max), 128) ||
+      !cached_map(&bmap, W, static_cast<uint64_t>(K), static_cast<uint64_t>(N), 256)) {
+    return cudaErrorInvalidValue;
+  }
+  GemmProblem pr;
+  pr.m_tiles = (rows_max + 127) / 128;
+  pr.m_rows_dev = f.count;
+  pr.m_rows_scale = f.rp;
+  pr.n_rows = N;
+  pr.n_rows_dev = nullptr;
+  pr.n_rows_scale = 1;
+  pr.k_chunks = K / kGemmKChunk;
+  pr.splits = 1;
+  pr.status = nullptr;
+  pr.b_constant = 0;
+  return launch_gemm_tc<256>(amap, bmap, pr, EpiPhase<EPI>{f, p, l, N, bias}, st);
 }
 
 // Identity in-projection (d == 768): x = bf16(src + pos[p]).
@@ -668,6 +816,7 @@ extern "C" MTT_B200_API int mtt_b200_launch_local_ar_frame(const mtt_b200_local_
                : MTT_B200_STATUS_CUDA_ERROR;
   }
   const int d = f.d, F = f.F;
+  const bool tc = tc_linear_supported(f);  // the layer GEMMs and heads on the tensor cores
   frame_begin_kernel<<<1, kBeginThreads, 0, st>>>(f);
   for (int p = 0; p < kPositions; ++p) {
     if (in_proj) {
@@ -681,15 +830,38 @@ extern "C" MTT_B200_API int mtt_b200_launch_local_ar_frame(const mtt_b200_local_
     }
     for (int l = 0; l < f.L; ++l) {
       const int64_t dd = static_cast<int64_t>(d) * d;
-      launch_linear<kProLn1, kEpiQkv>(f, st, p, l, 3 * d, d, f.qkv + l * 3 * dd, nullptr);
+      const bf16* w1 = f.w1 + static_cast<int64_t>(l) * F * d;
+      const bf16* w2 = f.w2 + static_cast<int64_t>(l) * F * d;
+      if (tc) {
+        if (launch_linear_tc<kProLn1, kEpiQkv>(f, st, p, l, 3 * d, d, f.qkv + l * 3 * dd, nullptr) != cudaSuccess) {
+          return MTT_B200_STATUS_CUDA_ERROR;
+        }
+      } else {
+        launch_linear<kProLn1, kEpiQkv>(f, st, p, l, 3 * d, d, f.qkv + l * 3 * dd, nullptr);
+      }
       const int warps = f.n * f.rp * f.H;
       attention_kernel<<<(warps + 7) / 8, 256, 0, st>>>(f, p, l);
-      launch_linear<kProAtt, kEpiResid>(f, st, p, l, d, d, f.o + l * dd, nullptr);
-      launch_linear<kProLn2, kEpiGelu>(f, st, p, l, F, d, f.w1 + static_cast<int64_t>(l) * F * d, nullptr);
-      launch_linear<kProH, kEpiResid>(f, st, p, l, d, F, f.w2 + static_cast<int64_t>(l) * F * d, nullptr);
+      if (tc) {
+        if (launch_linear_tc<kProAtt, kEpiResid>(f, st, p, l, d, d, f.o + l * dd, nullptr) != cudaSuccess ||
+            launch_linear_tc<kProLn2, kEpiGelu>(f, st, p, l, F, d, w1, nullptr) != cudaSuccess ||
+            launch_linear_tc<kProH, kEpiResid>(f, st, p, l, d, F, w2, nullptr) != cudaSuccess) {
+          return MTT_B200_STATUS_CUDA_ERROR;
+        }
+      } else {
+        launch_linear<kProAtt, kEpiResid>(f, st, p, l, d, d, f.o + l * dd, nullptr);
+        launch_linear<kProLn2, kEpiGelu>(f, st, p, l, F, d, w1, nullptr);
+        launch_linear<kProH, kEpiResid>(f, st, p, l, d, F, w2, nullptr);
+      }
     }
-    launch_linear<kProX, kEpiHead>(f, st, p, 0, kVocab, d, f.head_w + static_cast<int64_t>(p) * kVocab * d,
-                                   f.head_b + static_cast<int64_t>(p) * kVocab);
+    const bf16* hw = f.head_w + static_cast<int64_t>(p) * kVocab * d;
+    const bf16* hb = f.head_b + static_cast<int64_t>(p) * kVocab;
+    if (tc) {
+      if (launch_linear_tc<kProX, kEpiHead>(f, st, p, 0, kVocab, d, hw, hb) != cudaSuccess) {
+        return MTT_B200_STATUS_CUDA_ERROR;
+      }
+    } else {
+      launch_linear<kProX, kEpiHead>(f, st, p, 0, kVocab, d, hw, hb);
+    }
     sample_kernel<<<f.n, kSampleThreads, 0, st>>>(f, p);
   }
   if (f.final_w != nullptr && f.eos_pre == nullptr && launch_eos_projection(frame_eos_args(f), st) != cudaSuccess) {

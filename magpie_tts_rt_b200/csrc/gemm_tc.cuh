@@ -304,6 +304,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 // box of 64 columns x box_rows rows and the 128-byte swizzle (frame_fused.cu).
 bool make_weight_map(CUtensorMap* map, const void* base, uint64_t cols, uint64_t rows, uint32_t box_rows);
 
+// make_weight_map behind a process-wide cache: the same (pointer, shape,
+// box) recurs every step of a layer, and encoding a map costs host time.
+bool cached_map(CUtensorMap* out, const void* base, uint64_t cols, uint64_t rows, uint32_t box_rows);
+
 // Grid for a persistent GEMM: at most one CTA per SM (0 when the device
 // cannot be queried).
 int gemm_grid(int tiles);

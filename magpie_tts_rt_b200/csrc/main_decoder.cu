@@ -682,29 +682,6 @@ struct EpiPartial {
   }
 };
 
-// Tensor maps are host-encoded; the same (pointer, shape, box) recurs every
-// step, so they are kept (a few hundred per process at most).
-bool cached_map(CUtensorMap* out, const void* base, uint64_t cols, uint64_t rows, uint32_t box_rows) {
-  static std::mutex mu;
-  static std::map<std::tuple<const void*, uint64_t, uint64_t, uint32_t>, CUtensorMap> maps;
-  const auto key = std::make_tuple(base, cols, rows, box_rows);
-  {
-    std::lock_guard<std::mutex> lock(mu);
-    auto it = maps.find(key);
-    if (it != maps.end()) {
-      *out = it->second;
-      return true;
-    }
-  }
-  CUtensorMap m;
-  if (!make_weight_map(&m, base, cols, rows, box_rows)) return false;
-  std::lock_guard<std::mutex> lock(mu);
-  if (maps.size() > 4096) maps.clear();
-  maps.emplace(key, m);
-  *out = m;
-  return true;
-}
-
 // FFN2 (K = 3072) splits its K range in 4 (12 chunks of 64 each, as long as
 // the other GEMMs' K = 768); add_ln_kernel sums the f32 partials.  Splitting
 // the K = 768 GEMMs as well measured slower (the partials' traffic costs more
