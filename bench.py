@@ -87,6 +87,8 @@ def parse():
     ap.add_argument("--loop-only", action="store_true", help="run only the config-5 loop and print its object")
     ap.add_argument("--loop-steps", type=int, default=1024)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--latency-only", action="store_true",
+                    help="run only the config-2 latency measurement (with its phase breakdown) and print it")
     ap.add_argument("--r-shape-only", action="store_true",
                     help="run only the d=768 / 2-layer Local AR frame measurement and print its object")
     ap.add_argument("--r-sessions", type=int, nargs="*", default=None)
@@ -418,6 +420,48 @@ def latency_config2(eng_w, dev, frames=1000, warm=20):
             "frame_path": PATH_NAMES.get(eng.path, str(eng.path)),
             "p50_us": float(np.percentile(us, 50)), "p99_us": float(np.percentile(us, 99)),
             "mean_us": float(us.mean()), "frames": frames, "invalid": inv}
+
+
+PHASE_STAMPS = ["x ready", "qkv + partial scores", "scores round", "attention", "attention round",
+                "o-projection", "o round", "LN2 + FFN1", "FFN2 partials", "FFN2 partials round",
+                "FFN2 sum round", "head", "logits round", "sampling", "token round"]
+
+
+def latency_trace(eng_w, dev, frames=20):
+    """Per-position phase breakdown of the config-2 frame (library trace hook
+    mtt_b200_test_frame_trace): SM-clock stamps of the first CTA at 16 points
+    of each position, averaged over `frames` frames, in microseconds at the
+    clock measured over the frame (cycles / global-timer ns)."""
+    from magpie_tts_rt_b200 import _lib as L
+    from magpie_tts_rt_b200.local_ar import LocalArEngine, StreamBatch
+    eng = LocalArEngine(eng_w, max_streams=1, device=dev)
+    if PATH_NAMES.get(eng.path) != "fused cluster kernel":
+        return None
+    b = StreamBatch.allocate(1, device=dev)
+    b.rng_seed.fill_(1234)
+    b.unfinished.fill_(True)
+    g = torch.Generator().manual_seed(78)
+    stamps = torch.zeros(260, dtype=torch.int64, device=dev)
+    per = []
+    try:
+        L.lib.mtt_b200_test_frame_trace(ctypes.c_void_p(stamps.data_ptr()))
+        for f in range(frames + 3):
+            b.decoder_hidden.copy_(torch.randn(1, 2, EMBED, generator=g).to(torch.bfloat16))
+            eng.frame(b)
+            torch.cuda.synchronize(dev)
+            if f >= 3:
+                per.append(stamps.cpu().numpy().copy())
+    finally:
+        L.lib.mtt_b200_test_frame_trace(None)
+    a = np.stack(per).astype(np.float64)
+    mhz = (a[:, 258] - a[:, 256]) / (a[:, 259] - a[:, 257]) * 1000.0
+    pos = a[:, :256].reshape(frames, 16, 16)
+    d = np.diff(pos, axis=2) / mhz[:, None, None]  # us between consecutive stamps
+    per_pos = (pos[:, :, 15] - pos[:, :, 0]) / mhz[:, None]
+    return {"sm_mhz": float(np.median(mhz)),
+            "frame_us_in_kernel": float(np.median((a[:, 258] - a[:, 256]) / mhz)),
+            "position_us_mean": float(per_pos[:, 1:].mean()), "position0_us": float(per_pos[:, 0].mean()),
+            "phase_us_mean_p1_15": {k: float(d[:, 1:, i].mean()) for i, k in enumerate(PHASE_STAMPS)}}
 
 
 def tensor_probe(dev):
@@ -871,6 +915,14 @@ def main():
         if rank == 0:
             print(json.dumps({"eos_projection": out}), flush=True)
         return
+    if args.latency_only:
+        w = make_weights(SHAPE_BASELINE, seed=0, dtype=torch.bfloat16, profile="baseline")
+        dev = torch.device("cuda", local)
+        out = latency_config2(w, dev)
+        out["phase_breakdown"] = latency_trace(w, dev)
+        if rank == 0:
+            print(json.dumps({"latency_config2": out}), flush=True)
+        return
     if args.r_shape_only:
         out = r_shape_measure(torch.device("cuda", local), peaks, sizes=tuple(args.r_sessions or (64, 1024)))
         if rank == 0:
@@ -914,6 +966,7 @@ def main():
     latency = None
     if world == 1 and not args.no_latency:
         latency = latency_config2(res["w"], torch.device("cuda", local))
+        latency["phase_breakdown"] = latency_trace(res["w"], torch.device("cuda", local))
     align = None
     if world == 1 and not args.no_latency:
         align = alignment_gate_measure(torch.device("cuda", local), peaks)

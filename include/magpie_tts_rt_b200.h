@@ -403,7 +403,7 @@ MTT_B200_API int mtt_b200_launch_local_ar_frame(const mtt_b200_local_ar_shape_t*
  * instead of a caller workspace.  A batch fits when
  * mtt_b200_local_ar_frame_workspace_size(shape, n_streams, cfg) is at most
  * that size: with CFG up to 40 sessions of the benchmark shape (d=256,
- * 1 layer, FFN 1024) or 9 of the d=768 2-layer shape (74 and 17 without
+ * 1 layer, FFN 1024) or 7 of the d=768 2-layer shape (74 and 14 without
  * CFG).  A larger batch is rejected with
  * MTT_B200_STATUS_STATIC_WORKSPACE_TOO_SMALL and nothing is launched.  The
  * first call on a device (that device current) resolves the array's device
@@ -725,6 +725,17 @@ MTT_B200_API int mtt_b200_test_umma_cycles(int32_t n, int32_t accumulators, int3
                                            uint64_t* cycles, void* stream);
 MTT_B200_API int mtt_b200_test_dsmem_cycles(int32_t bytes_per_peer, int32_t rounds, int32_t clusters,
                                             uint64_t* cycles, void* stream);
+
+/* Trace hook: while `stamps` is non-null, every frame launched on the fused
+ * cluster path records, from CTA 0 of its first cluster, the SM clock at 16
+ * points of each position into stamps[16 * p + i] (i: 0 position start;
+ * 1 x ready; 2 q|k|v and partial scores; 3 their round; 4 attention; 5 its
+ * round; 6 o-projection; 7 its round; 8 LN2 + FFN1; 9 FFN2 partials; 10 their
+ * round; 11 FFN2 sum round; 12 head; 13 logits round; 14 sampling; 15 token
+ * round), then stamps[256..259] = clock and global timer (ns) at the frame's
+ * start and end.  `stamps` is a device buffer of 260 entries; null turns the
+ * hook off.  Process-wide; for measurement only. */
+MTT_B200_API int mtt_b200_test_frame_trace(uint64_t* stamps);
 
 MTT_B200_API int mtt_b200_launch_test_gemm(const void* x_bf16, const void* w_bf16, void* y_bf16, int32_t rows,
                                            int32_t n, int32_t k, int32_t gelu, int32_t splits, float* partial,

@@ -205,6 +205,7 @@ SIGNATURES = {
     "mtt_b200_launch_test_gemm": (I32, [P, P, P, I32, I32, I32, I32, I32, P, P]),
     "mtt_b200_test_umma_cycles": (I32, [I32, I32, I32, I32, P, P]),
     "mtt_b200_test_dsmem_cycles": (I32, [I32, I32, I32, P, P]),
+    "mtt_b200_test_frame_trace": (I32, [P]),
     "mtt_b200_session_engine_create": (I32, [ctypes.POINTER(SessionEngineConfig), ctypes.POINTER(P)]),
     "mtt_b200_session_engine_destroy": (None, [P]),
     "mtt_b200_session_engine_buffers": (I32, [P, ctypes.POINTER(SessionEngineBuffers)]),

@@ -33,6 +33,8 @@
 // active count exit at once.
 #include <cstddef>
 
+#include <atomic>
+
 #include "../../include/magpie_tts_rt_b200.h"
 #include "eos.cuh"
 #include "frame_common.cuh"
@@ -290,12 +292,110 @@ __global__ void __launch_bounds__(kLinThreads) linear_kernel(Frame f, int p, int
 // linear_kernel's does, 32 consecutive features of one row per lane.
 // ---------------------------------------------------------------------------
 
-template <int PRO>
-__global__ void __launch_bounds__(256) ln_rows_kernel(Frame f, int p, int l) {
+constexpr int kRowChunks = 4;  // 8-column chunks per lane: rows of up to 1024 features in registers
+
+// LayerNorm (no bias, eps 1e-5) of one row held in registers, v[8c + j] =
+// feature 8 (lane + 32c) + j, written to out; the same arithmetic and order
+// as load_row's LayerNorm prologue.
+__device__ __forceinline__ void ln_row_regs(const float (&v)[8 * kRowChunks], int K, const bf16* w, bf16* out) {
+  const int lane = threadIdx.x & 31;
+  float sum = 0.f;
+#pragma unroll
+  for (int c = 0; c < kRowChunks; ++c) {
+    if (lane * 8 + 256 * c < K) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) sum += v[8 * c + j];
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+  const float mean = sum / static_cast<float>(K);
+  float var = 0.f;
+#pragma unroll
+  for (int c = 0; c < kRowChunks; ++c) {
+    if (lane * 8 + 256 * c < K) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float dlt = v[8 * c + j] - mean;
+        var += dlt * dlt;
+      }
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) var += __shfl_xor_sync(0xffffffffu, var, o);
+  const float rstd = 1.0f / sqrtf(var / static_cast<float>(K) + 1.0e-5f);
+#pragma unroll
+  for (int c = 0; c < kRowChunks; ++c) {
+    const int k = lane * 8 + 256 * c;
+    if (k < K) {
+      float g[8];
+      unpack8(*reinterpret_cast<const uint4*>(w + k), g);
+      __align__(16) bf16 o8[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) o8[j] = f2bf(((v[8 * c + j] - mean) * rstd) * g[j]);
+      *reinterpret_cast<uint4*>(out + k) = *reinterpret_cast<const uint4*>(o8);
+    }
+  }
+}
+
+// att = LayerNorm(x) with weights w, one warp per row.
+__global__ void __launch_bounds__(256) ln_rows_kernel(Frame f, const bf16* w) {
   const int rows = *f.count * f.rp;
   const int r = blockIdx.x * 8 + (threadIdx.x >> 5);
   if (r >= rows) return;
-  load_row<PRO>(f, p, l, r, f.d, f.att + static_cast<int64_t>(r) * f.d);
+  const int lane = threadIdx.x & 31;
+  const bf16* xr = f.x + static_cast<int64_t>(r) * f.d;
+  float v[8 * kRowChunks];
+#pragma unroll
+  for (int c = 0; c < kRowChunks; ++c) {
+    const int k = lane * 8 + 256 * c;
+    float t[8];
+    if (k < f.d) unpack8(*reinterpret_cast<const uint4*>(xr + k), t);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[8 * c + j] = k < f.d ? t[j] : 0.f;
+  }
+  ln_row_regs(v, f.d, w, f.att + static_cast<int64_t>(r) * f.d);
+}
+
+// x = bf16(x + bf16(sum of the split GEMM's partials, in split order)), one
+// warp per row; with LN, att = LayerNorm(x) with weights lnw (the next
+// sub-layer's pre-norm).
+template <bool LN>
+__global__ void __launch_bounds__(256) resid_sum_kernel(Frame f, int splits, const bf16* lnw) {
+  const int rows = *f.count * f.rp;
+  const int r = blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (r >= rows) return;
+  const int lane = threadIdx.x & 31;
+  const int64_t rows_max = static_cast<int64_t>(f.n) * f.rp;
+  bf16* xr = f.x + static_cast<int64_t>(r) * f.d;
+  float v[8 * kRowChunks];
+#pragma unroll
+  for (int c = 0; c < kRowChunks; ++c) {
+    const int k = lane * 8 + 256 * c;
+    if (k < f.d) {
+      float a[8], acc[8];
+      unpack8(*reinterpret_cast<const uint4*>(xr + k), a);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[j] = 0.f;
+      for (int sp = 0; sp < splits; ++sp) {
+        const float4* pp = reinterpret_cast<const float4*>(f.part + (sp * rows_max + r) * f.d + k);
+        const float4 p0 = pp[0], p1 = pp[1];
+        acc[0] += p0.x; acc[1] += p0.y; acc[2] += p0.z; acc[3] += p0.w;
+        acc[4] += p1.x; acc[5] += p1.y; acc[6] += p1.z; acc[7] += p1.w;
+      }
+      __align__(16) bf16 o8[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        o8[j] = f2bf(__fadd_rn(a[j], round_bf16(acc[j])));
+        v[8 * c + j] = bf2f(o8[j]);
+      }
+      *reinterpret_cast<uint4*>(xr + k) = *reinterpret_cast<const uint4*>(o8);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[8 * c + j] = 0.f;
+    }
+  }
+  if constexpr (LN) ln_row_regs(v, f.d, lnw, f.att + static_cast<int64_t>(r) * f.d);
 }
 
 template <int EPI>
@@ -387,6 +487,24 @@ struct EpiPhase {
   }
 };
 
+// Split-K partial sums of a residual GEMM: part[ks][r][n] (f32), summed by
+// resid_sum_kernel.
+struct EpiPhasePart {
+  float* part;
+  int rows_max, N;
+  const int* count;
+  int rp;
+  __device__ __forceinline__ void chunk(int r, int n0, int ks, const uint32_t (&v)[32], int /*n_cols*/) const {
+    if (r >= *count * rp || n0 >= N) return;
+    float4* dst = reinterpret_cast<float4*>(part + (static_cast<int64_t>(ks) * rows_max + r) * N + n0);
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      dst[q] = make_float4(__uint_as_float(v[4 * q]), __uint_as_float(v[4 * q + 1]), __uint_as_float(v[4 * q + 2]),
+                           __uint_as_float(v[4 * q + 3]));
+    }
+  }
+};
+
 // A operand of a tensor-core linear layer: the rows it reads.
 template <int PRO>
 const bf16* tc_rows(const Frame& f) {
@@ -395,20 +513,17 @@ const bf16* tc_rows(const Frame& f) {
   return f.x;  // kProX
 }
 
-// K in whole 64-column chunks; q, k and v start on 32-column chunk bounds;
-// the row buffers on the 16-byte boundary a tensor map needs.
-bool tc_linear_supported(const Frame& f) {
-  const auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
-  return f.d % 64 == 0 && f.F % 64 == 0 && a16(f.att) && a16(f.h) && a16(f.x);
-}
+// K in whole 64-column chunks, q, k and v starting on 32-column chunk
+// bounds, rows that fit ln_row_regs (the workspace's 256-byte alignment puts
+// every row buffer on the 16-byte boundary a tensor map needs).
+bool tc_linear_supported(int d, int F) { return d % 64 == 0 && F % 64 == 0 && d <= 256 * kRowChunks; }
 
+// The GEMM of a tensor-core linear layer (its LayerNorm rows, where it has
+// one, already in `att`); EPI < 0: split-K partial sums into f.part.
 template <int PRO, int EPI>
 cudaError_t launch_linear_tc(const Frame& f, cudaStream_t st, int p, int l, int N, int K, const bf16* W,
-                             const bf16* bias) {
+                             const bf16* bias, int splits = 1) {
   const int rows_max = f.n * f.rp;
-  if constexpr (PRO == kProLn1 || PRO == kProLn2) {
-    ln_rows_kernel<PRO><<<(rows_max + 7) / 8, 256, 0, st>>>(f, p, l);
-  }
   CUtensorMap amap, bmap;
   if (!cached_map(&amap, tc_rows<PRO>(f), static_cast<uint64_t>(K), static_cast<uint64_t>(rows_max), 128) ||
       !cached_map(&bmap, W, static_cast<uint64_t>(K), static_cast<uint64_t>(N), 256)) {
@@ -421,31 +536,55 @@ cudaError_t launch_linear_tc(const Frame& f, cudaStream_t st, int p, int l, int 
   pr.n_rows = N;
   pr.n_rows_dev = nullptr;
   pr.n_rows_scale = 1;
-  pr.k_chunks = K / kGemmKChunk;
-  pr.splits = 1;
+  pr.k_chunks = K / kGemmKChunk / splits;
+  pr.splits = splits;
   pr.status = nullptr;
   pr.b_constant = 0;
-  return launch_gemm_tc<256>(amap, bmap, pr, EpiPhase<EPI>{f, p, l, N, bias}, st);
+  if constexpr (EPI < 0) {
+    return launch_gemm_tc<256>(amap, bmap, pr, EpiPhasePart{f.part, rows_max, N, f.count, f.rp}, st);
+  } else {
+    return launch_gemm_tc<256>(amap, bmap, pr, EpiPhase<EPI>{f, p, l, N, bias}, st);
+  }
 }
 
 // Identity in-projection (d == 768): x = bf16(src + pos[p]).
-__global__ void add_pos_kernel(Frame f, int p) {
+// Identity in-projection: x = bf16(src + pos[p]), src the decoder hidden row
+// (p = 0) or the embedding of the previous position's token; one warp per
+// row.  With LN (tensor-core layers) it also writes att = LN1_0(x).
+template <bool LN>
+__global__ void __launch_bounds__(256) add_pos_kernel(Frame f, int p) {
   const int rows = *f.count * f.rp;
-  const int64_t total = static_cast<int64_t>(rows) * f.d;
-  for (int64_t e = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; e < total;
-       e += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int r = static_cast<int>(e / f.d), k = static_cast<int>(e % f.d);
-    const int i = r / f.rp, sub = r % f.rp;
-    const int s = f.list[i];
-    float src;
-    if (p == 0) {
-      src = bf2f(f.hidden[(static_cast<int64_t>(s) * f.rp + sub) * kEmbed + k]);
-    } else {
-      const int64_t tok = input_token(f, s, p - 1);
-      src = bf2f(f.emb[(static_cast<int64_t>(p - 1) * kVocab + tok) * kEmbed + k]);
+  const int r = blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (r >= rows) return;
+  const int lane = threadIdx.x & 31;
+  const int i = r / f.rp, sub = r % f.rp;
+  const int s = f.list[i];
+  const bf16* src = p == 0 ? f.hidden + (static_cast<int64_t>(s) * f.rp + sub) * kEmbed
+                           : f.emb + (static_cast<int64_t>(p - 1) * kVocab + input_token(f, s, p - 1)) * kEmbed;
+  const bf16* pos = f.pos + static_cast<int64_t>(p) * f.d;
+  bf16* xr = f.x + static_cast<int64_t>(r) * f.d;
+  float v[8 * kRowChunks];
+#pragma unroll
+  for (int j = 0; j < 8 * kRowChunks; ++j) v[j] = 0.f;
+  for (int c = 0, k = lane * 8; k < f.d; ++c, k += 256) {
+    float a[8], b[8];
+    unpack8(*reinterpret_cast<const uint4*>(src + k), a);
+    unpack8(*reinterpret_cast<const uint4*>(pos + k), b);
+    __align__(16) bf16 o8[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) o8[j] = f2bf(__fadd_rn(a[j], b[j]));
+    *reinterpret_cast<uint4*>(xr + k) = *reinterpret_cast<const uint4*>(o8);
+    if constexpr (LN) {
+#pragma unroll
+      for (int cc = 0; cc < kRowChunks; ++cc) {
+        if (cc == c) {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) v[8 * cc + j] = bf2f(o8[j]);
+        }
+      }
     }
-    f.x[e] = f2bf(__fadd_rn(src, bf2f(f.pos[static_cast<int64_t>(p) * f.d + k])));
   }
+  if constexpr (LN) ln_row_regs(v, f.d, f.ln1, f.att + static_cast<int64_t>(r) * f.d);
 }
 
 // ---------------------------------------------------------------------------
@@ -463,12 +602,21 @@ __global__ void __launch_bounds__(256) attention_kernel(Frame f, int p, int l) {
       *reinterpret_cast<const __nv_bfloat162*>(f.q + static_cast<int64_t>(r) * f.d + hd * kHeadDim + 2 * lane));
   const bf16* kbase = f.kc + ((static_cast<int64_t>(l) * R + r) * kPositions) * f.d + hd * kHeadDim + 2 * lane;
   const bf16* vbase = f.vc + ((static_cast<int64_t>(l) * R + r) * kPositions) * f.d + hd * kHeadDim + 2 * lane;
+  // every key and value row of the window in flight at once
+  __nv_bfloat162 kr[kPositions], vr[kPositions];
+#pragma unroll
+  for (int j = 0; j < kPositions; ++j) {
+    if (j <= p) {
+      kr[j] = *reinterpret_cast<const __nv_bfloat162*>(kbase + j * f.d);
+      vr[j] = *reinterpret_cast<const __nv_bfloat162*>(vbase + j * f.d);
+    }
+  }
   float s[kPositions];
   float mx = -CUDART_INF_F;
 #pragma unroll
   for (int j = 0; j < kPositions; ++j) {
     if (j <= p) {
-      const float2 kv = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(kbase + j * f.d));
+      const float2 kv = __bfloat1622float2(kr[j]);
       float dot = qv.x * kv.x + qv.y * kv.y;
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
@@ -489,7 +637,7 @@ __global__ void __launch_bounds__(256) attention_kernel(Frame f, int p, int l) {
   for (int j = 0; j < kPositions; ++j) {
     if (j <= p) {
       const float prob = round_bf16(s[j] / sum);
-      const float2 vv = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(vbase + j * f.d));
+      const float2 vv = __bfloat1622float2(vr[j]);
       o0 = fmaf(prob, vv.x, o0);
       o1 = fmaf(prob, vv.y, o1);
     }
@@ -584,6 +732,10 @@ extern "C" MTT_B200_API size_t mtt_b200_local_ar_frame_workspace_size(const mtt_
 
 namespace {
 
+// Trace hook: device buffer for the fused cluster kernel's phase stamps
+// (mtt_b200_test_frame_trace); null in normal operation.
+std::atomic<uint64_t*> g_frame_trace{nullptr};
+
 // Resolves the path for a shape / configuration / batch size on the current
 // device.  AUTO, benchmark shape, by the batch's 16-row tiles (8 sessions
 // each): the fused 16-CTA cluster kernel while the tiles fit in one wave of
@@ -667,6 +819,11 @@ int32_t resolve_path(const mtt_b200_local_ar_shape_t* shape, const mtt_b200_samp
 
 }  // namespace
 
+extern "C" MTT_B200_API int mtt_b200_test_frame_trace(uint64_t* stamps) {
+  g_frame_trace.store(stamps);
+  return MTT_B200_STATUS_OK;
+}
+
 extern "C" MTT_B200_API int32_t mtt_b200_local_ar_frame_path(const mtt_b200_local_ar_shape_t* shape,
                                                              const mtt_b200_sampling_config_t* sampling,
                                                              int32_t n_streams) {
@@ -699,7 +856,16 @@ extern "C" MTT_B200_API int32_t mtt_b200_local_ar_frame_launch_count(const mtt_b
   }
   if (path != MTT_B200_FRAME_PATH_PHASE_KERNELS) return 0;
   // begin + 16 x (embed + 5 per layer + head + sample) + eos projection + end
-  return 1 + mtt::kPositions * (1 + 5 * shape->n_layers + 2) + 2;
+  // begin; per position: in-projection (+ LayerNorm rows on the tensor-core
+  // layers) or position add, the layers, head, sampling; EOS rows and
+  // projection GEMM; end
+  if (mtt::tc_linear_supported(shape->d_model, shape->d_ffn)) {
+    // 7 per layer; without the split, no LayerNorm launch after the last FFN2
+    const int in_proj = shape->d_model != mtt::kEmbed ? 2 : 1;
+    const int last = mtt::fused_frame_shape(shape->d_model, shape->n_layers, shape->d_ffn) ? 1 : 0;
+    return 1 + mtt::kPositions * (in_proj + 7 * shape->n_layers - last + 2) + 3;
+  }
+  return 1 + mtt::kPositions * (1 + 5 * shape->n_layers + 2) + 3;
 }
 
 extern "C" MTT_B200_API int mtt_b200_launch_local_ar_frame(const mtt_b200_local_ar_shape_t* shape,
@@ -778,6 +944,7 @@ extern "C" MTT_B200_API int mtt_b200_launch_local_ar_frame(const mtt_b200_local_
   f.forced = b->forced_tokens;
   f.logits_out = static_cast<bf16*>(b->logits_out);
   f.eos_pre = static_cast<const uint32_t*>(b->eos_projection);
+  f.trace = g_frame_trace.load();
   char* ws = static_cast<char*>(workspace);
   f.list = reinterpret_cast<int32_t*>(ws + lo.list);
   f.count = reinterpret_cast<int32_t*>(ws + lo.count);
@@ -797,6 +964,7 @@ extern "C" MTT_B200_API int mtt_b200_launch_local_ar_frame(const mtt_b200_local_
   f.inv = reinterpret_cast<int32_t*>(ws + lo.inv);
   f.eos_partial = reinterpret_cast<float*>(ws + lo.eos_partial);
   f.eos_logit = reinterpret_cast<float*>(ws + lo.eos_logit);
+  f.part = reinterpret_cast<float*>(ws + lo.part);
 
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int32_t path = resolve_path(shape, sampling, b->n_streams);
@@ -816,7 +984,16 @@ extern "C" MTT_B200_API int mtt_b200_launch_local_ar_frame(const mtt_b200_local_
                : MTT_B200_STATUS_CUDA_ERROR;
   }
   const int d = f.d, F = f.F;
-  const bool tc = tc_linear_supported(f);  // the layer GEMMs and heads on the tensor cores
+  // Tensor-core layers: LayerNorm rows come out of the kernel before each
+  // GEMM (the in-projection / position add, the residual sum of the previous
+  // split GEMM, or ln_rows_kernel); the o-projection and FFN2 split K and sum
+  // their partials in resid_sum_kernel (the benchmark shape: no split, the
+  // residual added in the GEMM epilogue).
+  const bool tc = tc_linear_supported(f.d, f.F);
+  const bool split = !fused_frame_shape(f.d, f.L, f.F);
+  const int rows_max = f.n * f.rp;
+  const int row_blocks = (rows_max + 7) / 8;
+  const int split_o = phase_splits(rows_max, d, d), split_f = phase_splits(rows_max, d, F);
   frame_begin_kernel<<<1, kBeginThreads, 0, st>>>(f);
   for (int p = 0; p < kPositions; ++p) {
     if (in_proj) {
@@ -825,29 +1002,48 @@ extern "C" MTT_B200_API int mtt_b200_launch_local_ar_frame(const mtt_b200_local_
       } else {
         launch_linear<kProGather, kEpiInProj>(f, st, p, 0, d, kEmbed, f.in_w, f.in_b);
       }
+      if (tc) ln_rows_kernel<<<row_blocks, 256, 0, st>>>(f, f.ln1);
+    } else if (tc) {
+      add_pos_kernel<true><<<row_blocks, 256, 0, st>>>(f, p);
     } else {
-      add_pos_kernel<<<148 * 4, 256, 0, st>>>(f, p);
+      add_pos_kernel<false><<<row_blocks, 256, 0, st>>>(f, p);
     }
     for (int l = 0; l < f.L; ++l) {
       const int64_t dd = static_cast<int64_t>(d) * d;
       const bf16* w1 = f.w1 + static_cast<int64_t>(l) * F * d;
       const bf16* w2 = f.w2 + static_cast<int64_t>(l) * F * d;
+      const int warps = f.n * f.rp * f.H;
       if (tc) {
+        const bf16* ln2 = f.ln2 + static_cast<int64_t>(l) * d;
+        const bf16* ln_next = l + 1 < f.L ? f.ln1 + static_cast<int64_t>(l + 1) * d : nullptr;
         if (launch_linear_tc<kProLn1, kEpiQkv>(f, st, p, l, 3 * d, d, f.qkv + l * 3 * dd, nullptr) != cudaSuccess) {
           return MTT_B200_STATUS_CUDA_ERROR;
         }
+        attention_kernel<<<(warps + 7) / 8, 256, 0, st>>>(f, p, l);
+        cudaError_t e;
+        if (split) {
+          e = launch_linear_tc<kProAtt, -1>(f, st, p, l, d, d, f.o + l * dd, nullptr, split_o);
+          if (e == cudaSuccess) resid_sum_kernel<true><<<row_blocks, 256, 0, st>>>(f, split_o, ln2);
+        } else {
+          e = launch_linear_tc<kProAtt, kEpiResid>(f, st, p, l, d, d, f.o + l * dd, nullptr);
+          if (e == cudaSuccess) ln_rows_kernel<<<row_blocks, 256, 0, st>>>(f, ln2);
+        }
+        if (e == cudaSuccess) e = launch_linear_tc<kProLn2, kEpiGelu>(f, st, p, l, F, d, w1, nullptr);
+        if (e == cudaSuccess && split) {
+          e = launch_linear_tc<kProH, -1>(f, st, p, l, d, F, w2, nullptr, split_f);
+          if (e == cudaSuccess && ln_next != nullptr) {
+            resid_sum_kernel<true><<<row_blocks, 256, 0, st>>>(f, split_f, ln_next);
+          } else if (e == cudaSuccess) {
+            resid_sum_kernel<false><<<row_blocks, 256, 0, st>>>(f, split_f, nullptr);
+          }
+        } else if (e == cudaSuccess) {
+          e = launch_linear_tc<kProH, kEpiResid>(f, st, p, l, d, F, w2, nullptr);
+          if (e == cudaSuccess && ln_next != nullptr) ln_rows_kernel<<<row_blocks, 256, 0, st>>>(f, ln_next);
+        }
+        if (e != cudaSuccess) return MTT_B200_STATUS_CUDA_ERROR;
       } else {
         launch_linear<kProLn1, kEpiQkv>(f, st, p, l, 3 * d, d, f.qkv + l * 3 * dd, nullptr);
-      }
-      const int warps = f.n * f.rp * f.H;
-      attention_kernel<<<(warps + 7) / 8, 256, 0, st>>>(f, p, l);
-      if (tc) {
-        if (launch_linear_tc<kProAtt, kEpiResid>(f, st, p, l, d, d, f.o + l * dd, nullptr) != cudaSuccess ||
-            launch_linear_tc<kProLn2, kEpiGelu>(f, st, p, l, F, d, w1, nullptr) != cudaSuccess ||
-            launch_linear_tc<kProH, kEpiResid>(f, st, p, l, d, F, w2, nullptr) != cudaSuccess) {
-          return MTT_B200_STATUS_CUDA_ERROR;
-        }
-      } else {
+        attention_kernel<<<(warps + 7) / 8, 256, 0, st>>>(f, p, l);
         launch_linear<kProAtt, kEpiResid>(f, st, p, l, d, d, f.o + l * dd, nullptr);
         launch_linear<kProLn2, kEpiGelu>(f, st, p, l, F, d, w1, nullptr);
         launch_linear<kProH, kEpiResid>(f, st, p, l, d, F, w2, nullptr);

@@ -2,6 +2,8 @@
 // (phase kernels in frame.cu, fused cluster kernel in frame_fused.cu).
 #pragma once
 
+#include <algorithm>
+
 #include <cuda.h>
 
 #include <cstddef>
@@ -33,6 +35,7 @@ struct Frame {
   const int64_t* forced;
   bf16* logits_out;
   const uint32_t* eos_pre;  // optional [n][32]: the EOS projection from the Main Decoder step
+  uint64_t* trace;          // optional phase clock stamps of the first CTA (fused cluster kernel)
   // workspace
   int32_t *list, *count, *eos_list, *eos_count, *eos_slot;
   bf16 *x, *q, *kc, *vc, *att, *h, *logits;
@@ -41,6 +44,7 @@ struct Frame {
   int64_t* ctr;
   int32_t* inv;
   float *eos_partial, *eos_logit;
+  float* part;  // phase kernels: f32 partial sums of the split residual GEMMs
 };
 
 // Position p of session s in codec_tokens: codebook p % 8, frame p / 8 of
@@ -65,10 +69,30 @@ __device__ __forceinline__ void commit_end(const Frame& f, int s, int32_t end) {
 
 struct Layout {
   size_t list, count, eos_list, eos_count, eos_slot, x, q, kc, vc, att, h, logits, tokens, emb_acc, ctr, inv,
-      eos_partial, eos_logit, total;
+      eos_partial, eos_logit, part, total;
 };
 
 inline size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
+
+// K splits of a phase-kernel tensor-core GEMM whose output feeds the residual
+// (o-projection, FFN2): the largest divisor of its 64-column K chunks, up to
+// 8, that keeps rows/128 x n/256 tiles x splits within one wave of 148 CTAs.
+// The f32 partial sums go to the workspace's `part` region.
+// The benchmark shape (d 256, 1 layer, FFN 1024) runs on the fused kernels;
+// the phase kernels serve it only when asked, without splitting K, so its
+// workspace keeps no room for partial sums.
+inline bool fused_frame_shape(int d, int L, int F) { return d == 256 && L == 1 && F == 1024; }
+constexpr int kPhaseGemmItems = 148;
+constexpr int kMaxPhaseSplits = 8;
+inline int phase_splits(int rows, int n, int k) {
+  const int tiles = ((rows + 127) / 128) * ((n + 255) / 256);
+  const int chunks = k / 64;
+  int best = 1;
+  for (int s = 2; s <= kMaxPhaseSplits; ++s) {
+    if (chunks % s == 0 && tiles * s <= kPhaseGemmItems) best = s;
+  }
+  return best;
+}
 
 inline Layout make_layout(int d, int L, int F, int n, int rp) {
   Layout lo{};
@@ -97,6 +121,10 @@ inline Layout make_layout(int d, int L, int F, int n, int rp) {
   lo.inv = take(4 * static_cast<size_t>(n));
   lo.eos_partial = take(4 * static_cast<size_t>(n) * kPositions * kEosChunks);
   lo.eos_logit = take(4 * static_cast<size_t>(n) * kPositions);
+  const int splits = fused_frame_shape(d, L, F)
+                         ? 0
+                         : std::max(phase_splits(static_cast<int>(R), d, d), phase_splits(static_cast<int>(R), d, F));
+  lo.part = take(4 * static_cast<size_t>(splits) * R * d);
   lo.total = off;
   return lo;
 }

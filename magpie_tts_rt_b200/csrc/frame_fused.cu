@@ -362,6 +362,21 @@ __device__ __forceinline__ const bf16* next_weights(const WeightMaps& maps, Smem
   return sm.ring[idx & 1];
 }
 
+// Phase clock stamps (trace hook): CTA 0 of the first cluster writes its SM
+// clock at 16 points of every position, then the clock and the global timer
+// at the start and the end of the frame (to convert cycles to time).
+__device__ __forceinline__ void stamp(const Frame& f, int p, int i) {
+  if (f.trace != nullptr && blockIdx.x == 0 && threadIdx.x == 0) f.trace[p * 16 + i] = clock64();
+}
+__device__ __forceinline__ void stamp_frame(const Frame& f, int at) {
+  if (f.trace != nullptr && blockIdx.x == 0 && threadIdx.x == 0) {
+    uint64_t ns;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(ns));
+    f.trace[kPositions * 16 + 2 * at] = clock64();
+    f.trace[kPositions * 16 + 2 * at + 1] = ns;
+  }
+}
+
 __device__ __forceinline__ int64_t fused_input_token(const Frame& f, const Smem& sm, int s_local, int p) {
   if (f.forced) {
     const int64_t t = f.forced[static_cast<int64_t>(sm.sess[s_local]) * kPositions + p];
@@ -444,7 +459,9 @@ __global__ void __cluster_dims__(kCS, 1, 1) __launch_bounds__(kThreads, 1)
   Round rd;
   const int head = c / kG, ds = c % kG;
   const uint32_t slice_bytes = kM * kDC * 2;  // a [16][16] bf16 slice
+  stamp_frame(f, 0);
   for (int p = 0; p < kPositions; ++p) {
+    stamp(f, p, 0);
     // ---------------- Ph0: in-projection + position embedding
     if (p > 0 && folded) {
       for (int i = threadIdx.x; i < kM * (kD / 8); i += blockDim.x) {
@@ -494,6 +511,7 @@ __global__ void __cluster_dims__(kCS, 1, 1) __launch_bounds__(kThreads, 1)
       push_all16(sm, rd, kDC, sm.x, kLd256, kDC * c);
       finish_round(sm, rd, kCS * slice_bytes);
     }
+    stamp(f, p, 1);
 
     // ---------------- Ph1: LN1, qkv slice, partial scores to the head group
     layer_norm16(sm.x, sm.xa, f.ln1);
@@ -526,8 +544,10 @@ __global__ void __cluster_dims__(kCS, 1, 1) __launch_bounds__(kThreads, 1)
       st_async_v4(cluster_addr(reinterpret_cast<const float*>(&sm.part[ds][0][0]) + ch * 4, dst), v,
                   cluster_addr(&sm.xbar[rd.bar()], dst));
     }
+    stamp(f, p, 2);
     push_tokens(sm, rd, c);
     finish_round(sm, rd, kG * uint32_t(kM * kPositions * 4) + kTokenBytes);
+    stamp(f, p, 3);
 
     // ---------------- Ph2: attention (head, dims slice), all-gathered
     {
@@ -556,8 +576,10 @@ __global__ void __cluster_dims__(kCS, 1, 1) __launch_bounds__(kThreads, 1)
       sm.stage[r * kHD + jk] = f2bf(o_acc);
     }
     __syncthreads();
+    stamp(f, p, 4);
     push_all16(sm, rd, kHD, sm.xa, kLd256, head * kHeadDim + ds * kHD);
     finish_round(sm, rd, kCS * slice_bytes);
+    stamp(f, p, 5);
 
     // ---------------- Ph3: o-projection + residual, all-gathered
     {
@@ -569,8 +591,10 @@ __global__ void __cluster_dims__(kCS, 1, 1) __launch_bounds__(kThreads, 1)
             pack_bf16x2(__fadd_rn(x0, round_bf16(v0)), __fadd_rn(x1, round_bf16(v1)));
       });
     }
+    stamp(f, p, 6);
     push_all16(sm, rd, kDC, sm.x, kLd256, kDC * c);
     finish_round(sm, rd, kCS * slice_bytes);
+    stamp(f, p, 7);
 
     // ---------------- Ph4: LN2, FFN1 slice + GELU, FFN2 partials to the owners
     layer_norm16(sm.x, sm.xa, f.ln2);
@@ -581,6 +605,7 @@ __global__ void __cluster_dims__(kCS, 1, 1) __launch_bounds__(kThreads, 1)
             pack_bf16x2(gelu_tanh_f(round_bf16(v0)), gelu_tanh_f(round_bf16(v1)));
       });
     }
+    stamp(f, p, 8);
     {
       const bf16* w = next_weights(maps, sm, folded, p, 4, c);
       gemm16<32, 4>(sm.hc, kLdH, w, kD, &sm.u.red[0][0], [&](int r, int j, float v0, float v1) {
@@ -588,7 +613,9 @@ __global__ void __cluster_dims__(kCS, 1, 1) __launch_bounds__(kThreads, 1)
         st_async_v2f(cluster_addr(&sm.big.recv[c][r][j % kDC], dst), v0, v1, cluster_addr(&sm.xbar[rd.bar()], dst));
       });
     }
+    stamp(f, p, 9);
     finish_round(sm, rd, kCS * uint32_t(kM * kDC * 4));
+    stamp(f, p, 10);
 
     // ---------------- Ph5: FFN2 output features (16 partials in CTA order) + residual
     {
@@ -602,6 +629,7 @@ __global__ void __cluster_dims__(kCS, 1, 1) __launch_bounds__(kThreads, 1)
     __syncthreads();
     push_all16(sm, rd, kDC, sm.x, kLd256, kDC * c);
     finish_round(sm, rd, kCS * slice_bytes);
+    stamp(f, p, 11);
 
     // ---------------- Ph6: head p; logits rows to the owners
     const int hcols = c < kCS - 1 ? kHeadCols : kVocab - (kCS - 1) * kHeadCols;
@@ -624,6 +652,7 @@ __global__ void __cluster_dims__(kCS, 1, 1) __launch_bounds__(kThreads, 1)
         }
       });
     }
+    stamp(f, p, 12);
     {
       const int per_row = hcols / 8;
       for (int i = threadIdx.x; i < rows * per_row; i += blockDim.x) {
@@ -636,6 +665,7 @@ __global__ void __cluster_dims__(kCS, 1, 1) __launch_bounds__(kThreads, 1)
     }
     push_tokens(sm, rd, c);
     finish_round(sm, rd, (c < n_sess ? uint32_t(rp * kVocab * 2) : 0u) + kTokenBytes);
+    stamp(f, p, 13);
 
     // ---------------- Ph7: owner samples, broadcasts the token
     if (owner) {
@@ -661,9 +691,12 @@ __global__ void __cluster_dims__(kCS, 1, 1) __launch_bounds__(kThreads, 1)
         if (!f.prm.argmax && counter_valid) sm.ctr = call.counter + 1;
       }
     }
+    stamp(f, p, 14);
     if (!owner) push_tokens(sm, rd, c);  // the owners' tokens are their 4 bytes
     finish_round(sm, rd, kTokenBytes);
+    stamp(f, p, 15);
   }
+  stamp_frame(f, 1);
 
   // ---- commit (owner): tokens, counter, flags, next-frame embedding
   if (owner) {
