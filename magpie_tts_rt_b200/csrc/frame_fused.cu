@@ -100,6 +100,10 @@ union BigBuffer {
   bf16 src[kM * kLd768];
   float recv[kCS][kM][kDC];
   unsigned char sample_scratch[kSampleScratchBytes];
+  struct {                           // this CTA's head columns in candidate form, per session
+    uint16_t key[kM][kHeadCols];
+    float score[kM][kHeadCols];
+  } cand_out;
 };
 
 struct __align__(1024) Smem {
@@ -112,14 +116,22 @@ struct __align__(1024) Smem {
   bf16 qs[kM][kHD];
   float part[kG][kM][kPositions];  // partial q.k received from the head group
   union {
-    bf16 lg[2 * kVocab];       // this CTA's session logits (owner), written by all CTAs
+    struct {                   // this CTA's session row in candidate form (owner), written by all CTAs
+      uint16_t key[2048];      // order keys of the constrained values
+      float score[2048];       // Philox-Gumbel scores
+      uint32_t nf[kCS];        // per sender: a raw value was non-finite
+    } cand;
     float red[8][kM * 8 * 2];  // cross-warp K-split partials
   } u;
   bf16 stage[kM * kHeadCols];  // outgoing slice (bf16) or partial scores (f32)
+  bf16 hbias[kHeadCols];       // this CTA's head bias slice of the position (fetched at its start)
   SampleShared samp;
   int32_t tok[kM][kPositions];  // tokens of the tile's sessions (every CTA)
   int32_t sess[kM];             // stream ids of the tile's sessions
-  int64_t ctr;                  // owner: working RNG counter
+  int64_t seed[kM];             // the tile's sessions: Philox seeds,
+  int64_t ctrs[kM];             // working RNG counters (every CTA advances them alike),
+  uint32_t flags[kM];           // unfinished | finished << 1 | forbid_eos << 2,
+  uint32_t cnf[kM];             // and this CTA's non-finite flag of the position
   int32_t inv;                  // owner: invalid flag
   int32_t n_sess;
   int32_t err;
@@ -128,6 +140,7 @@ struct __align__(1024) Smem {
   uint32_t sink[kCS];           // round tokens (never read)
 };
 constexpr size_t kSmemBytes = sizeof(Smem) + 1024;
+static_assert(kSmemBytes <= 227 * 1024, "fused frame shared memory exceeds the per-CTA limit");
 
 // ---------------------------------------------------------------------------
 // 16-row GEMM on the tile: C[16][8*NT] = A[16][16*KS] * B[8*NT][16*KS]^T.
@@ -260,12 +273,13 @@ struct Round {
   __device__ __forceinline__ uint32_t parity() const { return (r >> 1) & 1u; }
 };
 
-// Pushes the [16][cols] bf16 staging slice to every CTA's buffer at
-// (dst_ld, dst_col) (cols * 2 and dst_col * 2 multiples of 16 bytes).
-__device__ __forceinline__ void push_all16(Smem& sm, const Round& rd, int cols, const bf16* dst, int dst_ld,
+// Pushes rows [0, rows) of the [16][cols] bf16 staging slice to every CTA's
+// buffer at (dst_ld, dst_col) (cols * 2 and dst_col * 2 multiples of 16
+// bytes); rows past the tile's sessions are never sent.
+__device__ __forceinline__ void push_all16(Smem& sm, const Round& rd, int rows, int cols, const bf16* dst, int dst_ld,
                                            int dst_col) {
   const int per_row = cols / 8;
-  const int chunks = kM * per_row;
+  const int chunks = rows * per_row;
   for (int i = threadIdx.x; i < chunks * kCS; i += blockDim.x) {
     const int rank = i / chunks, k = i % chunks;
     const int r = k / per_row, cc = k % per_row;
@@ -434,11 +448,17 @@ __global__ void __cluster_dims__(kCS, 1, 1) __launch_bounds__(kThreads, 1)
   __syncthreads();
   if (warp == 0) issue_chunk(maps, sm, folded, 0, 0, c);
 
+  // ---- session state (every CTA scores every session's tokens)
+  if (static_cast<int>(threadIdx.x) < n_sess) {
+    const int sid = sm.sess[threadIdx.x];
+    sm.seed[threadIdx.x] = f.seed[sid];
+    sm.ctrs[threadIdx.x] = f.counter_io[sid];
+    sm.flags[threadIdx.x] = (f.unfinished[sid] ? 1u : 0u) | (f.finished[sid] ? 2u : 0u) | (f.forbid[sid] ? 4u : 0u);
+  }
   // ---- owner state
   const bool owner = c < n_sess;
   if (owner && threadIdx.x == 0) {
     const int sid = sm.sess[c];
-    sm.ctr = f.counter_io[sid];
     int32_t inv = 0;
     bool en = !f.unfinished[sid] && !f.finished[sid] && !f.forbid[sid];
     if (en && f.final_w == nullptr) {
@@ -454,14 +474,24 @@ __global__ void __cluster_dims__(kCS, 1, 1) __launch_bounds__(kThreads, 1)
       f.eos_slot[sid] = -1;
     }
   }
+  for (int i = threadIdx.x; i < kM * kLd256 / 8; i += blockDim.x) {
+    reinterpret_cast<uint4*>(sm.x)[i] = make_uint4(0, 0, 0, 0);  // rows past the tile's sessions stay zero
+  }
   cluster.sync();  // every CTA is running and its barriers initialised before any DSMEM access
 
   Round rd;
+  const int hcols = c < kCS - 1 ? kHeadCols : kVocab - (kCS - 1) * kHeadCols;
+  const bool bias_async = (reinterpret_cast<uintptr_t>(f.head_b) & 3u) == 0;
   const int head = c / kG, ds = c % kG;
-  const uint32_t slice_bytes = kM * kDC * 2;  // a [16][16] bf16 slice
+  const uint32_t slice_bytes = static_cast<uint32_t>(rows) * kDC * 2;  // the live rows of a [16][16] bf16 slice
   stamp_frame(f, 0);
   for (int p = 0; p < kPositions; ++p) {
     stamp(f, p, 0);
+    if (threadIdx.x < kM) sm.cnf[threadIdx.x] = 0;
+    // the head bias slice of this position, in flight until the head phase
+    if (bias_async && 2 * static_cast<int>(threadIdx.x) < hcols) {
+      cp_async4(&sm.hbias[2 * threadIdx.x], f.head_b + static_cast<int64_t>(p) * kVocab + kHeadCols * c + 2 * threadIdx.x);
+    }
     // ---------------- Ph0: in-projection + position embedding
     if (p > 0 && folded) {
       for (int i = threadIdx.x; i < kM * (kD / 8); i += blockDim.x) {
@@ -508,7 +538,7 @@ __global__ void __cluster_dims__(kCS, 1, 1) __launch_bounds__(kThreads, 1)
         *reinterpret_cast<uint32_t*>(sm.stage + r * kDC + j) =
             pack_bf16x2(__fadd_rn(y0, bf2f(pos[0])), __fadd_rn(y1, bf2f(pos[1])));
       });
-      push_all16(sm, rd, kDC, sm.x, kLd256, kDC * c);
+      push_all16(sm, rd, rows, kDC, sm.x, kLd256, kDC * c);
       finish_round(sm, rd, kCS * slice_bytes);
     }
     stamp(f, p, 1);
@@ -537,16 +567,18 @@ __global__ void __cluster_dims__(kCS, 1, 1) __launch_bounds__(kThreads, 1)
       }
       scores[r * kPositions + jk] = s;
       __syncthreads();
-      // 1 KB to each of the 4 CTAs of head h: 64 chunks each
+      // the live rows (64 bytes each) to each of the 4 CTAs of head h
       const int g = threadIdx.x >> 6, ch = threadIdx.x & 63;
       const int dst = head * kG + g;
-      const uint4 v = *reinterpret_cast<const uint4*>(scores + ch * 4);
-      st_async_v4(cluster_addr(reinterpret_cast<const float*>(&sm.part[ds][0][0]) + ch * 4, dst), v,
-                  cluster_addr(&sm.xbar[rd.bar()], dst));
+      if (ch < rows * 4) {
+        const uint4 v = *reinterpret_cast<const uint4*>(scores + ch * 4);
+        st_async_v4(cluster_addr(reinterpret_cast<const float*>(&sm.part[ds][0][0]) + ch * 4, dst), v,
+                    cluster_addr(&sm.xbar[rd.bar()], dst));
+      }
     }
     stamp(f, p, 2);
     push_tokens(sm, rd, c);
-    finish_round(sm, rd, kG * uint32_t(kM * kPositions * 4) + kTokenBytes);
+    finish_round(sm, rd, kG * uint32_t(rows * kPositions * 4) + kTokenBytes);
     stamp(f, p, 3);
 
     // ---------------- Ph2: attention (head, dims slice), all-gathered
@@ -577,7 +609,7 @@ __global__ void __cluster_dims__(kCS, 1, 1) __launch_bounds__(kThreads, 1)
     }
     __syncthreads();
     stamp(f, p, 4);
-    push_all16(sm, rd, kHD, sm.xa, kLd256, head * kHeadDim + ds * kHD);
+    push_all16(sm, rd, rows, kHD, sm.xa, kLd256, head * kHeadDim + ds * kHD);
     finish_round(sm, rd, kCS * slice_bytes);
     stamp(f, p, 5);
 
@@ -592,7 +624,7 @@ __global__ void __cluster_dims__(kCS, 1, 1) __launch_bounds__(kThreads, 1)
       });
     }
     stamp(f, p, 6);
-    push_all16(sm, rd, kDC, sm.x, kLd256, kDC * c);
+    push_all16(sm, rd, rows, kDC, sm.x, kLd256, kDC * c);
     finish_round(sm, rd, kCS * slice_bytes);
     stamp(f, p, 7);
 
@@ -610,11 +642,13 @@ __global__ void __cluster_dims__(kCS, 1, 1) __launch_bounds__(kThreads, 1)
       const bf16* w = next_weights(maps, sm, folded, p, 4, c);
       gemm16<32, 4>(sm.hc, kLdH, w, kD, &sm.u.red[0][0], [&](int r, int j, float v0, float v1) {
         const int dst = j / kDC;
-        st_async_v2f(cluster_addr(&sm.big.recv[c][r][j % kDC], dst), v0, v1, cluster_addr(&sm.xbar[rd.bar()], dst));
+        if (r < rows) {
+          st_async_v2f(cluster_addr(&sm.big.recv[c][r][j % kDC], dst), v0, v1, cluster_addr(&sm.xbar[rd.bar()], dst));
+        }
       });
     }
     stamp(f, p, 9);
-    finish_round(sm, rd, kCS * uint32_t(kM * kDC * 4));
+    finish_round(sm, rd, kCS * uint32_t(rows * kDC * 4));
     stamp(f, p, 10);
 
     // ---------------- Ph5: FFN2 output features (16 partials in CTA order) + residual
@@ -627,18 +661,18 @@ __global__ void __cluster_dims__(kCS, 1, 1) __launch_bounds__(kThreads, 1)
       sm.stage[r * kDC + j] = f2bf(__fadd_rn(bf2f(sm.x[r * kLd256 + n]), round_bf16(acc)));
     }
     __syncthreads();
-    push_all16(sm, rd, kDC, sm.x, kLd256, kDC * c);
+    push_all16(sm, rd, rows, kDC, sm.x, kLd256, kDC * c);
     finish_round(sm, rd, kCS * slice_bytes);
     stamp(f, p, 11);
 
     // ---------------- Ph6: head p; logits rows to the owners
-    const int hcols = c < kCS - 1 ? kHeadCols : kVocab - (kCS - 1) * kHeadCols;
+    if (bias_async) cp_async_wait_all();  // published by next_weights' barrier
     {
       const bf16* w = next_weights(maps, sm, folded, p, 5, c);
       gemm16<16, 16>(sm.x, kLd256, w, kHeadCols, &sm.u.red[0][0], [&](int r, int j, float v0, float v1) {
         if (j < hcols) {  // hcols is even: pairs never straddle it
           const int n = kHeadCols * c + j;
-          const bf16* hb = f.head_b + static_cast<int64_t>(p) * kVocab + n;
+          const bf16* hb = bias_async ? &sm.hbias[j] : f.head_b + static_cast<int64_t>(p) * kVocab + n;
           const bf16 y0 = f2bf(__fadd_rn(v0, bf2f(hb[0])));
           const bf16 y1 = f2bf(__fadd_rn(v1, bf2f(hb[1])));
           sm.stage[r * kHeadCols + j] = y0;
@@ -654,46 +688,76 @@ __global__ void __cluster_dims__(kCS, 1, 1) __launch_bounds__(kThreads, 1)
     }
     stamp(f, p, 12);
     {
-      const int per_row = hcols / 8;
-      for (int i = threadIdx.x; i < rows * per_row; i += blockDim.x) {
-        const int r = i / per_row, cc = i % per_row;
-        const int sl = r / rp, sub = r % rp;
-        const uint4 v = *reinterpret_cast<const uint4*>(sm.stage + r * kHeadCols + cc * 8);
-        st_async_v4(cluster_addr(&sm.u.lg[sub * kVocab + kHeadCols * c + cc * 8], sl), v,
-                    cluster_addr(&sm.xbar[rd.bar()], sl));
+      // every live session's row (pair) in candidate form: the constrained
+      // value's order key and its fast Philox-Gumbel score, for this CTA's columns
+      const float cfg = f.prm.cfg_scale, temp = f.prm.temperature;
+      for (int i = threadIdx.x; i < n_sess * hcols; i += blockDim.x) {
+        const int sl = i / hcols, j = i % hcols, t = kHeadCols * c + j;
+        const float cond = bf2f(sm.stage[(sl * rp) * kHeadCols + j]);
+        const float raw = rp == 2 ? guided_logit(cond, bf2f(sm.stage[(sl * rp + 1) * kHeadCols + j]), cfg) : cond;
+        const uint32_t fl = sm.flags[sl];
+        bool nf = false;
+        const float v = constrain_token(t, raw, fl & 1u, fl & 2u, fl & 4u, &nf);
+        if (nf) atomicOr(&sm.cnf[sl], 1u);
+        sm.big.cand_out.key[sl][j] = static_cast<uint16_t>(value_key16(v));
+        sm.big.cand_out.score[sl][j] =
+            f.prm.argmax ? 0.f : token_score_fast(v, t, temp, call_seed32(sm.seed[sl]), call_offset(sm.ctrs[sl]));
+      }
+      __syncthreads();
+      const int kch = hcols / 8, sch = hcols / 4, per = kch + sch;  // 16-byte chunks per session
+      for (int i = threadIdx.x; i < n_sess * per; i += blockDim.x) {
+        const int sl = i / per, q = i % per;
+        const uint32_t bar = cluster_addr(&sm.xbar[rd.bar()], sl);
+        if (q < kch) {
+          const uint4 v = reinterpret_cast<const uint4*>(&sm.big.cand_out.key[sl][0])[q];
+          st_async_v4(cluster_addr(&sm.u.cand.key[kHeadCols * c + 8 * q], sl), v, bar);
+        } else {
+          const uint4 v = reinterpret_cast<const uint4*>(&sm.big.cand_out.score[sl][0])[q - kch];
+          st_async_v4(cluster_addr(&sm.u.cand.score[kHeadCols * c + 4 * (q - kch)], sl), v, bar);
+        }
+      }
+      if (static_cast<int>(threadIdx.x) < n_sess) {
+        const int d = static_cast<int>(threadIdx.x);
+        st_async_b32(cluster_addr(&sm.u.cand.nf[c], d), sm.cnf[d], cluster_addr(&sm.xbar[rd.bar()], d));
       }
     }
     push_tokens(sm, rd, c);
-    finish_round(sm, rd, (c < n_sess ? uint32_t(rp * kVocab * 2) : 0u) + kTokenBytes);
+    finish_round(sm, rd, (c < n_sess ? uint32_t(kVocab * 6 + kCS * 4) : 0u) + kTokenBytes);
     stamp(f, p, 13);
 
-    // ---------------- Ph7: owner samples, broadcasts the token
+    // ---------------- Ph7: owner selects the token, broadcasts it
     if (owner) {
-      const int sid = sm.sess[c];
-      SampleCall call;
-      call.logits = &sm.u.lg[0];
-      call.uncond_offset = kVocab;
-      call.kind = rp == 2 ? kLogitsBf16Cfg : kLogitsBf16;
-      call.unfinished = f.unfinished[sid];
-      call.finished = f.finished[sid];
-      call.forbid_eos = f.forbid[sid];
-      call.seed = f.seed[sid];
-      call.counter = sm.ctr;
+      SampleCall call{};
+      call.kind = kLogitsBf16;
+      const uint32_t fl = sm.flags[c];
+      call.unfinished = fl & 1u;
+      call.finished = fl & 2u;
+      call.forbid_eos = fl & 4u;
+      call.seed = sm.seed[c];
+      call.counter = sm.ctrs[c];
+      uint32_t any_nf = 0;
+#pragma unroll
+      for (int k = 0; k < kCS; ++k) any_nf |= sm.u.cand.nf[k];
       int invalid = 0;
-      const int token = sample_block(call, f.prm, sm.samp, sm.big.sample_scratch, &invalid);
+      const int token =
+          sample_block_scored(sm.u.cand.key, sm.u.cand.score, any_nf != 0, call, f.prm, sm.samp, sm.big.sample_scratch,
+                              &invalid);
       if (threadIdx.x < kCS) {
         const int d = static_cast<int>(threadIdx.x);
         st_async_b32(cluster_addr(&sm.tok[c][p], d), static_cast<uint32_t>(token), cluster_addr(&sm.xbar[rd.bar()], d));
       }
-      if (threadIdx.x == 0) {
-        sm.inv |= invalid;
-        const bool counter_valid = call.counter >= 0 && call.counter <= kMaxCounter;
-        if (!f.prm.argmax && counter_valid) sm.ctr = call.counter + 1;
-      }
+      if (threadIdx.x == 0) sm.inv |= invalid;
     }
     stamp(f, p, 14);
     if (!owner) push_tokens(sm, rd, c);  // the owners' tokens are their 4 bytes
     finish_round(sm, rd, kTokenBytes);
+    // every CTA advances the tile's counters as the owners do (sampling only)
+    if (threadIdx.x == 0 && !f.prm.argmax) {
+      for (int sl = 0; sl < n_sess; ++sl) {
+        const int64_t k = sm.ctrs[sl];
+        if (k >= 0 && k <= kMaxCounter) sm.ctrs[sl] = k + 1;
+      }
+    }
     stamp(f, p, 15);
   }
   stamp_frame(f, 1);
@@ -708,7 +772,7 @@ __global__ void __cluster_dims__(kCS, 1, 1) __launch_bounds__(kThreads, 1)
       f.tokens[static_cast<int64_t>(sid) * kPositions + pp] = t;
     }
     if (threadIdx.x == 0) {
-      f.counter_io[sid] = sm.ctr;
+      f.counter_io[sid] = sm.ctrs[c];
       f.invalid_rows[sid] = sm.inv | (sm.err ? 4 : 0);
       if (f.eos_slot[sid] < 0) commit_end(f, sid, f.finished[sid] ? 0 : -1);
     }

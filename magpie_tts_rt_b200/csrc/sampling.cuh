@@ -54,6 +54,22 @@ struct SampleCall {
   int64_t counter;
 };
 
+// The constrained value of token t from its raw (guided) logit: forbidden
+// specials, the EOS gate, finished -> EOS only; a non-finite raw value
+// becomes -inf and sets *nonfinite.
+__device__ __forceinline__ float constrain_token(int t, float raw, bool unfinished, bool finished, bool forbid_eos,
+                                                 bool* nonfinite) {
+  float x = raw;
+  if (!isfinite(x)) {
+    *nonfinite = true;
+    x = -CUDART_INF_F;
+  }
+  const bool forbidden_special = t >= kCodebook && t != kEosId;
+  if (forbidden_special || ((unfinished || forbid_eos) && t == kEosId)) x = -CUDART_INF_F;
+  if (finished) x = (t == kEosId) ? 0.0f : -CUDART_INF_F;
+  return x;
+}
+
 // Loads this thread's 8 constrained values.  Returns per-thread non-finite flag.
 __device__ __forceinline__ bool load_constrained(const SampleCall& c, const SamplingParams& prm,
                                                  float (&v)[kItems]) {
@@ -94,18 +110,8 @@ __device__ __forceinline__ bool load_constrained(const SampleCall& c, const Samp
 #pragma unroll
   for (int i = 0; i < kItems; ++i) {
     const int t = base + i;
-    float x = -CUDART_INF_F;
-    if (t < kVocab) {
-      x = raw[i];
-      if (!isfinite(x)) {
-        nonfinite = true;
-        x = -CUDART_INF_F;
-      }
-      const bool forbidden_special = t >= kCodebook && t != kEosId;
-      if (forbidden_special || ((c.unfinished || c.forbid_eos) && t == kEosId)) x = -CUDART_INF_F;
-      if (c.finished) x = (t == kEosId) ? 0.0f : -CUDART_INF_F;
-    }
-    v[i] = x;
+    v[i] = t < kVocab ? constrain_token(t, raw[i], c.unfinished, c.finished, c.forbid_eos, &nonfinite)
+                      : -CUDART_INF_F;
   }
   return nonfinite;
 }
@@ -116,6 +122,25 @@ __device__ __forceinline__ uint32_t f32_key(float x) {
 }
 __device__ __forceinline__ float key_f32(uint32_t k) {
   return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
+}
+
+// Sums the per-warp histograms bin by bin into the first one (thread t owns
+// bin t: no two threads touch the same word), then publishes it.
+__device__ __forceinline__ void fold_histograms(uint32_t* hist) {
+  static_assert(kSampleThreads == 256, "one thread per bin");
+  uint32_t t = 0;
+#pragma unroll
+  for (int w = 0; w < kSampleWarps; ++w) t += hist[w * 256 + threadIdx.x];
+  hist[threadIdx.x] = t;
+  __syncthreads();
+}
+
+// Lane l's eight consecutive bins 8l .. 8l+7 of the folded histogram.
+__device__ __forceinline__ void lane_bins(const uint32_t* hist, int lane, uint32_t (&c)[8]) {
+  const uint4 a = reinterpret_cast<const uint4*>(hist + 8 * lane)[0];
+  const uint4 b = reinterpret_cast<const uint4*>(hist + 8 * lane)[1];
+  c[0] = a.x; c[1] = a.y; c[2] = a.z; c[3] = a.w;
+  c[4] = b.x; c[5] = b.y; c[6] = b.z; c[7] = b.w;
 }
 
 // One radix pass: histogram of digit (key >> shift) & 0xff over keys matching
@@ -135,17 +160,16 @@ __device__ __forceinline__ void radix_pass(const uint32_t (&key)[kItems], int sh
     if (base + i < kVocab && (key[i] & mask) == prefix) atomicAdd(&wh[(key[i] >> shift) & 0xffu], 1u);
   }
   __syncthreads();
+  fold_histograms(hist);
   if (warp == 0) {
-    uint32_t c[8];
+    // lane l owns digits 255 - 8l - j (descending), j = 0..7
+    uint32_t c[8], d[8];
+    lane_bins(hist, 31 - lane, d);
     uint32_t sum = 0;
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
-      const int bin = 255 - lane * 8 - j;
-      uint32_t t = 0;
-#pragma unroll
-      for (int w = 0; w < kSampleWarps; ++w) t += hist[w * 256 + bin];
-      c[j] = t;
-      sum += t;
+      c[j] = d[7 - j];
+      sum += c[j];
     }
     if (kFirst && lane == 0) {
       uint32_t finite = 0, nf = 0;
@@ -203,18 +227,14 @@ __device__ __forceinline__ bool window_kth_key16(const uint32_t (&key)[kItems], 
     if (base + i < kVocab && dist < 256u) atomicAdd(&wh[dist], 1u);
   }
   __syncthreads();
+  fold_histograms(hist);
   if (warp == 0) {
     // lane l owns distances 8l .. 8l+7 (descending keys)
     uint32_t c[8];
+    lane_bins(hist, lane, c);
     uint32_t sum = 0;
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      uint32_t t = 0;
-#pragma unroll
-      for (int w = 0; w < kSampleWarps; ++w) t += hist[w * 256 + lane * 8 + j];
-      c[j] = t;
-      sum += t;
-    }
+    for (int j = 0; j < 8; ++j) sum += c[j];
     if (lane == 0) {
       uint32_t finite = 0, nf = 0;
 #pragma unroll
@@ -446,6 +466,156 @@ __device__ __forceinline__ int sample_block(const SampleCall& c, const SamplingP
         if (score > best || (score == best && t < best_id)) {
           best = score;
           best_id = t;
+        }
+      }
+      block_argmax(best, best_id, sh);
+    }
+  }
+  const float b = sh.warp_best[0];
+  int token = sh.warp_best_id[0];
+  if (token >= kVocab || b == -CUDART_INF_F) {
+    invalid = 1;
+    token = 0;
+  }
+  *invalid_out = invalid;
+  __syncthreads();  // sh is reused by the next call
+  return token;
+}
+
+// ---------------------------------------------------------------------------
+// Pre-scored form (fused cluster kernel): the CTAs that hold a row's logits
+// compute every token's constrained value and fast Philox-Gumbel score where
+// the logits are; the row's owner receives, per token, the 16-bit order key
+// of the value and the fast score, and selects: the inclusive top-k
+// threshold on the keys (block_kth_key<16>), the left-most arg-max of the
+// fast scores of the finite tokens at or above it, and, when any other such
+// token lies within kVerifyMargin of that best, the arg-max of the exact
+// scores (value / T + clamped_gumbel) of those near tokens.  Same result as
+// sample_block on the same logits (the same fast-then-verify rule; the keys
+// order the bf16-valued values exactly).
+// ---------------------------------------------------------------------------
+
+constexpr uint32_t kNegInfKey16 = 0x007fu;  // f32_key(-inf) >> 16
+
+__device__ __forceinline__ uint32_t value_key16(float v) { return f32_key(v) >> 16; }
+// The bf16-valued value a 16-bit key stands for (exact inverse of value_key16).
+__device__ __forceinline__ float key16_value(uint32_t k) {
+  return key_f32((k << 16) | ((k & 0x8000u) ? 0u : 0xffffu));
+}
+
+// Philox stream of one (session, position) call: seed and counter offset
+// (0 where invalid; the call is then flagged invalid by the sampler).
+__device__ __forceinline__ uint32_t call_seed32(int64_t seed) {
+  return (seed >= 0 && static_cast<uint64_t>(seed) < (1ull << 32)) ? static_cast<uint32_t>(seed) : 0u;
+}
+__device__ __forceinline__ uint64_t call_offset(int64_t counter) {
+  return (counter >= 0 && counter <= kMaxCounter) ? static_cast<uint64_t>(counter) * kPhiloxStride : 0ull;
+}
+
+// Fast score of token t with constrained value v (-inf: not a candidate):
+// value / T + fast_gumbel, within 1e-4 of the exact score; the selecting
+// block rescores exactly whenever another candidate is within kVerifyMargin.
+__device__ __forceinline__ float token_score_fast(float v, int t, float temperature, uint32_t seed32, uint64_t off64) {
+  if (v == -CUDART_INF_F) return -CUDART_INF_F;
+  return __fadd_rn(__fdiv_rn(v, temperature), fast_gumbel(philox_uniform(seed32, off64 + static_cast<uint64_t>(t))));
+}
+
+// keys[t], fast scores[t] for t < kVocab (shared memory, 16-byte aligned);
+// any_nonfinite: a raw value of the row was non-finite.  c supplies the
+// flags, seed and counter (its logits are not read).  Returns the token
+// (block-uniform) and sets *invalid_out as sample_block does.
+__device__ __forceinline__ int sample_block_scored(const uint16_t* keys, const float* scores, bool any_nonfinite,
+                                                   const SampleCall& c, const SamplingParams& prm, SampleShared& sh,
+                                                   void* scratch, int* invalid_out) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int base = threadIdx.x * kItems;
+  uint32_t* hist = static_cast<uint32_t*>(scratch);
+  uint32_t key[kItems];
+  if (base + kItems <= kVocab) {
+    const uint4 k4 = *reinterpret_cast<const uint4*>(keys + base);
+    const uint16_t* kk = reinterpret_cast<const uint16_t*>(&k4);
+#pragma unroll
+    for (int i = 0; i < kItems; ++i) key[i] = kk[i];
+  } else {
+#pragma unroll
+    for (int i = 0; i < kItems; ++i) key[i] = base + i < kVocab ? keys[base + i] : kNegInfKey16;
+  }
+  uint32_t fin = 0;
+#pragma unroll
+  for (int i = 0; i < kItems; ++i) fin += (base + i < kVocab && key[i] != kNegInfKey16) ? 1u : 0u;
+  fin = __reduce_add_sync(0xffffffffu, fin);
+  if (lane == 0) {
+    sh.warp_nonfinite[warp] = any_nonfinite ? 1u : 0u;
+    sh.warp_finite[warp] = fin;
+  }
+  float best = -CUDART_INF_F;
+  int best_id = kVocab;
+  int invalid = 0;
+  // values compared as floats, as sample_block does (-0 and +0 tie)
+  float v[kItems];
+#pragma unroll
+  for (int i = 0; i < kItems; ++i) v[i] = key16_value(key[i]);
+  if (prm.argmax) {
+#pragma unroll
+    for (int i = 0; i < kItems; ++i) {
+      const int t = base + i;
+      if (t < kVocab && (v[i] > best || (v[i] == best && t < best_id))) {
+        best = v[i];
+        best_id = t;
+      }
+    }
+    block_argmax(best, best_id, sh);
+    uint32_t total = 0;
+#pragma unroll
+    for (int w = 0; w < kSampleWarps; ++w) total += sh.warp_finite[w];
+    invalid = (any_nonfinite || total == 0) ? 1 : 0;
+  } else {
+    const float threshold = key16_value(block_kth_key<16>(key, prm.top_k, sh, hist));
+    invalid = (sh.nonfinite || sh.finite_count == 0) ? 1 : 0;
+    if (c.unfinished && c.finished) invalid = 1;
+    if (c.finished && c.forbid_eos) invalid = 1;
+    const bool seed_valid = c.seed >= 0 && static_cast<uint64_t>(c.seed) < (1ull << 32);
+    const bool counter_valid = c.counter >= 0 && c.counter <= kMaxCounter;
+    if (!seed_valid || !counter_valid) invalid = 1;
+    uint32_t elig = 0;
+    float fs[kItems];
+#pragma unroll
+    for (int i = 0; i < kItems; ++i) {
+      const int t = base + i;
+      fs[i] = -CUDART_INF_F;
+      if (t < kVocab && v[i] >= threshold && v[i] != -CUDART_INF_F) {
+        elig |= 1u << i;
+        fs[i] = scores[t];
+        if (fs[i] > best || (fs[i] == best && t < best_id)) {
+          best = fs[i];
+          best_id = t;
+        }
+      }
+    }
+    block_argmax(best, best_id, sh);
+    const float fast_best = sh.warp_best[0];
+    uint32_t near = 0;
+#pragma unroll
+    for (int i = 0; i < kItems; ++i) {
+      if ((elig >> i & 1u) && fs[i] >= fast_best - kVerifyMargin) near |= 1u << i;
+    }
+    const int threads_near = __syncthreads_count(near != 0);
+    const int several = __syncthreads_or(__popc(near) > 1);
+    if (threads_near != 1 || several) {  // rescore the near tokens exactly (sh is rewritten)
+      const uint32_t seed32 = call_seed32(c.seed);
+      const uint64_t off64 = call_offset(c.counter);
+      best = -CUDART_INF_F;
+      best_id = kVocab;
+#pragma unroll
+      for (int i = 0; i < kItems; ++i) {
+        if (near >> i & 1u) {
+          const int t = base + i;
+          const float g = clamped_gumbel(philox_uniform(seed32, off64 + static_cast<uint64_t>(t)));
+          const float sc = __fadd_rn(__fdiv_rn(v[i], prm.temperature), g);
+          if (sc > best || (sc == best && t < best_id)) {
+            best = sc;
+            best_id = t;
+          }
         }
       }
       block_argmax(best, best_id, sh);
