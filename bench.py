@@ -715,8 +715,8 @@ def main_decoder_measure(dev, peaks, n=256, steps=20, text=128, cap=467, seed=13
     torch.cuda.synchronize(dev)
     cuda_graph = None
     if graph:
-        # one step captured once (the cuBLASLt handle and plans exist after the
-        # warm-up) and replayed; the positions advance on the device
+        # one step captured once (the tensor maps and kernel attributes exist
+        # after the warm-up) and replayed; the positions advance on the device
         cuda_graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(cuda_graph, stream=stream):
             one_step()
@@ -746,9 +746,9 @@ def main_decoder_measure(dev, peaks, n=256, steps=20, text=128, cap=467, seed=13
     out = {"workload": f"config 5 per GPU: {n} sessions x CFG pair, cache {cap}, {text} text tokens, positions "
                        f"U[218, {cap - steps - 4}) advancing one per step, {steps} steps",
            "us_per_step": us, "decoder_steps_per_s": n * 1e6 / us, "status_nonzero": bad,
-           "kernels": "per layer: 6 cuBLASLt GEMMs + self_attn_kernel + cross_attn_kernel + 3 add_ln_kernel + "
-                      "gelu_kernel",
-           "gpu_launches_per_step": 1 + LAYERS * 12,
+           "kernels": "per layer: 6 tcgen05 GEMMs (gemm_tc_kernel; GELU in the FFN1 epilogue, FFN2 split-K 4) + "
+                      "self_attn_kernel + cross_attn_kernel + 3 add_ln_kernel",
+           "gpu_launches_per_step": 1 + LAYERS * 11,
            "cuda_graph_per_step": graph,
            "roofline": {"bound": "hbm", "algorithmic_bytes_per_step": bytes_, "achieved": gbs, "unit": "GB/s",
                         "peak": peaks["hbm_gbs"], "frac": gbs / peaks["hbm_gbs"],

@@ -125,6 +125,7 @@ struct __align__(1024) Smem {
   } u;
   bf16 stage[kM * kHeadCols];  // outgoing slice (bf16) or partial scores (f32)
   bf16 hbias[kHeadCols];       // this CTA's head bias slice of the position (fetched at its start)
+  alignas(16) bf16 lnw[2][kD];  // LN1 and LN2 weights
   SampleShared samp;
   int32_t tok[kM][kPositions];  // tokens of the tile's sessions (every CTA)
   int32_t sess[kM];             // stream ids of the tile's sessions
@@ -316,20 +317,42 @@ constexpr uint32_t kTokenBytes = kCS * 4;
 // ---------------------------------------------------------------------------
 
 // Chunk kinds: 0 in-projection, 1 qkv, 2 o, 3 FFN1, 4 FFN2 (K slice), 5 head.
-// With the folded in-projection the in-projection chunk exists only at p = 0.
-__device__ __forceinline__ int chunk_index(bool folded, int p, int k) {
-  return folded ? (k == 0 ? 0 : 1 + 5 * p + (k - 1)) : 6 * p + k;
+// They travel in groups that share a ring slot: per position [0] (at p = 0,
+// or at every position without the folded tables), {1, 2}, {3, 4}, {5}.
+// Group g lives in slot g & 1 and is issued as soon as group g - 2's last
+// GEMM is done, so each group has the two phases before its use to arrive
+// (the head, 64 KB, is in flight from the o-projection on).
+constexpr int kGroupO = 3 * kHD * kD;  // element offset of o in group {1, 2}: 24 KB
+constexpr int kGroupF2 = kFC * kD;     // element offset of FFN2 in group {3, 4}: 32 KB
+static_assert(kGroupO + kDC * kD <= kSlotElems && kGroupF2 + kD * kFC <= kSlotElems, "group fits a slot");
+static_assert((kGroupO * 2) % 1024 == 0 && (kGroupF2 * 2) % 1024 == 0, "swizzle-atom aligned chunks");
+
+__device__ __forceinline__ int group_count(bool folded) { return folded ? 4 + 3 * (kPositions - 1) : 4 * kPositions; }
+
+// Group index of (position p, group kind q: 0 in-projection, 1 {qkv, o},
+// 2 {FFN1, FFN2}, 3 head), and back.
+__device__ __forceinline__ int group_index(bool folded, int p, int q) {
+  if (!folded) return 4 * p + q;
+  return p == 0 ? q : 4 + 3 * (p - 1) + (q - 1);
+}
+__device__ __forceinline__ void group_of(bool folded, int g, int& p, int& q) {
+  if (!folded || g < 4) {
+    p = g / 4;
+    q = g % 4;
+  } else {
+    p = 1 + (g - 4) / 3;
+    q = 1 + (g - 4) % 3;
+  }
 }
 
 __device__ __forceinline__ int chunk_rows(int k) {
   return k == 1 ? 3 * kHD : (k == 3 ? kFC : (k == 4 ? kD : (k == 5 ? kHeadCols : kDC)));
 }
 
-// Weight chunk (p, k) for CTA c: one TMA tensor copy per 64-column panel,
-// issued by the lanes of the calling warp; completes on the slot's mbarrier.
-__device__ __forceinline__ void issue_chunk(const WeightMaps& maps, Smem& sm, bool folded, int p, int k, int c) {
-  const int slot = chunk_index(folded, p, k) & 1;
-  bf16* dst = sm.ring[slot];
+// Weight chunk (p, k) for CTA c into dst: one TMA tensor copy per 64-column
+// panel, issued by the lanes of the calling warp; completes on bar.
+__device__ __forceinline__ void issue_chunk(const WeightMaps& maps, bf16* dst, unsigned long long* bar, int p, int k,
+                                            int c) {
   const int lane = threadIdx.x & 31;
   const int rows = chunk_rows(k);
   const CUtensorMap* map;
@@ -344,36 +367,60 @@ __device__ __forceinline__ void issue_chunk(const WeightMaps& maps, Smem& sm, bo
   }
   const int panels = K / kPanel;
   const int requests = k == 1 ? 3 * panels : panels;
-  if (lane == 0) {
-    fence_proxy_async();
-    mbar_expect_tx(&sm.mbar[slot], static_cast<uint32_t>(rows * K * 2));
-  }
-  __syncwarp();
   if (lane < requests) {
     if (k == 1) {  // q, k, v rows of head h = c / 4, dims [16(c%4), +16): three 16-row boxes per panel
       const int part = lane / panels, pp = lane % panels;
       const int y = part * kD + (c / kG) * kHeadDim + (c % kG) * kHD;
-      tma_load_2d(dst + pp * (rows * kPanel) + part * (kHD * kPanel), map, pp * kPanel, y, &sm.mbar[slot]);
+      tma_load_2d(dst + pp * (rows * kPanel) + part * (kHD * kPanel), map, pp * kPanel, y, bar);
     } else {
-      tma_load_2d(dst + lane * (rows * kPanel), map, x0 + lane * kPanel, row0, &sm.mbar[slot]);
+      tma_load_2d(dst + lane * (rows * kPanel), map, x0 + lane * kPanel, row0, bar);
     }
   }
 }
 
-// Waits for weight chunk (p, k) and issues the next chunk of the stream into
-// the other slot (freed by the previous weight GEMM).  Returns the slot.
-__device__ __forceinline__ const bf16* next_weights(const WeightMaps& maps, Smem& sm, bool folded, int p, int k,
-                                                    int c) {
-  const int idx = chunk_index(folded, p, k);
-  int np = p, nk = k + 1;
-  if (nk == 6) {
-    np = p + 1;
-    nk = folded ? 1 : 0;
+// Issues weight group g (the calling warp, one lane announcing its bytes);
+// nothing past the frame's last group.
+__device__ __forceinline__ void issue_group(const WeightMaps& maps, Smem& sm, bool folded, int g, int c) {
+  if (g >= group_count(folded)) return;
+  int p, q;
+  group_of(folded, g, p, q);
+  bf16* slot = sm.ring[g & 1];
+  unsigned long long* bar = &sm.mbar[g & 1];
+  // (selected arithmetically: a table indexed at run time would be a memory load)
+  const uint32_t bytes = q == 0   ? uint32_t(kDC * kEmbed * 2)
+                         : q == 1 ? uint32_t((3 * kHD + kDC) * kD * 2)
+                         : q == 2 ? uint32_t(2 * kFC * kD * 2)
+                                  : uint32_t(kHeadCols * kD * 2);
+  if ((threadIdx.x & 31) == 0) {
+    fence_proxy_async();  // the slot's previous contents were read through the generic proxy
+    mbar_expect_tx(bar, bytes);
   }
-  if ((threadIdx.x >> 5) == 0 && np < kPositions) issue_chunk(maps, sm, folded, np, nk, c);
-  if (sm.err == 0 && !mbar_wait(&sm.mbar[idx & 1], (idx >> 1) & 1)) sm.err = 1;
+  __syncwarp();
+  switch (q) {
+    case 0: issue_chunk(maps, slot, bar, p, 0, c); break;
+    case 1:
+      issue_chunk(maps, slot, bar, p, 1, c);
+      issue_chunk(maps, slot + kGroupO, bar, p, 2, c);
+      break;
+    case 2:
+      issue_chunk(maps, slot, bar, p, 3, c);
+      issue_chunk(maps, slot + kGroupF2, bar, p, 4, c);
+      break;
+    default: issue_chunk(maps, slot, bar, p, 5, c); break;
+  }
+}
+
+// Waits for weight group g; returns its slot.
+__device__ __forceinline__ const bf16* wait_group(Smem& sm, int g) {
+  if (sm.err == 0 && !mbar_wait(&sm.mbar[g & 1], (g >> 1) & 1)) sm.err = 1;
   __syncthreads();
-  return sm.ring[idx & 1];
+  return sm.ring[g & 1];
+}
+
+// After group g's last GEMM (whose closing barrier every thread has passed):
+// its slot takes group g + 2.
+__device__ __forceinline__ void release_group(const WeightMaps& maps, Smem& sm, bool folded, int g, int c) {
+  if ((threadIdx.x >> 5) == 0) issue_group(maps, sm, folded, g + 2, c);
 }
 
 // Phase clock stamps (trace hook): CTA 0 of the first cluster writes its SM
@@ -446,8 +493,19 @@ __global__ void __cluster_dims__(kCS, 1, 1) __launch_bounds__(kThreads, 1)
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncthreads();
-  if (warp == 0) issue_chunk(maps, sm, folded, 0, 0, c);
+  if (warp == 0 && lane < 6) {  // the six tensor maps into the TMA descriptor cache
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(reinterpret_cast<const CUtensorMap*>(&maps) + lane))
+                 : "memory");
+  }
+  if (warp == 0) {
+    issue_group(maps, sm, folded, 0, c);
+    issue_group(maps, sm, folded, 1, c);
+  }
 
+  for (int i = threadIdx.x; i < kD / 8; i += blockDim.x) {
+    reinterpret_cast<uint4*>(sm.lnw[0])[i] = reinterpret_cast<const uint4*>(f.ln1)[i];
+    reinterpret_cast<uint4*>(sm.lnw[1])[i] = reinterpret_cast<const uint4*>(f.ln2)[i];
+  }
   // ---- session state (every CTA scores every session's tokens)
   if (static_cast<int>(threadIdx.x) < n_sess) {
     const int sid = sm.sess[threadIdx.x];
@@ -529,7 +587,8 @@ __global__ void __cluster_dims__(kCS, 1, 1) __launch_bounds__(kThreads, 1)
         }
         *reinterpret_cast<uint4*>(sm.big.src + r * kLd768 + ch * 8) = v;
       }
-      const bf16* w = next_weights(maps, sm, folded, p, 0, c);
+      const int g = group_index(folded, p, 0);
+      const bf16* w = wait_group(sm, g);
       gemm16<2, 48>(sm.big.src, kLd768, w, kDC, &sm.u.red[0][0], [&](int r, int j, float v0, float v1) {
         const int n = kDC * c + j;
         const float y0 = round_bf16(__fadd_rn(v0, bf2f(f.in_b[n])));
@@ -538,15 +597,18 @@ __global__ void __cluster_dims__(kCS, 1, 1) __launch_bounds__(kThreads, 1)
         *reinterpret_cast<uint32_t*>(sm.stage + r * kDC + j) =
             pack_bf16x2(__fadd_rn(y0, bf2f(pos[0])), __fadd_rn(y1, bf2f(pos[1])));
       });
+      release_group(maps, sm, folded, g, c);
       push_all16(sm, rd, rows, kDC, sm.x, kLd256, kDC * c);
       finish_round(sm, rd, kCS * slice_bytes);
     }
     stamp(f, p, 1);
 
     // ---------------- Ph1: LN1, qkv slice, partial scores to the head group
-    layer_norm16(sm.x, sm.xa, f.ln1);
+    layer_norm16(sm.x, sm.xa, sm.lnw[0]);
+    const int g1 = group_index(folded, p, 1), g2 = g1 + 1, g3 = g1 + 2;
+    const bf16* wg1 = wait_group(sm, g1);
     {
-      const bf16* w = next_weights(maps, sm, folded, p, 1, c);
+      const bf16* w = wg1;
       gemm16<6, 16>(sm.xa, kLd256, w, 3 * kHD, &sm.u.red[0][0], [&](int r, int j, float v0, float v1) {
         const int part = j / kHD, i = j % kHD;  // j even: the pair stays inside one part
         const uint32_t y = pack_bf16x2(v0, v1);
@@ -615,7 +677,7 @@ __global__ void __cluster_dims__(kCS, 1, 1) __launch_bounds__(kThreads, 1)
 
     // ---------------- Ph3: o-projection + residual, all-gathered
     {
-      const bf16* w = next_weights(maps, sm, folded, p, 2, c);
+      const bf16* w = wg1 + kGroupO;
       gemm16<2, 16>(sm.xa, kLd256, w, kDC, &sm.u.red[0][0], [&](int r, int j, float v0, float v1) {
         const int n = kDC * c + j;
         const float x0 = bf2f(sm.x[r * kLd256 + n]), x1 = bf2f(sm.x[r * kLd256 + n + 1]);
@@ -623,15 +685,17 @@ __global__ void __cluster_dims__(kCS, 1, 1) __launch_bounds__(kThreads, 1)
             pack_bf16x2(__fadd_rn(x0, round_bf16(v0)), __fadd_rn(x1, round_bf16(v1)));
       });
     }
+    release_group(maps, sm, folded, g1, c);
     stamp(f, p, 6);
     push_all16(sm, rd, rows, kDC, sm.x, kLd256, kDC * c);
     finish_round(sm, rd, kCS * slice_bytes);
     stamp(f, p, 7);
 
     // ---------------- Ph4: LN2, FFN1 slice + GELU, FFN2 partials to the owners
-    layer_norm16(sm.x, sm.xa, f.ln2);
+    layer_norm16(sm.x, sm.xa, sm.lnw[1]);
+    const bf16* wg2 = wait_group(sm, g2);
     {
-      const bf16* w = next_weights(maps, sm, folded, p, 3, c);
+      const bf16* w = wg2;
       gemm16<8, 16>(sm.xa, kLd256, w, kFC, &sm.u.red[0][0], [&](int r, int j, float v0, float v1) {
         *reinterpret_cast<uint32_t*>(sm.hc + r * kLdH + j) =
             pack_bf16x2(gelu_tanh_f(round_bf16(v0)), gelu_tanh_f(round_bf16(v1)));
@@ -639,7 +703,7 @@ __global__ void __cluster_dims__(kCS, 1, 1) __launch_bounds__(kThreads, 1)
     }
     stamp(f, p, 8);
     {
-      const bf16* w = next_weights(maps, sm, folded, p, 4, c);
+      const bf16* w = wg2 + kGroupF2;
       gemm16<32, 4>(sm.hc, kLdH, w, kD, &sm.u.red[0][0], [&](int r, int j, float v0, float v1) {
         const int dst = j / kDC;
         if (r < rows) {
@@ -647,6 +711,7 @@ __global__ void __cluster_dims__(kCS, 1, 1) __launch_bounds__(kThreads, 1)
         }
       });
     }
+    release_group(maps, sm, folded, g2, c);
     stamp(f, p, 9);
     finish_round(sm, rd, kCS * uint32_t(rows * kDC * 4));
     stamp(f, p, 10);
@@ -666,9 +731,9 @@ __global__ void __cluster_dims__(kCS, 1, 1) __launch_bounds__(kThreads, 1)
     stamp(f, p, 11);
 
     // ---------------- Ph6: head p; logits rows to the owners
-    if (bias_async) cp_async_wait_all();  // published by next_weights' barrier
+    if (bias_async) cp_async_wait_all();  // published by wait_group's barrier
     {
-      const bf16* w = next_weights(maps, sm, folded, p, 5, c);
+      const bf16* w = wait_group(sm, g3);
       gemm16<16, 16>(sm.x, kLd256, w, kHeadCols, &sm.u.red[0][0], [&](int r, int j, float v0, float v1) {
         if (j < hcols) {  // hcols is even: pairs never straddle it
           const int n = kHeadCols * c + j;
@@ -686,6 +751,7 @@ __global__ void __cluster_dims__(kCS, 1, 1) __launch_bounds__(kThreads, 1)
         }
       });
     }
+    release_group(maps, sm, folded, g3, c);
     stamp(f, p, 12);
     {
       // every live session's row (pair) in candidate form: the constrained

@@ -256,7 +256,7 @@ def test_decoder_loop_graph_replay_matches_eager():
     tokens, end-frame indices."""
     eager_step, e_db, e_gate, e_fb = _loop_state(200)
     graph_step, g_db, g_gate, g_fb = _loop_state(200)
-    eager_step()  # also the library's one-time set-up (cuBLASLt handle and plans)
+    eager_step()  # also the library's one-time set-up (tensor maps, kernel attributes)
     graph_step()
     torch.cuda.synchronize()
     stream = torch.cuda.Stream()
