@@ -586,7 +586,10 @@ def r_shape_measure(dev, peaks, sizes=(64, 1024), calls=10, seed=5):
         tf = flops / (t * 1e-6) / 1e12
         res.update({"frame_call_us_eager": t_eager, "frame_call_us_graph": t_graph,
                     "frames_per_s": n / (t * 1e-6), "tflops": tf, "tensor_frac": tf / tensor_peak,
-                    "algorithmic_flops_per_call": flops, "invalid_rows": inv})
+                    "algorithmic_flops_per_call": flops, "invalid_rows": inv,
+                    "roofline": {"bound": "tensor", "kernel": "phase kernels (one frame call, CUDA graph)",
+                                 "achieved": tf, "peak": tensor_peak, "unit": "TFLOP/s", "frac": tf / tensor_peak,
+                                 "peak_kind": "measured sustained bf16", "traffic": None}})
         out[str(n)] = res
     return out
 

@@ -126,6 +126,7 @@ struct __align__(1024) Smem {
   bf16 stage[kM * kHeadCols];  // outgoing slice (bf16) or partial scores (f32)
   bf16 hbias[kHeadCols];       // this CTA's head bias slice of the position (fetched at its start)
   alignas(16) bf16 lnw[2][kD];  // LN1 and LN2 weights
+  float gum[kM][kHeadCols];      // fast Gumbel noise of this CTA's columns, per live session, this position
   SampleShared samp;
   int32_t tok[kM][kPositions];  // tokens of the tile's sessions (every CTA)
   int32_t sess[kM];             // stream ids of the tile's sessions
@@ -640,6 +641,16 @@ __global__ void __cluster_dims__(kCS, 1, 1) __launch_bounds__(kThreads, 1)
     }
     stamp(f, p, 2);
     push_tokens(sm, rd, c);
+    // the position's Gumbel noise depends only on (seed, counter, token):
+    // drawn here, while the scores round is in flight, and added to the
+    // values once the head's logits exist
+    if (!f.prm.argmax) {
+      for (int i = threadIdx.x; i < n_sess * hcols; i += blockDim.x) {
+        const int sl = i / hcols, j = i % hcols;
+        sm.gum[sl][j] = fast_gumbel(philox_uniform(
+            call_seed32(sm.seed[sl]), call_offset(sm.ctrs[sl]) + static_cast<uint64_t>(kHeadCols * c + j)));
+      }
+    }
     finish_round(sm, rd, kG * uint32_t(rows * kPositions * 4) + kTokenBytes);
     stamp(f, p, 3);
 
@@ -755,7 +766,8 @@ __global__ void __cluster_dims__(kCS, 1, 1) __launch_bounds__(kThreads, 1)
     stamp(f, p, 12);
     {
       // every live session's row (pair) in candidate form: the constrained
-      // value's order key and its fast Philox-Gumbel score, for this CTA's columns
+      // value's order key and its fast Philox-Gumbel score, for this CTA's
+      // columns (the argmax mode sends no scores: -inf)
       const float cfg = f.prm.cfg_scale, temp = f.prm.temperature;
       for (int i = threadIdx.x; i < n_sess * hcols; i += blockDim.x) {
         const int sl = i / hcols, j = i % hcols, t = kHeadCols * c + j;
@@ -766,8 +778,9 @@ __global__ void __cluster_dims__(kCS, 1, 1) __launch_bounds__(kThreads, 1)
         const float v = constrain_token(t, raw, fl & 1u, fl & 2u, fl & 4u, &nf);
         if (nf) atomicOr(&sm.cnf[sl], 1u);
         sm.big.cand_out.key[sl][j] = static_cast<uint16_t>(value_key16(v));
+        // token_score_fast with the noise drawn in Ph1
         sm.big.cand_out.score[sl][j] =
-            f.prm.argmax ? 0.f : token_score_fast(v, t, temp, call_seed32(sm.seed[sl]), call_offset(sm.ctrs[sl]));
+            f.prm.argmax || v == -CUDART_INF_F ? -CUDART_INF_F : __fadd_rn(__fdiv_rn(v, temp), sm.gum[sl][j]);
       }
       __syncthreads();
       const int kch = hcols / 8, sch = hcols / 4, per = kch + sch;  // 16-byte chunks per session
