@@ -591,59 +591,86 @@ __global__ void __launch_bounds__(256) add_pos_kernel(Frame f, int p) {
 // attention: one warp per (row, head), p + 1 keys
 // ---------------------------------------------------------------------------
 
+// Causal self-attention of position p for one (row, head) per warp: lane
+// 8 g + c holds head dims [8c, +8) of the window's positions g, g + 4, g + 8,
+// g + 12, so each lane issues at most four 16-byte key and four value loads,
+// all before the first use.  A score is summed over the 8 lanes of its group,
+// rounded as the reference rounds it (bf16, x 1/8, bf16) and gathered into
+// every lane, which runs the softmax over the positions in order; each lane
+// weights its own value rows and the four groups' sums are combined.
 __global__ void __launch_bounds__(256) attention_kernel(Frame f, int p, int l) {
   const int rows = *f.count * f.rp;
   const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (gw >= rows * f.H) return;
   const int r = gw / f.H, hd = gw % f.H;
+  const int g = lane >> 3, cc = lane & 7;
   const int64_t R = static_cast<int64_t>(f.n) * f.rp;
-  const float2 qv = __bfloat1622float2(
-      *reinterpret_cast<const __nv_bfloat162*>(f.q + static_cast<int64_t>(r) * f.d + hd * kHeadDim + 2 * lane));
-  const bf16* kbase = f.kc + ((static_cast<int64_t>(l) * R + r) * kPositions) * f.d + hd * kHeadDim + 2 * lane;
-  const bf16* vbase = f.vc + ((static_cast<int64_t>(l) * R + r) * kPositions) * f.d + hd * kHeadDim + 2 * lane;
-  // every key and value row of the window in flight at once
-  __nv_bfloat162 kr[kPositions], vr[kPositions];
+  float q[8];
+  unpack8(*reinterpret_cast<const uint4*>(f.q + static_cast<int64_t>(r) * f.d + hd * kHeadDim + 8 * cc), q);
+  const int64_t base = ((static_cast<int64_t>(l) * R + r) * kPositions) * f.d + hd * kHeadDim + 8 * cc;
+  uint4 kr[4], vr[4];
 #pragma unroll
-  for (int j = 0; j < kPositions; ++j) {
+  for (int i = 0; i < 4; ++i) {
+    const int j = g + 4 * i;
     if (j <= p) {
-      kr[j] = *reinterpret_cast<const __nv_bfloat162*>(kbase + j * f.d);
-      vr[j] = *reinterpret_cast<const __nv_bfloat162*>(vbase + j * f.d);
+      kr[i] = *reinterpret_cast<const uint4*>(f.kc + base + static_cast<int64_t>(j) * f.d);
+      vr[i] = *reinterpret_cast<const uint4*>(f.vc + base + static_cast<int64_t>(j) * f.d);
     }
   }
-  float s[kPositions];
+  float sc[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float dot = 0.f;
+    if (g + 4 * i <= p) {
+      float k[8];
+      unpack8(kr[i], k);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) dot = fmaf(q[e], k[e], dot);
+    }
+    dot += __shfl_xor_sync(0xffffffffu, dot, 1);
+    dot += __shfl_xor_sync(0xffffffffu, dot, 2);
+    dot += __shfl_xor_sync(0xffffffffu, dot, 4);
+    sc[i] = round_bf16(__fmul_rn(round_bf16(dot), 0.125f));
+  }
+  // position j's score lives in group j mod 4, slot j / 4
   float mx = -CUDART_INF_F;
+  float s[kPositions];
 #pragma unroll
   for (int j = 0; j < kPositions; ++j) {
-    if (j <= p) {
-      const float2 kv = __bfloat1622float2(kr[j]);
-      float dot = qv.x * kv.x + qv.y * kv.y;
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
-      s[j] = round_bf16(__fmul_rn(round_bf16(dot), 0.125f));
-      mx = fmaxf(mx, s[j]);
-    }
+    s[j] = __shfl_sync(0xffffffffu, sc[j >> 2], 8 * (j & 3));
+    if (j <= p) mx = fmaxf(mx, s[j]);
   }
   float sum = 0.f;
 #pragma unroll
   for (int j = 0; j < kPositions; ++j) {
-    if (j <= p) {
-      s[j] = expf(s[j] - mx);
-      sum += s[j];
-    }
+    if (j <= p) sum += expf(s[j] - mx);
   }
-  float o0 = 0.f, o1 = 0.f;
+  float o[8];
 #pragma unroll
-  for (int j = 0; j < kPositions; ++j) {
-    if (j <= p) {
-      const float prob = round_bf16(s[j] / sum);
-      const float2 vv = __bfloat1622float2(vr[j]);
-      o0 = fmaf(prob, vv.x, o0);
-      o1 = fmaf(prob, vv.y, o1);
+  for (int e = 0; e < 8; ++e) o[e] = 0.f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    if (g + 4 * i <= p) {
+      const float prob = round_bf16(expf(sc[i] - mx) / sum);
+      float v[8];
+      unpack8(vr[i], v);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) o[e] = fmaf(prob, v[e], o[e]);
     }
   }
-  *reinterpret_cast<__nv_bfloat162*>(f.att + static_cast<int64_t>(r) * f.d + hd * kHeadDim + 2 * lane) =
-      __floats2bfloat162_rn(o0, o1);
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    o[e] += __shfl_xor_sync(0xffffffffu, o[e], 8);
+    o[e] += __shfl_xor_sync(0xffffffffu, o[e], 16);
+  }
+  if (g == 0) {
+    __align__(16) bf16 o8[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) o8[e] = f2bf(o[e]);
+    *reinterpret_cast<uint4*>(f.att + static_cast<int64_t>(r) * f.d + hd * kHeadDim + 8 * cc) =
+        *reinterpret_cast<const uint4*>(o8);
+  }
 }
 
 // ---------------------------------------------------------------------------
