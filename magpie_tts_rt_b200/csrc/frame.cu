@@ -398,109 +398,139 @@ __global__ void __launch_bounds__(256) resid_sum_kernel(Frame f, int splits, con
   if constexpr (LN) ln_row_regs(v, f.d, lnw, f.att + static_cast<int64_t>(r) * f.d);
 }
 
+// Epilogues of the tensor-core linear layers.  A lane holds 32 consecutive
+// output features of one row; the warp stages its 32 rows in shared memory
+// (row stride 80 bytes: conflict-free 16-byte access) and writes them back
+// four lanes per row, so a store instruction covers eight whole 64-byte row
+// segments instead of 32 scattered 16-byte pieces.
+constexpr int kPhaseStageRow = 40;  // bf16 per staged row (64 bytes + 16 of padding)
+
 template <int EPI>
 struct EpiPhase {
   Frame f;
   int p, l, N;
   const bf16* bias;
 
-  __device__ __forceinline__ void chunk(int r, int n0, int /*ks*/, const uint32_t (&v)[32], int /*n_cols*/) const {
-    if (r >= *f.count * f.rp) return;  // rows past the active ones are padding
-    float y[32];
-#pragma unroll
-    for (int j = 0; j < 32; ++j) y[j] = __uint_as_float(v[j]);
-    if constexpr (EPI == kEpiHead) {
-      const int i = r / f.rp, sub = r % f.rp;
-      bf16* out = f.logits_out != nullptr
-                      ? f.logits_out + ((static_cast<int64_t>(f.list[i]) * kPositions + p) * f.rp + sub) * kVocab
-                      : nullptr;
-      bf16* lg = f.logits + static_cast<int64_t>(r) * kVocab;
-      if (n0 + 32 <= N) {  // rows of 2024 bf16 keep every 32-column chunk 16-byte aligned
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const uint4 b = reinterpret_cast<const uint4*>(bias + n0)[q];
-          float t[8];
-          unpack8(b, t);
-          uint32_t w[4];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const __nv_bfloat162 h = __floats2bfloat162_rn(__fadd_rn(y[8 * q + 2 * e], t[2 * e]),
-                                                           __fadd_rn(y[8 * q + 2 * e + 1], t[2 * e + 1]));
-            w[e] = *reinterpret_cast<const uint32_t*>(&h);
-          }
-          const uint4 o = make_uint4(w[0], w[1], w[2], w[3]);
-          reinterpret_cast<uint4*>(lg + n0)[q] = o;
-          if (out != nullptr) reinterpret_cast<uint4*>(out + n0)[q] = o;
-        }
-      } else {
-#pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          const int n = n0 + j;
-          if (n < N) {
-            const bf16 o = f2bf(__fadd_rn(y[j], bf2f(bias[n])));
-            lg[n] = o;
-            if (out != nullptr) out[n] = o;
-          }
-        }
-      }
-      return;
+  // destination of 8 features [n, n + 8) of row r (q, the K/V cache, FFN hidden)
+  __device__ __forceinline__ bf16* dst(int r, int n) const {
+    if constexpr (EPI == kEpiQkv) {
+      if (n < f.d) return f.q + static_cast<int64_t>(r) * f.d + n;
+      const int which = n < 2 * f.d ? 0 : 1;
+      const int col = n - (which + 1) * f.d;
+      const int64_t R = static_cast<int64_t>(f.n) * f.rp;
+      return (which == 0 ? f.kc : f.vc) + ((static_cast<int64_t>(l) * R + r) * kPositions + p) * f.d + col;
+    } else if constexpr (EPI == kEpiGelu) {
+      return f.h + static_cast<int64_t>(r) * f.F + n;
     } else {
-      if (n0 >= N) return;
-      bf16* dst;
-      if constexpr (EPI == kEpiQkv) {
-        if (n0 < f.d) {
-          dst = f.q + static_cast<int64_t>(r) * f.d + n0;
-        } else {
-          const int which = n0 < 2 * f.d ? 0 : 1;
-          const int col = n0 - (which + 1) * f.d;
-          const int64_t R = static_cast<int64_t>(f.n) * f.rp;
-          dst = (which == 0 ? f.kc : f.vc) + ((static_cast<int64_t>(l) * R + r) * kPositions + p) * f.d + col;
-        }
-      } else if constexpr (EPI == kEpiResid) {
-        dst = f.x + static_cast<int64_t>(r) * f.d + n0;
-        float x[32];
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          float t[8];
-          unpack8(reinterpret_cast<const uint4*>(dst)[q], t);
-#pragma unroll
-          for (int e = 0; e < 8; ++e) x[8 * q + e] = t[e];
-        }
-#pragma unroll
-        for (int j = 0; j < 32; ++j) y[j] = __fadd_rn(x[j], round_bf16(y[j]));
-      } else {  // kEpiGelu
-        dst = f.h + static_cast<int64_t>(r) * f.F + n0;
-#pragma unroll
-        for (int j = 0; j < 32; ++j) y[j] = gelu_tanh(round_bf16(y[j]));
-      }
+      return f.x + static_cast<int64_t>(r) * f.d + n;
+    }
+  }
+
+  __device__ __forceinline__ void chunk(int m, int n0, int /*ks*/, const uint32_t (&v)[32], int /*n_cols*/) const {
+    __shared__ __align__(16) bf16 stage[kGemmEpiWarps][32][kPhaseStageRow];
+    const int lane = threadIdx.x & 31, w = gemm_epi_warp();
+    float bvals[32];
+    if constexpr (EPI == kEpiHead) {
+      // the chunk's bias (the same 64 bytes for every lane: a broadcast load)
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
-        uint32_t w[4];
+        float t[8];
+        if (n0 + 8 * q < N) {
+          unpack8(reinterpret_cast<const uint4*>(bias + n0)[q], t);
+        } else {
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const __nv_bfloat162 h = __floats2bfloat162_rn(y[8 * q + 2 * e], y[8 * q + 2 * e + 1]);
-          w[e] = *reinterpret_cast<const uint32_t*>(&h);
+          for (int e = 0; e < 8; ++e) t[e] = 0.f;
         }
-        reinterpret_cast<uint4*>(dst)[q] = make_uint4(w[0], w[1], w[2], w[3]);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) bvals[8 * q + e] = t[e];
       }
     }
+    uint32_t packed[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      float a = __uint_as_float(v[2 * j]), b = __uint_as_float(v[2 * j + 1]);
+      if constexpr (EPI == kEpiHead) {
+        a = __fadd_rn(a, bvals[2 * j]);
+        b = __fadd_rn(b, bvals[2 * j + 1]);
+      } else if constexpr (EPI == kEpiGelu) {
+        a = gelu_tanh(round_bf16(a));
+        b = gelu_tanh(round_bf16(b));
+      }
+      // q|k|v: bf16(v); residual: bf16(v) here, added to x below
+      const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+      packed[j] = *reinterpret_cast<const uint32_t*>(&h);
+    }
+    uint4* mine = reinterpret_cast<uint4*>(stage[w][lane]);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) mine[q] = make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
+    __syncwarp();
+    const int m0 = m - lane;  // the warp's first row
+    const int rows = *f.count * f.rp;  // rows past the active ones are padding
+#pragma unroll
+    for (int it = 0; it < 4; ++it) {
+      const int rl = 8 * it + (lane >> 2), q = lane & 3;
+      const int r = m0 + rl, n = n0 + 8 * q;
+      if (r < rows && n < N) {
+        const uint4 y = reinterpret_cast<const uint4*>(stage[w][rl])[q];
+        if constexpr (EPI == kEpiHead) {
+          *reinterpret_cast<uint4*>(f.logits + static_cast<int64_t>(r) * kVocab + n) = y;
+          if (f.logits_out != nullptr) {
+            const int i = r / f.rp, sub = r % f.rp;
+            bf16* out = f.logits_out + ((static_cast<int64_t>(f.list[i]) * kPositions + p) * f.rp + sub) * kVocab + n;
+            *reinterpret_cast<uint4*>(out) = y;
+          }
+        } else if constexpr (EPI == kEpiResid) {
+          bf16* xp = dst(r, n);
+          float x8[8], y8[8];
+          unpack8(*reinterpret_cast<const uint4*>(xp), x8);
+          unpack8(y, y8);
+          __align__(16) bf16 o8[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) o8[e] = f2bf(__fadd_rn(x8[e], y8[e]));
+          *reinterpret_cast<uint4*>(xp) = *reinterpret_cast<const uint4*>(o8);
+        } else {
+          *reinterpret_cast<uint4*>(dst(r, n)) = y;
+        }
+      }
+    }
+    __syncwarp();
   }
 };
 
 // Split-K partial sums of a residual GEMM: part[ks][r][n] (f32), summed by
-// resid_sum_kernel.
+// resid_sum_kernel; staged like EpiPhase, 16 columns (64 bytes per row) at a
+// time.
+constexpr int kPhaseStageRowF = 20;  // f32 per staged row (64 bytes + 16 of padding)
 struct EpiPhasePart {
   float* part;
   int rows_max, N;
   const int* count;
   int rp;
-  __device__ __forceinline__ void chunk(int r, int n0, int ks, const uint32_t (&v)[32], int /*n_cols*/) const {
-    if (r >= *count * rp || n0 >= N) return;
-    float4* dst = reinterpret_cast<float4*>(part + (static_cast<int64_t>(ks) * rows_max + r) * N + n0);
+  __device__ __forceinline__ void chunk(int m, int n0, int ks, const uint32_t (&v)[32], int /*n_cols*/) const {
+    __shared__ __align__(16) float stage[kGemmEpiWarps][32][kPhaseStageRowF];
+    const int lane = threadIdx.x & 31, w = gemm_epi_warp();
+    const int m0 = m - lane;
+    const int rows = *count * rp;
+    float* base = part + static_cast<int64_t>(ks) * rows_max * N;
 #pragma unroll
-    for (int q = 0; q < 8; ++q) {
-      dst[q] = make_float4(__uint_as_float(v[4 * q]), __uint_as_float(v[4 * q + 1]), __uint_as_float(v[4 * q + 2]),
-                           __uint_as_float(v[4 * q + 3]));
+    for (int h = 0; h < 2; ++h) {
+      float4* mine = reinterpret_cast<float4*>(stage[w][lane]);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        mine[q] = make_float4(__uint_as_float(v[16 * h + 4 * q]), __uint_as_float(v[16 * h + 4 * q + 1]),
+                              __uint_as_float(v[16 * h + 4 * q + 2]), __uint_as_float(v[16 * h + 4 * q + 3]));
+      }
+      __syncwarp();
+#pragma unroll
+      for (int it = 0; it < 4; ++it) {
+        const int rl = 8 * it + (lane >> 2), q = lane & 3;
+        const int r = m0 + rl, n = n0 + 16 * h + 4 * q;
+        if (r < rows && n < N) {
+          *reinterpret_cast<float4*>(base + static_cast<int64_t>(r) * N + n) =
+              reinterpret_cast<const float4*>(stage[w][rl])[q];
+        }
+      }
+      __syncwarp();
     }
   }
 };
@@ -1078,7 +1108,7 @@ extern "C" MTT_B200_API int mtt_b200_launch_local_ar_frame(const mtt_b200_local_
     }
     const bf16* hw = f.head_w + static_cast<int64_t>(p) * kVocab * d;
     const bf16* hb = f.head_b + static_cast<int64_t>(p) * kVocab;
-    if (tc) {
+    if (tc && (reinterpret_cast<uintptr_t>(f.head_b) & 15u) == 0) {  // its epilogue reads the bias as 16-byte vectors
       if (launch_linear_tc<kProX, kEpiHead>(f, st, p, 0, kVocab, d, hw, hb) != cudaSuccess) {
         return MTT_B200_STATUS_CUDA_ERROR;
       }
