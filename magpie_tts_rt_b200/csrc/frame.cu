@@ -368,25 +368,49 @@ __global__ void __launch_bounds__(256) resid_sum_kernel(Frame f, int splits, con
   const int lane = threadIdx.x & 31;
   const int64_t rows_max = static_cast<int64_t>(f.n) * f.rp;
   bf16* xr = f.x + static_cast<int64_t>(r) * f.d;
+  // each split's slice of the row is loaded whole before it is added, two
+  // splits at a time (the sums still run split by split, in order)
+  uint4 xv[kRowChunks];
+  float acc[8 * kRowChunks];
+#pragma unroll
+  for (int c = 0; c < kRowChunks; ++c) {
+    const int k = lane * 8 + 256 * c;
+    if (k < f.d) xv[c] = *reinterpret_cast<const uint4*>(xr + k);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[8 * c + j] = 0.f;
+  }
+#pragma unroll 2
+  for (int sp = 0; sp < splits; ++sp) {
+    float4 pv[2 * kRowChunks];
+#pragma unroll
+    for (int c = 0; c < kRowChunks; ++c) {
+      const int k = lane * 8 + 256 * c;
+      if (k < f.d) {
+        const float4* pp = reinterpret_cast<const float4*>(f.part + (sp * rows_max + r) * f.d + k);
+        pv[2 * c] = pp[0];
+        pv[2 * c + 1] = pp[1];
+      }
+    }
+#pragma unroll
+    for (int c = 0; c < kRowChunks; ++c) {
+      if (lane * 8 + 256 * c < f.d) {
+        float* a = acc + 8 * c;
+        a[0] += pv[2 * c].x; a[1] += pv[2 * c].y; a[2] += pv[2 * c].z; a[3] += pv[2 * c].w;
+        a[4] += pv[2 * c + 1].x; a[5] += pv[2 * c + 1].y; a[6] += pv[2 * c + 1].z; a[7] += pv[2 * c + 1].w;
+      }
+    }
+  }
   float v[8 * kRowChunks];
 #pragma unroll
   for (int c = 0; c < kRowChunks; ++c) {
     const int k = lane * 8 + 256 * c;
     if (k < f.d) {
-      float a[8], acc[8];
-      unpack8(*reinterpret_cast<const uint4*>(xr + k), a);
-#pragma unroll
-      for (int j = 0; j < 8; ++j) acc[j] = 0.f;
-      for (int sp = 0; sp < splits; ++sp) {
-        const float4* pp = reinterpret_cast<const float4*>(f.part + (sp * rows_max + r) * f.d + k);
-        const float4 p0 = pp[0], p1 = pp[1];
-        acc[0] += p0.x; acc[1] += p0.y; acc[2] += p0.z; acc[3] += p0.w;
-        acc[4] += p1.x; acc[5] += p1.y; acc[6] += p1.z; acc[7] += p1.w;
-      }
+      float a[8];
+      unpack8(xv[c], a);
       __align__(16) bf16 o8[8];
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
-        o8[j] = f2bf(__fadd_rn(a[j], round_bf16(acc[j])));
+        o8[j] = f2bf(__fadd_rn(a[j], round_bf16(acc[8 * c + j])));
         v[8 * c + j] = bf2f(o8[j]);
       }
       *reinterpret_cast<uint4*>(xr + k) = *reinterpret_cast<const uint4*>(o8);
