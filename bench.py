@@ -57,7 +57,7 @@ from magpie_tts_rt_b200.model import EMBED, SHAPE_BASELINE, SHAPE_SOFIA, make_we
 METRIC = "Local-AR+sampling frames/sec per GPU and box (1/2/4/8); p50 per-frame us"
 PATH_NAMES = {1: "phase kernels", 2: "fused cluster kernel", 3: "tile kernel", 4: "pair kernel",
               5: "split kernel x1", 6: "split kernel x2", 7: "split kernel x4", 8: "split kernel x8",
-              9: "split kernel x2, 32-row tiles"}
+              9: "split kernel x2, 32-row tiles", 10: "quad kernel"}
 # DRAM bytes per launch of the frame kernel, measured by ncu (path, sessions per GPU)
 TRAFFIC = {("tile kernel", 1024): 27.64e6, ("pair kernel", 1024): 27.70e6, ("split kernel x4", 256): 23.13e6,
            ("split kernel x8", 64): 20.58e6, ("fused cluster kernel", 1): 18.76e6}
@@ -79,6 +79,7 @@ def parse():
     ap.add_argument("--sessions", type=int, default=None,
                     help="override sessions per GPU (profiling a smaller per-GPU batch, e.g. 256 = config 4 at 4 GPUs)")
     ap.add_argument("--no-latency", action="store_true")
+    ap.add_argument("--path", type=int, default=0, help="frame path for the config-4 workload (0: AUTO)")
     ap.add_argument("--main-decoder-only", action="store_true",
                     help="run only the Main Decoder step measurement and print its object (profiling)")
     ap.add_argument("--md-sessions", type=int, default=256, help="Main Decoder sessions per GPU (config 5: 256)")
@@ -259,7 +260,7 @@ def run_ours(args, world, rank, local):
     n, first, total = rank_streams(cfg, world, rank)
     dev = torch.device("cuda", local)
     w = make_weights(SHAPE_BASELINE, seed=0, dtype=torch.bfloat16, profile="baseline")
-    eng = LocalArEngine(w, max_streams=n, device=dev)
+    eng = LocalArEngine(w, max_streams=n, device=dev, path=args.path)
     eos = eos_schedule(cfg, total, cfg["frames"])[first:first + n]
     act, unf, fin, forb = flag_tables(eos, frames)
     frames_per_step_local = int(act.sum())
@@ -475,7 +476,7 @@ def tensor_probe(dev):
     out = {"umma_cycles_per_instruction": {}, "umma_mac_per_cycle_per_sm": {}}
     cyc = torch.zeros(1024, dtype=torch.int64, device=dev)
     n_mma = 2048
-    for n in (16, 32, 64, 128, 256):
+    for n in (16, 32, 48, 64, 96, 128, 256):
         if L.lib.mtt_b200_test_umma_cycles(n, 1, n_mma, sms, ctypes.c_void_p(cyc.data_ptr()), st) != 0:
             return None
         torch.cuda.synchronize(dev)

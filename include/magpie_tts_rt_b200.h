@@ -316,6 +316,10 @@ MTT_B200_API int mtt_b200_launch_fold_in_projection(const mtt_b200_local_ar_shap
 #define MTT_B200_FRAME_PATH_SPLIT_4 7
 #define MTT_B200_FRAME_PATH_SPLIT_8 8
 #define MTT_B200_FRAME_PATH_SPLIT_2X32 9
+/* QUAD: 16 sessions (32 rows) on a 4-CTA cluster, one attention head per CTA
+ * (its key/value cache in tensor memory), each CTA streaming a quarter of
+ * FFN and head weights, tcgen05 GEMMs on 32-row tiles (benchmark shape). */
+#define MTT_B200_FRAME_PATH_QUAD 10
 
 /* Sampling configuration; the reference's values are 80 / 0.6 / 2.5 with CFG
  * and top-k.  argmax != 0 selects greedy decoding (no RNG, counter unchanged;
@@ -420,14 +424,14 @@ MTT_B200_API int mtt_b200_launch_local_ar_frame_static_workspace(const mtt_b200_
                                                                 void* stream);
 
 /* The path (MTT_B200_FRAME_PATH_PHASE_KERNELS, _FUSED_CLUSTER, _FUSED_TILE,
- * _FUSED_PAIR or _SPLIT_1 / _2 / _4 / _8) that mtt_b200_launch_local_ar_frame takes for this shape,
+ * _FUSED_PAIR, _SPLIT_1 / _2 / _4 / _8 or _QUAD) that mtt_b200_launch_local_ar_frame takes for this shape,
  * configuration and batch size on the current device, or
  * MTT_B200_STATUS_UNSUPPORTED. */
 MTT_B200_API int32_t mtt_b200_local_ar_frame_path(const mtt_b200_local_ar_shape_t* shape,
                                                   const mtt_b200_sampling_config_t* sampling, int32_t n_streams);
 
 /* Thread-block clusters of a fused frame path (MTT_B200_FRAME_PATH_FUSED_CLUSTER,
- * _FUSED_TILE (1-CTA clusters), _FUSED_PAIR, _SPLIT_1 / _2 / _4 / _8) that
+ * _FUSED_TILE (1-CTA clusters), _FUSED_PAIR, _SPLIT_1 / _2 / _4 / _8, _QUAD) that
  * the current device runs at once, each holding one tile of the batch; 0 when
  * the path cannot run here.  AUTO compares the batch's tiles with these. */
 MTT_B200_API int32_t mtt_b200_local_ar_frame_path_clusters(int32_t path);
@@ -715,9 +719,10 @@ MTT_B200_API int mtt_b200_launch_test_log(const float* x, float* out, size_t cou
  * Returns MTT_B200_STATUS_*. */
 /* Measurement hooks (no reference counterpart).  cycles[c] of CTA c, 0 when
  * a bounded wait gave up.
- * umma_cycles: SM cycles for n_mma back-to-back tcgen05.mma kind::f16 of
- *   M = 128, N = n (16..256, multiple of 16), K = 16 into `accumulators`
- *   TMEM accumulators (accumulators * n <= 512), on `ctas` CTAs.
+ * umma_cycles: SM cycles for n_mma (a multiple of 16) back-to-back
+ *   tcgen05.mma kind::f16 of M = 128, N = n (16..256, multiple of 16), K = 16
+ *   into `accumulators` (a power of two, accumulators * n <= 512) TMEM
+ *   accumulators, on `ctas` CTAs.
  * dsmem_cycles: SM cycles for `rounds` rounds in which every CTA of an 8-CTA
  *   cluster bulk-copies bytes_per_peer (16..16384, multiple of 16) of its
  *   shared memory into each of its 7 peers', on `clusters` clusters. */

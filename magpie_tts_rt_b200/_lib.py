@@ -106,6 +106,7 @@ PATH_SPLIT_2 = 6
 PATH_SPLIT_4 = 7
 PATH_SPLIT_8 = 8
 PATH_SPLIT_2X32 = 9
+PATH_QUAD = 10
 
 
 class StreamBatch(ctypes.Structure):

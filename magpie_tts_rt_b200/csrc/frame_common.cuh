@@ -157,6 +157,12 @@ bool split_frame_supported(const Frame& f, int split, int rows);
 int split_frame_clusters(int split, int rows);
 cudaError_t launch_split_frame(const Frame& f, int split, int rows, cudaStream_t stream);
 
+// Quad kernel (frame_quad.cu): a 4-CTA cluster per 16-session tile (32 rows),
+// one attention head per CTA, tcgen05 GEMMs on 32-row tiles.
+bool quad_frame_supported(const Frame& f);
+int quad_frame_clusters();
+cudaError_t launch_quad_frame(const Frame& f, cudaStream_t stream);
+
 // EOS projection (tcgen05 GEMM, eos_proj.cuh) + decision for the sessions a
 // frame kernel registered in eos_list / eos_count.
 cudaError_t launch_frame_eos(const Frame& f, cudaStream_t stream);

@@ -3,9 +3,11 @@
 //
 // * mtt_b200_test_umma_cycles: SM cycles of one tcgen05.mma kind::f16
 //   (M = 128, K = 16, A and B in shared memory) for a given N, issued back to
-//   back from one thread into `accumulators` independent TMEM accumulators.
-//   On B200 the cost is the same for every N up to 256, so a row tile narrower
-//   than 256 leaves that fraction of the tensor core idle.
+//   back from one thread into `accumulators` independent TMEM accumulators
+//   (n_mma a multiple of 16, accumulators a power of two).  On B200 an
+//   instruction costs N / 2 cycles for N >= 128 (the dense peak) and about 46
+//   cycles for every N <= 32, whatever the number of accumulators: below
+//   N = 128 a narrower row tile leaves that fraction of the tensor core idle.
 // * mtt_b200_test_dsmem_bytes_per_cycle: the bytes per SM cycle that each CTA
 //   of an 8-CTA cluster pushes into its 7 peers' shared memory with bulk
 //   copies (cp.async.bulk shared::cta -> shared::cluster), rounds separated
@@ -49,10 +51,16 @@ __global__ void __launch_bounds__(128) umma_probe_kernel(int n_mma, int n, int a
     const uint32_t idesc = umma_idesc_bf16(128, n);
     const uint64_t a0 = umma_desc_sw128(smem);
     const uint64_t b0 = umma_desc_sw128(smem + 16384);
+    // 16 MMAs per iteration with precomputed operands, so the loop itself
+    // issues faster than the tensor core retires (accumulators: a power of two)
+    const uint32_t amask = static_cast<uint32_t>(accumulators - 1);
     const long long t0 = clock64();
-    for (int i = 0; i < n_mma; ++i) {
-      const uint32_t d = tmem_base + static_cast<uint32_t>((i % accumulators) * n);
-      umma_bf16(d, a0 + 2 * (i & 3), b0 + 2 * (i & 3), idesc, i >= accumulators);
+    for (int i = 0; i < n_mma; i += 16) {
+#pragma unroll
+      for (int u = 0; u < 16; ++u) {
+        const uint32_t d = tmem_base + ((static_cast<uint32_t>(u) & amask) * static_cast<uint32_t>(n));
+        umma_bf16(d, a0 + 2 * (u & 3), b0 + 2 * (u & 3), idesc, i + u >= accumulators);
+      }
     }
     umma_commit(&bar);
     const bool ok = mbar_wait(&bar, 0, 100000000ull);
@@ -123,8 +131,9 @@ __global__ void __cluster_dims__(8, 1, 1) __launch_bounds__(128)
 extern "C" MTT_B200_API int mtt_b200_test_umma_cycles(int32_t n, int32_t accumulators, int32_t n_mma,
                                                      int32_t ctas, uint64_t* cycles, void* stream) {
   using namespace mtt;
-  if (cycles == nullptr || n < 16 || n > 256 || n % 16 != 0 || accumulators < 1 || accumulators * n > 512 ||
-      n_mma < 1 || ctas < 1 || ctas > 1024) {
+  if (cycles == nullptr || n < 16 || n > 256 || n % 16 != 0 || accumulators < 1 ||
+      (accumulators & (accumulators - 1)) != 0 || accumulators * n > 512 || n_mma < 16 || n_mma % 16 != 0 ||
+      ctas < 1 || ctas > 1024) {
     return MTT_B200_STATUS_INVALID_ARGUMENT;
   }
   if (cudaFuncSetAttribute(umma_probe_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kProbeMmaSmem) !=

@@ -25,9 +25,15 @@ from oracle import sampler as S
 pytestmark = pytest.mark.gpu
 
 RTOL = 1e-2
-PATH_AUTO, PHASE, FUSED, TILE, PAIR, SPLIT1, SPLIT2, SPLIT4, SPLIT8, SPLIT2X32 = 0, 1, 2, 3, 4, 5, 6, 7, 8, 9
+PATH_AUTO, PHASE, FUSED, TILE, PAIR, SPLIT1, SPLIT2, SPLIT4, SPLIT8, SPLIT2X32, QUAD = 0, 1, 2, 3, 4, 5, 6, 7, 8, 9, 10
 SPLITS = [SPLIT1, SPLIT2, SPLIT4, SPLIT8, SPLIT2X32]
-BOTH = [PHASE, FUSED, TILE, PAIR] + SPLITS
+BOTH = [PHASE, FUSED, TILE, PAIR, QUAD] + SPLITS
+PATH_IDS = {PATH_AUTO: "auto", PHASE: "phase", FUSED: "cluster", TILE: "tile", PAIR: "pair", SPLIT1: "split1",
+            SPLIT2: "split2", SPLIT4: "split4", SPLIT8: "split8", SPLIT2X32: "split2x32", QUAD: "quad"}
+
+
+def path_id(v):
+    return PATH_IDS.get(v) if isinstance(v, int) and not isinstance(v, bool) and v in PATH_IDS else None
 
 
 def bits(t):
@@ -167,7 +173,8 @@ FLAGS6 = ([0, 1, 0, 0, 0, 1], [0, 0, 0, 1, 0, 1], [0, 0, 1, 0, 0, 0])  # incl. a
     (SHAPE_BASELINE, 11, FUSED, False), (SHAPE_BASELINE, 6, PAIR, True), (SHAPE_BASELINE, 11, PAIR, True),
     (SHAPE_BASELINE, 20, PAIR, True), (SHAPE_BASELINE, 11, PAIR, False), (SHAPE_SOFIA, 3, PHASE, True)] +
     [(SHAPE_BASELINE, n, sp, fold) for sp in SPLITS for n, fold in ((6, True), (11, True), (20, True), (11, False))] +
-    [(SHAPE_BASELINE, 24, SPLIT2X32, True), (SHAPE_BASELINE, 17, SPLIT2X32, False)])
+    [(SHAPE_BASELINE, 24, SPLIT2X32, True), (SHAPE_BASELINE, 17, SPLIT2X32, False)] +
+    [(SHAPE_BASELINE, n, QUAD, fold) for n, fold in ((6, True), (11, True), (20, True), (24, True), (17, False))])
 def test_frame_matches_oracle(engines, shape, n, path, fold):
     w = weights(shape, 21)
     eng = engines(shape, 21, 24, path=path, fold=fold)
@@ -210,7 +217,7 @@ def test_auto_path_for_the_benchmark_shape(engines):
     assert engines(SHAPE_SOFIA, 21, 1, with_final=False).path == PHASE
 
 
-@pytest.mark.parametrize("path", BOTH)
+@pytest.mark.parametrize("path", BOTH, ids=path_id)
 def test_frame_sequence_counters(engines, path):
     """Three consecutive frames of 4 sessions: the counter advances by 16 per
     frame and every frame matches the oracle (sequence_contract.py:95-160)."""
@@ -231,7 +238,7 @@ def test_frame_sequence_counters(engines, path):
         counter = gpu["counter"]
 
 
-@pytest.mark.parametrize("path", BOTH)
+@pytest.mark.parametrize("path", BOTH, ids=path_id)
 def test_inactive_streams_untouched(engines, path):
     shape = SHAPE_BASELINE
     w = weights(shape, 21)
@@ -249,7 +256,7 @@ def test_inactive_streams_untouched(engines, path):
     check_frame(w, hidden, flags, seed, counter, gpu, streams=np.nonzero(active)[0])
 
 
-@pytest.mark.parametrize("path", BOTH)
+@pytest.mark.parametrize("path", BOTH, ids=path_id)
 def test_frames_fill_the_emission_aggregate(path):
     """launch_finalize_local_step folded into the frame call
     (synthesis_kernels.cu:53-86): four frames write their [8][2] tokens
@@ -306,7 +313,7 @@ def test_frames_fill_the_emission_aggregate(path):
         assert rc == L.STATUS_INVALID_ARGUMENT, (stride, off)
 
 
-@pytest.mark.parametrize("path", BOTH)
+@pytest.mark.parametrize("path", BOTH, ids=path_id)
 def test_argmax_without_cfg(engines, path):
     """Greedy decoding, one row per stream (config 1's mode, bf16 on the GPU):
     no RNG, counter unchanged (magpietts_fused_sampling.py:136-197)."""
@@ -324,7 +331,8 @@ def test_argmax_without_cfg(engines, path):
 
 
 @pytest.mark.parametrize("name,path", [("A_bf16_cfg", PATH_AUTO), ("A_bf16_cfg", TILE), ("A_bf16_cfg", PAIR),
-                                       ("R_bf16_cfg", PATH_AUTO)] + [("A_bf16_cfg", sp) for sp in SPLITS])
+                                       ("R_bf16_cfg", PATH_AUTO), ("A_bf16_cfg", QUAD)] +
+                         [("A_bf16_cfg", sp) for sp in SPLITS], ids=path_id)
 def test_frame_against_reference_golden(engines, golden, golden_dir, name, path):
     """Teacher-forced on the reference's tokens, the GPU logits match the NeMo
     oracle's recorded logits within tolerance."""
@@ -341,7 +349,7 @@ def test_frame_against_reference_golden(engines, golden, golden_dir, name, path)
         check_logits(gpu["logits"][0], z[f"{name}/f{f}/logits"].reshape(POSITIONS, 2, VOCAB), name)
 
 
-@pytest.mark.parametrize("path", BOTH)
+@pytest.mark.parametrize("path", BOTH, ids=path_id)
 def test_batch_of_64_streams(engines, path):
     """Config 3's batch size: 64 sessions x CFG pair, seeds 0..63."""
     shape = SHAPE_BASELINE
@@ -382,7 +390,7 @@ def test_gpu_no_further_from_exact_than_oracle(engines):
     assert gpu_err.max() <= 2.0 * cpu_err.max() + 1e-4, (gpu_err.max(), cpu_err.max())
 
 
-@pytest.mark.parametrize("path", [FUSED, TILE, PAIR] + SPLITS)
+@pytest.mark.parametrize("path", [FUSED, TILE, PAIR, QUAD] + SPLITS, ids=path_id)
 @pytest.mark.parametrize("kind", ["flat", "sharp", "ties"])
 def test_sampler_row_shapes(path, kind):
     """Logit rows that drive each top-k select path: flat rows (every token
@@ -416,7 +424,7 @@ def test_sampler_row_shapes(path, kind):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs in this process")
-@pytest.mark.parametrize("path", [PATH_AUTO, FUSED, TILE, PAIR, SPLIT4, SPLIT8])
+@pytest.mark.parametrize("path", [PATH_AUTO, FUSED, TILE, PAIR, SPLIT4, SPLIT8, QUAD], ids=path_id)
 def test_frames_on_two_devices_in_one_process(path):
     """One process drives frames on cuda:0 and then cuda:1 (the reference
     allows several runtimes per process, tests/c_api/multi_runtime_plugin_gpu_tests.cpp).
