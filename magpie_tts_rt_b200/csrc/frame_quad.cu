@@ -37,7 +37,7 @@
 // (no multicast) that may come from different rows of a matrix (head c's q
 // and k rows); the weights stream through a ring filled by a producer warp
 // that runs ahead across GEMMs and positions.  One thread issues the MMAs;
-// tcgen05.commit frees a ring slot and signals an accumulator full.
+// tcgen05.commit frees the ring slots and signals an accumulator full.
 //
 // Tensor memory (512 columns x 128 lanes): lane 32 q + l holds row
 // 8 q + l / 4, head dims [16 (l % 4), +16); K of position j at columns
@@ -104,11 +104,25 @@ struct QuadMaps {
 // MMAs finish before LN1 writes xa) and the position's working buffers.
 // Peers push only into ab and v, never while the receiver's src is live (the
 // first push of a position, R1, follows the receiver's attention).
+// Attention exchange between the two warps of a TMEM lane quadrant (even and
+// odd positions): their exponentials, the odd warp's partial outputs, the
+// partial maxima.
+struct QuadAttn {
+  float e[128][17];
+  float o[128][17];
+  float m[2][128];
+};
+
 union QuadWork {
   bf16 src[12 * kQPanel];  // in-projection input rows (B operand, K = 768)
   struct {
-    bf16 xa[4 * kQPanel];   // LayerNorm output (B operand)
-    bf16 hid[4 * kQPanel];  // FFN hidden slice (B operand)
+    union {
+      struct {
+        bf16 xa[4 * kQPanel];   // LayerNorm output (B operand)
+        bf16 hid[4 * kQPanel];  // FFN hidden slice (B operand)
+      };
+      QuadAttn att;  // between the q|k|v MMAs and LN2 / FFN1
+    };
     union V {
       bf16 qkv[kQR * kQLdQkv];     // q | k | v of head c
       float red[kQC][kQOf][kQR];   // FFN2 partial sums of the owned features, by sender
@@ -126,7 +140,7 @@ struct __align__(1024) QuadSmem {
     uint16_t stage[kQS][kQVs];                 // head values of the other CTAs' sessions, before sending
     uint16_t lists[kQOwn][2 * kListCap + 16];  // sampler scratch (one warp per owned session)
   } xr;
-  __align__(16) bf16 hb[kQVs];  // head p bias, this CTA's vocabulary slice
+  __align__(16) bf16 hb[2][kQVs];  // head bias of positions p (p % 2) and p + 1, this CTA's vocabulary slice
   int32_t tok[kQS][kPositions];
   int32_t sess[kQS];
   uint32_t flags[kQS];                  // bit 0 unfinished, bit 1 finished, bit 2 forbid_eos
@@ -221,7 +235,7 @@ __device__ void q_producer(QuadSmem& sm, const QuadMaps& maps, int c, bool folde
       for (int b = 0; b < nb; ++b) {
         for (int k = 0; k < nk; ++k, ++it) {
           const int slot = it % kQSlots;
-          if (it >= kQSlots && qerr(sm) == 0 && !mbar_wait(&sm.empty[slot], ((it / kQSlots) - 1) & 1)) sm.err = 1;
+          if (it >= kQSlots && qerr(sm) == 0 && !mbar_wait_cta(&sm.empty[slot], ((it / kQSlots) - 1) & 1)) sm.err = 1;
           if (qerr(sm)) return;
           int x0, ra, rb;
           const CUtensorMap* map = q_chunk(maps, c, p, g, b, k, &x0, &ra, &rb);
@@ -249,46 +263,63 @@ __device__ __forceinline__ const bf16* q_operand(QuadSmem& sm, int g) {
 
 // The MMA warp's single thread: per GEMM wait until the consumers have
 // written its B operand; per M-block wait for a free accumulator buffer; per
-// chunk wait for the weights, issue 4 MMAs (K = 64) and free the slot.
+// group of 4 weight chunks (K = 256) wait for all four, then issue the 16
+// MMAs as one straight-line burst (a branch between tcgen05.mma instructions
+// halves their issue rate) and free the four slots.  The ring is consumed in
+// order by this one thread, so every parity wait is for the phase right
+// after the one it last saw complete.
 __device__ void q_mma(QuadSmem& sm, bool folded) {
   int it = 0, mb = 0, gn = 0;
   for (int p = 0; p < kPositions && qerr(sm) == 0; ++p) {
     for (int g = q_has_in(folded, p) ? Q_IN : Q_QKV; g <= Q_HEAD && qerr(sm) == 0; ++g) {
-      if (!mbar_wait(&sm.opready, gn & 1)) {
+      if (!mbar_wait_cta(&sm.opready, gn & 1)) {
         sm.err = 1;
         break;
       }
       ++gn;
       tmem_fence_after_sync();
       const bf16* bop = q_operand(sm, g);
-      const int nb = q_blocks(g), nk = q_kchunks(g);
-      for (int b = 0; b < nb && qerr(sm) == 0; ++b, ++mb) {
+      const int nb = q_blocks(g), ng = q_kchunks(g) / 4;
+      bool ok = true;
+      for (int b = 0; b < nb; ++b, ++mb) {
         const int db = mb % kQNbuf, use = mb / kQNbuf;
-        if (use >= 1 && !mbar_wait(&sm.dempty[db], (use - 1) & 1)) {
-          sm.err = 1;
-          break;
-        }
-        tmem_fence_after_sync();
+        ok = use < 1 || mbar_wait_cta(&sm.dempty[db], (use - 1) & 1);
         const uint32_t d = sm.tmem + kQAcc0 + 32u * static_cast<uint32_t>(db);
-        for (int k = 0; k < nk; ++k, ++it) {
-          const int slot = it % kQSlots;
-          if (!mbar_wait(&sm.full[slot], (it / kQSlots) & 1)) {
-            sm.err = 1;
-            break;
-          }
-          tmem_fence_after_sync();
-          const uint64_t a0 = umma_desc_sw128(sm.ring[slot]);
-          const uint64_t b0 = umma_desc_sw128(bop + k * kQPanel);
+        for (int gr = 0; gr < ng && ok; ++gr, it += 4) {
+          int slot[4];
 #pragma unroll
-          for (int kk = 0; kk < 4; ++kk) umma_bf16(d, a0 + 2 * kk, b0 + 2 * kk, kQIdesc, (k | kk) != 0);
-          umma_commit(&sm.empty[slot]);
+          for (int k = 0; k < 4; ++k) {
+            slot[k] = (it + k) % kQSlots;
+            ok = ok && mbar_wait_cta(&sm.full[slot[k]], ((it + k) / kQSlots) & 1);
+          }
+          if (!ok) break;
+          tmem_fence_after_sync();
+          const uint64_t b0 = umma_desc_sw128(bop + 4 * gr * kQPanel);
+          const uint64_t a0[4] = {umma_desc_sw128(sm.ring[slot[0]]), umma_desc_sw128(sm.ring[slot[1]]),
+                                  umma_desc_sw128(sm.ring[slot[2]]), umma_desc_sw128(sm.ring[slot[3]])};
+          const bool acc0 = gr != 0;
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) {
+              umma_bf16(d, a0[k] + 2 * kk, b0 + static_cast<uint64_t>(k * (kQPanel * 2 / 16)) + 2 * kk, kQIdesc,
+                        acc0 || (k | kk) != 0);
+            }
+          }
+#pragma unroll
+          for (int k = 0; k < 4; ++k) umma_commit(&sm.empty[slot[k]]);
         }
+        if (!ok) break;
         umma_commit(&sm.dfull[db]);
+      }
+      if (!ok) {
+        sm.err = 1;
+        break;
       }
     }
   }
   umma_commit(&sm.mmafin);
-  mbar_wait(&sm.mmafin, 0);
+  mbar_wait_cta(&sm.mmafin, 0);
   atomicExch(&sm.mma_done, 1);
 }
 
@@ -301,7 +332,7 @@ __device__ void q_mma(QuadSmem& sm, bool folded) {
 __device__ __forceinline__ void q_load_block(QuadSmem& sm, int mb, float (&v)[16]) {
   const int warp = threadIdx.x >> 5;
   const int db = mb % kQNbuf, use = mb / kQNbuf;
-  if (qerr(sm) == 0 && !mbar_wait(&sm.dfull[db], use & 1)) sm.err = 1;
+  if (qerr(sm) == 0 && !mbar_wait_cta(&sm.dfull[db], use & 1)) sm.err = 1;
   tmem_fence_after_sync();
   uint32_t r[16];
   tmem_ld16(r, sm.tmem + (static_cast<uint32_t>(32 * (warp & 3)) << 16) + kQAcc0 + 32u * db + 16u * (warp >> 2));
@@ -322,28 +353,42 @@ __device__ __forceinline__ void q_operand_ready(QuadSmem& sm) {
 // LayerNorm (no bias, eps 1e-5) of the 32 rows of x into the B operand xa;
 // lane holds weights g of columns [8 lane, +8); warp w: rows [4 w, +4).
 __device__ __forceinline__ void q_layer_norm(const bf16* x, bf16* xa, const float (&g)[8]) {
+  constexpr int kRows = kQR / kQW;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  float v[kRows][8], sum[kRows], var[kRows];
 #pragma unroll
-  for (int rr = 0; rr < kQR / kQW; ++rr) {
-    const int r = (kQR / kQW) * warp + rr;
-    float v[8];
-    unpack8(*reinterpret_cast<const uint4*>(x + r * kQLdX + lane * 8), v);
-    float sum = 0.f;
+  for (int rr = 0; rr < kRows; ++rr) {
+    unpack8(*reinterpret_cast<const uint4*>(x + (kRows * warp + rr) * kQLdX + lane * 8), v[rr]);
+    sum[rr] = 0.f;
 #pragma unroll
-    for (int j = 0; j < 8; ++j) sum += v[j];
+    for (int j = 0; j < 8; ++j) sum[rr] += v[rr][j];
+  }
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-    const float mean = sum / static_cast<float>(kQD);
-    float var = 0.f;
+  for (int o = 16; o > 0; o >>= 1) {
 #pragma unroll
-    for (int j = 0; j < 8; ++j) var += (v[j] - mean) * (v[j] - mean);
+    for (int rr = 0; rr < kRows; ++rr) sum[rr] += __shfl_xor_sync(0xffffffffu, sum[rr], o);
+  }
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) var += __shfl_xor_sync(0xffffffffu, var, o);
-    const float rstd = 1.0f / sqrtf(var / static_cast<float>(kQD) + 1.0e-5f);
+  for (int rr = 0; rr < kRows; ++rr) {
+    const float mean = sum[rr] / static_cast<float>(kQD);
+    sum[rr] = mean;
+    var[rr] = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) var[rr] += (v[rr][j] - mean) * (v[rr][j] - mean);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+#pragma unroll
+    for (int rr = 0; rr < kRows; ++rr) var[rr] += __shfl_xor_sync(0xffffffffu, var[rr], o);
+  }
+#pragma unroll
+  for (int rr = 0; rr < kRows; ++rr) {
+    const float mean = sum[rr];
+    const float rstd = 1.0f / sqrtf(var[rr] / static_cast<float>(kQD) + 1.0e-5f);
     float out[8];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) out[j] = ((v[j] - mean) * rstd) * g[j];
-    *qop_unit(xa, r, lane * 8) = pack8(out);
+    for (int j = 0; j < 8; ++j) out[j] = ((v[rr][j] - mean) * rstd) * g[j];
+    *qop_unit(xa, kRows * warp + rr, lane * 8) = pack8(out);
   }
 }
 
@@ -382,55 +427,27 @@ __device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&v)[8])
                : "memory");
 }
 
-// Dot products of q (16 dims of this lane) with 8 cached keys (64 columns:
-// 8 per position), reduced over the row's four lanes; s[j] for positions
-// base + j <= p, rounded as the reference rounds scores.
-__device__ __forceinline__ void q_scores8(const uint32_t (&kv)[64], const float (&q)[16], int base, int p,
-                                          float (&s)[kPositions]) {
-#pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    float d0 = 0.f, d1 = 0.f;
-#pragma unroll
-    for (int e = 0; e < 8; e += 2) {
-      const float2 t0 = __bfloat1622float2(bf2_of(kv[8 * j + e]));
-      const float2 t1 = __bfloat1622float2(bf2_of(kv[8 * j + e + 1]));
-      d0 = fmaf(q[2 * e], t0.x, d0);
-      d0 = fmaf(q[2 * e + 1], t0.y, d0);
-      d1 = fmaf(q[2 * e + 2], t1.x, d1);
-      d1 = fmaf(q[2 * e + 3], t1.y, d1);
-    }
-    float dot = d0 + d1;
-    dot += __shfl_xor_sync(0xffffffffu, dot, 1);
-    dot += __shfl_xor_sync(0xffffffffu, dot, 2);
-    if (base + j <= p) s[base + j] = round_bf16(__fmul_rn(round_bf16(dot), 0.125f));
-  }
-}
+// TMEM column block of cached position j: even positions in blocks 0..7,
+// odd ones in 8..15, so each of the two attention warps of a lane quadrant
+// reads its positions with one 64-column load.
+__device__ __forceinline__ uint32_t q_kv_block(int j) { return 8u * static_cast<uint32_t>(j & 1) + (j >> 1); }
 
-__device__ __forceinline__ void q_values8(const uint32_t (&kv)[64], const float (&prob)[kPositions], int base, int p,
-                                          float (&o)[16]) {
-#pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    if (base + j <= p) {
-      const float pr = prob[base + j];
-#pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        const float2 t = __bfloat1622float2(bf2_of(kv[8 * j + e]));
-        o[2 * e] = fmaf(pr, t.x, o[2 * e]);
-        o[2 * e + 1] = fmaf(pr, t.y, o[2 * e + 1]);
-      }
-    }
-  }
-}
-
-// Attention of head c for the tile's 32 rows at position p (warps 0..3):
-// thread (warp q, lane l) = row 8 q + l / 4, head dims [16 (l % 4), +16).
-// Appends this position's k and v to the TMEM cache, scores every cached
-// position, softmax, and writes the output columns into ab and every peer's ab.
+// Attention of head c for the tile's 32 rows at position p, all 8 consumer
+// warps: warp w reads TMEM lane quadrant q = w % 4 and takes the positions of
+// parity w / 4; thread (w, l) = row 8 q + l / 4, head dims [16 (l % 4), +16).
+// This position's k and v go into the TMEM cache (K at column 8 b(j), V at
+// 128 + 8 b(j)); scores, exponentials and the softmax sum as the reference
+// takes them (sum over positions in order); each warp sums its positions'
+// values; the even warp adds the odd warp's partial output and writes the
+// output columns into ab and every peer's ab.
 __device__ __forceinline__ void q_attention(QuadSmem& sm, int p, int c, uint32_t rd) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int r = 8 * warp + (lane >> 2), u = lane & 3;
-  const uint32_t tl = sm.tmem + (static_cast<uint32_t>(32 * warp) << 16);
+  const int q4 = warp & 3, part = warp >> 2;
+  const int r = 8 * q4 + (lane >> 2), u = lane & 3;
+  const int t128 = 32 * q4 + lane;
+  const uint32_t tl = sm.tmem + (static_cast<uint32_t>(32 * q4) << 16);
   const bf16* row = sm.u.a.v.qkv + r * kQLdQkv;
+  QuadAttn& at = sm.u.a.att;
   float q[16];
   {
     uint32_t kk[8], vv[8];
@@ -446,65 +463,95 @@ __device__ __forceinline__ void q_attention(QuadSmem& sm, int p, int c, uint32_t
       kk[4 * h] = ka.x, kk[4 * h + 1] = ka.y, kk[4 * h + 2] = ka.z, kk[4 * h + 3] = ka.w;
       vv[4 * h] = va.x, vv[4 * h + 1] = va.y, vv[4 * h + 2] = va.z, vv[4 * h + 3] = va.w;
     }
-    tmem_st8(tl + 8u * p, kk);
-    tmem_st8(tl + 128u + 8u * p, vv);
-    tmem_wait_st();
-  }
-  float s[kPositions];
-#pragma unroll
-  for (int j = 0; j < kPositions; ++j) s[j] = -CUDART_INF_F;
-  {
-    uint32_t kv[64];
-    tmem_ld64(kv, tl);
-    q_scores8(kv, q, 0, p, s);
-    if (p >= 8) {
-      tmem_ld64(kv, tl + 64u);
-      q_scores8(kv, q, 8, p, s);
+    // the warp that takes position p's parity caches it (only that warp reads it)
+    if ((p & 1) == part) {
+      tmem_st8(tl + 8u * q_kv_block(p), kk);
+      tmem_st8(tl + 128u + 8u * q_kv_block(p), vv);
+      tmem_wait_st();
     }
   }
-  float mx = s[0];
+  // scores of this warp's positions j = 2 i + part <= p
+  float s[8];
+  float mloc = -CUDART_INF_F;
+  {
+    uint32_t kv[64];
+    tmem_ld64(kv, tl + 64u * part);
 #pragma unroll
-  for (int j = 1; j < kPositions; ++j) mx = fmaxf(mx, s[j]);
-  float sum = 0.f;
-  float e[kPositions];
+    for (int i = 0; i < 8; ++i) {
+      float d0 = 0.f, d1 = 0.f;
 #pragma unroll
-  for (int j = 0; j < kPositions; ++j) {
-    e[j] = j <= p ? expf(s[j] - mx) : 0.f;
-    sum += e[j];
+      for (int e = 0; e < 8; e += 2) {
+        const float2 t0 = __bfloat1622float2(bf2_of(kv[8 * i + e]));
+        const float2 t1 = __bfloat1622float2(bf2_of(kv[8 * i + e + 1]));
+        d0 = fmaf(q[2 * e], t0.x, d0);
+        d0 = fmaf(q[2 * e + 1], t0.y, d0);
+        d1 = fmaf(q[2 * e + 2], t1.x, d1);
+        d1 = fmaf(q[2 * e + 3], t1.y, d1);
+      }
+      float dot = d0 + d1;
+      dot += __shfl_xor_sync(0xffffffffu, dot, 1);
+      dot += __shfl_xor_sync(0xffffffffu, dot, 2);
+      s[i] = 2 * i + part <= p ? round_bf16(__fmul_rn(round_bf16(dot), 0.125f)) : -CUDART_INF_F;
+      mloc = fmaxf(mloc, s[i]);
+    }
   }
-  float prob[kPositions];
+  at.m[part][t128] = mloc;
+  qbar();
+  const float mx = fmaxf(at.m[0][t128], at.m[1][t128]);
+  float e[8];
 #pragma unroll
-  for (int j = 0; j < kPositions; ++j) prob[j] = round_bf16(e[j] / sum);
+  for (int i = 0; i < 8; ++i) {
+    e[i] = 2 * i + part <= p ? expf(s[i] - mx) : 0.f;
+    at.e[t128][2 * i + part] = e[i];
+  }
+  qbar();
+  float sum = 0.f;
+#pragma unroll
+  for (int j = 0; j < kPositions; ++j) sum += at.e[t128][j];
   float o[16];
 #pragma unroll
   for (int d = 0; d < 16; ++d) o[d] = 0.f;
   {
     uint32_t kv[64];
-    tmem_ld64(kv, tl + 128u);
-    q_values8(kv, prob, 0, p, o);
-    if (p >= 8) {
-      tmem_ld64(kv, tl + 192u);
-      q_values8(kv, prob, 8, p, o);
+    tmem_ld64(kv, tl + 128u + 64u * part);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      if (2 * i + part <= p) {
+        const float pr = round_bf16(e[i] / sum);
+#pragma unroll
+        for (int d = 0; d < 8; ++d) {
+          const float2 t = __bfloat1622float2(bf2_of(kv[8 * i + d]));
+          o[2 * d] = fmaf(pr, t.x, o[2 * d]);
+          o[2 * d + 1] = fmaf(pr, t.y, o[2 * d + 1]);
+        }
+      }
     }
   }
-  float lo[8], hi[8];
+  if (part == 1) {
 #pragma unroll
-  for (int d = 0; d < 8; ++d) {
-    lo[d] = o[d];
-    hi[d] = o[8 + d];
+    for (int d = 0; d < 16; ++d) at.o[t128][d] = o[d];
   }
-  const int k0 = kHeadDim * c + 16 * u;
-  uint4* d0 = qop_unit(sm.ab, r, k0);
-  uint4* d1 = qop_unit(sm.ab, r, k0 + 8);
-  const uint4 w0 = pack8(lo), w1 = pack8(hi);
-  *d0 = w0;
-  *d1 = w1;
+  qbar();
+  if (part == 0) {
+    float lo[8], hi[8];
 #pragma unroll
-  for (int j = 0; j < kQC; ++j) {
-    if (j != c) {
-      const uint32_t bar = q_round_bar(sm, rd, j);
-      st_async_v4(cluster_addr(d0, j), w0, bar);
-      st_async_v4(cluster_addr(d1, j), w1, bar);
+    for (int d = 0; d < 8; ++d) {
+      lo[d] = o[d] + at.o[t128][d];
+      hi[d] = o[8 + d] + at.o[t128][8 + d];
+    }
+    const int k0 = kHeadDim * c + 16 * u;
+    uint4* d0 = qop_unit(sm.ab, r, k0);
+    uint4* d1 = qop_unit(sm.ab, r, k0 + 8);
+    const uint4 w0 = pack8(lo), w1 = pack8(hi);
+    *d0 = w0;
+    *d1 = w1;
+#pragma unroll
+    for (int j = 0; j < kQC; ++j) {
+      if (j != c) {
+        const uint32_t bar = q_round_bar(sm, rd, j);
+        st_async_v4(cluster_addr(d0, j), w0, bar);
+        st_async_v4(cluster_addr(d1, j), w1, bar);
+      }
     }
   }
 }
@@ -621,7 +668,7 @@ __global__ void __launch_bounds__(kQThreads, 1) quad_frame_kernel(Frame f, const
       // no copy may still be writing when the CTA leaves
       for (int s = 0; s < kQSlots; ++s) {
         const int last = sm.last_issued[s];
-        if (last >= 0) mbar_wait(&sm.full[s], (last / kQSlots) & 1);
+        if (last >= 0) mbar_wait_cta(&sm.full[s], (last / kQSlots) & 1);
       }
       atomicExch(&sm.producer_done, 1);
     } else if (warp == kQW + 1 && lane == 0) {
@@ -640,6 +687,16 @@ __global__ void __launch_bounds__(kQThreads, 1) quad_frame_kernel(Frame f, const
     const float cfg_scale = f.prm.cfg_scale, uncond_scale = __fsub_rn(1.0f, f.prm.cfg_scale);
     int mb = 0;       // M-blocks consumed
     uint32_t rd = 0;  // exchange rounds
+    if (threadIdx.x < kQVs / 8) {  // head bias of position 0
+      const int v0 = kQVs * c + 8 * threadIdx.x;
+      const uint4 z = make_uint4(0, 0, 0, 0);
+      *reinterpret_cast<uint4*>(sm.hb[0] + 8 * threadIdx.x) = v0 < kVocab ? *reinterpret_cast<const uint4*>(f.head_b + v0) : z;
+      *reinterpret_cast<uint4*>(sm.hb[1] + 8 * threadIdx.x) = z;
+    }
+    // flags of the 8 sessions whose rows this thread holds in the head epilogue
+    uint32_t fl8[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) fl8[i] = 8 * sh + i < n_sess ? sm.flags[8 * sh + i] : 0u;
     for (int p = 0; p < kPositions; ++p) {
       q_stamp(f, tracer, p, 0);
       // ---------------- input rows
@@ -674,17 +731,18 @@ __global__ void __launch_bounds__(kQThreads, 1) quad_frame_kernel(Frame f, const
           }
         }
       }
-      // head p bias slice; per-position flags
-      {
-        const bf16* hbp = f.head_b + static_cast<int64_t>(p) * kVocab;
-        if (threadIdx.x < kQVs / 8) {
-          const int v0 = kQVs * c + 8 * threadIdx.x;
-          uint4 u = make_uint4(0, 0, 0, 0);
-          if (v0 < kVocab) u = *reinterpret_cast<const uint4*>(hbp + v0);  // kVocab % 8 == 0
-          *reinterpret_cast<uint4*>(sm.hb + 8 * threadIdx.x) = u;
+      // head bias: position p's slice has landed (issued a position ahead),
+      // position p + 1's is issued now; per-position flags
+      if (threadIdx.x < kQVs / 8) {
+        const int v0 = kQVs * c + 8 * threadIdx.x;
+        if (v0 < kVocab) {  // kVocab % 8 == 0; the slice's tail past the vocabulary stays zero
+          cp_async_wait_all();
+          if (p + 1 < kPositions) {
+            cp_async16(sm.hb[(p + 1) & 1] + 8 * threadIdx.x, f.head_b + static_cast<int64_t>(p + 1) * kVocab + v0);
+          }
         }
-        if (threadIdx.x < kQS) sm.nf[threadIdx.x] = 0;
       }
+      if (threadIdx.x < kQS) sm.nf[threadIdx.x] = 0;
       qbar();
 
       // ---------------- LN1, q|k|v of head c
@@ -704,7 +762,7 @@ __global__ void __launch_bounds__(kQThreads, 1) quad_frame_kernel(Frame f, const
       q_stamp(f, tracer, p, 2);
 
       // ---------------- attention (R1: head c's output columns to every CTA)
-      if (warp < 4) q_attention(sm, p, c, rd);
+      q_attention(sm, p, c, rd);
       q_stamp(f, tracer, p, 3);
       q_round(sm, rd, static_cast<uint32_t>((kQC - 1) * kQR * kHeadDim * 2));
       fence_proxy_async();
@@ -792,41 +850,59 @@ __global__ void __launch_bounds__(kQThreads, 1) quad_frame_kernel(Frame f, const
       // ---------------- head p: bias, CFG combine, constraints (R5: values to the owners)
       {
         bf16* lo_base = f.logits_out;
+        const bf16* hbp = sm.hb[p & 1];
         for (int b = 0; b < 4; ++b, ++mb) {
           float v[16];
           q_load_block(sm, mb, v);
           const int vl = 128 * b + m_lane;
           const int t = kQVs * c + vl;
           const bool in_vocab = t < kVocab;
-          const float bias = bf2f(sm.hb[vl]);
+          const float bias = bf2f(hbp[vl]);
+          uint32_t nfm = 0;
 #pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const int slot = 8 * sh + i;
-            bool nfs = false;
-            if (in_vocab && slot < n_sess) {
-              const __nv_bfloat16 cb = f2bf(__fadd_rn(v[2 * i], bias));
-              const __nv_bfloat16 ub = f2bf(__fadd_rn(v[2 * i + 1], bias));
-              if (lo_base) {
-                bf16* lr = lo_base + (static_cast<int64_t>(sm.sess[slot]) * kPositions + p) * rp * kVocab;
-                lr[t] = cb;
-                if (cfg) lr[kVocab + t] = ub;
-              }
-              uint32_t g = __bfloat16_as_ushort(cb);
-              if (cfg) {
-                const float sc = round_bf16(__fmul_rn(bf2f(cb), cfg_scale));
-                g = __bfloat16_as_ushort(f2bf(__fadd_rn(sc, __fmul_rn(bf2f(ub), uncond_scale))));
-              }
-              const uint32_t fl = sm.flags[slot];
-              const uint16_t val =
-                  static_cast<uint16_t>(constrain(g, t, fl & 1u, (fl & 2u) != 0, (fl & 4u) != 0, nfs));
-              const int owner = slot / kQOwn;
-              if (owner == c) {
-                sm.u.a.v.vals[slot - own0][t] = val;
-              } else {
-                sm.xr.stage[slot][vl] = val;
+          for (int i2 = 0; i2 < 4; ++i2) {
+            // sessions 8 sh + 2 i2 (low halves) and + 1 (high halves): rows 2 s, 2 s + 1
+            const uint32_t cc = pack2_rn(__fadd_rn(v[4 * i2], bias), __fadd_rn(v[4 * i2 + 2], bias));
+            const uint32_t uu = pack2_rn(__fadd_rn(v[4 * i2 + 1], bias), __fadd_rn(v[4 * i2 + 3], bias));
+            const int s0 = 8 * sh + 2 * i2;
+            if (lo_base != nullptr && in_vocab) {
+#pragma unroll
+              for (int h = 0; h < 2; ++h) {
+                if (s0 + h < n_sess) {
+                  uint16_t* lr = reinterpret_cast<uint16_t*>(lo_base) +
+                                 (static_cast<int64_t>(sm.sess[s0 + h]) * kPositions + p) * rp * kVocab;
+                  lr[t] = static_cast<uint16_t>(h ? cc >> 16 : cc & 0xffffu);
+                  if (cfg) lr[kVocab + t] = static_cast<uint16_t>(h ? uu >> 16 : uu & 0xffffu);
+                }
               }
             }
-            if (__any_sync(0xffffffffu, nfs) && lane == 0) atomicOr(&sm.nf[slot], 1u);
+            const uint32_t g = cfg ? guided_value2(cc, uu, cfg_scale, uncond_scale) : cc;
+            uint32_t g0 = g & 0xffffu, g1 = g >> 16;
+            const uint32_t f0 = fl8[2 * i2], f1 = fl8[2 * i2 + 1];
+            if (t >= kCodebook || (g0 & 0x7f80u) == 0x7f80u || (g1 & 0x7f80u) == 0x7f80u || ((f0 | f1) & 2u)) {
+              bool n0 = false, n1 = false;
+              g0 = constrain(g0, t, f0 & 1u, (f0 & 2u) != 0, (f0 & 4u) != 0, n0);
+              g1 = constrain(g1, t, f1 & 1u, (f1 & 2u) != 0, (f1 & 4u) != 0, n1);
+              if (in_vocab) nfm |= (n0 ? 1u : 0u) << (2 * i2) | (n1 ? 1u : 0u) << (2 * i2 + 1);
+            }
+            if (in_vocab) {
+              // slots s0, s0 + 1 share their owner (owners hold 4 aligned slots)
+              const int owner = s0 / kQOwn;
+              if (owner == c) {
+                sm.u.a.v.vals[s0 - own0][t] = static_cast<uint16_t>(g0);
+                sm.u.a.v.vals[s0 + 1 - own0][t] = static_cast<uint16_t>(g1);
+              } else {
+                sm.xr.stage[s0][vl] = static_cast<uint16_t>(g0);
+                sm.xr.stage[s0 + 1][vl] = static_cast<uint16_t>(g1);
+              }
+            }
+          }
+          const uint32_t any = __reduce_or_sync(0xffffffffu, nfm);
+          if (lane == 0 && any != 0) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              if (any & (1u << i)) atomicOr(&sm.nf[8 * sh + i], 1u);
+            }
           }
         }
         qbar();

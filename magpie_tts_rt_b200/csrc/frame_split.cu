@@ -383,23 +383,58 @@ __device__ void mma_issuer(SplitSmem<C, R>& sm, bool folded) {
         }
         tmem_fence_after_sync();
         const uint32_t d = sm.tmem + K::dcol(db);
-        for (int k = 0; k < nk; ++k, ++it) {
-          if (pieces && (k & 1) == 0 && !wait_operand()) break;
-          const int kc = pieces ? (k & 1) : k;  // K-chunk within the operand buffer
-          const int slot = it % K::slots;
-          if (!mbar_wait(&sm.full[slot], (it / K::slots) & 1)) {
-            sm.err = 1;
-            break;
-          }
-          tmem_fence_after_sync();
+        if (pieces) {
+          for (int k = 0; k < nk; ++k, ++it) {
+            if ((k & 1) == 0 && !wait_operand()) break;
+            const int kc = k & 1;  // K-chunk within the operand piece
+            const int slot = it % K::slots;
+            if (!mbar_wait(&sm.full[slot], (it / K::slots) & 1)) {
+              sm.err = 1;
+              break;
+            }
+            tmem_fence_after_sync();
 #pragma unroll
-          for (int kk = 0; kk < 8; ++kk) {
-            const uint64_t a = umma_desc_sw128(sm.ring[slot] + (kk >> 2) * kPanelElems) + 2 * (kk & 3);
-            const uint64_t bd = umma_desc_sw128(bop + (2 * kc + (kk >> 2)) * K::op_panel) + 2 * (kk & 3);
-            umma_bf16(d, a, bd, K::idesc, (k | kk) != 0);
+            for (int kk = 0; kk < 8; ++kk) {
+              const uint64_t a = umma_desc_sw128(sm.ring[slot] + (kk >> 2) * kPanelElems) + 2 * (kk & 3);
+              const uint64_t bd = umma_desc_sw128(bop + (2 * kc + (kk >> 2)) * K::op_panel) + 2 * (kk & 3);
+              umma_bf16(d, a, bd, K::idesc, (k | kk) != 0);
+            }
+            umma_commit(&sm.empty[slot]);
+            if ((k & 1) == 1) umma_commit(&sm.srcfree);
           }
-          umma_commit(&sm.empty[slot]);
-          if (pieces && (k & 1) == 1) umma_commit(&sm.srcfree);
+        } else {
+          // two chunks (K = 256) at a time: wait for both, then their 16 MMAs
+          // as one straight-line burst (a branch between tcgen05.mma
+          // instructions halves their issue rate)
+          for (int k = 0; k < nk; k += 2) {
+            const bool two = k + 1 < nk;
+            const int s0 = it % K::slots, s1 = (it + 1) % K::slots;
+            bool ok = mbar_wait(&sm.full[s0], (it / K::slots) & 1);
+            if (two) ok = ok && mbar_wait(&sm.full[s1], ((it + 1) / K::slots) & 1);
+            if (!ok) {
+              sm.err = 1;
+              break;
+            }
+            tmem_fence_after_sync();
+            const uint64_t a0 = umma_desc_sw128(sm.ring[s0]), a1 = umma_desc_sw128(sm.ring[s1]);
+            const uint64_t b0 = umma_desc_sw128(bop + 2 * k * K::op_panel);
+            constexpr uint64_t kPanelStep = kPanelElems * 2 / 16, kOpStep = K::op_panel * 2 / 16;
+#pragma unroll
+            for (int kk = 0; kk < 8; ++kk) {
+              umma_bf16(d, a0 + (kk >> 2) * kPanelStep + 2 * (kk & 3), b0 + (kk >> 2) * kOpStep + 2 * (kk & 3),
+                        K::idesc, (k | kk) != 0);
+            }
+            if (two) {
+#pragma unroll
+              for (int kk = 0; kk < 8; ++kk) {
+                umma_bf16(d, a1 + (kk >> 2) * kPanelStep + 2 * (kk & 3),
+                          b0 + (2 + (kk >> 2)) * kOpStep + 2 * (kk & 3), K::idesc, true);
+              }
+            }
+            umma_commit(&sm.empty[s0]);
+            if (two) umma_commit(&sm.empty[s1]);
+            it += two ? 2 : 1;
+          }
         }
         umma_commit(&sm.dfull[db]);
       }

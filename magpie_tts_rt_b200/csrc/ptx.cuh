@@ -21,6 +21,10 @@ __device__ __forceinline__ void cp_async4(void* smem_dst, const void* gsrc) {
   asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_addr(smem_dst)), "l"(gsrc) : "memory");
 }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+// 16-byte form (both addresses 16-byte aligned), bypassing L1.
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gsrc) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(smem_dst)), "l"(gsrc) : "memory");
+}
 
 __device__ __forceinline__ uint32_t cluster_addr(const void* local, int rank) {
   uint32_t r;
@@ -50,19 +54,54 @@ __device__ __forceinline__ unsigned long long global_ns() {
 // Waits for the phase with the given parity; returns false when it did not
 // complete within limit_ns (the caller records the error and goes on, so a
 // broken pipeline costs milliseconds, never a hang).
+// One try with a suspend-time hint: a thread whose phase has not completed
+// sleeps until it completes (or the hint, 10 ms, runs out) instead of
+// spinning, so waiting warps leave their issue slots to the warps that work.
+__device__ __forceinline__ bool mbar_try(uint32_t a, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;\n"
+      " selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(done)
+      : "r"(a), "r"(parity), "r"(10000000u)
+      : "memory");
+  return done != 0;
+}
+
+// CTA-scope form, for barriers that only this CTA's threads, its TMA copies
+// and its tcgen05 commits complete: a cluster-scope acquire costs a few
+// hundred cycles even when the phase has long completed.
+__device__ __forceinline__ bool mbar_try_cta(uint32_t a, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n"
+      " selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(done)
+      : "r"(a), "r"(parity), "r"(10000000u)
+      : "memory");
+  return done != 0;
+}
+
+__device__ __forceinline__ bool mbar_wait_cta(unsigned long long* bar, uint32_t parity,
+                                              unsigned long long limit_ns = 20000000ull) {
+  const uint32_t a = smem_addr(bar);
+  if (mbar_try_cta(a, parity)) return true;
+  const unsigned long long t0 = global_ns();
+  while (true) {
+    if (mbar_try_cta(a, parity)) return true;
+    if (global_ns() - t0 > limit_ns) return false;
+  }
+}
+
+// The global timer is read only after a first unsuccessful try: a read costs
+// a few hundred cycles, which a phase that has already completed must not pay.
 __device__ __forceinline__ bool mbar_wait(unsigned long long* bar, uint32_t parity,
                                           unsigned long long limit_ns = 20000000ull) {
   const uint32_t a = smem_addr(bar);
+  if (mbar_try(a, parity)) return true;
   const unsigned long long t0 = global_ns();
   while (true) {
-    uint32_t done;
-    asm volatile(
-        "{\n .reg .pred p;\n mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n"
-        " selp.u32 %0, 1, 0, p;\n}\n"
-        : "=r"(done)
-        : "r"(a), "r"(parity)
-        : "memory");
-    if (done) return true;
+    if (mbar_try(a, parity)) return true;
     if (global_ns() - t0 > limit_ns) return false;
   }
 }
