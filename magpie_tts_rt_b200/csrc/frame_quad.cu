@@ -82,7 +82,7 @@ constexpr int kQF = 1024;
 constexpr int kQF1 = kQF / kQC;        // FFN features per CTA
 constexpr int kQOf = kQD / kQC;        // residual features owned per CTA (FFN2 reduction)
 constexpr int kQVs = 512;              // vocabulary slice per CTA
-constexpr int kQSlots = 7;             // weight ring slots
+constexpr int kQSlots = 8;             // weight ring slots
 constexpr int kQNbuf = 8;              // accumulator buffers
 constexpr int kQChunkK = 64;
 constexpr int kQChunkElems = 128 * kQChunkK;            // 16 KB
@@ -125,7 +125,7 @@ union QuadWork {
     };
     union V {
       bf16 qkv[kQR * kQLdQkv];     // q | k | v of head c
-      float red[kQC][kQOf][kQR];   // FFN2 partial sums of the owned features, by sender
+      float red[kQC - 1][kQOf][kQR];  // FFN2 partial sums of the owned features from the peers (sender order)
       uint16_t vals[kQOwn][2048];  // constrained values of the owned sessions
     } v;
   } a;
@@ -188,11 +188,13 @@ __device__ __forceinline__ void qop_store(bf16* base, int r, int k, bf16 v) {
 // ---------------------------------------------------------------------------
 
 __device__ __forceinline__ bool q_has_in(bool folded, int p) { return p == 0 || !folded; }
-__device__ __forceinline__ int q_blocks(int g) { return g == Q_HEAD ? 4 : 2; }
+__device__ __forceinline__ int q_blocks(int g) { return g == Q_HEAD ? 4 : (g == Q_O ? 1 : 2); }
 __device__ __forceinline__ int q_kchunks(int g) { return g == Q_IN ? kEmbed / kQChunkK : 4; }
 
 // Tensor map and origins of chunk (M-block b, K-chunk k) of GEMM g: K column
-// x0, rows ra (A rows 0..63) and rb (A rows 64..127).
+// x0, rows ra (A rows 0..63) and rb (A rows 64..127); rb < 0 when the block
+// has 64 weight rows only (A rows 64..127 keep stale weights, and the
+// epilogue ignores their lanes).
 __device__ __forceinline__ const CUtensorMap* q_chunk(const QuadMaps& m, int c, int p, int g, int b, int k, int* x0,
                                                       int* ra, int* rb) {
   *x0 = kQChunkK * k;
@@ -201,13 +203,13 @@ __device__ __forceinline__ const CUtensorMap* q_chunk(const QuadMaps& m, int c, 
       *ra = 128 * b;
       *rb = 128 * b + 64;
       return &m.in_proj;
-    case Q_QKV:  // block 0: head c's q and k rows; block 1: its v rows (twice)
+    case Q_QKV:  // block 0: head c's q and k rows; block 1: its v rows
       *ra = b == 0 ? kHeadDim * c : 2 * kQD + kHeadDim * c;
-      *rb = b == 0 ? kQD + kHeadDim * c : *ra;
+      *rb = b == 0 ? kQD + kHeadDim * c : -1;
       return &m.qkv;
-    case Q_O:
-      *ra = 128 * b;
-      *rb = 128 * b + 64;
+    case Q_O:  // output features [64 c, +64)
+      *ra = kQOf * c;
+      *rb = -1;
       return &m.o;
     case Q_F1:
       *ra = kQF1 * c + 128 * b;
@@ -239,10 +241,10 @@ __device__ void q_producer(QuadSmem& sm, const QuadMaps& maps, int c, bool folde
           if (qerr(sm)) return;
           int x0, ra, rb;
           const CUtensorMap* map = q_chunk(maps, c, p, g, b, k, &x0, &ra, &rb);
-          mbar_expect_tx(&sm.full[slot], kQChunkBytes);
+          mbar_expect_tx(&sm.full[slot], rb < 0 ? kQChunkBytes / 2 : kQChunkBytes);
           bf16* dst = sm.ring[slot];
           tma_load_2d(dst, map, x0, ra, &sm.full[slot]);
-          tma_load_2d(dst + kQBoxRows * 64, map, x0, rb, &sm.full[slot]);
+          if (rb >= 0) tma_load_2d(dst + kQBoxRows * 64, map, x0, rb, &sm.full[slot]);
           sm.last_issued[slot] = it;
         }
       }
@@ -769,18 +771,31 @@ __global__ void __launch_bounds__(kQThreads, 1) quad_frame_kernel(Frame f, const
       q_operand_ready(sm);
       q_stamp(f, tracer, p, 4);
 
-      // ---------------- o-projection (all features) + residual, LN2
-      for (int b = 0; b < 2; ++b, ++mb) {
+      // ---------------- o-projection features [64 c, +64) + residual (R2: the slice to every CTA), LN2
+      {
         float v[16];
         q_load_block(sm, mb, v);
-        const int n = 128 * b + m_lane;
+        ++mb;
+        if (m_lane < kQOf) {
+          const int n = kQOf * c + m_lane;
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          bf16* xr = sm.xr.x + (16 * sh + i) * kQLdX + n;
-          *xr = f2bf(__fadd_rn(bf2f(*xr), round_bf16(v[i])));
+          for (int i = 0; i < 16; ++i) {
+            bf16* xr = sm.xr.x + (16 * sh + i) * kQLdX + n;
+            *xr = f2bf(__fadd_rn(bf2f(*xr), round_bf16(v[i])));
+          }
         }
       }
       qbar();
+      {
+        // thread: row lane, features [64 c + 8 warp, +8)
+        const uint4* src = reinterpret_cast<const uint4*>(sm.xr.x + lane * kQLdX + kQOf * c + 8 * warp);
+        const uint4 w = *src;
+#pragma unroll
+        for (int j = 0; j < kQC; ++j) {
+          if (j != c) st_async_v4(cluster_addr(src, j), w, q_round_bar(sm, rd, j));
+        }
+      }
+      q_round(sm, rd, static_cast<uint32_t>((kQC - 1) * kQR * kQOf * 2));
       q_stamp(f, tracer, p, 5);
       q_layer_norm(sm.xr.x, sm.u.a.xa, g2);
       q_operand_ready(sm);
@@ -803,7 +818,10 @@ __global__ void __launch_bounds__(kQThreads, 1) quad_frame_kernel(Frame f, const
         q_load_block(sm, mb, v);
         const int n = 128 * b + m_lane;
         const int owner = n / kQOf, nl = n % kQOf;
-        float* dst = &sm.u.a.v.red[c][nl][16 * sh];
+        // the owner keeps its own partials in xa (free after the FFN1 MMAs), the
+        // peers' in red[slot], slot = the sender's rank skipping the owner's
+        float* dst = owner == c ? reinterpret_cast<float*>(sm.u.a.xa) + nl * kQR + 16 * sh
+                                : &sm.u.a.v.red[c < owner ? c : c - 1][nl][16 * sh];
         if (owner == c) {
 #pragma unroll
           for (int i = 0; i < 16; i += 4) *reinterpret_cast<float4*>(dst + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
@@ -828,10 +846,15 @@ __global__ void __launch_bounds__(kQThreads, 1) quad_frame_kernel(Frame f, const
         float xv[8];
         unpack8(*reinterpret_cast<const uint4*>(sm.xr.x + r * kQLdX + k0), xv);
 #pragma unroll
+        const float* own_part = reinterpret_cast<const float*>(sm.u.a.xa);
         for (int e = 0; e < 8; ++e) {
-          float s = sm.u.a.v.red[0][nl + e][r];
+          // the four partials in CTA order
+          float s = 0.f;
 #pragma unroll
-          for (int j = 1; j < kQC; ++j) s = __fadd_rn(s, sm.u.a.v.red[j][nl + e][r]);
+          for (int j = 0; j < kQC; ++j) {
+            const float pj = j == c ? own_part[(nl + e) * kQR + r] : sm.u.a.v.red[j < c ? j : j - 1][nl + e][r];
+            s = j == 0 ? pj : __fadd_rn(s, pj);
+          }
           xv[e] = __fadd_rn(xv[e], round_bf16(s));
         }
         const uint4 w = pack8(xv);
@@ -933,7 +956,8 @@ __global__ void __launch_bounds__(kQThreads, 1) quad_frame_kernel(Frame f, const
       }
       q_stamp(f, tracer, p, 12);
 
-      // ---------------- sampling (R6: the token to every CTA): one warp per owned session
+      // ---------------- sampling (R6: the token to every CTA): one warp per owned
+      // session (two warps per session with sample_group measured slower here)
       if (warp < n_own) {
         const int ls = warp, slot = own0 + ls;
         uint32_t nfs = sm.nf[slot];
