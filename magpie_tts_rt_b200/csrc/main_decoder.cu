@@ -692,9 +692,24 @@ constexpr int kMaxSplits = kFfn2Splits;
 // C[rows][N] = X[rows][K] W[N][K]^T on the tensor cores (K a multiple of
 // 64 x splits, N of 128); with partial != nullptr the K range is split in
 // `splits` and the f32 partial sums go to partial[split][rows][N].
+// The weight tile (N side) is the narrowest of 256 / 128 / 64 columns that
+// keeps every tile in one wave of the SMs: at 512 activation rows a 256-wide
+// tile leaves 12 of the 148 SMs to the 768 x 768 projections, each streaming
+// ~590 KB, where 64-wide tiles give 48 CTAs streaming ~290 KB each and MMAs
+// of N = 64 (~48 cycles against ~128 at N = 256).
+int gemm_weight_tile(int rows, int N, int splits) {
+  const int m_tiles = (rows + 127) / 128;
+  const int sms = gemm_grid(1 << 30);  // the device's SM count (0 when unknown)
+  int bn = N % 256 == 0 ? 256 : 128;
+  for (const int cand : {128, 64}) {
+    if (cand < bn && N % cand == 0 && m_tiles * (N / cand) * splits <= sms) bn = cand;
+  }
+  return bn;
+}
+
 bool tc_gemm(const bf16* X, const bf16* W, bf16* C, int rows, int N, int K, bool gelu, int splits, float* partial,
              cudaStream_t stream) {
-  const int bn = N % 256 == 0 ? 256 : 128;
+  const int bn = gemm_weight_tile(rows, N, partial != nullptr ? splits : 1);
   CUtensorMap amap, bmap;
   if (!cached_map(&amap, X, static_cast<uint64_t>(K), static_cast<uint64_t>(rows), 128) ||
       !cached_map(&bmap, W, static_cast<uint64_t>(K), static_cast<uint64_t>(N), static_cast<uint32_t>(bn))) {
@@ -714,10 +729,14 @@ bool tc_gemm(const bf16* X, const bf16* W, bf16* C, int rows, int N, int K, bool
   cudaError_t e;
   if (partial != nullptr) {
     EpiPartial epi{partial, N, rows, static_cast<size_t>(rows) * N};
-    e = bn == 128 ? launch_gemm_tc<128>(amap, bmap, pr, epi, stream) : launch_gemm_tc<256>(amap, bmap, pr, epi, stream);
+    e = bn == 64    ? launch_gemm_tc<64>(amap, bmap, pr, epi, stream)
+        : bn == 128 ? launch_gemm_tc<128>(amap, bmap, pr, epi, stream)
+                    : launch_gemm_tc<256>(amap, bmap, pr, epi, stream);
   } else {
     EpiRows epi{C, N, rows, gelu ? 1 : 0};
-    e = bn == 128 ? launch_gemm_tc<128>(amap, bmap, pr, epi, stream) : launch_gemm_tc<256>(amap, bmap, pr, epi, stream);
+    e = bn == 64    ? launch_gemm_tc<64>(amap, bmap, pr, epi, stream)
+        : bn == 128 ? launch_gemm_tc<128>(amap, bmap, pr, epi, stream)
+                    : launch_gemm_tc<256>(amap, bmap, pr, epi, stream);
   }
   return e == cudaSuccess;
 }
