@@ -595,6 +595,44 @@ def r_shape_measure(dev, peaks, sizes=(64, 1024), calls=10, seed=5):
     return out
 
 
+def frame_paths_measure(w, dev, peaks, sizes=(64, 256, 512, 1024), calls=20,
+                        paths=((10, "quad kernel"), (0, "AUTO"))):
+    """Frame-call time of the benchmark shape (config 4's flags at its first
+    frames: every session unfinished, CFG pair) on the quad kernel (4-CTA
+    cluster per 16 sessions, explicit path) next to the AUTO path, for the
+    sessions per GPU that config 4 puts on 8, 4, 2 and 1 GPUs and config 3's
+    64.  CUDA events on the launching stream."""
+    from magpie_tts_rt_b200.local_ar import LocalArEngine, StreamBatch
+    tensor_peak = peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"])
+    stream = torch.cuda.Stream(dev)
+    out = {"workload": "benchmark shape, CFG pair, all sessions unfinished, frame call timed alone"}
+    for n in sizes:
+        b = StreamBatch.allocate(n, device=dev)
+        g = torch.Generator().manual_seed(n)
+        b.decoder_hidden.copy_(torch.randn(n, 2, EMBED, generator=g).to(torch.bfloat16))
+        b.rng_seed.copy_(torch.arange(n))
+        b.unfinished.fill_(True)
+        row = {}
+        for path, name in paths:
+            eng = LocalArEngine(w, max_streams=n, device=dev, path=path)
+            with torch.cuda.stream(stream):
+                for _ in range(3):
+                    eng.frame(b, stream=stream)
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+                for _ in range(calls):
+                    eng.frame(b, stream=stream)
+                e1.record(stream)
+            torch.cuda.synchronize(dev)
+            t = e0.elapsed_time(e1) * 1000.0 / calls
+            tf = n * 2 * 2 * SHAPE_BASELINE.macs_per_row() / (t * 1e-6) / 1e12
+            row[name] = {"frame_path": PATH_NAMES.get(eng.path, str(eng.path)), "frame_call_us": t,
+                         "frames_per_s": n / (t * 1e-6), "tensor_frac": tf / tensor_peak,
+                         "invalid_rows": int(b.invalid_rows.count_nonzero().item())}
+        out[str(n)] = row
+    return out
+
+
 def alignment_gate_measure(dev, peaks, n=1024, stride=512, steps=200, seed=11):
     """The alignment gate (mtt_b200_launch_alignment_batch) for the config-4
     sessions of one GPU: text lengths U[64, 512], a fresh score row per step
@@ -981,11 +1019,12 @@ def main():
     loop = None
     if world == 1 and not args.no_latency and not args.no_loop:
         loop = loop_measure(torch.device("cuda", local), peaks, steps=args.loop_steps)
-    probe = eos = rshape = None
+    probe = eos = rshape = paths = None
     if world == 1 and not args.no_latency:
         probe = tensor_probe(torch.device("cuda", local))
         eos = eos_measure(res["w"], torch.device("cuda", local), peaks)
         rshape = r_shape_measure(torch.device("cuda", local), peaks)
+        paths = frame_paths_measure(res["w"], torch.device("cuda", local), peaks)
     cpu = None
     if world == 1 and rank == 0 and not args.no_cpu_baseline:
         cpu = cpu_oracle_sample()
@@ -1033,6 +1072,7 @@ def main():
                 "roofline": roof,
                 "latency_config2": latency, "alignment_gate": align, "main_decoder_step": md,
                 "config5_loop": loop, "eos_projection": eos, "tensor_probe": probe, "r_shape_frame": rshape,
+                "frame_paths": paths,
                 "cpu_baseline": cpu,
                 "checks": {"invalid_rows": res["invalid"], "forced_eos_ok": res["forced_ok"]}}
         print(json.dumps(line), flush=True)

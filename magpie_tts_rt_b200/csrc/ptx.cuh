@@ -51,37 +51,37 @@ __device__ __forceinline__ unsigned long long global_ns() {
   return t;
 }
 
-// Waits for the phase with the given parity; returns false when it did not
-// complete within limit_ns (the caller records the error and goes on, so a
-// broken pipeline costs milliseconds, never a hang).
-// One try with a suspend-time hint: a thread whose phase has not completed
-// sleeps until it completes (or the hint, 10 ms, runs out) instead of
-// spinning, so waiting warps leave their issue slots to the warps that work.
+// One try at the phase with the given parity (acquire at cluster scope: the
+// round barriers complete on peers' st.async data).
 __device__ __forceinline__ bool mbar_try(uint32_t a, uint32_t parity) {
   uint32_t done;
   asm volatile(
-      "{\n .reg .pred p;\n mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;\n"
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n"
       " selp.u32 %0, 1, 0, p;\n}\n"
       : "=r"(done)
-      : "r"(a), "r"(parity), "r"(10000000u)
+      : "r"(a), "r"(parity)
       : "memory");
   return done != 0;
 }
 
 // CTA-scope form, for barriers that only this CTA's threads, its TMA copies
-// and its tcgen05 commits complete: a cluster-scope acquire costs a few
-// hundred cycles even when the phase has long completed.
+// and its tcgen05 commits complete.
 __device__ __forceinline__ bool mbar_try_cta(uint32_t a, uint32_t parity) {
   uint32_t done;
   asm volatile(
-      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n"
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
       " selp.u32 %0, 1, 0, p;\n}\n"
       : "=r"(done)
-      : "r"(a), "r"(parity), "r"(10000000u)
+      : "r"(a), "r"(parity)
       : "memory");
   return done != 0;
 }
 
+// Waits for the phase with the given parity; returns false when it did not
+// complete within limit_ns (the caller records the error and goes on, so a
+// broken pipeline costs milliseconds, never a hang).  The global timer is
+// read only after a first unsuccessful try, so a phase that has already
+// completed costs one try.
 __device__ __forceinline__ bool mbar_wait_cta(unsigned long long* bar, uint32_t parity,
                                               unsigned long long limit_ns = 20000000ull) {
   const uint32_t a = smem_addr(bar);
@@ -93,8 +93,7 @@ __device__ __forceinline__ bool mbar_wait_cta(unsigned long long* bar, uint32_t 
   }
 }
 
-// The global timer is read only after a first unsuccessful try: a read costs
-// a few hundred cycles, which a phase that has already completed must not pay.
+// Cluster-scope form (mbar_try).
 __device__ __forceinline__ bool mbar_wait(unsigned long long* bar, uint32_t parity,
                                           unsigned long long limit_ns = 20000000ull) {
   const uint32_t a = smem_addr(bar);

@@ -69,12 +69,20 @@ def config4_flags(n, frame=60, seed=2024):
     return active, unfinished, finished, forbid
 
 
-@pytest.mark.parametrize("n", [1024, 512, 256, 128, 64])
-def test_auto_frame_at_bench_batch(n):
+QUAD = 10
+
+
+@pytest.mark.parametrize("n,path", [(1024, 0), (512, 0), (256, 0), (128, 0), (64, 0), (512, QUAD), (1024, QUAD)],
+                         ids=["1024-auto", "512-auto", "256-auto", "128-auto", "64-auto", "512-quad", "1024-quad"])
+def test_auto_frame_at_bench_batch(n, path):
+    """The AUTO path at each bench batch, and the quad kernel (explicit path)
+    at config 4's one- and two-GPU batches: one wave of 4-CTA clusters at 512
+    sessions, two waves at 1024."""
     from magpie_tts_rt_b200.local_ar import LocalArEngine
     w = bench_weights()
-    eng = LocalArEngine(w, max_streams=n)
-    tile = {2: 8, 3: 8, 4: 16, 9: 16}.get(eng.path, 8)
+    eng = LocalArEngine(w, max_streams=n, path=path)
+    assert path == 0 or eng.path == path
+    tile = {2: 8, 3: 8, 4: 16, 9: 16, QUAD: 16}.get(eng.path, 8)
     g = torch.Generator().manual_seed(1000 + n)
     hidden = torch.randn(n, 2, EMBED, generator=g).to(torch.bfloat16)
     active, uf, fi, fb = config4_flags(n)
