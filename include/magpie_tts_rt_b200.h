@@ -302,10 +302,10 @@ MTT_B200_API int mtt_b200_launch_fold_in_projection(const mtt_b200_local_ar_shap
  * streaming that fraction of every weight
  * matrix, with the GEMMs on tcgen05 tensor cores (accumulators and the KV
  * cache in tensor memory).  AUTO picks FUSED_CLUSTER while the batch's tiles
- * fit in one wave of its clusters, then SPLIT_8, _4 and _2 while theirs do
- * (fewer sessions per GPU: more CTAs per session, shorter frames), then
- * FUSED_PAIR while its 16-session tiles fit in one wave, then FUSED_TILE,
- * and the phase kernels for other shapes. */
+ * fit in one wave of its clusters, then SPLIT_8 and _4 while theirs do
+ * (fewer sessions per GPU: more CTAs per session, shorter frames), then QUAD
+ * and SPLIT_2 while theirs do, then FUSED_PAIR while its 16-session tiles fit
+ * in one wave, then FUSED_TILE, and the phase kernels for other shapes. */
 #define MTT_B200_FRAME_PATH_AUTO 0
 #define MTT_B200_FRAME_PATH_PHASE_KERNELS 1
 #define MTT_B200_FRAME_PATH_FUSED_CLUSTER 2

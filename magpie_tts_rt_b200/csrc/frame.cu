@@ -869,6 +869,10 @@ int32_t resolve_path(const mtt_b200_local_ar_shape_t* shape, const mtt_b200_samp
       if (tiles <= mtt::split_frame_clusters(4, 16) && mtt::split_frame_supported(probe, 4, 16)) {
         return MTT_B200_FRAME_PATH_SPLIT_4;
       }
+      // 16-session tiles on 4-CTA clusters while they fit in one wave
+      if ((n_streams + 15) / 16 <= mtt::quad_frame_clusters() && mtt::quad_frame_supported(probe)) {
+        return MTT_B200_FRAME_PATH_QUAD;
+      }
       if (tiles <= mtt::split_frame_clusters(2, 16) && mtt::split_frame_supported(probe, 2, 16)) {
         return MTT_B200_FRAME_PATH_SPLIT_2;
       }

@@ -83,6 +83,7 @@ constexpr int kQF1 = kQF / kQC;        // FFN features per CTA
 constexpr int kQOf = kQD / kQC;        // residual features owned per CTA (FFN2 reduction)
 constexpr int kQVs = 512;              // vocabulary slice per CTA
 constexpr int kQSlots = 8;             // weight ring slots
+constexpr int kQGroups = kQSlots / 4;  // ring groups of 4 chunks (one M-block's K = 256), one barrier pair each
 constexpr int kQNbuf = 8;              // accumulator buffers
 constexpr int kQChunkK = 64;
 constexpr int kQChunkElems = 128 * kQChunkK;            // 16 KB
@@ -149,14 +150,14 @@ struct __align__(1024) QuadSmem {
   int64_t ctr[kQOwn];
   int64_t seed[kQOwn];
   int32_t inv[kQOwn];
-  int32_t last_issued[kQSlots];
+  int32_t last_issued[kQGroups];
   int32_t n_sess;
   int32_t err;
   int32_t producer_done;
   int32_t mma_done;
   uint32_t tmem;
-  unsigned long long full[kQSlots];
-  unsigned long long empty[kQSlots];
+  unsigned long long full[kQGroups];
+  unsigned long long empty[kQGroups];
   unsigned long long dfull[kQNbuf];
   unsigned long long dempty[kQNbuf];
   unsigned long long opready;
@@ -229,23 +230,31 @@ __device__ __forceinline__ const CUtensorMap* q_chunk(const QuadMaps& m, int c, 
   }
 }
 
+// The producer fills the ring a group of 4 chunks (an M-block's K = 256) at a
+// time, all four landing on the group's one barrier.
 __device__ void q_producer(QuadSmem& sm, const QuadMaps& maps, int c, bool folded) {
-  int it = 0;
+  int git = 0;  // groups issued
   for (int p = 0; p < kPositions; ++p) {
     for (int g = q_has_in(folded, p) ? Q_IN : Q_QKV; g <= Q_HEAD; ++g) {
-      const int nb = q_blocks(g), nk = q_kchunks(g);
+      const int nb = q_blocks(g), ng = q_kchunks(g) / 4;
       for (int b = 0; b < nb; ++b) {
-        for (int k = 0; k < nk; ++k, ++it) {
-          const int slot = it % kQSlots;
-          if (it >= kQSlots && qerr(sm) == 0 && !mbar_wait_cta(&sm.empty[slot], ((it / kQSlots) - 1) & 1)) sm.err = 1;
+        for (int gr = 0; gr < ng; ++gr, ++git) {
+          const int gi = git % kQGroups;
+          if (git >= kQGroups && qerr(sm) == 0 && !mbar_wait_cta(&sm.empty[gi], ((git / kQGroups) - 1) & 1)) {
+            sm.err = 1;
+          }
           if (qerr(sm)) return;
           int x0, ra, rb;
-          const CUtensorMap* map = q_chunk(maps, c, p, g, b, k, &x0, &ra, &rb);
-          mbar_expect_tx(&sm.full[slot], rb < 0 ? kQChunkBytes / 2 : kQChunkBytes);
-          bf16* dst = sm.ring[slot];
-          tma_load_2d(dst, map, x0, ra, &sm.full[slot]);
-          if (rb >= 0) tma_load_2d(dst + kQBoxRows * 64, map, x0, rb, &sm.full[slot]);
-          sm.last_issued[slot] = it;
+          q_chunk(maps, c, p, g, b, 4 * gr, &x0, &ra, &rb);
+          mbar_expect_tx(&sm.full[gi], 4 * (rb < 0 ? kQChunkBytes / 2 : kQChunkBytes));
+#pragma unroll 1
+          for (int k = 0; k < 4; ++k) {
+            const CUtensorMap* map = q_chunk(maps, c, p, g, b, 4 * gr + k, &x0, &ra, &rb);
+            bf16* dst = sm.ring[4 * gi + k];
+            tma_load_2d(dst, map, x0, ra, &sm.full[gi]);
+            if (rb >= 0) tma_load_2d(dst + kQBoxRows * 64, map, x0, rb, &sm.full[gi]);
+          }
+          sm.last_issued[gi] = git;
         }
       }
     }
@@ -265,13 +274,13 @@ __device__ __forceinline__ const bf16* q_operand(QuadSmem& sm, int g) {
 
 // The MMA warp's single thread: per GEMM wait until the consumers have
 // written its B operand; per M-block wait for a free accumulator buffer; per
-// group of 4 weight chunks (K = 256) wait for all four, then issue the 16
-// MMAs as one straight-line burst (a branch between tcgen05.mma instructions
-// halves their issue rate) and free the four slots.  The ring is consumed in
-// order by this one thread, so every parity wait is for the phase right
-// after the one it last saw complete.
+// ring group (4 weight chunks, K = 256) wait on the group's barrier, then
+// issue the 16 MMAs as one straight-line burst (a branch between tcgen05.mma
+// instructions halves their issue rate) and free the group.  The ring is
+// consumed in order by this one thread, so every parity wait is for the
+// phase right after the one it last saw complete.
 __device__ void q_mma(QuadSmem& sm, bool folded) {
-  int it = 0, mb = 0, gn = 0;
+  int git = 0, mb = 0, gn = 0;
   for (int p = 0; p < kPositions && qerr(sm) == 0; ++p) {
     for (int g = q_has_in(folded, p) ? Q_IN : Q_QKV; g <= Q_HEAD && qerr(sm) == 0; ++g) {
       if (!mbar_wait_cta(&sm.opready, gn & 1)) {
@@ -287,29 +296,24 @@ __device__ void q_mma(QuadSmem& sm, bool folded) {
         const int db = mb % kQNbuf, use = mb / kQNbuf;
         ok = use < 1 || mbar_wait_cta(&sm.dempty[db], (use - 1) & 1);
         const uint32_t d = sm.tmem + kQAcc0 + 32u * static_cast<uint32_t>(db);
-        for (int gr = 0; gr < ng && ok; ++gr, it += 4) {
-          int slot[4];
-#pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            slot[k] = (it + k) % kQSlots;
-            ok = ok && mbar_wait_cta(&sm.full[slot[k]], ((it + k) / kQSlots) & 1);
-          }
+        for (int gr = 0; gr < ng && ok; ++gr, ++git) {
+          const int gi = git % kQGroups;
+          ok = mbar_wait_cta(&sm.full[gi], (git / kQGroups) & 1);
           if (!ok) break;
           tmem_fence_after_sync();
           const uint64_t b0 = umma_desc_sw128(bop + 4 * gr * kQPanel);
-          const uint64_t a0[4] = {umma_desc_sw128(sm.ring[slot[0]]), umma_desc_sw128(sm.ring[slot[1]]),
-                                  umma_desc_sw128(sm.ring[slot[2]]), umma_desc_sw128(sm.ring[slot[3]])};
+          const uint64_t a0 = umma_desc_sw128(sm.ring[4 * gi]);
+          constexpr uint64_t kSlotStep = kQChunkElems * 2 / 16, kPanelStep = kQPanel * 2 / 16;
           const bool acc0 = gr != 0;
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk) {
-              umma_bf16(d, a0[k] + 2 * kk, b0 + static_cast<uint64_t>(k * (kQPanel * 2 / 16)) + 2 * kk, kQIdesc,
+              umma_bf16(d, a0 + k * kSlotStep + 2 * kk, b0 + k * kPanelStep + 2 * kk, kQIdesc,
                         acc0 || (k | kk) != 0);
             }
           }
-#pragma unroll
-          for (int k = 0; k < 4; ++k) umma_commit(&sm.empty[slot[k]]);
+          umma_commit(&sm.empty[gi]);
         }
         if (!ok) break;
         umma_commit(&sm.dfull[db]);
@@ -354,13 +358,14 @@ __device__ __forceinline__ void q_operand_ready(QuadSmem& sm) {
 
 // LayerNorm (no bias, eps 1e-5) of the 32 rows of x into the B operand xa;
 // lane holds weights g of columns [8 lane, +8); warp w: rows [4 w, +4).
-__device__ __forceinline__ void q_layer_norm(const bf16* x, bf16* xa, const float (&g)[8]) {
+// LayerNorm (no bias, eps 1e-5) of the warp's rows [4 w, +4), held by lane
+// as columns [8 lane, +8) in v, into the B operand xa (lane holds weights g).
+__device__ __forceinline__ void q_layer_norm_rows(float (&v)[kQR / kQW][8], bf16* xa, const float (&g)[8]) {
   constexpr int kRows = kQR / kQW;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  float v[kRows][8], sum[kRows], var[kRows];
+  float sum[kRows], var[kRows];
 #pragma unroll
   for (int rr = 0; rr < kRows; ++rr) {
-    unpack8(*reinterpret_cast<const uint4*>(x + (kRows * warp + rr) * kQLdX + lane * 8), v[rr]);
     sum[rr] = 0.f;
 #pragma unroll
     for (int j = 0; j < 8; ++j) sum[rr] += v[rr][j];
@@ -392,6 +397,16 @@ __device__ __forceinline__ void q_layer_norm(const bf16* x, bf16* xa, const floa
     for (int j = 0; j < 8; ++j) out[j] = ((v[rr][j] - mean) * rstd) * g[j];
     *qop_unit(xa, kRows * warp + rr, lane * 8) = pack8(out);
   }
+}
+
+// LayerNorm of the 32 rows of x (row-major) into xa; warp w: rows [4 w, +4).
+__device__ __forceinline__ void q_layer_norm(const bf16* x, bf16* xa, const float (&g)[8]) {
+  constexpr int kRows = kQR / kQW;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  float v[kRows][8];
+#pragma unroll
+  for (int rr = 0; rr < kRows; ++rr) unpack8(*reinterpret_cast<const uint4*>(x + (kRows * warp + rr) * kQLdX + lane * 8), v[rr]);
+  q_layer_norm_rows(v, xa, g);
 }
 
 // Wait for round rd: this CTA announces on its own round barrier the bytes
@@ -614,7 +629,7 @@ __global__ void __launch_bounds__(kQThreads, 1) quad_frame_kernel(Frame f, const
   if (tracer) f.trace[256] = static_cast<uint64_t>(clock64()), f.trace[257] = global_ns();
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kQSlots; ++s) {
+    for (int s = 0; s < kQGroups; ++s) {
       mbar_init(&sm.full[s], 1);
       mbar_init(&sm.empty[s], 1);
       sm.last_issued[s] = -1;
@@ -668,9 +683,9 @@ __global__ void __launch_bounds__(kQThreads, 1) quad_frame_kernel(Frame f, const
     if (warp == kQW && lane == 0) {
       q_producer(sm, maps, c, folded);
       // no copy may still be writing when the CTA leaves
-      for (int s = 0; s < kQSlots; ++s) {
+      for (int s = 0; s < kQGroups; ++s) {
         const int last = sm.last_issued[s];
-        if (last >= 0) mbar_wait_cta(&sm.full[s], (last / kQSlots) & 1);
+        if (last >= 0) mbar_wait_cta(&sm.full[s], (last / kQGroups) & 1);
       }
       atomicExch(&sm.producer_done, 1);
     } else if (warp == kQW + 1 && lane == 0) {
@@ -745,10 +760,13 @@ __global__ void __launch_bounds__(kQThreads, 1) quad_frame_kernel(Frame f, const
         }
       }
       if (threadIdx.x < kQS) sm.nf[threadIdx.x] = 0;
-      qbar();
 
-      // ---------------- LN1, q|k|v of head c
-      q_layer_norm(sm.xr.x, sm.u.a.xa, g1);
+      // ---------------- LN1 (with the folded tables done by the previous
+      // position's row gather), q|k|v of head c
+      if (q_has_in(folded, p)) {
+        qbar();
+        q_layer_norm(sm.xr.x, sm.u.a.xa, g1);
+      }
       q_operand_ready(sm);
       q_stamp(f, tracer, p, 1);
       for (int b = 0; b < 2; ++b, ++mb) {
@@ -846,15 +864,18 @@ __global__ void __launch_bounds__(kQThreads, 1) quad_frame_kernel(Frame f, const
         float xv[8];
         unpack8(*reinterpret_cast<const uint4*>(sm.xr.x + r * kQLdX + k0), xv);
 #pragma unroll
-        const float* own_part = reinterpret_cast<const float*>(sm.u.a.xa);
-        for (int e = 0; e < 8; ++e) {
-          // the four partials in CTA order
-          float s = 0.f;
+        // the four partials in CTA order: this CTA's own in xa, the peers' in red
+        const float* src[kQC];
 #pragma unroll
-          for (int j = 0; j < kQC; ++j) {
-            const float pj = j == c ? own_part[(nl + e) * kQR + r] : sm.u.a.v.red[j < c ? j : j - 1][nl + e][r];
-            s = j == 0 ? pj : __fadd_rn(s, pj);
-          }
+        for (int j = 0; j < kQC; ++j) {
+          src[j] = (j == c ? reinterpret_cast<const float*>(sm.u.a.xa) : &sm.u.a.v.red[j < c ? j : j - 1][0][0]) +
+                   nl * kQR + r;
+        }
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          float s = src[0][e * kQR];
+#pragma unroll
+          for (int j = 1; j < kQC; ++j) s = __fadd_rn(s, src[j][e * kQR]);
           xv[e] = __fadd_rn(xv[e], round_bf16(s));
         }
         const uint4 w = pack8(xv);
@@ -1009,25 +1030,39 @@ __global__ void __launch_bounds__(kQThreads, 1) quad_frame_kernel(Frame f, const
       }
       q_stamp(f, tracer, p, 14);
 
-      // ---------------- next input rows (folded tables), every CTA, all rows
+      // ---------------- next input rows (folded tables), every CTA, all rows,
+      // and their LN1 for the next position's q|k|v (warp w: rows [4 w, +4))
       if (folded && p + 1 < kPositions) {
-        for (int r = warp; r < kQR; r += kQW) {
-          const int slot = r >> 1;
+        constexpr int kRows = kQR / kQW;
+        float v[kRows][8];
+        uint4 ev[kRows];
+#pragma unroll
+        for (int rr = 0; rr < kRows; ++rr) {
+          const int r = kRows * warp + rr;
+          ev[rr] = make_uint4(0, 0, 0, 0);
+          if (live(r)) {
+            const int64_t tin = q_input_token(f, sm, r >> 1, p);
+            ev[rr] = *reinterpret_cast<const uint4*>(f.emb_proj + (static_cast<int64_t>(p) * kVocab + tin) * kQD +
+                                                     lane * 8);
+          }
+        }
+        float p8[8];
+        unpack8(*reinterpret_cast<const uint4*>(f.pos + static_cast<int64_t>(p + 1) * kQD + lane * 8), p8);
+#pragma unroll
+        for (int rr = 0; rr < kRows; ++rr) {
+          const int r = kRows * warp + rr;
           uint4 row = make_uint4(0, 0, 0, 0);
           if (live(r)) {
-            const int64_t tin = q_input_token(f, sm, slot, p);
-            float e8[8], p8[8];
-            unpack8(*reinterpret_cast<const uint4*>(f.emb_proj + (static_cast<int64_t>(p) * kVocab + tin) * kQD +
-                                                    lane * 8),
-                    e8);
-            unpack8(*reinterpret_cast<const uint4*>(f.pos + static_cast<int64_t>(p + 1) * kQD + lane * 8), p8);
-            float y[8];
+            float e8[8], y[8];
+            unpack8(ev[rr], e8);
 #pragma unroll
             for (int e = 0; e < 8; ++e) y[e] = __fadd_rn(e8[e], p8[e]);
             row = pack8(y);
           }
           *reinterpret_cast<uint4*>(sm.xr.x + r * kQLdX + lane * 8) = row;
+          unpack8(row, v[rr]);
         }
+        q_layer_norm_rows(v, sm.u.a.xa, g1);
       }
       qbar();
       q_stamp(f, tracer, p, 15);

@@ -189,10 +189,11 @@ def test_frame_matches_oracle(engines, shape, n, path, fold):
 
 def test_auto_path_for_the_benchmark_shape(engines):
     """One wave of 16-CTA clusters: the cluster kernel (latency); then the
-    split kernel with the widest cluster whose tiles fit in one wave (8, 4,
-    then 2 CTAs per 8 sessions); the pair kernel while its 16-session tiles
-    fit in one wave; the tile kernel for the largest batches; other shapes:
-    phase kernels."""
+    split kernel with the widest cluster whose tiles fit in one wave (8, then
+    4 CTAs per 8 sessions); the quad kernel while its 16-session tiles fit in
+    one wave of 4-CTA clusters; split x2; the pair kernel while its
+    16-session tiles fit in one wave; the tile kernel for the largest
+    batches; other shapes: phase kernels."""
     from magpie_tts_rt_b200 import _lib as L
     eng = engines(SHAPE_BASELINE, 21, 16)
     assert eng.path == FUSED
@@ -207,7 +208,11 @@ def test_auto_path_for_the_benchmark_shape(engines):
     assert eng.path_for(8 * c8) == SPLIT8
     assert eng.path_for(8 * c8 + 1) == SPLIT4
     assert eng.path_for(8 * c4) == SPLIT4
-    assert eng.path_for(8 * c4 + 1) == SPLIT2
+    cq = L.lib.mtt_b200_local_ar_frame_path_clusters(QUAD)
+    assert 8 * c4 < 16 * cq < 8 * c2
+    assert eng.path_for(8 * c4 + 1) == QUAD
+    assert eng.path_for(16 * cq) == QUAD
+    assert eng.path_for(16 * cq + 1) == SPLIT2
     assert eng.path_for(8 * c2) == SPLIT2
     cp = L.lib.mtt_b200_local_ar_frame_path_clusters(PAIR)
     assert 8 * c2 < 16 * cp
