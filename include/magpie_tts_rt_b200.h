@@ -732,14 +732,18 @@ MTT_B200_API int mtt_b200_test_dsmem_cycles(int32_t bytes_per_peer, int32_t roun
                                             uint64_t* cycles, void* stream);
 
 /* Trace hook: while `stamps` is non-null, every frame launched on the fused
- * cluster path records, from CTA 0 of its first cluster, the SM clock at 16
- * points of each position into stamps[16 * p + i] (i: 0 position start;
- * 1 x ready; 2 q|k|v and partial scores; 3 their round; 4 attention; 5 its
- * round; 6 o-projection; 7 its round; 8 LN2 + FFN1; 9 FFN2 partials; 10 their
- * round; 11 FFN2 sum round; 12 head; 13 logits round; 14 sampling; 15 token
- * round), then stamps[256..259] = clock and global timer (ns) at the frame's
- * start and end.  `stamps` is a device buffer of 260 entries; null turns the
- * hook off.  Process-wide; for measurement only. */
+ * cluster path or the quad path records, from CTA 0 of its first cluster,
+ * the SM clock at 16 points of each position into stamps[16 * p + i], then
+ * stamps[256..259] = clock and global timer (ns) at the frame's start and end.
+ * Fused cluster path, i: 0 position start; 1 x ready; 2 q|k|v and partial
+ * scores; 3 their round; 4 attention; 5 its round; 6 o-projection; 7 its
+ * round; 8 LN2 + FFN1; 9 FFN2 partials; 10 their round; 11 FFN2 sum round;
+ * 12 head; 13 logits round; 14 sampling; 15 token round.  Quad path, i:
+ * 0 position start; 1 LN1 rows ready; 2 q|k|v; 3 attention; 4 its round;
+ * 5 o-projection and its round; 6 LN2; 7 FFN1; 8 FFN2 partials sent; 9 their
+ * round; 10 x'' and its round; 11 head; 12 values round; 13 sampling;
+ * 14 token round; 15 next rows and their LN1.  `stamps` is a device buffer of
+ * 260 entries; null turns the hook off.  Process-wide; for measurement only. */
 MTT_B200_API int mtt_b200_test_frame_trace(uint64_t* stamps);
 
 MTT_B200_API int mtt_b200_launch_test_gemm(const void* x_bf16, const void* w_bf16, void* y_bf16, int32_t rows,

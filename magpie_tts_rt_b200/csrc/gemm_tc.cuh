@@ -4,10 +4,12 @@
 //
 // A = a weight matrix [M][K] (PyTorch [out][in] layout, K contiguous), B =
 // activation rows [N][K] (K contiguous), f32 accumulation in tensor memory.
-// The weight rows are the MMA's M side (128 per tile) and the activation
-// rows its N side (BN = 64, 128 or 256 per tile): a tcgen05.mma of
-// M = 128, K = 16 costs the same ~150 SM cycles for every N up to 256
-// (measured on B200), so the row tile is as wide as the batch allows.
+// One operand is the MMA's M side (128 rows per tile) and the other its N
+// side (BN = 64, 128 or 256 per tile).  On B200 a tcgen05.mma of M = 128,
+// K = 16 issued back to back costs about 47 SM cycles for N <= 64 and N / 2
+// from N = 128 (the dense peak), so BN = 64 and 128 tiles run at about the
+// same time per instruction: callers pick the narrowest BN that keeps the
+// grid in one wave when few tiles would otherwise occupy few SMs.
 //
 // One CTA per SM walks the tiles (m, n, k-split) with a stride of the grid,
 // n fastest so that CTAs running at the same time share the weight tile in
