@@ -57,7 +57,7 @@ from magpie_tts_rt_b200.model import EMBED, SHAPE_BASELINE, SHAPE_SOFIA, make_we
 METRIC = "Local-AR+sampling frames/sec per GPU and box (1/2/4/8); p50 per-frame us"
 PATH_NAMES = {1: "phase kernels", 2: "fused cluster kernel", 3: "tile kernel", 4: "pair kernel",
               5: "split kernel x1", 6: "split kernel x2", 7: "split kernel x4", 8: "split kernel x8",
-              9: "split kernel x2, 32-row tiles", 10: "quad kernel"}
+              9: "split kernel x2, 32-row tiles", 10: "quad kernel", 11: "octo kernel"}
 # DRAM bytes per launch of the frame kernel, measured by ncu (path, sessions per GPU)
 TRAFFIC = {("tile kernel", 1024): 27.64e6, ("pair kernel", 1024): 27.70e6, ("split kernel x4", 256): 23.13e6,
            ("split kernel x8", 64): 20.58e6, ("fused cluster kernel", 1): 18.76e6}

@@ -320,6 +320,11 @@ MTT_B200_API int mtt_b200_launch_fold_in_projection(const mtt_b200_local_ar_shap
  * (its key/value cache in tensor memory), each CTA streaming a quarter of
  * FFN and head weights, tcgen05 GEMMs on 32-row tiles (benchmark shape). */
 #define MTT_B200_FRAME_PATH_QUAD 10
+/* OCTO: 16 sessions (32 rows) on an 8-CTA cluster, two CTAs per attention
+ * head, each CTA streaming an eighth of the FFN and head weights (benchmark
+ * shape); for batches whose 8-session tiles outnumber the 8-CTA clusters
+ * that fit at once. */
+#define MTT_B200_FRAME_PATH_OCTO 11
 
 /* Sampling configuration; the reference's values are 80 / 0.6 / 2.5 with CFG
  * and top-k.  argmax != 0 selects greedy decoding (no RNG, counter unchanged;

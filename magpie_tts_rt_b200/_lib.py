@@ -107,6 +107,7 @@ PATH_SPLIT_4 = 7
 PATH_SPLIT_8 = 8
 PATH_SPLIT_2X32 = 9
 PATH_QUAD = 10
+PATH_OCTO = 11
 
 
 class StreamBatch(ctypes.Structure):

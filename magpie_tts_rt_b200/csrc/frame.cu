@@ -899,6 +899,8 @@ int32_t resolve_path(const mtt_b200_local_ar_shape_t* shape, const mtt_b200_samp
                  : MTT_B200_STATUS_UNSUPPORTED;
     case MTT_B200_FRAME_PATH_QUAD:
       return mtt::quad_frame_supported(probe) ? MTT_B200_FRAME_PATH_QUAD : MTT_B200_STATUS_UNSUPPORTED;
+    case MTT_B200_FRAME_PATH_OCTO:
+      return mtt::octo_frame_supported(probe) ? MTT_B200_FRAME_PATH_OCTO : MTT_B200_STATUS_UNSUPPORTED;
     default:
       return MTT_B200_STATUS_INVALID_ARGUMENT;
   }
@@ -929,6 +931,7 @@ extern "C" MTT_B200_API int32_t mtt_b200_local_ar_frame_path_clusters(int32_t pa
     case MTT_B200_FRAME_PATH_SPLIT_8:
     case MTT_B200_FRAME_PATH_SPLIT_2X32: return mtt::split_frame_clusters(split_of_path(path), rows_of_path(path));
     case MTT_B200_FRAME_PATH_QUAD: return mtt::quad_frame_clusters();
+    case MTT_B200_FRAME_PATH_OCTO: return mtt::octo_frame_clusters();
     default: return 0;
   }
 }
@@ -939,7 +942,8 @@ extern "C" MTT_B200_API int32_t mtt_b200_local_ar_frame_launch_count(const mtt_b
   if (!mtt::shape_ok(shape) || sampling == nullptr || n_streams <= 0) return 0;
   const int32_t path = resolve_path(shape, sampling, n_streams);
   if (path == MTT_B200_FRAME_PATH_FUSED_CLUSTER || path == MTT_B200_FRAME_PATH_FUSED_TILE ||
-      path == MTT_B200_FRAME_PATH_FUSED_PAIR || path == MTT_B200_FRAME_PATH_QUAD || is_split_path(path)) {
+      path == MTT_B200_FRAME_PATH_FUSED_PAIR || path == MTT_B200_FRAME_PATH_QUAD || path == MTT_B200_FRAME_PATH_OCTO ||
+      is_split_path(path)) {
     return 3;  // fused frame, EOS projection, EOS finish
   }
   if (path != MTT_B200_FRAME_PATH_PHASE_KERNELS) return 0;
@@ -1068,6 +1072,9 @@ extern "C" MTT_B200_API int mtt_b200_launch_local_ar_frame(const mtt_b200_local_
   }
   if (path == MTT_B200_FRAME_PATH_QUAD) {
     return launch_quad_frame(f, st) == cudaSuccess ? MTT_B200_STATUS_OK : MTT_B200_STATUS_CUDA_ERROR;
+  }
+  if (path == MTT_B200_FRAME_PATH_OCTO) {
+    return launch_octo_frame(f, st) == cudaSuccess ? MTT_B200_STATUS_OK : MTT_B200_STATUS_CUDA_ERROR;
   }
   if (is_split_path(path)) {
     return launch_split_frame(f, split_of_path(path), rows_of_path(path), st) == cudaSuccess

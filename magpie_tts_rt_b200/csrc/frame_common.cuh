@@ -162,6 +162,12 @@ cudaError_t launch_split_frame(const Frame& f, int split, int rows, cudaStream_t
 bool quad_frame_supported(const Frame& f);
 int quad_frame_clusters();
 cudaError_t launch_quad_frame(const Frame& f, cudaStream_t stream);
+// Octo kernel (frame_quad.cu): the same 16-session tile on an 8-CTA cluster,
+// two CTAs per attention head, each streaming an eighth of the FFN and head
+// weights.
+bool octo_frame_supported(const Frame& f);
+int octo_frame_clusters();
+cudaError_t launch_octo_frame(const Frame& f, cudaStream_t stream);
 
 // EOS projection (tcgen05 GEMM, eos_proj.cuh) + decision for the sessions a
 // frame kernel registered in eos_list / eos_count.

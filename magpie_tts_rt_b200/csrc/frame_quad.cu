@@ -67,10 +67,8 @@ namespace cg = cooperative_groups;
 namespace mtt {
 namespace {
 
-constexpr int kQC = 4;                 // CTAs per cluster (one head each)
 constexpr int kQR = 32;                // tile rows
 constexpr int kQS = 16;                // session slots per tile
-constexpr int kQOwn = kQS / kQC;       // sessions sampled per CTA
 constexpr int kQW = 8;                 // consumer warps
 constexpr int kQT = kQW * 32;          // consumer threads
 constexpr int kQThreads = kQT + 128;   // + the control warpgroup (producer warp, MMA warp)
@@ -79,9 +77,6 @@ constexpr int kQConsumerRegs = 232;
 static_assert(128 * kQProducerRegs + kQT * kQConsumerRegs <= kQThreads * 168, "register split");
 constexpr int kQD = 256;
 constexpr int kQF = 1024;
-constexpr int kQF1 = kQF / kQC;        // FFN features per CTA
-constexpr int kQOf = kQD / kQC;        // residual features owned per CTA (FFN2 reduction)
-constexpr int kQVs = 512;              // vocabulary slice per CTA
 constexpr int kQSlots = 8;             // weight ring slots
 constexpr int kQGroups = kQSlots / 4;  // ring groups of 4 chunks (one M-block's K = 256), one barrier pair each
 constexpr int kQNbuf = 8;              // accumulator buffers
@@ -94,6 +89,19 @@ constexpr int kQLdX = kQD + 8;
 constexpr int kQLdQkv = 3 * kHeadDim + 8;
 constexpr uint32_t kQIdesc = umma_idesc_bf16(128, kQR);
 constexpr uint32_t kQAcc0 = 256;  // first accumulator column
+
+// What one CTA of a C-CTA cluster (C = 4: quad kernel, C = 8: octo kernel) owns.
+template <int C>
+struct QK {
+  static_assert(C == 4 || C == 8, "4- or 8-CTA clusters");
+  static constexpr int kOwn = kQS / C;   // sessions sampled per CTA
+  static constexpr int kF1 = kQF / C;    // FFN features per CTA (FFN2 K per CTA)
+  static constexpr int kOf = kQD / C;    // residual features owned per CTA (o-projection, FFN2 reduction)
+  static constexpr int kVs = 2048 / C;   // vocabulary slice per CTA
+  static constexpr int kPerHead = C / 4; // CTAs computing one attention head
+  // attention head of CTA c; with two CTAs per head each sends the peers its half of the rows
+  __host__ __device__ static constexpr int head(int c) { return c / kPerHead; }
+};
 
 enum QGemm { Q_IN = 0, Q_QKV, Q_O, Q_F1, Q_F2, Q_HEAD };
 
@@ -114,7 +122,9 @@ struct QuadAttn {
   float m[2][128];
 };
 
+template <int C>
 union QuadWork {
+  using K = QK<C>;
   bf16 src[12 * kQPanel];  // in-projection input rows (B operand, K = 768)
   struct {
     union {
@@ -125,31 +135,33 @@ union QuadWork {
       QuadAttn att;  // between the q|k|v MMAs and LN2 / FFN1
     };
     union V {
-      bf16 qkv[kQR * kQLdQkv];     // q | k | v of head c
-      float red[kQC - 1][kQOf][kQR];  // FFN2 partial sums of the owned features from the peers (sender order)
-      uint16_t vals[kQOwn][2048];  // constrained values of the owned sessions
+      bf16 qkv[kQR * kQLdQkv];     // q | k | v of the CTA's head
+      float red[C - 1][K::kOf][kQR];  // FFN2 partial sums of the owned features from the peers (sender order)
+      uint16_t vals[K::kOwn][2048];  // constrained values of the owned sessions
     } v;
   } a;
 };
 
+template <int C>
 struct __align__(1024) QuadSmem {
+  using K = QK<C>;
   bf16 ring[kQSlots][kQChunkElems];  // weight chunks (1024-byte aligned)
   bf16 ab[4 * kQPanel];              // attention output, then x'' (B operands; peers push into it)
-  QuadWork u;
+  QuadWork<C> u;
   union X {
     bf16 x[kQR * kQLdX];                       // residual stream (row-major)
-    uint16_t stage[kQS][kQVs];                 // head values of the other CTAs' sessions, before sending
-    uint16_t lists[kQOwn][2 * kListCap + 16];  // sampler scratch (one warp per owned session)
+    uint16_t stage[kQS][K::kVs];                 // head values of the other CTAs' sessions, before sending
+    uint16_t lists[K::kOwn][2 * kListCap + 16];  // sampler scratch (one warp per owned session)
   } xr;
-  __align__(16) bf16 hb[2][kQVs];  // head bias of positions p (p % 2) and p + 1, this CTA's vocabulary slice
+  __align__(16) bf16 hb[2][K::kVs];  // head bias of positions p (p % 2) and p + 1, this CTA's vocabulary slice
   int32_t tok[kQS][kPositions];
   int32_t sess[kQS];
   uint32_t flags[kQS];                  // bit 0 unfinished, bit 1 finished, bit 2 forbid_eos
   uint32_t nf[kQS];                     // non-finite guided logit in this CTA's slice, per session
-  uint32_t peer_nf[kQC][kQOwn];         // from each peer: its non-finite flag of each owned session
-  int64_t ctr[kQOwn];
-  int64_t seed[kQOwn];
-  int32_t inv[kQOwn];
+  uint32_t peer_nf[C][K::kOwn];         // from each peer: its non-finite flag of each owned session
+  int64_t ctr[K::kOwn];
+  int64_t seed[K::kOwn];
+  int32_t inv[K::kOwn];
   int32_t last_issued[kQGroups];
   int32_t n_sess;
   int32_t err;
@@ -163,13 +175,17 @@ struct __align__(1024) QuadSmem {
   unsigned long long opready;
   unsigned long long mmafin;
   unsigned long long xbar[2];
+  uint32_t r1_sink;  // the head partner's attention-round word (never read)
 };
 
-constexpr size_t kQuadSmemBytes = sizeof(QuadSmem) + 1024;
-static_assert(kQuadSmemBytes <= 232448, "quad kernel shared memory");
-static_assert(sizeof(QuadSmem::X) >= sizeof(uint16_t) * kQS * kQVs, "staging");
+template <int C>
+constexpr size_t quad_smem_bytes() { return sizeof(QuadSmem<C>) + 1024; }
+static_assert(quad_smem_bytes<4>() <= 232448 && quad_smem_bytes<8>() <= 232448, "quad / octo kernel shared memory");
+static_assert(sizeof(QuadSmem<4>::X) >= sizeof(uint16_t) * kQS * QK<4>::kVs, "staging");
+static_assert(sizeof(QuadSmem<8>::X) >= sizeof(uint16_t) * kQS * QK<8>::kVs, "staging");
 
-__device__ __forceinline__ int qerr(const QuadSmem& sm) { return *reinterpret_cast<const volatile int*>(&sm.err); }
+template <int C>
+__device__ __forceinline__ int qerr(const QuadSmem<C>& sm) { return *reinterpret_cast<const volatile int*>(&sm.err); }
 __device__ __forceinline__ void qbar() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
 
 // Byte offset of element (row r, column k) of a 32-row operand stored as
@@ -189,40 +205,73 @@ __device__ __forceinline__ void qop_store(bf16* base, int r, int k, bf16 v) {
 // ---------------------------------------------------------------------------
 
 __device__ __forceinline__ bool q_has_in(bool folded, int p) { return p == 0 || !folded; }
-__device__ __forceinline__ int q_blocks(int g) { return g == Q_HEAD ? 4 : (g == Q_O ? 1 : 2); }
-__device__ __forceinline__ int q_kchunks(int g) { return g == Q_IN ? kEmbed / kQChunkK : 4; }
+// M-blocks (128 weight rows each) of GEMM g, and K chunks (64 columns) per M-block.
+template <int C>
+__device__ __forceinline__ int q_blocks(int g) {
+  using K = QK<C>;
+  switch (g) {
+    case Q_O: return 1;
+    case Q_F1: return K::kF1 / 128;
+    case Q_HEAD: return K::kVs / 128;
+    default: return 2;  // in-projection, q|k|v, FFN2
+  }
+}
+template <int C>
+__device__ __forceinline__ int q_kchunks(int g) {
+  return g == Q_IN ? kEmbed / kQChunkK : (g == Q_F2 ? QK<C>::kF1 / kQChunkK : 4);
+}
+// Ring groups of GEMM g, 4 chunks each: one M-block's K = 256 (three groups
+// for K = 768); with 8 CTAs FFN2's two M-blocks have K = 128 and share one.
+template <int C>
+__device__ __forceinline__ int q_groups(int g) { return q_blocks<C>(g) * q_kchunks<C>(g) / 4; }
+// Chunk k (0..3) of ring group gr of GEMM g: its M-block b and K chunk kc.
+template <int C>
+__device__ __forceinline__ void q_group_chunk(int g, int gr, int k, int* b, int* kc) {
+  const int per_block = q_kchunks<C>(g);
+  if (per_block >= 4) {
+    *b = gr / (per_block / 4);
+    *kc = 4 * (gr % (per_block / 4)) + k;
+  } else {
+    *b = 2 * gr + k / 2;
+    *kc = k % 2;
+  }
+}
 
 // Tensor map and origins of chunk (M-block b, K-chunk k) of GEMM g: K column
 // x0, rows ra (A rows 0..63) and rb (A rows 64..127); rb < 0 when the block
 // has 64 weight rows only (A rows 64..127 keep stale weights, and the
 // epilogue ignores their lanes).
+template <int C>
 __device__ __forceinline__ const CUtensorMap* q_chunk(const QuadMaps& m, int c, int p, int g, int b, int k, int* x0,
                                                       int* ra, int* rb) {
+  using K = QK<C>;
+  const int h = K::head(c);
   *x0 = kQChunkK * k;
   switch (g) {
     case Q_IN:
       *ra = 128 * b;
       *rb = 128 * b + 64;
       return &m.in_proj;
-    case Q_QKV:  // block 0: head c's q and k rows; block 1: its v rows
-      *ra = b == 0 ? kHeadDim * c : 2 * kQD + kHeadDim * c;
-      *rb = b == 0 ? kQD + kHeadDim * c : -1;
+    case Q_QKV:  // block 0: head h's q and k rows; block 1: its v rows
+      *ra = b == 0 ? kHeadDim * h : 2 * kQD + kHeadDim * h;
+      *rb = b == 0 ? kQD + kHeadDim * h : -1;
       return &m.qkv;
-    case Q_O:  // output features [64 c, +64)
-      *ra = kQOf * c;
+    case Q_O:  // output features [kOf c, +kOf) in one 64-row box (8 CTAs: its upper 32 rows unused,
+               // past the matrix for the last CTA: zero fill)
+      *ra = K::kOf * c;
       *rb = -1;
       return &m.o;
     case Q_F1:
-      *ra = kQF1 * c + 128 * b;
+      *ra = K::kF1 * c + 128 * b;
       *rb = *ra + 64;
       return &m.ffn1;
     case Q_F2:
-      *x0 = kQF1 * c + kQChunkK * k;
+      *x0 = K::kF1 * c + kQChunkK * k;
       *ra = 128 * b;
       *rb = 128 * b + 64;
       return &m.ffn2;
     default: {
-      const int base = p * kVocab + kQVs * c + 128 * b;  // the last block of CTA 3 overhangs (ignored / zero fill)
+      const int base = p * kVocab + K::kVs * c + 128 * b;  // the last CTA's last block overhangs (ignored / zero fill)
       *ra = base;
       *rb = base + 64;
       return &m.head;
@@ -230,38 +279,40 @@ __device__ __forceinline__ const CUtensorMap* q_chunk(const QuadMaps& m, int c, 
   }
 }
 
-// The producer fills the ring a group of 4 chunks (an M-block's K = 256) at a
-// time, all four landing on the group's one barrier.
-__device__ void q_producer(QuadSmem& sm, const QuadMaps& maps, int c, bool folded) {
+// The producer fills the ring a group of 4 chunks at a time, all four landing
+// on the group's one barrier.
+template <int C>
+__device__ void q_producer(QuadSmem<C>& sm, const QuadMaps& maps, int c, bool folded) {
   int git = 0;  // groups issued
   for (int p = 0; p < kPositions; ++p) {
     for (int g = q_has_in(folded, p) ? Q_IN : Q_QKV; g <= Q_HEAD; ++g) {
-      const int nb = q_blocks(g), ng = q_kchunks(g) / 4;
-      for (int b = 0; b < nb; ++b) {
-        for (int gr = 0; gr < ng; ++gr, ++git) {
-          const int gi = git % kQGroups;
-          if (git >= kQGroups && qerr(sm) == 0 && !mbar_wait_cta(&sm.empty[gi], ((git / kQGroups) - 1) & 1)) {
-            sm.err = 1;
-          }
-          if (qerr(sm)) return;
-          int x0, ra, rb;
-          q_chunk(maps, c, p, g, b, 4 * gr, &x0, &ra, &rb);
-          mbar_expect_tx(&sm.full[gi], 4 * (rb < 0 ? kQChunkBytes / 2 : kQChunkBytes));
-#pragma unroll 1
-          for (int k = 0; k < 4; ++k) {
-            const CUtensorMap* map = q_chunk(maps, c, p, g, b, 4 * gr + k, &x0, &ra, &rb);
-            bf16* dst = sm.ring[4 * gi + k];
-            tma_load_2d(dst, map, x0, ra, &sm.full[gi]);
-            if (rb >= 0) tma_load_2d(dst + kQBoxRows * 64, map, x0, rb, &sm.full[gi]);
-          }
-          sm.last_issued[gi] = git;
+      const int ng = q_groups<C>(g);
+      for (int gr = 0; gr < ng; ++gr, ++git) {
+        const int gi = git % kQGroups;
+        if (git >= kQGroups && qerr(sm) == 0 && !mbar_wait_cta(&sm.empty[gi], ((git / kQGroups) - 1) & 1)) {
+          sm.err = 1;
         }
+        if (qerr(sm)) return;
+        int b, kc, x0, ra, rb;
+        q_group_chunk<C>(g, gr, 0, &b, &kc);
+        q_chunk<C>(maps, c, p, g, b, kc, &x0, &ra, &rb);
+        mbar_expect_tx(&sm.full[gi], 4 * (rb < 0 ? kQChunkBytes / 2 : kQChunkBytes));
+#pragma unroll 1
+        for (int k = 0; k < 4; ++k) {
+          q_group_chunk<C>(g, gr, k, &b, &kc);
+          const CUtensorMap* map = q_chunk<C>(maps, c, p, g, b, kc, &x0, &ra, &rb);
+          bf16* dst = sm.ring[4 * gi + k];
+          tma_load_2d(dst, map, x0, ra, &sm.full[gi]);
+          if (rb >= 0) tma_load_2d(dst + kQBoxRows * 64, map, x0, rb, &sm.full[gi]);
+        }
+        sm.last_issued[gi] = git;
       }
     }
   }
 }
 
-__device__ __forceinline__ const bf16* q_operand(QuadSmem& sm, int g) {
+template <int C>
+__device__ __forceinline__ const bf16* q_operand(QuadSmem<C>& sm, int g) {
   switch (g) {
     case Q_IN: return sm.u.src;
     case Q_QKV: return sm.u.a.xa;
@@ -274,12 +325,14 @@ __device__ __forceinline__ const bf16* q_operand(QuadSmem& sm, int g) {
 
 // The MMA warp's single thread: per GEMM wait until the consumers have
 // written its B operand; per M-block wait for a free accumulator buffer; per
-// ring group (4 weight chunks, K = 256) wait on the group's barrier, then
-// issue the 16 MMAs as one straight-line burst (a branch between tcgen05.mma
-// instructions halves their issue rate) and free the group.  The ring is
-// consumed in order by this one thread, so every parity wait is for the
-// phase right after the one it last saw complete.
-__device__ void q_mma(QuadSmem& sm, bool folded) {
+// ring group (4 weight chunks) wait on the group's barrier, then issue its 16
+// MMAs as one straight-line burst (a branch between tcgen05.mma instructions
+// halves their issue rate) and free the group.  The ring is consumed in
+// order by this one thread, so every parity wait is for the phase right
+// after the one it last saw complete.
+template <int C>
+__device__ void q_mma(QuadSmem<C>& sm, bool folded) {
+  constexpr uint64_t kSlotStep = kQChunkElems * 2 / 16, kPanelStep = kQPanel * 2 / 16;
   int git = 0, mb = 0, gn = 0;
   for (int p = 0; p < kPositions && qerr(sm) == 0; ++p) {
     for (int g = q_has_in(folded, p) ? Q_IN : Q_QKV; g <= Q_HEAD && qerr(sm) == 0; ++g) {
@@ -290,33 +343,64 @@ __device__ void q_mma(QuadSmem& sm, bool folded) {
       ++gn;
       tmem_fence_after_sync();
       const bf16* bop = q_operand(sm, g);
-      const int nb = q_blocks(g), ng = q_kchunks(g) / 4;
+      const int nb = q_blocks<C>(g), per_block = q_kchunks<C>(g);
       bool ok = true;
-      for (int b = 0; b < nb; ++b, ++mb) {
-        const int db = mb % kQNbuf, use = mb / kQNbuf;
-        ok = use < 1 || mbar_wait_cta(&sm.dempty[db], (use - 1) & 1);
-        const uint32_t d = sm.tmem + kQAcc0 + 32u * static_cast<uint32_t>(db);
-        for (int gr = 0; gr < ng && ok; ++gr, ++git) {
-          const int gi = git % kQGroups;
-          ok = mbar_wait_cta(&sm.full[gi], (git / kQGroups) & 1);
+      if (per_block >= 4) {
+        const int ng = per_block / 4;
+        for (int b = 0; b < nb; ++b, ++mb) {
+          const int db = mb % kQNbuf, use = mb / kQNbuf;
+          ok = use < 1 || mbar_wait_cta(&sm.dempty[db], (use - 1) & 1);
+          const uint32_t d = sm.tmem + kQAcc0 + 32u * static_cast<uint32_t>(db);
+          for (int gr = 0; gr < ng && ok; ++gr, ++git) {
+            const int gi = git % kQGroups;
+            ok = mbar_wait_cta(&sm.full[gi], (git / kQGroups) & 1);
+            if (!ok) break;
+            tmem_fence_after_sync();
+            const uint64_t b0 = umma_desc_sw128(bop + 4 * gr * kQPanel);
+            const uint64_t a0 = umma_desc_sw128(sm.ring[4 * gi]);
+            const bool acc0 = gr != 0;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+#pragma unroll
+              for (int kk = 0; kk < 4; ++kk) {
+                umma_bf16(d, a0 + k * kSlotStep + 2 * kk, b0 + k * kPanelStep + 2 * kk, kQIdesc,
+                          acc0 || (k | kk) != 0);
+              }
+            }
+            umma_commit(&sm.empty[gi]);
+          }
           if (!ok) break;
+          umma_commit(&sm.dfull[db]);
+        }
+      } else {
+        // one group holds two M-blocks of K = 128 (FFN2 with 8 CTAs): chunks
+        // 0, 1 accumulate into block mb's buffer, chunks 2, 3 into mb + 1's
+        const int db0 = mb % kQNbuf, db1 = (mb + 1) % kQNbuf;
+        const int use0 = mb / kQNbuf, use1 = (mb + 1) / kQNbuf;
+        ok = use0 < 1 || mbar_wait_cta(&sm.dempty[db0], (use0 - 1) & 1);
+        ok = ok && (use1 < 1 || mbar_wait_cta(&sm.dempty[db1], (use1 - 1) & 1));
+        const int gi = git % kQGroups;
+        ok = ok && mbar_wait_cta(&sm.full[gi], (git / kQGroups) & 1);
+        if (ok) {
           tmem_fence_after_sync();
-          const uint64_t b0 = umma_desc_sw128(bop + 4 * gr * kQPanel);
+          const uint32_t d0 = sm.tmem + kQAcc0 + 32u * static_cast<uint32_t>(db0);
+          const uint32_t d1 = sm.tmem + kQAcc0 + 32u * static_cast<uint32_t>(db1);
+          const uint64_t b0 = umma_desc_sw128(bop);
           const uint64_t a0 = umma_desc_sw128(sm.ring[4 * gi]);
-          constexpr uint64_t kSlotStep = kQChunkElems * 2 / 16, kPanelStep = kQPanel * 2 / 16;
-          const bool acc0 = gr != 0;
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk) {
-              umma_bf16(d, a0 + k * kSlotStep + 2 * kk, b0 + k * kPanelStep + 2 * kk, kQIdesc,
-                        acc0 || (k | kk) != 0);
+              umma_bf16(k < 2 ? d0 : d1, a0 + k * kSlotStep + 2 * kk, b0 + (k & 1) * kPanelStep + 2 * kk, kQIdesc,
+                        ((k & 1) | kk) != 0);
             }
           }
           umma_commit(&sm.empty[gi]);
+          umma_commit(&sm.dfull[db0]);
+          umma_commit(&sm.dfull[db1]);
         }
-        if (!ok) break;
-        umma_commit(&sm.dfull[db]);
+        ++git;
+        mb += 2;
       }
       if (!ok) {
         sm.err = 1;
@@ -335,7 +419,8 @@ __device__ void q_mma(QuadSmem& sm, bool folded) {
 
 // Epilogue read of M-block mb: warp w takes TMEM lanes [32 (w % 4), +32) (A
 // rows m) and columns [16 (w / 4), +16): v[i] = tile row 16 (w / 4) + i.
-__device__ __forceinline__ void q_load_block(QuadSmem& sm, int mb, float (&v)[16]) {
+template <int C>
+__device__ __forceinline__ void q_load_block(QuadSmem<C>& sm, int mb, float (&v)[16]) {
   const int warp = threadIdx.x >> 5;
   const int db = mb % kQNbuf, use = mb / kQNbuf;
   if (qerr(sm) == 0 && !mbar_wait_cta(&sm.dfull[db], use & 1)) sm.err = 1;
@@ -350,7 +435,8 @@ __device__ __forceinline__ void q_load_block(QuadSmem& sm, int mb, float (&v)[16
 }
 
 // B operand written: order the generic writes before the MMA warp's reads.
-__device__ __forceinline__ void q_operand_ready(QuadSmem& sm) {
+template <int C>
+__device__ __forceinline__ void q_operand_ready(QuadSmem<C>& sm) {
   fence_proxy_async();
   qbar();
   if (threadIdx.x == 0) mbar_arrive(&sm.opready);
@@ -412,7 +498,8 @@ __device__ __forceinline__ void q_layer_norm(const bf16* x, bf16* xa, const floa
 // Wait for round rd: this CTA announces on its own round barrier the bytes
 // its peers push to it in this round, and the round completes when they have
 // all landed.
-__device__ __forceinline__ void q_round(QuadSmem& sm, uint32_t& rd, uint32_t bytes_in) {
+template <int C>
+__device__ __forceinline__ void q_round(QuadSmem<C>& sm, uint32_t& rd, uint32_t bytes_in) {
   qbar();
   const int bar = static_cast<int>(rd & 1u);
   if (threadIdx.x == 0) mbar_expect_tx(&sm.xbar[bar], bytes_in);
@@ -420,20 +507,26 @@ __device__ __forceinline__ void q_round(QuadSmem& sm, uint32_t& rd, uint32_t byt
   ++rd;
 }
 
-__device__ __forceinline__ uint32_t q_round_bar(QuadSmem& sm, uint32_t rd, int peer) {
+template <int C>
+__device__ __forceinline__ uint32_t q_round_bar(QuadSmem<C>& sm, uint32_t rd, int peer) {
   return cluster_addr(&sm.xbar[rd & 1u], peer);
 }
 
 // Vocabulary values CTA j holds of each session (its slice, clipped to the vocabulary).
-__host__ __device__ constexpr int q_slice_len(int j) { return kQVs * (j + 1) <= kVocab ? kQVs : kVocab - kQVs * j; }
+template <int C>
+__host__ __device__ constexpr int q_slice_len(int j) {
+  return QK<C>::kVs * (j + 1) <= kVocab ? QK<C>::kVs : kVocab - QK<C>::kVs * j;
+}
 
 // Bytes CTA c receives in the head-values round: from every peer j its slice
 // of each of c's sessions plus one non-finite flag per session.
+template <int C>
 __device__ __forceinline__ uint32_t q_values_bytes_in(int c) {
+  using K = QK<C>;
   uint32_t b = 0;
 #pragma unroll
-  for (int j = 0; j < kQC; ++j) {
-    if (j != c) b += static_cast<uint32_t>(kQOwn * (q_slice_len(j) * 2 + 4));
+  for (int j = 0; j < C; ++j) {
+    if (j != c) b += static_cast<uint32_t>(K::kOwn * (q_slice_len<C>(j) * 2 + 4));
   }
   return b;
 }
@@ -449,15 +542,19 @@ __device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&v)[8])
 // reads its positions with one 64-column load.
 __device__ __forceinline__ uint32_t q_kv_block(int j) { return 8u * static_cast<uint32_t>(j & 1) + (j >> 1); }
 
-// Attention of head c for the tile's 32 rows at position p, all 8 consumer
-// warps: warp w reads TMEM lane quadrant q = w % 4 and takes the positions of
-// parity w / 4; thread (w, l) = row 8 q + l / 4, head dims [16 (l % 4), +16).
-// This position's k and v go into the TMEM cache (K at column 8 b(j), V at
-// 128 + 8 b(j)); scores, exponentials and the softmax sum as the reference
-// takes them (sum over positions in order); each warp sums its positions'
-// values; the even warp adds the odd warp's partial output and writes the
-// output columns into ab and every peer's ab.
-__device__ __forceinline__ void q_attention(QuadSmem& sm, int p, int c, uint32_t rd) {
+// Attention of the CTA's head h for the tile's 32 rows at position p, all 8
+// consumer warps: warp w reads TMEM lane quadrant q = w % 4 and takes the
+// positions of parity w / 4; thread (w, l) = row 8 q + l / 4, head dims
+// [16 (l % 4), +16).  This position's k and v go into the TMEM cache (K at
+// column 8 b(j), V at 128 + 8 b(j)); scores, exponentials and the softmax sum
+// as the reference takes them (sum over positions in order); each warp sums
+// its positions' values; the even warp adds the odd warp's partial output and
+// writes the output columns into ab and the peers' ab.  With two CTAs per
+// head (C = 8) both compute all 32 rows and each sends the other six CTAs its
+// half of them (rows [16 (c % 2), +16)).
+template <int C>
+__device__ __forceinline__ void q_attention(QuadSmem<C>& sm, int p, int c, uint32_t rd) {
+  using K = QK<C>;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int q4 = warp & 3, part = warp >> 2;
   const int r = 8 * q4 + (lane >> 2), u = lane & 3;
@@ -556,24 +653,33 @@ __device__ __forceinline__ void q_attention(QuadSmem& sm, int p, int c, uint32_t
       lo[d] = o[d] + at.o[t128][d];
       hi[d] = o[8 + d] + at.o[t128][8 + d];
     }
-    const int k0 = kHeadDim * c + 16 * u;
+    const int k0 = kHeadDim * K::head(c) + 16 * u;
     uint4* d0 = qop_unit(sm.ab, r, k0);
     uint4* d1 = qop_unit(sm.ab, r, k0 + 8);
     const uint4 w0 = pack8(lo), w1 = pack8(hi);
     *d0 = w0;
     *d1 = w1;
+    if (K::kPerHead == 1 || (q4 >> 1) == (c & 1)) {
 #pragma unroll
-    for (int j = 0; j < kQC; ++j) {
-      if (j != c) {
-        const uint32_t bar = q_round_bar(sm, rd, j);
-        st_async_v4(cluster_addr(d0, j), w0, bar);
-        st_async_v4(cluster_addr(d1, j), w1, bar);
+      for (int j = 0; j < C; ++j) {
+        if (K::head(j) != K::head(c)) {
+          const uint32_t bar = q_round_bar(sm, rd, j);
+          st_async_v4(cluster_addr(d0, j), w0, bar);
+          st_async_v4(cluster_addr(d1, j), w1, bar);
+        }
       }
     }
   }
+  // The head partner sends no rows in this round, only a word, so that this
+  // round, like every other, completes only after every peer has reached it
+  // (no CTA runs a round ahead into buffers its partner still uses).
+  if (K::kPerHead > 1 && threadIdx.x == 0) {
+    st_async_b32(cluster_addr(&sm.r1_sink, c ^ 1), 0u, q_round_bar(sm, rd, c ^ 1));
+  }
 }
 
-__device__ __forceinline__ int64_t q_input_token(const Frame& f, const QuadSmem& sm, int slot, int p) {
+template <int C>
+__device__ __forceinline__ int64_t q_input_token(const Frame& f, const QuadSmem<C>& sm, int slot, int p) {
   if (f.forced) {
     const int64_t t = f.forced[static_cast<int64_t>(sm.sess[slot]) * kPositions + p];
     return t < 0 ? 0 : (t >= kVocab ? kVocab - 1 : t);
@@ -589,15 +695,17 @@ __device__ __forceinline__ void q_stamp(const Frame& f, bool tracer, int p, int 
 // the kernel
 // ---------------------------------------------------------------------------
 
+template <int C>
 __global__ void __launch_bounds__(kQThreads, 1) quad_frame_kernel(Frame f, const __grid_constant__ QuadMaps maps) {
+  using K = QK<C>;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   const uint32_t pad = (1024u - (smem_addr(smem_raw) & 1023u)) & 1023u;
-  QuadSmem& sm = *reinterpret_cast<QuadSmem*>(smem_raw + pad);
+  QuadSmem<C>& sm = *reinterpret_cast<QuadSmem<C>*>(smem_raw + pad);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int rp = f.rp;
   const bool folded = f.emb_proj != nullptr;
   const int c = static_cast<int>(cg::this_cluster().block_rank());
-  const int tile = static_cast<int>(blockIdx.x) / kQC;
+  const int tile = static_cast<int>(blockIdx.x) / C;
   const bool tracer = f.trace != nullptr && blockIdx.x == 0 && threadIdx.x == 0;
 
   // ---- sessions [16 tile, +16) of the active list (every CTA of the cluster)
@@ -624,8 +732,8 @@ __global__ void __launch_bounds__(kQThreads, 1) quad_frame_kernel(Frame f, const
   const int n_sess = sm.n_sess;
   if (n_sess == 0) return;  // the same in every CTA of the cluster: none touches another
   auto live = [&](int r) { return (r >> 1) < n_sess && (r & 1) < rp; };
-  const int own0 = kQOwn * c;
-  const int n_own = n_sess - own0 <= 0 ? 0 : (n_sess - own0 < kQOwn ? n_sess - own0 : kQOwn);
+  const int own0 = K::kOwn * c;
+  const int n_own = n_sess - own0 <= 0 ? 0 : (n_sess - own0 < K::kOwn ? n_sess - own0 : K::kOwn);
   if (tracer) f.trace[256] = static_cast<uint64_t>(clock64()), f.trace[257] = global_ns();
 
   if (threadIdx.x == 0) {
@@ -704,8 +812,8 @@ __global__ void __launch_bounds__(kQThreads, 1) quad_frame_kernel(Frame f, const
     const float cfg_scale = f.prm.cfg_scale, uncond_scale = __fsub_rn(1.0f, f.prm.cfg_scale);
     int mb = 0;       // M-blocks consumed
     uint32_t rd = 0;  // exchange rounds
-    if (threadIdx.x < kQVs / 8) {  // head bias of position 0
-      const int v0 = kQVs * c + 8 * threadIdx.x;
+    if (threadIdx.x < K::kVs / 8) {  // head bias of position 0
+      const int v0 = K::kVs * c + 8 * threadIdx.x;
       const uint4 z = make_uint4(0, 0, 0, 0);
       *reinterpret_cast<uint4*>(sm.hb[0] + 8 * threadIdx.x) = v0 < kVocab ? *reinterpret_cast<const uint4*>(f.head_b + v0) : z;
       *reinterpret_cast<uint4*>(sm.hb[1] + 8 * threadIdx.x) = z;
@@ -750,8 +858,8 @@ __global__ void __launch_bounds__(kQThreads, 1) quad_frame_kernel(Frame f, const
       }
       // head bias: position p's slice has landed (issued a position ahead),
       // position p + 1's is issued now; per-position flags
-      if (threadIdx.x < kQVs / 8) {
-        const int v0 = kQVs * c + 8 * threadIdx.x;
+      if (threadIdx.x < K::kVs / 8) {
+        const int v0 = K::kVs * c + 8 * threadIdx.x;
         if (v0 < kVocab) {  // kVocab % 8 == 0; the slice's tail past the vocabulary stays zero
           cp_async_wait_all();
           if (p + 1 < kPositions) {
@@ -784,7 +892,8 @@ __global__ void __launch_bounds__(kQThreads, 1) quad_frame_kernel(Frame f, const
       // ---------------- attention (R1: head c's output columns to every CTA)
       q_attention(sm, p, c, rd);
       q_stamp(f, tracer, p, 3);
-      q_round(sm, rd, static_cast<uint32_t>((kQC - 1) * kQR * kHeadDim * 2));
+      q_round(sm, rd, static_cast<uint32_t>((C - K::kPerHead) * (kQR / K::kPerHead) * kHeadDim * 2 +
+                                            (K::kPerHead > 1 ? 4 : 0)));
       fence_proxy_async();
       q_operand_ready(sm);
       q_stamp(f, tracer, p, 4);
@@ -794,8 +903,8 @@ __global__ void __launch_bounds__(kQThreads, 1) quad_frame_kernel(Frame f, const
         float v[16];
         q_load_block(sm, mb, v);
         ++mb;
-        if (m_lane < kQOf) {
-          const int n = kQOf * c + m_lane;
+        if (m_lane < K::kOf) {
+          const int n = K::kOf * c + m_lane;
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
             bf16* xr = sm.xr.x + (16 * sh + i) * kQLdX + n;
@@ -804,23 +913,23 @@ __global__ void __launch_bounds__(kQThreads, 1) quad_frame_kernel(Frame f, const
         }
       }
       qbar();
-      {
-        // thread: row lane, features [64 c + 8 warp, +8)
-        const uint4* src = reinterpret_cast<const uint4*>(sm.xr.x + lane * kQLdX + kQOf * c + 8 * warp);
+      if (8 * warp < K::kOf) {
+        // thread: row lane, features [kOf c + 8 warp, +8)
+        const uint4* src = reinterpret_cast<const uint4*>(sm.xr.x + lane * kQLdX + K::kOf * c + 8 * warp);
         const uint4 w = *src;
 #pragma unroll
-        for (int j = 0; j < kQC; ++j) {
+        for (int j = 0; j < C; ++j) {
           if (j != c) st_async_v4(cluster_addr(src, j), w, q_round_bar(sm, rd, j));
         }
       }
-      q_round(sm, rd, static_cast<uint32_t>((kQC - 1) * kQR * kQOf * 2));
+      q_round(sm, rd, static_cast<uint32_t>((C - 1) * kQR * K::kOf * 2));
       q_stamp(f, tracer, p, 5);
       q_layer_norm(sm.xr.x, sm.u.a.xa, g2);
       q_operand_ready(sm);
       q_stamp(f, tracer, p, 6);
 
-      // ---------------- FFN1 + GELU (features [256 c, +256))
-      for (int b = 0; b < 2; ++b, ++mb) {
+      // ---------------- FFN1 + GELU (features [kF1 c, +kF1))
+      for (int b = 0; b < K::kF1 / 128; ++b, ++mb) {
         float v[16];
         q_load_block(sm, mb, v);
         const int fl = 128 * b + m_lane;
@@ -835,7 +944,7 @@ __global__ void __launch_bounds__(kQThreads, 1) quad_frame_kernel(Frame f, const
         float v[16];
         q_load_block(sm, mb, v);
         const int n = 128 * b + m_lane;
-        const int owner = n / kQOf, nl = n % kQOf;
+        const int owner = n / K::kOf, nl = n % K::kOf;
         // the owner keeps its own partials in xa (free after the FFN1 MMAs), the
         // peers' in red[slot], slot = the sender's rank skipping the owner's
         float* dst = owner == c ? reinterpret_cast<float*>(sm.u.a.xa) + nl * kQR + 16 * sh
@@ -855,19 +964,18 @@ __global__ void __launch_bounds__(kQThreads, 1) quad_frame_kernel(Frame f, const
         }
       }
       q_stamp(f, tracer, p, 8);
-      q_round(sm, rd, static_cast<uint32_t>((kQC - 1) * kQOf * kQR * 4));
+      q_round(sm, rd, static_cast<uint32_t>((C - 1) * K::kOf * kQR * 4));
       q_stamp(f, tracer, p, 9);
-      {
-        // thread: row lane, features [8 warp, +8) of this CTA's 64
+      if (8 * warp < K::kOf) {
+        // thread: row lane, features [8 warp, +8) of this CTA's kOf
         const int r = lane, nl = 8 * warp;
-        const int k0 = kQOf * c + nl;
+        const int k0 = K::kOf * c + nl;
         float xv[8];
         unpack8(*reinterpret_cast<const uint4*>(sm.xr.x + r * kQLdX + k0), xv);
+        // the C partials in CTA order: this CTA's own in xa, the peers' in red
+        const float* src[C];
 #pragma unroll
-        // the four partials in CTA order: this CTA's own in xa, the peers' in red
-        const float* src[kQC];
-#pragma unroll
-        for (int j = 0; j < kQC; ++j) {
+        for (int j = 0; j < C; ++j) {
           src[j] = (j == c ? reinterpret_cast<const float*>(sm.u.a.xa) : &sm.u.a.v.red[j < c ? j : j - 1][0][0]) +
                    nl * kQR + r;
         }
@@ -875,18 +983,18 @@ __global__ void __launch_bounds__(kQThreads, 1) quad_frame_kernel(Frame f, const
         for (int e = 0; e < 8; ++e) {
           float s = src[0][e * kQR];
 #pragma unroll
-          for (int j = 1; j < kQC; ++j) s = __fadd_rn(s, src[j][e * kQR]);
+          for (int j = 1; j < C; ++j) s = __fadd_rn(s, src[j][e * kQR]);
           xv[e] = __fadd_rn(xv[e], round_bf16(s));
         }
         const uint4 w = pack8(xv);
         uint4* d = qop_unit(sm.ab, r, k0);
         *d = w;
 #pragma unroll
-        for (int j = 0; j < kQC; ++j) {
+        for (int j = 0; j < C; ++j) {
           if (j != c) st_async_v4(cluster_addr(d, j), w, q_round_bar(sm, rd, j));
         }
       }
-      q_round(sm, rd, static_cast<uint32_t>((kQC - 1) * kQR * kQOf * 2));
+      q_round(sm, rd, static_cast<uint32_t>((C - 1) * kQR * K::kOf * 2));
       fence_proxy_async();
       q_operand_ready(sm);
       q_stamp(f, tracer, p, 10);
@@ -895,11 +1003,11 @@ __global__ void __launch_bounds__(kQThreads, 1) quad_frame_kernel(Frame f, const
       {
         bf16* lo_base = f.logits_out;
         const bf16* hbp = sm.hb[p & 1];
-        for (int b = 0; b < 4; ++b, ++mb) {
+        for (int b = 0; b < K::kVs / 128; ++b, ++mb) {
           float v[16];
           q_load_block(sm, mb, v);
           const int vl = 128 * b + m_lane;
-          const int t = kQVs * c + vl;
+          const int t = K::kVs * c + vl;
           const bool in_vocab = t < kVocab;
           const float bias = bf2f(hbp[vl]);
           uint32_t nfm = 0;
@@ -931,7 +1039,7 @@ __global__ void __launch_bounds__(kQThreads, 1) quad_frame_kernel(Frame f, const
             }
             if (in_vocab) {
               // slots s0, s0 + 1 share their owner (owners hold 4 aligned slots)
-              const int owner = s0 / kQOwn;
+              const int owner = s0 / K::kOwn;
               if (owner == c) {
                 sm.u.a.v.vals[s0 - own0][t] = static_cast<uint16_t>(g0);
                 sm.u.a.v.vals[s0 + 1 - own0][t] = static_cast<uint16_t>(g1);
@@ -953,27 +1061,27 @@ __global__ void __launch_bounds__(kQThreads, 1) quad_frame_kernel(Frame f, const
         q_stamp(f, tracer, p, 11);
         // the other CTAs' sessions: this CTA's vocabulary slice of each (all
         // four slots of every owner, live or not), and its non-finite flags
-        const int units = q_slice_len(c) / 8;
-        constexpr int kOther = kQS - kQOwn;
-        for (int i = threadIdx.x; i < kOther * (kQVs / 8); i += kQT) {
-          const int oi = i / (kQVs / 8), un = i % (kQVs / 8);
+        const int units = q_slice_len<C>(c) / 8;
+        constexpr int kOther = kQS - K::kOwn;
+        for (int i = threadIdx.x; i < kOther * (K::kVs / 8); i += kQT) {
+          const int oi = i / (K::kVs / 8), un = i % (K::kVs / 8);
           if (un < units) {
-            const int slot = oi < own0 ? oi : oi + kQOwn;  // skip the owned slots
-            const int owner = slot / kQOwn;
+            const int slot = oi < own0 ? oi : oi + K::kOwn;  // skip the owned slots
+            const int owner = slot / K::kOwn;
             const uint4 val = *reinterpret_cast<const uint4*>(&sm.xr.stage[slot][8 * un]);
-            st_async_v4(cluster_addr(&sm.u.a.v.vals[slot - kQOwn * owner][kQVs * c + 8 * un], owner), val,
+            st_async_v4(cluster_addr(&sm.u.a.v.vals[slot - K::kOwn * owner][K::kVs * c + 8 * un], owner), val,
                         q_round_bar(sm, rd, owner));
           }
         }
         if (threadIdx.x < kQS) {
           const int slot = threadIdx.x;
-          const int owner = slot / kQOwn;
+          const int owner = slot / K::kOwn;
           if (owner != c) {
-            st_async_b32(cluster_addr(&sm.peer_nf[c][slot - kQOwn * owner], owner), sm.nf[slot],
+            st_async_b32(cluster_addr(&sm.peer_nf[c][slot - K::kOwn * owner], owner), sm.nf[slot],
                          q_round_bar(sm, rd, owner));
           }
         }
-        q_round(sm, rd, q_values_bytes_in(c));
+        q_round(sm, rd, q_values_bytes_in<C>(c));
       }
       q_stamp(f, tracer, p, 12);
 
@@ -983,7 +1091,7 @@ __global__ void __launch_bounds__(kQThreads, 1) quad_frame_kernel(Frame f, const
         const int ls = warp, slot = own0 + ls;
         uint32_t nfs = sm.nf[slot];
 #pragma unroll
-        for (int j = 0; j < kQC; ++j) {
+        for (int j = 0; j < C; ++j) {
           if (j != c) nfs |= sm.peer_nf[j][ls];
         }
         RowSample rs;
@@ -1004,7 +1112,7 @@ __global__ void __launch_bounds__(kQThreads, 1) quad_frame_kernel(Frame f, const
           if (!f.prm.argmax && counter_valid) sm.ctr[ls] = counter + 1;
           if (p + 1 < kPositions) {
 #pragma unroll
-            for (int j = 0; j < kQC; ++j) {
+            for (int j = 0; j < C; ++j) {
               if (j != c) {
                 st_async_b32(cluster_addr(&sm.tok[slot][p], j), static_cast<uint32_t>(token),
                              q_round_bar(sm, rd, j));
@@ -1016,15 +1124,15 @@ __global__ void __launch_bounds__(kQThreads, 1) quad_frame_kernel(Frame f, const
       q_stamp(f, tracer, p, 13);
       if (p + 1 < kPositions) {
         // dead owned slots still announce their 4 bytes: push a zero token for them
-        if (threadIdx.x >= n_own && threadIdx.x < kQOwn) {
+        if (threadIdx.x >= n_own && threadIdx.x < K::kOwn) {
           const int slot = own0 + threadIdx.x;
           sm.tok[slot][p] = 0;
 #pragma unroll
-          for (int j = 0; j < kQC; ++j) {
+          for (int j = 0; j < C; ++j) {
             if (j != c) st_async_b32(cluster_addr(&sm.tok[slot][p], j), 0u, q_round_bar(sm, rd, j));
           }
         }
-        q_round(sm, rd, static_cast<uint32_t>((kQC - 1) * kQOwn * 4));
+        q_round(sm, rd, static_cast<uint32_t>((C - 1) * K::kOwn * 4));
       } else {
         qbar();
       }
@@ -1123,38 +1231,37 @@ __global__ void __launch_bounds__(kQThreads, 1) quad_frame_kernel(Frame f, const
   cg::this_cluster().sync();  // no CTA leaves while a peer may still push into it
 }
 
-}  // namespace
-
-int quad_frame_clusters() {
+template <int C>
+int clusters_of() {
   static PerDeviceInt cache;  // the opt-in below is per device context
   return cache.get([] {
     int clusters = 0;
-    if (cudaFuncSetAttribute(quad_frame_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(kQuadSmemBytes)) == cudaSuccess) {
+    if (cudaFuncSetAttribute(quad_frame_kernel<C>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(quad_smem_bytes<C>())) == cudaSuccess) {
       cudaLaunchConfig_t cfg = {};
       cudaLaunchAttribute attr[1];
       attr[0].id = cudaLaunchAttributeClusterDimension;
-      attr[0].val.clusterDim.x = kQC;
+      attr[0].val.clusterDim.x = C;
       attr[0].val.clusterDim.y = 1;
       attr[0].val.clusterDim.z = 1;
-      cfg.gridDim = dim3(kQC);
+      cfg.gridDim = dim3(C);
       cfg.blockDim = dim3(kQThreads);
-      cfg.dynamicSmemBytes = kQuadSmemBytes;
+      cfg.dynamicSmemBytes = quad_smem_bytes<C>();
       cfg.attrs = attr;
       cfg.numAttrs = 1;
-      if (cudaOccupancyMaxActiveClusters(&clusters, quad_frame_kernel, &cfg) != cudaSuccess) clusters = 0;
+      if (cudaOccupancyMaxActiveClusters(&clusters, quad_frame_kernel<C>, &cfg) != cudaSuccess) clusters = 0;
     }
     cudaGetLastError();
     return clusters;
   });
 }
 
-bool quad_frame_supported(const Frame& f) {
-  if (f.d != kQD || f.H != 4 || f.F != kQF || f.L != 1 || !f.in_proj || (f.rp != 1 && f.rp != 2)) return false;
-  return quad_frame_clusters() > 0;
+bool shape_supported(const Frame& f) {
+  return f.d == kQD && f.H == 4 && f.F == kQF && f.L == 1 && f.in_proj && (f.rp == 1 || f.rp == 2);
 }
 
-cudaError_t launch_quad_frame(const Frame& f, cudaStream_t stream) {
+template <int C>
+cudaError_t launch(const Frame& f, cudaStream_t stream) {
   QuadMaps maps;
   if (!make_weight_map(&maps.in_proj, f.in_w, kEmbed, kQD, kQBoxRows) ||
       !make_weight_map(&maps.qkv, f.qkv, kQD, 3 * kQD, kQBoxRows) ||
@@ -1169,18 +1276,28 @@ cudaError_t launch_quad_frame(const Frame& f, cudaStream_t stream) {
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = kQC;
+  attr[0].val.clusterDim.x = C;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
-  cfg.gridDim = dim3(tiles * kQC);
+  cfg.gridDim = dim3(tiles * C);
   cfg.blockDim = dim3(kQThreads);
-  cfg.dynamicSmemBytes = kQuadSmemBytes;
+  cfg.dynamicSmemBytes = quad_smem_bytes<C>();
   cfg.stream = stream;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  e = cudaLaunchKernelEx(&cfg, quad_frame_kernel, f, maps);
+  e = cudaLaunchKernelEx(&cfg, quad_frame_kernel<C>, f, maps);
   if (e != cudaSuccess) return e;
   return launch_frame_eos(f, stream);
 }
+
+}  // namespace
+
+int quad_frame_clusters() { return clusters_of<4>(); }
+bool quad_frame_supported(const Frame& f) { return shape_supported(f) && quad_frame_clusters() > 0; }
+cudaError_t launch_quad_frame(const Frame& f, cudaStream_t stream) { return launch<4>(f, stream); }
+
+int octo_frame_clusters() { return clusters_of<8>(); }
+bool octo_frame_supported(const Frame& f) { return shape_supported(f) && octo_frame_clusters() > 0; }
+cudaError_t launch_octo_frame(const Frame& f, cudaStream_t stream) { return launch<8>(f, stream); }
 
 }  // namespace mtt

@@ -69,20 +69,23 @@ def config4_flags(n, frame=60, seed=2024):
     return active, unfinished, finished, forbid
 
 
-QUAD = 10
+QUAD, OCTO = 10, 11
 
 
-@pytest.mark.parametrize("n,path", [(1024, 0), (512, 0), (256, 0), (128, 0), (64, 0), (512, QUAD), (1024, QUAD)],
-                         ids=["1024-auto", "512-auto", "256-auto", "128-auto", "64-auto", "512-quad", "1024-quad"])
+@pytest.mark.parametrize("n,path", [(1024, 0), (512, 0), (256, 0), (128, 0), (64, 0), (512, QUAD), (1024, QUAD),
+                                    (128, OCTO), (64, OCTO)],
+                         ids=["1024-auto", "512-auto", "256-auto", "128-auto", "64-auto", "512-quad", "1024-quad",
+                              "128-octo", "64-octo"])
 def test_auto_frame_at_bench_batch(n, path):
-    """The AUTO path at each bench batch, and the quad kernel (explicit path)
-    at config 4's one- and two-GPU batches: one wave of 4-CTA clusters at 512
-    sessions, two waves at 1024."""
+    """The AUTO path at each bench batch, the quad kernel (explicit path) at
+    config 4's one- and two-GPU batches (one wave of 4-CTA clusters at 512
+    sessions, two waves at 1024), and the octo kernel at config 4's
+    eight-GPU batch and config 3's."""
     from magpie_tts_rt_b200.local_ar import LocalArEngine
     w = bench_weights()
     eng = LocalArEngine(w, max_streams=n, path=path)
     assert path == 0 or eng.path == path
-    tile = {2: 8, 3: 8, 4: 16, 9: 16, QUAD: 16}.get(eng.path, 8)
+    tile = {2: 8, 3: 8, 4: 16, 9: 16, QUAD: 16, OCTO: 16}.get(eng.path, 8)
     g = torch.Generator().manual_seed(1000 + n)
     hidden = torch.randn(n, 2, EMBED, generator=g).to(torch.bfloat16)
     active, uf, fi, fb = config4_flags(n)
@@ -94,7 +97,7 @@ def test_auto_frame_at_bench_batch(n, path):
         assert gpu["counter"][s] == counter[s], s
     sel = [s for s in spread(n, tile) if active[s]]
     sel += [s for s in np.nonzero(active & ~uf & ~fi)[0] if s not in sel]  # every EOS-enabled / forbid session
-    if n <= 64:
+    if n <= 128:
         sel = list(np.nonzero(active)[0])  # every active session
     assert len(sel) >= min(64, int(active.sum()))
     check_frame(w, hidden, (uf, fi, fb), seed, counter, gpu, streams=sorted(sel))

@@ -25,11 +25,12 @@ from oracle import sampler as S
 pytestmark = pytest.mark.gpu
 
 RTOL = 1e-2
-PATH_AUTO, PHASE, FUSED, TILE, PAIR, SPLIT1, SPLIT2, SPLIT4, SPLIT8, SPLIT2X32, QUAD = 0, 1, 2, 3, 4, 5, 6, 7, 8, 9, 10
+PATH_AUTO, PHASE, FUSED, TILE, PAIR, SPLIT1, SPLIT2, SPLIT4, SPLIT8, SPLIT2X32, QUAD, OCTO = range(12)
 SPLITS = [SPLIT1, SPLIT2, SPLIT4, SPLIT8, SPLIT2X32]
-BOTH = [PHASE, FUSED, TILE, PAIR, QUAD] + SPLITS
+BOTH = [PHASE, FUSED, TILE, PAIR, QUAD, OCTO] + SPLITS
 PATH_IDS = {PATH_AUTO: "auto", PHASE: "phase", FUSED: "cluster", TILE: "tile", PAIR: "pair", SPLIT1: "split1",
-            SPLIT2: "split2", SPLIT4: "split4", SPLIT8: "split8", SPLIT2X32: "split2x32", QUAD: "quad"}
+            SPLIT2: "split2", SPLIT4: "split4", SPLIT8: "split8", SPLIT2X32: "split2x32", QUAD: "quad",
+            OCTO: "octo"}
 
 
 def path_id(v):
@@ -174,7 +175,8 @@ FLAGS6 = ([0, 1, 0, 0, 0, 1], [0, 0, 0, 1, 0, 1], [0, 0, 1, 0, 0, 0])  # incl. a
     (SHAPE_BASELINE, 20, PAIR, True), (SHAPE_BASELINE, 11, PAIR, False), (SHAPE_SOFIA, 3, PHASE, True)] +
     [(SHAPE_BASELINE, n, sp, fold) for sp in SPLITS for n, fold in ((6, True), (11, True), (20, True), (11, False))] +
     [(SHAPE_BASELINE, 24, SPLIT2X32, True), (SHAPE_BASELINE, 17, SPLIT2X32, False)] +
-    [(SHAPE_BASELINE, n, QUAD, fold) for n, fold in ((6, True), (11, True), (20, True), (24, True), (17, False))])
+    [(SHAPE_BASELINE, n, qp, fold) for qp in (QUAD, OCTO)
+     for n, fold in ((6, True), (11, True), (20, True), (24, True), (17, False))])
 def test_frame_matches_oracle(engines, shape, n, path, fold):
     w = weights(shape, 21)
     eng = engines(shape, 21, 24, path=path, fold=fold)
@@ -336,7 +338,7 @@ def test_argmax_without_cfg(engines, path):
 
 
 @pytest.mark.parametrize("name,path", [("A_bf16_cfg", PATH_AUTO), ("A_bf16_cfg", TILE), ("A_bf16_cfg", PAIR),
-                                       ("R_bf16_cfg", PATH_AUTO), ("A_bf16_cfg", QUAD)] +
+                                       ("R_bf16_cfg", PATH_AUTO), ("A_bf16_cfg", QUAD), ("A_bf16_cfg", OCTO)] +
                          [("A_bf16_cfg", sp) for sp in SPLITS], ids=path_id)
 def test_frame_against_reference_golden(engines, golden, golden_dir, name, path):
     """Teacher-forced on the reference's tokens, the GPU logits match the NeMo
@@ -395,7 +397,7 @@ def test_gpu_no_further_from_exact_than_oracle(engines):
     assert gpu_err.max() <= 2.0 * cpu_err.max() + 1e-4, (gpu_err.max(), cpu_err.max())
 
 
-@pytest.mark.parametrize("path", [FUSED, TILE, PAIR, QUAD] + SPLITS, ids=path_id)
+@pytest.mark.parametrize("path", [FUSED, TILE, PAIR, QUAD, OCTO] + SPLITS, ids=path_id)
 @pytest.mark.parametrize("kind", ["flat", "sharp", "ties"])
 def test_sampler_row_shapes(path, kind):
     """Logit rows that drive each top-k select path: flat rows (every token
@@ -429,7 +431,7 @@ def test_sampler_row_shapes(path, kind):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs in this process")
-@pytest.mark.parametrize("path", [PATH_AUTO, FUSED, TILE, PAIR, SPLIT4, SPLIT8, QUAD], ids=path_id)
+@pytest.mark.parametrize("path", [PATH_AUTO, FUSED, TILE, PAIR, SPLIT4, SPLIT8, QUAD, OCTO], ids=path_id)
 def test_frames_on_two_devices_in_one_process(path):
     """One process drives frames on cuda:0 and then cuda:1 (the reference
     allows several runtimes per process, tests/c_api/multi_runtime_plugin_gpu_tests.cpp).
