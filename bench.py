@@ -385,6 +385,29 @@ def run_ours(args, world, rank, local):
                 launches=launches_per_frame * frames * args.steps, eng=eng, w=w)
 
 
+def config3_measure(args, peaks):
+    """Config 3 on one GPU: 64 sessions x CFG pair, per-session EOS forced at a
+    frame U[200, 600] and finished sessions masked out of later frames, 600
+    frames per step; frames/s resident and end to end, and the frame call's
+    HBM and tensor fractions (algorithmic bytes: the 18.6 MB of weights read
+    once per frame plus 31 KB per active session)."""
+    import argparse
+    a3 = argparse.Namespace(**{**vars(args), "workload": "config3", "sessions": None, "frames": None, "path": 0,
+                               "steps": 2, "warmup": 3})
+    r = run_ours(a3, 1, 0, 0)
+    shape = SHAPE_BASELINE
+    active_per_frame = r["frames_per_step"] / r["frames"]
+    t_frame = r["t"] / a3.steps / r["frames"]
+    bytes_ = shape.frame_weight_params() * 2 + active_per_frame * 31_000
+    flops = active_per_frame * 2 * 2 * shape.macs_per_row()
+    tensor_peak = peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"])
+    return {"workload": "config 3: 64 sessions x CFG pair, EOS forced at U[200,600], finished sessions masked, "
+                        "600 frames", "frame_path": r["path"], "frames_per_s": r["value"], "e2e_frames_per_s": r["e2e"],
+            "avg_frame_call_us": t_frame * 1e6, "hbm_frac": bytes_ / t_frame / 1e9 / peaks["hbm_gbs"],
+            "tensor_frac": flops / t_frame / 1e12 / tensor_peak, "invalid_rows": r["invalid"],
+            "forced_eos_ok": r["forced_ok"]}
+
+
 def latency_config2(eng_w, dev, frames=1000, warm=20):
     """Config 2: B=1 CFG pair, seed 1234, new hidden each frame; one CUDA-graph
     launch per frame; per-frame device time by CUDA events."""
@@ -595,13 +618,14 @@ def r_shape_measure(dev, peaks, sizes=(64, 1024), calls=10, seed=5):
     return out
 
 
-def frame_paths_measure(w, dev, peaks, sizes=(64, 256, 512, 1024), calls=20,
-                        paths=((10, "quad kernel"), (0, "AUTO"))):
+def frame_paths_measure(w, dev, peaks, sizes=(64, 128, 256, 512, 1024), calls=20,
+                        paths=((10, "quad kernel"), (11, "octo kernel"), (0, "AUTO"))):
     """Frame-call time of the benchmark shape (config 4's flags at its first
     frames: every session unfinished, CFG pair) on the quad kernel (4-CTA
-    cluster per 16 sessions, explicit path) next to the AUTO path, for the
-    sessions per GPU that config 4 puts on 8, 4, 2 and 1 GPUs and config 3's
-    64.  CUDA events on the launching stream."""
+    cluster per 16 sessions) and the octo kernel (8-CTA cluster per 16
+    sessions), explicit paths, next to the AUTO path, for the sessions per GPU
+    that config 4 puts on 8, 4, 2 and 1 GPUs and config 3's 64 (the octo
+    kernel up to 256 sessions).  CUDA events on the launching stream."""
     from magpie_tts_rt_b200.local_ar import LocalArEngine, StreamBatch
     tensor_peak = peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"])
     stream = torch.cuda.Stream(dev)
@@ -614,6 +638,8 @@ def frame_paths_measure(w, dev, peaks, sizes=(64, 256, 512, 1024), calls=20,
         b.unfinished.fill_(True)
         row = {}
         for path, name in paths:
+            if path == 11 and n > 256:
+                continue
             eng = LocalArEngine(w, max_streams=n, device=dev, path=path)
             with torch.cuda.stream(stream):
                 for _ in range(3):
@@ -1025,6 +1051,9 @@ def main():
         eos = eos_measure(res["w"], torch.device("cuda", local), peaks)
         rshape = r_shape_measure(torch.device("cuda", local), peaks)
         paths = frame_paths_measure(res["w"], torch.device("cuda", local), peaks)
+    c3 = None
+    if world == 1 and not args.no_latency and args.workload == "config4":
+        c3 = config3_measure(args, peaks)
     cpu = None
     if world == 1 and rank == 0 and not args.no_cpu_baseline:
         cpu = cpu_oracle_sample()
@@ -1048,7 +1077,9 @@ def main():
                            "split kernel x2": "split_frame_kernel<2, 16>",
                            "split kernel x4": "split_frame_kernel<4, 16>",
                            "split kernel x8": "split_frame_kernel<8, 16>",
-                           "split kernel x2, 32-row tiles": "split_frame_kernel<2, 32>"}.get(res["path"], res["path"]) +
+                           "split kernel x2, 32-row tiles": "split_frame_kernel<2, 32>",
+                           "quad kernel": "quad_frame_kernel<4>", "octo kernel": "quad_frame_kernel<8>"}.get(
+                              res["path"], res["path"]) +
                           " (per frame call, with the EOS projection/decision kernels: 0.6% of device time)",
                 "achieved": tf, "peak": tensor_peak, "unit": "TFLOP/s", "frac": tf / tensor_peak,
                 "peak_kind": f"{peaks_kind} sustained bf16",
@@ -1072,7 +1103,7 @@ def main():
                 "roofline": roof,
                 "latency_config2": latency, "alignment_gate": align, "main_decoder_step": md,
                 "config5_loop": loop, "eos_projection": eos, "tensor_probe": probe, "r_shape_frame": rshape,
-                "frame_paths": paths,
+                "frame_paths": paths, "config3": c3,
                 "cpu_baseline": cpu,
                 "checks": {"invalid_rows": res["invalid"], "forced_eos_ok": res["forced_ok"]}}
         print(json.dumps(line), flush=True)
