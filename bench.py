@@ -93,6 +93,8 @@ def parse():
     ap.add_argument("--r-shape-only", action="store_true",
                     help="run only the d=768 / 2-layer Local AR frame measurement and print its object")
     ap.add_argument("--r-sessions", type=int, nargs="*", default=None)
+    ap.add_argument("--phase-trace", default=None, metavar="PATH:SESSIONS",
+                    help="print the per-position phase breakdown of the quad (10) or octo (11) kernel and exit")
     ap.add_argument("--eos-only", action="store_true",
                     help="run only the EOS-projection measurement and print its object (profiling)")
     ap.add_argument("--eos-sessions", type=int, nargs="*", default=None,
@@ -486,6 +488,47 @@ def latency_trace(eng_w, dev, frames=20):
             "frame_us_in_kernel": float(np.median((a[:, 258] - a[:, 256]) / mhz)),
             "position_us_mean": float(per_pos[:, 1:].mean()), "position0_us": float(per_pos[:, 0].mean()),
             "phase_us_mean_p1_15": {k: float(d[:, 1:, i].mean()) for i, k in enumerate(PHASE_STAMPS)}}
+
+
+QUAD_STAMPS = ["input rows", "q|k|v", "attention", "attention round", "o-projection + round", "LN2", "FFN1",
+               "FFN2 partials", "FFN2 partials round", "FFN2 sum + x'' round", "head", "values round", "sampling",
+               "token round", "next rows + LN1"]
+
+
+def quad_trace(w, dev, path, n, frames=10):
+    """Per-position phase breakdown of the quad (path 10) or octo (path 11)
+    kernel at n sessions (library trace hook mtt_b200_test_frame_trace):
+    SM-clock stamps of CTA 0 at 16 points of each position, averaged over
+    positions 1..15 of `frames` frames, in microseconds at the clock measured
+    over the frame."""
+    from magpie_tts_rt_b200 import _lib as L
+    from magpie_tts_rt_b200.local_ar import LocalArEngine, StreamBatch
+    eng = LocalArEngine(w, max_streams=n, device=dev, path=path)
+    b = StreamBatch.allocate(n, device=dev)
+    b.rng_seed.copy_(torch.arange(n))
+    b.unfinished.fill_(True)
+    g = torch.Generator().manual_seed(78)
+    stamps = torch.zeros(260, dtype=torch.int64, device=dev)
+    per = []
+    try:
+        L.lib.mtt_b200_test_frame_trace(ctypes.c_void_p(stamps.data_ptr()))
+        for f in range(frames + 3):
+            b.decoder_hidden.copy_(torch.randn(n, 2, EMBED, generator=g).to(torch.bfloat16))
+            eng.frame(b)
+            torch.cuda.synchronize(dev)
+            if f >= 3:
+                per.append(stamps.cpu().numpy().copy())
+    finally:
+        L.lib.mtt_b200_test_frame_trace(None)
+    a = np.stack(per).astype(np.float64)
+    mhz = (a[:, 258] - a[:, 256]) / (a[:, 259] - a[:, 257]) * 1000.0
+    pos = a[:, :256].reshape(frames, 16, 16)
+    d = np.diff(pos, axis=2) / mhz[:, None, None]
+    per_pos = (pos[:, :, 15] - pos[:, :, 0]) / mhz[:, None]
+    return {"frame_path": PATH_NAMES.get(eng.path, str(eng.path)), "sessions": n, "sm_mhz": float(np.median(mhz)),
+            "frame_us_in_kernel": float(np.median((a[:, 258] - a[:, 256]) / mhz)),
+            "position_us_mean": float(per_pos[:, 1:].mean()),
+            "phase_us_mean_p1_15": {k: float(d[:, 1:, i].mean()) for i, k in enumerate(QUAD_STAMPS)}}
 
 
 def tensor_probe(dev):
@@ -976,6 +1019,13 @@ def main():
         if world > 1:
             import torch.distributed as dist
             dist.destroy_process_group()
+        return
+    if args.phase_trace:
+        path, n = (int(v) for v in args.phase_trace.split(":"))
+        w = make_weights(SHAPE_BASELINE, seed=0, dtype=torch.bfloat16, profile="baseline")
+        out = quad_trace(w, torch.device("cuda", local), path, n)
+        if rank == 0:
+            print(json.dumps({"phase_trace": out}), flush=True)
         return
     if args.eos_only:
         w = make_weights(SHAPE_BASELINE, seed=0, dtype=torch.bfloat16, profile="baseline")
