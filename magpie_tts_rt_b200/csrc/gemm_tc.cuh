@@ -203,7 +203,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         decode(i, n_tiles, m_tiles, mt, nt, ks);
         for (int kc = 0; kc < pr.k_chunks; ++kc, ++it) {
           const int s = it % S;
-          if (it >= S && !mbar_wait(&empty[s], ((it / S) - 1) & 1)) *errv = 1;
+          if (it >= S && !mbar_wait_cta(&empty[s], ((it / S) - 1) & 1)) *errv = 1;
           if (*errv) break;
           unsigned char* sa = ring + static_cast<size_t>(s) * G::kStageBytes;
           const int kx = (ks * pr.k_chunks + kc) * kGemmKChunk;
@@ -220,7 +220,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       // no copy may still be landing in shared memory when the CTA leaves
       for (int s = 0; s < S; ++s) {
         const int last = last_issued[s];
-        if (last >= 0) mbar_wait(&full[s], (last / S) & 1);
+        if (last >= 0) mbar_wait_cta(&full[s], (last / S) & 1);
       }
     }
   } else if (warp == 1) {
@@ -228,32 +228,49 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       int it = 0, t = 0;
       for (int i = blockIdx.x; i < items && *errv == 0; i += gridDim.x, ++t) {
         const int buf = t & 1, use = t >> 1;
-        if (use >= 1 && !mbar_wait(&tempty[buf], (use - 1) & 1)) {
+        if (use >= 1 && !mbar_wait_cta(&tempty[buf], (use - 1) & 1)) {
           *errv = 1;
           break;
         }
         tmem_fence_after_sync();
         const uint32_t d = tmem + static_cast<uint32_t>(buf * BN);
-        for (int kc = 0; kc < pr.k_chunks; ++kc, ++it) {
-          const int s = it % S;
-          if (!mbar_wait(&full[s], (it / S) & 1)) {
+        // BN <= 128: two stages (K = 128) at a time, waiting for both, then
+        // their 8 MMAs as one straight-line burst (a wait between tcgen05.mma
+        // instructions roughly doubles their issue cost at these widths);
+        // BN = 256: stage by stage (each MMA costs twice as much, and waiting
+        // for a second stage only delays the first)
+        constexpr bool kPairs = BN < 256;
+        for (int kc = 0; kc < pr.k_chunks; kc += kPairs ? 2 : 1) {
+          const bool two = kPairs && kc + 1 < pr.k_chunks;
+          const int s0 = it % S, s1 = (it + 1) % S;
+          bool ok = mbar_wait_cta(&full[s0], (it / S) & 1);
+          if (two) ok = ok && mbar_wait_cta(&full[s1], ((it + 1) / S) & 1);
+          if (!ok) {
             *errv = 1;
             break;
           }
           tmem_fence_after_sync();
-          const unsigned char* sa = ring + static_cast<size_t>(s) * G::kStageBytes;
-          const uint64_t ad = umma_desc_sw128(sa), bd = umma_desc_sw128(sa + G::kABytes);
+          const unsigned char* sa0 = ring + static_cast<size_t>(s0) * G::kStageBytes;
+          const unsigned char* sa1 = ring + static_cast<size_t>(s1) * G::kStageBytes;
+          const uint64_t ad0 = umma_desc_sw128(sa0), bd0 = umma_desc_sw128(sa0 + G::kABytes);
+          const uint64_t ad1 = umma_desc_sw128(sa1), bd1 = umma_desc_sw128(sa1 + G::kABytes);
 #pragma unroll
           for (int kk = 0; kk < kGemmKChunk / 16; ++kk) {
-            umma_bf16(d, ad + 2 * kk, bd + 2 * kk, G::kIdesc, (kc | kk) != 0);
+            umma_bf16(d, ad0 + 2 * kk, bd0 + 2 * kk, G::kIdesc, (kc | kk) != 0);
           }
-          umma_commit(&empty[s]);
+          if (two) {
+#pragma unroll
+            for (int kk = 0; kk < kGemmKChunk / 16; ++kk) umma_bf16(d, ad1 + 2 * kk, bd1 + 2 * kk, G::kIdesc, true);
+          }
+          umma_commit(&empty[s0]);
+          if (two) umma_commit(&empty[s1]);
+          it += two ? 2 : 1;
         }
         umma_commit(&tfull[buf]);
       }
       // every MMA this thread issued has completed before tensor memory is freed
       umma_commit(&fin);
-      mbar_wait(&fin, 0);
+      mbar_wait_cta(&fin, 0);
     }
   } else {
     const int q = warp & 3;             // the tensor-memory lane quadrant this warp may read
@@ -261,7 +278,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     int t = 0;
     for (int i = blockIdx.x; i < items; i += gridDim.x, ++t) {
       const int buf = t & 1, use = t >> 1;
-      const bool ok = *errv == 0 && mbar_wait(&tfull[buf], use & 1);
+      const bool ok = *errv == 0 && mbar_wait_cta(&tfull[buf], use & 1);
       if (!__all_sync(0xffffffffu, ok)) {
         if (lane == 0) *errv = 1;
         break;
