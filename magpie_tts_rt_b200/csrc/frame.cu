@@ -572,15 +572,40 @@ const bf16* tc_rows(const Frame& f) {
 // every row buffer on the 16-byte boundary a tensor map needs).
 bool tc_linear_supported(int d, int F) { return d % 64 == 0 && F % 64 == 0 && d <= 256 * kRowChunks; }
 
+// Weight-tile width (N side) of a phase GEMM: the narrowest of 256 / 128 / 64
+// columns whose tiles (x K splits) still fit in one wave of the SMs.  Few
+// activation rows give few 128-row tiles, and 64-wide weight tiles then put
+// 4x the CTAs on the K loop (each MMA of N = 64 costs ~48 cycles against
+// ~128 at N = 256); large batches keep 256-wide tiles.
+int phase_weight_tile(int m_tiles, int N, int splits) {
+  const int sms = gemm_grid(1 << 30);
+  int bn = 256;
+  for (const int cand : {128, 64}) {
+    if (m_tiles * ((N + cand - 1) / cand) * splits <= sms) bn = cand;
+  }
+  return bn;
+}
+
+template <int BN, int PRO, int EPI>
+cudaError_t launch_linear_tc_bn(const Frame& f, cudaStream_t st, int p, int l, int N, const bf16* bias,
+                                const CUtensorMap& amap, const CUtensorMap& bmap, const GemmProblem& pr) {
+  if constexpr (EPI < 0) {
+    return launch_gemm_tc<BN>(amap, bmap, pr, EpiPhasePart{f.part, f.n * f.rp, N, f.count, f.rp}, st);
+  } else {
+    return launch_gemm_tc<BN>(amap, bmap, pr, EpiPhase<EPI>{f, p, l, N, bias}, st);
+  }
+}
+
 // The GEMM of a tensor-core linear layer (its LayerNorm rows, where it has
 // one, already in `att`); EPI < 0: split-K partial sums into f.part.
 template <int PRO, int EPI>
 cudaError_t launch_linear_tc(const Frame& f, cudaStream_t st, int p, int l, int N, int K, const bf16* W,
                              const bf16* bias, int splits = 1) {
   const int rows_max = f.n * f.rp;
+  const int bn = phase_weight_tile((rows_max + 127) / 128, N, splits);
   CUtensorMap amap, bmap;
   if (!cached_map(&amap, tc_rows<PRO>(f), static_cast<uint64_t>(K), static_cast<uint64_t>(rows_max), 128) ||
-      !cached_map(&bmap, W, static_cast<uint64_t>(K), static_cast<uint64_t>(N), 256)) {
+      !cached_map(&bmap, W, static_cast<uint64_t>(K), static_cast<uint64_t>(N), static_cast<uint32_t>(bn))) {
     return cudaErrorInvalidValue;
   }
   GemmProblem pr;
@@ -594,11 +619,9 @@ cudaError_t launch_linear_tc(const Frame& f, cudaStream_t st, int p, int l, int 
   pr.splits = splits;
   pr.status = nullptr;
   pr.b_constant = 0;
-  if constexpr (EPI < 0) {
-    return launch_gemm_tc<256>(amap, bmap, pr, EpiPhasePart{f.part, rows_max, N, f.count, f.rp}, st);
-  } else {
-    return launch_gemm_tc<256>(amap, bmap, pr, EpiPhase<EPI>{f, p, l, N, bias}, st);
-  }
+  return bn == 64    ? launch_linear_tc_bn<64, PRO, EPI>(f, st, p, l, N, bias, amap, bmap, pr)
+         : bn == 128 ? launch_linear_tc_bn<128, PRO, EPI>(f, st, p, l, N, bias, amap, bmap, pr)
+                     : launch_linear_tc_bn<256, PRO, EPI>(f, st, p, l, N, bias, amap, bmap, pr);
 }
 
 // Identity in-projection (d == 768): x = bf16(src + pos[p]).
