@@ -358,10 +358,10 @@ __global__ void __launch_bounds__(256) ln_rows_kernel(Frame f, const bf16* w) {
 }
 
 // x = bf16(x + bf16(sum of the split GEMM's partials, in split order)), one
-// warp per row; with LN, att = LayerNorm(x) with weights lnw (the next
+// warp per row (large batches); with LN, att = LayerNorm(x) with weights lnw (the next
 // sub-layer's pre-norm).
 template <bool LN>
-__global__ void __launch_bounds__(256) resid_sum_kernel(Frame f, int splits, const bf16* lnw) {
+__global__ void __launch_bounds__(256) resid_sum_rows_kernel(Frame f, int splits, const bf16* lnw) {
   const int rows = *f.count * f.rp;
   const int r = blockIdx.x * 8 + (threadIdx.x >> 5);
   if (r >= rows) return;
@@ -420,6 +420,108 @@ __global__ void __launch_bounds__(256) resid_sum_kernel(Frame f, int splits, con
     }
   }
   if constexpr (LN) ln_row_regs(v, f.d, lnw, f.att + static_cast<int64_t>(r) * f.d);
+}
+
+// The same for small batches (x = bf16(x + bf16(sum of the partials))); with
+// LN, att = LayerNorm(x) with weights lnw (the next sub-layer's pre-norm).
+// A row is spread over d / 256 warps (8 features a lane) and a CTA holds two
+// rows, so that every split's slice of the row is loaded before the first
+// add (the sums still run split by split, in order); the LayerNorm's row sums
+// cross the row's warps through shared memory.
+template <bool LN>
+__global__ void __launch_bounds__(256) resid_sum_wide_kernel(Frame f, int splits, const bf16* lnw) {
+  __shared__ float red[2][4][2];  // [row of the CTA][warp of the row][sum, squared deviations]
+  const int wpr = (f.d + 255) / 256;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int rl = warp / wpr, part = warp % wpr;
+  const int rows = *f.count * f.rp;
+  const int r = 2 * static_cast<int>(blockIdx.x) + rl;
+  const int k = 256 * part + 8 * lane;
+  const bool has = r < rows && k < f.d;
+  const int64_t rows_max = static_cast<int64_t>(f.n) * f.rp;
+  bf16* xr = f.x + static_cast<int64_t>(r) * f.d;
+  uint4 xv = make_uint4(0, 0, 0, 0);
+  float4 pv[kMaxPhaseSplits][2];
+  if (has) {
+    xv = *reinterpret_cast<const uint4*>(xr + k);
+#pragma unroll
+    for (int sp = 0; sp < kMaxPhaseSplits; ++sp) {
+      if (sp < splits) {
+        const float4* pp = reinterpret_cast<const float4*>(f.part + (sp * rows_max + r) * f.d + k);
+        pv[sp][0] = pp[0];
+        pv[sp][1] = pp[1];
+      }
+    }
+  }
+  float v[8];
+  {
+    float acc[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[j] = 0.f;
+#pragma unroll
+    for (int sp = 0; sp < kMaxPhaseSplits; ++sp) {
+      if (has && sp < splits) {
+        acc[0] += pv[sp][0].x; acc[1] += pv[sp][0].y; acc[2] += pv[sp][0].z; acc[3] += pv[sp][0].w;
+        acc[4] += pv[sp][1].x; acc[5] += pv[sp][1].y; acc[6] += pv[sp][1].z; acc[7] += pv[sp][1].w;
+      }
+    }
+    float a[8];
+    unpack8(xv, a);
+    __align__(16) bf16 o8[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      o8[j] = f2bf(__fadd_rn(a[j], round_bf16(acc[j])));
+      v[j] = has ? bf2f(o8[j]) : 0.f;
+    }
+    if (has) *reinterpret_cast<uint4*>(xr + k) = *reinterpret_cast<const uint4*>(o8);
+  }
+  if constexpr (LN) {
+    float sum = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) sum += v[j];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    if (lane == 0 && rl < 2) red[rl][part][0] = sum;
+    __syncthreads();
+    float tot = 0.f;
+    for (int q = 0; q < wpr; ++q) tot += red[rl < 2 ? rl : 0][q][0];
+    const float mean = tot / static_cast<float>(f.d);
+    float sq = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float dlt = v[j] - mean;
+      sq += has ? dlt * dlt : 0.f;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
+    if (lane == 0 && rl < 2) red[rl][part][1] = sq;
+    __syncthreads();
+    float var = 0.f;
+    for (int q = 0; q < wpr; ++q) var += red[rl < 2 ? rl : 0][q][1];
+    const float rstd = 1.0f / sqrtf(var / static_cast<float>(f.d) + 1.0e-5f);
+    if (has) {
+      float g[8];
+      unpack8(*reinterpret_cast<const uint4*>(lnw + k), g);
+      __align__(16) bf16 o8[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) o8[j] = f2bf(((v[j] - mean) * rstd) * g[j]);
+      *reinterpret_cast<uint4*>(f.att + static_cast<int64_t>(r) * f.d + k) = *reinterpret_cast<const uint4*>(o8);
+    }
+  }
+}
+
+
+// The residual sum of a split GEMM: rows over d / 256 warps each while one
+// warp per row would leave SMs idle (fewer than 8 rows per SM), one warp per
+// row above that (measured faster for large batches).
+template <bool LN>
+void launch_resid_sum(const Frame& f, int splits, const bf16* lnw, cudaStream_t st) {
+  const int rows_max = f.n * f.rp;
+  if ((rows_max + 7) / 8 < gemm_grid(1 << 30)) {
+    resid_sum_wide_kernel<LN><<<(rows_max + 1) / 2, 64 * ((f.d + 255) / 256), 0, st>>>(f, splits, lnw);
+  } else {
+    resid_sum_rows_kernel<LN><<<(rows_max + 7) / 8, 256, 0, st>>>(f, splits, lnw);
+  }
 }
 
 // Epilogues of the tensor-core linear layers.  A lane holds 32 consecutive
@@ -522,7 +624,7 @@ struct EpiPhase {
 };
 
 // Split-K partial sums of a residual GEMM: part[ks][r][n] (f32), summed by
-// resid_sum_kernel; staged like EpiPhase, 16 columns (64 bytes per row) at a
+// launch_resid_sum; staged like EpiPhase, 16 columns (64 bytes per row) at a
 // time.
 constexpr int kPhaseStageRowF = 20;  // f32 per staged row (64 bytes + 16 of padding)
 struct EpiPhasePart {
@@ -1108,7 +1210,7 @@ extern "C" MTT_B200_API int mtt_b200_launch_local_ar_frame(const mtt_b200_local_
   // Tensor-core layers: LayerNorm rows come out of the kernel before each
   // GEMM (the in-projection / position add, the residual sum of the previous
   // split GEMM, or ln_rows_kernel); the o-projection and FFN2 split K and sum
-  // their partials in resid_sum_kernel (the benchmark shape: no split, the
+  // their partials in launch_resid_sum (the benchmark shape: no split, the
   // residual added in the GEMM epilogue).
   const bool tc = tc_linear_supported(f.d, f.F);
   const bool split = !fused_frame_shape(f.d, f.L, f.F);
@@ -1144,7 +1246,7 @@ extern "C" MTT_B200_API int mtt_b200_launch_local_ar_frame(const mtt_b200_local_
         cudaError_t e;
         if (split) {
           e = launch_linear_tc<kProAtt, -1>(f, st, p, l, d, d, f.o + l * dd, nullptr, split_o);
-          if (e == cudaSuccess) resid_sum_kernel<true><<<row_blocks, 256, 0, st>>>(f, split_o, ln2);
+          if (e == cudaSuccess) launch_resid_sum<true>(f, split_o, ln2, st);
         } else {
           e = launch_linear_tc<kProAtt, kEpiResid>(f, st, p, l, d, d, f.o + l * dd, nullptr);
           if (e == cudaSuccess) ln_rows_kernel<<<row_blocks, 256, 0, st>>>(f, ln2);
@@ -1153,9 +1255,9 @@ extern "C" MTT_B200_API int mtt_b200_launch_local_ar_frame(const mtt_b200_local_
         if (e == cudaSuccess && split) {
           e = launch_linear_tc<kProH, -1>(f, st, p, l, d, F, w2, nullptr, split_f);
           if (e == cudaSuccess && ln_next != nullptr) {
-            resid_sum_kernel<true><<<row_blocks, 256, 0, st>>>(f, split_f, ln_next);
+            launch_resid_sum<true>(f, split_f, ln_next, st);
           } else if (e == cudaSuccess) {
-            resid_sum_kernel<false><<<row_blocks, 256, 0, st>>>(f, split_f, nullptr);
+            launch_resid_sum<false>(f, split_f, nullptr, st);
           }
         } else if (e == cudaSuccess) {
           e = launch_linear_tc<kProH, kEpiResid>(f, st, p, l, d, F, w2, nullptr);
