@@ -730,16 +730,39 @@ cudaError_t launch_linear_tc(const Frame& f, cudaStream_t st, int p, int l, int 
 // Identity in-projection: x = bf16(src + pos[p]), src the decoder hidden row
 // (p = 0) or the embedding of the previous position's token; one warp per
 // row.  With LN (tensor-core layers) it also writes att = LN1_0(x).
+__device__ __forceinline__ void pos_row(const Frame& f, int r, const bf16* src, int p);
+
 template <bool LN>
 __global__ void __launch_bounds__(256) add_pos_kernel(Frame f, int p) {
   const int rows = *f.count * f.rp;
   const int r = blockIdx.x * 8 + (threadIdx.x >> 5);
   if (r >= rows) return;
-  const int lane = threadIdx.x & 31;
   const int i = r / f.rp, sub = r % f.rp;
   const int s = f.list[i];
   const bf16* src = p == 0 ? f.hidden + (static_cast<int64_t>(s) * f.rp + sub) * kEmbed
                            : f.emb + (static_cast<int64_t>(p - 1) * kVocab + input_token(f, s, p - 1)) * kEmbed;
+  if constexpr (LN) {
+    pos_row(f, r, src, p);
+  } else {
+    const int lane = threadIdx.x & 31;
+    const bf16* pos = f.pos + static_cast<int64_t>(p) * f.d;
+    bf16* xr = f.x + static_cast<int64_t>(r) * f.d;
+    for (int k = lane * 8; k < f.d; k += 256) {
+      float a[8], b[8];
+      unpack8(*reinterpret_cast<const uint4*>(src + k), a);
+      unpack8(*reinterpret_cast<const uint4*>(pos + k), b);
+      __align__(16) bf16 o8[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) o8[j] = f2bf(__fadd_rn(a[j], b[j]));
+      *reinterpret_cast<uint4*>(xr + k) = *reinterpret_cast<const uint4*>(o8);
+    }
+  }
+}
+
+// Row r of the identity in-projection at position p, one warp: x = bf16(src +
+// pos[p]) and att = LN1_0(x).
+__device__ __forceinline__ void pos_row(const Frame& f, int r, const bf16* src, int p) {
+  const int lane = threadIdx.x & 31;
   const bf16* pos = f.pos + static_cast<int64_t>(p) * f.d;
   bf16* xr = f.x + static_cast<int64_t>(r) * f.d;
   float v[8 * kRowChunks];
@@ -753,17 +776,15 @@ __global__ void __launch_bounds__(256) add_pos_kernel(Frame f, int p) {
 #pragma unroll
     for (int j = 0; j < 8; ++j) o8[j] = f2bf(__fadd_rn(a[j], b[j]));
     *reinterpret_cast<uint4*>(xr + k) = *reinterpret_cast<const uint4*>(o8);
-    if constexpr (LN) {
 #pragma unroll
-      for (int cc = 0; cc < kRowChunks; ++cc) {
-        if (cc == c) {
+    for (int cc = 0; cc < kRowChunks; ++cc) {
+      if (cc == c) {
 #pragma unroll
-          for (int j = 0; j < 8; ++j) v[8 * cc + j] = bf2f(o8[j]);
-        }
+        for (int j = 0; j < 8; ++j) v[8 * cc + j] = bf2f(o8[j]);
       }
     }
   }
-  if constexpr (LN) ln_row_regs(v, f.d, f.ln1, f.att + static_cast<int64_t>(r) * f.d);
+  ln_row_regs(v, f.d, f.ln1, f.att + static_cast<int64_t>(r) * f.d);
 }
 
 // ---------------------------------------------------------------------------
@@ -856,6 +877,10 @@ __global__ void __launch_bounds__(256) attention_kernel(Frame f, int p, int l) {
 // sampling + running embedding sum
 // ---------------------------------------------------------------------------
 
+// NEXT (identity in-projection, tensor-core layers): the CTA also writes the
+// next position's input rows of its session and their LN1 (what
+// add_pos_kernel<true> would do), one warp per row.
+template <bool NEXT>
 __global__ void __launch_bounds__(kSampleThreads) sample_kernel(Frame f, int p) {
   __shared__ SampleShared sh;
   __shared__ __align__(16) unsigned char scratch[kSampleScratchBytes];
@@ -884,6 +909,17 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(Frame f, int p) 
   for (int k = threadIdx.x; k < kEmbed; k += blockDim.x) {
     const float v = bf2f(row[k]);
     acc[k] = p == 0 ? v : round_bf16(__fadd_rn(acc[k], v));
+  }
+  if constexpr (NEXT) {
+    const int warp = threadIdx.x >> 5;
+    if (p + 1 < kPositions && warp < f.rp) {
+      int64_t tin = token;
+      if (f.forced) {
+        const int64_t t = f.forced[static_cast<int64_t>(s) * kPositions + p];
+        tin = t < 0 ? 0 : (t >= kVocab ? kVocab - 1 : t);
+      }
+      pos_row(f, i * f.rp + warp, f.emb + (static_cast<int64_t>(p) * kVocab + tin) * kEmbed, p + 1);
+    }
   }
 }
 
@@ -1077,10 +1113,13 @@ extern "C" MTT_B200_API int32_t mtt_b200_local_ar_frame_launch_count(const mtt_b
   // layers) or position add, the layers, head, sampling; EOS rows and
   // projection GEMM; end
   if (mtt::tc_linear_supported(shape->d_model, shape->d_ffn)) {
-    // 7 per layer; without the split, no LayerNorm launch after the last FFN2
-    const int in_proj = shape->d_model != mtt::kEmbed ? 2 : 1;
+    // 7 per layer; without the split, no LayerNorm launch after the last FFN2;
+    // with the identity in-projection only position 0 has a position-add
+    // launch (the sampling kernel writes the next position's rows)
     const int last = mtt::fused_frame_shape(shape->d_model, shape->n_layers, shape->d_ffn) ? 1 : 0;
-    return 1 + mtt::kPositions * (in_proj + 7 * shape->n_layers - last + 2) + 3;
+    const int per_position = 7 * shape->n_layers - last + 2;
+    if (shape->d_model != mtt::kEmbed) return 1 + mtt::kPositions * (2 + per_position) + 3;
+    return 1 + 1 + mtt::kPositions * per_position + 3;
   }
   return 1 + mtt::kPositions * (1 + 5 * shape->n_layers + 2) + 3;
 }
@@ -1227,7 +1266,8 @@ extern "C" MTT_B200_API int mtt_b200_launch_local_ar_frame(const mtt_b200_local_
       }
       if (tc) ln_rows_kernel<<<row_blocks, 256, 0, st>>>(f, f.ln1);
     } else if (tc) {
-      add_pos_kernel<true><<<row_blocks, 256, 0, st>>>(f, p);
+      // position p >= 1's rows come from the previous position's sampling kernel
+      if (p == 0) add_pos_kernel<true><<<row_blocks, 256, 0, st>>>(f, p);
     } else {
       add_pos_kernel<false><<<row_blocks, 256, 0, st>>>(f, p);
     }
@@ -1281,7 +1321,11 @@ extern "C" MTT_B200_API int mtt_b200_launch_local_ar_frame(const mtt_b200_local_
     } else {
       launch_linear<kProX, kEpiHead>(f, st, p, 0, kVocab, d, hw, hb);
     }
-    sample_kernel<<<f.n, kSampleThreads, 0, st>>>(f, p);
+    if (tc && !in_proj) {
+      sample_kernel<true><<<f.n, kSampleThreads, 0, st>>>(f, p);
+    } else {
+      sample_kernel<false><<<f.n, kSampleThreads, 0, st>>>(f, p);
+    }
   }
   if (f.final_w != nullptr && f.eos_pre == nullptr && launch_eos_projection(frame_eos_args(f), st) != cudaSuccess) {
     return MTT_B200_STATUS_CUDA_ERROR;

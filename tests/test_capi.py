@@ -92,8 +92,10 @@ def test_workspace_sizes():
     phase = L.SamplingConfig(80, 0.6, 2.5, 0, 1, L.PATH_PHASE_KERNELS)
     # begin + 16 x (in-projection, LN rows, 6 layer launches, head, sampling) + EOS rows, EOS GEMM, end
     assert L.lib.mtt_b200_local_ar_frame_launch_count(ctypes.byref(ok), ctypes.byref(phase), 64) == 1 + 16 * 10 + 3
-    sofia = L.Shape(768, 2, 12, 3072)  # identity in-projection: the position add writes the LN rows
-    assert L.lib.mtt_b200_local_ar_frame_launch_count(ctypes.byref(sofia), ctypes.byref(phase), 64) == 1 + 16 * 17 + 3
+    # identity in-projection: the position add (position 0) or the previous position's sampling kernel
+    # writes the rows and their LN
+    sofia = L.Shape(768, 2, 12, 3072)
+    assert L.lib.mtt_b200_local_ar_frame_launch_count(ctypes.byref(sofia), ctypes.byref(phase), 64) == 1 + 1 + 16 * 16 + 3
     assert L.lib.mtt_b200_local_ar_frame_path(ctypes.byref(ok), ctypes.byref(phase), 64) == L.PATH_PHASE_KERNELS
     assert L.lib.mtt_b200_local_ar_frame_path(ctypes.byref(ok), ctypes.byref(phase), 0) == -1
     bad_path = L.SamplingConfig(80, 0.6, 2.5, 0, 1, 99)
