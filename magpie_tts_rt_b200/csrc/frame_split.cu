@@ -215,6 +215,11 @@ __device__ __forceinline__ int err_flag(const SplitSmem<C, R>& sm) {
 }
 __device__ __forceinline__ void cbar() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
 
+// Phase clock stamp of the first CTA (library trace hook: mtt_b200_test_frame_trace).
+__device__ __forceinline__ void s_stamp(const Frame& f, bool tracer, int p, int i) {
+  if (tracer) f.trace[kPositions * p + i] = static_cast<uint64_t>(clock64());
+}
+
 // Byte offset of element (row r, column k) of an R-row operand stored as
 // 64-column panels with the 128-byte swizzle.
 template <int R>
@@ -890,8 +895,11 @@ __global__ void __launch_bounds__(kSThreads, 1) split_frame_kernel(Frame f, cons
     int mb = 0;          // M-blocks consumed
     uint32_t rd = 0;     // exchange rounds
     int src_pieces = 0;  // in-projection input pieces staged (32-row tiles)
+    const bool tracer = f.trace != nullptr && blockIdx.x == 0 && threadIdx.x == 0;
+    if (tracer) f.trace[256] = static_cast<uint64_t>(clock64()), f.trace[257] = global_ns();
     for (int p = 0; p < kPositions; ++p) {
       // ---------------- input rows
+      s_stamp(f, tracer, p, 0);
       if (has_in_projection(folded, p)) {
         // the rows' 768 inputs (p = 0: decoder hidden; else the sampled token's
         // embedding), whole or in pieces of 256 columns per M-block
@@ -957,6 +965,7 @@ __global__ void __launch_bounds__(kSThreads, 1) split_frame_kernel(Frame f, cons
       // ---------------- LN1, qkv of the CTA's heads
       layer_norm_op<R>(sm.x, sm.xa, g1);
       operand_ready(sm);
+      s_stamp(f, tracer, p, 1);
       for (int b = 0; b < K::nq; ++b, ++mb) {
         float v[R / 2];
         load_block(sm, mb, v);
@@ -969,14 +978,17 @@ __global__ void __launch_bounds__(kSThreads, 1) split_frame_kernel(Frame f, cons
       }
       cbar();
 
+      s_stamp(f, tracer, p, 2);
       // ---------------- attention (R1: the heads' outputs to every CTA)
       attention<C, R>(sm, p, c, rd);
+      s_stamp(f, tracer, p, 3);
       if constexpr (C > 1) {
         finish_round(sm, rd, static_cast<uint32_t>((C - 1) * K::att_rows * kHeadDim * K::nh * 2));
         fence_proxy_async();
       }
       operand_ready(sm);
 
+      s_stamp(f, tracer, p, 4);
       // ---------------- o-projection + residual (R2: the CTA's features to every CTA)
       for (int b = 0; b < K::no; ++b, ++mb) {
         float v[R / 2];
@@ -1010,9 +1022,11 @@ __global__ void __launch_bounds__(kSThreads, 1) split_frame_kernel(Frame f, cons
         finish_round(sm, rd, static_cast<uint32_t>((C - 1) * R * K::of * 2));
       }
 
+      s_stamp(f, tracer, p, 5);
       // ---------------- LN2, FFN1 + GELU
       layer_norm_op<R>(sm.x, sm.xa, g2);
       operand_ready(sm);
+      s_stamp(f, tracer, p, 6);
       for (int b = 0; b < K::nf1; ++b, ++mb) {
         float v[R / 2];
         load_block(sm, mb, v);
@@ -1022,6 +1036,7 @@ __global__ void __launch_bounds__(kSThreads, 1) split_frame_kernel(Frame f, cons
       }
       operand_ready(sm);
 
+      s_stamp(f, tracer, p, 7);
       // ---------------- FFN2 (+ R3 reduce-scatter, R4 all-gather) + residual
       float own_part[R / 2];  // 32-row tiles: this CTA's partials of its own features
 #pragma unroll
@@ -1057,7 +1072,9 @@ __global__ void __launch_bounds__(kSThreads, 1) split_frame_kernel(Frame f, cons
         }
       }
       if constexpr (C > 1) {
+        s_stamp(f, tracer, p, 8);
         finish_round(sm, rd, static_cast<uint32_t>((C - 1) * R * K::of * 4));
+        s_stamp(f, tracer, p, 9);
         if constexpr (K::red_slots == C) {
           constexpr int upr = K::of / 8;
           for (int i = threadIdx.x; i < R * upr; i += kSC) {
@@ -1098,6 +1115,7 @@ __global__ void __launch_bounds__(kSThreads, 1) split_frame_kernel(Frame f, cons
       x_to_operand<R>(sm.x, sm.ab);
       operand_ready(sm);
 
+      s_stamp(f, tracer, p, 10);
       // ---------------- head p: bias, CFG combine, constraints (R5: values to the owners)
       {
         bf16* lo_base = f.logits_out;
@@ -1151,6 +1169,7 @@ __global__ void __launch_bounds__(kSThreads, 1) split_frame_kernel(Frame f, cons
           }
         }
         cbar();
+        s_stamp(f, tracer, p, 11);
         if constexpr (C > 1) {
           // the other CTAs' sessions: this CTA's vocabulary slice of each, and its non-finite flags
           constexpr int full_units = K::vs / 8;
@@ -1183,6 +1202,7 @@ __global__ void __launch_bounds__(kSThreads, 1) split_frame_kernel(Frame f, cons
           finish_round(sm, rd, values_bytes_in<C, R>(c));
         }
       }
+      s_stamp(f, tracer, p, 12);
 
       // ---------------- sampling (R6: the token to every CTA): one warp per owned
       // session, or a group of 8 / own >= 4 warps per session
@@ -1239,6 +1259,7 @@ __global__ void __launch_bounds__(kSThreads, 1) split_frame_kernel(Frame f, cons
           }
         }
       }
+      s_stamp(f, tracer, p, 13);
       if constexpr (C > 1) {
         if (p + 1 < kPositions) {
           // dead owned slots still announce their 4 bytes: push a zero token for them
@@ -1258,6 +1279,7 @@ __global__ void __launch_bounds__(kSThreads, 1) split_frame_kernel(Frame f, cons
         cbar();
       }
 
+      s_stamp(f, tracer, p, 14);
       // ---------------- next input rows (folded tables), every CTA, all sessions
       if (folded && p + 1 < kPositions) {
         for (int slot = warp; slot < n_sess; slot += kSW) {
@@ -1276,8 +1298,10 @@ __global__ void __launch_bounds__(kSThreads, 1) split_frame_kernel(Frame f, cons
         }
       }
       cbar();
+      s_stamp(f, tracer, p, 15);
     }
 
+    if (tracer) f.trace[258] = static_cast<uint64_t>(clock64()), f.trace[259] = global_ns();
     // ---- commit (owned sessions): tokens, counters, flags, next-frame embedding
     for (int i = threadIdx.x; i < n_own * kPositions; i += kSC) {
       const int ls = i / kPositions, pp = i % kPositions;
