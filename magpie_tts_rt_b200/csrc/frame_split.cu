@@ -597,9 +597,156 @@ __device__ __forceinline__ uint32_t values_bytes_in(int c) {
 // and pushed to every peer.
 // ---------------------------------------------------------------------------
 
+// Four 32-bit TMEM columns of lane (lane field of taddr) + t stored by thread t.
+__device__ __forceinline__ void tmem_st4(uint32_t taddr, const uint32_t (&v)[4]) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1,%2,%3,%4};" ::"r"(taddr), "r"(v[0]), "r"(v[1]), "r"(v[2]),
+               "r"(v[3])
+               : "memory");
+}
+
+// 32 columns of the warp's lanes, then the wait (one wait for the whole load).
+__device__ __forceinline__ void tmem_ld32w(uint32_t (&v)[32], uint32_t taddr) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,"
+      "%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
+        "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]), "=r"(v[16]),
+        "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]),
+        "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+      : "r"(taddr)
+      : "memory");
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(v[0]), "+r"(v[1]), "+r"(v[2]), "+r"(v[3]), "+r"(v[4]), "+r"(v[5]), "+r"(v[6]), "+r"(v[7]),
+                 "+r"(v[8]), "+r"(v[9]), "+r"(v[10]), "+r"(v[11]), "+r"(v[12]), "+r"(v[13]), "+r"(v[14]), "+r"(v[15]),
+                 "+r"(v[16]), "+r"(v[17]), "+r"(v[18]), "+r"(v[19]), "+r"(v[20]), "+r"(v[21]), "+r"(v[22]),
+                 "+r"(v[23]), "+r"(v[24]), "+r"(v[25]), "+r"(v[26]), "+r"(v[27]), "+r"(v[28]), "+r"(v[29]),
+                 "+r"(v[30]), "+r"(v[31])
+               :
+               : "memory");
+}
+
+// Attention with one head per CTA and 16-row tiles (C = 4, 8), spread over
+// all four TMEM lane quadrants so that all eight consumer warps attend: lane
+// 32 q + l holds row 4 q + l / 8, head dims [8 (l % 8), +8); K of position j
+// at columns 4 b(j), V at 64 + 4 b(j) (b(j) = 8 (j mod 2) + j / 2, so each
+// parity's positions are 32 contiguous columns); positions 0..15 all cached.
+// Warp w reads quadrant w % 4 and takes the positions of parity w / 4; the
+// score of a position is summed over the 8 lanes of its row, rounded as the
+// reference rounds it (bf16, x 1/8, bf16); the softmax sum runs over the
+// positions in order; the odd warp's partial output joins the even warp's.
+template <int C, int R>
+__device__ __forceinline__ void attention_spread(SplitSmem<C, R>& sm, int p, int c, uint32_t rd) {
+  using K = Cfg<C, R>;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int q4 = warp & 3, part = warp >> 2;
+  const int r = 4 * q4 + (lane >> 3), u = lane & 7;
+  const uint32_t tl = sm.tmem + (static_cast<uint32_t>(32 * q4) << 16);
+  const bf16* qrow = sm.q.qkv + r * K::ldq + 8 * u;  // the CTA's head: q, then k, then v
+  {  // append k (part 0) or v (part 1) of position p
+    const uint4 t = *reinterpret_cast<const uint4*>(qrow + kHeadDim * (1 + part));
+    const uint32_t kv[4] = {t.x, t.y, t.z, t.w};
+    tmem_st4(tl + 64u * static_cast<uint32_t>(part) + 4u * static_cast<uint32_t>(tmem_block(p)), kv);
+    tmem_wait_st();
+  }
+  float q[8];
+  unpack8(*reinterpret_cast<const uint4*>(qrow), q);
+  tmem_fence_before_sync();
+  cbar();
+  tmem_fence_after_sync();
+  float s[8];
+  {
+    uint32_t kv[32];
+    tmem_ld32w(kv, tl + 32u * static_cast<uint32_t>(part));
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      float d0 = 0.f, d1 = 0.f;
+#pragma unroll
+      for (int e = 0; e < 4; e += 2) {
+        const float2 t0 = __bfloat1622float2(bf2_of(kv[4 * i + e]));
+        const float2 t1 = __bfloat1622float2(bf2_of(kv[4 * i + e + 1]));
+        d0 = fmaf(q[2 * e], t0.x, d0);
+        d0 = fmaf(q[2 * e + 1], t0.y, d0);
+        d1 = fmaf(q[2 * e + 2], t1.x, d1);
+        d1 = fmaf(q[2 * e + 3], t1.y, d1);
+      }
+      float dot = d0 + d1;
+      dot += __shfl_xor_sync(0xffffffffu, dot, 1);
+      dot += __shfl_xor_sync(0xffffffffu, dot, 2);
+      dot += __shfl_xor_sync(0xffffffffu, dot, 4);
+      s[i] = 2 * i + part <= p ? round_bf16(__fmul_rn(round_bf16(dot), 0.125f)) : -CUDART_INF_F;
+    }
+  }
+  float* my_s = sm.u.att.s[part][q4][lane];
+#pragma unroll
+  for (int m = 0; m < 8; ++m) my_s[m] = s[m];
+  cbar();
+  float all[kPositions];
+#pragma unroll
+  for (int m = 0; m < 8; ++m) {
+    all[2 * m] = sm.u.att.s[0][q4][lane][m];
+    all[2 * m + 1] = sm.u.att.s[1][q4][lane][m];
+  }
+  float mx = all[0];
+#pragma unroll
+  for (int j = 1; j < kPositions; ++j) mx = fmaxf(mx, all[j]);
+  float sum = 0.f;
+#pragma unroll
+  for (int j = 0; j < kPositions; ++j) {
+    all[j] = j <= p ? expf(all[j] - mx) : 0.f;
+    sum += all[j];
+  }
+  float o[8];
+#pragma unroll
+  for (int d = 0; d < 8; ++d) o[d] = 0.f;
+  {
+    uint32_t vv[32];
+    tmem_ld32w(vv, tl + 64u + 32u * static_cast<uint32_t>(part));
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      if (2 * i + part <= p) {
+        // select between two compile-time indices (a runtime index would put `all` in local memory)
+        const float e = part ? all[2 * i + 1] : all[2 * i];
+        const float prob = round_bf16(e / sum);
+#pragma unroll
+        for (int d = 0; d < 4; ++d) {
+          const float2 t = __bfloat1622float2(bf2_of(vv[4 * i + d]));
+          o[2 * d] = fmaf(prob, t.x, o[2 * d]);
+          o[2 * d + 1] = fmaf(prob, t.y, o[2 * d + 1]);
+        }
+      }
+    }
+  }
+  if (part == 1) {
+    float* dst = sm.u.att.o[q4][lane];
+#pragma unroll
+    for (int d = 0; d < 8; ++d) dst[d] = o[d];
+  }
+  cbar();
+  if (part == 0) {
+    const float* src = sm.u.att.o[q4][lane];
+#pragma unroll
+    for (int d = 0; d < 8; ++d) o[d] += src[d];
+    const int col = kHeadDim * head_base<C, R>(c) + 8 * u;
+    const bool send = C <= kHeads || (r >> 3) == (c & 1);
+    const uint4 w = pack8(o);
+    uint4* dst = op_unit<R>(sm.ab, r, col);
+    *dst = w;
+    if (send) {
+#pragma unroll
+      for (int jc = 0; jc < C; ++jc) {
+        if (jc != c) st_async_v4(cluster_addr(dst, jc), w, cluster_addr(&sm.xbar[rd & 1u], jc));
+      }
+    }
+  }
+}
+
 template <int C, int R>
 __device__ __forceinline__ void attention(SplitSmem<C, R>& sm, int p, int c, uint32_t rd) {
   using K = Cfg<C, R>;
+  if constexpr (K::nh == 1 && R == 16) {
+    attention_spread<C, R>(sm, p, c, rd);
+    return;
+  }
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int q4 = warp & 3, part = warp >> 2;
   const int lh = R == 32 ? q4 >> 1 : q4;  // local head of this quadrant
