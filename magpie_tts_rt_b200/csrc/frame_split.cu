@@ -1270,6 +1270,9 @@ __global__ void __launch_bounds__(kSThreads, 1) split_frame_kernel(Frame f, cons
         // between FFN1 and the next position's LN1), [non-owned slot][vs]
         uint16_t* out32 = reinterpret_cast<uint16_t*>(sm.xa);
         constexpr int H = R / 4;  // sessions per warp half
+        uint32_t fl[H];           // flags of the thread's sessions H sh + i (0 for dead slots)
+#pragma unroll
+        for (int i = 0; i < H; ++i) fl[i] = H * sh + i < n_sess ? sm.flags[H * sh + i] : 0u;
         for (int b = 0; b < K::nhb; ++b, ++mb) {
           float v[R / 2];
           load_block(sm, mb, v);
@@ -1277,41 +1280,64 @@ __global__ void __launch_bounds__(kSThreads, 1) split_frame_kernel(Frame f, cons
           const int t = K::vs * c + vl;
           const bool in_vocab = t < kVocab;
           const float bias = bf2f(sm.hb[vl]);
+          uint32_t nfm = 0;   // non-finite guided logit, bit i: session H sh + i
+          uint32_t keys[H];
 #pragma unroll
-          for (int i = 0; i < H; ++i) {
-            const int slot = H * sh + i;
-            bool nfs = false;
-            uint32_t key = 0;
-            if (in_vocab && slot < n_sess) {
-              const __nv_bfloat16 cb = f2bf(__fadd_rn(v[i], bias));
-              const __nv_bfloat16 ub = f2bf(__fadd_rn(v[H + i], bias));
-              if (lo_base) {
-                bf16* lr = lo_base + (static_cast<int64_t>(sm.sess[slot]) * kPositions + p) * rp * kVocab;
-                lr[t] = cb;
-                if (cfg) lr[kVocab + t] = ub;
-              }
-              uint32_t g = __bfloat16_as_ushort(cb);
-              if (cfg) {
-                const float sc = round_bf16(__fmul_rn(bf2f(cb), cfg_scale));
-                g = __bfloat16_as_ushort(f2bf(__fadd_rn(sc, __fmul_rn(bf2f(ub), uncond_scale))));
-              }
-              const uint32_t fl = sm.flags[slot];
-              const uint16_t val =
-                  static_cast<uint16_t>(constrain(g, t, fl & 1u, (fl & 2u) != 0, (fl & 4u) != 0, nfs));
-              key = sample_key(val);
-              const int owner = slot / K::own;
-              if (owner == c) {
-                sm.u.v.own[slot - own0][t] = val;
-              } else if constexpr (R == 16) {
-                sm.u.v.out[slot][vl] = val;
-              } else {
-                out32[(slot < own0 ? slot : slot - K::own) * K::vs + vl] = val;
+          for (int i = 0; i < H; i += 2) {  // sessions H sh + i and + 1 as the halves of bf16x2 values
+            const uint32_t c2 = pack2_rn(__fadd_rn(v[i], bias), __fadd_rn(v[i + 1], bias));
+            const uint32_t u2 = pack2_rn(__fadd_rn(v[H + i], bias), __fadd_rn(v[H + i + 1], bias));
+            if (lo_base && in_vocab) {
+#pragma unroll
+              for (int h = 0; h < 2; ++h) {
+                const int slot = H * sh + i + h;
+                if (slot < n_sess) {
+                  uint16_t* lr = reinterpret_cast<uint16_t*>(lo_base) +
+                                 (static_cast<int64_t>(sm.sess[slot]) * kPositions + p) * rp * kVocab;
+                  lr[t] = static_cast<uint16_t>(h ? c2 >> 16 : c2 & 0xffffu);
+                  if (cfg) lr[kVocab + t] = static_cast<uint16_t>(h ? u2 >> 16 : u2 & 0xffffu);
+                }
               }
             }
-            if (__any_sync(0xffffffffu, nfs) && lane == 0) atomicOr(&sm.nf[slot], 1u);
-            if constexpr (K::sw > 1) {  // the group sampler takes the row maximum from here
-              const uint32_t km = __reduce_max_sync(0xffffffffu, key);
-              if (lane == 0 && km != 0) atomicMax(&sm.vmax[slot], km);
+            const uint32_t g2 = cfg ? guided_value2(c2, u2, cfg_scale, uncond_scale) : c2;
+            uint32_t g0 = g2 & 0xffffu, g1 = g2 >> 16;
+            // constraints only where they can change a value: specials, non-finite values, finished rows
+            if (t >= kCodebook || (g0 & 0x7f80u) == 0x7f80u || (g1 & 0x7f80u) == 0x7f80u || ((fl[i] | fl[i + 1]) & 2u)) {
+              bool n0 = false, n1 = false;
+              g0 = constrain(g0, t, fl[i] & 1u, (fl[i] & 2u) != 0, (fl[i] & 4u) != 0, n0);
+              g1 = constrain(g1, t, fl[i + 1] & 1u, (fl[i + 1] & 2u) != 0, (fl[i + 1] & 4u) != 0, n1);
+              nfm |= (n0 ? 1u : 0u) << i | (n1 ? 1u : 0u) << (i + 1);
+            }
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              const int slot = H * sh + i + h;
+              const uint32_t val = h ? g1 : g0;
+              const bool live = in_vocab && slot < n_sess;
+              keys[i + h] = live ? sample_key(val) : 0u;
+              if (!live) continue;
+              const int owner = slot / K::own;
+              if (owner == c) {
+                sm.u.v.own[slot - own0][t] = static_cast<uint16_t>(val);
+              } else if constexpr (R == 16) {
+                sm.u.v.out[slot][vl] = static_cast<uint16_t>(val);
+              } else {
+                out32[(slot < own0 ? slot : slot - K::own) * K::vs + vl] = static_cast<uint16_t>(val);
+              }
+            }
+          }
+          if (!in_vocab) nfm = 0;
+          nfm &= (1u << (n_sess - H * sh < 0 ? 0 : (n_sess - H * sh < H ? n_sess - H * sh : H))) - 1u;
+          const uint32_t any = __reduce_or_sync(0xffffffffu, nfm);
+          if (lane == 0 && any != 0) {
+#pragma unroll
+            for (int i = 0; i < H; ++i) {
+              if (any & (1u << i)) atomicOr(&sm.nf[H * sh + i], 1u);
+            }
+          }
+          if constexpr (K::sw > 1) {  // the group sampler takes the row maximum from here
+#pragma unroll
+            for (int i = 0; i < H; ++i) {
+              const uint32_t km = __reduce_max_sync(0xffffffffu, keys[i]);
+              if (lane == 0 && km != 0) atomicMax(&sm.vmax[H * sh + i], km);
             }
           }
         }
