@@ -94,7 +94,8 @@ def parse():
                     help="run only the d=768 / 2-layer Local AR frame measurement and print its object")
     ap.add_argument("--r-sessions", type=int, nargs="*", default=None)
     ap.add_argument("--phase-trace", default=None, metavar="PATH:SESSIONS",
-                    help="print the per-position phase breakdown of the split (5-9), quad (10) or octo (11) kernel and exit")
+                    help="print the per-position phase breakdown of the pair (4), split (5-9), quad (10) or octo (11) "
+                         "kernel and exit")
     ap.add_argument("--eos-only", action="store_true",
                     help="run only the EOS-projection measurement and print its object (profiling)")
     ap.add_argument("--eos-sessions", type=int, nargs="*", default=None,
@@ -496,9 +497,10 @@ QUAD_STAMPS = ["input rows", "q|k|v", "attention", "attention round", "o-project
 
 
 def quad_trace(w, dev, path, n, frames=10):
-    """Per-position phase breakdown of the split (paths 5-9), quad (path 10)
-    or octo (path 11) kernel at n sessions (library trace hook
-    mtt_b200_test_frame_trace; the three kernels stamp the same 16 points):
+    """Per-position phase breakdown of the pair (path 4), split (paths 5-9),
+    quad (path 10) or octo (path 11) kernel at n sessions (library trace hook
+    mtt_b200_test_frame_trace; the kernels stamp the same 16 points, the pair
+    kernel's sampling phase including the next position's rows):
     SM-clock stamps of CTA 0 at 16 points of each position, averaged over
     positions 1..15 of `frames` frames, in microseconds at the clock measured
     over the frame."""

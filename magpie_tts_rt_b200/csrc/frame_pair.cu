@@ -125,6 +125,11 @@ static_assert(kPSmemBytes <= 232448, "pair kernel shared memory");
 __device__ __forceinline__ int err_flag(const PairSmem& sm) { return *reinterpret_cast<const volatile int*>(&sm.err); }
 __device__ __forceinline__ void cbar() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
 
+// Phase clock stamp of the first CTA (library trace hook: mtt_b200_test_frame_trace).
+__device__ __forceinline__ void p_stamp(const Frame& f, bool tracer, int p, int i) {
+  if (tracer) f.trace[kPositions * p + i] = static_cast<uint64_t>(clock64());
+}
+
 // ---------------------------------------------------------------------------
 // weight stream
 // ---------------------------------------------------------------------------
@@ -559,8 +564,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
     const bool own_is_a = c == 0;  // slots 0..7 are sampled by CTA 0, 8..15 by CTA 1
     Round rd;
     int it = 0;
+    const bool tracer = f.trace != nullptr && blockIdx.x == 0 && threadIdx.x == 0;
+    if (tracer) f.trace[256] = static_cast<uint64_t>(clock64()), f.trace[257] = global_ns();
     for (int p = 0; p < kPositions; ++p) {
       // ---------------- input rows
+      p_stamp(f, tracer, p, 0);
       if (has_in_projection(folded, p)) {
         float acc[2][2][2][4];  // nb, m-tile, chain
 #pragma unroll
@@ -634,6 +642,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
       // ---------------- LN1, q|k|v of this CTA's heads
       layer_norm_rows32(sm.x, sm.xa, g1);
       cbar();
+      p_stamp(f, tracer, p, 1);
       {
         uint32_t a[2][16][4];
         load_a2(a, sm.xa, kLdX);
@@ -649,9 +658,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
         });
       }
       cbar();
+      p_stamp(f, tracer, p, 2);
       // ---------------- attention of heads 2c, 2c+1; outputs to the peer
       attention_pair(sm, p, c, peer, peer_bar(sm, rd, peer));
+      p_stamp(f, tracer, p, 3);
       finish_round(sm, rd, kPR * 128 * 2);  // R1
+      p_stamp(f, tracer, p, 4);
       // ---------------- o-projection features [128c, +128) + residual
       {
         uint32_t a[2][16][4];
@@ -672,9 +684,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
         });
       }
       finish_round(sm, rd, kPR * 128 * 2);  // R2
+      p_stamp(f, tracer, p, 5);
       // ---------------- LN2, FFN1 features [512c, +512) + GELU
       layer_norm_rows32(sm.x, sm.xa, g2);
       cbar();
+      p_stamp(f, tracer, p, 6);
       {
         uint32_t a[2][16][4];
         load_a2(a, sm.xa, kLdX);
@@ -691,6 +705,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
         });
       }
       cbar();
+      p_stamp(f, tracer, p, 7);
       // ---------------- FFN2 partial sums over this CTA's 512 hidden features
       float own[2][2][4];  // this CTA's output features (nb = 2c, 2c+1), m-tile
       {
@@ -732,7 +747,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
           }
         }
       }
+      p_stamp(f, tracer, p, 8);
       finish_round(sm, rd, kPR * 128 * 4);  // R3
+      p_stamp(f, tracer, p, 9);
       // ---------------- own output features: CTA 0's partial + CTA 1's partial, + residual
       {
         const uint32_t rb = peer_bar(sm, rd, peer);
@@ -756,6 +773,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
         }
       }
       finish_round(sm, rd, kPR * 128 * 2);  // R4
+      p_stamp(f, tracer, p, 10);
       // ---------------- head p, this CTA's vocabulary half, all 16 sessions
       {
         uint32_t a[2][16][4];
@@ -803,7 +821,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
         cbar();
         if (threadIdx.x < kPOwn) push_b32(&sm.peer_nonfinite[threadIdx.x], peer, sm.stage_nonfinite[threadIdx.x], rb);
       }
+      p_stamp(f, tracer, p, 11);
       finish_round(sm, rd, n_own * kHalf * 2 + kPOwn * 4);  // R5: the peer's half of this CTA's sessions
+      p_stamp(f, tracer, p, 12);
       // ---------------- sampling of sessions 8c..8c+7; tokens and next input rows to both CTAs
       if (warp < n_own) {
         const int ls = warp, slot = own0 + warp;
@@ -846,13 +866,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
           }
         }
       }
+      p_stamp(f, tracer, p, 13);
       if (p + 1 < kPositions) {
         if (threadIdx.x == 0) push_b32(&sm.sink, peer, 0u, peer_bar(sm, rd, peer));  // the round's token
         finish_round(sm, rd, n_peer * (4 + (folded ? rp * kD * 2 : 0)) + 4);  // R6: the peer's tokens and rows
       } else {
         cbar();
       }
+      p_stamp(f, tracer, p, 14);
+      p_stamp(f, tracer, p, 15);
     }
+    if (tracer) f.trace[258] = static_cast<uint64_t>(clock64()), f.trace[259] = global_ns();
     // ---- commit: tokens, counters, flags, next-frame embedding of the sessions this CTA sampled
     if (threadIdx.x == 0 && sm.err) {
       for (int s = 0; s < kPSlots; ++s) {
