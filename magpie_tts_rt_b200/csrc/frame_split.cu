@@ -1109,8 +1109,9 @@ __global__ void __launch_bounds__(kSThreads, 1) split_frame_kernel(Frame f, cons
       }
       cbar();
 
-      // ---------------- LN1, qkv of the CTA's heads
-      layer_norm_op<R>(sm.x, sm.xa, g1);
+      // ---------------- LN1 (with the folded tables done by the previous
+      // position's row gather), qkv of the CTA's heads
+      if (has_in_projection(folded, p)) layer_norm_op<R>(sm.x, sm.xa, g1);
       operand_ready(sm);
       s_stamp(f, tracer, p, 1);
       for (int b = 0; b < K::nq; ++b, ++mb) {
@@ -1468,6 +1469,28 @@ __global__ void __launch_bounds__(kSThreads, 1) split_frame_kernel(Frame f, cons
           const uint4 row = pack8(y);
           *reinterpret_cast<uint4*>(sm.x + slot * kLdX + lane * 8) = row;
           if (rp == 2) *reinterpret_cast<uint4*>(sm.x + (slot + K::S) * kLdX + lane * 8) = row;
+          // the next position's LN1 of the row, from registers (the same arithmetic as
+          // layer_norm_op; the conditional and unconditional rows are the same row)
+          float v[8];
+          unpack8(row, v);
+          float sum = 0.f;
+#pragma unroll
+          for (int j = 0; j < 8; ++j) sum += v[j];
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+          const float mean = sum / static_cast<float>(kD);
+          float var = 0.f;
+#pragma unroll
+          for (int j = 0; j < 8; ++j) var += (v[j] - mean) * (v[j] - mean);
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) var += __shfl_xor_sync(0xffffffffu, var, o);
+          const float rstd = 1.0f / sqrtf(var / static_cast<float>(kD) + 1.0e-5f);
+          float out[8];
+#pragma unroll
+          for (int j = 0; j < 8; ++j) out[j] = ((v[j] - mean) * rstd) * g1[j];
+          const uint4 ln = pack8(out);
+          *op_unit<R>(sm.xa, slot, lane * 8) = ln;
+          if (rp == 2) *op_unit<R>(sm.xa, slot + K::S, lane * 8) = ln;
         }
       }
       cbar();
