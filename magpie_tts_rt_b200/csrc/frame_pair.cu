@@ -30,11 +30,14 @@
 // touch during the phase before that round (x columns it does not own, the
 // peer-attention buffer xr, the FFN2 receive buffer red, the value columns of
 // the other vocabulary half).  Weights stream through a four-slot TMA ring
-// (no multicast) filled by a producer warp; GEMMs are mma.sync m16n8k16 with
-// the 32-row A operand in registers.  TMEM holds the KV cache of the CTA's
-// two heads: lane 32q + t, quadrant q = (local head q/2, rows 16(q%2)..+16),
-// t = 2 (row % 16) + half; columns as in the tile kernel.  Every wait is
-// bounded; a timeout sets invalid bit 4 for the pair's sessions.
+// (no multicast) filled by a producer warp.  GEMMs are mma.sync m16n8k16 with
+// the 32-row A operand in registers, except the head: tcgen05.mma with 128
+// vocabulary rows on M and the 32 tile rows on N, accumulating in TMEM
+// columns of the KV cache that no position has written yet.  TMEM holds the
+// KV cache of the CTA's two heads: lane 32q + t, quadrant q = (local head
+// q/2, rows 16(q%2)..+16), t = 2 (row % 16) + half; columns as in the tile
+// kernel.  Every wait is bounded; a timeout sets invalid bit 4 for the pair's
+// sessions.
 #include <cooperative_groups.h>
 #include <cuda.h>
 
@@ -55,8 +58,8 @@ constexpr int kPOwn = 8;                     // slots each CTA samples
 constexpr int kPW = 8;                       // consumer warps
 constexpr int kPC = kPW * 32;                // consumer threads
 constexpr int kPThreads = kPC + 128;         // + the producer warpgroup
-constexpr int kPProducerRegs = 40;
-constexpr int kPConsumerRegs = 232;
+constexpr int kPProducerRegs = 56;   // the producer and head MMA threads
+constexpr int kPConsumerRegs = 224;
 static_assert(128 * kPProducerRegs + kPC * kPConsumerRegs <= kPThreads * 168, "register split");
 constexpr int kD = 256;
 constexpr int kF = 1024;
@@ -67,6 +70,7 @@ constexpr int kCPanel = 64;
 constexpr int kCElems = kCRows * kCK;
 constexpr uint32_t kCBytes = kCElems * 2;
 constexpr int kPSlots = 4;
+constexpr int kHeadRows = 128;  // head chunks: 128 vocabulary rows x 128 K columns (tcgen05 M = 128)
 constexpr int kLdX = kD + 8;    // 264
 constexpr int kLdR = 128 + 8;   // 136: the peer's two heads
 constexpr int kLdQ = 384 + 8;   // 392: this CTA's q | k | v
@@ -95,8 +99,8 @@ union PairU {
 
 struct __align__(1024) PairSmem {
   bf16 ring[kPSlots][kCElems];
+  bf16 xa[kPR * kLdX];  // LN output / this CTA's attention heads / the head's B operand / sampler lists
   bf16 x[kPR * kLdX];   // residual stream (all rows, all features)
-  bf16 xa[kPR * kLdX];  // LN output / this CTA's attention heads / sampler lists
   bf16 xr[kPR * kLdR];  // the peer's attention heads
   PairU u;
   float red[kPR][128];  // the peer's FFN2 partial sums of this CTA's output features
@@ -117,8 +121,16 @@ struct __align__(1024) PairSmem {
   unsigned long long full[kPSlots];
   unsigned long long empty[kPSlots];
   unsigned long long xbar[2];
+  unsigned long long hbar[2];   // head accumulator buffer b holds a finished M-block (tcgen05.commit)
+  unsigned long long hfree[2];  // every consumer warp has read head buffer b
+  unsigned long long hop;       // the head's B operand of this position is in xa
+  unsigned long long hfin;      // every head MMA has completed (teardown)
+  int32_t mma_done;
   uint32_t sink;  // round token (never read)
 };
+// xa follows the ring at a 1024-byte boundary: the head reads it as a
+// swizzled tcgen05 operand (8-row, 1024-byte swizzle atoms).
+static_assert((kPSlots * kCElems * 2) % 1024 == 0 && kPR * 64 * 2 * 4 <= kPR * kLdX * 2, "head operand in xa");
 constexpr size_t kPSmemBytes = sizeof(PairSmem) + 1024;
 static_assert(kPSmemBytes <= 232448, "pair kernel shared memory");
 
@@ -173,7 +185,10 @@ __device__ __forceinline__ const CUtensorMap* chunk_origin(const PairMaps& m, in
     return &m.ffn2;
   }
   k -= 8;
-  *y = p * kVocab + kHalf * c + kCRows * k;  // rows past this CTA's half are ignored
+  // head: M-block k / 2 (vocabulary rows [128 (k / 2), +128) of this CTA's
+  // half; rows past the half are ignored), K columns [128 (k % 2), +128)
+  *x = 128 * (k & 1);
+  *y = p * kVocab + kHalf * c + 128 * (k >> 1);
   return &m.head;
 }
 
@@ -189,9 +204,16 @@ __device__ void producer(PairSmem& sm, const PairMaps& maps, int c, bool folded)
       const CUtensorMap* map = chunk_origin(maps, c, folded, p, k, &x, &y);
       fence_proxy_async();
       mbar_expect_tx(&sm.full[slot], kCBytes);
+      if (map == &maps.head) {  // two 128-row x 64-column panels
 #pragma unroll
-      for (int b = 0; b < kCK / kCPanel; ++b) {
-        tma_load_2d(sm.ring[slot] + b * (kCRows * kCPanel), map, x + b * kCPanel, y, &sm.full[slot]);
+        for (int b = 0; b < 2; ++b) {
+          tma_load_2d(sm.ring[slot] + b * (kHeadRows * kCPanel), map, x + b * kCPanel, y, &sm.full[slot]);
+        }
+      } else {  // four 64-row x 64-column panels
+#pragma unroll
+        for (int b = 0; b < kCK / kCPanel; ++b) {
+          tma_load_2d(sm.ring[slot] + b * (kCRows * kCPanel), map, x + b * kCPanel, y, &sm.full[slot]);
+        }
       }
       sm.last_issued[slot] = it;
     }
@@ -278,6 +300,120 @@ __device__ __forceinline__ void gemm_n2(PairSmem& sm, int& it, const uint32_t (&
   }
 }
 
+// ---------------------------------------------------------------------------
+// head on tcgen05: D[vocabulary row m][tile row n] in TMEM lane m, with the
+// accumulators in key/value columns no position has written yet.  Position j
+// keeps its keys in columns 16 tmem_block(j) + [0, 16) and its values 256
+// higher; blocks 14 and 15 (positions 13 and 15) are adjacent.  Positions
+// 0..12, and 15 once its attention has read the cache: two N = 32 buffers,
+// columns [224, 256) and [480, 512).  Position 13: the key / value blocks of
+// positions 15 (buffer 0) and 14 (buffer 1), each buffer two N = 16 halves
+// (tile rows 0..15 in the key block, 16..31 in the value block).  Position
+// 14: position 15's blocks, one buffer.
+// ---------------------------------------------------------------------------
+
+__device__ __forceinline__ bool head_wide(int p) { return p <= 12 || p == 15; }
+__device__ __forceinline__ int head_nbuf(int p) { return p == 14 ? 1 : 2; }
+// Columns of buffer b: tile rows 0..15 from ca, rows 16..31 from cb.
+__device__ __forceinline__ void head_cols(int p, int b, uint32_t& ca, uint32_t& cb) {
+  if (head_wide(p)) {
+    ca = b ? 480u : 224u;
+    cb = ca + 16u;
+  } else {
+    ca = 16u * static_cast<uint32_t>(tmem_block(b ? 14 : 15));
+    cb = ca + 256u;
+  }
+}
+
+// The head MMA thread: the MMAs of head M-block mb (chunks it0 + 2 mb: K 0..127 and
+// it0 + 2 mb + 1: K 128..255) into buffer b, then a commit to hbar[b], also
+// after an error (the waiting warps always see the phase complete).
+__device__ __forceinline__ void issue_head_block(PairSmem& sm, int it0, int mb, int p, int b) {
+  const bf16* c0 = acquire(sm, it0 + 2 * mb);
+  const bf16* c1 = acquire(sm, it0 + 2 * mb + 1);
+  if (err_flag(sm) == 0) {
+    tmem_fence_after_sync();
+    uint32_t ca, cb;
+    head_cols(p, b, ca, cb);
+    const uint32_t da = sm.tmem + ca, db = sm.tmem + cb;
+    const uint64_t a0 = umma_desc_sw128(c0), a1 = umma_desc_sw128(c1), b0 = umma_desc_sw128(sm.xa);
+    constexpr uint64_t kPanelStep = kHeadRows * kCPanel * 2 / 16;  // 128-row weight panel
+    constexpr uint64_t kOpStep = kPR * kCPanel * 2 / 16;           // 32-row operand panel
+    constexpr uint64_t kHalfRows = 16 * 128 / 16;                  // operand rows 16..31
+    // straight-line bursts (a branch between tcgen05.mma instructions slows their issue)
+    if (head_wide(p)) {
+      constexpr uint32_t idesc = umma_idesc_bf16(128, 32);
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk) {
+        umma_bf16(da, a0 + (kk >> 2) * kPanelStep + 2 * (kk & 3), b0 + (kk >> 2) * kOpStep + 2 * (kk & 3), idesc,
+                  kk != 0);
+      }
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk) {
+        umma_bf16(da, a1 + (kk >> 2) * kPanelStep + 2 * (kk & 3), b0 + (2 + (kk >> 2)) * kOpStep + 2 * (kk & 3),
+                  idesc, true);
+      }
+    } else {
+      // positions 13 and 14 only: a rolled loop keeps this thread within its registers
+      constexpr uint32_t idesc = umma_idesc_bf16(128, 16);
+#pragma unroll 1
+      for (int kk = 0; kk < 16; ++kk) {
+        const uint64_t a = ((kk >> 3) ? a1 : a0) + ((kk >> 2) & 1) * kPanelStep + 2 * (kk & 3);
+        const uint64_t bd = b0 + (kk >> 2) * kOpStep + 2 * (kk & 3);
+        umma_bf16(da, a, bd, idesc, kk != 0);
+        umma_bf16(db, a, bd + kHalfRows, idesc, kk != 0);
+      }
+    }
+  }
+  umma_commit(&sm.hbar[b]);
+}
+
+// Two 8-column loads (lanes of this warp's quadrant) and one wait.
+__device__ __forceinline__ void tmem_ld8x2(uint32_t (&v)[16], uint32_t ta, uint32_t tb) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7])
+               : "r"(ta)
+               : "memory");
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+               : "r"(tb)
+               : "memory");
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(v[0]), "+r"(v[1]), "+r"(v[2]), "+r"(v[3]), "+r"(v[4]), "+r"(v[5]), "+r"(v[6]), "+r"(v[7]),
+                 "+r"(v[8]), "+r"(v[9]), "+r"(v[10]), "+r"(v[11]), "+r"(v[12]), "+r"(v[13]), "+r"(v[14]), "+r"(v[15])
+               :
+               : "memory");
+}
+
+// The head MMA thread (one lane of the control warpgroup): per position,
+// once the consumers have put the B operand in xa, the eight M-blocks
+// alternate over the position's buffers; a buffer is reused after every
+// consumer warp has read it.  Waits are skipped after an error (all bounded).
+__device__ void head_mma(PairSmem& sm, bool folded) {
+  int it = 0, u0 = 0, u1 = 0;  // chunks before this position, uses of buffers 0 and 1
+  for (int p = 0; p < kPositions; ++p) {
+    const int n = chunks_in_position(folded, p);
+    const int it0 = it + n - 2 * 8;  // the head's 16 chunks end the position
+    it += n;
+    if (err_flag(sm) == 0 && !mbar_wait_cta(&sm.hop, p & 1)) sm.err = 1;
+    const int nb = head_nbuf(p);
+    for (int mb = 0; mb < 8; ++mb) {
+      const int b = nb == 2 ? (mb & 1) : 0;
+      const int u = b ? u1 : u0;
+      if (u >= 1 && err_flag(sm) == 0 && !mbar_wait_cta(&sm.hfree[b], (u - 1) & 1)) sm.err = 1;
+      if (b) {
+        ++u1;
+      } else {
+        ++u0;
+      }
+      issue_head_block(sm, it0, mb, p, b);
+    }
+  }
+  umma_commit(&sm.hfin);
+  mbar_wait_cta(&sm.hfin, 0);
+  atomicExch(&sm.mma_done, 1);
+}
+
 __device__ __forceinline__ void layer_norm_rows32(const bf16* x, bf16* xa, const float (&g)[8]) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
 #pragma unroll
@@ -347,7 +483,8 @@ __device__ __forceinline__ void attention_pair(PairSmem& sm, int p, int c, int p
   const int row = 16 * (q & 1) + (lane >> 1), half = lane & 1;
   const uint32_t tl = sm.tmem + (static_cast<uint32_t>(32 * q) << 16);
   const bf16* qrow = sm.u.qkv + row * kLdQ + kHeadDim * hl + 32 * half;
-  {  // append k (part 0) or v (part 1) of position p
+  {  // append k (part 0) or v (part 1) of position p (its columns may have held a head accumulator)
+    tmem_fence_after_sync();
     uint32_t kv[16];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
@@ -497,6 +634,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
       const int left = seen - first;
       sm.n_sess = left <= 0 ? 0 : (left < kPS ? left : kPS);
       sm.err = 0;
+      sm.mma_done = 0;
     }
   }
   __syncthreads();
@@ -515,6 +653,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
     }
     mbar_init(&sm.xbar[0], 1);
     mbar_init(&sm.xbar[1], 1);
+    mbar_init(&sm.hbar[0], 1);
+    mbar_init(&sm.hbar[1], 1);
+    mbar_init(&sm.hfree[0], kPW);
+    mbar_init(&sm.hfree[1], kPW);
+    mbar_init(&sm.hop, 1);
+    mbar_init(&sm.hfin, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncwarp();
@@ -554,14 +698,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
   if (warp >= kPW) {  // producer warpgroup
     asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kPProducerRegs));
     if (warp == kPW && lane == 0) producer(sm, maps, c, folded);
+    if (warp == kPW + 1 && lane == 0) head_mma(sm, folded);
   } else {
     asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kPConsumerRegs));
     float g1[8], g2[8];
     unpack8(*reinterpret_cast<const uint4*>(f.ln1 + lane * 8), g1);
     unpack8(*reinterpret_cast<const uint4*>(f.ln2 + lane * 8), g2);
-    // head epilogue: this thread holds rows of slots sa = lane / 4 and sb = sa + 8
-    const int sa = lane >> 2, sb = sa + 8;
-    const bool own_is_a = c == 0;  // slots 0..7 are sampled by CTA 0, 8..15 by CTA 1
     Round rd;
     int it = 0;
     const bool tracer = f.trace != nullptr && blockIdx.x == 0 && threadIdx.x == 0;
@@ -775,49 +917,105 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
       finish_round(sm, rd, kPR * 128 * 2);  // R4
       p_stamp(f, tracer, p, 10);
       // ---------------- head p, this CTA's vocabulary half, all 16 sessions
+      // (tcgen05: M = 128 vocabulary rows, N = the 32 tile rows, K = 256; one
+      // thread of the control warpgroup issues, buffer b's M-block lands on hbar[b])
       {
-        uint32_t a[2][16][4];
-        load_a2(a, sm.x, kLdX);
-        bool nf_a = false, nf_b = false;
+        // B operand: x as four 32-row x 64-column panels with the 128-byte swizzle
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int q = threadIdx.x + kPC * i;  // 16-byte unit: row q / 32, columns [8 (q % 32), +8)
+          const int r = q >> 5, kc = q & 31;
+          const uint4 u = *reinterpret_cast<const uint4*>(sm.x + r * kLdX + 8 * kc);
+          *reinterpret_cast<uint4*>(reinterpret_cast<unsigned char*>(sm.xa) + (kc >> 3) * (kPR * 128) + r * 128 +
+                                    (((kc & 7) ^ (r & 7)) << 4)) = u;
+        }
+        fence_proxy_async();
+        tmem_fence_before_sync();  // the attention's key/value reads come before the MMAs' writes
+        cbar();
+        if (threadIdx.x == 0) mbar_arrive(&sm.hop);
+        const int nbuf = head_nbuf(p);
+        // this warp: vocabulary entries [32 (warp % 4), +32) of each M-block,
+        // slots 8 g..8 g + 7 (sampled by CTA g); after the lane-pair exchange
+        // an even lane holds entries (j, j + 1) of slots 8 g + 0..3, an odd
+        // lane entries (j - 1, j) of slots 8 g + 4..7
+        const int g = warp >> 2;
+        const bool local = g == c, odd = lane & 1;
+        const int s0 = 8 * g + 4 * (lane & 1);
         const uint32_t rb = peer_bar(sm, rd, peer);
-        const uint32_t fa = sm.flags[sa], fb = sm.flags[sb];
-        const bool live_a = sa < n_sess, live_b = sb < n_sess;
         const bool cfg = rp == 2;
         const float cfg_scale = f.prm.cfg_scale, uncond_scale = __fsub_rn(1.0f, f.prm.cfg_scale);
-        bf16* lo_a = (f.logits_out && live_a)
-                         ? f.logits_out + (static_cast<int64_t>(sm.sess[sa]) * kPositions + p) * rp * kVocab : nullptr;
-        bf16* lo_b = (f.logits_out && live_b)
-                         ? f.logits_out + (static_cast<int64_t>(sm.sess[sb]) * kPositions + p) * rp * kVocab : nullptr;
-        uint16_t* dst_row = sm.u.val + (lane >> 2) * kVocab;  // the slot's row in its sampling CTA
-        gemm_n2(sm, it, a, 16, [&](int nb, const float (&acc)[2][4]) {
-          const int j = kCRows * nb + 8 * warp + 2 * (lane & 3);
-          if (j < kHalf) {
-            const int n = kHalf * c + j;
-            const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(sm.hb + j));
+        uint32_t fl[4];
+        bool live_s[4], nf[4];
+        bf16* lo[4];
 #pragma unroll
-            for (int hh = 0; hh < 2; ++hh) {  // hh 0: slot sa (acc[.][0..1]), hh 1: slot sb (acc[.][2..3])
-              if (!(hh ? live_b : live_a)) continue;
-              const uint32_t c2 = pack2_rn(__fadd_rn(acc[0][2 * hh], b.x), __fadd_rn(acc[0][2 * hh + 1], b.y));
-              const uint32_t u2 = pack2_rn(__fadd_rn(acc[1][2 * hh], b.x), __fadd_rn(acc[1][2 * hh + 1], b.y));
-              bf16* lo = hh ? lo_b : lo_a;
-              if (lo) {
-                *reinterpret_cast<uint32_t*>(lo + n) = c2;
-                if (cfg) *reinterpret_cast<uint32_t*>(lo + kVocab + n) = u2;
+        for (int i = 0; i < 4; ++i) {
+          const int s = s0 + i;
+          fl[i] = sm.flags[s];
+          live_s[i] = s < n_sess;
+          nf[i] = false;
+          lo[i] = (f.logits_out && live_s[i])
+                      ? f.logits_out + (static_cast<int64_t>(sm.sess[s]) * kPositions + p) * rp * kVocab : nullptr;
+        }
+        const uint32_t tl = sm.tmem + (static_cast<uint32_t>(32 * (warp & 3)) << 16);
+        uint32_t hph = 0;  // bit b: parity of buffer b's next phase
+#pragma unroll 1
+        for (int mb = 0; mb < 8; ++mb) {
+          const int b = nbuf == 2 ? (mb & 1) : 0;
+          if (!mbar_wait_cta(&sm.hbar[b], (hph >> b) & 1u)) sm.err = 1;
+          hph ^= 1u << b;
+          tmem_fence_after_sync();
+          uint32_t ca, cb;
+          head_cols(p, b, ca, cb);
+          uint32_t v[16];  // v[i]: slot 8 g + i conditional row, v[8 + i]: unconditional
+          tmem_ld8x2(v, tl + ca + 8 * g, tl + cb + 8 * g);
+          release(sm, it);
+          release(sm, it + 1);
+          it += 2;
+          tmem_fence_before_sync();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&sm.hfree[b]);  // this warp has read buffer b
+          float cv[4][2], uv[4][2];  // [local slot][entry j & ~1, j | 1]
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float mc = __uint_as_float(odd ? v[4 + i] : v[i]);
+            const float mu = __uint_as_float(odd ? v[12 + i] : v[8 + i]);
+            const float gc = __shfl_xor_sync(0xffffffffu, __uint_as_float(odd ? v[i] : v[4 + i]), 1);
+            const float gu = __shfl_xor_sync(0xffffffffu, __uint_as_float(odd ? v[8 + i] : v[12 + i]), 1);
+            cv[i][0] = odd ? gc : mc;
+            cv[i][1] = odd ? mc : gc;
+            uv[i][0] = odd ? gu : mu;
+            uv[i][1] = odd ? mu : gu;
+          }
+          const int jl = 128 * mb + 32 * (warp & 3) + (lane & ~1);
+          if (jl < kHalf) {
+            const int n = kHalf * c + jl;
+            const float2 bias = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(sm.hb + jl));
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              if (!live_s[i]) continue;
+              const uint32_t c2 = pack2_rn(__fadd_rn(cv[i][0], bias.x), __fadd_rn(cv[i][1], bias.y));
+              const uint32_t u2 = pack2_rn(__fadd_rn(uv[i][0], bias.x), __fadd_rn(uv[i][1], bias.y));
+              if (lo[i]) {
+                *reinterpret_cast<uint32_t*>(lo[i] + n) = c2;
+                if (cfg) *reinterpret_cast<uint32_t*>(lo[i] + kVocab + n) = u2;
               }
-              const uint32_t g = cfg ? guided_value2(c2, u2, cfg_scale, uncond_scale) : c2;
-              const uint32_t v = constrain2(g, n, hh ? fb : fa, hh ? nf_b : nf_a);
-              if ((hh == 0) == own_is_a) {
-                *reinterpret_cast<uint32_t*>(dst_row + n) = v;
+              const uint32_t gv = cfg ? guided_value2(c2, u2, cfg_scale, uncond_scale) : c2;
+              const uint32_t val = constrain2(gv, n, fl[i], nf[i]);
+              uint16_t* dst = sm.u.val + ((s0 + i) & 7) * kVocab + n;  // the slot's row in its sampling CTA
+              if (local) {
+                *reinterpret_cast<uint32_t*>(dst) = val;
               } else {
-                push_b32(dst_row + n, peer, v, rb);
+                push_b32(dst, peer, val, rb);
               }
             }
           }
-        });
-        // the non-finite flags: slot a's to this CTA (own_is_a) or the peer, slot b's the other way round
-        const int ls = lane >> 2;
-        if (nf_a) atomicOr(own_is_a ? &sm.nonfinite[ls] : &sm.stage_nonfinite[ls], 1u);
-        if (nf_b) atomicOr(own_is_a ? &sm.stage_nonfinite[ls] : &sm.nonfinite[ls], 1u);
+        }
+        tmem_fence_before_sync();
+        // the non-finite flags: to this CTA for its own slots, staged for the peer's
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          if (nf[i]) atomicOr(local ? &sm.nonfinite[(s0 + i) & 7] : &sm.stage_nonfinite[(s0 + i) & 7], 1u);
+        }
         cbar();
         if (threadIdx.x < kPOwn) push_b32(&sm.peer_nonfinite[threadIdx.x], peer, sm.stage_nonfinite[threadIdx.x], rb);
       }
@@ -916,6 +1114,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
       for (int e = 0; e < 8; ++e) out[e] = __fdiv_rn(acc[e], 16.0f);
       *reinterpret_cast<uint4*>(f.next_emb + static_cast<int64_t>(sm.sess[slot]) * kEmbed + k8) = pack8(out);
     }
+    // the head MMA thread's MMAs have completed before TMEM is freed (bounded)
+    if (threadIdx.x == 0) {
+      const unsigned long long t0 = global_ns();
+      while (*reinterpret_cast<volatile int*>(&sm.mma_done) == 0 && global_ns() - t0 < 20000000ull) __nanosleep(1000);
+    }
     tmem_fence_before_sync();
     cbar();
     if (warp == 0) {
@@ -955,7 +1158,7 @@ cudaError_t launch_pair_frame(const Frame& f, cudaStream_t stream) {
   if (!make_weight_map(&maps.in_proj, f.in_w, kEmbed, kD, kCRows) ||
       !make_weight_map(&maps.qkv, f.qkv, kD, 3 * kD, kCRows) || !make_weight_map(&maps.o, f.o, kD, kD, kCRows) ||
       !make_weight_map(&maps.ffn1, f.w1, kD, kF, kCRows) || !make_weight_map(&maps.ffn2, f.w2, kF, kD, kCRows) ||
-      !make_weight_map(&maps.head, f.head_w, kD, static_cast<uint64_t>(kPositions) * kVocab, kCRows)) {
+      !make_weight_map(&maps.head, f.head_w, kD, static_cast<uint64_t>(kPositions) * kVocab, kHeadRows)) {
     return cudaErrorInvalidValue;
   }
   const int pairs = (f.n + kPS - 1) / kPS;
