@@ -59,7 +59,7 @@ PATH_NAMES = {1: "phase kernels", 2: "fused cluster kernel", 3: "tile kernel", 4
               5: "split kernel x1", 6: "split kernel x2", 7: "split kernel x4", 8: "split kernel x8",
               9: "split kernel x2, 32-row tiles", 10: "quad kernel", 11: "octo kernel"}
 # DRAM bytes per launch of the frame kernel, measured by ncu (path, sessions per GPU)
-TRAFFIC = {("tile kernel", 1024): 27.64e6, ("pair kernel", 1024): 27.70e6, ("split kernel x4", 256): 23.12e6,
+TRAFFIC = {("tile kernel", 1024): 27.64e6, ("pair kernel", 1024): 27.71e6, ("split kernel x4", 256): 23.12e6,
            ("split kernel x8", 64): 20.56e6, ("fused cluster kernel", 1): 18.76e6}
 WORKLOADS = {
     "config4": dict(total_streams=1024, frames=500, eos_frac=0.05, eos_lo=50, eos_hi=500, weak=False),
