@@ -961,7 +961,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
 #pragma unroll 1
         for (int mb = 0; mb < 8; ++mb) {
           const int b = nbuf == 2 ? (mb & 1) : 0;
-          if (!mbar_wait_cta(&sm.hbar[b], (hph >> b) & 1u)) sm.err = 1;
+          if (err_flag(sm) == 0 && !mbar_wait_cta(&sm.hbar[b], (hph >> b) & 1u)) sm.err = 1;
           hph ^= 1u << b;
           tmem_fence_after_sync();
           uint32_t ca, cb;
