@@ -57,7 +57,7 @@ constexpr int kPS = 16;                      // session slots per pair
 constexpr int kPOwn = 8;                     // slots each CTA samples
 constexpr int kPW = 8;                       // consumer warps
 constexpr int kPC = kPW * 32;                // consumer threads
-constexpr int kPThreads = kPC + 128;         // + the producer warpgroup
+constexpr int kPThreads = kPC + 128;         // + the control warpgroup (TMA producer, head MMA thread)
 constexpr int kPProducerRegs = 56;   // the producer and head MMA threads
 constexpr int kPConsumerRegs = 224;
 static_assert(128 * kPProducerRegs + kPC * kPConsumerRegs <= kPThreads * 168, "register split");
@@ -695,7 +695,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
   tmem_fence_after_sync();
   cluster.sync();  // both CTAs' barriers are initialised before any push
 
-  if (warp >= kPW) {  // producer warpgroup
+  if (warp >= kPW) {  // control warpgroup: the TMA producer and the head MMA thread
     asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kPProducerRegs));
     if (warp == kPW && lane == 0) producer(sm, maps, c, folded);
     if (warp == kPW + 1 && lane == 0) head_mma(sm, folded);
